@@ -1,0 +1,351 @@
+#!/usr/bin/env python3
+"""Decode benchmark for the B200 text-decode path (one JSON line on rank 0).
+
+Workload (config 0 of the reference's decode benchmark): the 24-layer, 1024-hidden
+HunyuanOCR text decoder, vocab 120818 tied, fp32 weights and KV cache, random-init
+~N(0, 0.02) weights (seeded counter generator), a 1024-position prompt (768
+N(0,1) image-embedding rows on a 24x32 mRoPE grid + 256 uniform text ids), then
+256 greedy tokens with repetition penalty 1.08.
+
+One step = the AR decode of those 256 tokens from the prefilled state (255
+decoder steps, each one CUDA-graph replay of embed -> 24 layers -> LM head ->
+penalised argmax, token kept on the device). `value` = decode tokens/s with the
+prompt state resident in HBM; `e2e` = tokens/s of the reference-facing call
+(hy_run_vlm_decode_with_prompt: host prompt -> prefill -> 256 tokens -> host).
+
+Multi-GPU (torchrun, one process per GPU): replicas only - each rank decodes its
+own request; value = tokens of all ranks / max rank time ("scaling": "weak").
+
+--impl reference: times the CPU oracle (the reference's CPU fp32 decode path
+restated in numpy, oracle/hy_oracle.py) on the host cores for the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PROMPT_GRID = (24, 32)
+PROMPT_TEXT = 256
+GEN_TOKENS = 256
+HIDDEN = 1024
+V = 120818
+LAYERS = 24
+FFN = 3584
+PENALTY = 1.08
+# Algorithmic bytes (fp32): weights read once per token, 8 unique KV heads.
+DECODER_WEIGHT_BYTES = LAYERS * (4096 * 1024 + 1024 * 2048 + 2 * FFN * 1024 + 1024 * FFN) * 4
+LM_HEAD_BYTES = V * HIDDEN * 4
+KV_ROW_BYTES = LAYERS * 8 * 128 * 4 * 2
+KERNELS_PER_AR_STEP = LAYERS * 5 + 1
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def ar_bytes_per_token(seq: int, gen: int) -> float:
+    """Mean algorithmic bytes per decode token over steps with KV length seq..seq+gen-2."""
+    mean_past = seq + (gen - 2) / 2.0
+    return DECODER_WEIGHT_BYTES + LM_HEAD_BYTES + (mean_past + 1) * KV_ROW_BYTES + HIDDEN * 4
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def dist_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def dist_barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def prompt_arrays(seed: int):
+    """Same prompt layout as oracle.synthetic_prompt (counter generator), built without the oracle."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("hy_b200_prompt", os.path.join(REPO, "hunyuanocr-ncnn_b200",
+                                                                                   "synthetic.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod.synthetic_prompt(seed, PROMPT_GRID[0], PROMPT_GRID[1], PROMPT_TEXT, V)
+
+
+def run_b200(args, world, rank, local):
+    sys.path.insert(0, REPO)
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    pkg.load_library()
+    ids, pos, feats, image_token = prompt_arrays(seed=rank)
+    seq = ids.shape[0]
+    rt = pkg.TextRuntime.synthetic(seed=0, device=local, max_prefill=seq, max_tokens=GEN_TOKENS + 64,
+                                   max_context=seq + GEN_TOKENS + 64)
+    # Prefill + first token through the reference-facing call (also the e2e warm-up).
+    res = rt.run_vlm_decode_with_prompt(ids, pos, image_token, feats, max_tokens=GEN_TOKENS)
+    first, first_raw = res.generated_tokens[0], res.raw_top1_tokens[0]
+    n_tok = len(res.generated_tokens)
+
+    def one_step():
+        # Rewind to the prefilled state: length = prompt, history = prompt ids.
+        rt.set_length(seq)
+        rt.set_history(ids)
+        toks, _ = rt.generate(first, first_raw, GEN_TOKENS, PENALTY)
+        return toks
+
+    for _ in range(args.warmup):
+        toks = one_step()
+        assert toks == res.generated_tokens, "decode is not deterministic"
+    import torch
+    ext = torch.cuda.ExternalStream(rt.stream, device=local)
+    dist_barrier(world)
+    torch.cuda.synchronize(local)
+    with ClockSampler(local) as clocks:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(ext)
+        for _ in range(args.steps):
+            one_step()
+        e1.record(ext)
+        e1.synchronize()
+        torch.cuda.synchronize(local)
+        dist_barrier(world)
+    ms = e0.elapsed_time(e1)
+    ms_max = dist_max(ms, world)
+    decode_tokens = (n_tok - 1) * args.steps * world
+    value = decode_tokens / (ms_max / 1e3)
+
+    # Device-only decode loop without the host polling (graph replays back to back).
+    rt.set_length(seq)
+    rt.set_history(ids)
+    dev_ms = rt.bench_ar_steps(GEN_TOKENS - 1)
+
+    # e2e: reference-facing call with host buffers (prompt upload, prefill, 256 tokens, tokens back).
+    e2e_times = []
+    for _ in range(max(1, args.steps)):
+        t0 = time.perf_counter()
+        r2 = rt.run_vlm_decode_with_prompt(ids, pos, image_token, feats, max_tokens=GEN_TOKENS)
+        e2e_times.append(time.perf_counter() - t0)
+        assert r2.generated_tokens == res.generated_tokens
+    e2e_t = dist_max(max(e2e_times), world)
+    e2e_value = len(r2.generated_tokens) * world / e2e_t
+
+    # Roofline of the dominant GEMV launch: the LM head + argmax (494.9 MB streamed per launch).
+    peak, peak_kind = measured_peaks()
+    lm_ms = rt.bench_kernel(0, 20)
+    lm_gbs = LM_HEAD_BYTES / (lm_ms / 1e3) / 1e9
+    gu_ms = rt.bench_kernel(1, 20)
+    attn_ms = rt.bench_kernel(2, 50)
+    bpt = ar_bytes_per_token(seq, n_tok)
+    step_gbs = bpt * (n_tok - 1) * args.steps / (ms / 1e3) / 1e9
+    rt.close()
+    if rank != 0:
+        return None
+    cs = clocks.summary()
+    return {
+        "metric": "decode tokens/s (AR, bs=1, fp32)",
+        "value": round(value, 2),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_max / args.steps, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded random-init weights ~N(0,0.02); prompt 768 N(0,1) image rows + 256 text ids)",
+        "config": {"workload": "config0: 24-layer decoder, prompt 1024 (768 image rows on 24x32 mRoPE + 256 text), "
+                               "256 greedy tokens, penalty 1.08, fp32 weights+KV",
+                   "prompt": seq, "generated": n_tok, "parallelism": f"replicas x{world}",
+                   "l2": "weights 2.16 GB per token > 126 MB L2 (no flush needed)"},
+        "device_loop_tokens_per_s": round((GEN_TOKENS - 1) / (dev_ms / 1e3), 2),
+        "step_roofline": {"bytes_per_token": round(bpt), "achieved_gbs": round(step_gbs, 1),
+                          "peak_gbs": peak, "frac": round(step_gbs / peak, 4),
+                          "roofline_tokens_per_s": round(peak * 1e9 / bpt, 1)},
+        "roofline": {"bound": "hbm", "kernel": "gemv_kernel<f32,1024,1,NORM,ARGMAX> (LM head + penalised argmax)",
+                     "achieved": round(lm_gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(lm_gbs / peak, 4), "traffic": None, "peak_source": peak_kind,
+                     "bytes_per_launch": LM_HEAD_BYTES, "launch_us": round(lm_ms * 1e3, 2)},
+        "kernel_us": {"lm_head": round(lm_ms * 1e3, 2), "gate_up_gemv": round(gu_ms * 1e3, 2),
+                      "attention_l1024": round(attn_ms * 1e3, 2)},
+        "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "scope": "prefill + 256 tokens per call",
+                "h2d_bytes_per_step": int(ids.nbytes + pos.nbytes + feats.nbytes),
+                "d2h_bytes_per_step": int(2 * 4 * len(r2.generated_tokens))},
+        "gpu_launches": int(KERNELS_PER_AR_STEP * 4 * ((GEN_TOKENS - 1 + 3) // 4) * args.steps),
+        "clocks": cs,
+        "cpu_baseline": cpu_baseline(args) if (world == 1 and not args.no_cpu) else None,
+    }
+
+
+def cpu_decode_sample(steps: int, threads: int | None = None):
+    """Time the oracle's AR decode step at full size on a KV cache of 1024 rows."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("hy_oracle_build", os.path.join(REPO, "oracle", "build.py"))
+    ob = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ob)
+    ob.build()
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import hy_oracle as O
+    cfg = O.ModelConfig()
+    w = O.make_weights(cfg, 0)
+    seq = PROMPT_GRID[0] * PROMPT_GRID[1] + PROMPT_TEXT
+    cache = O.KVCache.empty(cfg.num_layers, seq + steps + 1)
+    rng = np.random.default_rng(0)
+    for li in range(cfg.num_layers):
+        cache.k[li][:, :seq] = rng.standard_normal((8, seq, 128), dtype=np.float32)
+        cache.v[li][:, :seq] = rng.standard_normal((8, seq, 128), dtype=np.float32)
+    cache.length = seq
+    history = list(range(0, 2 * seq, 2))
+    tok = 7
+    t0 = time.perf_counter()
+    for i in range(steps):
+        pos = seq + i
+        h, _ = O.decoder_forward(w, cfg, w.embed[tok:tok + 1], O.make_decode_mask(pos), O.rope_rows(pos, 1, True),
+                                 O.rope_rows(pos, 1, False), cache)
+        tok, _ = O.select_next_token(O.lm_head(w, h)[0], history, PENALTY)
+        history.append(tok)
+    dt = time.perf_counter() - t0
+    return steps / dt, dt
+
+
+def cpu_baseline(args):
+    steps = args.cpu_steps
+    tps, dt = cpu_decode_sample(steps)
+    return {"value": round(tps, 3), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{steps} AR decode steps of the config0 model at KV length 1024 (oracle/hy_oracle.py, "
+                      f"numpy fp32 GEMV + fp64 attention, {dt:.1f} s)"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return None
+    times = []
+    for _ in range(args.warmup):
+        cpu_decode_sample(2)
+    for _ in range(args.steps):
+        tps, dt = cpu_decode_sample(args.cpu_steps)
+        times.append(dt)
+    value = args.cpu_steps * args.steps / sum(times)
+    base = {"value": round(value, 3), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{args.cpu_steps} AR decode steps per step at KV length 1024, config0 model, "
+                      "oracle/hy_oracle.py (ncnn is not available to build the reference's own CPU path)"}
+    return {"impl": "reference", "metric": "decode tokens/s (AR, bs=1, fp32)", "value": base["value"],
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1e3 * sum(times) / len(times), 2), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config0 decode step, KV length 1024, host CPU"},
+            "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--cpu-steps", type=int, default=16)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+        out = run_reference(args, world, rank)
+    else:
+        world, rank, local = dist_setup(args.gpus)
+        out = run_b200(args, world, rank, local)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

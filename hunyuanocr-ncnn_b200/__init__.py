@@ -1,0 +1,398 @@
+"""Python host binding of the B200 text-decode library (ctypes over include/hy_decode.h).
+
+The library itself is C++/CUDA (``csrc/``), built in-tree into
+``libhy_decode.so``. This module only marshals numpy arrays across the C ABI
+and mirrors the names of the reference's text runtime
+(src/text_runtime.cpp, include/hunyuan_ocr/text_runtime.h) so that host code
+and tests read like the reference's: ``TextRuntime.run_vlm_decode_with_prompt``,
+``run_decoder_step``, ``select_logit_rows``, ``dflash_verify_block``.
+
+Errors follow the reference's convention of a message per failing call: a
+non-zero status raises ``HyError`` carrying ``hy_last_error()``. There is no
+CPU fallback: importing this module without the built library raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libhy_decode.so")
+
+HY_OK = 0
+HY_ERR_INVALID_ARGUMENT = 1
+HY_ERR_CUDA = 2
+HY_ERR_OUT_OF_MEMORY = 3
+HY_ERR_CAPACITY = 4
+HY_ERR_DEVICE_TIMEOUT = 5
+HY_ERR_NOT_READY = 6
+HY_ERR_UNSUPPORTED = 7
+DTYPE_F32 = 0
+DTYPE_BF16 = 1
+HIDDEN = 1024
+HEAD_DIM = 128
+QKV_WIDTH = 4096
+DFLASH_BLOCK = 16
+
+EXPORTED_SYMBOLS = (
+    "hy_version", "hy_last_error", "hy_config_init", "hy_ctx_create", "hy_ctx_create_synthetic",
+    "hy_ctx_destroy", "hy_ctx_config", "hy_ctx_device_bytes", "hy_build_mrope", "hy_rope_value",
+    "hy_seq_reset", "hy_seq_length", "hy_seq_truncate", "hy_history_set", "hy_history_add",
+    "hy_prefill", "hy_decoder_step", "hy_lm_head_select", "hy_generate", "hy_verify_block",
+    "hy_dflash_generate_synthetic", "hy_run_vlm_decode_with_prompt", "hy_attention", "hy_kv_write",
+    "hy_kv_read", "hy_seq_set_length", "hy_bench_ar_steps", "hy_bench_kernel", "hy_ctx_stream",
+)
+
+
+class HyError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"hy status {status}: {message}")
+        self.status = status
+        self.message = message
+
+
+class Config(ctypes.Structure):
+    _fields_ = [
+        ("num_layers", ctypes.c_int), ("vocab_size", ctypes.c_int), ("ffn_dim", ctypes.c_int),
+        ("max_context", ctypes.c_int), ("max_prefill", ctypes.c_int), ("max_tokens", ctypes.c_int),
+        ("weight_dtype", ctypes.c_int), ("kv_dtype", ctypes.c_int), ("rms_norm_eps", ctypes.c_float),
+        ("attn_scale", ctypes.c_float), ("device", ctypes.c_int),
+    ]
+
+
+class _LayerWeights(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in (
+        "input_norm", "q_proj", "k_proj", "v_proj", "query_norm", "key_norm", "o_proj", "post_norm",
+        "gate_proj", "up_proj", "down_proj")]
+
+
+class _Weights(ctypes.Structure):
+    _fields_ = [("embed", ctypes.c_void_p), ("final_norm", ctypes.c_void_p),
+                ("layers", ctypes.POINTER(_LayerWeights))]
+
+
+_LIB = None
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_F = ctypes.c_float
+
+
+def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load libhy_decode.so (raises if it has not been built)."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not os.path.exists(path):
+        raise ImportError(f"{path} is missing; build it with `python __graft_entry__.py build` "
+                          "(there is no CPU fallback for the decode path)")
+    lib = ctypes.CDLL(path)
+    sig = {
+        "hy_version": ([], ctypes.c_char_p),
+        "hy_last_error": ([], ctypes.c_char_p),
+        "hy_config_init": ([ctypes.POINTER(Config)], _I),
+        "hy_ctx_create": ([ctypes.POINTER(Config), ctypes.POINTER(_Weights), ctypes.POINTER(_P)], _I),
+        "hy_ctx_create_synthetic": ([ctypes.POINTER(Config), ctypes.c_uint64, _F, _F, ctypes.POINTER(_P)], _I),
+        "hy_ctx_destroy": ([_P], None),
+        "hy_ctx_config": ([_P, ctypes.POINTER(Config)], _I),
+        "hy_ctx_device_bytes": ([_P], ctypes.c_size_t),
+        "hy_ctx_stream": ([_P], _P),
+        "hy_build_mrope": ([_P, _I, _I, _P], _I),
+        "hy_rope_value": ([_I, _I, _I], _F),
+        "hy_seq_reset": ([_P], _I),
+        "hy_seq_length": ([_P, ctypes.POINTER(_I)], _I),
+        "hy_seq_truncate": ([_P, _I], _I),
+        "hy_seq_set_length": ([_P, _I], _I),
+        "hy_history_set": ([_P, _P, _I], _I),
+        "hy_history_add": ([_P, _P, _I], _I),
+        "hy_prefill": ([_P, _P, _P, _P, _I, _P, _P], _I),
+        "hy_decoder_step": ([_P, _P, _I, _P, _P, _P, _P], _I),
+        "hy_lm_head_select": ([_P, _P, _I, _P, _F, _P, _P, _P], _I),
+        "hy_generate": ([_P, _I, _I, _I, _F, _P, _I, _P, _P, ctypes.POINTER(_I)], _I),
+        "hy_verify_block": ([_P, _P, _I, _F, _P, _I, _P, ctypes.POINTER(_I), ctypes.POINTER(_I),
+                             ctypes.POINTER(_I)], _I),
+        "hy_dflash_generate_synthetic": ([_P, _I, _I, _F, _P, _I, _P, _I, _F, ctypes.c_uint64, _P,
+                                          ctypes.POINTER(_I), _P, ctypes.POINTER(_I)], _I),
+        "hy_run_vlm_decode_with_prompt": ([_P, _P, _P, _I, _I, _P, _I, _I, _F, _P, _I, _P, _P,
+                                           ctypes.POINTER(_I)], _I),
+        "hy_attention": ([_P, _I, _P, _I, _P, _P, _P], _I),
+        "hy_kv_write": ([_P, _I, _I, _I, _P, _P], _I),
+        "hy_kv_read": ([_P, _I, _I, _I, _P, _P], _I),
+        "hy_bench_ar_steps": ([_P, _I, ctypes.POINTER(_F)], _I),
+        "hy_bench_kernel": ([_P, _I, _I, ctypes.POINTER(_F)], _I),
+    }
+    for name, (argtypes, restype) in sig.items():
+        fn = getattr(lib, name)
+        fn.argtypes = argtypes
+        fn.restype = restype
+    _LIB = lib
+    return lib
+
+
+def _check(status: int) -> None:
+    if status != HY_OK:
+        raise HyError(status, _LIB.hy_last_error().decode(errors="replace"))
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _i32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.int32)
+
+
+def _ptr(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data
+
+
+def default_config(**overrides) -> Config:
+    lib = load_library()
+    cfg = Config()
+    _check(lib.hy_config_init(ctypes.byref(cfg)))
+    for k, v in overrides.items():
+        setattr(cfg, k, v)
+    return cfg
+
+
+def build_mrope(position_ids: np.ndarray, seq_len: int, use_cos: bool) -> np.ndarray:
+    """detail::build_mrope (src/text_runtime.cpp:42-63), evaluated by the library's host code."""
+    lib = load_library()
+    pos = _i32(position_ids).reshape(-1)
+    out = np.empty((seq_len, HEAD_DIM), np.float32)
+    _check(lib.hy_build_mrope(_ptr(pos), seq_len, int(use_cos), _ptr(out)))
+    return out
+
+
+def rope_rows(start: int, rows: int, use_cos: bool) -> np.ndarray:
+    """build_decode_rope / build_verify_rope (src/text_runtime.cpp:228-251) via rope_value."""
+    lib = load_library()
+    out = np.empty((rows, HEAD_DIM), np.float32)
+    for r in range(rows):
+        for d in range(HEAD_DIM):
+            out[r, d] = lib.hy_rope_value(start + r, d, int(use_cos))
+    return out
+
+
+@dataclass
+class TextDecodeResult:
+    """include/hunyuan_ocr/text_runtime.h:41-51 (the fields this path fills)."""
+    seq_len: int
+    repetition_penalty: float
+    generated_tokens: list
+    raw_top1_tokens: list
+
+
+@dataclass
+class DFlashDecodeResult:
+    """include/hunyuan_ocr/text_runtime.h:76-83."""
+    generated_tokens: list
+    block_count: int
+    drafted_token_count: int
+    accepted_draft_token_count: int
+    acceptance_lengths: list
+
+
+class TextRuntime:
+    """One device context: weights, KV cache and decode state on one GPU.
+
+    Mirrors hunyuan_ocr::TextRuntime (include/hunyuan_ocr/text_runtime.h:85-158)
+    for the text-decode path, over the C ABI in include/hy_decode.h.
+    """
+
+    def __init__(self, ctx, cfg: Config):
+        self._ctx = ctx
+        self.cfg = cfg
+
+    # -- construction ------------------------------------------------------
+    @classmethod
+    def synthetic(cls, seed: int = 0, std: float = 0.02, norm_std: float = 0.0, **cfg_overrides) -> "TextRuntime":
+        lib = load_library()
+        cfg = default_config(**cfg_overrides)
+        ctx = ctypes.c_void_p()
+        _check(lib.hy_ctx_create_synthetic(ctypes.byref(cfg), seed, std, norm_std, ctypes.byref(ctx)))
+        return cls(ctx, cfg)
+
+    @classmethod
+    def from_weights(cls, weights, **cfg_overrides) -> "TextRuntime":
+        """weights: an object with .embed, .final_norm and .layers[i].{input_norm, q, k, v, q_norm,
+        k_norm, o, post_norm, gate, up, down} numpy fp32 arrays (nn.Linear layout)."""
+        lib = load_library()
+        cfg = default_config(**cfg_overrides)
+        keep = []
+
+        def p(a):
+            a = _f32(a)
+            keep.append(a)
+            return a.ctypes.data
+
+        layers = (_LayerWeights * cfg.num_layers)()
+        for i, lw in enumerate(weights.layers[:cfg.num_layers]):
+            layers[i] = _LayerWeights(p(lw.input_norm), p(lw.q), p(lw.k), p(lw.v), p(lw.q_norm), p(lw.k_norm),
+                                      p(lw.o), p(lw.post_norm), p(lw.gate), p(lw.up), p(lw.down))
+        w = _Weights(p(weights.embed), p(weights.final_norm), layers)
+        ctx = ctypes.c_void_p()
+        _check(lib.hy_ctx_create(ctypes.byref(cfg), ctypes.byref(w), ctypes.byref(ctx)))
+        return cls(ctx, cfg)
+
+    def close(self) -> None:
+        if self._ctx:
+            _LIB.hy_ctx_destroy(self._ctx)
+            self._ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    @property
+    def device_bytes(self) -> int:
+        return int(_LIB.hy_ctx_device_bytes(self._ctx))
+
+    @property
+    def stream(self) -> int:
+        return int(_LIB.hy_ctx_stream(self._ctx) or 0)
+
+    # -- sequence state ----------------------------------------------------
+    def reset(self) -> None:
+        _check(_LIB.hy_seq_reset(self._ctx))
+
+    @property
+    def kv_length(self) -> int:
+        n = ctypes.c_int()
+        _check(_LIB.hy_seq_length(self._ctx, ctypes.byref(n)))
+        return n.value
+
+    def truncate(self, rows: int) -> None:
+        """view_dflash_rows (src/dflash_runtime.cpp:97-119)."""
+        _check(_LIB.hy_seq_truncate(self._ctx, rows))
+
+    def set_length(self, rows: int) -> None:
+        _check(_LIB.hy_seq_set_length(self._ctx, rows))
+
+    def set_history(self, ids) -> None:
+        a = _i32(ids)
+        _check(_LIB.hy_history_set(self._ctx, _ptr(a), a.size))
+
+    def add_history(self, ids) -> None:
+        a = _i32(ids)
+        _check(_LIB.hy_history_add(self._ctx, _ptr(a), a.size))
+
+    # -- decoder -----------------------------------------------------------
+    def prefill(self, inputs_embeds: np.ndarray, cos: np.ndarray, sin: np.ndarray) -> np.ndarray:
+        """run_decoder_prefill (src/text_runtime.cpp:648-674); returns the final-normed last hidden row."""
+        e, c, s = _f32(inputs_embeds), _f32(cos), _f32(sin)
+        out = np.empty(HIDDEN, np.float32)
+        _check(_LIB.hy_prefill(self._ctx, _ptr(e), _ptr(c), _ptr(s), e.shape[0], _ptr(out), None))
+        return out
+
+    def run_decoder_step(self, embeds: np.ndarray, cos: np.ndarray, sin: np.ndarray, aux: bool = False):
+        """detail::run_decoder_step (src/text_decoder_step.h:29-38): returns (hidden, aux_hidden|None)."""
+        e, c, s = _f32(embeds), _f32(cos), _f32(sin)
+        rows = e.shape[0]
+        hidden = np.empty((rows, HIDDEN), np.float32)
+        auxh = np.empty((4, rows, HIDDEN), np.float32) if aux else None
+        _check(_LIB.hy_decoder_step(self._ctx, _ptr(e), rows, _ptr(c), _ptr(s), _ptr(hidden), _ptr(auxh)))
+        return hidden, auxh
+
+    def select_logit_rows(self, hidden: np.ndarray, penalty: float, row_prefix=None, want_logits: bool = False):
+        """run_lm_head + select_logit_rows (src/text_runtime.cpp:430-439, 757-797) with the current history."""
+        h = _f32(hidden).reshape(-1, HIDDEN)
+        rows = h.shape[0]
+        tok = np.empty(rows, np.int32)
+        raw = np.empty(rows, np.int32)
+        pre = None if row_prefix is None else _i32(row_prefix)
+        logits = np.empty((rows, self.cfg.vocab_size), np.float32) if want_logits else None
+        _check(_LIB.hy_lm_head_select(self._ctx, _ptr(h), rows, _ptr(pre), penalty, _ptr(tok), _ptr(raw),
+                                      _ptr(logits)))
+        return tok, raw, logits
+
+    def attention(self, layer: int, qkv: np.ndarray, cos: np.ndarray, sin: np.ndarray) -> np.ndarray:
+        q, c, s = _f32(qkv), _f32(cos), _f32(sin)
+        rows = q.shape[0]
+        out = np.empty((rows, 2048), np.float32)
+        _check(_LIB.hy_attention(self._ctx, layer, _ptr(q), rows, _ptr(c), _ptr(s), _ptr(out)))
+        return out
+
+    def kv_write(self, layer: int, start: int, k: np.ndarray, v: np.ndarray) -> None:
+        k, v = _f32(k), _f32(v)
+        _check(_LIB.hy_kv_write(self._ctx, layer, start, k.shape[1], _ptr(k), _ptr(v)))
+
+    def kv_read(self, layer: int, start: int, rows: int):
+        k = np.empty((8, rows, HEAD_DIM), np.float32)
+        v = np.empty((8, rows, HEAD_DIM), np.float32)
+        _check(_LIB.hy_kv_read(self._ctx, layer, start, rows, _ptr(k), _ptr(v)))
+        return k, v
+
+    # -- loops -------------------------------------------------------------
+    def generate(self, first_token: int, first_raw: int, max_tokens: int, penalty: float, eos_ids=()):
+        eos = _i32(list(eos_ids)) if len(eos_ids) else None
+        tokens = np.empty(max_tokens, np.int32)
+        raw = np.empty(max_tokens, np.int32)
+        n = ctypes.c_int()
+        _check(_LIB.hy_generate(self._ctx, first_token, first_raw, max_tokens, penalty, _ptr(eos),
+                                0 if eos is None else eos.size, _ptr(tokens), _ptr(raw), ctypes.byref(n)))
+        return tokens[:n.value].tolist(), raw[:n.value].tolist()
+
+    def dflash_verify_block(self, proposed, max_commit: int, penalty: float, eos_ids=()):
+        p = _i32(proposed)
+        eos = _i32(list(eos_ids)) if len(eos_ids) else None
+        post = np.empty(DFLASH_BLOCK, np.int32)
+        acc, com, stop = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        _check(_LIB.hy_verify_block(self._ctx, _ptr(p), max_commit, penalty, _ptr(eos),
+                                    0 if eos is None else eos.size, _ptr(post), ctypes.byref(acc),
+                                    ctypes.byref(com), ctypes.byref(stop)))
+        return post.tolist(), acc.value, com.value, bool(stop.value)
+
+    def dflash_generate_synthetic(self, first_token: int, max_tokens: int, penalty: float, greedy, p: float,
+                                  seed: int, eos_ids=()) -> DFlashDecodeResult:
+        g = _i32(greedy)
+        eos = _i32(list(eos_ids)) if len(eos_ids) else None
+        tokens = np.empty(max_tokens, np.int32)
+        acc = np.empty(max_tokens + DFLASH_BLOCK, np.int32)
+        n, nb = ctypes.c_int(), ctypes.c_int()
+        _check(_LIB.hy_dflash_generate_synthetic(self._ctx, first_token, max_tokens, penalty, _ptr(eos),
+                                                 0 if eos is None else eos.size, _ptr(g), g.size, p, seed,
+                                                 _ptr(tokens), ctypes.byref(n), _ptr(acc), ctypes.byref(nb)))
+        accl = acc[:nb.value].tolist()
+        return DFlashDecodeResult(tokens[:n.value].tolist(), nb.value, nb.value * (DFLASH_BLOCK - 1),
+                                  int(sum(accl)), accl)
+
+    def run_vlm_decode_with_prompt(self, input_ids, position_ids, image_token_id: int, vision_features,
+                                   max_tokens: int, repetition_penalty: float = 1.08,
+                                   eos_ids=()) -> TextDecodeResult:
+        """TextRuntime::run_vlm_decode_with_prompt (src/text_runtime.cpp:2053-2094)."""
+        ids = _i32(input_ids)
+        pos = _i32(position_ids).reshape(-1)
+        feats = _f32(vision_features).reshape(-1, HIDDEN)
+        eos = _i32(list(eos_ids)) if len(eos_ids) else None
+        mt = max_tokens if max_tokens > 0 else 1024
+        tokens = np.empty(mt, np.int32)
+        raw = np.empty(mt, np.int32)
+        n = ctypes.c_int()
+        _check(_LIB.hy_run_vlm_decode_with_prompt(self._ctx, _ptr(ids), _ptr(pos), ids.size, image_token_id,
+                                                  _ptr(feats), feats.shape[0], max_tokens, repetition_penalty,
+                                                  _ptr(eos), 0 if eos is None else eos.size, _ptr(tokens),
+                                                  _ptr(raw), ctypes.byref(n)))
+        return TextDecodeResult(ids.size, repetition_penalty, tokens[:n.value].tolist(), raw[:n.value].tolist())
+
+    # -- timing hooks --------------------------------------------------------
+    def bench_ar_steps(self, count: int) -> float:
+        ms = ctypes.c_float()
+        _check(_LIB.hy_bench_ar_steps(self._ctx, count, ctypes.byref(ms)))
+        return ms.value
+
+    def bench_kernel(self, which: int, count: int) -> float:
+        ms = ctypes.c_float()
+        _check(_LIB.hy_bench_kernel(self._ctx, which, count, ctypes.byref(ms)))
+        return ms.value

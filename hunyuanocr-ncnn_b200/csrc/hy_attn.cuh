@@ -1,0 +1,380 @@
+// GQA decode/verify attention over the KV cache, split over the key axis
+// (flash-decode), with the per-head RoPE, QK RMSNorm and KV append fused into
+// the prologue.
+//
+// Replaces, for the decode and DFlash-verify steps:
+//   - MultimodalRotaryEmbed (src/multimodal_rope.cpp:176-187): full-width
+//     cos/sin, out[d] = x[d]c[d] - x[d+64]s[d], out[d+64] = x[d+64]c[d+64] + x[d]s[d+64];
+//   - query_layernorm / key_layernorm applied after RoPE (export/text_decoder_kv.py:70-73);
+//   - append_or_grow_kv_cache (src/kv_cache_capacity.cpp:232-280): rows are
+//     written in place into a cache reserved up front;
+//   - PreciseSDPA::forward (src/precise_sdpa.cpp:281-329): softmax(q k^T * scale + mask) v,
+//     here with fp32 accumulation and an online (max-rescaled) softmax. The
+//     mask is the one the reference builds: zeros for decode
+//     (src/text_runtime.cpp:221-226) and causal inside a verify block
+//     (src/dflash_runtime.cpp:60-76), i.e. row m sees keys <= past + m.
+//
+// The cache keeps the 8 unique KV heads, [8][capacity][128] per layer; q head
+// h reads KV head h / 2, which is what the reference's repeat_kv expansion to
+// 16 heads amounts to (export/text_decoder_kv.py:21-27).
+//
+// Grid (S, 8): split s < S-1 streams keys [s*chunk, ...) of the past rows
+// through a shared-memory ring with cp.async.bulk; split S-1 computes the new
+// rows (RoPE + norm), appends them and attends to them. Each CTA leaves a
+// partial (max, sum, acc[128]) per query; the last CTA of a head (atomic
+// ticket) merges the S partials into the output.
+//
+// Lane layout inside a warp: lane = (pg, qq, qr); qr = dim quarter (lowest two
+// bits), qq = query, pg = position subgroup. A lane owns the 32 dims
+// d = 4*(qr + 4j) + e (j < 8, e < 4), so the four quarters of a warp read
+// distinct bank groups of a K/V row and a score needs only two shuffles.
+#pragma once
+
+#include "hy_device.cuh"
+
+namespace hy {
+
+constexpr int kAttnWarps = 8;
+constexpr int kAttnThreads = (kAttnWarps + 1) * 32;
+constexpr int kAttnPos = 32;      // key positions per ring stage
+constexpr int kAttnStages = 3;
+constexpr int kPartStride = 132;  // (max, sum, -, -) + acc[128]
+
+struct AttnArgs {
+    const float* qkv;   // [rows x ldq]: q [0, 2048), k [2048, 3072), v [3072, 4096)
+    int ldq;
+    const float* qn_w;
+    const float* kn_w;
+    const float* cos;   // rope row = (rope_state ? kv_len : 0) + m, [.. x 128]
+    const float* sin;
+    int rope_state;
+    void* kc;           // this layer's K cache [8][cap][128] of KT
+    void* vc;
+    int cap;
+    const DecodeState* st;  // past = st->kv_len when st, else past_fixed
+    int past_fixed;
+    int rows;
+    float scale_log2;   // attention scale * log2(e)
+    float eps;
+    float* part;        // [8][S][2*MT][kPartStride]
+    int* counter;       // [8]
+    float* out;         // [rows x 2048]
+    int* err;
+};
+
+template <int MT, typename KT>
+struct AttnShape {
+    static constexpr int NQ = 2 * MT;                              // queries per KV head
+    static constexpr int ROWB = kHeadDim * static_cast<int>(sizeof(KT));
+    static constexpr int STAGE = 2 * kAttnPos * ROWB;               // K block then V block
+    static constexpr int QS_OFF = 0;                                // [NQ][128] f32
+    static constexpr int NEW_OFF = QS_OFF + NQ * kHeadDim * 4;      // K new [MT][128], V new [MT][128] f32
+    static constexpr int RING_OFF = NEW_OFF + 2 * MT * kHeadDim * 4;
+    static constexpr int NSTREAM = (MT == 1) ? 32 : 2;
+    // Per-stream softmax states reuse the ring once every stage has been consumed.
+    static constexpr int SCR_OFF = RING_OFF;   // [NSTREAM][NQ] (m, l), [NSTREAM][NQ][128] acc
+    static constexpr int SCR_BYTES = NSTREAM * NQ * 8 + NSTREAM * NQ * kHeadDim * 4;
+    static_assert(SCR_BYTES <= kAttnStages * STAGE, "scratch must fit in the ring");
+    static constexpr int BAR_OFF = RING_OFF + kAttnStages * STAGE;
+    static constexpr int SMEM = BAR_OFF + 2 * kAttnStages * 8 + 16;
+};
+
+__device__ __forceinline__ void attn_consumers_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// RoPE (full-width, non-interleaved) + RMSNorm of one 128-vector by one warp.
+// Lane l owns dims l, l+32, l+64, l+96.
+__device__ __forceinline__ void rope_norm_vec(const float* x, const float* c, const float* s, const float* w, float eps,
+                                              int lane, float out[4])
+{
+    const float x0 = x[lane], x1 = x[lane + 32], x2 = x[lane + 64], x3 = x[lane + 96];
+    float y0 = x0 * c[lane] - x2 * s[lane];
+    float y1 = x1 * c[lane + 32] - x3 * s[lane + 32];
+    float y2 = x2 * c[lane + 64] + x0 * s[lane + 64];
+    float y3 = x3 * c[lane + 96] + x1 * s[lane + 96];
+    const float ss = warp_sum(y0 * y0 + y1 * y1 + y2 * y2 + y3 * y3);
+    const float ri = 1.0f / sqrtf(ss / static_cast<float>(kHeadDim) + eps);
+    out[0] = w[lane] * (y0 * ri);
+    out[1] = w[lane + 32] * (y1 * ri);
+    out[2] = w[lane + 64] * (y2 * ri);
+    out[3] = w[lane + 96] * (y3 * ri);
+}
+
+template <int MT, typename KT>
+__global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const AttnArgs a)
+{
+    using S = AttnShape<MT, KT>;
+    constexpr int NQ = S::NQ, NSTREAM = S::NSTREAM, ROWB = S::ROWB, STAGE = S::STAGE;
+    extern __shared__ __align__(128) unsigned char smem[];
+    float* qs = reinterpret_cast<float*>(smem + S::QS_OFF);
+    float* knew = reinterpret_cast<float*>(smem + S::NEW_OFF);
+    float* vnew = knew + MT * kHeadDim;
+    unsigned char* ring = smem + S::RING_OFF;
+    float* scr_ml = reinterpret_cast<float*>(smem + S::SCR_OFF);       // [NSTREAM][NQ][2]
+    float* scr_acc = scr_ml + NSTREAM * NQ * 2;                        // [NSTREAM][NQ][128]
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
+    uint64_t* empty = full + kAttnStages;
+    __shared__ int s_last;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nsplit = gridDim.x, split = blockIdx.x, g = blockIdx.y;
+    const bool new_split = (split == nsplit - 1);
+    // Rows [0, past) were written by earlier steps, so they (and past itself)
+    // may be read before griddepcontrol.wait.
+    const int past = a.st ? a.st->kv_len : a.past_fixed;
+    const int rows = a.rows;
+    int p0 = 0, p1 = 0;
+    if (!new_split)
+    {
+        const int chunk = (past + nsplit - 2) / (nsplit - 1);
+        p0 = min(past, split * chunk);
+        p1 = min(past, p0 + chunk);
+    }
+    const int npos = p1 - p0;
+    const int nstage = (npos + kAttnPos - 1) / kAttnPos;
+
+    if (tid == 0)
+    {
+        for (int s = 0; s < kAttnStages; ++s)
+        {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kAttnWarps);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    const KT* kbase = static_cast<const KT*>(a.kc) + static_cast<size_t>(g) * a.cap * kHeadDim;
+    const KT* vbase = static_cast<const KT*>(a.vc) + static_cast<size_t>(g) * a.cap * kHeadDim;
+
+    if (warp == kAttnWarps)
+    {
+        // ---------------- producer: stream K/V rows [p0, p1) ----------------
+        if (lane == 0 && nstage > 0)
+        {
+            const uint64_t pol = l2_evict_first_policy();
+            int issued = 0;
+            for (int i = 0; i < nstage; ++i)
+            {
+                const int slot = i % kAttnStages;
+                if (i >= kAttnStages &&
+                    !mbar_wait(&empty[slot], ((i / kAttnStages) - 1) & 1, a.err, kErrTimeoutEmpty))
+                    break;
+                const int q0 = p0 + i * kAttnPos;
+                const int n = min(kAttnPos, p1 - q0);
+                const uint32_t bytes = static_cast<uint32_t>(n * ROWB);
+                mbar_arrive_expect_tx(&full[slot], 2 * bytes);
+                unsigned char* dst = ring + slot * STAGE;
+                bulk_g2s(dst, kbase + static_cast<size_t>(q0) * kHeadDim, bytes, &full[slot], pol);
+                bulk_g2s(dst + kAttnPos * ROWB, vbase + static_cast<size_t>(q0) * kHeadDim, bytes, &full[slot], pol);
+                issued = i + 1;
+            }
+            for (int i = (issued > kAttnStages ? issued - kAttnStages : 0); i < issued; ++i)
+                mbar_wait(&full[i % kAttnStages], (i / kAttnStages) & 1, a.err, kErrTimeoutFull);
+        }
+        return;
+    }
+
+    // ---------------- consumers ----------------
+    pdl_wait();
+
+    // Prologue: rotate + normalise the 2*MT queries (and, in the new-row split,
+    // the MT keys; values are copied), append the new rows to the cache.
+    const int nvec = new_split ? (NQ + 2 * MT) : NQ;
+    for (int v = warp; v < nvec; v += kAttnWarps)
+    {
+        int m, kind, head;
+        if (v < NQ) { kind = 0; head = v / MT; m = v % MT; }
+        else if (v < NQ + MT) { kind = 1; head = 0; m = v - NQ; }
+        else { kind = 2; head = 0; m = v - NQ - MT; }
+        float* dst = (kind == 0) ? (qs + v * kHeadDim) : (kind == 1 ? knew + m * kHeadDim : vnew + m * kHeadDim);
+        if (m >= rows)
+        {
+            for (int d = lane; d < kHeadDim; d += 32) dst[d] = 0.f;
+            continue;
+        }
+        const float* src = a.qkv + static_cast<size_t>(m) * a.ldq;
+        const int prow = (a.rope_state ? past : 0) + m;
+        const float* c = a.cos + static_cast<size_t>(prow) * kHeadDim;
+        const float* s = a.sin + static_cast<size_t>(prow) * kHeadDim;
+        if (kind == 0)
+        {
+            float o[4];
+            rope_norm_vec(src + (2 * g + head) * kHeadDim, c, s, a.qn_w, a.eps, lane, o);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = o[i] * a.scale_log2;
+        }
+        else if (kind == 1)
+        {
+            float o[4];
+            rope_norm_vec(src + kQWidth + g * kHeadDim, c, s, a.kn_w, a.eps, lane, o);
+            KT* krow = const_cast<KT*>(kbase) + static_cast<size_t>(past + m) * kHeadDim;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+            {
+                const KT q = from_f32<KT>(o[i]);
+                krow[lane + 32 * i] = q;
+                dst[lane + 32 * i] = to_f32<KT>(q);
+            }
+        }
+        else
+        {
+            const float* vsrc = src + kQWidth + kKVWidth + g * kHeadDim;
+            KT* vrow = const_cast<KT*>(vbase) + static_cast<size_t>(past + m) * kHeadDim;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+            {
+                const KT q = from_f32<KT>(vsrc[lane + 32 * i]);
+                vrow[lane + 32 * i] = q;
+                dst[lane + 32 * i] = to_f32<KT>(q);
+            }
+        }
+    }
+    attn_consumers_sync();
+    pdl_launch();
+
+    // Lane roles.
+    const int qr = lane & 3;
+    int qi, stream;
+    if (MT == 1)
+    {
+        qi = (lane >> 2) & 1;
+        stream = warp * 4 + (lane >> 3);
+    }
+    else
+    {
+        qi = (warp & 3) * 8 + (lane >> 2);
+        stream = warp >> 2;
+    }
+    const int qm = qi % MT;   // query row of this lane's query
+    float4 q4[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) q4[j] = *reinterpret_cast<const float4*>(qs + qi * kHeadDim + 4 * (qr + 4 * j));
+    float mx = -INFINITY, l = 0.f;
+    float4 acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+
+    // One key position for this lane's query; every lane of the warp calls it
+    // the same number of times (the shuffles use the full mask).
+    auto visit = [&](const auto* krow, const auto* vrow, bool visible) {
+        float sc = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) sc += dot4(q4[j], load4(krow + 4 * (qr + 4 * j)));
+        sc += __shfl_xor_sync(0xffffffffu, sc, 1);
+        sc += __shfl_xor_sync(0xffffffffu, sc, 2);
+        if (!visible) return;
+        const float mn = fmaxf(mx, sc);
+        const float corr = exp2f(mx - mn);
+        const float pe = exp2f(sc - mn);
+        l = l * corr + pe;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+        {
+            const float4 vv = load4(vrow + 4 * (qr + 4 * j));
+            acc[j].x = acc[j].x * corr + pe * vv.x;
+            acc[j].y = acc[j].y * corr + pe * vv.y;
+            acc[j].z = acc[j].z * corr + pe * vv.z;
+            acc[j].w = acc[j].w * corr + pe * vv.w;
+        }
+        mx = mn;
+    };
+
+    // Past rows from the ring.
+    for (int i = 0; i < nstage; ++i)
+    {
+        const int slot = i % kAttnStages;
+        const bool ok = mbar_wait(&full[slot], (i / kAttnStages) & 1, a.err, kErrTimeoutFull);
+        if (!__all_sync(0xffffffffu, ok)) break;
+        const KT* kst = reinterpret_cast<const KT*>(ring + slot * STAGE);
+        const KT* vst = reinterpret_cast<const KT*>(ring + slot * STAGE + kAttnPos * ROWB);
+        const int n = min(kAttnPos, npos - i * kAttnPos);
+        for (int jb = 0; jb < n; jb += NSTREAM)
+        {
+            const int j = jb + stream;
+            const int jj = (j < n) ? j : 0;
+            visit(kst + jj * kHeadDim, vst + jj * kHeadDim, j < n);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+    // New rows (causal inside the block: row m sees new row j iff j <= m).
+    if (new_split)
+    {
+        for (int jb = 0; jb < rows; jb += NSTREAM)
+        {
+            const int j = jb + stream;
+            const int jj = (j < rows) ? j : 0;
+            visit(knew + jj * kHeadDim, vnew + jj * kHeadDim, j < rows && j <= qm);
+        }
+    }
+
+    // Per-stream states to shared memory (aliasing the drained ring).
+    attn_consumers_sync();
+    if (qr == 0)
+    {
+        scr_ml[(stream * NQ + qi) * 2 + 0] = mx;
+        scr_ml[(stream * NQ + qi) * 2 + 1] = l;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        *reinterpret_cast<float4*>(scr_acc + (stream * NQ + qi) * kHeadDim + 4 * (qr + 4 * j)) = acc[j];
+    attn_consumers_sync();
+
+    // CTA partial per query.
+    float* part = a.part + (static_cast<size_t>(g) * nsplit + split) * NQ * kPartStride;
+    for (int e = tid; e < NQ * kHeadDim; e += 256)
+    {
+        const int q = e / kHeadDim, d = e % kHeadDim;
+        float M = -INFINITY;
+        for (int s = 0; s < NSTREAM; ++s) M = fmaxf(M, scr_ml[(s * NQ + q) * 2]);
+        float L = 0.f, A = 0.f;
+        if (M != -INFINITY)
+        {
+            for (int s = 0; s < NSTREAM; ++s)
+            {
+                const float ms = scr_ml[(s * NQ + q) * 2];
+                if (ms == -INFINITY) continue;
+                const float f = exp2f(ms - M);
+                L += f * scr_ml[(s * NQ + q) * 2 + 1];
+                A += f * scr_acc[(s * NQ + q) * kHeadDim + d];
+            }
+        }
+        if (d == 0)
+        {
+            part[q * kPartStride + 0] = M;
+            part[q * kPartStride + 1] = L;
+        }
+        part[q * kPartStride + 4 + d] = A;
+    }
+    __threadfence();
+    attn_consumers_sync();
+    if (tid == 0) s_last = (atomicAdd(&a.counter[g], 1) == nsplit - 1) ? 1 : 0;
+    attn_consumers_sync();
+    if (!s_last) return;
+    __threadfence();
+
+    // Last CTA of this head: merge the S partials.
+    const float* hp = a.part + static_cast<size_t>(g) * nsplit * NQ * kPartStride;
+    for (int e = tid; e < NQ * kHeadDim; e += 256)
+    {
+        const int q = e / kHeadDim, d = e % kHeadDim;
+        const int m = q % MT, head = q / MT;
+        if (m >= rows) continue;
+        float M = -INFINITY;
+        for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(hp + (s * NQ + q) * kPartStride));
+        float L = 0.f, A = 0.f;
+        for (int s = 0; s < nsplit; ++s)
+        {
+            const float* ps = hp + (s * NQ + q) * kPartStride;
+            const float ms = __ldcg(ps);
+            if (ms == -INFINITY) continue;
+            const float f = exp2f(ms - M);
+            L += f * __ldcg(ps + 1);
+            A += f * __ldcg(ps + 4 + d);
+        }
+        a.out[static_cast<size_t>(m) * kQWidth + (2 * g + head) * kHeadDim + d] = A / L;
+    }
+    if (tid == 0) a.counter[g] = 0;
+}
+
+}  // namespace hy

@@ -1,0 +1,1436 @@
+// C ABI of the B200 text-decode library (include/hy_decode.h): device context,
+// weight upload / synthetic generation, kernel launchers with programmatic
+// dependent launch, CUDA-graph capture of the AR step and of the DFlash verify
+// block, and the host loops that drive them.
+#include "hy_attn.cuh"
+#include "hy_device.cuh"
+#include "hy_gemv.cuh"
+#include "hy_util.cuh"
+
+#include "hy_decode.h"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+using namespace hy;
+
+namespace {
+
+thread_local std::string g_error;
+
+int fail(int code, const std::string& msg)
+{
+    g_error = msg;
+    return code;
+}
+
+#define HY_CUDA(call)                                                                          \
+    do {                                                                                       \
+        cudaError_t e_ = (call);                                                               \
+        if (e_ != cudaSuccess)                                                                 \
+            return fail(e_ == cudaErrorMemoryAllocation ? HY_ERR_OUT_OF_MEMORY : HY_ERR_CUDA,  \
+                        std::string(#call) + ": " + cudaGetErrorString(e_));                   \
+    } while (0)
+
+constexpr int kFfn = 3584;                // kernels are specialised for the model's FFN width
+constexpr int kAttnSplitsAR = 19;         // 18 past splits + the new-row split (152 CTAs)
+constexpr int kAttnSplitsVerify = 10;
+constexpr int kMaxSplits = 20;
+constexpr int kArStepsPerGraph = 4;
+constexpr unsigned long long kTidEmbed = 1, kTidFinalNorm = 2, kLayerTidBase = 100, kLayerTidStride = 16;
+constexpr unsigned long long kTidDrafts = 9003;
+enum { J_INPUT_NORM, J_Q, J_K, J_V, J_Q_NORM, J_K_NORM, J_O, J_POST_NORM, J_GATE, J_UP, J_DOWN };
+constexpr int kAuxLayerIds[kAuxLayers] = {1, 8, 15, 22};
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+float host_synth_mult(float std_dev) { return static_cast<float>(static_cast<double>(std_dev) * std::sqrt(3.0) / 65536.0); }
+
+}  // namespace
+
+struct hy_ctx {
+    hy_config cfg{};
+    cudaStream_t stream = nullptr;
+    int num_sms = 148;
+    size_t device_bytes = 0;
+    std::vector<void*> allocs;
+
+    // weights
+    void* embed = nullptr;                 // [V x 1024] WT
+    std::vector<void*> wqkv, wo, wgu, wd;  // per layer
+    float* norms = nullptr;                // per layer: input[1024], post[1024], qn[128], kn[128]; then final[1024]
+    // KV cache [layers][8][cap][128] KT
+    void* kc = nullptr;
+    void* vc = nullptr;
+    // rope (1-D) tables [max_context x 128]
+    float* rope_cos = nullptr;
+    float* rope_sin = nullptr;
+    float* pre_cos = nullptr;   // prefill / explicit-row tables [max(max_prefill,16) x 128]
+    float* pre_sin = nullptr;
+    float* prompt = nullptr;    // [max_prefill x 1024]
+    // step buffers
+    float* x = nullptr;         // [16 x 1024] residual stream
+    float* qkv = nullptr;       // [16 x 4096]
+    float* attn = nullptr;      // [16 x 2048]
+    float* gu = nullptr;        // [16 x 2 ffn]
+    float* tmp = nullptr;       // [16 x 1024]
+    float* hidden = nullptr;    // [16 x 1024]
+    float* aux = nullptr;       // [4 x 16 x 1024]
+    float* attn_part = nullptr;
+    int* attn_cnt = nullptr;    // [layers][8]
+    float4* lm_part = nullptr;  // [num_sms * 16]
+    int* lm_cnt = nullptr;
+    unsigned* hist = nullptr;   // [ceil(V/32)]
+    DecodeState* st = nullptr;
+    int* log_tokens = nullptr;
+    int* log_raw = nullptr;
+    int* accept_log = nullptr;
+    int* proposed = nullptr;    // [16]
+    int* posterior = nullptr;   // [16]
+    int* tok_out = nullptr;     // [16]
+    int* raw_out = nullptr;     // [16]
+    int* prefix = nullptr;      // [16]
+    int* greedy = nullptr;      // [max_tokens + 32]
+    int* ids_buf = nullptr;     // [max_prefill]
+    int* feat_idx = nullptr;    // [max_prefill]
+    float* feats = nullptr;     // vision features [max_prefill x 1024]
+    float* logits = nullptr;    // [16 x V] (lazily)
+    int* err = nullptr;
+    DecodeState* h_st = nullptr;  // pinned mirror
+    int kv_len = 0;               // host mirror of the sequence length
+
+    cudaGraphExec_t g_ar = nullptr;
+    cudaGraphExec_t g_verify_draft = nullptr;
+    cudaGraphExec_t g_verify_ids = nullptr;
+
+    size_t kv_elem() const { return cfg.kv_dtype == HY_DTYPE_BF16 ? 2 : 4; }
+    size_t w_elem() const { return cfg.weight_dtype == HY_DTYPE_BF16 ? 2 : 4; }
+    float* in_norm(int l) const { return norms + static_cast<size_t>(l) * 2304; }
+    float* post_norm(int l) const { return norms + static_cast<size_t>(l) * 2304 + 1024; }
+    float* qn(int l) const { return norms + static_cast<size_t>(l) * 2304 + 2048; }
+    float* kn(int l) const { return norms + static_cast<size_t>(l) * 2304 + 2176; }
+    float* final_norm() const { return norms + static_cast<size_t>(cfg.num_layers) * 2304; }
+    void* kc_layer(int l) const
+    {
+        return static_cast<char*>(kc) + static_cast<size_t>(l) * kNumKVHeads * cfg.max_context * kHeadDim * kv_elem();
+    }
+    void* vc_layer(int l) const
+    {
+        return static_cast<char*>(vc) + static_cast<size_t>(l) * kNumKVHeads * cfg.max_context * kHeadDim * kv_elem();
+    }
+};
+
+namespace {
+
+template <typename T>
+int dalloc(hy_ctx* c, T** p, size_t count)
+{
+    void* v = nullptr;
+    const size_t bytes = align_up(std::max<size_t>(count * sizeof(T), 16), 256);
+    cudaError_t e = cudaMalloc(&v, bytes);
+    if (e != cudaSuccess)
+        return fail(HY_ERR_OUT_OF_MEMORY, "cudaMalloc(" + std::to_string(bytes) + " bytes) failed: " + cudaGetErrorString(e));
+    c->allocs.push_back(v);
+    c->device_bytes += bytes;
+    *p = static_cast<T*>(v);
+    return HY_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Launch helpers.
+// ---------------------------------------------------------------------------
+// Every decode kernel is launched with programmatic stream serialization: its
+// producer warp may start streaming weights while the previous kernel drains;
+// its consumers wait with griddepcontrol.wait. `pdl` is false for a kernel
+// that follows a copy in the stream.
+thread_local bool t_next_plain = false;
+
+template <typename Kern, typename Args>
+cudaError_t launch_pdl(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, const Args& args)
+{
+    const bool pdl = !t_next_plain;
+    t_next_plain = false;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, args);
+}
+
+template <typename WT, int KP, int MT, int PRO, int EPI>
+cudaError_t run_gemv(hy_ctx* c, const GemvArgs& a)
+{
+    using S = GemvShape<WT, KP, MT>;
+    auto k = gemv_kernel<WT, KP, MT, PRO, EPI>;
+    static unsigned long long configured = 0;  // per instantiation, one bit per device
+    const unsigned long long bit = 1ull << (c->cfg.device & 63);
+    if (!(configured & bit))
+    {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
+        if (e != cudaSuccess) return e;
+        configured |= bit;
+    }
+    return launch_pdl(k, dim3(c->num_sms), dim3(kGemvThreads), S::SMEM, c->stream, a);
+}
+
+template <int MT, typename KT>
+cudaError_t run_attn(hy_ctx* c, const AttnArgs& a, int splits)
+{
+    using S = AttnShape<MT, KT>;
+    auto k = attn_kernel<MT, KT>;
+    static unsigned long long configured = 0;
+    const unsigned long long bit = 1ull << (c->cfg.device & 63);
+    if (!(configured & bit))
+    {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
+        if (e != cudaSuccess) return e;
+        configured |= bit;
+    }
+    return launch_pdl(k, dim3(splits, kNumKVHeads), dim3(kAttnThreads), S::SMEM, c->stream, a);
+}
+
+// How the first layer's input rows are produced.
+struct StepSource {
+    int src;          // SRC_X (ctx->x already holds the rows) or a gather mode
+    const int* ids;   // SRC_GATHER_IDS
+};
+
+struct StepPlan {
+    int rows;          // active rows (1..16)
+    StepSource source;
+    const float* cos;  // rope tables and indexing
+    const float* sin;
+    int rope_state;
+    bool past_from_state;
+    int past_fixed;
+    int lm_mode;       // -1: no LM head; else LM_* with PRO_NORM on x
+    float** aux;       // optional [4] aux outputs (row stride 1024), nullable
+};
+
+GemvArgs base_args(hy_ctx* c)
+{
+    GemvArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.eps = c->cfg.rms_norm_eps;
+    a.st = c->st;
+    a.vocab = c->cfg.vocab_size;
+    a.err = c->err;
+    a.table = c->embed;
+    a.hist = c->hist;
+    a.part = c->lm_part;
+    a.counter = c->lm_cnt;
+    return a;
+}
+
+template <typename WT, typename KT, int MT>
+cudaError_t enqueue_step_t(hy_ctx* c, const StepPlan& p)
+{
+    const hy_config& cfg = c->cfg;
+    const int ffn = cfg.ffn_dim;
+    cudaError_t e = cudaSuccess;
+    for (int l = 0; l < cfg.num_layers; ++l)
+    {
+        // q/k/v projections with the input RMSNorm (and, on layer 0, the embedding gather).
+        GemvArgs q = base_args(c);
+        q.W = c->wqkv[l];
+        q.N = kQKVRows;
+        q.ldw = kHidden;
+        q.rows = p.rows;
+        q.src = (l == 0) ? p.source.src : SRC_X;
+        q.ids = p.source.ids;
+        q.ids_out = (l == 0 && p.source.src == SRC_GATHER_DRAFT) ? c->proposed : nullptr;
+        q.greedy = c->greedy;
+        q.x_store = c->x;
+        q.x = c->x;
+        q.ldx = kHidden;
+        q.norm_w = c->in_norm(l);
+        q.out = c->qkv;
+        q.ldo = kQKVRows;
+        if ((e = run_gemv<WT, kHidden, MT, PRO_NORM, EPI_STORE>(c, q)) != cudaSuccess) return e;
+
+        AttnArgs at;
+        std::memset(&at, 0, sizeof(at));
+        at.qkv = c->qkv;
+        at.ldq = kQKVRows;
+        at.qn_w = c->qn(l);
+        at.kn_w = c->kn(l);
+        at.cos = p.cos;
+        at.sin = p.sin;
+        at.rope_state = p.rope_state;
+        at.kc = c->kc_layer(l);
+        at.vc = c->vc_layer(l);
+        at.cap = cfg.max_context;
+        at.st = p.past_from_state ? c->st : nullptr;
+        at.past_fixed = p.past_fixed;
+        at.rows = p.rows;
+        at.scale_log2 = cfg.attn_scale * 1.4426950408889634f;
+        at.eps = cfg.rms_norm_eps;
+        at.part = c->attn_part;
+        at.counter = c->attn_cnt + l * kNumKVHeads;
+        at.out = c->attn;
+        at.err = c->err;
+        if ((e = run_attn<MT, KT>(c, at, MT == 1 ? kAttnSplitsAR : kAttnSplitsVerify)) != cudaSuccess) return e;
+
+        GemvArgs o = base_args(c);
+        o.W = c->wo[l];
+        o.N = kHidden;
+        o.ldw = kQWidth;
+        o.rows = p.rows;
+        o.src = SRC_X;
+        o.x = c->attn;
+        o.ldx = kQWidth;
+        o.out = c->x;
+        o.ldo = kHidden;
+        if ((e = run_gemv<WT, kQWidth, MT, PRO_PLAIN, EPI_RESID>(c, o)) != cudaSuccess) return e;
+
+        GemvArgs gu = base_args(c);
+        gu.W = c->wgu[l];
+        gu.N = 2 * ffn;
+        gu.ldw = kHidden;
+        gu.rows = p.rows;
+        gu.src = SRC_X;
+        gu.x = c->x;
+        gu.ldx = kHidden;
+        gu.norm_w = c->post_norm(l);
+        gu.out = c->gu;
+        gu.ldo = 2 * ffn;
+        if ((e = run_gemv<WT, kHidden, MT, PRO_NORM, EPI_STORE>(c, gu)) != cudaSuccess) return e;
+
+        float* aux = nullptr;
+        if (p.aux)
+            for (int i = 0; i < kAuxLayers; ++i)
+                if (kAuxLayerIds[i] == l) aux = p.aux[i];
+        GemvArgs d = base_args(c);
+        d.W = c->wd[l];
+        d.N = kHidden;
+        d.ldw = ffn;
+        d.rows = p.rows;
+        d.src = SRC_X;
+        d.x = c->gu;
+        d.ldx = 2 * ffn;
+        d.up_off = ffn;
+        if constexpr (MT == 1)
+        {
+            d.out = c->x;
+            d.ldo = kHidden;
+            d.aux = aux;
+            d.ld_aux = kHidden;
+            if ((e = run_gemv<WT, kFfn, MT, PRO_SWIGLU, EPI_RESID>(c, d)) != cudaSuccess) return e;
+        }
+        else
+        {
+            // K split in two halves so the 16 activation rows fit in shared memory.
+            GemvArgs d1 = d;
+            d1.k_off = 0;
+            d1.out = c->tmp;
+            d1.ldo = kHidden;
+            if ((e = run_gemv<WT, kFfn / 2, MT, PRO_SWIGLU, EPI_STORE>(c, d1)) != cudaSuccess) return e;
+            GemvArgs d2 = d;
+            d2.k_off = kFfn / 2;
+            d2.out = c->x;
+            d2.ldo = kHidden;
+            d2.extra = c->tmp;
+            d2.aux = aux;
+            d2.ld_aux = kHidden;
+            if ((e = run_gemv<WT, kFfn / 2, MT, PRO_SWIGLU, EPI_RESID>(c, d2)) != cudaSuccess) return e;
+        }
+    }
+    if (p.lm_mode >= 0)
+    {
+        GemvArgs lm = base_args(c);
+        lm.W = c->embed;
+        lm.N = cfg.vocab_size;
+        lm.ldw = kHidden;
+        lm.rows = p.rows;
+        lm.src = SRC_X;
+        lm.x = c->x;
+        lm.ldx = kHidden;
+        lm.norm_w = c->final_norm();
+        lm.lm_mode = p.lm_mode;
+        lm.prefix = (p.lm_mode == LM_VERIFY) ? c->proposed : nullptr;
+        lm.tok_out = c->tok_out;
+        lm.raw_out = c->raw_out;
+        lm.log_tokens = c->log_tokens;
+        lm.log_raw = c->log_raw;
+        lm.accept_log = c->accept_log;
+        lm.posterior_out = c->posterior;
+        if ((e = run_gemv<WT, kHidden, MT, PRO_NORM, EPI_ARGMAX>(c, lm)) != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+cudaError_t enqueue_step(hy_ctx* c, const StepPlan& p)
+{
+    const bool wb = c->cfg.weight_dtype == HY_DTYPE_BF16, kb = c->cfg.kv_dtype == HY_DTYPE_BF16;
+    const bool one = p.rows == 1;
+    if (!wb && !kb) return one ? enqueue_step_t<float, float, 1>(c, p) : enqueue_step_t<float, float, 16>(c, p);
+    if (!wb && kb)
+        return one ? enqueue_step_t<float, __nv_bfloat16, 1>(c, p) : enqueue_step_t<float, __nv_bfloat16, 16>(c, p);
+    if (wb && !kb)
+        return one ? enqueue_step_t<__nv_bfloat16, float, 1>(c, p) : enqueue_step_t<__nv_bfloat16, float, 16>(c, p);
+    return one ? enqueue_step_t<__nv_bfloat16, __nv_bfloat16, 1>(c, p)
+               : enqueue_step_t<__nv_bfloat16, __nv_bfloat16, 16>(c, p);
+}
+
+// LM head + selection over rows of ctx->x that are already final-normed.
+template <typename WT, int MT>
+cudaError_t enqueue_lm_select_t(hy_ctx* c, int rows, const float* x, float penalty, bool with_prefix, float* logits)
+{
+    GemvArgs lm = base_args(c);
+    lm.W = c->embed;
+    lm.N = c->cfg.vocab_size;
+    lm.ldw = kHidden;
+    lm.rows = rows;
+    lm.src = SRC_X;
+    lm.x = x;
+    lm.ldx = kHidden;
+    lm.lm_mode = LM_NONE;
+    lm.penalty = penalty;
+    lm.prefix = with_prefix ? c->prefix : nullptr;
+    lm.logits = logits;
+    lm.ldl = c->cfg.vocab_size;
+    lm.tok_out = c->tok_out;
+    lm.raw_out = c->raw_out;
+    return run_gemv<WT, kHidden, MT, PRO_PLAIN, EPI_ARGMAX>(c, lm);
+}
+
+cudaError_t enqueue_lm_select(hy_ctx* c, int rows, const float* x, float penalty, bool with_prefix, float* logits)
+{
+    if (c->cfg.weight_dtype == HY_DTYPE_BF16)
+        return rows == 1 ? enqueue_lm_select_t<__nv_bfloat16, 1>(c, rows, x, penalty, with_prefix, logits)
+                         : enqueue_lm_select_t<__nv_bfloat16, 16>(c, rows, x, penalty, with_prefix, logits);
+    return rows == 1 ? enqueue_lm_select_t<float, 1>(c, rows, x, penalty, with_prefix, logits)
+                     : enqueue_lm_select_t<float, 16>(c, rows, x, penalty, with_prefix, logits);
+}
+
+int check_device_error(hy_ctx* c)
+{
+    int h = 0;
+    HY_CUDA(cudaMemcpyAsync(&h, c->err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    HY_CUDA(cudaStreamSynchronize(c->stream));
+    if (h != 0)
+    {
+        HY_CUDA(cudaMemsetAsync(c->err, 0, sizeof(int), c->stream));
+        HY_CUDA(cudaStreamSynchronize(c->stream));
+        if (h & (kErrTimeoutFull | kErrTimeoutEmpty))
+            return fail(HY_ERR_DEVICE_TIMEOUT, "a device-side bounded wait timed out (error bits " + std::to_string(h) + ")");
+        return fail(HY_ERR_INVALID_ARGUMENT, "device-side bounds check failed (error bits " + std::to_string(h) + ")");
+    }
+    return HY_OK;
+}
+
+int sync_state_to_host(hy_ctx* c)
+{
+    HY_CUDA(cudaMemcpyAsync(c->h_st, c->st, sizeof(DecodeState), cudaMemcpyDeviceToHost, c->stream));
+    HY_CUDA(cudaStreamSynchronize(c->stream));
+    c->kv_len = c->h_st->kv_len;
+    return HY_OK;
+}
+
+int push_state(hy_ctx* c)
+{
+    HY_CUDA(cudaMemcpyAsync(c->st, c->h_st, sizeof(DecodeState), cudaMemcpyHostToDevice, c->stream));
+    HY_CUDA(cudaStreamSynchronize(c->stream));
+    return HY_OK;
+}
+
+int set_eos(hy_ctx* c, const int* eos_ids, int n_eos)
+{
+    if (n_eos < 0 || n_eos > kMaxEos || (n_eos > 0 && !eos_ids))
+        return fail(HY_ERR_INVALID_ARGUMENT, "at most " + std::to_string(kMaxEos) + " EOS ids are supported");
+    c->h_st->n_eos = n_eos;
+    for (int i = 0; i < n_eos; ++i) c->h_st->eos[i] = eos_ids[i];
+    return HY_OK;
+}
+
+int capture(hy_ctx* c, cudaGraphExec_t* out, const StepPlan& p, int repeats)
+{
+    cudaGraph_t graph = nullptr;
+    HY_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    cudaError_t e = cudaSuccess;
+    for (int i = 0; i < repeats && e == cudaSuccess; ++i) e = enqueue_step(c, p);
+    cudaError_t e2 = cudaStreamEndCapture(c->stream, &graph);
+    if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+    if (e2 != cudaSuccess) return fail(HY_ERR_CUDA, std::string("graph capture end: ") + cudaGetErrorString(e2));
+    e = cudaGraphInstantiate(out, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+    return HY_OK;
+}
+
+int ensure_graphs(hy_ctx* c)
+{
+    if (!c->g_ar)
+    {
+        StepPlan p{};
+        p.rows = 1;
+        p.source.src = SRC_GATHER_STATE;
+        p.cos = c->rope_cos;
+        p.sin = c->rope_sin;
+        p.rope_state = 1;
+        p.past_from_state = true;
+        p.lm_mode = LM_AR;
+        int rc = capture(c, &c->g_ar, p, kArStepsPerGraph);
+        if (rc) return rc;
+    }
+    if (!c->g_verify_draft)
+    {
+        StepPlan p{};
+        p.rows = kBlock;
+        p.source.src = SRC_GATHER_DRAFT;
+        p.cos = c->rope_cos;
+        p.sin = c->rope_sin;
+        p.rope_state = 1;
+        p.past_from_state = true;
+        p.lm_mode = LM_VERIFY;
+        int rc = capture(c, &c->g_verify_draft, p, 1);
+        if (rc) return rc;
+    }
+    if (!c->g_verify_ids)
+    {
+        StepPlan p{};
+        p.rows = kBlock;
+        p.source.src = SRC_GATHER_IDS;
+        p.source.ids = c->proposed;
+        p.cos = c->rope_cos;
+        p.sin = c->rope_sin;
+        p.rope_state = 1;
+        p.past_from_state = true;
+        p.lm_mode = LM_VERIFY;
+        int rc = capture(c, &c->g_verify_ids, p, 1);
+        if (rc) return rc;
+    }
+    return HY_OK;
+}
+
+// rope_value (src/text_runtime.cpp:182-193), in the reference's float arithmetic.
+float rope_value_host(int position, int dim, bool use_cos)
+{
+    const float base = static_cast<float>(10000.0 * std::pow(1000.0, 128.0 / 126.0));
+    const int half_dim = dim % (kHeadDim / 2);
+    const float exponent = static_cast<float>(2 * half_dim) / static_cast<float>(kHeadDim);
+    const float inv_freq = 1.0f / std::pow(base, exponent);
+    const float angle = static_cast<float>(position) * inv_freq;
+    return use_cos ? std::cos(angle) : std::sin(angle);
+}
+
+int validate_config(const hy_config* cfg)
+{
+    if (!cfg) return fail(HY_ERR_INVALID_ARGUMENT, "config is null");
+    if (cfg->num_layers <= 0 || cfg->num_layers > 64) return fail(HY_ERR_INVALID_ARGUMENT, "num_layers must be in 1..64");
+    if (cfg->vocab_size < 16 || cfg->vocab_size > (1 << 24)) return fail(HY_ERR_INVALID_ARGUMENT, "vocab_size out of range");
+    if (cfg->ffn_dim != kFfn) return fail(HY_ERR_UNSUPPORTED, "ffn_dim must be 3584 (kernels are specialised for it)");
+    if (cfg->max_context < 32 || cfg->max_context > (1 << 20))
+        return fail(HY_ERR_INVALID_ARGUMENT, "max_context out of range");
+    if (cfg->max_prefill < 1 || cfg->max_prefill > cfg->max_context)
+        return fail(HY_ERR_INVALID_ARGUMENT, "max_prefill must be in 1..max_context");
+    if (cfg->max_tokens < 1) return fail(HY_ERR_INVALID_ARGUMENT, "max_tokens must be positive");
+    if ((cfg->weight_dtype != HY_DTYPE_F32 && cfg->weight_dtype != HY_DTYPE_BF16) ||
+        (cfg->kv_dtype != HY_DTYPE_F32 && cfg->kv_dtype != HY_DTYPE_BF16))
+        return fail(HY_ERR_INVALID_ARGUMENT, "dtype must be HY_DTYPE_F32 or HY_DTYPE_BF16");
+    if (!(cfg->rms_norm_eps > 0.f) || !(cfg->attn_scale > 0.f)) return fail(HY_ERR_INVALID_ARGUMENT, "eps/scale must be positive");
+    return HY_OK;
+}
+
+int alloc_ctx(hy_ctx* c)
+{
+    const hy_config& cfg = c->cfg;
+    HY_CUDA(cudaSetDevice(cfg.device));
+    HY_CUDA(cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, cfg.device));
+    HY_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    const size_t we = c->w_elem();
+    const int L = cfg.num_layers, ffn = cfg.ffn_dim;
+    int rc;
+    unsigned char* wbytes = nullptr;
+    const size_t per_layer = align_up(static_cast<size_t>(kQKVRows) * kHidden * we, 256) +
+                             align_up(static_cast<size_t>(kHidden) * kQWidth * we, 256) +
+                             align_up(static_cast<size_t>(2 * ffn) * kHidden * we, 256) +
+                             align_up(static_cast<size_t>(kHidden) * ffn * we, 256);
+    const size_t embed_bytes = align_up(static_cast<size_t>(cfg.vocab_size) * kHidden * we, 256);
+    if ((rc = dalloc(c, &wbytes, embed_bytes + per_layer * L))) return rc;
+    c->embed = wbytes;
+    unsigned char* p = wbytes + embed_bytes;
+    for (int l = 0; l < L; ++l)
+    {
+        c->wqkv.push_back(p);
+        p += align_up(static_cast<size_t>(kQKVRows) * kHidden * we, 256);
+        c->wo.push_back(p);
+        p += align_up(static_cast<size_t>(kHidden) * kQWidth * we, 256);
+        c->wgu.push_back(p);
+        p += align_up(static_cast<size_t>(2 * ffn) * kHidden * we, 256);
+        c->wd.push_back(p);
+        p += align_up(static_cast<size_t>(kHidden) * ffn * we, 256);
+    }
+    if ((rc = dalloc(c, &c->norms, static_cast<size_t>(L) * 2304 + kHidden))) return rc;
+    const size_t kv_count = static_cast<size_t>(L) * kNumKVHeads * cfg.max_context * kHeadDim;
+    unsigned char* kvb = nullptr;
+    if ((rc = dalloc(c, &kvb, kv_count * c->kv_elem()))) return rc;
+    c->kc = kvb;
+    if ((rc = dalloc(c, &kvb, kv_count * c->kv_elem()))) return rc;
+    c->vc = kvb;
+    HY_CUDA(cudaMemsetAsync(c->kc, 0, kv_count * c->kv_elem(), c->stream));
+    HY_CUDA(cudaMemsetAsync(c->vc, 0, kv_count * c->kv_elem(), c->stream));
+    const size_t rope_rows = static_cast<size_t>(cfg.max_context);
+    if ((rc = dalloc(c, &c->rope_cos, rope_rows * kHeadDim))) return rc;
+    if ((rc = dalloc(c, &c->rope_sin, rope_rows * kHeadDim))) return rc;
+    const size_t pre_rows = static_cast<size_t>(std::max(cfg.max_prefill, kMaxStepRows));
+    if ((rc = dalloc(c, &c->pre_cos, pre_rows * kHeadDim))) return rc;
+    if ((rc = dalloc(c, &c->pre_sin, pre_rows * kHeadDim))) return rc;
+    if ((rc = dalloc(c, &c->prompt, pre_rows * kHidden))) return rc;
+    if ((rc = dalloc(c, &c->feats, pre_rows * kHidden))) return rc;
+    if ((rc = dalloc(c, &c->ids_buf, pre_rows))) return rc;
+    if ((rc = dalloc(c, &c->feat_idx, pre_rows))) return rc;
+    if ((rc = dalloc(c, &c->x, kMaxStepRows * kHidden))) return rc;
+    if ((rc = dalloc(c, &c->qkv, kMaxStepRows * kQKVRows))) return rc;
+    if ((rc = dalloc(c, &c->attn, kMaxStepRows * kQWidth))) return rc;
+    if ((rc = dalloc(c, &c->gu, static_cast<size_t>(kMaxStepRows) * 2 * ffn))) return rc;
+    if ((rc = dalloc(c, &c->tmp, kMaxStepRows * kHidden))) return rc;
+    if ((rc = dalloc(c, &c->hidden, kMaxStepRows * kHidden))) return rc;
+    if ((rc = dalloc(c, &c->aux, static_cast<size_t>(kAuxLayers) * kMaxStepRows * kHidden))) return rc;
+    if ((rc = dalloc(c, &c->attn_part, static_cast<size_t>(kNumKVHeads) * kMaxSplits * 2 * kMaxStepRows * kPartStride)))
+        return rc;
+    if ((rc = dalloc(c, &c->attn_cnt, static_cast<size_t>(L) * kNumKVHeads))) return rc;
+    if ((rc = dalloc(c, &c->lm_part, static_cast<size_t>(c->num_sms) * kMaxStepRows))) return rc;
+    if ((rc = dalloc(c, &c->lm_cnt, 1))) return rc;
+    if ((rc = dalloc(c, &c->hist, (static_cast<size_t>(cfg.vocab_size) + 31) / 32))) return rc;
+    if ((rc = dalloc(c, &c->st, 1))) return rc;
+    const size_t ntok = static_cast<size_t>(cfg.max_tokens) + 2 * kBlock;
+    if ((rc = dalloc(c, &c->log_tokens, ntok))) return rc;
+    if ((rc = dalloc(c, &c->log_raw, ntok))) return rc;
+    if ((rc = dalloc(c, &c->accept_log, ntok))) return rc;
+    if ((rc = dalloc(c, &c->greedy, ntok))) return rc;
+    if ((rc = dalloc(c, &c->proposed, kBlock))) return rc;
+    if ((rc = dalloc(c, &c->posterior, kBlock))) return rc;
+    if ((rc = dalloc(c, &c->tok_out, kBlock))) return rc;
+    if ((rc = dalloc(c, &c->raw_out, kBlock))) return rc;
+    if ((rc = dalloc(c, &c->prefix, kBlock))) return rc;
+    if ((rc = dalloc(c, &c->err, 1))) return rc;
+    HY_CUDA(cudaMemsetAsync(c->attn_cnt, 0, sizeof(int) * L * kNumKVHeads, c->stream));
+    HY_CUDA(cudaMemsetAsync(c->lm_cnt, 0, sizeof(int), c->stream));
+    HY_CUDA(cudaMemsetAsync(c->err, 0, sizeof(int), c->stream));
+    HY_CUDA(cudaMemsetAsync(c->hist, 0, sizeof(unsigned) * ((cfg.vocab_size + 31) / 32), c->stream));
+    HY_CUDA(cudaMemsetAsync(c->proposed, 0, sizeof(int) * kBlock, c->stream));
+    HY_CUDA(cudaMemsetAsync(c->prefix, 0xff, sizeof(int) * kBlock, c->stream));
+    HY_CUDA(cudaMallocHost(reinterpret_cast<void**>(&c->h_st), sizeof(DecodeState)));
+    std::memset(c->h_st, 0, sizeof(DecodeState));
+    c->h_st->penalty = 1.08f;
+    if ((rc = push_state(c))) return rc;
+
+    // 1-D RoPE table for decode / verify positions.
+    std::vector<float> cs(rope_rows * kHeadDim), sn(rope_rows * kHeadDim);
+    float inv[kHeadDim];
+    {
+        const float base = static_cast<float>(10000.0 * std::pow(1000.0, 128.0 / 126.0));
+        for (int d = 0; d < kHeadDim; ++d)
+            inv[d] = 1.0f / std::pow(base, static_cast<float>(2 * (d % (kHeadDim / 2))) / static_cast<float>(kHeadDim));
+    }
+    for (size_t pos = 0; pos < rope_rows; ++pos)
+        for (int d = 0; d < kHeadDim; ++d)
+        {
+            const float angle = static_cast<float>(static_cast<int>(pos)) * inv[d];
+            cs[pos * kHeadDim + d] = std::cos(angle);
+            sn[pos * kHeadDim + d] = std::sin(angle);
+        }
+    HY_CUDA(cudaMemcpy(c->rope_cos, cs.data(), cs.size() * sizeof(float), cudaMemcpyHostToDevice));
+    HY_CUDA(cudaMemcpy(c->rope_sin, sn.data(), sn.size() * sizeof(float), cudaMemcpyHostToDevice));
+    return HY_OK;
+}
+
+template <typename WT>
+void launch_synth(WT* out, size_t count, unsigned long long seed, unsigned long long tid, float std_dev, float offset,
+                  cudaStream_t s)
+{
+    synth_fill_kernel<WT><<<1184, 256, 0, s>>>(out, count, synth_base(seed, tid), host_synth_mult(std_dev), offset);
+}
+
+int fill_synthetic(hy_ctx* c, unsigned long long seed, float std_dev, float norm_std)
+{
+    const hy_config& cfg = c->cfg;
+    const int ffn = cfg.ffn_dim;
+    auto lin = [&](void* dst, size_t off_elems, unsigned long long tid, size_t count) {
+        if (cfg.weight_dtype == HY_DTYPE_BF16)
+            launch_synth(static_cast<__nv_bfloat16*>(dst) + off_elems, count, seed, tid, std_dev, 0.f, c->stream);
+        else
+            launch_synth(static_cast<float*>(dst) + off_elems, count, seed, tid, std_dev, 0.f, c->stream);
+    };
+    lin(c->embed, 0, kTidEmbed, static_cast<size_t>(cfg.vocab_size) * kHidden);
+    launch_synth(c->final_norm(), kHidden, seed, kTidFinalNorm, norm_std, 1.0f, c->stream);
+    for (int l = 0; l < cfg.num_layers; ++l)
+    {
+        const unsigned long long b = kLayerTidBase + kLayerTidStride * l;
+        launch_synth(c->in_norm(l), kHidden, seed, b + J_INPUT_NORM, norm_std, 1.0f, c->stream);
+        launch_synth(c->post_norm(l), kHidden, seed, b + J_POST_NORM, norm_std, 1.0f, c->stream);
+        launch_synth(c->qn(l), kHeadDim, seed, b + J_Q_NORM, norm_std, 1.0f, c->stream);
+        launch_synth(c->kn(l), kHeadDim, seed, b + J_K_NORM, norm_std, 1.0f, c->stream);
+        lin(c->wqkv[l], 0, b + J_Q, static_cast<size_t>(kQWidth) * kHidden);
+        lin(c->wqkv[l], static_cast<size_t>(kQWidth) * kHidden, b + J_K, static_cast<size_t>(kKVWidth) * kHidden);
+        lin(c->wqkv[l], static_cast<size_t>(kQWidth + kKVWidth) * kHidden, b + J_V,
+            static_cast<size_t>(kKVWidth) * kHidden);
+        lin(c->wo[l], 0, b + J_O, static_cast<size_t>(kHidden) * kQWidth);
+        lin(c->wgu[l], 0, b + J_GATE, static_cast<size_t>(ffn) * kHidden);
+        lin(c->wgu[l], static_cast<size_t>(ffn) * kHidden, b + J_UP, static_cast<size_t>(ffn) * kHidden);
+        lin(c->wd[l], 0, b + J_DOWN, static_cast<size_t>(kHidden) * ffn);
+    }
+    HY_CUDA(cudaGetLastError());
+    HY_CUDA(cudaStreamSynchronize(c->stream));
+    return HY_OK;
+}
+
+int upload_weights(hy_ctx* c, const hy_weights* w)
+{
+    const hy_config& cfg = c->cfg;
+    const int ffn = cfg.ffn_dim;
+    if (!w || !w->embed || !w->final_norm || !w->layers) return fail(HY_ERR_INVALID_ARGUMENT, "weights are incomplete");
+    for (int l = 0; l < cfg.num_layers; ++l)
+    {
+        const hy_layer_weights& lw = w->layers[l];
+        if (!lw.input_norm || !lw.q_proj || !lw.k_proj || !lw.v_proj || !lw.query_norm || !lw.key_norm || !lw.o_proj ||
+            !lw.post_norm || !lw.gate_proj || !lw.up_proj || !lw.down_proj)
+            return fail(HY_ERR_INVALID_ARGUMENT, "layer " + std::to_string(l) + " weights are incomplete");
+    }
+    float* staging = nullptr;
+    const bool bf = cfg.weight_dtype == HY_DTYPE_BF16;
+    if (bf)
+    {
+        void* s = nullptr;
+        HY_CUDA(cudaMalloc(&s, static_cast<size_t>(std::max(cfg.vocab_size, 2 * ffn)) * kHidden * sizeof(float)));
+        staging = static_cast<float*>(s);
+    }
+    auto put = [&](void* dst, size_t off_elems, const float* src, size_t count) -> cudaError_t {
+        if (!bf)
+            return cudaMemcpy(static_cast<float*>(dst) + off_elems, src, count * sizeof(float), cudaMemcpyHostToDevice);
+        cudaError_t e = cudaMemcpy(staging, src, count * sizeof(float), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return e;
+        f32_to_bf16_kernel<<<1184, 256, 0, c->stream>>>(staging, static_cast<__nv_bfloat16*>(dst) + off_elems, count);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        return cudaStreamSynchronize(c->stream);
+    };
+    cudaError_t e = put(c->embed, 0, w->embed, static_cast<size_t>(cfg.vocab_size) * kHidden);
+    for (int l = 0; l < cfg.num_layers && e == cudaSuccess; ++l)
+    {
+        const hy_layer_weights& lw = w->layers[l];
+        e = put(c->wqkv[l], 0, lw.q_proj, static_cast<size_t>(kQWidth) * kHidden);
+        if (e == cudaSuccess) e = put(c->wqkv[l], static_cast<size_t>(kQWidth) * kHidden, lw.k_proj, static_cast<size_t>(kKVWidth) * kHidden);
+        if (e == cudaSuccess)
+            e = put(c->wqkv[l], static_cast<size_t>(kQWidth + kKVWidth) * kHidden, lw.v_proj, static_cast<size_t>(kKVWidth) * kHidden);
+        if (e == cudaSuccess) e = put(c->wo[l], 0, lw.o_proj, static_cast<size_t>(kHidden) * kQWidth);
+        if (e == cudaSuccess) e = put(c->wgu[l], 0, lw.gate_proj, static_cast<size_t>(ffn) * kHidden);
+        if (e == cudaSuccess) e = put(c->wgu[l], static_cast<size_t>(ffn) * kHidden, lw.up_proj, static_cast<size_t>(ffn) * kHidden);
+        if (e == cudaSuccess) e = put(c->wd[l], 0, lw.down_proj, static_cast<size_t>(kHidden) * ffn);
+        if (e == cudaSuccess) e = cudaMemcpy(c->in_norm(l), lw.input_norm, kHidden * sizeof(float), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(c->post_norm(l), lw.post_norm, kHidden * sizeof(float), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(c->qn(l), lw.query_norm, kHeadDim * sizeof(float), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(c->kn(l), lw.key_norm, kHeadDim * sizeof(float), cudaMemcpyHostToDevice);
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(c->final_norm(), w->final_norm, kHidden * sizeof(float), cudaMemcpyHostToDevice);
+    if (staging) cudaFree(staging);
+    if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("weight upload: ") + cudaGetErrorString(e));
+    return HY_OK;
+}
+
+void free_ctx(hy_ctx* c)
+{
+    if (!c) return;
+    cudaSetDevice(c->cfg.device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    if (c->g_ar) cudaGraphExecDestroy(c->g_ar);
+    if (c->g_verify_draft) cudaGraphExecDestroy(c->g_verify_draft);
+    if (c->g_verify_ids) cudaGraphExecDestroy(c->g_verify_ids);
+    for (void* p : c->allocs) cudaFree(p);
+    if (c->logits) cudaFree(c->logits);
+    if (c->h_st) cudaFreeHost(c->h_st);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+int finish_create(hy_ctx* c, hy_ctx** out)
+{
+    int rc = ensure_graphs(c);
+    if (rc)
+    {
+        free_ctx(c);
+        return rc;
+    }
+    *out = c;
+    return HY_OK;
+}
+
+int set_device(hy_ctx* c)
+{
+    HY_CUDA(cudaSetDevice(c->cfg.device));
+    return HY_OK;
+}
+
+// One step outside a graph (prefill chunks, hy_decoder_step): rows of ctx->x at
+// explicit positions past..past+rows-1 with explicit rope rows.
+int run_direct_step(hy_ctx* c, int rows, int past, const float* cos, const float* sin, float** aux)
+{
+    StepPlan p{};
+    p.rows = rows;
+    p.source.src = SRC_X;
+    p.cos = cos;
+    p.sin = sin;
+    p.rope_state = 0;
+    p.past_from_state = false;
+    p.past_fixed = past;
+    p.lm_mode = -1;
+    p.aux = aux;
+    t_next_plain = true;   // the rows were just copied into ctx->x
+    cudaError_t e = enqueue_step(c, p);
+    if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("decoder step launch: ") + cudaGetErrorString(e));
+    return HY_OK;
+}
+
+int set_length(hy_ctx* c, int rows)
+{
+    c->h_st->kv_len = rows;
+    c->kv_len = rows;
+    HY_CUDA(cudaMemcpyAsync(&c->st->kv_len, &c->h_st->kv_len, sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    HY_CUDA(cudaStreamSynchronize(c->stream));
+    return HY_OK;
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+const char* hy_version(void) { return "hy_decode 0.1 (sm_100a)"; }
+
+const char* hy_last_error(void) { return g_error.c_str(); }
+
+int hy_config_init(hy_config* cfg)
+{
+    if (!cfg) return fail(HY_ERR_INVALID_ARGUMENT, "config is null");
+    cfg->num_layers = 24;
+    cfg->vocab_size = 120818;
+    cfg->ffn_dim = kFfn;
+    cfg->max_context = 8192 + 64;
+    cfg->max_prefill = 2048;
+    cfg->max_tokens = 2048;
+    cfg->weight_dtype = HY_DTYPE_F32;
+    cfg->kv_dtype = HY_DTYPE_F32;
+    cfg->rms_norm_eps = 1e-5f;
+    cfg->attn_scale = 0.0883883f;
+    cfg->device = 0;
+    return HY_OK;
+}
+
+int hy_ctx_create(const hy_config* cfg, const hy_weights* weights, hy_ctx** out)
+{
+    if (!out) return fail(HY_ERR_INVALID_ARGUMENT, "out is null");
+    *out = nullptr;
+    int rc = validate_config(cfg);
+    if (rc) return rc;
+    hy_ctx* c = new hy_ctx();
+    c->cfg = *cfg;
+    if ((rc = alloc_ctx(c)) || (rc = upload_weights(c, weights)))
+    {
+        free_ctx(c);
+        return rc;
+    }
+    return finish_create(c, out);
+}
+
+int hy_ctx_create_synthetic(const hy_config* cfg, uint64_t seed, float std_dev, float norm_std, hy_ctx** out)
+{
+    if (!out) return fail(HY_ERR_INVALID_ARGUMENT, "out is null");
+    *out = nullptr;
+    int rc = validate_config(cfg);
+    if (rc) return rc;
+    hy_ctx* c = new hy_ctx();
+    c->cfg = *cfg;
+    if ((rc = alloc_ctx(c)) || (rc = fill_synthetic(c, seed, std_dev, norm_std)))
+    {
+        free_ctx(c);
+        return rc;
+    }
+    return finish_create(c, out);
+}
+
+void hy_ctx_destroy(hy_ctx* ctx) { free_ctx(ctx); }
+
+int hy_ctx_config(const hy_ctx* ctx, hy_config* cfg)
+{
+    if (!ctx || !cfg) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    *cfg = ctx->cfg;
+    return HY_OK;
+}
+
+size_t hy_ctx_device_bytes(const hy_ctx* ctx) { return ctx ? ctx->device_bytes : 0; }
+
+void* hy_ctx_stream(hy_ctx* ctx) { return ctx ? static_cast<void*>(ctx->stream) : nullptr; }
+
+int hy_build_mrope(const int* position_ids, int seq_len, int use_cos, float* out)
+{
+    // detail::build_mrope (src/text_runtime.cpp:42-63).
+    if (!position_ids || !out || seq_len <= 0) return fail(HY_ERR_INVALID_ARGUMENT, "invalid mrope arguments");
+    constexpr int section = kHeadDim / 4;
+    const float base = static_cast<float>(10000.0 * std::pow(1000.0, 128.0 / 126.0));
+    for (int dim = 0; dim < kHeadDim; ++dim)
+    {
+        const int axis = dim / section;
+        const int fd = dim % (kHeadDim / 2);
+        const float inv_freq = 1.0f / std::pow(base, static_cast<float>(2 * fd) / kHeadDim);
+        for (int t = 0; t < seq_len; ++t)
+        {
+            const int position = position_ids[static_cast<size_t>(axis) * seq_len + t];
+            const float angle = static_cast<float>(position) * inv_freq;
+            out[static_cast<size_t>(t) * kHeadDim + dim] = use_cos ? std::cos(angle) : std::sin(angle);
+        }
+    }
+    return HY_OK;
+}
+
+float hy_rope_value(int position, int dim, int use_cos) { return rope_value_host(position, dim, use_cos != 0); }
+
+int hy_seq_reset(hy_ctx* c)
+{
+    if (!c) return fail(HY_ERR_INVALID_ARGUMENT, "ctx is null");
+    int rc = set_device(c);
+    if (rc) return rc;
+    HY_CUDA(cudaMemsetAsync(c->hist, 0, sizeof(unsigned) * ((c->cfg.vocab_size + 31) / 32), c->stream));
+    return set_length(c, 0);
+}
+
+int hy_seq_length(hy_ctx* c, int* rows)
+{
+    if (!c || !rows) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    *rows = c->kv_len;
+    return HY_OK;
+}
+
+int hy_seq_truncate(hy_ctx* c, int rows)
+{
+    // view_dflash_rows (src/dflash_runtime.cpp:97-119) rejects rows <= 0 or > h.
+    if (!c) return fail(HY_ERR_INVALID_ARGUMENT, "ctx is null");
+    if (rows <= 0 || rows > c->kv_len) return fail(HY_ERR_INVALID_ARGUMENT, "invalid DFlash row view");
+    int rc = set_device(c);
+    if (rc) return rc;
+    return set_length(c, rows);
+}
+
+int hy_seq_set_length(hy_ctx* c, int rows)
+{
+    if (!c) return fail(HY_ERR_INVALID_ARGUMENT, "ctx is null");
+    if (rows < 0 || rows > c->cfg.max_context) return fail(HY_ERR_CAPACITY, "length exceeds the KV capacity");
+    int rc = set_device(c);
+    if (rc) return rc;
+    return set_length(c, rows);
+}
+
+static int history_upload(hy_ctx* c, const int* ids, int n, bool clear)
+{
+    if (!c || n < 0 || (n > 0 && !ids)) return fail(HY_ERR_INVALID_ARGUMENT, "invalid history arguments");
+    int rc = set_device(c);
+    if (rc) return rc;
+    if (clear) HY_CUDA(cudaMemsetAsync(c->hist, 0, sizeof(unsigned) * ((c->cfg.vocab_size + 31) / 32), c->stream));
+    if (n > 0)
+    {
+        int* d = nullptr;
+        HY_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&d), sizeof(int) * n, c->stream));
+        HY_CUDA(cudaMemcpyAsync(d, ids, sizeof(int) * n, cudaMemcpyHostToDevice, c->stream));
+        hist_add_kernel<<<(n + 255) / 256, 256, 0, c->stream>>>(c->hist, d, n, c->cfg.vocab_size);
+        HY_CUDA(cudaGetLastError());
+        HY_CUDA(cudaFreeAsync(d, c->stream));
+    }
+    HY_CUDA(cudaStreamSynchronize(c->stream));
+    return HY_OK;
+}
+
+int hy_history_set(hy_ctx* c, const int* ids, int n) { return history_upload(c, ids, n, true); }
+int hy_history_add(hy_ctx* c, const int* ids, int n) { return history_upload(c, ids, n, false); }
+
+int hy_prefill(hy_ctx* c, const float* embeds, const float* cos, const float* sin, int seq, float* last_hidden,
+               float* aux_hidden)
+{
+    if (!c || !embeds || !cos || !sin) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    if (seq <= 0) return fail(HY_ERR_INVALID_ARGUMENT, "seq_len must be positive");
+    if (seq > c->cfg.max_prefill || seq > c->cfg.max_context)
+        return fail(HY_ERR_CAPACITY, "prompt of " + std::to_string(seq) + " rows exceeds max_prefill");
+    if (aux_hidden) return fail(HY_ERR_UNSUPPORTED, "prefill aux hidden states are produced per step only");
+    int rc = set_device(c);
+    if (rc) return rc;
+    HY_CUDA(cudaMemcpyAsync(c->prompt, embeds, sizeof(float) * seq * kHidden, cudaMemcpyHostToDevice, c->stream));
+    HY_CUDA(cudaMemcpyAsync(c->pre_cos, cos, sizeof(float) * seq * kHeadDim, cudaMemcpyHostToDevice, c->stream));
+    HY_CUDA(cudaMemcpyAsync(c->pre_sin, sin, sizeof(float) * seq * kHeadDim, cudaMemcpyHostToDevice, c->stream));
+    for (int p0 = 0; p0 < seq; p0 += kMaxStepRows)
+    {
+        const int rows = std::min(kMaxStepRows, seq - p0);
+        HY_CUDA(cudaMemcpyAsync(c->x, c->prompt + static_cast<size_t>(p0) * kHidden, sizeof(float) * rows * kHidden,
+                                cudaMemcpyDeviceToDevice, c->stream));
+        if ((rc = run_direct_step(c, rows, p0, c->pre_cos + static_cast<size_t>(p0) * kHeadDim,
+                                  c->pre_sin + static_cast<size_t>(p0) * kHeadDim, nullptr)))
+            return rc;
+        if (p0 + rows == seq && last_hidden)
+        {
+            rmsnorm_rows_kernel<<<1, 256, 0, c->stream>>>(c->x + static_cast<size_t>(rows - 1) * kHidden, c->final_norm(),
+                                                         c->cfg.rms_norm_eps, c->hidden, kHidden);
+            HY_CUDA(cudaGetLastError());
+            HY_CUDA(cudaMemcpyAsync(last_hidden, c->hidden, sizeof(float) * kHidden, cudaMemcpyDeviceToHost, c->stream));
+        }
+    }
+    if ((rc = check_device_error(c))) return rc;
+    return set_length(c, seq);
+}
+
+int hy_decoder_step(hy_ctx* c, const float* embeds, int rows, const float* cos, const float* sin, float* hidden,
+                    float* aux_hidden)
+{
+    if (!c || !embeds || !cos || !sin) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    if (rows < 1 || rows > kMaxStepRows) return fail(HY_ERR_INVALID_ARGUMENT, "rows must be in 1..16");
+    if (c->kv_len + rows > c->cfg.max_context) return fail(HY_ERR_CAPACITY, "KV capacity exceeded");
+    int rc = set_device(c);
+    if (rc) return rc;
+    HY_CUDA(cudaMemcpyAsync(c->x, embeds, sizeof(float) * rows * kHidden, cudaMemcpyHostToDevice, c->stream));
+    HY_CUDA(cudaMemcpyAsync(c->pre_cos, cos, sizeof(float) * rows * kHeadDim, cudaMemcpyHostToDevice, c->stream));
+    HY_CUDA(cudaMemcpyAsync(c->pre_sin, sin, sizeof(float) * rows * kHeadDim, cudaMemcpyHostToDevice, c->stream));
+    float* aux[kAuxLayers];
+    for (int i = 0; i < kAuxLayers; ++i) aux[i] = c->aux + static_cast<size_t>(i) * kMaxStepRows * kHidden;
+    if ((rc = run_direct_step(c, rows, c->kv_len, c->pre_cos, c->pre_sin, aux_hidden ? aux : nullptr))) return rc;
+    if (hidden)
+    {
+        rmsnorm_rows_kernel<<<rows, 256, 0, c->stream>>>(c->x, c->final_norm(), c->cfg.rms_norm_eps, c->hidden, kHidden);
+        HY_CUDA(cudaGetLastError());
+        HY_CUDA(cudaMemcpyAsync(hidden, c->hidden, sizeof(float) * rows * kHidden, cudaMemcpyDeviceToHost, c->stream));
+    }
+    if (aux_hidden)
+        for (int i = 0; i < kAuxLayers; ++i)
+            HY_CUDA(cudaMemcpyAsync(aux_hidden + static_cast<size_t>(i) * rows * kHidden, aux[i],
+                                    sizeof(float) * rows * kHidden, cudaMemcpyDeviceToHost, c->stream));
+    if ((rc = check_device_error(c))) return rc;
+    return set_length(c, c->kv_len + rows);
+}
+
+int hy_lm_head_select(hy_ctx* c, const float* hidden, int rows, const int* row_prefix, float penalty, int* tokens,
+                      int* raw_top1, float* logits)
+{
+    if (!c || !hidden || !tokens) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    if (rows < 1 || rows > kMaxStepRows) return fail(HY_ERR_INVALID_ARGUMENT, "rows must be in 1..16");
+    if (!std::isfinite(penalty) || penalty <= 0.f) return fail(HY_ERR_INVALID_ARGUMENT, "repetition_penalty must be positive");
+    int rc = set_device(c);
+    if (rc) return rc;
+    HY_CUDA(cudaMemcpyAsync(c->hidden, hidden, sizeof(float) * rows * kHidden, cudaMemcpyHostToDevice, c->stream));
+    if (row_prefix) HY_CUDA(cudaMemcpyAsync(c->prefix, row_prefix, sizeof(int) * rows, cudaMemcpyHostToDevice, c->stream));
+    if (logits && !c->logits)
+        HY_CUDA(cudaMalloc(reinterpret_cast<void**>(&c->logits), sizeof(float) * kMaxStepRows * c->cfg.vocab_size));
+    t_next_plain = true;
+    cudaError_t e = enqueue_lm_select(c, rows, c->hidden, penalty, row_prefix != nullptr, logits ? c->logits : nullptr);
+    if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("LM head launch: ") + cudaGetErrorString(e));
+    HY_CUDA(cudaMemcpyAsync(tokens, c->tok_out, sizeof(int) * rows, cudaMemcpyDeviceToHost, c->stream));
+    if (raw_top1) HY_CUDA(cudaMemcpyAsync(raw_top1, c->raw_out, sizeof(int) * rows, cudaMemcpyDeviceToHost, c->stream));
+    if (logits)
+        HY_CUDA(cudaMemcpyAsync(logits, c->logits, sizeof(float) * rows * c->cfg.vocab_size, cudaMemcpyDeviceToHost,
+                                c->stream));
+    return check_device_error(c);
+}
+
+int hy_generate(hy_ctx* c, int first_token, int first_raw_top1, int max_tokens, float penalty, const int* eos_ids,
+                int n_eos, int* tokens, int* raw_top1, int* n_tokens)
+{
+    if (!c || !n_tokens) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    if (max_tokens < 1 || max_tokens > c->cfg.max_tokens)
+        return fail(HY_ERR_CAPACITY, "max_tokens must be in 1..config max_tokens");
+    if (first_token < 0 || first_token >= c->cfg.vocab_size) return fail(HY_ERR_INVALID_ARGUMENT, "first_token out of range");
+    if (!std::isfinite(penalty) || penalty <= 0.f) return fail(HY_ERR_INVALID_ARGUMENT, "repetition_penalty must be positive");
+    if (c->kv_len + max_tokens > c->cfg.max_context) return fail(HY_ERR_CAPACITY, "KV capacity exceeded");
+    int rc = set_device(c);
+    if (rc) return rc;
+    if ((rc = set_eos(c, eos_ids, n_eos))) return rc;
+    DecodeState& h = *c->h_st;
+    h.kv_len = c->kv_len;
+    h.cur_token = first_token;
+    h.n_gen = 1;
+    h.max_tokens = max_tokens;
+    h.penalty = penalty;
+    bool first_eos = false;
+    for (int i = 0; i < n_eos; ++i) first_eos |= (eos_ids[i] == first_token);
+    h.done = (first_eos || max_tokens <= 1) ? 1 : 0;
+    if ((rc = push_state(c))) return rc;
+    HY_CUDA(cudaMemcpyAsync(c->log_tokens, &first_token, sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    HY_CUDA(cudaMemcpyAsync(c->log_raw, &first_raw_top1, sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    if ((rc = history_upload(c, &first_token, 1, false))) return rc;
+    int launched_steps = 0;
+    while (!h.done && launched_steps < max_tokens - 1)
+    {
+        for (int i = 0; i < 4 && launched_steps < max_tokens - 1; ++i)
+        {
+            HY_CUDA(cudaGraphLaunch(c->g_ar, c->stream));
+            launched_steps += kArStepsPerGraph;
+        }
+        if ((rc = sync_state_to_host(c))) return rc;
+    }
+    if ((rc = check_device_error(c))) return rc;
+    if ((rc = sync_state_to_host(c))) return rc;
+    *n_tokens = h.n_gen;
+    if (tokens) HY_CUDA(cudaMemcpy(tokens, c->log_tokens, sizeof(int) * h.n_gen, cudaMemcpyDeviceToHost));
+    if (raw_top1) HY_CUDA(cudaMemcpy(raw_top1, c->log_raw, sizeof(int) * h.n_gen, cudaMemcpyDeviceToHost));
+    return HY_OK;
+}
+
+int hy_verify_block(hy_ctx* c, const int* proposed, int max_commit, float penalty, const int* eos_ids, int n_eos,
+                    int* posterior, int* acceptance_length, int* committed, int* stop)
+{
+    if (!c || !proposed) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    if (max_commit < 1 || max_commit > c->cfg.max_tokens) return fail(HY_ERR_INVALID_ARGUMENT, "max_commit out of range");
+    if (!std::isfinite(penalty) || penalty <= 0.f) return fail(HY_ERR_INVALID_ARGUMENT, "repetition_penalty must be positive");
+    if (c->kv_len + kBlock > c->cfg.max_context) return fail(HY_ERR_CAPACITY, "KV capacity exceeded");
+    for (int i = 0; i < kBlock; ++i)
+        if (proposed[i] < 0 || proposed[i] >= c->cfg.vocab_size) return fail(HY_ERR_INVALID_ARGUMENT, "proposed id out of range");
+    int rc = set_device(c);
+    if (rc) return rc;
+    if ((rc = set_eos(c, eos_ids, n_eos))) return rc;
+    DecodeState& h = *c->h_st;
+    h.kv_len = c->kv_len;
+    h.cur_token = proposed[0];
+    h.n_gen = 0;
+    h.max_tokens = max_commit;
+    h.done = 0;
+    h.penalty = penalty;
+    h.block_count = 0;
+    if ((rc = push_state(c))) return rc;
+    HY_CUDA(cudaMemcpyAsync(c->proposed, proposed, sizeof(int) * kBlock, cudaMemcpyHostToDevice, c->stream));
+    HY_CUDA(cudaGraphLaunch(c->g_verify_ids, c->stream));
+    if ((rc = check_device_error(c))) return rc;
+    if ((rc = sync_state_to_host(c))) return rc;
+    if (posterior) HY_CUDA(cudaMemcpy(posterior, c->posterior, sizeof(int) * kBlock, cudaMemcpyDeviceToHost));
+    if (acceptance_length) *acceptance_length = h.accept;
+    if (committed) *committed = h.committed;
+    if (stop) *stop = h.stop;
+    return HY_OK;
+}
+
+int hy_dflash_generate_synthetic(hy_ctx* c, int first_token, int max_tokens, float penalty, const int* eos_ids,
+                                 int n_eos, const int* greedy, int n_greedy, float p, uint64_t seed, int* tokens,
+                                 int* n_tokens, int* acceptance_lengths, int* n_blocks)
+{
+    if (!c || !n_tokens || (n_greedy > 0 && !greedy)) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    if (max_tokens < 1 || max_tokens > c->cfg.max_tokens)
+        return fail(HY_ERR_CAPACITY, "max_tokens must be in 1..config max_tokens");
+    if (n_greedy < 0 || n_greedy > c->cfg.max_tokens + 2 * kBlock) return fail(HY_ERR_CAPACITY, "greedy sequence too long");
+    if (first_token < 0 || first_token >= c->cfg.vocab_size) return fail(HY_ERR_INVALID_ARGUMENT, "first_token out of range");
+    if (!std::isfinite(penalty) || penalty <= 0.f) return fail(HY_ERR_INVALID_ARGUMENT, "repetition_penalty must be positive");
+    if (c->kv_len + max_tokens + kBlock > c->cfg.max_context) return fail(HY_ERR_CAPACITY, "KV capacity exceeded");
+    int rc = set_device(c);
+    if (rc) return rc;
+    if ((rc = set_eos(c, eos_ids, n_eos))) return rc;
+    if (n_greedy > 0)
+        HY_CUDA(cudaMemcpyAsync(c->greedy, greedy, sizeof(int) * n_greedy, cudaMemcpyHostToDevice, c->stream));
+    DecodeState& h = *c->h_st;
+    h.kv_len = c->kv_len;
+    h.cur_token = first_token;
+    h.n_gen = 0;
+    h.max_tokens = max_tokens;
+    h.done = 0;
+    h.penalty = penalty;
+    h.block_count = 0;
+    h.n_greedy = n_greedy;
+    h.draft_p = p;
+    h.draft_base = synth_base(seed, kTidDrafts);
+    if ((rc = push_state(c))) return rc;
+    int launched = 0;
+    while (!h.done && launched < max_tokens)
+    {
+        for (int i = 0; i < 4 && launched < max_tokens; ++i, ++launched)
+            HY_CUDA(cudaGraphLaunch(c->g_verify_draft, c->stream));
+        if ((rc = sync_state_to_host(c))) return rc;
+    }
+    if ((rc = check_device_error(c))) return rc;
+    if ((rc = sync_state_to_host(c))) return rc;
+    *n_tokens = h.n_gen;
+    if (n_blocks) *n_blocks = h.block_count;
+    if (tokens) HY_CUDA(cudaMemcpy(tokens, c->log_tokens, sizeof(int) * h.n_gen, cudaMemcpyDeviceToHost));
+    if (acceptance_lengths)
+        HY_CUDA(cudaMemcpy(acceptance_lengths, c->accept_log, sizeof(int) * h.block_count, cudaMemcpyDeviceToHost));
+    return HY_OK;
+}
+
+int hy_run_vlm_decode_with_prompt(hy_ctx* c, const int* input_ids, const int* position_ids, int seq_len,
+                                  int image_token_id, const float* vision_features, int vision_token_count,
+                                  int max_tokens, float repetition_penalty, const int* eos_ids, int n_eos, int* tokens,
+                                  int* raw_top1, int* n_tokens)
+{
+    // prepare_prompt_embeddings checks (src/text_runtime.cpp:506-568).
+    if (!c || !input_ids || !position_ids || !n_tokens) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    if (seq_len <= 0) return fail(HY_ERR_INVALID_ARGUMENT, "prompt input_ids must not be empty");
+    if (vision_token_count <= 0 || !vision_features) return fail(HY_ERR_INVALID_ARGUMENT, "vision feature size mismatch");
+    if (!std::isfinite(repetition_penalty) || repetition_penalty <= 0.f)
+        return fail(HY_ERR_INVALID_ARGUMENT, "repetition_penalty must be positive");
+    if (seq_len > c->cfg.max_prefill) return fail(HY_ERR_CAPACITY, "prompt exceeds max_prefill");
+    if (max_tokens <= 0) max_tokens = 1024;   // src/text_runtime.cpp:1336-1341
+    if (max_tokens > c->cfg.max_tokens) return fail(HY_ERR_CAPACITY, "max_tokens exceeds config max_tokens");
+    std::vector<int> feat_idx(seq_len, -1);
+    int injected = 0;
+    for (int t = 0; t < seq_len; ++t)
+    {
+        if (input_ids[t] != image_token_id) continue;
+        if (injected >= vision_token_count) return fail(HY_ERR_INVALID_ARGUMENT, "more image tokens than vision features");
+        feat_idx[t] = injected++;
+    }
+    if (injected != vision_token_count)
+        return fail(HY_ERR_INVALID_ARGUMENT, "image token count mismatch: injected " + std::to_string(injected) +
+                                                 ", expected " + std::to_string(vision_token_count));
+    int rc = set_device(c);
+    if (rc) return rc;
+    std::vector<float> cos(static_cast<size_t>(seq_len) * kHeadDim), sin(static_cast<size_t>(seq_len) * kHeadDim);
+    if ((rc = hy_build_mrope(position_ids, seq_len, 1, cos.data())) || (rc = hy_build_mrope(position_ids, seq_len, 0, sin.data())))
+        return rc;
+    HY_CUDA(cudaMemcpyAsync(c->ids_buf, input_ids, sizeof(int) * seq_len, cudaMemcpyHostToDevice, c->stream));
+    HY_CUDA(cudaMemcpyAsync(c->feat_idx, feat_idx.data(), sizeof(int) * seq_len, cudaMemcpyHostToDevice, c->stream));
+    HY_CUDA(cudaMemcpyAsync(c->feats, vision_features, sizeof(float) * vision_token_count * kHidden,
+                            cudaMemcpyHostToDevice, c->stream));
+    HY_CUDA(cudaMemcpyAsync(c->pre_cos, cos.data(), sizeof(float) * seq_len * kHeadDim, cudaMemcpyHostToDevice, c->stream));
+    HY_CUDA(cudaMemcpyAsync(c->pre_sin, sin.data(), sizeof(float) * seq_len * kHeadDim, cudaMemcpyHostToDevice, c->stream));
+    if (c->cfg.weight_dtype == HY_DTYPE_BF16)
+        embed_prompt_kernel<__nv_bfloat16><<<seq_len, 256, 0, c->stream>>>(
+            c->ids_buf, c->feat_idx, c->feats, static_cast<const __nv_bfloat16*>(c->embed), c->cfg.vocab_size, c->prompt, c->err);
+    else
+        embed_prompt_kernel<float><<<seq_len, 256, 0, c->stream>>>(c->ids_buf, c->feat_idx, c->feats,
+                                                                     static_cast<const float*>(c->embed),
+                                                                     c->cfg.vocab_size, c->prompt, c->err);
+    HY_CUDA(cudaGetLastError());
+    // History = prompt ids (src/text_runtime.cpp:1393).
+    HY_CUDA(cudaMemsetAsync(c->hist, 0, sizeof(unsigned) * ((c->cfg.vocab_size + 31) / 32), c->stream));
+    hist_add_kernel<<<(seq_len + 255) / 256, 256, 0, c->stream>>>(c->hist, c->ids_buf, seq_len, c->cfg.vocab_size);
+    HY_CUDA(cudaGetLastError());
+    for (int p0 = 0; p0 < seq_len; p0 += kMaxStepRows)
+    {
+        const int rows = std::min(kMaxStepRows, seq_len - p0);
+        HY_CUDA(cudaMemcpyAsync(c->x, c->prompt + static_cast<size_t>(p0) * kHidden, sizeof(float) * rows * kHidden,
+                                cudaMemcpyDeviceToDevice, c->stream));
+        if ((rc = run_direct_step(c, rows, p0, c->pre_cos + static_cast<size_t>(p0) * kHeadDim,
+                                  c->pre_sin + static_cast<size_t>(p0) * kHeadDim, nullptr)))
+            return rc;
+        if (p0 + rows == seq_len)
+        {
+            rmsnorm_rows_kernel<<<1, 256, 0, c->stream>>>(c->x + static_cast<size_t>(rows - 1) * kHidden, c->final_norm(),
+                                                         c->cfg.rms_norm_eps, c->hidden, kHidden);
+            HY_CUDA(cudaGetLastError());
+        }
+    }
+    cudaError_t e = enqueue_lm_select(c, 1, c->hidden, repetition_penalty, false, nullptr);
+    if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("LM head launch: ") + cudaGetErrorString(e));
+    int first = 0, first_raw = 0;
+    HY_CUDA(cudaMemcpyAsync(&first, c->tok_out, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    HY_CUDA(cudaMemcpyAsync(&first_raw, c->raw_out, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    if ((rc = check_device_error(c))) return rc;
+    if ((rc = set_length(c, seq_len))) return rc;
+    return hy_generate(c, first, first_raw, max_tokens, repetition_penalty, eos_ids, n_eos, tokens, raw_top1, n_tokens);
+}
+
+int hy_attention(hy_ctx* c, int layer, const float* qkv, int rows, const float* cos, const float* sin, float* out)
+{
+    if (!c || !qkv || !cos || !sin || !out) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    if (layer < 0 || layer >= c->cfg.num_layers) return fail(HY_ERR_INVALID_ARGUMENT, "layer out of range");
+    if (rows < 1 || rows > kMaxStepRows) return fail(HY_ERR_INVALID_ARGUMENT, "rows must be in 1..16");
+    if (c->kv_len + rows > c->cfg.max_context) return fail(HY_ERR_CAPACITY, "KV capacity exceeded");
+    int rc = set_device(c);
+    if (rc) return rc;
+    HY_CUDA(cudaMemcpyAsync(c->qkv, qkv, sizeof(float) * rows * kQKVRows, cudaMemcpyHostToDevice, c->stream));
+    HY_CUDA(cudaMemcpyAsync(c->pre_cos, cos, sizeof(float) * rows * kHeadDim, cudaMemcpyHostToDevice, c->stream));
+    HY_CUDA(cudaMemcpyAsync(c->pre_sin, sin, sizeof(float) * rows * kHeadDim, cudaMemcpyHostToDevice, c->stream));
+    AttnArgs at;
+    std::memset(&at, 0, sizeof(at));
+    at.qkv = c->qkv;
+    at.ldq = kQKVRows;
+    at.qn_w = c->qn(layer);
+    at.kn_w = c->kn(layer);
+    at.cos = c->pre_cos;
+    at.sin = c->pre_sin;
+    at.kc = c->kc_layer(layer);
+    at.vc = c->vc_layer(layer);
+    at.cap = c->cfg.max_context;
+    at.past_fixed = c->kv_len;
+    at.rows = rows;
+    at.scale_log2 = c->cfg.attn_scale * 1.4426950408889634f;
+    at.eps = c->cfg.rms_norm_eps;
+    at.part = c->attn_part;
+    at.counter = c->attn_cnt + layer * kNumKVHeads;
+    at.out = c->attn;
+    at.err = c->err;
+    const bool kb = c->cfg.kv_dtype == HY_DTYPE_BF16;
+    cudaError_t e;
+    t_next_plain = true;
+    if (rows == 1)
+        e = kb ? run_attn<1, __nv_bfloat16>(c, at, kAttnSplitsAR) : run_attn<1, float>(c, at, kAttnSplitsAR);
+    else
+        e = kb ? run_attn<16, __nv_bfloat16>(c, at, kAttnSplitsVerify) : run_attn<16, float>(c, at, kAttnSplitsVerify);
+    if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("attention launch: ") + cudaGetErrorString(e));
+    HY_CUDA(cudaMemcpyAsync(out, c->attn, sizeof(float) * rows * kQWidth, cudaMemcpyDeviceToHost, c->stream));
+    if ((rc = check_device_error(c))) return rc;
+    return set_length(c, c->kv_len + rows);
+}
+
+static int kv_copy(hy_ctx* c, int layer, int start, int rows, const float* k, const float* v, float* ko, float* vo)
+{
+    if (!c || layer < 0 || layer >= c->cfg.num_layers || start < 0 || rows <= 0 ||
+        start + rows > c->cfg.max_context)
+        return fail(HY_ERR_INVALID_ARGUMENT, "invalid KV range");
+    int rc = set_device(c);
+    if (rc) return rc;
+    const size_t es = c->kv_elem();
+    const size_t n = static_cast<size_t>(rows) * kHeadDim;
+    float* stage = nullptr;
+    HY_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&stage), n * sizeof(float), c->stream));
+    for (int which = 0; which < 2; ++which)
+    {
+        char* base = static_cast<char*>(which == 0 ? c->kc_layer(layer) : c->vc_layer(layer));
+        for (int g = 0; g < kNumKVHeads; ++g)
+        {
+            char* dst = base + (static_cast<size_t>(g) * c->cfg.max_context + start) * kHeadDim * es;
+            const float* hin = (which == 0 ? k : v);
+            float* hout = (which == 0 ? ko : vo);
+            if (hin)
+            {
+                if (es == 4)
+                    HY_CUDA(cudaMemcpyAsync(dst, hin + g * n, n * 4, cudaMemcpyHostToDevice, c->stream));
+                else
+                {
+                    HY_CUDA(cudaMemcpyAsync(stage, hin + g * n, n * 4, cudaMemcpyHostToDevice, c->stream));
+                    f32_to_bf16_kernel<<<64, 256, 0, c->stream>>>(stage, reinterpret_cast<__nv_bfloat16*>(dst), n);
+                }
+            }
+            if (hout)
+            {
+                if (es == 4)
+                    HY_CUDA(cudaMemcpyAsync(hout + g * n, dst, n * 4, cudaMemcpyDeviceToHost, c->stream));
+                else
+                {
+                    to_f32_kernel<__nv_bfloat16><<<64, 256, 0, c->stream>>>(reinterpret_cast<const __nv_bfloat16*>(dst),
+                                                                             stage, n);
+                    HY_CUDA(cudaMemcpyAsync(hout + g * n, stage, n * 4, cudaMemcpyDeviceToHost, c->stream));
+                }
+            }
+        }
+    }
+    HY_CUDA(cudaFreeAsync(stage, c->stream));
+    HY_CUDA(cudaStreamSynchronize(c->stream));
+    return HY_OK;
+}
+
+int hy_kv_write(hy_ctx* c, int layer, int start, int rows, const float* k, const float* v)
+{
+    if (!k || !v) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    return kv_copy(c, layer, start, rows, k, v, nullptr, nullptr);
+}
+
+int hy_kv_read(hy_ctx* c, int layer, int start, int rows, float* k, float* v)
+{
+    if (!k || !v) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    return kv_copy(c, layer, start, rows, nullptr, nullptr, k, v);
+}
+
+int hy_bench_ar_steps(hy_ctx* c, int count, float* ms)
+{
+    if (!c || !ms || count < 1) return fail(HY_ERR_INVALID_ARGUMENT, "invalid arguments");
+    int rc = set_device(c);
+    if (rc) return rc;
+    DecodeState& h = *c->h_st;
+    h.kv_len = c->kv_len;
+    h.n_gen = 1;
+    h.max_tokens = std::min(c->cfg.max_tokens, count * kArStepsPerGraph + 2);
+    h.done = 0;
+    h.n_eos = 0;
+    if (c->kv_len + h.max_tokens > c->cfg.max_context) return fail(HY_ERR_CAPACITY, "KV capacity exceeded");
+    if ((rc = push_state(c))) return rc;
+    cudaEvent_t e0, e1;
+    HY_CUDA(cudaEventCreate(&e0));
+    HY_CUDA(cudaEventCreate(&e1));
+    const int graphs = (count + kArStepsPerGraph - 1) / kArStepsPerGraph;
+    HY_CUDA(cudaEventRecord(e0, c->stream));
+    for (int i = 0; i < graphs; ++i) HY_CUDA(cudaGraphLaunch(c->g_ar, c->stream));
+    HY_CUDA(cudaEventRecord(e1, c->stream));
+    HY_CUDA(cudaEventSynchronize(e1));
+    float t = 0.f;
+    HY_CUDA(cudaEventElapsedTime(&t, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    *ms = t;
+    if ((rc = check_device_error(c))) return rc;
+    // Restore the sequence length the steps advanced.
+    return set_length(c, c->kv_len);
+}
+
+int hy_bench_kernel(hy_ctx* c, int which, int count, float* ms)
+{
+    if (!c || !ms || count < 1) return fail(HY_ERR_INVALID_ARGUMENT, "invalid arguments");
+    int rc = set_device(c);
+    if (rc) return rc;
+    cudaEvent_t e0, e1;
+    HY_CUDA(cudaEventCreate(&e0));
+    HY_CUDA(cudaEventCreate(&e1));
+    const bool wb = c->cfg.weight_dtype == HY_DTYPE_BF16;
+    auto once = [&]() -> cudaError_t {
+        if (which == 0)
+            return enqueue_lm_select(c, 1, c->hidden, 1.08f, false, nullptr);
+        if (which == 1)
+        {
+            GemvArgs gu = base_args(c);
+            gu.W = c->wgu[0];
+            gu.N = 2 * c->cfg.ffn_dim;
+            gu.ldw = kHidden;
+            gu.rows = 1;
+            gu.src = SRC_X;
+            gu.x = c->x;
+            gu.ldx = kHidden;
+            gu.norm_w = c->post_norm(0);
+            gu.out = c->gu;
+            gu.ldo = 2 * c->cfg.ffn_dim;
+            return wb ? run_gemv<__nv_bfloat16, kHidden, 1, PRO_NORM, EPI_STORE>(c, gu)
+                      : run_gemv<float, kHidden, 1, PRO_NORM, EPI_STORE>(c, gu);
+        }
+        AttnArgs at;
+        std::memset(&at, 0, sizeof(at));
+        at.qkv = c->qkv;
+        at.ldq = kQKVRows;
+        at.qn_w = c->qn(0);
+        at.kn_w = c->kn(0);
+        at.cos = c->rope_cos;
+        at.sin = c->rope_sin;
+        at.rope_state = 0;
+        at.kc = c->kc_layer(0);
+        at.vc = c->vc_layer(0);
+        at.cap = c->cfg.max_context;
+        at.past_fixed = c->kv_len;
+        at.rows = 1;
+        at.scale_log2 = c->cfg.attn_scale * 1.4426950408889634f;
+        at.eps = c->cfg.rms_norm_eps;
+        at.part = c->attn_part;
+        at.counter = c->attn_cnt;
+        at.out = c->attn;
+        at.err = c->err;
+        return c->cfg.kv_dtype == HY_DTYPE_BF16 ? run_attn<1, __nv_bfloat16>(c, at, kAttnSplitsAR)
+                                                : run_attn<1, float>(c, at, kAttnSplitsAR);
+    };
+    cudaError_t e = once();  // warm-up
+    if (e != cudaSuccess) return fail(HY_ERR_CUDA, cudaGetErrorString(e));
+    HY_CUDA(cudaEventRecord(e0, c->stream));
+    for (int i = 0; i < count && e == cudaSuccess; ++i) e = once();
+    HY_CUDA(cudaEventRecord(e1, c->stream));
+    if (e != cudaSuccess) return fail(HY_ERR_CUDA, cudaGetErrorString(e));
+    HY_CUDA(cudaEventSynchronize(e1));
+    float t = 0.f;
+    HY_CUDA(cudaEventElapsedTime(&t, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    *ms = t / count;
+    return check_device_error(c);
+}
+
+}  // extern "C"

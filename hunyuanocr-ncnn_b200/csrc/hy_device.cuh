@@ -1,0 +1,225 @@
+// Device primitives shared by the decode kernels (sm_100a).
+//
+// Weight and KV rows are streamed from HBM into shared memory with the bulk
+// copy engine (cp.async.bulk, the non-tensor form of TMA; never with
+// multicast), completing on an mbarrier. Every wait on an mbarrier is bounded
+// by a wall-clock limit read from %globaltimer; a wait that gives up sets a
+// bit in the context's device error word and the kernel drains its own copies
+// before returning, so a fault in the pipeline reports an error instead of
+// hanging the GPU.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace hy {
+
+constexpr int kHidden = 1024;
+constexpr int kHeadDim = 128;
+constexpr int kNumQHeads = 16;
+constexpr int kNumKVHeads = 8;
+constexpr int kQWidth = kNumQHeads * kHeadDim;    // 2048
+constexpr int kKVWidth = kNumKVHeads * kHeadDim;  // 1024
+constexpr int kQKVRows = kQWidth + 2 * kKVWidth;  // 4096
+constexpr int kMaxStepRows = 16;
+constexpr int kBlock = 16;   // DFlash block
+constexpr int kMaxEos = 8;
+constexpr int kAuxLayers = 4;
+
+// Device error bits (context error word).
+constexpr int kErrTimeoutFull = 1;
+constexpr int kErrTimeoutEmpty = 2;
+constexpr int kErrBounds = 4;
+
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+
+// ---------------------------------------------------------------------------
+// Decode state kept on the device between steps (no host round trip).
+// ---------------------------------------------------------------------------
+struct DecodeState {
+    int kv_len;        // rows in the KV cache
+    int cur_token;     // next token to embed (AR) / proposed[0] of the next block (DFlash)
+    int n_gen;         // tokens written to the token log
+    int max_tokens;    // generation limit (token log)
+    int done;          // set by the commit when EOS or max_tokens is reached
+    int block_count;   // DFlash blocks run
+    int n_eos;
+    int eos[kMaxEos];
+    float penalty;
+    // synthetic drafter
+    int n_greedy;
+    float draft_p;
+    int pad0;
+    unsigned long long draft_base;
+    // last verify block outputs
+    int accept;        // dflash_acceptance_length
+    int committed;
+    int stop;
+    int pad1;
+};
+
+// ---------------------------------------------------------------------------
+// PTX wrappers.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p)
+{
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init()
+{
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ unsigned long long global_ns()
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait for phase `parity` of `bar`. Returns false (and sets `err_bit`
+// in *err) when the wall-clock limit passes first.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int err_bit)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    while (true)
+    {
+        for (int i = 0; i < 32; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (global_ns() - t0 > kWaitLimitNs)
+        {
+            if (err) atomicOr(err, err_bit);
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ uint64_t l2_evict_first_policy()
+{
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// Bulk global->shared copy (no multicast). dst, src and bytes must be 16-byte aligned.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol)
+{
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+
+// Programmatic dependent launch: wait for the previous grid in the stream
+// (a no-op when the launch carried no programmatic dependency) / let the next
+// grid start its prologue.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
+// Numeric helpers.
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+// Four consecutive elements of T as float4 (T = float: one 16-byte load;
+// T = bf16: one 8-byte load).
+template <typename T>
+__device__ __forceinline__ float4 load4(const T* p);
+template <>
+__device__ __forceinline__ float4 load4<float>(const float* p) { return *reinterpret_cast<const float4*>(p); }
+template <>
+__device__ __forceinline__ float4 load4<__nv_bfloat16>(const __nv_bfloat16* p)
+{
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    float4 r;
+    r.x = __uint_as_float(u.x << 16);
+    r.y = __uint_as_float(u.x & 0xFFFF0000u);
+    r.z = __uint_as_float(u.y << 16);
+    r.w = __uint_as_float(u.y & 0xFFFF0000u);
+    return r;
+}
+
+__device__ __forceinline__ float warp_sum(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float dot4(float4 a, float4 b)
+{
+    return a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+}
+
+// splitmix64 finalizer; the synthetic weight generator and the synthetic
+// drafter are both counter streams of it.
+__host__ __device__ __forceinline__ unsigned long long splitmix64(unsigned long long z)
+{
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+__host__ __device__ __forceinline__ unsigned long long synth_base(unsigned long long seed, unsigned long long tid)
+{
+    return splitmix64(seed * 0x9E3779B97F4A7C15ull + tid * 0xD1B54A32D192ED03ull);
+}
+
+// Value i of a counter stream: offset + float(c) * mult with
+// c = (sum of the four 16-bit fields of splitmix64(base + i)) - 131070,
+// each step correctly rounded (no contraction into an FMA).
+__device__ __forceinline__ float synth_value(unsigned long long base, unsigned long long i, float mult, float offset)
+{
+    const unsigned long long h = splitmix64(base + i);
+    const int c = static_cast<int>((h & 0xFFFFull) + ((h >> 16) & 0xFFFFull) + ((h >> 32) & 0xFFFFull) + (h >> 48)) -
+                  131070;
+    return __fadd_rn(offset, __fmul_rn(static_cast<float>(c), mult));
+}
+
+}  // namespace hy

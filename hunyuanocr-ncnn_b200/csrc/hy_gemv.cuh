@@ -1,0 +1,531 @@
+// Streaming row GEMV for the decode step: y[m, n] = <xs[m, :], W[n, k_off : k_off + KP]>
+// for the `rows` (<= MT) activation rows of one decoder step.
+//
+// This replaces ncnn's Gemm layers of the exported decoder (pnnx Linear,
+// export/text_decoder_kv.py:64-69, 93-95; the Vulkan M=1 -> GEMV dispatch of
+// patches/ncnn/0004-vulkan-gemm-m1.patch:78-114) and the LM head
+// (export/export_lm_head.py:16-24) with the host token selection
+// (src/text_runtime.cpp:730-797) fused into its epilogue.
+//
+// Layout: one CTA per SM owns a contiguous block of weight rows. A producer
+// warp streams that block (contiguous in HBM) through a ring of shared-memory
+// stages with cp.async.bulk, hinting L2 to evict it first; 8 consumer warps
+// each take groups of RPW rows and dot them with the activation rows held in
+// shared memory. The producer starts before griddepcontrol.wait, so under
+// programmatic dependent launch the weight stream overlaps the tail of the
+// previous kernel.
+//
+// Prologues: plain copy, RMSNorm (HunYuanDenseV1RMSNorm: w * (x * 1/sqrt(mean(x^2)+eps))),
+// SwiGLU (silu(gate) * up), and embedding gather from the tied table (AR token,
+// explicit ids, or the synthetic drafter), which also writes the residual stream.
+// Epilogues: store, residual add (+ optional aux copy), penalised argmax with
+// a last-CTA reduction and the AR / DFlash commit.
+#pragma once
+
+#include "hy_device.cuh"
+
+namespace hy {
+
+enum { PRO_PLAIN = 0, PRO_NORM = 1, PRO_SWIGLU = 2 };
+enum { EPI_STORE = 0, EPI_RESID = 1, EPI_ARGMAX = 2 };
+enum { SRC_X = 0, SRC_GATHER_STATE = 1, SRC_GATHER_IDS = 2, SRC_GATHER_DRAFT = 3 };
+enum { LM_NONE = 0, LM_AR = 1, LM_VERIFY = 2 };
+
+constexpr int kGemvWarps = 8;
+constexpr int kGemvThreads = (kGemvWarps + 1) * 32;
+constexpr int kStageBytes = 16384;
+constexpr int kRingBytes = 96 * 1024;
+constexpr int kSmemBudget = 225 * 1024;   // dynamic shared memory per CTA we allow ourselves
+
+struct GemvArgs {
+    const void* W;   // [N x ldw] of WT; this launch reads columns [k_off, k_off + KP)
+    int N, ldw, k_off;
+    int rows;        // active activation rows (<= MT)
+    int src;         // SRC_*
+    const float* x;  // SRC_X: row m at x + m * ldx + k_off (SwiGLU: gate there, up at + up_off)
+    int ldx, up_off;
+    const float* norm_w;
+    float eps;
+    const void* table;    // gather: tied embedding table [vocab x 1024] of WT
+    const int* ids;       // SRC_GATHER_IDS
+    DecodeState* st;
+    const int* greedy;    // SRC_GATHER_DRAFT
+    int vocab;
+    int* ids_out;         // gather: CTA 0 writes the gathered ids
+    float* x_store;       // gather: fp32 rows written to the residual stream [rows x 1024]
+    float* out;           // STORE / RESID target, out[m * ldo + n]
+    int ldo;
+    const float* extra;   // RESID: out = out + (extra + dot) (second half of a K split)
+    float* aux;           // RESID: optional copy of the result, aux[m * ld_aux + n]
+    int ld_aux;
+    int lm_mode;          // LM_*
+    unsigned* hist;       // penalty history bitmap (read; updated by the commit)
+    const int* prefix;    // row m also counts prefix[0..m] as history (nullable)
+    float* logits;        // optional dump [rows x ldl]
+    int ldl;
+    float4* part;         // [gridDim.x * MT] per-CTA (raw max, raw idx, pen max, pen idx)
+    int* counter;
+    int* tok_out;         // LM_NONE: [rows]
+    int* raw_out;
+    int* log_tokens;      // LM_AR / LM_VERIFY token log
+    int* log_raw;
+    int* accept_log;
+    int* posterior_out;   // LM_VERIFY [16]
+    float penalty;        // LM_NONE penalty (AR / verify read st->penalty)
+    int* err;
+};
+
+template <typename WT, int KP, int MT>
+struct GemvShape {
+    static constexpr int RPW = (MT == 1) ? 1 : 2;
+    static constexpr int SEG = KP * static_cast<int>(sizeof(WT));
+    static constexpr int SPS0 = kStageBytes / SEG;
+    static constexpr int SPS = (SPS0 < RPW) ? RPW : (SPS0 / RPW) * RPW;
+    static constexpr int STAGE = SPS * SEG;
+    static constexpr int GPS = SPS / RPW;
+    static constexpr int XS_BYTES = MT * KP * 4;
+    static constexpr int RED_BYTES = (kGemvWarps * MT + MT) * 16 + 16;
+    static constexpr int NST_RING = kRingBytes / STAGE;
+    static constexpr int NST_FIT = (kSmemBudget - XS_BYTES - RED_BYTES - 512) / STAGE;
+    static constexpr int NST = NST_RING < NST_FIT ? NST_RING : NST_FIT;
+    static constexpr int BAR_OFF = XS_BYTES + NST * STAGE;
+    static constexpr int RED_OFF = BAR_OFF + 2 * NST * 8;
+    static constexpr int SMEM = RED_OFF + RED_BYTES;
+};
+
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+struct ArgBest {
+    float rv;
+    int ri;
+    float pv;
+    int pi;
+};
+
+__device__ __forceinline__ void best_update(float& bv, int& bi, float v, int i)
+{
+    if (bi < 0 || v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+}
+
+__device__ __forceinline__ bool is_eos(const DecodeState* st, int tok)
+{
+    bool e = false;
+    for (int i = 0; i < st->n_eos && i < kMaxEos; ++i) e |= (st->eos[i] == tok);
+    return e;
+}
+
+// Synthetic drafter: slot i of the current block (see hy_decode.h).
+__device__ __forceinline__ int draft_id(const DecodeState* st, const int* greedy, int vocab, int i)
+{
+    if (i == 0) return st->cur_token;
+    const unsigned long long h = splitmix64(st->draft_base + 16ull * static_cast<unsigned long long>(st->block_count) + i);
+    const float u = static_cast<float>(h >> 40) * 5.9604644775390625e-08f;  // 2^-24
+    const int j = st->n_gen + i;
+    if (u < st->draft_p && j < st->n_greedy) return greedy[j];
+    return static_cast<int>((h & 0xFFFFFFFFull) % static_cast<unsigned long long>(vocab));
+}
+
+template <typename WT, int KP, int MT, int PRO, int EPI>
+__global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(const GemvArgs a)
+{
+    using S = GemvShape<WT, KP, MT>;
+    constexpr int RPW = S::RPW, SEG = S::SEG, SPS = S::SPS, STAGE = S::STAGE, NST = S::NST;
+    static_assert(NST >= 2, "ring too small");
+    static_assert(SEG % 16 == 0, "segments must be 16-byte multiples");
+    static_assert(KP % 128 == 0, "K slice must be a multiple of 128");
+
+    extern __shared__ __align__(128) unsigned char smem[];
+    float* xs = reinterpret_cast<float*>(smem);
+    unsigned char* ring = smem + S::XS_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
+    uint64_t* empty = full + NST;
+    float4* red4 = reinterpret_cast<float4*>(smem + S::RED_OFF);   // [8 warps][MT] trackers, [MT] merged
+    int* redi = reinterpret_cast<int*>(red4 + kGemvWarps * MT + MT);  // last-CTA flag
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = gridDim.x, b = blockIdx.x;
+    const int r0 = static_cast<int>(static_cast<long long>(a.N) * b / G);
+    const int r1 = static_cast<int>(static_cast<long long>(a.N) * (b + 1) / G);
+    const int R = r1 - r0;
+    const int nstage = (R + SPS - 1) / SPS;
+
+    if (tid == 0)
+    {
+        for (int s = 0; s < NST; ++s)
+        {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], S::GPS);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == kGemvWarps)
+    {
+        // ---------------- producer ----------------
+        if (lane == 0)
+        {
+            const uint64_t pol = l2_evict_first_policy();
+            const WT* W = static_cast<const WT*>(a.W);
+            int issued = 0;
+            for (int i = 0; i < nstage; ++i)
+            {
+                const int slot = i % NST;
+                if (i >= NST && !mbar_wait(&empty[slot], ((i / NST) - 1) & 1, a.err, kErrTimeoutEmpty)) break;
+                const int sr0 = r0 + i * SPS;
+                const int nseg = min(SPS, r1 - sr0);
+                mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(nseg * SEG));
+                unsigned char* dst = ring + slot * STAGE;
+                if (a.ldw == KP)
+                {
+                    bulk_g2s(dst, W + static_cast<size_t>(sr0) * KP, static_cast<uint32_t>(nseg * SEG), &full[slot], pol);
+                }
+                else
+                {
+                    for (int j = 0; j < nseg; ++j)
+                        bulk_g2s(dst + j * SEG, W + static_cast<size_t>(sr0 + j) * a.ldw + a.k_off, SEG, &full[slot], pol);
+                }
+                issued = i + 1;
+            }
+            // Drain: never leave the CTA with copies in flight.
+            for (int i = (issued > NST ? issued - NST : 0); i < issued; ++i)
+                mbar_wait(&full[i % NST], (i / NST) & 1, a.err, kErrTimeoutFull);
+        }
+        return;
+    }
+
+    // ---------------- consumers (256 threads) ----------------
+    pdl_wait();
+
+    __shared__ int s_ids[kMaxStepRows];
+    __shared__ float s_rinv[kMaxStepRows];
+    __shared__ int s_prefix[kMaxStepRows];
+    const int rows = a.rows;
+
+    // Source row ids for gathers.
+    if (a.src != SRC_X)
+    {
+        if (tid < MT)
+        {
+            int id = 0;
+            if (tid < rows)
+            {
+                if (a.src == SRC_GATHER_STATE) id = a.st->cur_token;
+                else if (a.src == SRC_GATHER_IDS) id = a.ids[tid];
+                else id = draft_id(a.st, a.greedy, a.vocab, tid);
+                if (id < 0 || id >= a.vocab)
+                {
+                    atomicOr(a.err, kErrBounds);
+                    id = 0;
+                }
+                if (b == 0 && a.ids_out) a.ids_out[tid] = id;
+            }
+            s_ids[tid] = id;
+        }
+    }
+    if (EPI == EPI_ARGMAX && tid < MT) s_prefix[tid] = (a.prefix && tid < rows) ? a.prefix[tid] : -1;
+    consumers_sync();
+
+    // Stage the activation rows (fp32) in shared memory.
+    for (int m = 0; m < MT; ++m)
+    {
+        float* xr = xs + m * KP;
+        if (m >= rows)
+        {
+            for (int k = tid * 4; k < KP; k += 256 * 4) *reinterpret_cast<float4*>(xr + k) = make_float4(0.f, 0.f, 0.f, 0.f);
+            continue;
+        }
+        if (a.src != SRC_X)
+        {
+            const WT* trow = static_cast<const WT*>(a.table) + static_cast<size_t>(s_ids[m]) * kHidden;
+            for (int k = tid * 4; k < KP; k += 256 * 4)
+            {
+                const float4 v = load4(trow + k);
+                *reinterpret_cast<float4*>(xr + k) = v;
+            }
+        }
+        else if (PRO == PRO_SWIGLU)
+        {
+            const float* g = a.x + static_cast<size_t>(m) * a.ldx + a.k_off;
+            const float* u = g + a.up_off;
+            for (int k = tid * 4; k < KP; k += 256 * 4)
+            {
+                const float4 gv = *reinterpret_cast<const float4*>(g + k);
+                const float4 uv = *reinterpret_cast<const float4*>(u + k);
+                float4 r;
+                r.x = (gv.x / (1.0f + expf(-gv.x))) * uv.x;
+                r.y = (gv.y / (1.0f + expf(-gv.y))) * uv.y;
+                r.z = (gv.z / (1.0f + expf(-gv.z))) * uv.z;
+                r.w = (gv.w / (1.0f + expf(-gv.w))) * uv.w;
+                *reinterpret_cast<float4*>(xr + k) = r;
+            }
+        }
+        else
+        {
+            const float* xp = a.x + static_cast<size_t>(m) * a.ldx + a.k_off;
+            for (int k = tid * 4; k < KP; k += 256 * 4)
+                *reinterpret_cast<float4*>(xr + k) = *reinterpret_cast<const float4*>(xp + k);
+        }
+    }
+    consumers_sync();
+
+    // Gather: publish the embedding rows as the residual stream (CTA slices).
+    if (a.src != SRC_X && a.x_store)
+    {
+        const int total = rows * kHidden;
+        const int per = (total + G - 1) / G;
+        const int beg = b * per, end = min(total, beg + per);
+        for (int i = beg + tid; i < end; i += 256) a.x_store[i] = xs[(i / kHidden) * KP + (i % kHidden)];
+    }
+
+    if (PRO == PRO_NORM)
+    {
+        // Per-row 1/sqrt(mean(x^2) + eps), then xs = w * (x * rinv).
+        float* wsum = reinterpret_cast<float*>(red4);   // [8 warps][MT]
+        for (int m = 0; m < MT; ++m)
+        {
+            float ss = 0.f;
+            for (int k = tid * 4; k < KP; k += 256 * 4)
+            {
+                const float4 v = *reinterpret_cast<const float4*>(xs + m * KP + k);
+                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+            }
+            ss = warp_sum(ss);
+            if (lane == 0) wsum[warp * MT + m] = ss;
+        }
+        consumers_sync();
+        if (tid < MT)
+        {
+            float t = 0.f;
+            for (int w = 0; w < kGemvWarps; ++w) t += wsum[w * MT + tid];
+            s_rinv[tid] = 1.0f / sqrtf(t / static_cast<float>(KP) + a.eps);
+        }
+        consumers_sync();
+        for (int m = 0; m < rows; ++m)
+        {
+            const float ri = s_rinv[m];
+            for (int k = tid * 4; k < KP; k += 256 * 4)
+            {
+                float4 v = *reinterpret_cast<float4*>(xs + m * KP + k);
+                const float4 w = *reinterpret_cast<const float4*>(a.norm_w + a.k_off + k);
+                v.x = w.x * (v.x * ri);
+                v.y = w.y * (v.y * ri);
+                v.z = w.z * (v.z * ri);
+                v.w = w.w * (v.w * ri);
+                *reinterpret_cast<float4*>(xs + m * KP + k) = v;
+            }
+        }
+        consumers_sync();
+    }
+
+    pdl_launch();
+
+    // ---------------- main loop ----------------
+    const float pen = (EPI == EPI_ARGMAX) ? ((a.lm_mode == LM_NONE) ? a.penalty : a.st->penalty) : 1.0f;
+    ArgBest best;
+    best.rv = 0.f; best.ri = -1; best.pv = 0.f; best.pi = -1;
+    const int ngroups = (R + RPW - 1) / RPW;
+    for (int gi = warp; gi < ngroups; gi += kGemvWarps)
+    {
+        const int seg0 = gi * RPW;
+        const int stage = seg0 / SPS, slot = stage % NST;
+        const bool ok = mbar_wait(&full[slot], (stage / NST) & 1, a.err, kErrTimeoutFull);
+        if (!__all_sync(0xffffffffu, ok)) break;
+        const WT* wrow = reinterpret_cast<const WT*>(ring + slot * STAGE + (seg0 % SPS) * SEG);
+        const int nr = min(RPW, R - seg0);
+        float acc[RPW][MT];
+#pragma unroll
+        for (int r = 0; r < RPW; ++r)
+#pragma unroll
+            for (int m = 0; m < MT; ++m) acc[r][m] = 0.f;
+#pragma unroll 4
+        for (int c = lane; c < KP / 4; c += 32)
+        {
+            float4 w[RPW];
+#pragma unroll
+            for (int r = 0; r < RPW; ++r)
+                w[r] = (r < nr) ? load4(wrow + r * KP + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int m = 0; m < MT; ++m)
+            {
+                const float4 xv = *reinterpret_cast<const float4*>(xs + m * KP + 4 * c);
+#pragma unroll
+                for (int r = 0; r < RPW; ++r) acc[r][m] += dot4(w[r], xv);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < RPW; ++r)
+#pragma unroll
+            for (int m = 0; m < MT; ++m) acc[r][m] = warp_sum(acc[r][m]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+
+        const int n0 = r0 + seg0;
+        if (EPI == EPI_STORE || EPI == EPI_RESID)
+        {
+#pragma unroll
+            for (int r = 0; r < RPW; ++r)
+#pragma unroll
+                for (int m = 0; m < MT; ++m)
+                {
+                    if (lane == ((r * MT + m) & 31) && r < nr && m < rows)
+                    {
+                        const size_t o = static_cast<size_t>(m) * a.ldo + (n0 + r);
+                        float v = acc[r][m];
+                        if (EPI == EPI_RESID)
+                        {
+                            if (a.extra) v = a.extra[o] + v;
+                            v = a.out[o] + v;
+                            if (a.aux) a.aux[static_cast<size_t>(m) * a.ld_aux + (n0 + r)] = v;
+                        }
+                        a.out[o] = v;
+                    }
+                }
+        }
+        else
+        {
+            // Penalised argmax: lane m tracks activation row m.
+#pragma unroll
+            for (int r = 0; r < RPW; ++r)
+            {
+                if (r >= nr) break;
+                const int v = n0 + r;
+                const bool in_hist = (a.hist[v >> 5] >> (v & 31)) & 1u;
+#pragma unroll
+                for (int m = 0; m < MT; ++m)
+                {
+                    if (lane == m && m < rows)
+                    {
+                        const float s = acc[r][m];
+                        if (a.logits) a.logits[static_cast<size_t>(m) * a.ldl + v] = s;
+                        bool hit = in_hist;
+                        for (int j = 0; j <= m; ++j) hit |= (s_prefix[j] == v);
+                        const float ps = hit ? (s < 0.0f ? s * pen : s / pen) : s;
+                        if (best.ri < 0 || s > best.rv) { best.rv = s; best.ri = v; }
+                        if (best.pi < 0 || ps > best.pv) { best.pv = ps; best.pi = v; }
+                    }
+                }
+            }
+        }
+    }
+
+    if (EPI != EPI_ARGMAX) return;
+
+    // ---------------- argmax reduction ----------------
+    if (lane < MT)
+        red4[warp * MT + lane] = make_float4(best.rv, __int_as_float(best.ri), best.pv, __int_as_float(best.pi));
+    consumers_sync();
+    if (tid < MT)
+    {
+        float rv = 0.f, pv = 0.f;
+        int ri = -1, pi = -1;
+        for (int w = 0; w < kGemvWarps; ++w)
+        {
+            const float4 t = red4[w * MT + tid];
+            const int ti = __float_as_int(t.y), tp = __float_as_int(t.w);
+            if (ti >= 0) best_update(rv, ri, t.x, ti);
+            if (tp >= 0) best_update(pv, pi, t.z, tp);
+        }
+        a.part[b * MT + tid] = make_float4(rv, __int_as_float(ri), pv, __int_as_float(pi));
+        __threadfence();
+    }
+    consumers_sync();
+    if (tid == 0) redi[0] = (atomicAdd(a.counter, 1) == G - 1) ? 1 : 0;
+    consumers_sync();
+    if (!redi[0]) return;
+    __threadfence();
+
+    float4* merged = red4 + kGemvWarps * MT;   // [MT]
+    if (tid < MT)
+    {
+        float rv = 0.f, pv = 0.f;
+        int ri = -1, pi = -1;
+        for (int c = 0; c < G; ++c)
+        {
+            const float4 t = __ldcg(&a.part[c * MT + tid]);
+            const int ti = __float_as_int(t.y), tp = __float_as_int(t.w);
+            if (ti >= 0) best_update(rv, ri, t.x, ti);
+            if (tp >= 0) best_update(pv, pi, t.z, tp);
+        }
+        merged[tid] = make_float4(rv, __int_as_float(ri), pv, __int_as_float(pi));
+    }
+    consumers_sync();
+    if (tid != 0) return;
+    *a.counter = 0;
+
+    if (a.lm_mode == LM_NONE)
+    {
+        for (int m = 0; m < rows; ++m)
+        {
+            a.tok_out[m] = __float_as_int(merged[m].w);
+            a.raw_out[m] = __float_as_int(merged[m].y);
+        }
+        return;
+    }
+    DecodeState* st = a.st;
+    if (st->done) return;
+    if (a.lm_mode == LM_AR)
+    {
+        const int tok = __float_as_int(merged[0].w);
+        const int n = st->n_gen;
+        if (n >= st->max_tokens)
+        {
+            st->done = 1;
+            return;
+        }
+        a.log_tokens[n] = tok;
+        a.log_raw[n] = __float_as_int(merged[0].y);
+        st->n_gen = n + 1;
+        st->cur_token = tok;
+        st->kv_len += 1;
+        a.hist[tok >> 5] |= 1u << (tok & 31);
+        if (is_eos(st, tok) || n + 1 >= st->max_tokens) st->done = 1;
+        return;
+    }
+    // LM_VERIFY: dflash_acceptance_length + commit + rollback (src/dflash_runtime.cpp:78-95,
+    // src/text_runtime.cpp:1240-1296).
+    int posterior[kBlock];
+    for (int r = 0; r < kBlock; ++r)
+    {
+        posterior[r] = __float_as_int(merged[r].w);
+        a.posterior_out[r] = posterior[r];
+    }
+    int accept = 0;
+    for (int i = 1; i < kBlock; ++i)
+    {
+        if (s_prefix[i] != posterior[i - 1]) break;
+        ++accept;
+    }
+    const int available = accept + 1;
+    const int remaining = st->max_tokens - st->n_gen;
+    int committed = min(available, remaining);
+    int stop = 0;
+    for (int i = 0; i < committed; ++i)
+    {
+        const int tok = s_prefix[i];
+        a.log_tokens[st->n_gen + i] = tok;
+        a.log_raw[st->n_gen + i] = -1;
+        if (is_eos(st, tok))
+        {
+            committed = i + 1;
+            stop = 1;
+            break;
+        }
+    }
+    for (int i = 0; i < committed; ++i)
+    {
+        const int tok = s_prefix[i];
+        a.hist[tok >> 5] |= 1u << (tok & 31);
+    }
+    st->n_gen += committed;
+    a.accept_log[st->block_count] = max(0, committed - 1);
+    st->block_count += 1;
+    st->kv_len += committed;
+    st->cur_token = posterior[accept];
+    st->accept = accept;
+    st->committed = committed;
+    st->stop = stop;
+    if (committed < available || stop || st->n_gen >= st->max_tokens) st->done = 1;
+}
+
+}  // namespace hy

@@ -1,0 +1,224 @@
+/*
+ * hy_decode.h — C ABI of the B200 (sm_100a) text-decode library for
+ * HunyuanOCR 1.5's 24-layer text decoder.
+ *
+ * The library replaces the text-decode hot path of HunyuanOCR-ncnn: the ncnn
+ * decoder net driven by src/text_runtime.cpp, the PreciseSDPA and
+ * MultimodalRotaryEmbed custom layers, the KV-cache append helpers, the tied
+ * LM head and host token selection, and the DFlash verify/accept/rollback
+ * logic. Every entry point below names the reference interface it replaces
+ * (paths are relative to the HunyuanOCR-ncnn source tree).
+ *
+ * Conventions (mirroring the reference's `bool f(..., std::string* error)`):
+ *   - every function returns an int status, HY_OK (0) on success;
+ *   - on failure hy_last_error() returns a message for the calling thread;
+ *   - all pointers are HOST pointers unless a name says otherwise, tensors
+ *     are dense row-major fp32 (ids int32), sizes are element counts;
+ *   - one context owns one device, one CUDA stream, the weights and one
+ *     sequence's KV cache; calls on one context must not overlap (the
+ *     reference runtime is sequential too, README_en.md:167).
+ */
+#ifndef HY_DECODE_H
+#define HY_DECODE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum hy_status {
+    HY_OK = 0,
+    HY_ERR_INVALID_ARGUMENT = 1,
+    HY_ERR_CUDA = 2,
+    HY_ERR_OUT_OF_MEMORY = 3,
+    HY_ERR_CAPACITY = 4,       /* KV / prompt / token capacity exceeded */
+    HY_ERR_DEVICE_TIMEOUT = 5, /* a bounded device wait gave up */
+    HY_ERR_NOT_READY = 6,
+    HY_ERR_UNSUPPORTED = 7
+};
+
+enum hy_dtype { HY_DTYPE_F32 = 0, HY_DTYPE_BF16 = 1 };
+
+/* Fixed model geometry: src/text_decoder_step.h:19-24. */
+#define HY_HIDDEN 1024
+#define HY_HEAD_DIM 128
+#define HY_NUM_Q_HEADS 16
+#define HY_NUM_KV_HEADS 8
+/* DFlash block (include/hunyuan_ocr/dflash_runtime.h:17-18). */
+#define HY_DFLASH_BLOCK 16
+#define HY_DFLASH_MASK_TOKEN 120817
+/* Rows one decoder step accepts: 1 (AR) up to a DFlash block. */
+#define HY_MAX_STEP_ROWS 16
+/* Aux hidden states exported for the DFlash draft net
+ * (export/text_decoder_kv.py:11, layers 1, 8, 15, 22). */
+#define HY_NUM_AUX_LAYERS 4
+
+typedef struct hy_config {
+    int num_layers;     /* 24 */
+    int vocab_size;     /* 120818 */
+    int ffn_dim;        /* 3584; a multiple of 128 */
+    int max_context;    /* KV rows reserved per layer (prompt + generated + one block) */
+    int max_prefill;    /* longest prompt hy_prefill accepts */
+    int max_tokens;     /* longest generation (device token log) */
+    int weight_dtype;   /* HY_DTYPE_F32 (reference parity) or HY_DTYPE_BF16 */
+    int kv_dtype;       /* HY_DTYPE_F32 or HY_DTYPE_BF16 */
+    float rms_norm_eps; /* 1e-5 */
+    float attn_scale;   /* 0.0883883: export/add_kvcache.py:26 prints 1/sqrt(128) with %g */
+    int device;         /* CUDA device ordinal */
+} hy_config;
+
+/* nn.Linear layout [out x in]; norms are vectors (export/text_decoder_kv.py:49-96). */
+typedef struct hy_layer_weights {
+    const float* input_norm; /* [1024] */
+    const float* q_proj;     /* [2048 x 1024] */
+    const float* k_proj;     /* [1024 x 1024] */
+    const float* v_proj;     /* [1024 x 1024] */
+    const float* query_norm; /* [128] */
+    const float* key_norm;   /* [128] */
+    const float* o_proj;     /* [1024 x 2048] */
+    const float* post_norm;  /* [1024] */
+    const float* gate_proj;  /* [ffn x 1024] */
+    const float* up_proj;    /* [ffn x 1024] */
+    const float* down_proj;  /* [1024 x ffn] */
+} hy_layer_weights;
+
+typedef struct hy_weights {
+    const float* embed;              /* [vocab x 1024]: text_embed and the tied LM head */
+    const float* final_norm;         /* [1024] */
+    const hy_layer_weights* layers;  /* [num_layers] */
+} hy_weights;
+
+typedef struct hy_ctx hy_ctx;
+
+const char* hy_version(void);
+const char* hy_last_error(void);
+
+/* Defaults of the reference model (src/text_runtime.cpp:97-104). */
+int hy_config_init(hy_config* cfg);
+
+/* Replaces TextRuntime::load (src/text_runtime.cpp:1685-1749): uploads one
+ * device copy of the weights (the tied table serves both embedding and LM
+ * head, as SharedModelData does, src/mapped_model_file.h:50-67), reserves the
+ * KV cache and the 1-D RoPE table, and captures the step graphs. */
+int hy_ctx_create(const hy_config* cfg, const hy_weights* weights, hy_ctx** out);
+
+/* Same, with the weights generated on the device by the library's seeded
+ * counter generator (linears/embedding ~N(0, std), norms 1 + ~N(0, norm_std)).
+ * Used for benchmarks on synthetic random-init weights. */
+int hy_ctx_create_synthetic(const hy_config* cfg, uint64_t seed, float std, float norm_std, hy_ctx** out);
+
+void hy_ctx_destroy(hy_ctx* ctx);
+int hy_ctx_config(const hy_ctx* ctx, hy_config* cfg);
+size_t hy_ctx_device_bytes(const hy_ctx* ctx);   /* replaces mapped_weight_bytes() */
+
+/* ---- host table builders (host code, no device work) ---------------- */
+/* detail::build_mrope (src/text_runtime.cpp:42-63): position_ids [4 x seq]
+ * axis-major, out [seq x 128]. */
+int hy_build_mrope(const int* position_ids, int seq_len, int use_cos, float* out);
+/* rope_value (src/text_runtime.cpp:182-193). */
+float hy_rope_value(int position, int dim, int use_cos);
+
+/* ---- sequence state --------------------------------------------------- */
+/* Empty KV cache and penalty history. */
+int hy_seq_reset(hy_ctx* ctx);
+int hy_seq_length(hy_ctx* ctx, int* kv_rows);
+/* view_dflash_rows (src/dflash_runtime.cpp:97-119): keep the first `rows` KV rows. */
+int hy_seq_truncate(hy_ctx* ctx, int rows);
+/* Penalty history = set(ids) (select_next_token's unordered_set,
+ * src/text_runtime.cpp:744-750); hy_history_add inserts more ids. */
+int hy_history_set(hy_ctx* ctx, const int* ids, int n);
+int hy_history_add(hy_ctx* ctx, const int* ids, int n);
+
+/* ---- decoder ---------------------------------------------------------- */
+/* run_decoder_prefill (src/text_runtime.cpp:648-674) on an empty cache:
+ * inputs_embeds [seq x 1024], cos/sin [seq x 128] (hy_build_mrope), causal mask
+ * (make_prefill_mask, 207-219). Writes KV rows [0, seq). Outputs (nullable):
+ * last_hidden [1024] = final-normed hidden of the last row; aux_hidden
+ * [4 x seq x 1024] = un-normed hidden after layers 1, 8, 15, 22. */
+int hy_prefill(hy_ctx* ctx, const float* inputs_embeds, const float* cos, const float* sin, int seq_len,
+               float* last_hidden, float* aux_hidden);
+
+/* detail::run_decoder_step (src/text_decoder_step.h:29-38): `rows` (1..16)
+ * new embeddings at KV positions [len, len+rows) with row r attending to keys
+ * <= len + r (make_decode_mask / build_dflash_verify_mask). cos/sin [rows x 128].
+ * Appends the rows to the cache. hidden [rows x 1024] (final-normed, nullable),
+ * aux_hidden [4 x rows x 1024] (nullable). */
+int hy_decoder_step(hy_ctx* ctx, const float* embeds, int rows, const float* cos, const float* sin,
+                    float* hidden, float* aux_hidden);
+
+/* run_lm_head + select_logit_rows (src/text_runtime.cpp:430-439, 757-797) over
+ * `rows` final-normed hidden rows [rows x 1024] with the context's penalty
+ * history; row r also counts row_prefix[0..r] (nullable) as history.
+ * tokens/raw_top1 [rows]; logits [rows x vocab] (nullable). */
+int hy_lm_head_select(hy_ctx* ctx, const float* hidden, int rows, const int* row_prefix, float penalty,
+                      int* tokens, int* raw_top1, float* logits);
+
+/* ---- on-device loops -------------------------------------------------- */
+/* The AR loop of decode_from_embeddings (src/text_runtime.cpp:1417-1508):
+ * starting from first_token (already selected from the prefill logits and
+ * not yet in the history), runs up to max_tokens-1 decoder steps on the
+ * device, each one CUDA-graph launch (embed -> 24 layers -> LM head ->
+ * penalised argmax -> EOS check), with the token kept on the device.
+ * tokens/raw_top1 (nullable) receive n_tokens ids including first_token;
+ * raw_top1[0] is first_raw_top1. */
+int hy_generate(hy_ctx* ctx, int first_token, int first_raw_top1, int max_tokens, float penalty,
+                const int* eos_ids, int n_eos, int* tokens, int* raw_top1, int* n_tokens);
+
+/* One DFlash block, the verify half of run_dflash_block plus the commit of
+ * decode_dflash_from_embeddings (src/text_runtime.cpp:959-1070, 1240-1296):
+ * verify forward over proposed[16] at the current length, posterior with the
+ * per-row history, dflash_acceptance_length, commit of min(accept+1,
+ * max_commit) tokens (cut at EOS) and KV rollback to length + committed.
+ * posterior [16]; *stop is set when the commit hit EOS or was cut short. */
+int hy_verify_block(hy_ctx* ctx, const int* proposed, int max_commit, float penalty, const int* eos_ids,
+                    int n_eos, int* posterior, int* acceptance_length, int* committed, int* stop);
+
+/* The DFlash loop (src/text_runtime.cpp:1206-1296) entirely on the device,
+ * with a synthetic drafter standing in for the draft net: draft slot i of
+ * block b is greedy[n_committed + i] with probability p, else a uniform id
+ * (counter-generator stream `seed`). One graph launch per block. */
+int hy_dflash_generate_synthetic(hy_ctx* ctx, int first_token, int max_tokens, float penalty,
+                                 const int* eos_ids, int n_eos, const int* greedy, int n_greedy, float p,
+                                 uint64_t seed, int* tokens, int* n_tokens, int* acceptance_lengths,
+                                 int* n_blocks);
+
+/* TextRuntime::run_vlm_decode_with_prompt (src/text_runtime.cpp:2053-2094):
+ * prompt embedding with vision-feature injection (prepare_prompt_embeddings,
+ * 506-568), mRoPE tables, prefill, first-token selection and the AR loop.
+ * vision_features [vision_token_count x 1024]. */
+int hy_run_vlm_decode_with_prompt(hy_ctx* ctx, const int* input_ids, const int* position_ids, int seq_len,
+                                  int image_token_id, const float* vision_features, int vision_token_count,
+                                  int max_tokens, float repetition_penalty, const int* eos_ids, int n_eos,
+                                  int* tokens, int* raw_top1, int* n_tokens);
+
+/* ---- standalone kernels (benchmarks and parity tests) ----------------- */
+/* Attention alone (PreciseSDPA decode/verify, src/precise_sdpa.cpp:281-329,
+ * with the RoPE/QK-norm/append of export/text_decoder_kv.py:66-79): on layer
+ * `layer` at the current length, rows (1..16) of raw projections
+ * qkv [rows x 4096] (q 2048 | k 1024 | v 1024) are rotated with cos/sin
+ * [rows x 128], QK-normed, appended, and attended; out [rows x 2048]. */
+int hy_attention(hy_ctx* ctx, int layer, const float* qkv, int rows, const float* cos, const float* sin,
+                 float* out);
+/* Write/read KV rows [start, start+rows) of one layer; k, v [8 x rows x 128]. */
+int hy_kv_write(hy_ctx* ctx, int layer, int start, int rows, const float* k, const float* v);
+int hy_kv_read(hy_ctx* ctx, int layer, int start, int rows, float* k, float* v);
+int hy_seq_set_length(hy_ctx* ctx, int rows);
+
+/* ---- device-resident timing hooks (benchmarks) ------------------------ */
+/* Replays `count` AR step graphs back to back on the context's stream
+ * without host copies and returns the device time in ms (CUDA events). */
+int hy_bench_ar_steps(hy_ctx* ctx, int count, float* ms);
+/* Times `count` launches of one kernel family on the context's stream:
+ * which = 0: LM head GEMV + argmax (M=1); 1: gate/up GEMV of layer 0;
+ * 2: attention of layer 0 at the current length (M=1). ms = mean per launch. */
+int hy_bench_kernel(hy_ctx* ctx, int which, int count, float* ms);
+/* Raw stream handle (cudaStream_t) for external event timing. */
+void* hy_ctx_stream(hy_ctx* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HY_DECODE_H */

@@ -1,0 +1,662 @@
+"""CPU oracle for the HunyuanOCR text-decode hot path (test infrastructure).
+
+This module is the checker, not the product. Only tests/, the smoke check in
+__graft_entry__.py and bench.py's CPU-baseline leg may import it. The product
+path (the CUDA library behind include/hy_decode.h) never calls into it.
+
+It restates, in numpy, the reference's CPU fp32 decode path:
+  * the decoder graph of export/text_decoder_kv.py (``_layer_forward`` 49-96,
+    ``prefill`` 98-112, ``decode`` 168-183) that ncnn executes through
+    ``run_decoder_step_impl`` (src/text_runtime.cpp:678-728);
+  * PreciseSDPA's fp64-accumulated attention (src/precise_sdpa.cpp:281-329),
+    with the ``%g``-printed scale literal 0.0883883 written into the ncnn param
+    by export/add_kvcache.py:26,57-59;
+  * the full-width RoPE of src/multimodal_rope.cpp:176-187;
+  * the host logic of src/text_runtime.cpp (build_mrope 42-63, rope_value
+    182-193, masks 207-251, select_next_token 730-755, select_logit_rows
+    757-797, the AR loop 1307-1521, the DFlash block 880-1071 and loop
+    1142-1305) and src/dflash_runtime.cpp (build_dflash_block 20-25,
+    build_dflash_verify_mask 60-76, dflash_acceptance_length 78-95).
+
+Pinning: tests/test_oracle_golden.py checks this module against
+tests/golden/*.npz, produced by tests/golden/make_golden.py from the
+reference's own TextDecoderExternalRopeKVWrapper (export/text_decoder_kv.py)
+over a random-init transformers HunYuanDenseV1Model, and against the
+known-answer values of the reference's C++ tests (tests/text_rope_test.cpp,
+tests/multimodal_rope_test.cpp, tests/precise_sdpa_test.cpp,
+tests/dflash_runtime_test.cpp).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+from dataclasses import dataclass, field
+
+import numpy as np
+
+# Model constants: src/text_decoder_step.h:19-24, src/text_runtime.cpp:97-104,
+# include/hunyuan_ocr/dflash_runtime.h:17-18.
+HIDDEN = 1024
+HEAD_DIM = 128
+NUM_Q_HEADS = 16
+NUM_KV_HEADS = 8
+Q_WIDTH = NUM_Q_HEADS * HEAD_DIM          # 2048
+KV_WIDTH = NUM_KV_HEADS * HEAD_DIM        # 1024
+FFN = 3584
+VOCAB = 120818
+NUM_LAYERS = 24
+RMS_EPS = 1e-5
+ROPE_THETA = 10000.0
+ROPE_ALPHA = 1000.0
+MASK_NEG_INF = np.float32(-1.0e38)
+DEFAULT_PENALTY = 1.08
+DFLASH_BLOCK = 16
+DFLASH_MASK_TOKEN = 120817
+IMAGE_TOKEN_ID = 120120                   # src/prompt_builder.cpp:8
+EOS_ID = 120020                           # models/model.json.example
+DFLASH_TARGET_LAYER_IDS = (1, 8, 15, 22)  # export/text_decoder_kv.py:11
+# export/add_kvcache.py:26 writes f"{1/sqrt(128):g}" into the SDPA param.
+NCNN_SDPA_SCALE = float(np.float32(float(f"{1.0 / math.sqrt(HEAD_DIM):g}")))
+EXACT_SDPA_SCALE = 1.0 / math.sqrt(HEAD_DIM)
+
+
+# ---------------------------------------------------------------------------
+# Synthetic weights (same generator as oracle/synth.c and the CUDA library).
+# ---------------------------------------------------------------------------
+_M64 = (1 << 64) - 1
+_GOLDEN = 0x9E3779B97F4A7C15
+_TID = 0xD1B54A32D192ED03
+
+
+def _splitmix64_scalar(z: int) -> int:
+    z = (z + _GOLDEN) & _M64
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & _M64
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & _M64
+    return z ^ (z >> 31)
+
+
+def _splitmix64_np(z: np.ndarray) -> np.ndarray:
+    z = z + np.uint64(_GOLDEN)
+    z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+    z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+    return z ^ (z >> np.uint64(31))
+
+
+def synth_mult(std: float) -> np.float32:
+    return np.float32(float(std) * math.sqrt(3.0) / 65536.0)
+
+
+def synth_tensor(seed: int, tensor_id: int, count: int, std: float, offset: float = 0.0) -> np.ndarray:
+    """Counter-based generator; see the header of oracle/synth.c for the definition."""
+    base = _splitmix64_scalar((seed * _GOLDEN + tensor_id * _TID) & _M64)
+    out = np.empty(count, dtype=np.float32)
+    mult = synth_mult(std)
+    off = np.float32(offset)
+    chunk = 1 << 22
+    with np.errstate(over="ignore"):
+        for start in range(0, count, chunk):
+            n = min(chunk, count - start)
+            idx = np.arange(start, start + n, dtype=np.uint64) + np.uint64(base)
+            h = _splitmix64_np(idx)
+            s = ((h & np.uint64(0xFFFF)) + ((h >> np.uint64(16)) & np.uint64(0xFFFF))
+                 + ((h >> np.uint64(32)) & np.uint64(0xFFFF)) + (h >> np.uint64(48)))
+            c = (s.astype(np.int64) - 131070).astype(np.float32)
+            out[start:start + n] = off + c * mult
+    return out
+
+
+_SYNTH_LIB = None
+
+
+def _synth_lib():
+    global _SYNTH_LIB
+    if _SYNTH_LIB is None:
+        path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libhy_synth.so")
+        if not os.path.exists(path):
+            return None
+        lib = ctypes.CDLL(path)
+        lib.hy_synth_fill.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float, ctypes.c_float,
+                                      ctypes.c_void_p, ctypes.c_size_t]
+        lib.hy_synth_fill.restype = None
+        _SYNTH_LIB = lib
+    return _SYNTH_LIB
+
+
+def synth_tensor_fast(seed: int, tensor_id: int, count: int, std: float, offset: float = 0.0) -> np.ndarray:
+    """Same values as synth_tensor, through oracle/libhy_synth.so when it is built."""
+    lib = _synth_lib()
+    if lib is None:
+        return synth_tensor(seed, tensor_id, count, std, offset)
+    out = np.empty(count, dtype=np.float32)
+    lib.hy_synth_fill(seed, tensor_id, std, offset, out.ctypes.data, count)
+    return out
+
+
+# Tensor ids of the synthetic weight set (shared with the CUDA generator).
+TID_EMBED = 1
+TID_FINAL_NORM = 2
+LAYER_TID_BASE = 100
+LAYER_TID_STRIDE = 16
+(J_INPUT_NORM, J_Q, J_K, J_V, J_Q_NORM, J_K_NORM, J_O, J_POST_NORM, J_GATE, J_UP, J_DOWN) = range(11)
+
+
+@dataclass
+class ModelConfig:
+    num_layers: int = NUM_LAYERS
+    vocab: int = VOCAB
+    ffn: int = FFN
+    rms_eps: float = RMS_EPS
+    attn_scale: float = NCNN_SDPA_SCALE
+
+
+@dataclass
+class LayerWeights:
+    input_norm: np.ndarray
+    q: np.ndarray
+    k: np.ndarray
+    v: np.ndarray
+    q_norm: np.ndarray
+    k_norm: np.ndarray
+    o: np.ndarray
+    post_norm: np.ndarray
+    gate: np.ndarray
+    up: np.ndarray
+    down: np.ndarray
+
+
+@dataclass
+class Weights:
+    embed: np.ndarray
+    final_norm: np.ndarray
+    layers: list = field(default_factory=list)
+
+
+def make_weights(cfg: ModelConfig, seed: int, std: float = 0.02, norm_std: float = 0.0,
+                 fast: bool = True) -> Weights:
+    """Seeded N(0, std)-like linears/embedding, norms = 1 + N(0, norm_std)."""
+    gen = synth_tensor_fast if fast else synth_tensor
+
+    def lin(tid, rows, cols):
+        return gen(seed, tid, rows * cols, std).reshape(rows, cols)
+
+    def norm(tid, n):
+        return gen(seed, tid, n, norm_std, 1.0)
+
+    layers = []
+    for li in range(cfg.num_layers):
+        b = LAYER_TID_BASE + LAYER_TID_STRIDE * li
+        layers.append(LayerWeights(
+            input_norm=norm(b + J_INPUT_NORM, HIDDEN),
+            q=lin(b + J_Q, Q_WIDTH, HIDDEN),
+            k=lin(b + J_K, KV_WIDTH, HIDDEN),
+            v=lin(b + J_V, KV_WIDTH, HIDDEN),
+            q_norm=norm(b + J_Q_NORM, HEAD_DIM),
+            k_norm=norm(b + J_K_NORM, HEAD_DIM),
+            o=lin(b + J_O, HIDDEN, Q_WIDTH),
+            post_norm=norm(b + J_POST_NORM, HIDDEN),
+            gate=lin(b + J_GATE, cfg.ffn, HIDDEN),
+            up=lin(b + J_UP, cfg.ffn, HIDDEN),
+            down=lin(b + J_DOWN, HIDDEN, cfg.ffn),
+        ))
+    return Weights(embed=lin(TID_EMBED, cfg.vocab, HIDDEN),
+                   final_norm=norm(TID_FINAL_NORM, HIDDEN), layers=layers)
+
+
+# ---------------------------------------------------------------------------
+# Host logic: RoPE tables and masks.
+# ---------------------------------------------------------------------------
+def _f32(x) -> np.float32:
+    return np.float32(x)
+
+
+def mrope_base() -> np.float32:
+    # src/text_runtime.cpp:47 and 184-187: float(10000 * 1000^(128/126)) in double.
+    return _f32(ROPE_THETA * math.pow(ROPE_ALPHA, HEAD_DIM / (HEAD_DIM - 2)))
+
+
+def inv_freq_table() -> np.ndarray:
+    """inv_freq[d] = 1.0f / powf(base, float(2*(d%64))/128) (src/text_runtime.cpp:53, 188-189)."""
+    base = mrope_base()
+    out = np.empty(HEAD_DIM, dtype=np.float32)
+    for d in range(HEAD_DIM):
+        fd = d % (HEAD_DIM // 2)
+        expo = _f32(_f32(2 * fd) / _f32(HEAD_DIM))
+        # powf is evaluated in double and rounded once (a correctly rounded powf).
+        out[d] = _f32(1.0) / _f32(math.pow(float(base), float(expo)))
+    return out
+
+
+def _cos32(angle: np.ndarray) -> np.ndarray:
+    """cosf of fp32 angles, evaluated in double and rounded once."""
+    return np.cos(np.asarray(angle, dtype=np.float32).astype(np.float64)).astype(np.float32)
+
+
+def _sin32(angle: np.ndarray) -> np.ndarray:
+    return np.sin(np.asarray(angle, dtype=np.float32).astype(np.float64)).astype(np.float32)
+
+
+def build_mrope(position_ids: np.ndarray, seq_len: int, use_cos: bool) -> np.ndarray:
+    """src/text_runtime.cpp:42-63: dim d uses position axis d/32 and frequency index d%64."""
+    pos = np.asarray(position_ids, dtype=np.int32).reshape(4, seq_len)
+    inv = inv_freq_table()
+    out = np.empty((seq_len, HEAD_DIM), dtype=np.float32)
+    for d in range(HEAD_DIM):
+        axis = d // (HEAD_DIM // 4)
+        angle = pos[axis].astype(np.float32) * inv[d]
+        out[:, d] = _cos32(angle) if use_cos else _sin32(angle)
+    return out
+
+
+def rope_rows(start: int, rows: int, use_cos: bool) -> np.ndarray:
+    """build_decode_rope / build_verify_rope (src/text_runtime.cpp:228-251) via rope_value (182-193)."""
+    inv = inv_freq_table()
+    pos = np.arange(start, start + rows, dtype=np.int64).astype(np.float32)
+    angle = (pos[:, None] * inv[None, :]).astype(np.float32)
+    return _cos32(angle) if use_cos else _sin32(angle)
+
+
+def make_prefill_mask(seq_len: int) -> np.ndarray:
+    """src/text_runtime.cpp:207-219."""
+    r = np.arange(seq_len)
+    return np.where(r[None, :] > r[:, None], MASK_NEG_INF, np.float32(0.0)).astype(np.float32)
+
+
+def make_decode_mask(past_len: int) -> np.ndarray:
+    """src/text_runtime.cpp:221-226."""
+    return np.zeros((1, past_len + 1), dtype=np.float32)
+
+
+def build_dflash_verify_mask(past_len: int) -> np.ndarray:
+    """src/dflash_runtime.cpp:60-76: row r sees columns <= past_len + r."""
+    key_len = past_len + DFLASH_BLOCK
+    col = np.arange(key_len)[None, :]
+    row = np.arange(DFLASH_BLOCK)[:, None]
+    return np.where(col > past_len + row, MASK_NEG_INF, np.float32(0.0)).astype(np.float32)
+
+
+def build_dflash_block(first_token: int) -> list:
+    """src/dflash_runtime.cpp:20-25."""
+    return [int(first_token)] + [DFLASH_MASK_TOKEN] * (DFLASH_BLOCK - 1)
+
+
+def dflash_acceptance_length(proposed, posterior) -> int:
+    """src/dflash_runtime.cpp:78-95."""
+    if len(proposed) == 0 or len(proposed) != len(posterior):
+        return -1
+    accepted = 0
+    for i in range(1, len(proposed)):
+        if proposed[i] != posterior[i - 1]:
+            break
+        accepted += 1
+    return accepted
+
+
+# ---------------------------------------------------------------------------
+# Decoder math.
+# ---------------------------------------------------------------------------
+def rms_norm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    """HunYuanDenseV1RMSNorm: x * rsqrt(mean(x^2) + eps), then weight * (.)."""
+    x = x.astype(np.float32)
+    var = np.mean(x * x, axis=-1, keepdims=True, dtype=np.float32)
+    return (w * (x * (np.float32(1.0) / np.sqrt(var + np.float32(eps))))).astype(np.float32)
+
+
+def apply_rope(x: np.ndarray, cos: np.ndarray, sin: np.ndarray) -> np.ndarray:
+    """Full-width non-interleaved RoPE (src/multimodal_rope.cpp:176-187).
+
+    x [..., rows, 128]; cos/sin [rows, 128].
+    out[d] = x[d] c[d] - x[d+64] s[d];  out[d+64] = x[d+64] c[d+64] + x[d] s[d+64].
+    """
+    h = x.shape[-1] // 2
+    x1, x2 = x[..., :h], x[..., h:]
+    out = np.empty_like(x, dtype=np.float32)
+    out[..., :h] = x1 * cos[:, :h] - x2 * sin[:, :h]
+    out[..., h:] = x2 * cos[:, h:] + x1 * sin[:, h:]
+    return out
+
+
+def precise_sdpa(q: np.ndarray, k: np.ndarray, v: np.ndarray, mask: np.ndarray, scale: float) -> np.ndarray:
+    """PreciseSDPA decode/verify (src/precise_sdpa.cpp:281-329), GQA without expansion.
+
+    q [16, M, 128]; k, v [8, L, 128] (8 unique KV heads; q head h reads KV head
+    h // 2, which is what repeat_kv_for_attention's expansion amounts to,
+    export/text_decoder_kv.py:21-27); mask [M, L] additive. fp64 accumulation.
+    """
+    groups = q.shape[0] // k.shape[0]
+    out = np.empty(q.shape, dtype=np.float32)
+    m64 = mask.astype(np.float64)
+    for kvh in range(k.shape[0]):
+        k64 = k[kvh].astype(np.float64)
+        v64 = v[kvh].astype(np.float64)
+        for g in range(groups):
+            h = kvh * groups + g
+            s = (q[h].astype(np.float64) @ k64.T) * float(scale) + m64
+            s = np.exp(s - s.max(axis=1, keepdims=True))
+            s /= s.sum(axis=1, keepdims=True)
+            out[h] = (s @ v64).astype(np.float32)
+    return out
+
+
+@dataclass
+class KVCache:
+    """Per layer K/V [8, capacity, 128] fp32 and the logical length (rows)."""
+    k: list
+    v: list
+    length: int = 0
+
+    @staticmethod
+    def empty(num_layers: int, capacity: int) -> "KVCache":
+        return KVCache([np.zeros((NUM_KV_HEADS, capacity, HEAD_DIM), np.float32) for _ in range(num_layers)],
+                       [np.zeros((NUM_KV_HEADS, capacity, HEAD_DIM), np.float32) for _ in range(num_layers)], 0)
+
+
+def layer_forward(lw: LayerWeights, x: np.ndarray, mask: np.ndarray, cos: np.ndarray, sin: np.ndarray,
+                  cache_k: np.ndarray, cache_v: np.ndarray, past: int, cfg: ModelConfig) -> np.ndarray:
+    """One decoder layer (export/text_decoder_kv.py:49-96); appends M rows at `past`.
+
+    x [M, 1024]. Keys are cached after RoPE and key_layernorm, as PreciseSDPA
+    appends the post-norm keys (src/precise_sdpa.cpp:233-262).
+    """
+    m_rows = x.shape[0]
+    h = rms_norm(x, lw.input_norm, cfg.rms_eps)
+    q = (h @ lw.q.T).reshape(m_rows, NUM_Q_HEADS, HEAD_DIM).transpose(1, 0, 2)
+    k = (h @ lw.k.T).reshape(m_rows, NUM_KV_HEADS, HEAD_DIM).transpose(1, 0, 2)
+    v = (h @ lw.v.T).reshape(m_rows, NUM_KV_HEADS, HEAD_DIM).transpose(1, 0, 2)
+    q = apply_rope(q, cos, sin)
+    k = apply_rope(k, cos, sin)
+    q = rms_norm(q, lw.q_norm, cfg.rms_eps)
+    k = rms_norm(k, lw.k_norm, cfg.rms_eps)
+    cache_k[:, past:past + m_rows] = k
+    cache_v[:, past:past + m_rows] = v
+    L = past + m_rows
+    attn = precise_sdpa(q, cache_k[:, :L], cache_v[:, :L], mask, cfg.attn_scale)
+    attn = attn.transpose(1, 0, 2).reshape(m_rows, Q_WIDTH)
+    x = (x + attn @ lw.o.T).astype(np.float32)
+    m = rms_norm(x, lw.post_norm, cfg.rms_eps)
+    g = m @ lw.gate.T
+    u = m @ lw.up.T
+    act = (g / (np.float32(1.0) + np.exp(-g))) * u
+    return (x + act.astype(np.float32) @ lw.down.T).astype(np.float32)
+
+
+def decoder_forward(w: Weights, cfg: ModelConfig, x: np.ndarray, mask: np.ndarray, cos: np.ndarray,
+                    sin: np.ndarray, cache: KVCache, aux: bool = False):
+    """Prefill/decode/verify over all layers, final norm applied (export/text_decoder_kv.py:98-183).
+
+    Returns (normed hidden [M,1024], aux hidden list or None). Advances cache.length by M.
+    """
+    past = cache.length
+    x = x.astype(np.float32)
+    aux_out = [] if aux else None
+    for li, lw in enumerate(w.layers):
+        x = layer_forward(lw, x, mask, cos, sin, cache.k[li], cache.v[li], past, cfg)
+        if aux and li in DFLASH_TARGET_LAYER_IDS:
+            aux_out.append(x.copy())
+    cache.length = past + x.shape[0]
+    return rms_norm(x, w.final_norm, cfg.rms_eps), aux_out
+
+
+def lm_head(w: Weights, hidden: np.ndarray) -> np.ndarray:
+    """Tied LM head (export/export_lm_head.py:16-24): logits = h E^T."""
+    return (hidden.astype(np.float32) @ w.embed.T).astype(np.float32)
+
+
+def select_next_token(logits: np.ndarray, history, penalty: float):
+    """src/text_runtime.cpp:730-755. Returns (token, raw_top1).
+
+    raw top-1 is the first index of the strict maximum; then each unique history
+    id in [0, V) is penalised (s<0 ? s*pen : s/pen) and the first index of the
+    maximum is returned.
+    """
+    scores = np.array(logits, dtype=np.float32, copy=True)
+    raw = int(np.argmax(scores))
+    pen = np.float32(penalty)
+    ids = np.unique(np.asarray(list(history), dtype=np.int64))
+    ids = ids[(ids >= 0) & (ids < scores.shape[0])]
+    s = scores[ids]
+    scores[ids] = np.where(s < 0, s * pen, s / pen)
+    return int(np.argmax(scores)), raw
+
+
+def select_logit_rows(logits: np.ndarray, initial_history, row_prefix, penalty: float) -> list:
+    """src/text_runtime.cpp:757-797: row r's history is initial + row_prefix[0..r]."""
+    history = list(initial_history)
+    out = []
+    for r in range(logits.shape[0]):
+        if row_prefix is not None:
+            history.append(int(row_prefix[r]))
+        out.append(select_next_token(logits[r], history, penalty)[0])
+    return out
+
+
+def top2_margin(logits: np.ndarray) -> float:
+    part = np.partition(logits.astype(np.float64), -2)
+    return float(part[-1] - part[-2])
+
+
+# ---------------------------------------------------------------------------
+# Prompt and loops.
+# ---------------------------------------------------------------------------
+@dataclass
+class Prompt:
+    input_ids: np.ndarray        # [seq] int32
+    position_ids: np.ndarray     # [4, seq] int32, axis-major
+    vision_features: np.ndarray  # [n_img, 1024] fp32
+    image_token_id: int = IMAGE_TOKEN_ID
+
+
+TID_PROMPT_FEATURES = 9001
+TID_PROMPT_IDS = 9002
+
+
+def synth_ids(seed: int, tensor_id: int, count: int, vocab: int) -> np.ndarray:
+    """Uniform ids in [0, vocab): splitmix64 of the same counter stream, modulo vocab."""
+    base = _splitmix64_scalar((seed * _GOLDEN + tensor_id * _TID) & _M64)
+    with np.errstate(over="ignore"):
+        h = _splitmix64_np(np.arange(count, dtype=np.uint64) + np.uint64(base))
+    return (h % np.uint64(vocab)).astype(np.int64)
+
+
+def synthetic_prompt(seed: int, grid_h: int, grid_w: int, n_text: int, vocab: int,
+                     image_token_id: int = IMAGE_TOKEN_ID) -> Prompt:
+    """Image rows first on a grid_h x grid_w mRoPE grid, then n_text text ids.
+
+    Image slot i: axis0 = i, axis1 = i % grid_w, axis2 = i // grid_w, axis3 = 0
+    (the spatial id layout of src/prompt_builder.cpp:94-120); text slots carry
+    their sequence index on all four axes. Features are N(0,1)-like from the
+    counter generator; text ids are uniform in [0, vocab) and never equal the
+    image token id.
+    """
+    n_img = grid_h * grid_w
+    seq = n_img + n_text
+    text = synth_ids(seed, TID_PROMPT_IDS, n_text, vocab)
+    text = np.where(text == image_token_id, (text + 1) % vocab, text)
+    ids = np.concatenate([np.full(n_img, image_token_id, np.int64), text]).astype(np.int32)
+    pos = np.tile(np.arange(seq, dtype=np.int32), (4, 1))
+    i = np.arange(n_img)
+    pos[1, :n_img] = i % grid_w
+    pos[2, :n_img] = i // grid_w
+    pos[3, :n_img] = 0
+    feats = synth_tensor_fast(seed, TID_PROMPT_FEATURES, n_img * HIDDEN, 1.0).reshape(n_img, HIDDEN)
+    return Prompt(ids, pos, feats, image_token_id)
+
+
+def prepare_prompt_embeddings(w: Weights, prompt: Prompt) -> np.ndarray:
+    """src/text_runtime.cpp:506-568: embed ids, then inject features at image slots in order."""
+    ids = prompt.input_ids.astype(np.int64)
+    emb = w.embed[np.clip(ids, 0, w.embed.shape[0] - 1)].copy()
+    slots = np.nonzero(ids == prompt.image_token_id)[0]
+    if len(slots) != prompt.vision_features.shape[0]:
+        raise ValueError("image token count mismatch")
+    emb[slots] = prompt.vision_features
+    return emb.astype(np.float32)
+
+
+@dataclass
+class DecodeTrace:
+    tokens: list
+    raw_top1: list
+    margins: list
+    logits: list          # per generated token (optional, when keep_logits)
+    hidden: list
+
+
+def prefill(w: Weights, cfg: ModelConfig, prompt: Prompt, capacity: int, aux: bool = False):
+    """run_decoder_prefill (src/text_runtime.cpp:648-674) with the 4-axis mRoPE tables."""
+    seq = prompt.input_ids.shape[0]
+    emb = prepare_prompt_embeddings(w, prompt)
+    cos = build_mrope(prompt.position_ids, seq, True)
+    sin = build_mrope(prompt.position_ids, seq, False)
+    cache = KVCache.empty(cfg.num_layers, capacity)
+    hidden, aux_h = decoder_forward(w, cfg, emb, make_prefill_mask(seq), cos, sin, cache, aux)
+    return hidden, cache, aux_h
+
+
+def decode_ar(w: Weights, cfg: ModelConfig, prompt: Prompt, max_tokens: int, penalty: float = DEFAULT_PENALTY,
+              eos_ids=(), capacity: int | None = None, keep_logits: bool = False,
+              prefill_state=None) -> DecodeTrace:
+    """decode_from_embeddings (src/text_runtime.cpp:1307-1521)."""
+    seq = prompt.input_ids.shape[0]
+    if capacity is None:
+        capacity = seq + max_tokens + DFLASH_BLOCK
+    if prefill_state is None:
+        hidden, cache, _ = prefill(w, cfg, prompt, capacity)
+    else:
+        hidden, cache = prefill_state
+    logits = lm_head(w, hidden[seq - 1:seq])[0]
+    history = [int(t) for t in prompt.input_ids]
+    tok, raw = select_next_token(logits, history, penalty)
+    tr = DecodeTrace([], [], [], [], [])
+    tr.margins.append(top2_margin(logits))
+    if keep_logits:
+        tr.logits.append(logits)
+        tr.hidden.append(hidden[seq - 1].copy())
+    for out_index in range(max_tokens):
+        tr.tokens.append(tok)
+        tr.raw_top1.append(raw)
+        history.append(tok)
+        if tok in eos_ids or out_index + 1 >= max_tokens:
+            break
+        emb = w.embed[tok:tok + 1]
+        position = seq + out_index
+        cos = rope_rows(position, 1, True)
+        sin = rope_rows(position, 1, False)
+        h, _ = decoder_forward(w, cfg, emb, make_decode_mask(position), cos, sin, cache)
+        logits = lm_head(w, h)[0]
+        tok, raw = select_next_token(logits, history, penalty)
+        tr.margins.append(top2_margin(logits))
+        if keep_logits:
+            tr.logits.append(logits)
+            tr.hidden.append(h[0].copy())
+    return tr
+
+
+def verify_block(w: Weights, cfg: ModelConfig, cache: KVCache, proposed, history_before_block,
+                 penalty: float):
+    """The verify half of run_dflash_block (src/text_runtime.cpp:959-1070).
+
+    Runs the M=16 verify forward at positions context_len..context_len+15 with
+    the causal-in-block mask, then select_logit_rows with the growing history.
+    Returns (posterior, acceptance_length, logits, hidden); the cache keeps
+    context_len + 16 rows (the caller rolls back).
+    """
+    ctx = cache.length
+    emb = w.embed[np.asarray(proposed, dtype=np.int64)]
+    mask = build_dflash_verify_mask(ctx)
+    cos = rope_rows(ctx, DFLASH_BLOCK, True)
+    sin = rope_rows(ctx, DFLASH_BLOCK, False)
+    hidden, _ = decoder_forward(w, cfg, emb, mask, cos, sin, cache)
+    logits = lm_head(w, hidden)
+    posterior = select_logit_rows(logits, history_before_block, proposed, penalty)
+    return posterior, dflash_acceptance_length(proposed, posterior), logits, hidden
+
+
+@dataclass
+class DFlashTrace:
+    tokens: list
+    acceptance_lengths: list
+    block_count: int = 0
+    drafted: int = 0
+    accepted: int = 0
+
+
+def decode_dflash(w: Weights, cfg: ModelConfig, prompt: Prompt, max_tokens: int, draft_fn,
+                  penalty: float = DEFAULT_PENALTY, eos_ids=(), capacity: int | None = None,
+                  prefill_state=None) -> DFlashTrace:
+    """decode_dflash_from_embeddings (src/text_runtime.cpp:1142-1305).
+
+    draft_fn(block_index, n_committed, current_token) -> 15 draft ids stands in
+    for the draft network (src/dflash_runtime.cpp:213-290).
+    """
+    seq = prompt.input_ids.shape[0]
+    if capacity is None:
+        capacity = seq + max_tokens + 2 * DFLASH_BLOCK
+    if prefill_state is None:
+        hidden, cache, _ = prefill(w, cfg, prompt, capacity)
+    else:
+        hidden, cache = prefill_state
+    logits = lm_head(w, hidden[seq - 1:seq])[0]
+    history = [int(t) for t in prompt.input_ids]
+    current, _ = select_next_token(logits, history, penalty)
+    tr = DFlashTrace([], [])
+    stop = False
+    block_index = 0
+    while len(tr.tokens) < max_tokens and not stop:
+        ctx = cache.length
+        proposed = build_dflash_block(current)
+        proposed[1:] = [int(t) for t in draft_fn(block_index, len(tr.tokens), current)]
+        posterior, accept, _, _ = verify_block(w, cfg, cache, proposed, history, penalty)
+        if accept < 0 or accept >= DFLASH_BLOCK:
+            raise RuntimeError("invalid DFlash acceptance length")
+        available = accept + 1
+        remaining = max_tokens - len(tr.tokens)
+        committed = min(available, remaining)
+        for i in range(committed):
+            tok = proposed[i]
+            tr.tokens.append(tok)
+            if tok in eos_ids:
+                committed = i + 1
+                stop = True
+                break
+        tr.block_count += 1
+        tr.drafted += DFLASH_BLOCK - 1
+        tr.accepted += max(0, committed - 1)
+        tr.acceptance_lengths.append(max(0, committed - 1))
+        block_index += 1
+        if committed < available or stop or len(tr.tokens) >= max_tokens:
+            break
+        cache.length = ctx + committed            # view_dflash_rows rollback
+        history.extend(proposed[:committed])
+        current = posterior[accept]
+    return tr
+
+
+TID_DRAFTS = 9003
+
+
+def synthetic_drafter(greedy: list, p: float, vocab: int, seed: int):
+    """Config-3 drafts: draft i of a block equals the target's greedy token with probability p.
+
+    For block b and draft slot i in 1..15: h = splitmix64(base + 16*b + i) on
+    the counter stream of (seed, TID_DRAFTS); u = (h >> 40) * 2^-24; the draft
+    is greedy[n_committed + i] when u < p (and that index exists), else
+    (h & 0xFFFFFFFF) % vocab. The CUDA library's device drafter uses the same
+    rule, so both sides see identical drafts.
+    """
+    base = _splitmix64_scalar((seed * _GOLDEN + TID_DRAFTS * _TID) & _M64)
+    pf = np.float32(p)
+
+    def fn(block_index: int, n_committed: int, current: int):
+        out = []
+        for i in range(1, DFLASH_BLOCK):
+            h = _splitmix64_scalar((base + 16 * block_index + i) & _M64)
+            u = np.float32(h >> 40) * np.float32(2.0 ** -24)
+            j = n_committed + i
+            if u < pf and j < len(greedy):
+                out.append(int(greedy[j]))
+            else:
+                out.append(int((h & 0xFFFFFFFF) % vocab))
+        return out
+    return fn
