@@ -45,7 +45,10 @@ EXPORTED_SYMBOLS = (
     "hy_prefill", "hy_decoder_step", "hy_lm_head_select", "hy_generate", "hy_verify_block",
     "hy_dflash_generate_synthetic", "hy_run_vlm_decode_with_prompt", "hy_attention", "hy_kv_write",
     "hy_kv_read", "hy_seq_set_length", "hy_bench_ar_steps", "hy_bench_kernel", "hy_ctx_stream",
+    "hy_ctx_set_ar_path", "hy_ctx_ar_path", "hy_trace_persistent", "hy_debug_progress",
 )
+AR_PATH_PERSISTENT = 0
+AR_PATH_GRAPH = 1
 
 
 class HyError(RuntimeError):
@@ -123,6 +126,10 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "hy_kv_read": ([_P, _I, _I, _I, _P, _P], _I),
         "hy_bench_ar_steps": ([_P, _I, ctypes.POINTER(_F)], _I),
         "hy_bench_kernel": ([_P, _I, _I, ctypes.POINTER(_F)], _I),
+        "hy_ctx_set_ar_path": ([_P, _I], _I),
+        "hy_ctx_ar_path": ([_P], _I),
+        "hy_trace_persistent": ([_P, _I, _I, _P], _I),
+        "hy_debug_progress": ([_P, _P, _I], _I),
     }
     for name, (argtypes, restype) in sig.items():
         fn = getattr(lib, name)
@@ -254,6 +261,14 @@ class TextRuntime:
 
     def __exit__(self, *exc):
         self.close()
+
+    @property
+    def ar_path(self) -> int:
+        return int(_LIB.hy_ctx_ar_path(self._ctx))
+
+    @ar_path.setter
+    def ar_path(self, path: int) -> None:
+        _check(_LIB.hy_ctx_set_ar_path(self._ctx, path))
 
     @property
     def device_bytes(self) -> int:
@@ -391,6 +406,19 @@ class TextRuntime:
         ms = ctypes.c_float()
         _check(_LIB.hy_bench_ar_steps(self._ctx, count, ctypes.byref(ms)))
         return ms.value
+
+    def trace_persistent(self, tokens: int, trace_token: int) -> np.ndarray:
+        """Phase timestamps (ns) [4 CTAs, phases, 8]: start, after grid wait, after prologue, arrive,
+        producer first issue, producer last issue (slots 6, 7 unused)."""
+        phases = 5 * self.cfg.num_layers + 1
+        out = np.zeros((4, phases, 8), np.uint64)
+        _check(_LIB.hy_trace_persistent(self._ctx, tokens, trace_token, _ptr(out)))
+        return out
+
+    def debug_progress(self, n: int = 148) -> np.ndarray:
+        out = np.zeros(n, np.uint32)
+        _check(_LIB.hy_debug_progress(self._ctx, _ptr(out), n))
+        return out
 
     def bench_kernel(self, which: int, count: int) -> float:
         ms = ctypes.c_float()

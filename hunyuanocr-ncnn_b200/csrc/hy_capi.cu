@@ -5,6 +5,7 @@
 #include "hy_attn.cuh"
 #include "hy_device.cuh"
 #include "hy_gemv.cuh"
+#include "hy_mega.cuh"
 #include "hy_util.cuh"
 
 #include "hy_decode.h"
@@ -14,6 +15,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -44,6 +46,7 @@ constexpr int kAttnSplitsAR = 19;         // 18 past splits + the new-row split 
 constexpr int kAttnSplitsVerify = 10;
 constexpr int kMaxSplits = 20;
 constexpr int kArStepsPerGraph = 4;
+constexpr int kMegaChunk = 64;            // tokens per persistent-kernel launch
 constexpr unsigned long long kTidEmbed = 1, kTidFinalNorm = 2, kLayerTidBase = 100, kLayerTidStride = 16;
 constexpr unsigned long long kTidDrafts = 9003;
 enum { J_INPUT_NORM, J_Q, J_K, J_V, J_Q_NORM, J_K_NORM, J_O, J_POST_NORM, J_GATE, J_UP, J_DOWN };
@@ -105,6 +108,14 @@ struct hy_ctx {
     int* err = nullptr;
     DecodeState* h_st = nullptr;  // pinned mirror
     int kv_len = 0;               // host mirror of the sequence length
+
+    // Persistent AR decode kernel (cooperative, one CTA per SM).
+    const void** wptrs = nullptr;  // device arrays: wqkv[L], wo[L], wgu[L], wd[L]
+    unsigned* bar = nullptr;       // grid barrier counter
+    int* dbg = nullptr;            // persistent-kernel self-check record [4]
+    unsigned* progress = nullptr;  // host-mapped per-CTA phase progress (HY_DEBUG_PROGRESS=1)
+    int ar_path = HY_AR_PATH_PERSISTENT;
+    bool mega_ok = false;
 
     cudaGraphExec_t g_ar = nullptr;
     cudaGraphExec_t g_verify_draft = nullptr;
@@ -321,7 +332,6 @@ cudaError_t enqueue_step_t(hy_ctx* c, const StepPlan& p)
         d.src = SRC_X;
         d.x = c->gu;
         d.ldx = 2 * ffn;
-        d.up_off = ffn;
         if constexpr (MT == 1)
         {
             d.out = c->x;
@@ -418,6 +428,19 @@ cudaError_t enqueue_lm_select(hy_ctx* c, int rows, const float* x, float penalty
 
 int check_device_error(hy_ctx* c)
 {
+    if (c->dbg)
+    {
+        int d[4] = {0, 0, 0, 0};
+        HY_CUDA(cudaMemcpyAsync(d, c->dbg, sizeof(d), cudaMemcpyDeviceToHost, c->stream));
+        HY_CUDA(cudaStreamSynchronize(c->stream));
+        if (d[0] != 0)
+        {
+            HY_CUDA(cudaMemsetAsync(c->dbg, 0, sizeof(d), c->stream));
+            return fail(HY_ERR_INVALID_ARGUMENT, "persistent kernel self-check " + std::to_string(d[0]) + " failed (cta " +
+                                                     std::to_string(d[1]) + ", phase " + std::to_string(d[2]) + ", index " +
+                                                     std::to_string(d[3]) + ")");
+        }
+    }
     int h = 0;
     HY_CUDA(cudaMemcpyAsync(&h, c->err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
     HY_CUDA(cudaStreamSynchronize(c->stream));
@@ -471,8 +494,103 @@ int capture(hy_ctx* c, cudaGraphExec_t* out, const StepPlan& p, int repeats)
     return HY_OK;
 }
 
+thread_local unsigned long long* t_trace = nullptr;
+thread_local int t_trace_token = 0;
+
+template <typename WT, typename KT>
+cudaError_t launch_mega_t(hy_ctx* c, int steps)
+{
+    auto k = mega_decode_kernel<WT, KT>;
+    MegaArgs a;
+    std::memset(&a, 0, sizeof(a));
+    const int L = c->cfg.num_layers;
+    a.embed = c->embed;
+    a.wqkv = c->wptrs;
+    a.wo = c->wptrs + L;
+    a.wgu = c->wptrs + 2 * L;
+    a.wd = c->wptrs + 3 * L;
+    a.norms = c->norms;
+    a.kc = c->kc;
+    a.vc = c->vc;
+    a.cap = c->cfg.max_context;
+    a.rope_cos = c->rope_cos;
+    a.rope_sin = c->rope_sin;
+    a.x = c->x;
+    a.qkv = c->qkv;
+    a.attn = c->attn;
+    a.gu = c->gu;
+    a.attn_part = c->attn_part;
+    a.attn_cnt = c->attn_cnt;
+    a.lm_part = c->lm_part;
+    a.lm_cnt = c->lm_cnt;
+    a.hist = c->hist;
+    a.st = c->st;
+    a.log_tokens = c->log_tokens;
+    a.log_raw = c->log_raw;
+    a.bar = c->bar;
+    a.num_layers = L;
+    a.vocab = c->cfg.vocab_size;
+    a.ffn = c->cfg.ffn_dim;
+    a.eps = c->cfg.rms_norm_eps;
+    a.scale_log2 = c->cfg.attn_scale * 1.4426950408889634f;
+    a.steps = steps;
+    a.err = c->err;
+    a.trace = t_trace;
+    a.trace_token = t_trace_token;
+    a.dbg = c->dbg;
+    if (c->progress)
+    {
+        unsigned* dp = nullptr;
+        cudaHostGetDevicePointer(reinterpret_cast<void**>(&dp), c->progress, 0);
+        a.progress = dp;
+    }
+    cudaError_t e = cudaMemsetAsync(c->bar, 0, sizeof(unsigned), c->stream);
+    if (e != cudaSuccess) return e;
+    void* params[] = {&a};
+    return cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(k), dim3(c->num_sms), dim3(kMegaThreads), params,
+                                       MegaSmem::SIZE, c->stream);
+}
+
+cudaError_t launch_mega(hy_ctx* c, int steps)
+{
+    const bool wb = c->cfg.weight_dtype == HY_DTYPE_BF16, kb = c->cfg.kv_dtype == HY_DTYPE_BF16;
+    if (!wb && !kb) return launch_mega_t<float, float>(c, steps);
+    if (!wb && kb) return launch_mega_t<float, __nv_bfloat16>(c, steps);
+    if (wb && !kb) return launch_mega_t<__nv_bfloat16, float>(c, steps);
+    return launch_mega_t<__nv_bfloat16, __nv_bfloat16>(c, steps);
+}
+
+template <typename WT, typename KT>
+int setup_mega_t(hy_ctx* c)
+{
+    auto k = mega_decode_kernel<WT, KT>;
+    HY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, MegaSmem::SIZE));
+    int per_sm = 0;
+    HY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kMegaThreads, MegaSmem::SIZE));
+    int coop = 0;
+    HY_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->cfg.device));
+    // All attention splits (8 heads x 18) need a CTA each; one CTA per SM must fit.
+    c->mega_ok = coop && per_sm >= 1 && c->num_sms >= kNumKVHeads * kMegaSplits &&
+                 (c->cfg.vocab_size + c->num_sms - 1) / c->num_sms <= 32 * (kMegaHistWords - 2);
+    if (!c->mega_ok) c->ar_path = HY_AR_PATH_GRAPH;
+    return HY_OK;
+}
+
+int setup_mega(hy_ctx* c)
+{
+    const bool wb = c->cfg.weight_dtype == HY_DTYPE_BF16, kb = c->cfg.kv_dtype == HY_DTYPE_BF16;
+    if (!wb && !kb) return setup_mega_t<float, float>(c);
+    if (!wb && kb) return setup_mega_t<float, __nv_bfloat16>(c);
+    if (wb && !kb) return setup_mega_t<__nv_bfloat16, float>(c);
+    return setup_mega_t<__nv_bfloat16, __nv_bfloat16>(c);
+}
+
 int ensure_graphs(hy_ctx* c)
 {
+    {
+        int rc = setup_mega(c);
+        if (rc) return rc;
+    }
     if (!c->g_ar)
     {
         StepPlan p{};
@@ -618,6 +736,26 @@ int alloc_ctx(hy_ctx* c)
     if ((rc = dalloc(c, &c->raw_out, kBlock))) return rc;
     if ((rc = dalloc(c, &c->prefix, kBlock))) return rc;
     if ((rc = dalloc(c, &c->err, 1))) return rc;
+    if ((rc = dalloc(c, &c->bar, 1))) return rc;
+    if ((rc = dalloc(c, &c->dbg, 4))) return rc;
+    HY_CUDA(cudaMemsetAsync(c->dbg, 0, 4 * sizeof(int), c->stream));
+    if (const char* e = std::getenv("HY_DEBUG_PROGRESS"); e && e[0] == '1')
+    {
+        HY_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&c->progress), 1024 * sizeof(unsigned), cudaHostAllocMapped));
+        std::memset(c->progress, 0, 1024 * sizeof(unsigned));
+    }
+    if ((rc = dalloc(c, &c->wptrs, static_cast<size_t>(4) * L))) return rc;
+    {
+        std::vector<const void*> h(4 * static_cast<size_t>(L));
+        for (int l = 0; l < L; ++l)
+        {
+            h[l] = c->wqkv[l];
+            h[L + l] = c->wo[l];
+            h[2 * L + l] = c->wgu[l];
+            h[3 * L + l] = c->wd[l];
+        }
+        HY_CUDA(cudaMemcpy(c->wptrs, h.data(), h.size() * sizeof(void*), cudaMemcpyHostToDevice));
+    }
     HY_CUDA(cudaMemsetAsync(c->attn_cnt, 0, sizeof(int) * L * kNumKVHeads, c->stream));
     HY_CUDA(cudaMemsetAsync(c->lm_cnt, 0, sizeof(int), c->stream));
     HY_CUDA(cudaMemsetAsync(c->err, 0, sizeof(int), c->stream));
@@ -666,6 +804,16 @@ int fill_synthetic(hy_ctx* c, unsigned long long seed, float std_dev, float norm
         else
             launch_synth(static_cast<float*>(dst) + off_elems, count, seed, tid, std_dev, 0.f, c->stream);
     };
+    auto lin_rows = [&](void* dst, unsigned long long tid, int rows, int cols, int row_mult, int row_off) {
+        const unsigned long long base = synth_base(seed, tid);
+        const float mult = host_synth_mult(std_dev);
+        if (cfg.weight_dtype == HY_DTYPE_BF16)
+            synth_fill_rows_kernel<__nv_bfloat16><<<1184, 256, 0, c->stream>>>(static_cast<__nv_bfloat16*>(dst), rows, cols,
+                                                                               row_mult, row_off, base, mult);
+        else
+            synth_fill_rows_kernel<float><<<1184, 256, 0, c->stream>>>(static_cast<float*>(dst), rows, cols, row_mult,
+                                                                       row_off, base, mult);
+    };
     lin(c->embed, 0, kTidEmbed, static_cast<size_t>(cfg.vocab_size) * kHidden);
     launch_synth(c->final_norm(), kHidden, seed, kTidFinalNorm, norm_std, 1.0f, c->stream);
     for (int l = 0; l < cfg.num_layers; ++l)
@@ -680,8 +828,9 @@ int fill_synthetic(hy_ctx* c, unsigned long long seed, float std_dev, float norm
         lin(c->wqkv[l], static_cast<size_t>(kQWidth + kKVWidth) * kHidden, b + J_V,
             static_cast<size_t>(kKVWidth) * kHidden);
         lin(c->wo[l], 0, b + J_O, static_cast<size_t>(kHidden) * kQWidth);
-        lin(c->wgu[l], 0, b + J_GATE, static_cast<size_t>(ffn) * kHidden);
-        lin(c->wgu[l], static_cast<size_t>(ffn) * kHidden, b + J_UP, static_cast<size_t>(ffn) * kHidden);
+        // gate_proj row j -> row 2j, up_proj row j -> row 2j + 1 (SwiGLU pairs stay together).
+        lin_rows(c->wgu[l], b + J_GATE, ffn, kHidden, 2, 0);
+        lin_rows(c->wgu[l], b + J_UP, ffn, kHidden, 2, 1);
         lin(c->wd[l], 0, b + J_DOWN, static_cast<size_t>(kHidden) * ffn);
     }
     HY_CUDA(cudaGetLastError());
@@ -719,6 +868,19 @@ int upload_weights(hy_ctx* c, const hy_weights* w)
         if (e != cudaSuccess) return e;
         return cudaStreamSynchronize(c->stream);
     };
+    // rows r of src -> rows 2r + off of dst (gate/up interleave).
+    auto put_rows = [&](void* dst, const float* src, int rows, int off) -> cudaError_t {
+        const size_t es = bf ? 2 : 4;
+        if (!bf)
+            return cudaMemcpy2D(static_cast<char*>(dst) + static_cast<size_t>(off) * kHidden * es, 2 * kHidden * es, src,
+                                kHidden * sizeof(float), kHidden * sizeof(float), rows, cudaMemcpyHostToDevice);
+        cudaError_t e = cudaMemcpy(staging, src, static_cast<size_t>(rows) * kHidden * sizeof(float), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return e;
+        f32_to_bf16_rows_kernel<<<1184, 256, 0, c->stream>>>(staging, static_cast<__nv_bfloat16*>(dst), rows, kHidden, 2, off);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        return cudaStreamSynchronize(c->stream);
+    };
     cudaError_t e = put(c->embed, 0, w->embed, static_cast<size_t>(cfg.vocab_size) * kHidden);
     for (int l = 0; l < cfg.num_layers && e == cudaSuccess; ++l)
     {
@@ -728,8 +890,8 @@ int upload_weights(hy_ctx* c, const hy_weights* w)
         if (e == cudaSuccess)
             e = put(c->wqkv[l], static_cast<size_t>(kQWidth + kKVWidth) * kHidden, lw.v_proj, static_cast<size_t>(kKVWidth) * kHidden);
         if (e == cudaSuccess) e = put(c->wo[l], 0, lw.o_proj, static_cast<size_t>(kHidden) * kQWidth);
-        if (e == cudaSuccess) e = put(c->wgu[l], 0, lw.gate_proj, static_cast<size_t>(ffn) * kHidden);
-        if (e == cudaSuccess) e = put(c->wgu[l], static_cast<size_t>(ffn) * kHidden, lw.up_proj, static_cast<size_t>(ffn) * kHidden);
+        if (e == cudaSuccess) e = put_rows(c->wgu[l], lw.gate_proj, ffn, 0);
+        if (e == cudaSuccess) e = put_rows(c->wgu[l], lw.up_proj, ffn, 1);
         if (e == cudaSuccess) e = put(c->wd[l], 0, lw.down_proj, static_cast<size_t>(kHidden) * ffn);
         if (e == cudaSuccess) e = cudaMemcpy(c->in_norm(l), lw.input_norm, kHidden * sizeof(float), cudaMemcpyHostToDevice);
         if (e == cudaSuccess) e = cudaMemcpy(c->post_norm(l), lw.post_norm, kHidden * sizeof(float), cudaMemcpyHostToDevice);
@@ -753,6 +915,7 @@ void free_ctx(hy_ctx* c)
     for (void* p : c->allocs) cudaFree(p);
     if (c->logits) cudaFree(c->logits);
     if (c->h_st) cudaFreeHost(c->h_st);
+    if (c->progress) cudaFreeHost(c->progress);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
 }
@@ -899,6 +1062,62 @@ int hy_build_mrope(const int* position_ids, int seq_len, int use_cos, float* out
 }
 
 float hy_rope_value(int position, int dim, int use_cos) { return rope_value_host(position, dim, use_cos != 0); }
+
+int hy_ctx_set_ar_path(hy_ctx* c, int path)
+{
+    if (!c) return fail(HY_ERR_INVALID_ARGUMENT, "ctx is null");
+    if (path != HY_AR_PATH_PERSISTENT && path != HY_AR_PATH_GRAPH) return fail(HY_ERR_INVALID_ARGUMENT, "unknown AR path");
+    if (path == HY_AR_PATH_PERSISTENT && !c->mega_ok)
+        return fail(HY_ERR_UNSUPPORTED, "the persistent decode kernel needs a cooperative launch of >= 144 co-resident CTAs");
+    c->ar_path = path;
+    return HY_OK;
+}
+
+int hy_ctx_ar_path(const hy_ctx* c) { return c ? c->ar_path : -1; }
+
+int hy_debug_progress(const hy_ctx* c, unsigned* out, int n)
+{
+    if (!c || !out || n <= 0) return fail(HY_ERR_INVALID_ARGUMENT, "invalid arguments");
+    if (!c->progress) return fail(HY_ERR_NOT_READY, "start the process with HY_DEBUG_PROGRESS=1");
+    for (int i = 0; i < n && i < 1024; ++i) out[i] = c->progress[i];
+    return HY_OK;
+}
+
+int hy_trace_persistent(hy_ctx* c, int tokens, int trace_token, unsigned long long* out)
+{
+    if (!c || !out || tokens < 1 || trace_token < 0 || trace_token >= tokens || tokens > kMegaChunk)
+        return fail(HY_ERR_INVALID_ARGUMENT, "invalid trace arguments");
+    if (!c->mega_ok) return fail(HY_ERR_UNSUPPORTED, "the persistent decode kernel is not available");
+    if (c->kv_len + tokens > c->cfg.max_context) return fail(HY_ERR_CAPACITY, "KV capacity exceeded");
+    int rc = set_device(c);
+    if (rc) return rc;
+    const int phases = 5 * c->cfg.num_layers + 1;
+    const size_t n = static_cast<size_t>(kTraceCtas) * phases * kTraceSlots;
+    unsigned long long* d = nullptr;
+    HY_CUDA(cudaMalloc(reinterpret_cast<void**>(&d), n * sizeof(unsigned long long)));
+    HY_CUDA(cudaMemsetAsync(d, 0, n * sizeof(unsigned long long), c->stream));
+    DecodeState& h = *c->h_st;
+    h.kv_len = c->kv_len;
+    h.n_gen = 1;
+    h.max_tokens = tokens + 1;
+    h.done = 0;
+    h.n_eos = 0;
+    if ((rc = push_state(c)))
+    {
+        cudaFree(d);
+        return rc;
+    }
+    t_trace = d;
+    t_trace_token = trace_token;
+    cudaError_t e = launch_mega(c, tokens);
+    t_trace = nullptr;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out, d, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    cudaFree(d);
+    if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("trace launch: ") + cudaGetErrorString(e));
+    if ((rc = check_device_error(c))) return rc;
+    return set_length(c, c->kv_len);
+}
 
 int hy_seq_reset(hy_ctx* c)
 {
@@ -1069,12 +1288,23 @@ int hy_generate(hy_ctx* c, int first_token, int first_raw_top1, int max_tokens, 
     int launched_steps = 0;
     while (!h.done && launched_steps < max_tokens - 1)
     {
-        for (int i = 0; i < 4 && launched_steps < max_tokens - 1; ++i)
+        if (c->ar_path == HY_AR_PATH_PERSISTENT)
         {
-            HY_CUDA(cudaGraphLaunch(c->g_ar, c->stream));
-            launched_steps += kArStepsPerGraph;
+            const int n = std::min(kMegaChunk, max_tokens - 1 - launched_steps);
+            cudaError_t e = launch_mega(c, n);
+            if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("persistent decode launch: ") + cudaGetErrorString(e));
+            launched_steps += n;
+        }
+        else
+        {
+            for (int i = 0; i < 4 && launched_steps < max_tokens - 1; ++i)
+            {
+                HY_CUDA(cudaGraphLaunch(c->g_ar, c->stream));
+                launched_steps += kArStepsPerGraph;
+            }
         }
         if ((rc = sync_state_to_host(c))) return rc;
+        if (h.kv_len + 0 > c->cfg.max_context) return fail(HY_ERR_CAPACITY, "KV capacity exceeded");
     }
     if ((rc = check_device_error(c))) return rc;
     if ((rc = sync_state_to_host(c))) return rc;
@@ -1354,7 +1584,18 @@ int hy_bench_ar_steps(hy_ctx* c, int count, float* ms)
     HY_CUDA(cudaEventCreate(&e1));
     const int graphs = (count + kArStepsPerGraph - 1) / kArStepsPerGraph;
     HY_CUDA(cudaEventRecord(e0, c->stream));
-    for (int i = 0; i < graphs; ++i) HY_CUDA(cudaGraphLaunch(c->g_ar, c->stream));
+    if (c->ar_path == HY_AR_PATH_PERSISTENT)
+    {
+        for (int done = 0; done < count; done += kMegaChunk)
+        {
+            cudaError_t e = launch_mega(c, std::min(kMegaChunk, count - done));
+            if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("persistent decode launch: ") + cudaGetErrorString(e));
+        }
+    }
+    else
+    {
+        for (int i = 0; i < graphs; ++i) HY_CUDA(cudaGraphLaunch(c->g_ar, c->stream));
+    }
     HY_CUDA(cudaEventRecord(e1, c->stream));
     HY_CUDA(cudaEventSynchronize(e1));
     float t = 0.f;

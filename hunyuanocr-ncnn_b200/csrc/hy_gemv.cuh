@@ -42,8 +42,8 @@ struct GemvArgs {
     int N, ldw, k_off;
     int rows;        // active activation rows (<= MT)
     int src;         // SRC_*
-    const float* x;  // SRC_X: row m at x + m * ldx + k_off (SwiGLU: gate there, up at + up_off)
-    int ldx, up_off;
+    const float* x;  // SRC_X: row m at x + m * ldx + k_off; SwiGLU: interleaved (gate_k, up_k) pairs at x + m * ldx + 2 * (k_off + k)
+    int ldx;
     const float* norm_w;
     float eps;
     const void* table;    // gather: tied embedding table [vocab x 1024] of WT
@@ -131,6 +131,7 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
     using S = GemvShape<WT, KP, MT>;
     constexpr int RPW = S::RPW, SEG = S::SEG, SPS = S::SPS, STAGE = S::STAGE, NST = S::NST;
     static_assert(NST >= 2, "ring too small");
+    static_assert(S::GPS <= kGemvWarps, "a warp may own at most one row group per stage");
     static_assert(SEG % 16 == 0, "segments must be 16-byte multiples");
     static_assert(KP % 128 == 0, "K slice must be a multiple of 128");
 
@@ -154,7 +155,7 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
         for (int s = 0; s < NST; ++s)
         {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], S::GPS);
+            mbar_init(&empty[s], kGemvWarps);
         }
         fence_mbar_init();
     }
@@ -246,17 +247,17 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
         }
         else if (PRO == PRO_SWIGLU)
         {
-            const float* g = a.x + static_cast<size_t>(m) * a.ldx + a.k_off;
-            const float* u = g + a.up_off;
+            // act_k = silu(gate_k) * up_k; the gate/up projection rows are interleaved.
+            const float* gu = a.x + static_cast<size_t>(m) * a.ldx + 2 * a.k_off;
             for (int k = tid * 4; k < KP; k += 256 * 4)
             {
-                const float4 gv = *reinterpret_cast<const float4*>(g + k);
-                const float4 uv = *reinterpret_cast<const float4*>(u + k);
+                const float4 p0 = *reinterpret_cast<const float4*>(gu + 2 * k);
+                const float4 p1 = *reinterpret_cast<const float4*>(gu + 2 * k + 4);
                 float4 r;
-                r.x = (gv.x / (1.0f + expf(-gv.x))) * uv.x;
-                r.y = (gv.y / (1.0f + expf(-gv.y))) * uv.y;
-                r.z = (gv.z / (1.0f + expf(-gv.z))) * uv.z;
-                r.w = (gv.w / (1.0f + expf(-gv.w))) * uv.w;
+                r.x = (p0.x / (1.0f + expf(-p0.x))) * p0.y;
+                r.y = (p0.z / (1.0f + expf(-p0.z))) * p0.w;
+                r.z = (p1.x / (1.0f + expf(-p1.x))) * p1.y;
+                r.w = (p1.z / (1.0f + expf(-p1.z))) * p1.w;
                 *reinterpret_cast<float4*>(xr + k) = r;
             }
         }
@@ -324,41 +325,53 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
     const float pen = (EPI == EPI_ARGMAX) ? ((a.lm_mode == LM_NONE) ? a.penalty : a.st->penalty) : 1.0f;
     ArgBest best;
     best.rv = 0.f; best.ri = -1; best.pv = 0.f; best.pi = -1;
+    // Every consumer warp observes every stage in order and arrives once on it;
+    // the warp owning a row group of the stage (group gi -> warp gi % 8)
+    // computes it before arriving. (An mbarrier parity wait is only meaningful
+    // one phase ahead, so no warp may skip past a stage that has not landed, nor
+    // let a slot be reused before it has seen it.)
     const int ngroups = (R + RPW - 1) / RPW;
-    for (int gi = warp; gi < ngroups; gi += kGemvWarps)
+    int gi = warp;   // next group this warp owns
+    for (int stage = 0; stage < nstage; ++stage)
     {
-        const int seg0 = gi * RPW;
-        const int stage = seg0 / SPS, slot = stage % NST;
+        const int slot = stage % NST;
         const bool ok = mbar_wait(&full[slot], (stage / NST) & 1, a.err, kErrTimeoutFull);
         if (!__all_sync(0xffffffffu, ok)) break;
-        const WT* wrow = reinterpret_cast<const WT*>(ring + slot * STAGE + (seg0 % SPS) * SEG);
-        const int nr = min(RPW, R - seg0);
+        const int seg0 = gi * RPW;
+        const bool mine = gi < ngroups && seg0 < (stage + 1) * SPS;   // at most one group per warp per stage
+        const int nr = mine ? min(RPW, R - seg0) : 0;
         float acc[RPW][MT];
 #pragma unroll
         for (int r = 0; r < RPW; ++r)
 #pragma unroll
             for (int m = 0; m < MT; ++m) acc[r][m] = 0.f;
-#pragma unroll 4
-        for (int c = lane; c < KP / 4; c += 32)
+        if (mine)
         {
-            float4 w[RPW];
+            const WT* wrow = reinterpret_cast<const WT*>(ring + slot * STAGE + (seg0 % SPS) * SEG);
+#pragma unroll 4
+            for (int c = lane; c < KP / 4; c += 32)
+            {
+                float4 w[RPW];
+#pragma unroll
+                for (int r = 0; r < RPW; ++r)
+                    w[r] = (r < nr) ? load4(wrow + r * KP + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int m = 0; m < MT; ++m)
+                {
+                    const float4 xv = *reinterpret_cast<const float4*>(xs + m * KP + 4 * c);
+#pragma unroll
+                    for (int r = 0; r < RPW; ++r) acc[r][m] += dot4(w[r], xv);
+                }
+            }
 #pragma unroll
             for (int r = 0; r < RPW; ++r)
-                w[r] = (r < nr) ? load4(wrow + r * KP + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int m = 0; m < MT; ++m)
-            {
-                const float4 xv = *reinterpret_cast<const float4*>(xs + m * KP + 4 * c);
-#pragma unroll
-                for (int r = 0; r < RPW; ++r) acc[r][m] += dot4(w[r], xv);
-            }
+                for (int m = 0; m < MT; ++m) acc[r][m] = warp_sum(acc[r][m]);
         }
-#pragma unroll
-        for (int r = 0; r < RPW; ++r)
-#pragma unroll
-            for (int m = 0; m < MT; ++m) acc[r][m] = warp_sum(acc[r][m]);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
+        if (!mine) continue;
+        gi += kGemvWarps;
 
         const int n0 = r0 + seg0;
         if (EPI == EPI_STORE || EPI == EPI_RESID)

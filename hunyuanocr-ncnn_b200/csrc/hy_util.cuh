@@ -15,6 +15,32 @@ __global__ void synth_fill_kernel(WT* out, size_t count, unsigned long long base
         out[i] = from_f32<WT>(synth_value(base, i, mult, offset));
 }
 
+// Row r of a [rows x cols] counter stream goes to row r * row_mult + row_off of out.
+template <typename WT>
+__global__ void synth_fill_rows_kernel(WT* out, int rows, int cols, int row_mult, int row_off, unsigned long long base,
+                                       float mult)
+{
+    const size_t count = static_cast<size_t>(rows) * cols;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < count;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    {
+        const size_t r = i / cols, c = i % cols;
+        out[(r * row_mult + row_off) * cols + c] = from_f32<WT>(synth_value(base, i, mult, 0.0f));
+    }
+}
+
+__global__ void f32_to_bf16_rows_kernel(const float* in, __nv_bfloat16* out, int rows, int cols, int row_mult,
+                                        int row_off)
+{
+    const size_t count = static_cast<size_t>(rows) * cols;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < count;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    {
+        const size_t r = i / cols, c = i % cols;
+        out[(r * row_mult + row_off) * cols + c] = __float2bfloat16_rn(in[i]);
+    }
+}
+
 __global__ void f32_to_bf16_kernel(const float* in, __nv_bfloat16* out, size_t count)
 {
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < count;

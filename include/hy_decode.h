@@ -110,6 +110,27 @@ int hy_ctx_create(const hy_config* cfg, const hy_weights* weights, hy_ctx** out)
 int hy_ctx_create_synthetic(const hy_config* cfg, uint64_t seed, float std, float norm_std, hy_ctx** out);
 
 void hy_ctx_destroy(hy_ctx* ctx);
+
+/* How hy_generate runs the AR loop. HY_AR_PATH_PERSISTENT (default): one
+ * cooperative kernel per up to 64 tokens, one CTA per SM, all 24 layers and the
+ * LM head of each token inside it with grid barriers between phases.
+ * HY_AR_PATH_GRAPH: one CUDA-graph replay of 121 kernels per token. Both compute
+ * the same step (the reference's decode loop, src/text_runtime.cpp:1417-1508). */
+enum hy_ar_path { HY_AR_PATH_PERSISTENT = 0, HY_AR_PATH_GRAPH = 1 };
+int hy_ctx_set_ar_path(hy_ctx* ctx, int path);
+int hy_ctx_ar_path(const hy_ctx* ctx);
+/* Per-phase trace of the persistent kernel (the counterpart of the reference's
+ * stage timers, include/hunyuan_ocr/text_runtime.h:32-39): runs `tokens` AR
+ * steps from the current state and, for CTAs 0..3 during token `trace_token`,
+ * stores %globaltimer (ns) at phase start, after the grid wait, after the
+ * prologue, at the barrier arrive, and the producer's first and last stage
+ * issue: out[(cta * (5 * num_layers + 1) + phase) * 8 + i] (slots 6, 7 unused).
+ * The sequence length is restored afterwards. */
+int hy_trace_persistent(hy_ctx* ctx, int tokens, int trace_token, unsigned long long* out);
+/* Failure diagnosis for the persistent kernel: with HY_DEBUG_PROGRESS=1 in the
+ * environment at context creation, each CTA records in host-mapped memory how
+ * many phases it completed; readable even after a device fault. */
+int hy_debug_progress(const hy_ctx* ctx, unsigned* out, int n);
 int hy_ctx_config(const hy_ctx* ctx, hy_config* cfg);
 size_t hy_ctx_device_bytes(const hy_ctx* ctx);   /* replaces mapped_weight_bytes() */
 

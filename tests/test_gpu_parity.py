@@ -195,6 +195,22 @@ def test_dflash_is_lossless_and_matches_oracle(small, oracle):
         assert out.block_count == ref.block_count
 
 
+@pytest.mark.parametrize("path", ["persistent", "graph"])
+def test_ar_paths_match_oracle(pkg, small, oracle, path):
+    cfg, w, rt = small
+    prompt = oracle.synthetic_prompt(33, 4, 6, 16, cfg.vocab, cfg.vocab - 3)
+    want = oracle.decode_ar(w, cfg, prompt, 150)
+    rt.ar_path = pkg.AR_PATH_PERSISTENT if path == "persistent" else pkg.AR_PATH_GRAPH
+    try:
+        res = rt.run_vlm_decode_with_prompt(prompt.input_ids, prompt.position_ids, prompt.image_token_id,
+                                            prompt.vision_features, max_tokens=150)
+    finally:
+        rt.ar_path = pkg.AR_PATH_PERSISTENT
+    assert res.generated_tokens == want.tokens
+    assert res.raw_top1_tokens == want.raw_top1
+    assert rt.kv_length == prompt.input_ids.shape[0] + 149
+
+
 def test_eos_stops_generation(small, oracle):
     cfg, w, rt = small
     prompt = oracle.synthetic_prompt(21, 4, 6, 16, cfg.vocab, cfg.vocab - 3)
