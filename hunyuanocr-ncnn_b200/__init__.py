@@ -409,9 +409,9 @@ class TextRuntime:
 
     def trace_persistent(self, tokens: int, trace_token: int) -> np.ndarray:
         """Phase timestamps (ns) [4 CTAs, phases, 8]: start, after grid wait, after prologue, arrive,
-        producer first issue, producer last issue (slots 6, 7 unused)."""
+        producer first issue, producer last issue, consumer (thread 0) passing the first and last stage wait."""
         phases = 5 * self.cfg.num_layers + 1
-        out = np.zeros((4, phases, 8), np.uint64)
+        out = np.zeros((4, phases, 12), np.uint64)
         _check(_LIB.hy_trace_persistent(self._ctx, tokens, trace_token, _ptr(out)))
         return out
 

@@ -39,7 +39,7 @@ constexpr int kMegaWarps = 8;
 constexpr int kMegaThreads = (kMegaWarps + 1) * 32;
 constexpr int kMegaStage = 16384;
 constexpr int kMegaNst = 13;
-constexpr int kMegaSplits = 18;   // per KV head: 17 splits of the past rows + the new-row split
+constexpr int kMegaSplits = 9;    // per KV head: 8 splits of the past rows + the new-row split
 constexpr int kMegaMaxK = 3584;
 
 struct MegaArgs {
@@ -97,7 +97,7 @@ __device__ __forceinline__ bool mega_check(bool ok, int* dbg, int code, int b, i
 }
 
 constexpr int kTraceCtas = 4;
-constexpr int kTraceSlots = 8;
+constexpr int kTraceSlots = 12;
 
 struct MegaSmem {
     static constexpr int RING = 0;
@@ -215,7 +215,10 @@ __device__ __forceinline__ bool grid_wait(const unsigned* bar, unsigned target, 
     while (true)
     {
         for (int i = 0; i < 16; ++i)
+        {
             if (ld_acquire_u32(bar) >= target) return true;
+            __nanosleep(20);
+        }
         if (global_ns() - t0 > kWaitLimitNs)
         {
             atomicOr(err, kErrTimeoutFull);
@@ -228,7 +231,7 @@ __device__ __forceinline__ bool grid_wait(const unsigned* bar, unsigned target, 
 __device__ __forceinline__ void grid_arrive(unsigned* bar)
 {
     __threadfence();
-    atomicAdd(bar, 1u);
+    asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
 }
 
 // <row0, xs> and <row1, xs> over K elements by one warp: lane-strided float4s,
@@ -451,10 +454,40 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
             }
             else if (kind == PH_O)
             {
-                const float4 v0 = __ldcg(reinterpret_cast<const float4*>(a.attn) + tid);
-                const float4 v1 = __ldcg(reinterpret_cast<const float4*>(a.attn) + tid + 256);
-                reinterpret_cast<float4*>(xs)[tid] = v0;
-                reinterpret_cast<float4*>(xs)[tid + 256] = v1;
+                // Merge the attention partials of every split (split-K flash-decode
+                // combine): thread t handles q head t / 16, dims 8 * (t % 16) .. +8.
+                // All loads are issued before any use, so this is one L2 round trip.
+                const int h = tid >> 4, d0 = (tid & 15) * 8;
+                const float* hp = a.attn_part + (static_cast<size_t>(h >> 1) * kMegaSplits * 2 + (h & 1)) * kPartStride;
+                float ms[kMegaSplits], ls[kMegaSplits];
+                float4 va[kMegaSplits], vb[kMegaSplits];
+#pragma unroll
+                for (int sp = 0; sp < kMegaSplits; ++sp)
+                {
+                    const float* ps = hp + static_cast<size_t>(sp) * 2 * kPartStride;
+                    ms[sp] = __ldcg(ps);
+                    ls[sp] = __ldcg(ps + 1);
+                    va[sp] = __ldcg(reinterpret_cast<const float4*>(ps + 4 + d0));
+                    vb[sp] = __ldcg(reinterpret_cast<const float4*>(ps + 8 + d0));
+                }
+                float M = -INFINITY;
+#pragma unroll
+                for (int sp = 0; sp < kMegaSplits; ++sp) M = fmaxf(M, ms[sp]);
+                float Lsum = 0.f;
+                float4 A0 = make_float4(0.f, 0.f, 0.f, 0.f), A1 = A0;
+#pragma unroll
+                for (int sp = 0; sp < kMegaSplits; ++sp)
+                {
+                    const float f = (ms[sp] == -INFINITY) ? 0.f : exp2f(ms[sp] - M);
+                    Lsum += f * ls[sp];
+                    A0.x += f * va[sp].x; A0.y += f * va[sp].y; A0.z += f * va[sp].z; A0.w += f * va[sp].w;
+                    A1.x += f * vb[sp].x; A1.y += f * vb[sp].y; A1.z += f * vb[sp].z; A1.w += f * vb[sp].w;
+                }
+                const float inv = 1.0f / Lsum;
+                A0.x *= inv; A0.y *= inv; A0.z *= inv; A0.w *= inv;
+                A1.x *= inv; A1.y *= inv; A1.z *= inv; A1.w *= inv;
+                *reinterpret_cast<float4*>(xs + h * kHeadDim + d0) = A0;
+                *reinterpret_cast<float4*>(xs + h * kHeadDim + d0 + 4) = A1;
                 consumers_sync();
             }
             else if (kind == PH_GU || kind == PH_LM)
@@ -507,22 +540,39 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                 const int rpu = (p.per_stage >= 2) ? 2 : 1;
                 const unsigned gs0 = gs;
                 int o = warp;   // next unit this warp owns
+                // Residual rows of this warp's first unit, fetched now so the
+                // epilogue's read-modify-write does not wait on L2.
+                float xpre0 = 0.f, xpre1 = 0.f;
+                if ((kind == PH_O || kind == PH_DOWN) && lane == 0 && warp * rpu < p.count)
+                {
+                    xpre0 = __ldcg(xg + p.r0 + warp * rpu);
+                    if (rpu == 2 && warp * rpu + 1 < p.count) xpre1 = __ldcg(xg + p.r0 + warp * rpu + 1);
+                }
+                unsigned long long t_wait = 0, t_dot = 0, n_units = 0;   // warp-0 trace accumulators
                 for (int i = 0; i < p.nstage && !bad; ++i)
                 {
                     const unsigned gsi = gs0 + i;
                     const int slot = gsi % kMegaNst;
+                    const unsigned long long tw0 = tracing ? global_ns() : 0;
                     const bool okw = mbar_wait(&full[slot], (gsi / kMegaNst) & 1, a.err, kErrTimeoutFull);
+                    if (tracing) t_wait += global_ns() - tw0;
                     if (!__all_sync(0xffffffffu, okw))
                     {
                         if (lane == 0) redi[0] = 1;
                         bad = true;
                         break;
                     }
+                    if (tracing)
+                    {
+                        if (i == 0) tr[6] = global_ns();
+                        if (i == p.nstage - 1) tr[7] = global_ns();
+                    }
                     const int row_end = min(p.count, (i + 1) * p.per_stage);
                     const int q = o * rpu;
                     const bool mine = q < row_end;   // at most one unit per warp per stage
                     const bool two = mine && (rpu == 2) && (q + 1 < p.count);
                     float2 d = make_float2(0.f, 0.f);
+                    const unsigned long long td0 = tracing ? global_ns() : 0;
                     if (mine)
                     {
                         const int j = q - i * p.per_stage;
@@ -537,6 +587,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                         o += kMegaWarps;
                     }
                     __syncwarp();
+                    if (tracing && mine)
+                    {
+                        t_dot += global_ns() - td0;
+                        ++n_units;
+                    }
                     if (lane == 0) mbar_arrive(&empty[slot]);
                     if (mine && lane == 0)
                     {
@@ -556,8 +611,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                         }
                         else if (kind == PH_O || kind == PH_DOWN)
                         {
-                            const float x0 = __ldcg(xg + nrow);
-                            const float x1 = two ? __ldcg(xg + nrow + 1) : 0.f;
+                            const bool first = (q == warp * rpu);
+                            const float x0 = first ? xpre0 : __ldcg(xg + nrow);
+                            const float x1 = two ? (first ? xpre1 : __ldcg(xg + nrow + 1)) : 0.f;
                             xg[nrow] = x0 + v0;
                             if (two) xg[nrow + 1] = x1 + v1;
                         }
@@ -578,6 +634,12 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                     }
                 }
                 gs = gs0 + p.nstage;
+                if (tracing)
+                {
+                    tr[8] = t_wait;
+                    tr[9] = t_dot;
+                    tr[10] = n_units;
+                }
                 if (kind == PH_LM)
                 {
                     if (lane == 0) red4[warp] = make_float4(best_rv, __int_as_float(best_ri), best_pv, __int_as_float(best_pi));
@@ -750,6 +812,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                         bad = true;
                         continue;
                     }
+                    if (tracing)
+                    {
+                        if (i == 0) tr[6] = global_ns();
+                        if (i == p.nstage - 1) tr[7] = global_ns();
+                    }
                     const KT* kst = ringk + (static_cast<size_t>(slot) * kMegaStage) / sizeof(KT);
                     const KT* vst = kst + static_cast<size_t>(p.per_stage) * kHeadDim;
                     const int n = min(p.per_stage, p.count - i * p.per_stage);
@@ -824,50 +891,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                         part[1] = Lsum;
                     }
                     part[4 + d] = A;
-                    __threadfence();
                 }
-                consumers_sync();
-                if (tid == 0) redi[1] = (atomicAdd(&a.attn_cnt[layer * kNumKVHeads + g], 1) == kMegaSplits - 1) ? 1 : 0;
-                consumers_sync();
-                if (redi[1])
-                {
-                    __threadfence();
-                    float* wts = ascr;  // [kMegaSplits][2] weights (reuse scratch)
-                    const float* hp = a.attn_part + static_cast<size_t>(g) * kMegaSplits * 2 * kPartStride;
-                    if (tid < 2)
-                    {
-                        float Ms[kMegaSplits], Ls[kMegaSplits];
-                        float M = -INFINITY;
-#pragma unroll
-                        for (int sp = 0; sp < kMegaSplits; ++sp)
-                        {
-                            Ms[sp] = __ldcg(hp + (sp * 2 + tid) * kPartStride);
-                            Ls[sp] = __ldcg(hp + (sp * 2 + tid) * kPartStride + 1);
-                        }
-#pragma unroll
-                        for (int sp = 0; sp < kMegaSplits; ++sp) M = fmaxf(M, Ms[sp]);
-                        float Lsum = 0.f;
-#pragma unroll
-                        for (int sp = 0; sp < kMegaSplits; ++sp)
-                        {
-                            const float f = (Ms[sp] == -INFINITY) ? 0.f : exp2f(Ms[sp] - M);
-                            Ms[sp] = f;
-                            Lsum += f * Ls[sp];
-                        }
-#pragma unroll
-                        for (int sp = 0; sp < kMegaSplits; ++sp) wts[sp * 2 + tid] = Ms[sp] / Lsum;
-                    }
-                    consumers_sync();
-                    const int q = tid >> 7, d = tid & 127;
-                    float vals[kMegaSplits];
-#pragma unroll
-                    for (int sp = 0; sp < kMegaSplits; ++sp) vals[sp] = __ldcg(hp + (sp * 2 + q) * kPartStride + 4 + d);
-                    float A = 0.f;
-#pragma unroll
-                    for (int sp = 0; sp < kMegaSplits; ++sp) A += wts[sp * 2 + q] * vals[sp];
-                    a.attn[(2 * g + q) * kHeadDim + d] = A;
-                    if (tid == 0) a.attn_cnt[layer * kNumKVHeads + g] = 0;
-                }
+                // The o-projection phase merges the partials of all splits.
             }
 
             // ---------------- phase done: arrive on the grid barrier ----------------

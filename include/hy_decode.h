@@ -124,7 +124,9 @@ int hy_ctx_ar_path(const hy_ctx* ctx);
  * steps from the current state and, for CTAs 0..3 during token `trace_token`,
  * stores %globaltimer (ns) at phase start, after the grid wait, after the
  * prologue, at the barrier arrive, and the producer's first and last stage
- * issue: out[(cta * (5 * num_layers + 1) + phase) * 8 + i] (slots 6, 7 unused).
+ * issue, the first and last stage observed, and for warp 0 of a GEMV phase the
+ * ns spent waiting for stages, the ns spent in its dot products and its unit
+ * count: out[(cta * (5 * num_layers + 1) + phase) * 12 + i] (slot 11 unused).
  * The sequence length is restored afterwards. */
 int hy_trace_persistent(hy_ctx* ctx, int tokens, int trace_token, unsigned long long* out);
 /* Failure diagnosis for the persistent kernel: with HY_DEBUG_PROGRESS=1 in the
