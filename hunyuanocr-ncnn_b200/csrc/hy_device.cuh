@@ -145,6 +145,13 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
+// Bulk prefetch of global memory into L2 (no destination, no completion).
+// src and bytes must be 16-byte aligned.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes)
+{
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Programmatic dependent launch: wait for the previous grid in the stream
 // (a no-op when the launch carried no programmatic dependency) / let the next
 // grid start its prologue.

@@ -6,27 +6,35 @@
 // export/text_decoder_kv.py:49-96 plus the LM head and select_next_token) is
 // a chain of 121 dependent phases per token: for each layer q/k/v projection,
 // attention, o projection, gate/up projection, down projection; then the LM
-// head. Each phase reads a different slice of the weights, and no weight byte
-// depends on an activation. So the kernel splits every CTA into
-//   - a producer warp that walks the token's phase list and streams this CTA's
-//     share of every phase (weight rows, or the K/V rows of its attention
-//     split) through a 12-stage x 16 KB shared-memory ring with cp.async.bulk;
-//     it only waits for free ring slots, never for the grid, so HBM stays busy
-//     while the consumers cross a phase boundary;
-//   - 8 consumer warps that, per phase, wait on a grid barrier (the phase's
-//     input activations are complete), stage the activation vector in shared
-//     memory (with the fused RMSNorm / SwiGLU / embedding gather), consume the
-//     ring stages of that phase and write their outputs, then arrive on the
-//     barrier.
-// Attention splits each KV head's keys over 17 CTAs plus one CTA for the new
-// row (RoPE + QK-norm + append); the last CTA of a head (atomic ticket) merges
-// the partials. The LM head's last CTA merges the per-CTA argmax partials and
-// commits the token (token log, state, penalty history).
+// head. Every phase is split across the CTAs (rows of the weight matrix, or a
+// range of cached positions for attention), and each CTA's share is cut into
+// stages of at most 16 KB.
+//
+// The CTA's stage sequence (over all phases and tokens of the launch) is dealt
+// round-robin to its 6 consumer warps: warp w owns the stages g with
+// g % 6 == w and has two 16 KB shared-memory slots of its own. A producer warp
+// walks the sequence and streams each stage into its owner's next slot with
+// cp.async.bulk (no multicast) as soon as the owner has released it, across
+// phase boundaries too - no weight byte depends on an activation, so the next
+// phase's weights are usually resident before its grid barrier opens. A
+// consumer warp waits only on its own slots, so the warps never wait on one
+// another inside a phase. A stage's rows are reduced in one pass: the warp
+// holds the activation vector in registers (K = 1024) and a transposing
+// butterfly leaves each row's sum in its own group of lanes, which then run the
+// epilogue in parallel.
+//
+// Warps meet at phase boundaries, where a grid barrier makes the phase's input
+// activations visible and the CTA stages them in shared memory (fused RMSNorm,
+// SwiGLU, embedding gather, attention split-K merge). Attention splits each KV
+// head's cached positions over 8 CTAs plus one CTA for the new row (RoPE +
+// QK-norm + KV append); every CTA merges the split partials in the
+// o-projection prologue. The LM head's last CTA (atomic ticket) merges the
+// per-CTA argmax partials and commits the token.
 //
 // The grid barrier is a monotonic counter (zeroed before each launch): phase p
 // may start when it reaches p * gridDim.x. All waits are bounded by wall clock;
-// a wait that gives up sets the error word and the CTA winds down (the
-// producer drains its in-flight copies first).
+// a wait that gives up sets the error word, the consumers leave together at the
+// end of the phase, and the producer drains its in-flight copies first.
 #pragma once
 
 #include "hy_attn.cuh"
@@ -35,12 +43,16 @@
 
 namespace hy {
 
-constexpr int kMegaWarps = 8;
-constexpr int kMegaThreads = (kMegaWarps + 1) * 32;
-constexpr int kMegaStage = 16384;
-constexpr int kMegaNst = 13;
-constexpr int kMegaSplits = 9;    // per KV head: 8 splits of the past rows + the new-row split
+constexpr int kMegaWarps = 6;                          // consumer warps
+constexpr int kMegaConsumers = kMegaWarps * 32;
+constexpr int kMegaThreads = kMegaConsumers + 32;      // + the producer warp
+constexpr int kMegaStage = 16384;        // bytes per slot
+constexpr int kMegaSlots = 2;            // slots per warp
+constexpr int kMegaSplits = 9;           // per KV head: 8 splits of the past rows + the new-row split
 constexpr int kMegaMaxK = 3584;
+constexpr int kMegaHistWords = 64;       // LM rows per CTA <= 32 * 62
+constexpr int kMegaResRows = 32;         // o/down rows per CTA (1024 / gridDim.x)
+constexpr int kMegaMaxLayers = 64;
 
 struct MegaArgs {
     const void* embed;
@@ -56,10 +68,10 @@ struct MegaArgs {
     const float* rope_sin;
     float* x;                 // residual stream [1024]
     float* qkv;               // [4096]
-    float* attn;              // [2048]
-    float* gu;                // [2 * ffn]
+    float* attn;              // unused here
+    float* gu;                // act = silu(gate) * up, [ffn]
     float* attn_part;         // [8][kMegaSplits][2][kPartStride]
-    int* attn_cnt;            // [L][8]
+    int* attn_cnt;            // unused here
     float4* lm_part;          // [gridDim.x]
     int* lm_cnt;
     unsigned* hist;
@@ -72,9 +84,8 @@ struct MegaArgs {
     int steps;                // tokens in this launch
     int* err;
     // Optional phase trace: for CTAs b < kTraceCtas and token trace_token,
-    // %globaltimer at phase start, after the grid wait, after the prologue and at
-    // the barrier arrive (consumer thread 0), then the producer's first and last
-    // stage issue of the phase: trace[(b * phases + ph) * kTraceSlots + i].
+    // %globaltimer at phase start, after the grid wait, after the prologue and
+    // at the barrier arrive (thread 0): trace[(b * phases + ph) * kTraceSlots + i].
     unsigned long long* trace;
     int trace_token;
     // Self-checks: the first failed bounds check stores (code, cta, phase, index)
@@ -84,32 +95,20 @@ struct MegaArgs {
     volatile unsigned* progress;
 };
 
-__device__ __forceinline__ bool mega_check(bool ok, int* dbg, int code, int b, int ph, int idx)
-{
-    if (ok) return true;
-    if (dbg && atomicCAS(dbg, 0, code) == 0)
-    {
-        dbg[1] = b;
-        dbg[2] = ph;
-        dbg[3] = idx;
-    }
-    return false;
-}
-
 constexpr int kTraceCtas = 4;
 constexpr int kTraceSlots = 12;
 
 struct MegaSmem {
-    static constexpr int RING = 0;
-    static constexpr int XS = RING + kMegaNst * kMegaStage;            // [3584] f32 activation vector
+    static constexpr int RING = 0;                                          // [warp][slot] x 16 KB
+    static constexpr int XS = RING + kMegaWarps * kMegaSlots * kMegaStage;  // [3584] f32 activation vector
     // Attention phases do not use the activation vector; their buffers alias it.
-    static constexpr int QS = XS;                                       // [2][128]
-    static constexpr int NEWKV = QS + 2 * kHeadDim * 4;                 // k[128], v[128]
-    static constexpr int ASCR = NEWKV + 2 * kHeadDim * 4;               // [8 warps][2][kPartStride]
+    static constexpr int QS = XS;                                           // [2][128]
+    static constexpr int NEWKV = QS + 2 * kHeadDim * 4;                     // k[128], v[128]
+    static constexpr int ASCR = NEWKV + 2 * kHeadDim * 4;                   // [warps][2][kPartStride]
     static_assert(ASCR + kMegaWarps * 2 * kPartStride * 4 <= XS + kMegaMaxK * 4, "attention scratch must fit");
-    static constexpr int RED = XS + kMegaMaxK * 4;                      // 64 float4 + ints
-    static constexpr int BARS = RED + 64 * 16 + 64 * 4;
-    static constexpr int SIZE = BARS + 2 * kMegaNst * 8;
+    static constexpr int RED = XS + kMegaMaxK * 4;                          // 64 float4 + 64 ints
+    static constexpr int BARS = RED + 64 * 16 + 64 * 4;                     // full[warp][slot], empty[warp][slot]
+    static constexpr int SIZE = BARS + 2 * kMegaWarps * kMegaSlots * 8;
 };
 
 enum { PH_QKV = 0, PH_ATTN = 1, PH_O = 2, PH_GU = 3, PH_DOWN = 4, PH_LM = 5 };
@@ -121,22 +120,75 @@ struct MegaPlan {
     int kind;
     int K;                      // gemv: row length (elements)
     int r0;                     // gemv: first row index
-    int count;                  // gemv: rows; attn: key positions
+    int count;                  // gemv: rows; attn: positions
     int unit_bytes;             // gemv: bytes per row; attn: bytes per K (or V) row
-    int per_stage;              // rows / positions per ring stage
+    int per_stage;              // rows / positions per stage
     int nstage;
-    int g, split, p0;           // attn
+    int g, split;               // attn
 };
 
-template <typename WT, typename KT>
-__device__ __forceinline__ MegaPlan mega_plan(const MegaArgs& a, int layer, int kind, int past, int b, int G)
+// This CTA's row split of one GEMV phase kind; the same for every layer and token.
+struct KindPlan {
+    int r0, count, per_stage, nstage, unit_bytes, K;
+};
+
+// Per-CTA plan tables in shared memory, built once per launch, so that the
+// stage walk never waits on a global load or a 64-bit division.
+struct MegaTables {
+    KindPlan kp[6];                                  // by phase kind (PH_ATTN unused)
+    const unsigned char* w[5][kMegaMaxLayers];       // weight base by kind and layer (PH_ATTN unused)
+    const unsigned char* embed;                      // tied LM head
+};
+
+template <typename WT>
+__device__ __forceinline__ void mega_init_tables(const MegaArgs& a, MegaTables& tb, int b, int G, int tid)
+{
+    if (tid < 6 && tid != PH_ATTN)
+    {
+        const int kind = tid;
+        int N, K;
+        switch (kind)
+        {
+        case PH_QKV: N = kQKVRows; K = kHidden; break;
+        case PH_O: N = kHidden; K = kQWidth; break;
+        case PH_GU: N = 2 * a.ffn; K = kHidden; break;
+        case PH_DOWN: N = kHidden; K = a.ffn; break;
+        default: N = a.vocab; K = kHidden; break;
+        }
+        // gate/up rows are interleaved (2j = gate_j, 2j+1 = up_j): that phase is
+        // split by pairs, and a stage never splits a pair.
+        const int unit = (kind == PH_GU) ? 2 : 1;
+        KindPlan k;
+        k.r0 = unit * static_cast<int>(static_cast<long long>(N / unit) * b / G);
+        const int r1 = unit * static_cast<int>(static_cast<long long>(N / unit) * (b + 1) / G);
+        k.count = r1 - k.r0;
+        k.K = K;
+        k.unit_bytes = K * static_cast<int>(sizeof(WT));
+        k.per_stage = min(8, max(1, kMegaStage / k.unit_bytes));
+        if (unit == 2) k.per_stage &= ~1;
+        k.nstage = (k.count + k.per_stage - 1) / k.per_stage;
+        tb.kp[kind] = k;
+    }
+    if (tid == 0) tb.embed = static_cast<const unsigned char*>(a.embed);
+    for (int e = tid; e < 4 * a.num_layers; e += kMegaThreads)
+    {
+        const int j = e / a.num_layers, l = e - j * a.num_layers;
+        const void* const* arr = (j == 0) ? a.wqkv : (j == 1) ? a.wo : (j == 2) ? a.wgu : a.wd;
+        tb.w[(j == 0) ? PH_QKV : j + 1][l] = static_cast<const unsigned char*>(arr[l]);
+    }
+}
+
+template <typename KT>
+__device__ __forceinline__ MegaPlan mega_plan(const MegaArgs& a, const MegaTables& tb, int layer, int kind, int past,
+                                              int b)
 {
     MegaPlan p;
     p.kind = kind;
-    p.src = p.src2 = nullptr;
-    p.g = p.split = p.p0 = 0;
+    p.src2 = nullptr;
+    p.g = p.split = 0;
     if (kind == PH_ATTN)
     {
+        p.src = nullptr;
         p.K = kHeadDim;
         p.r0 = 0;
         p.unit_bytes = kHeadDim * static_cast<int>(sizeof(KT));
@@ -145,13 +197,12 @@ __device__ __forceinline__ MegaPlan mega_plan(const MegaArgs& a, int layer, int 
         if (b < kNumKVHeads * kMegaSplits)
         {
             p.g = b / kMegaSplits;
-            p.split = b % kMegaSplits;
+            p.split = b - p.g * kMegaSplits;
             if (p.split < kMegaSplits - 1)
             {
                 const int chunk = (past + kMegaSplits - 2) / (kMegaSplits - 1);
                 const int p0 = min(past, p.split * chunk);
                 const int p1 = min(past, p0 + chunk);
-                p.p0 = p0;
                 p.count = p1 - p0;
                 const size_t off = ((static_cast<size_t>(layer) * kNumKVHeads + p.g) * a.cap + p0) * kHeadDim * sizeof(KT);
                 p.src = static_cast<const unsigned char*>(a.kc) + off;
@@ -161,25 +212,14 @@ __device__ __forceinline__ MegaPlan mega_plan(const MegaArgs& a, int layer, int 
         p.nstage = (p.count + p.per_stage - 1) / p.per_stage;
         return p;
     }
-    const void* W;
-    int N;
-    switch (kind)
-    {
-    case PH_QKV: W = a.wqkv[layer]; N = kQKVRows; p.K = kHidden; break;
-    case PH_O: W = a.wo[layer]; N = kHidden; p.K = kQWidth; break;
-    case PH_GU: W = a.wgu[layer]; N = 2 * a.ffn; p.K = kHidden; break;
-    case PH_DOWN: W = a.wd[layer]; N = kHidden; p.K = a.ffn; break;
-    default: W = a.embed; N = a.vocab; p.K = kHidden; break;
-    }
-    // gate/up rows are interleaved (2j = gate_j, 2j+1 = up_j): split that phase by pairs.
-    const int unit = (kind == PH_GU) ? 2 : 1;
-    p.r0 = unit * static_cast<int>(static_cast<long long>(N / unit) * b / G);
-    const int r1 = unit * static_cast<int>(static_cast<long long>(N / unit) * (b + 1) / G);
-    p.count = r1 - p.r0;
-    p.unit_bytes = p.K * static_cast<int>(sizeof(WT));
-    p.per_stage = max(1, kMegaStage / p.unit_bytes);
-    p.nstage = (p.count + p.per_stage - 1) / p.per_stage;
-    p.src = static_cast<const unsigned char*>(W) + static_cast<size_t>(p.r0) * p.unit_bytes;
+    const KindPlan& k = tb.kp[kind];
+    p.K = k.K;
+    p.r0 = k.r0;
+    p.count = k.count;
+    p.unit_bytes = k.unit_bytes;
+    p.per_stage = k.per_stage;
+    p.nstage = k.nstage;
+    p.src = ((kind == PH_LM) ? tb.embed : tb.w[kind][layer]) + static_cast<size_t>(k.r0) * k.unit_bytes;
     return p;
 }
 
@@ -205,7 +245,7 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p)
 }
 
 // Thread 0 only: poll with acquire loads. Returns false on timeout.
-// (Measured on B200 under streaming load: __threadfence + atomicAdd + acquire
+// (Measured on B200 under streaming load: __threadfence + red + acquire
 // polling costs ~2.0 us per grid barrier; red.release or a trailing
 // fence.acq_rel.gpu costs ~3.0 us.)
 __device__ __forceinline__ bool grid_wait(const unsigned* bar, unsigned target, int* err)
@@ -234,40 +274,85 @@ __device__ __forceinline__ void grid_arrive(unsigned* bar)
     asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
 }
 
-// <row0, xs> and <row1, xs> over K elements by one warp: lane-strided float4s,
-// two accumulators per row to shorten the FMA chains, and one interleaved
-// butterfly for both sums. `two` is warp-uniform; row1 is not read without it.
+// Rows per stage of a K-element row of WT (at most 8; even for K = 1024, so a
+// gate/up pair never straddles two stages).
 template <typename WT, int K>
-__device__ __forceinline__ float2 row_dot2(const WT* row0, const WT* row1, const float* xs, int lane, bool two)
+struct StageRows {
+    static constexpr int v = (kMegaStage / (K * static_cast<int>(sizeof(WT)))) < 8
+                                 ? (kMegaStage / (K * static_cast<int>(sizeof(WT))))
+                                 : 8;
+    static_assert(v >= 1, "a row must fit in a stage");
+};
+
+// Warp sum of R per-lane partials at once: halving exchanges (each lane keeps
+// the half of the rows named by its lane bit and adds its partner's copy of
+// them), then a plain butterfly. Lane l returns the sum of row l / (32 / R):
+// R - 1 + log2(32 / R) shuffles instead of 5 R.
+template <int R>
+__device__ __forceinline__ float reduce_rows(float (&v)[R], int lane)
+{
+#pragma unroll
+    for (int h = R / 2, o = 16; h >= 1; h >>= 1, o >>= 1)
+    {
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int j = 0; j < h; ++j)
+        {
+            const float send = up ? v[j] : v[j + h];
+            const float keep = up ? v[j + h] : v[j];
+            v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+    }
+    float s = v[0];
+#pragma unroll
+    for (int o = 16 / R; o >= 1; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    return s;
+}
+
+// Partial dot products of the R rows of one stage with x (lane-strided
+// float4s), reduced with reduce_rows. x comes from registers (XREG, K = 1024:
+// lane l holds float4 l + 32 i in xr[i]) or from shared memory.
+template <typename WT, int K, int R, bool XREG>
+__device__ __forceinline__ float stage_dot(const WT* rows, const float4 (&xr)[8], const float* xs, int lane)
 {
     static_assert(K % 128 == 0, "K must be a multiple of 128");
-    float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+    static_assert(!XREG || K == 1024, "register-resident x is 1024 wide");
+    constexpr int A = (R >= 4) ? 1 : 2;   // accumulators per row (FMA chain length)
+    float acc[R * A];
+#pragma unroll
+    for (int j = 0; j < R * A; ++j) acc[j] = 0.f;
 #pragma unroll
     for (int i = 0; i < K / 128; ++i)
     {
         const int c = lane + 32 * i;
-        const float4 xv = *reinterpret_cast<const float4*>(xs + 4 * c);
-        const float4 w0 = load4(row0 + 4 * c);
-        if (i & 1) a1 += dot4(w0, xv);
-        else a0 += dot4(w0, xv);
-        if (two)
-        {
-            const float4 w1 = load4(row1 + 4 * c);
-            if (i & 1) b1 += dot4(w1, xv);
-            else b0 += dot4(w1, xv);
-        }
-    }
-    float a = a0 + a1, b = b0 + b1;
+        float4 x;
+        if constexpr (XREG) x = xr[i];
+        else x = *reinterpret_cast<const float4*>(xs + 4 * c);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-    {
-        a += __shfl_xor_sync(0xffffffffu, a, o);
-        b += __shfl_xor_sync(0xffffffffu, b, o);
+        for (int r = 0; r < R; ++r) acc[r * A + (i % A)] += dot4(load4(rows + r * K + 4 * c), x);
     }
-    return make_float2(a, b);
+    float v[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+    {
+        v[r] = acc[r * A];
+#pragma unroll
+        for (int j = 1; j < A; ++j) v[r] += acc[r * A + j];
+    }
+    return reduce_rows<R>(v, lane);
 }
 
-constexpr int kMegaHistWords = 64;   // LM rows per CTA <= 32 * 62
+__device__ __forceinline__ bool mega_check(bool ok, int* dbg, int code, int b, int ph, int idx)
+{
+    if (ok) return true;
+    if (dbg && atomicCAS(dbg, 0, code) == 0)
+    {
+        dbg[1] = b;
+        dbg[2] = ph;
+        dbg[3] = idx;
+    }
+    return false;
+}
 
 // RoPE + RMSNorm of one 128-vector (as rope_norm_vec) whose source was
 // written by other CTAs of this launch: read through L2, never a stale L1 line.
@@ -287,25 +372,94 @@ __device__ __forceinline__ void rope_norm_vec_cg(const float* x, const float* c,
     out[3] = w[lane + 96] * (y3 * ri);
 }
 
-// xs = w * x for a 1024-vector x written by other CTAs; returns 1/sqrt(mean(x^2)+eps)
-// after one CTA barrier. The GEMV multiplies its dot products by it, i.e. the
-// RMSNorm's per-row scale is applied after the projection.
-__device__ __forceinline__ float mega_load_normed(float* xs, float4 v, const float* w, float eps, float* s_norm, int tid)
+// Named barrier of the consumer warps (the producer warp never joins it).
+__device__ __forceinline__ void mega_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kMegaConsumers) : "memory"); }
+
+// xs = w * x for a 1024-vector x given as float4 i = tid + 192 u in v[u];
+// returns 1/sqrt(mean(x^2)+eps) after one CTA barrier. The GEMV multiplies its
+// dot products by it, i.e. the RMSNorm's per-row scale is applied after the projection.
+__device__ __forceinline__ float mega_load_normed(float* xs, const float4 v[2], const float* w, float eps,
+                                                  float* s_norm, int tid)
 {
-    const float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
-    const float4 wv = *reinterpret_cast<const float4*>(w + tid * 4);
-    float4 o;
-    o.x = wv.x * v.x;
-    o.y = wv.y * v.y;
-    o.z = wv.z * v.z;
-    o.w = wv.w * v.w;
-    *reinterpret_cast<float4*>(xs + tid * 4) = o;
+    float ss = 0.f;
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+    {
+        const int i = tid + kMegaConsumers * u;
+        if (i < kHidden / 4)
+        {
+            const float4 wv = *reinterpret_cast<const float4*>(w + 4 * i);
+            ss += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
+            float4 o;
+            o.x = wv.x * v[u].x;
+            o.y = wv.y * v[u].y;
+            o.z = wv.z * v[u].z;
+            o.w = wv.w * v[u].w;
+            *reinterpret_cast<float4*>(xs + 4 * i) = o;
+        }
+    }
+    ss = warp_sum(ss);
     if ((tid & 31) == 0) s_norm[tid >> 5] = ss;
-    consumers_sync();
+    mega_sync();
     float t = 0.f;
 #pragma unroll
     for (int i = 0; i < kMegaWarps; ++i) t += s_norm[i];
     return 1.0f / sqrtf(t / static_cast<float>(kHidden) + eps);
+}
+
+// One GEMV stage of a consumer warp: dot products of the stage's rows, slot
+// release, and the epilogue run by one lane per row.
+struct LmBest {
+    float rv, pv;
+    int ri, pi;
+};
+
+template <typename WT, int K, bool XREG>
+__device__ __forceinline__ void gemv_stage(const MegaArgs& a, const MegaPlan& p, int kind, const WT* rows,
+                                           const float4 (&xr)[8], const float* xs, int q0, float rinv, float* xg,
+                                           const float* xres_s, const unsigned* hist_s, float pen, LmBest& best,
+                                           uint64_t* empty_bar, int lane, int b, int ph)
+{
+    constexpr int R = StageRows<WT, K>::v;
+    const float val = stage_dot<WT, K, R, XREG>(rows, xr, xs, lane) * rinv;
+    // Every lane's slot reads have returned (their values went through the
+    // shuffles): hand the slot back to the producer.
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty_bar);
+
+    const int n = min(R, p.count - q0);
+    constexpr int LPR = 32 / R;   // lanes holding each row's sum
+    const int r = lane / LPR;
+    const int row = p.r0 + q0 + r;
+    const int nrows = (kind == PH_QKV) ? kQKVRows : (kind == PH_GU) ? 2 * a.ffn : (kind == PH_LM) ? a.vocab : kHidden;
+    const bool ok = mega_check(p.r0 + q0 + n <= nrows && ((kind != PH_O && kind != PH_DOWN) || q0 + n <= kMegaResRows),
+                               a.dbg, 2, b, ph, p.r0 + q0);
+    const bool lead = ok && (lane % LPR) == 0 && r < n;
+    if (kind == PH_QKV)
+    {
+        if (lead) a.qkv[row] = val;
+    }
+    else if (kind == PH_GU)
+    {
+        // act = silu(gate) * up; gate = even row, up = the next row's lanes.
+        const float up = __shfl_down_sync(0xffffffffu, val, LPR);
+        if (lead && !(r & 1)) a.gu[row >> 1] = (val / (1.0f + expf(-val))) * up;
+    }
+    else if (kind == PH_O || kind == PH_DOWN)
+    {
+        if (lead) xg[row] = xres_s[q0 + r] + val;
+    }
+    else if (lead)
+    {
+        const int wi = (row >> 5) - (p.r0 >> 5);
+        if (mega_check(wi >= 0 && wi < kMegaHistWords, a.dbg, 3, b, ph, wi))
+        {
+            const bool hit = (hist_s[wi] >> (row & 31)) & 1u;
+            const float ps = hit ? (val < 0.0f ? val * pen : val / pen) : val;
+            if (best.ri < 0 || val > best.rv) { best.rv = val; best.ri = row; }
+            if (best.pi < 0 || ps > best.pv) { best.pv = ps; best.pi = row; }
+        }
+    }
 }
 
 template <typename WT, typename KT>
@@ -320,10 +474,12 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
     float* ascr = reinterpret_cast<float*>(smem + MegaSmem::ASCR);
     float4* red4 = reinterpret_cast<float4*>(smem + MegaSmem::RED);
     int* redi = reinterpret_cast<int*>(red4 + 64);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + MegaSmem::BARS);
-    uint64_t* empty = full + kMegaNst;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + MegaSmem::BARS);   // [warp][slot]
+    uint64_t* empty = full + kMegaWarps * kMegaSlots;                      // [warp][slot]
     __shared__ unsigned hist_s[kMegaHistWords];
+    __shared__ float xres_s[kMegaResRows];
     __shared__ float s_norm[kMegaWarps];
+    __shared__ MegaTables tb;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, b = blockIdx.x;
@@ -333,14 +489,15 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
 
     if (tid == 0)
     {
-        for (int s = 0; s < kMegaNst; ++s)
+        for (int s = 0; s < kMegaWarps * kMegaSlots; ++s)
         {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kMegaWarps);
+            mbar_init(&empty[s], 1);
         }
         fence_mbar_init();
         redi[0] = 0;  // abort flag
     }
+    mega_init_tables<WT>(a, tb, b, G, tid);
     __syncthreads();
 
     if (warp == kMegaWarps)
@@ -348,66 +505,79 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
         // ======================= producer =======================
         if (lane != 0) return;
         const uint64_t pol = l2_evict_first_policy();
-        unsigned gs = 0;
+        unsigned g = 0;   // global stage index: owner warp g % 6, its stage number g / 6
         bool ok = true;
         for (int t = 0; t < a.steps && ok; ++t)
         {
-            const int past = kv0 + t;
             for (int ph = 0; ph < phases && ok; ++ph)
             {
                 int layer, kind;
                 mega_phase_of(ph, L, layer, kind);
-                const MegaPlan p = mega_plan<WT, KT>(a, layer, kind, past, b, G);
-                if (kind == PH_ATTN && p.nstage > 0) asm volatile("fence.proxy.async.global;" ::: "memory");
-                unsigned long long* ptr_ = (a.trace && t == a.trace_token && b < kTraceCtas)
-                                               ? a.trace + (static_cast<size_t>(b) * phases + ph) * kTraceSlots
-                                               : nullptr;
-                for (int i = 0; i < p.nstage; ++i, ++gs)
+                const MegaPlan p = mega_plan<KT>(a, tb, layer, kind, kv0 + t, b);
+                for (int i = 0; i < p.nstage; ++i, ++g)
                 {
-                    const int slot = gs % kMegaNst;
-                    if (gs >= kMegaNst && !mbar_wait(&empty[slot], ((gs / kMegaNst) - 1) & 1, a.err, kErrTimeoutEmpty))
+                    const int w = g % kMegaWarps;
+                    const unsigned j = g / kMegaWarps;
+                    const int s = w * kMegaSlots + static_cast<int>(j % kMegaSlots);
+                    // The owner released this slot's previous stage (j - kMegaSlots).
+                    if (j >= kMegaSlots && !mbar_wait(&empty[s], ((j / kMegaSlots) - 1) & 1, a.err, kErrTimeoutEmpty))
                     {
                         ok = false;
                         break;
                     }
-                    if (ptr_)
-                    {
-                        if (i == 0) ptr_[4] = global_ns();
-                        if (i == p.nstage - 1) ptr_[5] = global_ns();
-                    }
                     const int n = min(p.per_stage, p.count - i * p.per_stage);
                     const uint32_t bytes = static_cast<uint32_t>(n * p.unit_bytes);
-                    unsigned char* dst = ring + slot * kMegaStage;
+                    unsigned char* dst = ring + static_cast<size_t>(s) * kMegaStage;
                     const size_t off = static_cast<size_t>(i) * p.per_stage * p.unit_bytes;
                     if (kind == PH_ATTN)
                     {
-                        mbar_arrive_expect_tx(&full[slot], 2 * bytes);
-                        bulk_g2s(dst, p.src + off, bytes, &full[slot], pol);
-                        bulk_g2s(dst + p.per_stage * p.unit_bytes, p.src2 + off, bytes, &full[slot], pol);
+                        // (The K/V rows' writers fenced them for the async proxy.)
+                        mbar_arrive_expect_tx(&full[s], 2 * bytes);
+                        bulk_g2s(dst, p.src + off, bytes, &full[s], pol);
+                        bulk_g2s(dst + p.per_stage * p.unit_bytes, p.src2 + off, bytes, &full[s], pol);
                     }
                     else
                     {
-                        mbar_arrive_expect_tx(&full[slot], bytes);
-                        bulk_g2s(dst, p.src + off, bytes, &full[slot], pol);
+                        mbar_arrive_expect_tx(&full[s], bytes);
+                        bulk_g2s(dst, p.src + off, bytes, &full[s], pol);
                     }
                 }
             }
         }
-        // Drain: the last kMegaNst stages issued (earlier ones completed before their slot was reused).
-        const unsigned first = gs > kMegaNst ? gs - kMegaNst : 0;
-        for (unsigned i = first; i < gs; ++i) mbar_wait(&full[i % kMegaNst], (i / kMegaNst) & 1, a.err, kErrTimeoutFull);
+        // Drain: the last kMegaSlots stages of every warp (earlier ones landed
+        // before their slot was released).
+        const unsigned tail = kMegaWarps * kMegaSlots;
+        for (unsigned gg = (g > tail ? g - tail : 0); gg < g; ++gg)
+        {
+            const unsigned j = gg / kMegaWarps;
+            mbar_wait(&full[(gg % kMegaWarps) * kMegaSlots + j % kMegaSlots], (j / kMegaSlots) & 1, a.err,
+                      kErrTimeoutFull);
+        }
         return;
     }
 
     // ======================= consumers =======================
-    unsigned gs = 0;
+    uint64_t* myfull = full + warp * kMegaSlots;
+    uint64_t* myempty = empty + warp * kMegaSlots;
+    const unsigned char* myring = ring + static_cast<size_t>(warp) * kMegaSlots * kMegaStage;
+    unsigned consumed = 0;   // this warp's stages consumed so far
+    // Wait for the next own stage; its slot, or -1 on timeout. Each wait is on
+    // the barrier's next phase: the producer refills a slot only after the
+    // warp released it (parity waits are exact one phase ahead).
+    auto wait_own = [&]() -> int {
+        const int slot = consumed % kMegaSlots;
+        const bool okw = mbar_wait(&myfull[slot], (consumed / kMegaSlots) & 1, a.err, kErrTimeoutFull);
+        ++consumed;
+        return __all_sync(0xffffffffu, okw) ? slot : -1;
+    };
+
+    unsigned gs = 0;          // global stage index of the current phase's first stage
     unsigned phase_no = 0;
     float* xg = a.x;
-    // A failed ring wait marks this warp bad; every warp still walks the same
-    // sequence of CTA barriers, and the CTA leaves together after the phase.
+    // A failed wait marks the warp bad and raises the CTA's abort flag; every
+    // warp still takes the phase's CTA barriers, and the CTA leaves together.
     bool bad = false;
-    // Per-warp argmax trackers for the LM phase.
-    for (int t = 0; t < a.steps; ++t)
+    for (int t = 0; t < a.steps && !bad; ++t)
     {
         const int past = kv0 + t;
         for (int ph = 0; ph < phases; ++ph, ++phase_no)
@@ -417,233 +587,205 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
             const bool tracing = a.trace && t == a.trace_token && b < kTraceCtas && tid == 0;
             unsigned long long* tr = tracing ? a.trace + (static_cast<size_t>(b) * phases + ph) * kTraceSlots : nullptr;
             if (tracing) tr[0] = global_ns();
+            // Warp-0 trace: SM cycles waiting on slots / working, stages.
+            const bool wtr = a.trace && t == a.trace_token && b < kTraceCtas && tid == 0;
+            long long wwait = 0, wwork = 0, wn = 0;
             if (phase_no > 0)
             {
                 if (tid == 0 && !grid_wait(a.bar, phase_no * G, a.err)) redi[0] = 1;
-                consumers_sync();
-                if (redi[0]) return;
+                mega_sync();
+                if (redi[0])
+                {
+                    bad = true;
+                    break;
+                }
             }
             if (tracing) tr[1] = global_ns();
-            const MegaPlan p = mega_plan<WT, KT>(a, layer, kind, past, b, G);
+            const MegaPlan p = mega_plan<KT>(a, tb, layer, kind, past, b);
             const float* lnorm = a.norms + static_cast<size_t>(layer) * 2304;
+            // This warp's stages of the phase: first, first + 6, ...
+            const int first = static_cast<int>((warp - static_cast<int>(gs % kMegaWarps) + kMegaWarps) % kMegaWarps);
 
             // ---------------- prologue: activation vector ----------------
             float rinv = 1.0f;   // RMSNorm scale applied to the dot products
-            if (kind == PH_QKV)
+            if (kind == PH_QKV || kind == PH_GU || kind == PH_LM)
             {
-                float4 v;
-                if (layer == 0)
+                const bool gather = (kind == PH_QKV && layer == 0);
+                int id = 0;
+                if (gather)
                 {
-                    int id = __ldcg(&a.st->cur_token);
+                    id = __ldcg(&a.st->cur_token);
                     if (id < 0 || id >= a.vocab)
                     {
                         if (tid == 0) atomicOr(a.err, kErrBounds);
                         id = 0;
                     }
-                    v = load4(static_cast<const WT*>(a.embed) + static_cast<size_t>(id) * kHidden + tid * 4);
+                }
+                float4 v[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u)
+                {
+                    const int i = tid + kMegaConsumers * u;
+                    v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (i < kHidden / 4)
+                        v[u] = gather ? load4(static_cast<const WT*>(a.embed) + static_cast<size_t>(id) * kHidden + 4 * i)
+                                      : __ldcg(reinterpret_cast<const float4*>(xg) + i);
+                }
+                if (gather)
+                {
                     // Publish this CTA's slice of the residual stream.
                     const int chunk = (kHidden + G - 1) / G;
                     const int i = b * chunk + tid;
-                    if (tid < chunk && i < kHidden) xg[i] = to_f32<WT>(static_cast<const WT*>(a.embed)[static_cast<size_t>(id) * kHidden + i]);
+                    if (tid < chunk && i < kHidden)
+                        xg[i] = to_f32<WT>(static_cast<const WT*>(a.embed)[static_cast<size_t>(id) * kHidden + i]);
                 }
-                else
-                {
-                    v = __ldcg(reinterpret_cast<const float4*>(xg) + tid);
-                }
-                rinv = mega_load_normed(xs, v, lnorm, a.eps, s_norm, tid);
-            }
-            else if (kind == PH_O)
-            {
-                // Merge the attention partials of every split (split-K flash-decode
-                // combine): thread t handles q head t / 16, dims 8 * (t % 16) .. +8.
-                // All loads are issued before any use, so this is one L2 round trip.
-                const int h = tid >> 4, d0 = (tid & 15) * 8;
-                const float* hp = a.attn_part + (static_cast<size_t>(h >> 1) * kMegaSplits * 2 + (h & 1)) * kPartStride;
-                float ms[kMegaSplits], ls[kMegaSplits];
-                float4 va[kMegaSplits], vb[kMegaSplits];
-#pragma unroll
-                for (int sp = 0; sp < kMegaSplits; ++sp)
-                {
-                    const float* ps = hp + static_cast<size_t>(sp) * 2 * kPartStride;
-                    ms[sp] = __ldcg(ps);
-                    ls[sp] = __ldcg(ps + 1);
-                    va[sp] = __ldcg(reinterpret_cast<const float4*>(ps + 4 + d0));
-                    vb[sp] = __ldcg(reinterpret_cast<const float4*>(ps + 8 + d0));
-                }
-                float M = -INFINITY;
-#pragma unroll
-                for (int sp = 0; sp < kMegaSplits; ++sp) M = fmaxf(M, ms[sp]);
-                float Lsum = 0.f;
-                float4 A0 = make_float4(0.f, 0.f, 0.f, 0.f), A1 = A0;
-#pragma unroll
-                for (int sp = 0; sp < kMegaSplits; ++sp)
-                {
-                    const float f = (ms[sp] == -INFINITY) ? 0.f : exp2f(ms[sp] - M);
-                    Lsum += f * ls[sp];
-                    A0.x += f * va[sp].x; A0.y += f * va[sp].y; A0.z += f * va[sp].z; A0.w += f * va[sp].w;
-                    A1.x += f * vb[sp].x; A1.y += f * vb[sp].y; A1.z += f * vb[sp].z; A1.w += f * vb[sp].w;
-                }
-                const float inv = 1.0f / Lsum;
-                A0.x *= inv; A0.y *= inv; A0.z *= inv; A0.w *= inv;
-                A1.x *= inv; A1.y *= inv; A1.z *= inv; A1.w *= inv;
-                *reinterpret_cast<float4*>(xs + h * kHeadDim + d0) = A0;
-                *reinterpret_cast<float4*>(xs + h * kHeadDim + d0 + 4) = A1;
-                consumers_sync();
-            }
-            else if (kind == PH_GU || kind == PH_LM)
-            {
-                const float4 v = __ldcg(reinterpret_cast<const float4*>(xg) + tid);
                 if (kind == PH_LM && p.count > 0)
                 {
                     // Penalty-history words covering this CTA's vocab rows.
                     const int w0 = p.r0 >> 5, w1 = (p.r0 + p.count - 1) >> 5;
                     if (tid <= w1 - w0 && tid < kMegaHistWords) hist_s[tid] = __ldcg(a.hist + w0 + tid);
                 }
-                rinv = mega_load_normed(xs, v, kind == PH_GU ? lnorm + kHidden : a.norms + static_cast<size_t>(L) * 2304,
-                                        a.eps, s_norm, tid);
+                const float* nw = (kind == PH_QKV) ? lnorm
+                                  : (kind == PH_GU) ? lnorm + kHidden
+                                                    : a.norms + static_cast<size_t>(L) * 2304;
+                rinv = mega_load_normed(xs, v, nw, a.eps, s_norm, tid);
             }
-            else if (kind == PH_DOWN)
+            else if (kind == PH_O || kind == PH_DOWN)
             {
-                // The gate/up phase already wrote act = silu(gate) * up; all loads issue before use.
-                constexpr int kPer = (kMegaMaxK / 4 + 255) / 256;
-                float4 av[kPer];
-#pragma unroll
-                for (int u = 0; u < kPer; ++u)
+                // Residual rows this CTA updates in the epilogue.
+                if (tid < p.count && tid < kMegaResRows) xres_s[tid] = __ldcg(xg + p.r0 + tid);
+                if (kind == PH_O)
                 {
-                    const int i = tid + 256 * u;
-                    if (i < a.ffn / 4) av[u] = __ldcg(reinterpret_cast<const float4*>(a.gu) + i);
-                }
+                    // Merge the attention partials of every split (split-K
+                    // flash-decode combine): 12 threads per q head, thread k
+                    // taking float4 columns k, k + 12, k + 24 (< 32). All loads
+                    // issue before any use: one L2 round trip.
+                    static_assert(kMegaConsumers == kNumQHeads * 12, "12 threads per head");
+                    const int h = tid / 12, k0 = tid - 12 * h;
+                    const float* hp = a.attn_part + (static_cast<size_t>(h >> 1) * kMegaSplits * 2 + (h & 1)) * kPartStride;
+                    float ms[kMegaSplits], ls[kMegaSplits];
+                    float4 va[kMegaSplits][3];
 #pragma unroll
-                for (int u = 0; u < kPer; ++u)
-                {
-                    const int i = tid + 256 * u;
-                    if (i < a.ffn / 4) reinterpret_cast<float4*>(xs)[i] = av[u];
+                    for (int sp = 0; sp < kMegaSplits; ++sp)
+                    {
+                        const float* ps = hp + static_cast<size_t>(sp) * 2 * kPartStride;
+                        ms[sp] = __ldcg(ps);
+                        ls[sp] = __ldcg(ps + 1);
+#pragma unroll
+                        for (int j = 0; j < 3; ++j)
+                            va[sp][j] = (k0 + 12 * j < kHeadDim / 4)
+                                            ? __ldcg(reinterpret_cast<const float4*>(ps + 4) + k0 + 12 * j)
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                    float M = -INFINITY;
+#pragma unroll
+                    for (int sp = 0; sp < kMegaSplits; ++sp) M = fmaxf(M, ms[sp]);
+                    float Lsum = 0.f;
+                    float4 A[3];
+#pragma unroll
+                    for (int j = 0; j < 3; ++j) A[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                    for (int sp = 0; sp < kMegaSplits; ++sp)
+                    {
+                        const float f = (ms[sp] == -INFINITY) ? 0.f : exp2f(ms[sp] - M);
+                        Lsum += f * ls[sp];
+#pragma unroll
+                        for (int j = 0; j < 3; ++j)
+                        {
+                            A[j].x += f * va[sp][j].x;
+                            A[j].y += f * va[sp][j].y;
+                            A[j].z += f * va[sp][j].z;
+                            A[j].w += f * va[sp][j].w;
+                        }
+                    }
+                    const float inv = 1.0f / Lsum;
+#pragma unroll
+                    for (int j = 0; j < 3; ++j)
+                    {
+                        if (k0 + 12 * j >= kHeadDim / 4) break;
+                        float4 o = A[j];
+                        o.x *= inv; o.y *= inv; o.z *= inv; o.w *= inv;
+                        *reinterpret_cast<float4*>(xs + h * kHeadDim + 4 * (k0 + 12 * j)) = o;
+                    }
                 }
-                consumers_sync();
+                else
+                {
+                    // The gate/up phase wrote act = silu(gate) * up; all loads issue before use.
+                    constexpr int kPer = (kMegaMaxK / 4 + kMegaConsumers - 1) / kMegaConsumers;
+                    float4 av[kPer];
+#pragma unroll
+                    for (int u = 0; u < kPer; ++u)
+                    {
+                        const int i = tid + kMegaConsumers * u;
+                        if (i < a.ffn / 4) av[u] = __ldcg(reinterpret_cast<const float4*>(a.gu) + i);
+                    }
+#pragma unroll
+                    for (int u = 0; u < kPer; ++u)
+                    {
+                        const int i = tid + kMegaConsumers * u;
+                        if (i < a.ffn / 4) reinterpret_cast<float4*>(xs)[i] = av[u];
+                    }
+                }
+                mega_sync();
             }
-
             if (tracing) tr[2] = global_ns();
+
             if (kind != PH_ATTN)
             {
-                // ---------------- GEMV rows ----------------
-                float best_rv = 0.f, best_pv = 0.f;
-                int best_ri = -1, best_pi = -1;
+                // ---------------- GEMV rows of this warp's stages ----------------
+                LmBest best{0.f, 0.f, -1, -1};
                 const float pen = a.st->penalty;
-                const WT* ringw = reinterpret_cast<const WT*>(ring);
-                // Units of up to two rows (a gate/up pair for PH_GU): unit o belongs to
-                // warp o % 8 and its rows share one ring stage. Every warp observes
-                // every stage of the phase in order and arrives once on it (the
-                // owner after its dot products, the others at once): an mbarrier
-                // parity wait is only meaningful one phase ahead, so no warp may skip
-                // ahead of a stage that has not landed, nor let a slot be reused
-                // before it has seen it.
-                const int rpu = (p.per_stage >= 2) ? 2 : 1;
-                const unsigned gs0 = gs;
-                int o = warp;   // next unit this warp owns
-                // Residual rows of this warp's first unit, fetched now so the
-                // epilogue's read-modify-write does not wait on L2.
-                float xpre0 = 0.f, xpre1 = 0.f;
-                if ((kind == PH_O || kind == PH_DOWN) && lane == 0 && warp * rpu < p.count)
+                // The normalised activation vector in registers for K = 1024.
+                float4 xr[8];
+                if (p.K == kHidden)
                 {
-                    xpre0 = __ldcg(xg + p.r0 + warp * rpu);
-                    if (rpu == 2 && warp * rpu + 1 < p.count) xpre1 = __ldcg(xg + p.r0 + warp * rpu + 1);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) xr[i] = reinterpret_cast<const float4*>(xs)[lane + 32 * i];
                 }
-                unsigned long long t_wait = 0, t_dot = 0, n_units = 0;   // warp-0 trace accumulators
-                for (int i = 0; i < p.nstage && !bad; ++i)
+                for (int i = first; i < p.nstage && !bad; i += kMegaWarps)
                 {
-                    const unsigned gsi = gs0 + i;
-                    const int slot = gsi % kMegaNst;
-                    const unsigned long long tw0 = tracing ? global_ns() : 0;
-                    const bool okw = mbar_wait(&full[slot], (gsi / kMegaNst) & 1, a.err, kErrTimeoutFull);
-                    if (tracing) t_wait += global_ns() - tw0;
-                    if (!__all_sync(0xffffffffu, okw))
+                    const long long c0 = wtr ? clock64() : 0;
+                    const int slot = wait_own();
+                    const long long c1 = wtr ? clock64() : 0;
+                    if (slot < 0)
                     {
                         if (lane == 0) redi[0] = 1;
                         bad = true;
                         break;
                     }
-                    if (tracing)
+                    const WT* rows = reinterpret_cast<const WT*>(myring + slot * kMegaStage);
+                    const int q0 = i * p.per_stage;
+                    if (p.K == kHidden)
+                        gemv_stage<WT, kHidden, true>(a, p, kind, rows, xr, xs, q0, rinv, xg, xres_s, hist_s, pen, best,
+                                                      &myempty[slot], lane, b, ph);
+                    else if (p.K == kQWidth)
+                        gemv_stage<WT, kQWidth, false>(a, p, kind, rows, xr, xs, q0, rinv, xg, xres_s, hist_s, pen, best,
+                                                       &myempty[slot], lane, b, ph);
+                    else
+                        gemv_stage<WT, kMegaMaxK, false>(a, p, kind, rows, xr, xs, q0, rinv, xg, xres_s, hist_s, pen,
+                                                         best, &myempty[slot], lane, b, ph);
+                    if (wtr)
                     {
-                        if (i == 0) tr[6] = global_ns();
-                        if (i == p.nstage - 1) tr[7] = global_ns();
+                        wwait += c1 - c0;
+                        wwork += clock64() - c1;
+                        ++wn;
                     }
-                    const int row_end = min(p.count, (i + 1) * p.per_stage);
-                    const int q = o * rpu;
-                    const bool mine = q < row_end;   // at most one unit per warp per stage
-                    const bool two = mine && (rpu == 2) && (q + 1 < p.count);
-                    float2 d = make_float2(0.f, 0.f);
-                    const unsigned long long td0 = tracing ? global_ns() : 0;
-                    if (mine)
-                    {
-                        const int j = q - i * p.per_stage;
-                        const WT* row = ringw + (static_cast<size_t>(slot) * kMegaStage) / sizeof(WT) + static_cast<size_t>(j) * p.K;
-                        if (mega_check(j >= 0 && (j + (two ? 2 : 1)) * p.K * static_cast<int>(sizeof(WT)) <= kMegaStage,
-                                       a.dbg, 1, b, ph, j * 1000 + p.K))
-                        {
-                            if (p.K == kHidden) d = row_dot2<WT, kHidden>(row, row + kHidden, xs, lane, two);
-                            else if (p.K == kQWidth) d = row_dot2<WT, kQWidth>(row, row + kQWidth, xs, lane, two);
-                            else d = row_dot2<WT, kMegaMaxK>(row, row + kMegaMaxK, xs, lane, two);
-                        }
-                        o += kMegaWarps;
-                    }
-                    __syncwarp();
-                    if (tracing && mine)
-                    {
-                        t_dot += global_ns() - td0;
-                        ++n_units;
-                    }
-                    if (lane == 0) mbar_arrive(&empty[slot]);
-                    if (mine && lane == 0)
-                    {
-                        const int nrow = p.r0 + q;
-                        const float v0 = d.x * rinv, v1 = d.y * rinv;
-                        const int nlimit = (kind == PH_QKV) ? kQKVRows : (kind == PH_GU) ? 2 * a.ffn
-                                         : (kind == PH_LM) ? a.vocab : kHidden;
-                        if (!mega_check(nrow >= 0 && nrow + (two ? 1 : 0) < nlimit, a.dbg, 2, b, ph, nrow)) continue;
-                        if (kind == PH_QKV)
-                        {
-                            a.qkv[nrow] = v0;
-                            if (two) a.qkv[nrow + 1] = v1;
-                        }
-                        else if (kind == PH_GU)
-                        {
-                            a.gu[nrow >> 1] = (v0 / (1.0f + expf(-v0))) * v1;   // act = silu(gate) * up
-                        }
-                        else if (kind == PH_O || kind == PH_DOWN)
-                        {
-                            const bool first = (q == warp * rpu);
-                            const float x0 = first ? xpre0 : __ldcg(xg + nrow);
-                            const float x1 = two ? (first ? xpre1 : __ldcg(xg + nrow + 1)) : 0.f;
-                            xg[nrow] = x0 + v0;
-                            if (two) xg[nrow + 1] = x1 + v1;
-                        }
-                        else
-                        {
-                            for (int r = 0; r < (two ? 2 : 1); ++r)
-                            {
-                                const float acc = r ? v1 : v0;
-                                const int vr = nrow + r;
-                                const int wi = (vr >> 5) - (p.r0 >> 5);
-                                if (!mega_check(wi >= 0 && wi < kMegaHistWords, a.dbg, 3, b, ph, wi)) continue;
-                                const bool hit = (hist_s[wi] >> (vr & 31)) & 1u;
-                                const float ps = hit ? (acc < 0.0f ? acc * pen : acc / pen) : acc;
-                                if (best_ri < 0 || acc > best_rv) { best_rv = acc; best_ri = vr; }
-                                if (best_pi < 0 || ps > best_pv) { best_pv = ps; best_pi = vr; }
-                            }
-                        }
-                    }
-                }
-                gs = gs0 + p.nstage;
-                if (tracing)
-                {
-                    tr[8] = t_wait;
-                    tr[9] = t_dot;
-                    tr[10] = n_units;
                 }
                 if (kind == PH_LM)
                 {
-                    if (lane == 0) red4[warp] = make_float4(best_rv, __int_as_float(best_ri), best_pv, __int_as_float(best_pi));
-                    consumers_sync();
+                    // This warp's best rows: merge the lanes, then the warps.
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1)
+                    {
+                        const float orv = __shfl_xor_sync(0xffffffffu, best.rv, o);
+                        const int ori = __shfl_xor_sync(0xffffffffu, best.ri, o);
+                        const float opv = __shfl_xor_sync(0xffffffffu, best.pv, o);
+                        const int opi = __shfl_xor_sync(0xffffffffu, best.pi, o);
+                        if (ori >= 0) best_update(best.rv, best.ri, orv, ori);
+                        if (opi >= 0) best_update(best.pv, best.pi, opv, opi);
+                    }
+                    if (lane == 0) red4[warp] = make_float4(best.rv, __int_as_float(best.ri), best.pv, __int_as_float(best.pi));
+                    mega_sync();
                     if (tid == 0)
                     {
                         float rv = 0.f, pv = 0.f;
@@ -658,14 +800,14 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                         __threadfence();
                         redi[1] = (atomicAdd(a.lm_cnt, 1) == G - 1) ? 1 : 0;
                     }
-                    consumers_sync();
+                    mega_sync();
                     if (redi[1])
                     {
-                        // Last CTA: merge the G partials (parallel loads, then a tree in shared memory).
+                        // Last CTA: merge the G partials (parallel loads, then a tree).
                         __threadfence();
                         float rv = 0.f, pv = 0.f;
                         int ri = -1, pi = -1;
-                        for (int c = tid; c < G; c += 256)
+                        for (int c = tid; c < G; c += kMegaConsumers)
                         {
                             const float4 v = __ldcg(&a.lm_part[c]);
                             if (__float_as_int(v.y) >= 0) best_update(rv, ri, v.x, __float_as_int(v.y));
@@ -682,7 +824,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                             if (opi >= 0) best_update(pv, pi, opv, opi);
                         }
                         if (lane == 0) red4[8 + warp] = make_float4(rv, __int_as_float(ri), pv, __int_as_float(pi));
-                        consumers_sync();
+                        mega_sync();
                         if (tid == 0)
                         {
                             float frv = 0.f, fpv = 0.f;
@@ -695,7 +837,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                             }
                             *a.lm_cnt = 0;
                             volatile DecodeState* st = a.st;
-                            if (!mega_check(fpi >= 0 && fpi < a.vocab && fri >= 0 && fri < a.vocab, a.dbg, 4, b, phases - 1, fpi))
+                            if (!mega_check(fpi >= 0 && fpi < a.vocab && fri >= 0 && fri < a.vocab, a.dbg, 4, b, ph, fpi))
                             {
                                 st->done = 1;
                             }
@@ -751,6 +893,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                         krow[lane + 32 * i] = q;
                         knew[lane + 32 * i] = to_f32<KT>(q);
                     }
+                    // Later tokens read this row with bulk copies (async proxy).
+                    asm volatile("fence.proxy.async.global;" ::: "memory");
                 }
                 else if (new_split && warp == 3)
                 {
@@ -764,12 +908,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                         vrow[lane + 32 * i] = q;
                         vnew[lane + 32 * i] = to_f32<KT>(q);
                     }
+                    asm volatile("fence.proxy.async.global;" ::: "memory");
                 }
-                consumers_sync();
+                mega_sync();
 
-                // lane = (pg: 2, qq: 2, qr: 8); a lane owns dims 4*(qr + 8j) + e, j < 4.
+                // lane = (pg: 2, qq: 2, qr: 8): position group, query, dim
+                // group; a lane owns dims 4 * (qr + 8 j) + e of query qq, j < 4.
                 const int qr = lane & 7, qq = (lane >> 3) & 1, pg = lane >> 4;
-                const int stream = warp * 2 + pg;  // 16 position streams
                 float4 q4[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) q4[j] = *reinterpret_cast<const float4*>(qs + qq * kHeadDim + 4 * (qr + 8 * j));
@@ -777,6 +922,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                 float4 acc[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                // Online softmax over one position (scores in log2 units).
                 auto visit = [&](const auto* krow, const auto* vrow, bool visible) {
                     float sc = 0.f;
 #pragma unroll
@@ -800,37 +946,29 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                     }
                     mx = mn;
                 };
-                const KT* ringk = reinterpret_cast<const KT*>(ring);
-                for (int i = 0; i < p.nstage; ++i, ++gs)
+                for (int i = first; i < p.nstage && !bad; i += kMegaWarps)
                 {
-                    const int slot = gs % kMegaNst;
-                    if (bad) continue;
-                    const bool okw = mbar_wait(&full[slot], (gs / kMegaNst) & 1, a.err, kErrTimeoutFull);
-                    if (!__all_sync(0xffffffffu, okw))
+                    const int slot = wait_own();
+                    if (slot < 0)
                     {
                         if (lane == 0) redi[0] = 1;
                         bad = true;
-                        continue;
+                        break;
                     }
-                    if (tracing)
-                    {
-                        if (i == 0) tr[6] = global_ns();
-                        if (i == p.nstage - 1) tr[7] = global_ns();
-                    }
-                    const KT* kst = ringk + (static_cast<size_t>(slot) * kMegaStage) / sizeof(KT);
+                    const KT* kst = reinterpret_cast<const KT*>(myring + slot * kMegaStage);
                     const KT* vst = kst + static_cast<size_t>(p.per_stage) * kHeadDim;
                     const int n = min(p.per_stage, p.count - i * p.per_stage);
-                    for (int jb = 0; jb < n; jb += 16)
+                    for (int jb = 0; jb < n; jb += 2)
                     {
-                        const int j = jb + stream;
+                        const int j = jb + pg;
                         const int jj = (j < n) ? j : 0;
                         visit(kst + static_cast<size_t>(jj) * kHeadDim, vst + static_cast<size_t>(jj) * kHeadDim, j < n);
                     }
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&empty[slot]);
+                    if (lane == 0) mbar_arrive(&myempty[slot]);
                 }
                 if (new_split && warp == 0) visit(knew, vnew, pg == 0);
-                // Merge the two position groups of the warp (lanes l and l^16).
+                // Merge the two position groups of the warp (lanes l and l ^ 16).
                 {
                     const float m2 = __shfl_xor_sync(0xffffffffu, mx, 16);
                     const float l2 = __shfl_xor_sync(0xffffffffu, l, 16);
@@ -864,10 +1002,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
 #pragma unroll
                     for (int j = 0; j < 4; ++j) *reinterpret_cast<float4*>(w + 4 + 4 * (qr + 8 * j)) = acc[j];
                 }
-                consumers_sync();
-                // CTA partial per query (256 threads = 2 queries x 128 dims).
+                mega_sync();
+                // This CTA's partial per query: 2 queries x 128 dims.
+                for (int e = tid; e < 2 * kHeadDim; e += kMegaConsumers)
                 {
-                    const int q = tid >> 7, d = tid & 127;
+                    const int q = e >> 7, d = e & 127;
                     float M = -INFINITY;
 #pragma unroll
                     for (int w = 0; w < kMegaWarps; ++w) M = fmaxf(M, ascr[(w * 2 + q) * kPartStride]);
@@ -895,9 +1034,20 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                 // The o-projection phase merges the partials of all splits.
             }
 
+            gs += p.nstage;
+            if (wtr)
+            {
+                tr[4] = wwait;
+                tr[5] = wwork;
+                tr[6] = wn;
+            }
             // ---------------- phase done: arrive on the grid barrier ----------------
-            consumers_sync();
-            if (redi[0]) return;
+            mega_sync();
+            if (redi[0])
+            {
+                bad = true;
+                break;
+            }
             if (tracing) tr[3] = global_ns();
             if (tid == 0)
             {
