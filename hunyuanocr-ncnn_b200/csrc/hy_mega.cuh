@@ -105,7 +105,8 @@ struct MegaSmem {
     static constexpr int QS = XS;                                           // [2][128]
     static constexpr int NEWKV = QS + 2 * kHeadDim * 4;                     // k[128], v[128]
     static constexpr int ASCR = NEWKV + 2 * kHeadDim * 4;                   // [warps][2][kPartStride]
-    static_assert(ASCR + kMegaWarps * 2 * kPartStride * 4 <= XS + kMegaMaxK * 4, "attention scratch must fit");
+    static constexpr int PBUF = ASCR + kMegaWarps * 2 * kPartStride * 4;    // [warps][32] softmax weights
+    static_assert(PBUF + kMegaWarps * 32 * 4 <= XS + kMegaMaxK * 4, "attention scratch must fit");
     static constexpr int RED = XS + kMegaMaxK * 4;                          // 64 float4 + 64 ints
     static constexpr int BARS = RED + 64 * 16 + 64 * 4;                     // full[warp][slot], empty[warp][slot]
     static constexpr int SIZE = BARS + 2 * kMegaWarps * kMegaSlots * 8;
@@ -472,6 +473,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
     float* knew = reinterpret_cast<float*>(smem + MegaSmem::NEWKV);
     float* vnew = knew + kHeadDim;
     float* ascr = reinterpret_cast<float*>(smem + MegaSmem::ASCR);
+    float* pbuf_all = reinterpret_cast<float*>(smem + MegaSmem::PBUF);
     float4* red4 = reinterpret_cast<float4*>(smem + MegaSmem::RED);
     int* redi = reinterpret_cast<int*>(red4 + 64);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + MegaSmem::BARS);   // [warp][slot]
@@ -912,39 +914,77 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                 }
                 mega_sync();
 
-                // lane = (pg: 2, qq: 2, qr: 8): position group, query, dim
-                // group; a lane owns dims 4 * (qr + 8 j) + e of query qq, j < 4.
-                const int qr = lane & 7, qq = (lane >> 3) & 1, pg = lane >> 4;
-                float4 q4[4];
+                // Lane l owns dims 4l..4l+3 of both queries (o0, o1); the
+                // running max / sum of each query (m0, l0, m1, l1) are kept
+                // in every lane. Scores are in log2 units (q carries scale * log2 e).
+                const float4 qv0 = reinterpret_cast<const float4*>(qs)[lane];
+                const float4 qv1 = reinterpret_cast<const float4*>(qs + kHeadDim)[lane];
+                float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+                float4 o0 = make_float4(0.f, 0.f, 0.f, 0.f), o1 = o0;
+                float* pbuf = pbuf_all + warp * 32;
+                // Rescale the running state to new maxima mn0 / mn1.
+                auto rescale = [&](float mn0, float mn1) {
+                    const float c0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - mn0);
+                    const float c1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - mn1);
+                    l0 *= c0;
+                    l1 *= c1;
+                    o0.x *= c0; o0.y *= c0; o0.z *= c0; o0.w *= c0;
+                    o1.x *= c1; o1.y *= c1; o1.z *= c1; o1.w *= c1;
+                    m0 = mn0;
+                    m1 = mn1;
+                };
+                // 16 cached positions starting at row `base` of the stage, nv of them valid.
+                auto block16 = [&](const KT* kst, const KT* vst, int nv) {
+                    float v[32];   // v[q * 16 + j]: partial score of query q, position j
 #pragma unroll
-                for (int j = 0; j < 4; ++j) q4[j] = *reinterpret_cast<const float4*>(qs + qq * kHeadDim + 4 * (qr + 8 * j));
-                float mx = -INFINITY, l = 0.f;
-                float4 acc[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-                // Online softmax over one position (scores in log2 units).
-                auto visit = [&](const auto* krow, const auto* vrow, bool visible) {
-                    float sc = 0.f;
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) sc += dot4(q4[j], load4(krow + 4 * (qr + 8 * j)));
-                    sc += __shfl_xor_sync(0xffffffffu, sc, 1);
-                    sc += __shfl_xor_sync(0xffffffffu, sc, 2);
-                    sc += __shfl_xor_sync(0xffffffffu, sc, 4);
-                    if (!visible) return;
-                    const float mn = fmaxf(mx, sc);
-                    const float corr = exp2f(mx - mn);
-                    const float pe = exp2f(sc - mn);
-                    l = l * corr + pe;
-#pragma unroll
-                    for (int j = 0; j < 4; ++j)
+                    for (int j = 0; j < 16; ++j)
                     {
-                        const float4 vv = load4(vrow + 4 * (qr + 8 * j));
-                        acc[j].x = acc[j].x * corr + pe * vv.x;
-                        acc[j].y = acc[j].y * corr + pe * vv.y;
-                        acc[j].z = acc[j].z * corr + pe * vv.z;
-                        acc[j].w = acc[j].w * corr + pe * vv.w;
+                        const float4 k = load4(kst + static_cast<size_t>(j) * kHeadDim + 4 * lane);
+                        v[j] = dot4(qv0, k);
+                        v[16 + j] = dot4(qv1, k);
                     }
-                    mx = mn;
+                    // Lane l: full score of query l >> 4, position l & 15.
+                    float sc = reduce_rows<32>(v, lane);
+                    const bool valid = (lane & 15) < nv;
+                    sc = valid ? sc : -INFINITY;
+                    float mx = sc;
+#pragma unroll
+                    for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                    const float mn0 = fmaxf(m0, __shfl_sync(0xffffffffu, mx, 0));
+                    const float mn1 = fmaxf(m1, __shfl_sync(0xffffffffu, mx, 16));
+                    const float pe = valid ? exp2f(sc - ((lane < 16) ? mn0 : mn1)) : 0.f;
+                    float ps = pe;
+#pragma unroll
+                    for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+                    rescale(mn0, mn1);
+                    l0 += __shfl_sync(0xffffffffu, ps, 0);
+                    l1 += __shfl_sync(0xffffffffu, ps, 16);
+                    pbuf[lane] = pe;
+                    __syncwarp();
+                    auto accum = [&](int j, float p0, float p1) {
+                        const float4 vv = load4(vst + static_cast<size_t>(j) * kHeadDim + 4 * lane);
+                        o0.x += p0 * vv.x; o0.y += p0 * vv.y; o0.z += p0 * vv.z; o0.w += p0 * vv.w;
+                        o1.x += p1 * vv.x; o1.y += p1 * vv.y; o1.z += p1 * vv.z; o1.w += p1 * vv.w;
+                    };
+                    if (nv == 16)
+                    {
+#pragma unroll
+                        for (int j4 = 0; j4 < 4; ++j4)
+                        {
+                            const float4 P0 = reinterpret_cast<const float4*>(pbuf)[j4];
+                            const float4 P1 = reinterpret_cast<const float4*>(pbuf + 16)[j4];
+                            accum(4 * j4 + 0, P0.x, P1.x);
+                            accum(4 * j4 + 1, P0.y, P1.y);
+                            accum(4 * j4 + 2, P0.z, P1.z);
+                            accum(4 * j4 + 3, P0.w, P1.w);
+                        }
+                    }
+                    else
+                    {
+                        // Warp-uniform bound: rows past nv hold stale data and are never read.
+                        for (int j = 0; j < nv; ++j) accum(j, pbuf[j], pbuf[16 + j]);
+                    }
+                    __syncwarp();
                 };
                 for (int i = first; i < p.nstage && !bad; i += kMegaWarps)
                 {
@@ -958,49 +998,43 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                     const KT* kst = reinterpret_cast<const KT*>(myring + slot * kMegaStage);
                     const KT* vst = kst + static_cast<size_t>(p.per_stage) * kHeadDim;
                     const int n = min(p.per_stage, p.count - i * p.per_stage);
-                    for (int jb = 0; jb < n; jb += 2)
-                    {
-                        const int j = jb + pg;
-                        const int jj = (j < n) ? j : 0;
-                        visit(kst + static_cast<size_t>(jj) * kHeadDim, vst + static_cast<size_t>(jj) * kHeadDim, j < n);
-                    }
+                    for (int h = 0; h < n; h += 16)
+                        block16(kst + static_cast<size_t>(h) * kHeadDim, vst + static_cast<size_t>(h) * kHeadDim,
+                                min(16, n - h));
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&myempty[slot]);
                 }
-                if (new_split && warp == 0) visit(knew, vnew, pg == 0);
-                // Merge the two position groups of the warp (lanes l and l ^ 16).
+                if (new_split && warp == 0)
                 {
-                    const float m2 = __shfl_xor_sync(0xffffffffu, mx, 16);
-                    const float l2 = __shfl_xor_sync(0xffffffffu, l, 16);
-                    const float M = fmaxf(mx, m2);
-                    const float f1 = (mx == -INFINITY) ? 0.f : exp2f(mx - M);
-                    const float f2 = (m2 == -INFINITY) ? 0.f : exp2f(m2 - M);
-                    l = l * f1 + l2 * f2;
+                    // The new row (already rounded to the cache type).
+                    const float4 k = reinterpret_cast<const float4*>(knew)[lane];
+                    const float4 vv = reinterpret_cast<const float4*>(vnew)[lane];
+                    float s0 = dot4(qv0, k), s1 = dot4(qv1, k);
 #pragma unroll
-                    for (int j = 0; j < 4; ++j)
+                    for (int o = 16; o > 0; o >>= 1)
                     {
-                        float4 o2;
-                        o2.x = __shfl_xor_sync(0xffffffffu, acc[j].x, 16);
-                        o2.y = __shfl_xor_sync(0xffffffffu, acc[j].y, 16);
-                        o2.z = __shfl_xor_sync(0xffffffffu, acc[j].z, 16);
-                        o2.w = __shfl_xor_sync(0xffffffffu, acc[j].w, 16);
-                        acc[j].x = acc[j].x * f1 + o2.x * f2;
-                        acc[j].y = acc[j].y * f1 + o2.y * f2;
-                        acc[j].z = acc[j].z * f1 + o2.z * f2;
-                        acc[j].w = acc[j].w * f1 + o2.w * f2;
+                        s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+                        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
                     }
-                    mx = M;
+                    rescale(fmaxf(m0, s0), fmaxf(m1, s1));
+                    const float p0 = exp2f(s0 - m0), p1 = exp2f(s1 - m1);
+                    l0 += p0;
+                    l1 += p1;
+                    o0.x += p0 * vv.x; o0.y += p0 * vv.y; o0.z += p0 * vv.z; o0.w += p0 * vv.w;
+                    o1.x += p1 * vv.x; o1.y += p1 * vv.y; o1.z += p1 * vv.z; o1.w += p1 * vv.w;
                 }
-                if (pg == 0)
                 {
-                    float* w = ascr + (warp * 2 + qq) * kPartStride;
-                    if (qr == 0)
+                    float* w0 = ascr + (warp * 2 + 0) * kPartStride;
+                    float* w1 = ascr + (warp * 2 + 1) * kPartStride;
+                    if (lane == 0)
                     {
-                        w[0] = mx;
-                        w[1] = l;
+                        w0[0] = m0;
+                        w0[1] = l0;
+                        w1[0] = m1;
+                        w1[1] = l1;
                     }
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) *reinterpret_cast<float4*>(w + 4 + 4 * (qr + 8 * j)) = acc[j];
+                    reinterpret_cast<float4*>(w0 + 4)[lane] = o0;
+                    reinterpret_cast<float4*>(w1 + 4)[lane] = o1;
                 }
                 mega_sync();
                 // This CTA's partial per query: 2 queries x 128 dims.
