@@ -46,6 +46,7 @@ EXPORTED_SYMBOLS = (
     "hy_dflash_generate_synthetic", "hy_run_vlm_decode_with_prompt", "hy_attention", "hy_kv_write",
     "hy_kv_read", "hy_seq_set_length", "hy_bench_ar_steps", "hy_bench_kernel", "hy_ctx_stream",
     "hy_ctx_set_ar_path", "hy_ctx_ar_path", "hy_trace_persistent", "hy_debug_progress",
+    "hy_lm_head_select_noalloc",
 )
 AR_PATH_PERSISTENT = 0
 AR_PATH_GRAPH = 1
@@ -114,6 +115,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "hy_prefill": ([_P, _P, _P, _P, _I, _P, _P], _I),
         "hy_decoder_step": ([_P, _P, _I, _P, _P, _P, _P], _I),
         "hy_lm_head_select": ([_P, _P, _I, _P, _F, _P, _P, _P], _I),
+        "hy_lm_head_select_noalloc": ([_P, _P, _I, _F, _P, _P], _I),
         "hy_generate": ([_P, _I, _I, _I, _F, _P, _I, _P, _P, ctypes.POINTER(_I)], _I),
         "hy_verify_block": ([_P, _P, _I, _F, _P, _I, _P, ctypes.POINTER(_I), ctypes.POINTER(_I),
                              ctypes.POINTER(_I)], _I),
@@ -331,6 +333,13 @@ class TextRuntime:
         _check(_LIB.hy_lm_head_select(self._ctx, _ptr(h), rows, _ptr(pre), penalty, _ptr(tok), _ptr(raw),
                                       _ptr(logits)))
         return tok, raw, logits
+
+    def select_logit_rows_noalloc(self, hidden_dev: int, rows: int, penalty: float, tokens_dev: int,
+                                  raw_top1_dev: int) -> None:
+        """select_logit_rows on device pointers (ints), allocating nothing: the
+        argmax scratch is a static device-global array (no reference counterpart)."""
+        _check(_LIB.hy_lm_head_select_noalloc(self._ctx, ctypes.c_void_p(hidden_dev), rows, penalty,
+                                              ctypes.c_void_p(tokens_dev), ctypes.c_void_p(raw_top1_dev)))
 
     def attention(self, layer: int, qkv: np.ndarray, cos: np.ndarray, sin: np.ndarray) -> np.ndarray:
         q, c, s = _f32(qkv), _f32(cos), _f32(sin)

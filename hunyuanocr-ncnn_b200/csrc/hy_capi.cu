@@ -968,6 +968,67 @@ int set_length(hy_ctx* c, int rows)
     return HY_OK;
 }
 
+// ---------------------------------------------------------------------------
+// LM-head select with device-global scratch, allocating nothing.
+//
+// For callers that cannot allocate device memory while they decode: a host
+// runtime that reserves the device's memory up front for its own caching
+// allocator (a cudaMalloc then fails or fragments that pool), or one that must
+// not take the implicit device-wide synchronisation of cudaMalloc/cudaFree in
+// the middle of a decode loop that shares the GPU with other streams. Inputs
+// and outputs are device pointers; the argmax kernel's per-CTA partials and
+// its completion ticket live in the file-scope array below instead of in
+// context-owned buffers. The array is one per device and process, so calls
+// that overlap in time on the same device (any context, stream or thread)
+// race on it.
+// ---------------------------------------------------------------------------
+constexpr int kSelectScratchCtas = 256;      // partial slots per row (one launch: one CTA per SM)
+constexpr size_t kSelectTicketBytes = 256;   // the completion ticket (one int), padded
+constexpr size_t kSelectScratchBytes = kSelectTicketBytes + sizeof(float4) * kSelectScratchCtas * kMaxStepRows;  // 65,792 B
+static __device__ __align__(256) unsigned char g_select_scratch[kSelectScratchBytes];
+
+// Device address of g_select_scratch, resolved once per device with that device current.
+int select_scratch_address(int device, unsigned char** out)
+{
+    static std::mutex m;
+    static unsigned char* addr[64] = {};
+    if (device < 0 || device >= 64) return fail(HY_ERR_INVALID_ARGUMENT, "device index out of range");
+    std::lock_guard<std::mutex> lock(m);
+    if (!addr[device])
+    {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_select_scratch);
+        if (e != cudaSuccess)
+            return fail(HY_ERR_CUDA, std::string("cudaGetSymbolAddress(select scratch): ") + cudaGetErrorString(e));
+        addr[device] = static_cast<unsigned char*>(p);
+    }
+    *out = addr[device];
+    return HY_OK;
+}
+
+template <typename WT, int MT>
+cudaError_t enqueue_lm_select_scratch_t(hy_ctx* c, int rows, const float* x, float penalty, unsigned char* scratch,
+                                        int* tokens, int* raw_top1)
+{
+    GemvArgs lm = base_args(c);
+    lm.part = reinterpret_cast<float4*>(scratch + kSelectTicketBytes);
+    lm.counter = reinterpret_cast<int*>(scratch);
+    lm.W = c->embed;
+    lm.N = c->cfg.vocab_size;
+    lm.ldw = kHidden;
+    lm.rows = rows;
+    lm.src = SRC_X;
+    lm.x = x;
+    lm.ldx = kHidden;
+    lm.lm_mode = LM_NONE;
+    lm.penalty = penalty;
+    lm.prefix = nullptr;
+    lm.logits = nullptr;
+    lm.tok_out = tokens;
+    lm.raw_out = raw_top1;
+    return run_gemv<WT, kHidden, MT, PRO_PLAIN, EPI_ARGMAX>(c, lm);
+}
+
 }  // namespace
 
 // ===========================================================================
@@ -1258,6 +1319,39 @@ int hy_lm_head_select(hy_ctx* c, const float* hidden, int rows, const int* row_p
     if (logits)
         HY_CUDA(cudaMemcpyAsync(logits, c->logits, sizeof(float) * rows * c->cfg.vocab_size, cudaMemcpyDeviceToHost,
                                 c->stream));
+    return check_device_error(c);
+}
+
+int hy_lm_head_select_noalloc(hy_ctx* c, const float* hidden_dev, int rows, float penalty, int* tokens_dev,
+                              int* raw_top1_dev)
+{
+    if (!c || !hidden_dev || !tokens_dev || !raw_top1_dev) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    if (rows < 1 || rows > kMaxStepRows)
+        return fail(HY_ERR_CAPACITY, "rows must be in 1..16 (the static select scratch holds partials for 16 rows)");
+    if (c->num_sms > kSelectScratchCtas)
+        return fail(HY_ERR_CAPACITY, "the static select scratch holds partials for at most " +
+                                         std::to_string(kSelectScratchCtas) + " CTAs; this device launches " +
+                                         std::to_string(c->num_sms));
+    if (reinterpret_cast<uintptr_t>(hidden_dev) % 16 != 0)
+        return fail(HY_ERR_INVALID_ARGUMENT, "hidden_dev must be 16-byte aligned");
+    if (!std::isfinite(penalty) || penalty <= 0.f) return fail(HY_ERR_INVALID_ARGUMENT, "repetition_penalty must be positive");
+    int rc = set_device(c);
+    if (rc) return rc;
+    unsigned char* scratch = nullptr;
+    if ((rc = select_scratch_address(c->cfg.device, &scratch))) return rc;
+    // The ticket must be zero when the launch starts (its last CTA re-zeroes
+    // it; clearing it here also recovers from an aborted launch). The partials
+    // need no clearing: every CTA writes its own slots before taking a ticket.
+    HY_CUDA(cudaMemsetAsync(scratch, 0, sizeof(int), c->stream));
+    t_next_plain = true;
+    cudaError_t e;
+    if (c->cfg.weight_dtype == HY_DTYPE_BF16)
+        e = rows == 1 ? enqueue_lm_select_scratch_t<__nv_bfloat16, 1>(c, rows, hidden_dev, penalty, scratch, tokens_dev, raw_top1_dev)
+                      : enqueue_lm_select_scratch_t<__nv_bfloat16, 16>(c, rows, hidden_dev, penalty, scratch, tokens_dev, raw_top1_dev);
+    else
+        e = rows == 1 ? enqueue_lm_select_scratch_t<float, 1>(c, rows, hidden_dev, penalty, scratch, tokens_dev, raw_top1_dev)
+                      : enqueue_lm_select_scratch_t<float, 16>(c, rows, hidden_dev, penalty, scratch, tokens_dev, raw_top1_dev);
+    if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("LM head launch: ") + cudaGetErrorString(e));
     return check_device_error(c);
 }
 

@@ -178,6 +178,21 @@ int hy_decoder_step(hy_ctx* ctx, const float* embeds, int rows, const float* cos
 int hy_lm_head_select(hy_ctx* ctx, const float* hidden, int rows, const int* row_prefix, float penalty,
                       int* tokens, int* raw_top1, float* logits);
 
+/* No reference counterpart. hy_lm_head_select on DEVICE buffers that
+ * allocates nothing: hidden_dev [rows x 1024] final-normed rows (16-byte
+ * aligned), tokens_dev / raw_top1_dev [rows] written on the device, history
+ * from the context, no row prefix, no logits. For callers that cannot
+ * allocate device memory mid-decode (their memory is reserved by their own
+ * caching allocator, or a cudaMalloc/cudaFree would synchronise a GPU shared
+ * with other streams). The argmax kernel's scratch is a static device-global
+ * array of 65,792 bytes (partials for at most 16 rows x 256 CTAs), one per
+ * device and process: rows > 16 or a device launching more than 256 CTAs is
+ * rejected with HY_ERR_CAPACITY, and calls that overlap in time on one device
+ * race on the scratch. The first call on each device resolves the array's
+ * address (cudaGetSymbolAddress), so make one call before any stream capture. */
+int hy_lm_head_select_noalloc(hy_ctx* ctx, const float* hidden_dev, int rows, float penalty, int* tokens_dev,
+                              int* raw_top1_dev);
+
 /* ---- on-device loops -------------------------------------------------- */
 /* The AR loop of decode_from_embeddings (src/text_runtime.cpp:1417-1508):
  * starting from first_token (already selected from the prefill logits and
