@@ -14,7 +14,6 @@
 
 #include <algorithm>
 #include <cmath>
-#include <cstdlib>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -113,6 +112,13 @@ struct hy_ctx {
     // Persistent AR decode kernel (cooperative, one CTA per SM).
     const void** wptrs = nullptr;  // device arrays: wqkv[L], wo[L], wgu[L], wd[L]
     unsigned* bar = nullptr;       // grid barrier counter
+    // Persistent kernel: activations exchanged between CTAs as 64-bit words
+    // (value | epoch << 32), and the launch counter that makes epochs unique.
+    unsigned long long* x_ep = nullptr;    // [1024]
+    unsigned long long* qkv_ep = nullptr;  // [4096]
+    unsigned long long* act_ep = nullptr;  // [ffn]
+    unsigned long long* tok_ep = nullptr;  // [1]
+    unsigned mega_seq = 0;
     int* dbg = nullptr;            // persistent-kernel self-check record [4]
     unsigned* progress = nullptr;  // host-mapped per-CTA phase progress (HY_DEBUG_PROGRESS=1)
     int ar_path = HY_AR_PATH_PERSISTENT;
@@ -545,6 +551,24 @@ cudaError_t launch_mega_t(hy_ctx* c, int steps)
         cudaHostGetDevicePointer(reinterpret_cast<void**>(&dp), c->progress, 0);
         a.progress = dp;
     }
+    // Epochs of this launch: epoch_base + 1 .. epoch_base + steps * phases (< kMegaEpochSpan).
+    // Epoch 0 never occurs, so zeroed words are never taken for data; on wrap-around
+    // the words are cleared again.
+    if (c->mega_seq == 0 || c->mega_seq >= 0xFFFFFFFFu / kMegaEpochSpan)
+    {
+        c->mega_seq = 0;
+        cudaError_t z = cudaMemsetAsync(c->x_ep, 0, sizeof(unsigned long long) * kHidden, c->stream);
+        if (z == cudaSuccess) z = cudaMemsetAsync(c->qkv_ep, 0, sizeof(unsigned long long) * kQKVRows, c->stream);
+        if (z == cudaSuccess) z = cudaMemsetAsync(c->act_ep, 0, sizeof(unsigned long long) * c->cfg.ffn_dim, c->stream);
+        if (z == cudaSuccess) z = cudaMemsetAsync(c->tok_ep, 0, sizeof(unsigned long long), c->stream);
+        if (z != cudaSuccess) return z;
+    }
+    ++c->mega_seq;
+    a.x_ep = c->x_ep;
+    a.qkv_ep = c->qkv_ep;
+    a.act_ep = c->act_ep;
+    a.tok_ep = c->tok_ep;
+    a.epoch_base = c->mega_seq * kMegaEpochSpan;
     cudaError_t e = cudaMemsetAsync(c->bar, 0, sizeof(unsigned), c->stream);
     if (e != cudaSuccess) return e;
     void* params[] = {&a};
@@ -739,6 +763,10 @@ int alloc_ctx(hy_ctx* c)
     if ((rc = dalloc(c, &c->err, 1))) return rc;
     if ((rc = dalloc(c, &c->bar, 1))) return rc;
     if ((rc = dalloc(c, &c->dbg, 4))) return rc;
+    if ((rc = dalloc(c, &c->x_ep, kHidden))) return rc;
+    if ((rc = dalloc(c, &c->qkv_ep, kQKVRows))) return rc;
+    if ((rc = dalloc(c, &c->act_ep, cfg.ffn_dim))) return rc;
+    if ((rc = dalloc(c, &c->tok_ep, 1))) return rc;
     HY_CUDA(cudaMemsetAsync(c->dbg, 0, 4 * sizeof(int), c->stream));
     if (const char* e = std::getenv("HY_DEBUG_PROGRESS"); e && e[0] == '1')
     {

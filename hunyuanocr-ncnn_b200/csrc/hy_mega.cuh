@@ -53,6 +53,7 @@ constexpr int kMegaMaxK = 3584;
 constexpr int kMegaHistWords = 64;       // LM rows per CTA <= 32 * 62
 constexpr int kMegaResRows = 32;         // o/down rows per CTA (1024 / gridDim.x)
 constexpr int kMegaMaxLayers = 64;
+constexpr unsigned kMegaEpochSpan = 32768;   // epochs per launch (>= 64 tokens x 321 phases)
 
 struct MegaArgs {
     const void* embed;
@@ -93,6 +94,15 @@ struct MegaArgs {
     // thread 0 of each CTA stores the number of phases it completed.
     int* dbg;
     volatile unsigned* progress;
+    // Activations passed between CTAs as 64-bit words: float bits | epoch << 32,
+    // written and read with single-copy-atomic 64-bit accesses, so a reader that
+    // sees the phase's epoch sees that phase's value (no barrier, no fence).
+    // Epoch of phase ph of token t: epoch_base + t * phases + ph + 1.
+    unsigned long long* x_ep;    // residual stream [1024] (o / down outputs)
+    unsigned long long* qkv_ep;  // q/k/v projections [4096]
+    unsigned long long* act_ep;  // silu(gate) * up [ffn]
+    unsigned long long* tok_ep;  // committed token (int bits) [1], written with release
+    unsigned epoch_base;
 };
 
 constexpr int kTraceCtas = 4;
@@ -109,7 +119,8 @@ struct MegaSmem {
     static_assert(PBUF + kMegaWarps * 32 * 4 <= XS + kMegaMaxK * 4, "attention scratch must fit");
     static constexpr int RED = XS + kMegaMaxK * 4;                          // 64 float4 + 64 ints
     static constexpr int BARS = RED + 64 * 16 + 64 * 4;                     // full[warp][slot], empty[warp][slot]
-    static constexpr int SIZE = BARS + 2 * kMegaWarps * kMegaSlots * 8;
+    static constexpr int TOKBAR = BARS + 2 * kMegaWarps * kMegaSlots * 8;  // token-start mbarrier
+    static constexpr int SIZE = TOKBAR + 8;
 };
 
 enum { PH_QKV = 0, PH_ATTN = 1, PH_O = 2, PH_GU = 3, PH_DOWN = 4, PH_LM = 5 };
@@ -275,6 +286,82 @@ __device__ __forceinline__ void grid_arrive(unsigned* bar)
     asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
 }
 
+// ---- epoch words ----
+__device__ __forceinline__ unsigned long long ep_word(float v, unsigned e)
+{
+    return (static_cast<unsigned long long>(e) << 32) | __float_as_uint(v);
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p)
+{
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p)
+{
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v)
+{
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void st_release_u64(unsigned long long* p, unsigned long long v)
+{
+    asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Poll the words src[first + stride * u] (u < PER, index < n) until each
+// carries epoch e, and return their values in out[u] (0 past n). Every round
+// has all of the thread's outstanding loads in flight at once. Returns false
+// (and sets the timeout bit) when the wall-clock limit passes first.
+template <int PER>
+__device__ __forceinline__ bool poll_words(const unsigned long long* src, int n, int first, int stride, unsigned e,
+                                           float (&out)[PER], int* err)
+{
+    const unsigned long long done = static_cast<unsigned long long>(e) << 32;   // value 0, epoch e
+    unsigned long long w[PER];
+#pragma unroll
+    for (int u = 0; u < PER; ++u)
+    {
+        const int i = first + stride * u;
+        w[u] = (i < n) ? ld_relaxed_u64(src + i) : done;
+    }
+    unsigned long long t0 = 0;
+    bool ok = true;
+    while (true)
+    {
+        bool all = true;
+#pragma unroll
+        for (int u = 0; u < PER; ++u) all &= static_cast<unsigned>(w[u] >> 32) == e;
+        if (all) break;
+        const unsigned long long now = global_ns();
+        if (t0 == 0) t0 = now;
+        else if (now - t0 > kWaitLimitNs)
+        {
+            atomicOr(err, kErrTimeoutFull);
+            ok = false;
+            break;
+        }
+        __nanosleep(32);
+#pragma unroll
+        for (int u = 0; u < PER; ++u)
+            if (static_cast<unsigned>(w[u] >> 32) != e) w[u] = ld_relaxed_u64(src + first + stride * u);
+    }
+#pragma unroll
+    for (int u = 0; u < PER; ++u) out[u] = __uint_as_float(static_cast<unsigned>(w[u]));
+    return ok;
+}
+
+// Where a GEMV phase's epilogue publishes its outputs, and with which epoch.
+struct EpOut {
+    unsigned long long* qkv;
+    unsigned long long* act;
+    unsigned long long* x;
+    unsigned e;
+};
+
 // Rows per stage of a K-element row of WT (at most 8; even for K = 1024, so a
 // gate/up pair never straddles two stages).
 template <typename WT, int K>
@@ -408,6 +495,50 @@ __device__ __forceinline__ float mega_load_normed(float* xs, const float4 v[2], 
     return 1.0f / sqrtf(t / static_cast<float>(kHidden) + eps);
 }
 
+// xs = w * x for a 1024-vector x given as x[tid + 192 u] in v[u] (u < 6);
+// returns 1/sqrt(mean(x^2)+eps) after one consumer barrier (the GEMV applies
+// the RMSNorm's per-row scale to its dot products).
+constexpr int kXPer = (kHidden + kMegaConsumers - 1) / kMegaConsumers;   // 6
+
+__device__ __forceinline__ float mega_load_normed_s(float* xs, const float (&v)[kXPer], const float* w, float eps,
+                                                    float* s_norm, int tid)
+{
+    float ss = 0.f;
+#pragma unroll
+    for (int u = 0; u < kXPer; ++u)
+    {
+        const int i = tid + kMegaConsumers * u;
+        if (i < kHidden)
+        {
+            ss += v[u] * v[u];
+            xs[i] = w[i] * v[u];
+        }
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) s_norm[tid >> 5] = ss;
+    mega_sync();
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMegaWarps; ++i) t += s_norm[i];
+    return 1.0f / sqrtf(t / static_cast<float>(kHidden) + eps);
+}
+
+// RoPE + RMSNorm of one 128-vector given as x[lane + 32 j] in x[j] (as rope_norm_vec).
+__device__ __forceinline__ void rope_norm_vals(const float (&x)[4], const float* c, const float* s, const float* w,
+                                               float eps, int lane, float out[4])
+{
+    float y0 = x[0] * c[lane] - x[2] * s[lane];
+    float y1 = x[1] * c[lane + 32] - x[3] * s[lane + 32];
+    float y2 = x[2] * c[lane + 64] + x[0] * s[lane + 64];
+    float y3 = x[3] * c[lane + 96] + x[1] * s[lane + 96];
+    const float ss = warp_sum(y0 * y0 + y1 * y1 + y2 * y2 + y3 * y3);
+    const float ri = 1.0f / sqrtf(ss / static_cast<float>(kHeadDim) + eps);
+    out[0] = w[lane] * (y0 * ri);
+    out[1] = w[lane + 32] * (y1 * ri);
+    out[2] = w[lane + 64] * (y2 * ri);
+    out[3] = w[lane + 96] * (y3 * ri);
+}
+
 // One GEMV stage of a consumer warp: dot products of the stage's rows, slot
 // release, and the epilogue run by one lane per row.
 struct LmBest {
@@ -417,8 +548,8 @@ struct LmBest {
 
 template <typename WT, int K, bool XREG>
 __device__ __forceinline__ void gemv_stage(const MegaArgs& a, const MegaPlan& p, int kind, const WT* rows,
-                                           const float4 (&xr)[8], const float* xs, int q0, float rinv, float* xg,
-                                           const float* xres_s, const unsigned* hist_s, float pen, LmBest& best,
+                                           const float4 (&xr)[8], const float* xs, int q0, float rinv, const EpOut& eo,
+                                           float* xres_s, const unsigned* hist_s, float pen, LmBest& best,
                                            uint64_t* empty_bar, int lane, int b, int ph)
 {
     constexpr int R = StageRows<WT, K>::v;
@@ -438,17 +569,23 @@ __device__ __forceinline__ void gemv_stage(const MegaArgs& a, const MegaPlan& p,
     const bool lead = ok && (lane % LPR) == 0 && r < n;
     if (kind == PH_QKV)
     {
-        if (lead) a.qkv[row] = val;
+        if (lead) st_relaxed_u64(eo.qkv + row, ep_word(val, eo.e));
     }
     else if (kind == PH_GU)
     {
         // act = silu(gate) * up; gate = even row, up = the next row's lanes.
         const float up = __shfl_down_sync(0xffffffffu, val, LPR);
-        if (lead && !(r & 1)) a.gu[row >> 1] = (val / (1.0f + expf(-val))) * up;
+        if (lead && !(r & 1)) st_relaxed_u64(eo.act + (row >> 1), ep_word((val / (1.0f + expf(-val))) * up, eo.e));
     }
     else if (kind == PH_O || kind == PH_DOWN)
     {
-        if (lead) xg[row] = xres_s[q0 + r] + val;
+        // The residual rows this CTA owns stay in shared memory across phases.
+        if (lead)
+        {
+            const float xn = xres_s[q0 + r] + val;
+            xres_s[q0 + r] = xn;
+            st_relaxed_u64(eo.x + row, ep_word(xn, eo.e));
+        }
     }
     else if (lead)
     {
@@ -478,6 +615,10 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
     int* redi = reinterpret_cast<int*>(red4 + 64);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + MegaSmem::BARS);   // [warp][slot]
     uint64_t* empty = full + kMegaWarps * kMegaSlots;                      // [warp][slot]
+    // Completes once per token t >= 1 when the consumers have acquired the
+    // previous token's commit; the producer waits on it before streaming the
+    // token's K/V rows, whose newest row the previous token wrote.
+    uint64_t* tokbar = reinterpret_cast<uint64_t*>(smem + MegaSmem::TOKBAR);
     __shared__ unsigned hist_s[kMegaHistWords];
     __shared__ float xres_s[kMegaResRows];
     __shared__ float s_norm[kMegaWarps];
@@ -496,6 +637,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
+        mbar_init(tokbar, 1);
         fence_mbar_init();
         redi[0] = 0;  // abort flag
     }
@@ -516,6 +658,12 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                 int layer, kind;
                 mega_phase_of(ph, L, layer, kind);
                 const MegaPlan p = mega_plan<KT>(a, tb, layer, kind, kv0 + t, b);
+                if (kind == PH_ATTN && layer == 0 && t > 0 && p.nstage > 0 &&
+                    !mbar_wait(tokbar, (t - 1) & 1, a.err, kErrTimeoutEmpty))
+                {
+                    ok = false;
+                    break;
+                }
                 for (int i = 0; i < p.nstage; ++i, ++g)
                 {
                     const int w = g % kMegaWarps;
@@ -574,72 +722,82 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
     };
 
     unsigned gs = 0;          // global stage index of the current phase's first stage
-    unsigned phase_no = 0;
-    float* xg = a.x;
+    const MegaPlan po = mega_plan<KT>(a, tb, 0, PH_O, kv0, b);   // this CTA's residual rows (o and down)
     // A failed wait marks the warp bad and raises the CTA's abort flag; every
     // warp still takes the phase's CTA barriers, and the CTA leaves together.
     bool bad = false;
     for (int t = 0; t < a.steps && !bad; ++t)
     {
         const int past = kv0 + t;
-        for (int ph = 0; ph < phases; ++ph, ++phase_no)
+        for (int ph = 0; ph < phases; ++ph)
         {
             int layer, kind;
             mega_phase_of(ph, L, layer, kind);
+            // Epoch of the previous phase's outputs (for ph = 0: the previous token's commit).
+            const unsigned e_in = a.epoch_base + static_cast<unsigned>(t * phases + ph);
+            const EpOut eo{a.qkv_ep, a.act_ep, a.x_ep, e_in + 1};
             const bool tracing = a.trace && t == a.trace_token && b < kTraceCtas && tid == 0;
             unsigned long long* tr = tracing ? a.trace + (static_cast<size_t>(b) * phases + ph) * kTraceSlots : nullptr;
             if (tracing) tr[0] = global_ns();
             // Warp-0 trace: SM cycles waiting on slots / working, stages.
             const bool wtr = a.trace && t == a.trace_token && b < kTraceCtas && tid == 0;
             long long wwait = 0, wwork = 0, wn = 0;
-            if (phase_no > 0)
-            {
-                if (tid == 0 && !grid_wait(a.bar, phase_no * G, a.err)) redi[0] = 1;
-                mega_sync();
-                if (redi[0])
-                {
-                    bad = true;
-                    break;
-                }
-            }
-            if (tracing) tr[1] = global_ns();
             const MegaPlan p = mega_plan<KT>(a, tb, layer, kind, past, b);
             const float* lnorm = a.norms + static_cast<size_t>(layer) * 2304;
             // This warp's stages of the phase: first, first + 6, ...
             const int first = static_cast<int>((warp - static_cast<int>(gs % kMegaWarps) + kMegaWarps) % kMegaWarps);
 
-            // ---------------- prologue: activation vector ----------------
+            // ---------------- prologue: wait for and stage the activation vector ----------------
             float rinv = 1.0f;   // RMSNorm scale applied to the dot products
             if (kind == PH_QKV || kind == PH_GU || kind == PH_LM)
             {
-                const bool gather = (kind == PH_QKV && layer == 0);
-                int id = 0;
-                if (gather)
+                float v[kXPer];
+                if (kind == PH_QKV && layer == 0)
                 {
-                    id = __ldcg(&a.st->cur_token);
+                    // The token: set by the host for the launch's first token, then
+                    // published by the previous token's commit (acquire: its history
+                    // bits and state writes are visible after this).
+                    int id;
+                    if (t == 0)
+                    {
+                        id = __ldcg(&a.st->cur_token);
+                    }
+                    else
+                    {
+                        unsigned long long w = ld_acquire_u64(a.tok_ep);
+                        const unsigned long long t0 = global_ns();
+                        while (static_cast<unsigned>(w >> 32) != e_in)
+                        {
+                            if (global_ns() - t0 > kWaitLimitNs)
+                            {
+                                atomicOr(a.err, kErrTimeoutFull);
+                                redi[0] = 1;
+                                break;
+                            }
+                            __nanosleep(32);
+                            w = ld_acquire_u64(a.tok_ep);
+                        }
+                        id = static_cast<int>(static_cast<unsigned>(w));
+                        if (tid == 0) mbar_arrive(tokbar);   // after this thread's acquire
+                    }
                     if (id < 0 || id >= a.vocab)
                     {
                         if (tid == 0) atomicOr(a.err, kErrBounds);
                         id = 0;
                     }
-                }
-                float4 v[2];
+                    const WT* erow = static_cast<const WT*>(a.embed) + static_cast<size_t>(id) * kHidden;
 #pragma unroll
-                for (int u = 0; u < 2; ++u)
-                {
-                    const int i = tid + kMegaConsumers * u;
-                    v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (i < kHidden / 4)
-                        v[u] = gather ? load4(static_cast<const WT*>(a.embed) + static_cast<size_t>(id) * kHidden + 4 * i)
-                                      : __ldcg(reinterpret_cast<const float4*>(xg) + i);
+                    for (int u = 0; u < kXPer; ++u)
+                    {
+                        const int i = tid + kMegaConsumers * u;
+                        v[u] = (i < kHidden) ? to_f32<WT>(erow[i]) : 0.f;
+                    }
+                    // The residual rows this CTA owns start as the embedding.
+                    if (tid < po.count && tid < kMegaResRows) xres_s[tid] = to_f32<WT>(erow[po.r0 + tid]);
                 }
-                if (gather)
+                else if (!poll_words<kXPer>(a.x_ep, kHidden, tid, kMegaConsumers, e_in, v, a.err))
                 {
-                    // Publish this CTA's slice of the residual stream.
-                    const int chunk = (kHidden + G - 1) / G;
-                    const int i = b * chunk + tid;
-                    if (tid < chunk && i < kHidden)
-                        xg[i] = to_f32<WT>(static_cast<const WT*>(a.embed)[static_cast<size_t>(id) * kHidden + i]);
+                    redi[0] = 1;
                 }
                 if (kind == PH_LM && p.count > 0)
                 {
@@ -650,13 +808,29 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                 const float* nw = (kind == PH_QKV) ? lnorm
                                   : (kind == PH_GU) ? lnorm + kHidden
                                                     : a.norms + static_cast<size_t>(L) * 2304;
-                rinv = mega_load_normed(xs, v, nw, a.eps, s_norm, tid);
+                rinv = mega_load_normed_s(xs, v, nw, a.eps, s_norm, tid);   // (one consumer barrier)
             }
-            else if (kind == PH_O || kind == PH_DOWN)
+            else if (kind == PH_DOWN)
             {
-                // Residual rows this CTA updates in the epilogue.
-                if (tid < p.count && tid < kMegaResRows) xres_s[tid] = __ldcg(xg + p.r0 + tid);
-                if (kind == PH_O)
+                // act = silu(gate) * up from the gate/up phase.
+                constexpr int kPer = (kMegaMaxK + kMegaConsumers - 1) / kMegaConsumers;
+                float v[kPer];
+                if (!poll_words<kPer>(a.act_ep, a.ffn, tid, kMegaConsumers, e_in, v, a.err)) redi[0] = 1;
+#pragma unroll
+                for (int u = 0; u < kPer; ++u)
+                {
+                    const int i = tid + kMegaConsumers * u;
+                    if (i < a.ffn) xs[i] = v[u];
+                }
+                mega_sync();
+            }
+            else if (kind == PH_O)
+            {
+                // All attention splits of this layer have written their partials.
+                const unsigned target = static_cast<unsigned>(t * L + layer + 1) * static_cast<unsigned>(G);
+                if (tid == 0 && !grid_wait(a.bar, target, a.err)) redi[0] = 1;
+                mega_sync();
+                if (!redi[0])
                 {
                     // Merge the attention partials of every split (split-K
                     // flash-decode combine): 12 threads per q head, thread k
@@ -710,26 +884,16 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                         *reinterpret_cast<float4*>(xs + h * kHeadDim + 4 * (k0 + 12 * j)) = o;
                     }
                 }
-                else
-                {
-                    // The gate/up phase wrote act = silu(gate) * up; all loads issue before use.
-                    constexpr int kPer = (kMegaMaxK / 4 + kMegaConsumers - 1) / kMegaConsumers;
-                    float4 av[kPer];
-#pragma unroll
-                    for (int u = 0; u < kPer; ++u)
-                    {
-                        const int i = tid + kMegaConsumers * u;
-                        if (i < a.ffn / 4) av[u] = __ldcg(reinterpret_cast<const float4*>(a.gu) + i);
-                    }
-#pragma unroll
-                    for (int u = 0; u < kPer; ++u)
-                    {
-                        const int i = tid + kMegaConsumers * u;
-                        if (i < a.ffn / 4) reinterpret_cast<float4*>(xs)[i] = av[u];
-                    }
-                }
                 mega_sync();
             }
+            // (Attention polls its inputs below; every other kind has passed a
+            // consumer barrier after its polls, so the flag is settled here.)
+            if (kind != PH_ATTN && redi[0])
+            {
+                bad = true;
+                break;
+            }
+            if (tracing) tr[1] = global_ns();
             if (tracing) tr[2] = global_ns();
 
             if (kind != PH_ATTN)
@@ -758,13 +922,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                     const WT* rows = reinterpret_cast<const WT*>(myring + slot * kMegaStage);
                     const int q0 = i * p.per_stage;
                     if (p.K == kHidden)
-                        gemv_stage<WT, kHidden, true>(a, p, kind, rows, xr, xs, q0, rinv, xg, xres_s, hist_s, pen, best,
+                        gemv_stage<WT, kHidden, true>(a, p, kind, rows, xr, xs, q0, rinv, eo, xres_s, hist_s, pen, best,
                                                       &myempty[slot], lane, b, ph);
                     else if (p.K == kQWidth)
-                        gemv_stage<WT, kQWidth, false>(a, p, kind, rows, xr, xs, q0, rinv, xg, xres_s, hist_s, pen, best,
+                        gemv_stage<WT, kQWidth, false>(a, p, kind, rows, xr, xs, q0, rinv, eo, xres_s, hist_s, pen, best,
                                                        &myempty[slot], lane, b, ph);
                     else
-                        gemv_stage<WT, kMegaMaxK, false>(a, p, kind, rows, xr, xs, q0, rinv, xg, xres_s, hist_s, pen,
+                        gemv_stage<WT, kMegaMaxK, false>(a, p, kind, rows, xr, xs, q0, rinv, eo, xres_s, hist_s, pen,
                                                          best, &myempty[slot], lane, b, ph);
                     if (wtr)
                     {
@@ -860,7 +1024,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                                     if (eos || n + 1 >= st->max_tokens) st->done = 1;
                                 }
                             }
+                            // Publish the next token (also after the stream ended: the
+                            // remaining tokens of the launch still run, uncommitted).
+                            // Release: the history bits, the state and the ticket reset
+                            // above are visible to whoever acquires this word.
                             __threadfence();
+                            st_release_u64(a.tok_ep, (static_cast<unsigned long long>(eo.e) << 32) |
+                                                         static_cast<unsigned>(st->cur_token));
                         }
                     }
                 }
@@ -874,17 +1044,22 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                 const float* kn_w = lnorm + 2176;
                 const float* c = a.rope_cos + static_cast<size_t>(past) * kHeadDim;
                 const float* s = a.rope_sin + static_cast<size_t>(past) * kHeadDim;
+                // q/k/v of this KV head from the q/k/v phase (epoch words).
                 if (warp < 2)
                 {
-                    float o[4];
-                    rope_norm_vec_cg(a.qkv + (2 * g + warp) * kHeadDim, c, s, qn_w, a.eps, lane, o);
+                    float x[4], o[4];
+                    if (!poll_words<4>(a.qkv_ep + (2 * g + warp) * kHeadDim, kHeadDim, lane, 32, e_in, x, a.err))
+                        redi[0] = 1;
+                    rope_norm_vals(x, c, s, qn_w, a.eps, lane, o);
 #pragma unroll
                     for (int i = 0; i < 4; ++i) qs[warp * kHeadDim + lane + 32 * i] = o[i] * a.scale_log2;
                 }
                 else if (new_split && warp == 2)
                 {
-                    float o[4];
-                    rope_norm_vec_cg(a.qkv + kQWidth + g * kHeadDim, c, s, kn_w, a.eps, lane, o);
+                    float x[4], o[4];
+                    if (!poll_words<4>(a.qkv_ep + kQWidth + g * kHeadDim, kHeadDim, lane, 32, e_in, x, a.err))
+                        redi[0] = 1;
+                    rope_norm_vals(x, c, s, kn_w, a.eps, lane, o);
                     mega_check(past >= 0 && past < a.cap, a.dbg, 5, b, ph, past);
                     KT* krow = static_cast<KT*>(a.kc) +
                                ((static_cast<size_t>(layer) * kNumKVHeads + g) * a.cap + min(past, a.cap - 1)) * kHeadDim;
@@ -900,13 +1075,15 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                 }
                 else if (new_split && warp == 3)
                 {
-                    const float* vsrc = a.qkv + kQWidth + kKVWidth + g * kHeadDim;
+                    float x[4];
+                    if (!poll_words<4>(a.qkv_ep + kQWidth + kKVWidth + g * kHeadDim, kHeadDim, lane, 32, e_in, x, a.err))
+                        redi[0] = 1;
                     KT* vrow = static_cast<KT*>(a.vc) +
                                ((static_cast<size_t>(layer) * kNumKVHeads + g) * a.cap + min(past, a.cap - 1)) * kHeadDim;
 #pragma unroll
                     for (int i = 0; i < 4; ++i)
                     {
-                        const KT q = from_f32<KT>(__ldcg(vsrc + lane + 32 * i));
+                        const KT q = from_f32<KT>(x[i]);
                         vrow[lane + 32 * i] = q;
                         vnew[lane + 32 * i] = to_f32<KT>(q);
                     }
@@ -1075,7 +1252,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                 tr[5] = wwork;
                 tr[6] = wn;
             }
-            // ---------------- phase done: arrive on the grid barrier ----------------
+            // ---------------- phase done ----------------
             mega_sync();
             if (redi[0])
             {
@@ -1085,8 +1262,10 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
             if (tracing) tr[3] = global_ns();
             if (tid == 0)
             {
-                grid_arrive(a.bar);
-                if (a.progress) a.progress[b] = phase_no + 1;
+                // The attention partials are plain stores: the o-projection
+                // phase waits for every CTA on the grid barrier.
+                if (kind == PH_ATTN) grid_arrive(a.bar);
+                if (a.progress) a.progress[b] = static_cast<unsigned>(t * phases + ph + 1);
             }
         }
     }
