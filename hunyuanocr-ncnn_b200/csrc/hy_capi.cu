@@ -118,6 +118,8 @@ struct hy_ctx {
     unsigned long long* qkv_ep = nullptr;  // [4096]
     unsigned long long* act_ep = nullptr;  // [ffn]
     unsigned long long* tok_ep = nullptr;  // [1]
+    unsigned long long* attn_ep = nullptr;      // [8][8][2][130]
+    unsigned long long* attn_out_ep = nullptr;  // [2048]
     unsigned mega_seq = 0;
     int* dbg = nullptr;            // persistent-kernel self-check record [4]
     unsigned* progress = nullptr;  // host-mapped per-CTA phase progress (HY_DEBUG_PROGRESS=1)
@@ -561,6 +563,10 @@ cudaError_t launch_mega_t(hy_ctx* c, int steps)
         if (z == cudaSuccess) z = cudaMemsetAsync(c->qkv_ep, 0, sizeof(unsigned long long) * kQKVRows, c->stream);
         if (z == cudaSuccess) z = cudaMemsetAsync(c->act_ep, 0, sizeof(unsigned long long) * c->cfg.ffn_dim, c->stream);
         if (z == cudaSuccess) z = cudaMemsetAsync(c->tok_ep, 0, sizeof(unsigned long long), c->stream);
+        if (z == cudaSuccess)
+            z = cudaMemsetAsync(c->attn_ep, 0,
+                                sizeof(unsigned long long) * kNumKVHeads * (kMegaSplits - 1) * 2 * kAttnWords, c->stream);
+        if (z == cudaSuccess) z = cudaMemsetAsync(c->attn_out_ep, 0, sizeof(unsigned long long) * kQWidth, c->stream);
         if (z != cudaSuccess) return z;
     }
     ++c->mega_seq;
@@ -568,6 +574,8 @@ cudaError_t launch_mega_t(hy_ctx* c, int steps)
     a.qkv_ep = c->qkv_ep;
     a.act_ep = c->act_ep;
     a.tok_ep = c->tok_ep;
+    a.attn_ep = c->attn_ep;
+    a.attn_out_ep = c->attn_out_ep;
     a.epoch_base = c->mega_seq * kMegaEpochSpan;
     cudaError_t e = cudaMemsetAsync(c->bar, 0, sizeof(unsigned), c->stream);
     if (e != cudaSuccess) return e;
@@ -767,6 +775,8 @@ int alloc_ctx(hy_ctx* c)
     if ((rc = dalloc(c, &c->qkv_ep, kQKVRows))) return rc;
     if ((rc = dalloc(c, &c->act_ep, cfg.ffn_dim))) return rc;
     if ((rc = dalloc(c, &c->tok_ep, 1))) return rc;
+    if ((rc = dalloc(c, &c->attn_ep, static_cast<size_t>(kNumKVHeads) * (kMegaSplits - 1) * 2 * kAttnWords))) return rc;
+    if ((rc = dalloc(c, &c->attn_out_ep, kQWidth))) return rc;
     HY_CUDA(cudaMemsetAsync(c->dbg, 0, 4 * sizeof(int), c->stream));
     if (const char* e = std::getenv("HY_DEBUG_PROGRESS"); e && e[0] == '1')
     {

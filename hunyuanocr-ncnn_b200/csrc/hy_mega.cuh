@@ -54,6 +54,7 @@ constexpr int kMegaHistWords = 64;       // LM rows per CTA <= 32 * 62
 constexpr int kMegaResRows = 32;         // o/down rows per CTA (1024 / gridDim.x)
 constexpr int kMegaMaxLayers = 64;
 constexpr unsigned kMegaEpochSpan = 32768;   // epochs per launch (>= 64 tokens x 321 phases)
+constexpr int kAttnWords = 2 + 128;          // one split partial of one query: max, sum, acc[128]
 
 struct MegaArgs {
     const void* embed;
@@ -102,6 +103,8 @@ struct MegaArgs {
     unsigned long long* qkv_ep;  // q/k/v projections [4096]
     unsigned long long* act_ep;  // silu(gate) * up [ffn]
     unsigned long long* tok_ep;  // committed token (int bits) [1], written with release
+    unsigned long long* attn_ep;      // split partials [8 heads][8 past splits][2][kAttnWords]
+    unsigned long long* attn_out_ep;  // merged attention output [2048]
     unsigned epoch_base;
 };
 
@@ -116,8 +119,10 @@ struct MegaSmem {
     static constexpr int NEWKV = QS + 2 * kHeadDim * 4;                     // k[128], v[128]
     static constexpr int ASCR = NEWKV + 2 * kHeadDim * 4;                   // [warps][2][kPartStride]
     static constexpr int PBUF = ASCR + kMegaWarps * 2 * kPartStride * 4;    // [warps][32] softmax weights
-    static_assert(PBUF + kMegaWarps * 32 * 4 <= XS + kMegaMaxK * 4, "attention scratch must fit");
-    static constexpr int RED = XS + kMegaMaxK * 4;                          // 64 float4 + 64 ints
+    static constexpr int MINE = PBUF + kMegaWarps * 32 * 4;                 // [2][kPartStride] this CTA's partial
+    static constexpr int PARTS = MINE + 2 * kPartStride * 4;                // [8 splits][2][130] polled partials
+    static constexpr int XS_END = PARTS + (kMegaSplits - 1) * 2 * kAttnWords * 4;
+    static constexpr int RED = (XS_END > XS + kMegaMaxK * 4 ? XS_END : XS + kMegaMaxK * 4);   // 64 float4 + 64 ints
     static constexpr int BARS = RED + 64 * 16 + 64 * 4;                     // full[warp][slot], empty[warp][slot]
     static constexpr int TOKBAR = BARS + 2 * kMegaWarps * kMegaSlots * 8;  // token-start mbarrier
     static constexpr int SIZE = TOKBAR + 8;
@@ -826,63 +831,15 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
             }
             else if (kind == PH_O)
             {
-                // All attention splits of this layer have written their partials.
-                const unsigned target = static_cast<unsigned>(t * L + layer + 1) * static_cast<unsigned>(G);
-                if (tid == 0 && !grid_wait(a.bar, target, a.err)) redi[0] = 1;
-                mega_sync();
-                if (!redi[0])
+                // The attention output of all 16 heads (merged by each head pair's new-row split).
+                constexpr int kPer = (kQWidth + kMegaConsumers - 1) / kMegaConsumers;
+                float v[kPer];
+                if (!poll_words<kPer>(a.attn_out_ep, kQWidth, tid, kMegaConsumers, e_in, v, a.err)) redi[0] = 1;
+#pragma unroll
+                for (int u = 0; u < kPer; ++u)
                 {
-                    // Merge the attention partials of every split (split-K
-                    // flash-decode combine): 12 threads per q head, thread k
-                    // taking float4 columns k, k + 12, k + 24 (< 32). All loads
-                    // issue before any use: one L2 round trip.
-                    static_assert(kMegaConsumers == kNumQHeads * 12, "12 threads per head");
-                    const int h = tid / 12, k0 = tid - 12 * h;
-                    const float* hp = a.attn_part + (static_cast<size_t>(h >> 1) * kMegaSplits * 2 + (h & 1)) * kPartStride;
-                    float ms[kMegaSplits], ls[kMegaSplits];
-                    float4 va[kMegaSplits][3];
-#pragma unroll
-                    for (int sp = 0; sp < kMegaSplits; ++sp)
-                    {
-                        const float* ps = hp + static_cast<size_t>(sp) * 2 * kPartStride;
-                        ms[sp] = __ldcg(ps);
-                        ls[sp] = __ldcg(ps + 1);
-#pragma unroll
-                        for (int j = 0; j < 3; ++j)
-                            va[sp][j] = (k0 + 12 * j < kHeadDim / 4)
-                                            ? __ldcg(reinterpret_cast<const float4*>(ps + 4) + k0 + 12 * j)
-                                            : make_float4(0.f, 0.f, 0.f, 0.f);
-                    }
-                    float M = -INFINITY;
-#pragma unroll
-                    for (int sp = 0; sp < kMegaSplits; ++sp) M = fmaxf(M, ms[sp]);
-                    float Lsum = 0.f;
-                    float4 A[3];
-#pragma unroll
-                    for (int j = 0; j < 3; ++j) A[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                    for (int sp = 0; sp < kMegaSplits; ++sp)
-                    {
-                        const float f = (ms[sp] == -INFINITY) ? 0.f : exp2f(ms[sp] - M);
-                        Lsum += f * ls[sp];
-#pragma unroll
-                        for (int j = 0; j < 3; ++j)
-                        {
-                            A[j].x += f * va[sp][j].x;
-                            A[j].y += f * va[sp][j].y;
-                            A[j].z += f * va[sp][j].z;
-                            A[j].w += f * va[sp][j].w;
-                        }
-                    }
-                    const float inv = 1.0f / Lsum;
-#pragma unroll
-                    for (int j = 0; j < 3; ++j)
-                    {
-                        if (k0 + 12 * j >= kHeadDim / 4) break;
-                        float4 o = A[j];
-                        o.x *= inv; o.y *= inv; o.z *= inv; o.w *= inv;
-                        *reinterpret_cast<float4*>(xs + h * kHeadDim + 4 * (k0 + 12 * j)) = o;
-                    }
+                    const int i = tid + kMegaConsumers * u;
+                    if (i < kQWidth) xs[i] = v[u];
                 }
                 mega_sync();
             }
@@ -1163,9 +1120,16 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                     }
                     __syncwarp();
                 };
+                // Trace: the warp that owns the split's first stage records its
+                // slot-wait / work cycles and stages in slots 7..9, and the
+                // time its stage loop ended in slot 10.
+                const bool atr = a.trace && t == a.trace_token && b < kTraceCtas && lane == 0 && first == 0;
+                long long await_ = 0, awork = 0, an = 0;
                 for (int i = first; i < p.nstage && !bad; i += kMegaWarps)
                 {
+                    const long long c0 = atr ? clock64() : 0;
                     const int slot = wait_own();
+                    const long long c1 = atr ? clock64() : 0;
                     if (slot < 0)
                     {
                         if (lane == 0) redi[0] = 1;
@@ -1180,6 +1144,20 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                                 min(16, n - h));
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&myempty[slot]);
+                    if (atr)
+                    {
+                        await_ += c1 - c0;
+                        awork += clock64() - c1;
+                        ++an;
+                    }
+                }
+                if (atr)
+                {
+                    unsigned long long* ta = a.trace + (static_cast<size_t>(b) * phases + ph) * kTraceSlots;
+                    ta[7] = await_;
+                    ta[8] = awork;
+                    ta[9] = an;
+                    ta[10] = global_ns();
                 }
                 if (new_split && warp == 0)
                 {
@@ -1214,7 +1192,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                     reinterpret_cast<float4*>(w1 + 4)[lane] = o1;
                 }
                 mega_sync();
-                // This CTA's partial per query: 2 queries x 128 dims.
+                // This CTA's partial per query: 2 queries x 128 dims. A past
+                // split publishes it as epoch words; the new-row split keeps it.
+                float* mine = reinterpret_cast<float*>(smem + MegaSmem::MINE);
                 for (int e = tid; e < 2 * kHeadDim; e += kMegaConsumers)
                 {
                     const int q = e >> 7, d = e & 127;
@@ -1234,15 +1214,70 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                             A += f * sw[4 + d];
                         }
                     }
-                    float* part = a.attn_part + ((static_cast<size_t>(g) * kMegaSplits + p.split) * 2 + q) * kPartStride;
-                    if (d == 0)
+                    if (!new_split)
                     {
-                        part[0] = M;
-                        part[1] = Lsum;
+                        unsigned long long* part =
+                            a.attn_ep + ((static_cast<size_t>(g) * (kMegaSplits - 1) + p.split) * 2 + q) * kAttnWords;
+                        if (d == 0)
+                        {
+                            st_relaxed_u64(part, ep_word(M, eo.e));
+                            st_relaxed_u64(part + 1, ep_word(Lsum, eo.e));
+                        }
+                        st_relaxed_u64(part + 2 + d, ep_word(A, eo.e));
                     }
-                    part[4 + d] = A;
+                    else
+                    {
+                        if (d == 0)
+                        {
+                            mine[q * kPartStride] = M;
+                            mine[q * kPartStride + 1] = Lsum;
+                        }
+                        mine[q * kPartStride + 4 + d] = A;
+                    }
                 }
-                // The o-projection phase merges the partials of all splits.
+                if (new_split)
+                {
+                    // Merge the head pair's split partials (split-K flash-decode
+                    // combine, splits in order, this CTA's new-row split last) and
+                    // publish the two heads' outputs for the o projection.
+                    constexpr int kWords = (kMegaSplits - 1) * 2 * kAttnWords;
+                    constexpr int kPer = (kWords + kMegaConsumers - 1) / kMegaConsumers;
+                    float* parts = reinterpret_cast<float*>(smem + MegaSmem::PARTS);
+                    float v[kPer];
+                    if (!poll_words<kPer>(a.attn_ep + static_cast<size_t>(g) * kWords, kWords, tid, kMegaConsumers, eo.e,
+                                          v, a.err))
+                        redi[0] = 1;
+#pragma unroll
+                    for (int u = 0; u < kPer; ++u)
+                    {
+                        const int i = tid + kMegaConsumers * u;
+                        if (i < kWords) parts[i] = v[u];
+                    }
+                    mega_sync();
+                    for (int e = tid; e < 2 * kHeadDim; e += kMegaConsumers)
+                    {
+                        const int q = e >> 7, d = e & 127;
+                        const float mm = mine[q * kPartStride];
+                        float M = mm;
+#pragma unroll
+                        for (int sp = 0; sp < kMegaSplits - 1; ++sp) M = fmaxf(M, parts[(sp * 2 + q) * kAttnWords]);
+                        float Lsum = 0.f, A = 0.f;
+#pragma unroll
+                        for (int sp = 0; sp < kMegaSplits - 1; ++sp)
+                        {
+                            const float* ps = parts + (sp * 2 + q) * kAttnWords;
+                            const float f = (ps[0] == -INFINITY) ? 0.f : exp2f(ps[0] - M);
+                            Lsum += f * ps[1];
+                            A += f * ps[2 + d];
+                        }
+                        {
+                            const float f = (mm == -INFINITY) ? 0.f : exp2f(mm - M);
+                            Lsum += f * mine[q * kPartStride + 1];
+                            A += f * mine[q * kPartStride + 4 + d];
+                        }
+                        st_relaxed_u64(a.attn_out_ep + (2 * g + q) * kHeadDim + d, ep_word(A * (1.0f / Lsum), eo.e));
+                    }
+                }
             }
 
             gs += p.nstage;
@@ -1260,13 +1295,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                 break;
             }
             if (tracing) tr[3] = global_ns();
-            if (tid == 0)
-            {
-                // The attention partials are plain stores: the o-projection
-                // phase waits for every CTA on the grid barrier.
-                if (kind == PH_ATTN) grid_arrive(a.bar);
-                if (a.progress) a.progress[b] = static_cast<unsigned>(t * phases + ph + 1);
-            }
+            if (tid == 0 && a.progress) a.progress[b] = static_cast<unsigned>(t * phases + ph + 1);
         }
     }
 }
