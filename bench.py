@@ -8,10 +8,12 @@ N(0,1) image-embedding rows on a 24x32 mRoPE grid + 256 uniform text ids), then
 256 greedy tokens with repetition penalty 1.08.
 
 One step = the AR decode of those 256 tokens from the prefilled state (255
-decoder steps, each one CUDA-graph replay of embed -> 24 layers -> LM head ->
-penalised argmax, token kept on the device). `value` = decode tokens/s with the
-prompt state resident in HBM; `e2e` = tokens/s of the reference-facing call
-(hy_run_vlm_decode_with_prompt: host prompt -> prefill -> 256 tokens -> host).
+decoder steps run by the persistent decode kernel, 64 tokens per launch: embed
+-> 24 layers -> LM head -> penalised argmax -> commit, token kept on the
+device). `value` = decode tokens/s with the prompt state resident in HBM;
+`e2e` = tokens/s of the reference-facing call (hy_run_vlm_decode_with_prompt:
+host prompt -> prefill -> 256 tokens -> host). `dflash` = config 3 (KV 2048,
+block 16, synthetic drafts at p = 0.3 / 0.7 / 0.9), device-timed.
 
 Multi-GPU (torchrun, one process per GPU): replicas only - each rank decodes its
 own request; value = tokens of all ranks / max rank time ("scaling": "weak").
@@ -46,7 +48,10 @@ PENALTY = 1.08
 DECODER_WEIGHT_BYTES = LAYERS * (4096 * 1024 + 1024 * 2048 + 2 * FFN * 1024 + 1024 * FFN) * 4
 LM_HEAD_BYTES = V * HIDDEN * 4
 KV_ROW_BYTES = LAYERS * 8 * 128 * 4 * 2
-KERNELS_PER_AR_STEP = LAYERS * 5 + 1
+MEGA_CHUNK = 64                      # tokens per persistent-kernel launch (hy_capi.cu kMegaChunk)
+# DRAM bytes (read + write) per full 64-token launch: from the ncu capture summarised in
+# profiles/mega_decode_kernel_config0.md (None until captured).
+MEGA_TRAFFIC_PER_LAUNCH = None
 
 
 def measured_peaks():
@@ -158,6 +163,50 @@ def prompt_arrays(seed: int):
     return mod.synthetic_prompt(seed, PROMPT_GRID[0], PROMPT_GRID[1], PROMPT_TEXT, V)
 
 
+def device_ms(rt, fn):
+    """Run fn() and return the CUDA-event time (ms) of the work it enqueues on the context's stream."""
+    import torch
+    ext = torch.cuda.ExternalStream(rt.stream)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(ext)
+    out = fn()
+    e1.record(ext)
+    e1.synchronize()
+    return e0.elapsed_time(e1), out
+
+
+def dflash_leg(pkg, local):
+    """DFlash (config 3): KV length 2048, block 16, synthetic drafts equal to the greedy token
+    with probability p, repeated for 256 committed tokens; tokens/s per p, device-timed."""
+    seq, n_tok = 2048, 257
+    rt = pkg.TextRuntime.synthetic(seed=0, device=local, max_prefill=64, max_tokens=n_tok + 64,
+                                   max_context=seq + n_tok + 64)
+    hist = list(range(1, 257))
+    rt.set_length(seq)
+    rt.set_history(hist)
+    greedy, _ = rt.generate(1234, 1234, n_tok + 16, PENALTY)
+    out = {}
+    for p in (0.3, 0.7, 0.9):
+        best = None
+        for _ in range(2):
+            rt.set_length(seq)
+            rt.set_history(hist)
+            ms, r = device_ms(rt, lambda: rt.dflash_generate_synthetic(1234, n_tok, PENALTY, greedy, p, seed=7))
+            assert r.generated_tokens == greedy[:len(r.generated_tokens)], "DFlash is not lossless"
+            best = ms if best is None else min(best, ms)
+        out[f"p{p}"] = {"tokens_per_s": round((len(r.generated_tokens) - 1) / (best / 1e3), 1),
+                        "blocks": r.block_count,
+                        "mean_accept": round(float(np.mean(r.acceptance_lengths)), 3),
+                        "ms_per_block": round(best / max(1, r.block_count), 3)}
+    rt.set_length(seq)
+    rt.set_history(hist)
+    ms, _ = device_ms(rt, lambda: rt.bench_ar_steps(n_tok - 1))
+    out["ar_tokens_per_s_kv2048"] = round((n_tok - 1) / (ms / 1e3), 1)
+    rt.close()
+    return out
+
+
 def run_b200(args, world, rank, local):
     sys.path.insert(0, REPO)
     import __graft_entry__ as ge
@@ -201,10 +250,15 @@ def run_b200(args, world, rank, local):
     decode_tokens = (n_tok - 1) * args.steps * world
     value = decode_tokens / (ms_max / 1e3)
 
-    # Device-only decode loop without the host polling (graph replays back to back).
+    # The dominant kernel: the persistent decode kernel (one launch per <= 64 tokens),
+    # launched back to back on the context stream with no host work between launches.
     rt.set_length(seq)
     rt.set_history(ids)
-    dev_ms = rt.bench_ar_steps(GEN_TOKENS - 1)
+    dev_ms, _ = device_ms(rt, lambda: rt.bench_ar_steps(GEN_TOKENS - 1))
+    launches = (GEN_TOKENS - 1 + MEGA_CHUNK - 1) // MEGA_CHUNK
+    bpt = ar_bytes_per_token(seq, n_tok)
+    peak, peak_kind = measured_peaks()
+    mega_gbs = bpt * (GEN_TOKENS - 1) / (dev_ms / 1e3) / 1e9
 
     # e2e: reference-facing call with host buffers (prompt upload, prefill, 256 tokens, tokens back).
     e2e_times = []
@@ -216,15 +270,12 @@ def run_b200(args, world, rank, local):
     e2e_t = dist_max(max(e2e_times), world)
     e2e_value = len(r2.generated_tokens) * world / e2e_t
 
-    # Roofline of the dominant GEMV launch: the LM head + argmax (494.9 MB streamed per launch).
-    peak, peak_kind = measured_peaks()
+    # Configs 1 and 2 alone: LM head + argmax (M=1), gate/up GEMV, attention at KV 1024.
     lm_ms = rt.bench_kernel(0, 20)
-    lm_gbs = LM_HEAD_BYTES / (lm_ms / 1e3) / 1e9
     gu_ms = rt.bench_kernel(1, 20)
     attn_ms = rt.bench_kernel(2, 50)
-    bpt = ar_bytes_per_token(seq, n_tok)
-    step_gbs = bpt * (n_tok - 1) * args.steps / (ms / 1e3) / 1e9
     rt.close()
+    dflash = dflash_leg(pkg, local) if (world == 1 and not args.no_dflash) else None
     if rank != 0:
         return None
     cs = clocks.summary()
@@ -246,19 +297,20 @@ def run_b200(args, world, rank, local):
                    "prompt": seq, "generated": n_tok, "parallelism": f"replicas x{world}",
                    "l2": "weights 2.16 GB per token > 126 MB L2 (no flush needed)"},
         "device_loop_tokens_per_s": round((GEN_TOKENS - 1) / (dev_ms / 1e3), 2),
-        "step_roofline": {"bytes_per_token": round(bpt), "achieved_gbs": round(step_gbs, 1),
-                          "peak_gbs": peak, "frac": round(step_gbs / peak, 4),
-                          "roofline_tokens_per_s": round(peak * 1e9 / bpt, 1)},
-        "roofline": {"bound": "hbm", "kernel": "gemv_kernel<f32,1024,1,NORM,ARGMAX> (LM head + penalised argmax)",
-                     "achieved": round(lm_gbs, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(lm_gbs / peak, 4), "traffic": None, "peak_source": peak_kind,
-                     "bytes_per_launch": LM_HEAD_BYTES, "launch_us": round(lm_ms * 1e3, 2)},
-        "kernel_us": {"lm_head": round(lm_ms * 1e3, 2), "gate_up_gemv": round(gu_ms * 1e3, 2),
-                      "attention_l1024": round(attn_ms * 1e3, 2)},
+        "roofline": {"bound": "hbm", "kernel": "mega_decode_kernel<f32,f32> (persistent: whole tokens per launch)",
+                     "achieved": round(mega_gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(mega_gbs / peak, 4), "traffic": MEGA_TRAFFIC_PER_LAUNCH,
+                     "peak_source": peak_kind, "bytes_per_token": round(bpt),
+                     "tokens_per_launch": MEGA_CHUNK, "launch_us": round(dev_ms * 1e3 / launches, 1),
+                     "roofline_tokens_per_s": round(peak * 1e9 / bpt, 1)},
+        "kernel_us": {"lm_head_m1": round(lm_ms * 1e3, 2), "gate_up_gemv_m1": round(gu_ms * 1e3, 2),
+                      "attention_kv1024_q1": round(attn_ms * 1e3, 2),
+                      "lm_head_m1_gbs": round(LM_HEAD_BYTES / (lm_ms / 1e3) / 1e9, 1)},
+        "dflash": dflash,
         "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "scope": "prefill + 256 tokens per call",
                 "h2d_bytes_per_step": int(ids.nbytes + pos.nbytes + feats.nbytes),
                 "d2h_bytes_per_step": int(2 * 4 * len(r2.generated_tokens))},
-        "gpu_launches": int(KERNELS_PER_AR_STEP * 4 * ((GEN_TOKENS - 1 + 3) // 4) * args.steps),
+        "gpu_launches": int(launches * args.steps),
         "clocks": cs,
         "cpu_baseline": cpu_baseline(args) if (world == 1 and not args.no_cpu) else None,
     }
@@ -333,6 +385,7 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--cpu-steps", type=int, default=16)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-dflash", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
         world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))

@@ -1,0 +1,52 @@
+"""Small, self-contained decode workload for profiling the decode kernels.
+
+Builds a synthetic context (seeded random weights) with a reduced layer count
+and vocabulary so that one kernel launch is short and the device footprint is a
+few hundred MB (still larger than L2), sets the KV length, and runs a few AR
+decode launches. Meant to be run under a profiler, e.g.
+
+    ncu --set full --clock-control none -k regex:mega_decode -s 1 -c 1 \
+        python hunyuanocr-ncnn_b200/profile_case.py
+
+Prints one line with the last launch's device time.
+"""
+import argparse
+import os
+import sys
+
+_ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if _ROOT not in sys.path:
+    sys.path.insert(0, _ROOT)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--layers", type=int, default=4)
+    ap.add_argument("--vocab", type=int, default=16384)
+    ap.add_argument("--past", type=int, default=1024, help="KV length before decoding")
+    ap.add_argument("--tokens", type=int, default=8, help="tokens per measured call")
+    ap.add_argument("--calls", type=int, default=3)
+    ap.add_argument("--path", choices=["persistent", "graph"], default="persistent")
+    ap.add_argument("--dtype", choices=["f32", "bf16"], default="f32", help="weight and KV dtype")
+    args = ap.parse_args(argv)
+
+    import __graft_entry__ as ge
+
+    pkg = ge.load_package()
+    dt = pkg.DTYPE_F32 if args.dtype == "f32" else pkg.DTYPE_BF16
+    rt = pkg.TextRuntime.synthetic(seed=0, num_layers=args.layers, vocab_size=args.vocab, max_prefill=64,
+                                   max_tokens=args.tokens + 8, max_context=args.past + args.tokens + 8,
+                                   weight_dtype=dt, kv_dtype=dt)
+    rt.ar_path = pkg.AR_PATH_PERSISTENT if args.path == "persistent" else pkg.AR_PATH_GRAPH
+    ms = 0.0
+    for _ in range(args.calls):
+        rt.set_length(args.past)
+        rt.set_history([1, 2, 3])
+        ms = rt.bench_ar_steps(args.tokens)
+    print(f"{args.path} {args.dtype} layers={args.layers} vocab={args.vocab} past={args.past} "
+          f"tokens={args.tokens}: {ms:.3f} ms per call")
+    rt.close()
+
+
+if __name__ == "__main__":
+    main()
