@@ -49,9 +49,9 @@ DECODER_WEIGHT_BYTES = LAYERS * (4096 * 1024 + 1024 * 2048 + 2 * FFN * 1024 + 10
 LM_HEAD_BYTES = V * HIDDEN * 4
 KV_ROW_BYTES = LAYERS * 8 * 128 * 4 * 2
 MEGA_CHUNK = 64                      # tokens per persistent-kernel launch (hy_capi.cu kMegaChunk)
-# DRAM bytes (read + write) per full 64-token launch: from the ncu capture summarised in
-# profiles/mega_decode_kernel_config0.md (None until captured).
-MEGA_TRAFFIC_PER_LAUNCH = None
+# DRAM bytes (read + write) of one full 64-token launch (tokens 129-192), from the 1-pass ncu
+# capture summarised in profiles/mega_decode_kernel_config0.md.
+MEGA_TRAFFIC_PER_LAUNCH = 152.88e9
 
 
 def measured_peaks():
