@@ -70,12 +70,12 @@ struct AttnShape {
     static constexpr int QS_OFF = 0;                                // [NQ][128] f32
     static constexpr int NEW_OFF = QS_OFF + NQ * kHeadDim * 4;      // K new [MT][128], V new [MT][128] f32
     static constexpr int RING_OFF = NEW_OFF + 2 * MT * kHeadDim * 4;
-    static constexpr int NSTREAM = (MT == 1) ? 32 : 2;
+    static constexpr int NSTREAM = (MT == 1) ? 32 : 4;
     // Per-stream softmax states reuse the ring once every stage has been consumed.
     static constexpr int SCR_OFF = RING_OFF;   // [NSTREAM][NQ] (m, l), [NSTREAM][NQ][128] acc
     static constexpr int SCR_BYTES = NSTREAM * NQ * 8 + NSTREAM * NQ * kHeadDim * 4;
-    static_assert(SCR_BYTES <= kAttnStages * STAGE, "scratch must fit in the ring");
-    static constexpr int BAR_OFF = RING_OFF + kAttnStages * STAGE;
+    static constexpr int RING_REGION = (SCR_BYTES > kAttnStages * STAGE) ? SCR_BYTES : kAttnStages * STAGE;
+    static constexpr int BAR_OFF = RING_OFF + RING_REGION;
     static constexpr int SMEM = BAR_OFF + 2 * kAttnStages * 8 + 16;
 };
 
@@ -100,7 +100,7 @@ __device__ __forceinline__ void rope_norm_vec(const float* x, const float* c, co
 }
 
 template <int MT, typename KT>
-__global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const AttnArgs a)
+__global__ void __launch_bounds__(kAttnThreads, (MT == 1) ? 2 : 1) attn_kernel(const AttnArgs a)
 {
     using S = AttnShape<MT, KT>;
     constexpr int NQ = S::NQ, NSTREAM = S::NSTREAM, ROWB = S::ROWB, STAGE = S::STAGE;
@@ -180,33 +180,86 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const AttnArgs a)
     // Prologue: rotate + normalise the 2*MT queries (and, in the new-row split,
     // the MT keys; values are copied), append the new rows to the cache.
     const int nvec = new_split ? (NQ + 2 * MT) : NQ;
-    for (int v = warp; v < nvec; v += kAttnWarps)
+    // A warp's vectors are v = warp + 8 jv; all their loads (the row, the RoPE
+    // cos / sin rows) are issued before any is used: one L2 round trip.
+    constexpr int kMaxVec = (4 * MT + kAttnWarps - 1) / kAttnWarps;
+    float xv[kMaxVec][4], cv[kMaxVec][4], sv[kMaxVec][4];
+#pragma unroll
+    for (int jv = 0; jv < kMaxVec; ++jv)
     {
+        const int v = warp + kAttnWarps * jv;
         int m, kind, head;
         if (v < NQ) { kind = 0; head = v / MT; m = v % MT; }
         else if (v < NQ + MT) { kind = 1; head = 0; m = v - NQ; }
         else { kind = 2; head = 0; m = v - NQ - MT; }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) xv[jv][i] = cv[jv][i] = sv[jv][i] = 0.f;
+        if (v >= nvec || m >= rows) continue;
+        const float* src = a.qkv + static_cast<size_t>(m) * a.ldq +
+                           ((kind == 0) ? (2 * g + head) * kHeadDim : (kind == 1) ? kQWidth + g * kHeadDim
+                                                                                  : kQWidth + kKVWidth + g * kHeadDim);
+        const int prow = (a.rope_state ? past : 0) + m;
+        const float* c = a.cos + static_cast<size_t>(prow) * kHeadDim;
+        const float* sn = a.sin + static_cast<size_t>(prow) * kHeadDim;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+        {
+            xv[jv][i] = src[lane + 32 * i];
+            if (kind != 2)
+            {
+                cv[jv][i] = c[lane + 32 * i];
+                sv[jv][i] = sn[lane + 32 * i];
+            }
+        }
+    }
+#pragma unroll
+    for (int jv = 0; jv < kMaxVec; ++jv)
+    {
+        const int v = warp + kAttnWarps * jv;
+        if (v >= nvec) break;
+        int m, kind, head;
+        if (v < NQ) { kind = 0; head = v / MT; m = v % MT; }
+        else if (v < NQ + MT) { kind = 1; head = 0; m = v - NQ; }
+        else { kind = 2; head = 0; m = v - NQ - MT; }
+        (void)head;
         float* dst = (kind == 0) ? (qs + v * kHeadDim) : (kind == 1 ? knew + m * kHeadDim : vnew + m * kHeadDim);
         if (m >= rows)
         {
             for (int d = lane; d < kHeadDim; d += 32) dst[d] = 0.f;
             continue;
         }
-        const float* src = a.qkv + static_cast<size_t>(m) * a.ldq;
-        const int prow = (a.rope_state ? past : 0) + m;
-        const float* c = a.cos + static_cast<size_t>(prow) * kHeadDim;
-        const float* s = a.sin + static_cast<size_t>(prow) * kHeadDim;
+        if (kind == 2)
+        {
+            KT* vrow = const_cast<KT*>(vbase) + static_cast<size_t>(past + m) * kHeadDim;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+            {
+                const KT q = from_f32<KT>(xv[jv][i]);
+                vrow[lane + 32 * i] = q;
+                dst[lane + 32 * i] = to_f32<KT>(q);
+            }
+            continue;
+        }
+        // RoPE (full-width, non-interleaved) + RMSNorm, lane l owning dims l + 32 i.
+        const float* nw = (kind == 0) ? a.qn_w : a.kn_w;
+        const float y0 = xv[jv][0] * cv[jv][0] - xv[jv][2] * sv[jv][0];
+        const float y1 = xv[jv][1] * cv[jv][1] - xv[jv][3] * sv[jv][1];
+        const float y2 = xv[jv][2] * cv[jv][2] + xv[jv][0] * sv[jv][2];
+        const float y3 = xv[jv][3] * cv[jv][3] + xv[jv][1] * sv[jv][3];
+        const float ss = warp_sum(y0 * y0 + y1 * y1 + y2 * y2 + y3 * y3);
+        const float ri = 1.0f / sqrtf(ss / static_cast<float>(kHeadDim) + a.eps);
+        float o[4];
+        o[0] = nw[lane] * (y0 * ri);
+        o[1] = nw[lane + 32] * (y1 * ri);
+        o[2] = nw[lane + 64] * (y2 * ri);
+        o[3] = nw[lane + 96] * (y3 * ri);
         if (kind == 0)
         {
-            float o[4];
-            rope_norm_vec(src + (2 * g + head) * kHeadDim, c, s, a.qn_w, a.eps, lane, o);
 #pragma unroll
             for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = o[i] * a.scale_log2;
         }
-        else if (kind == 1)
+        else
         {
-            float o[4];
-            rope_norm_vec(src + kQWidth + g * kHeadDim, c, s, a.kn_w, a.eps, lane, o);
             KT* krow = const_cast<KT*>(kbase) + static_cast<size_t>(past + m) * kHeadDim;
 #pragma unroll
             for (int i = 0; i < 4; ++i)
@@ -216,109 +269,207 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const AttnArgs a)
                 dst[lane + 32 * i] = to_f32<KT>(q);
             }
         }
-        else
-        {
-            const float* vsrc = src + kQWidth + kKVWidth + g * kHeadDim;
-            KT* vrow = const_cast<KT*>(vbase) + static_cast<size_t>(past + m) * kHeadDim;
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-            {
-                const KT q = from_f32<KT>(vsrc[lane + 32 * i]);
-                vrow[lane + 32 * i] = q;
-                dst[lane + 32 * i] = to_f32<KT>(q);
-            }
-        }
     }
     attn_consumers_sync();
     pdl_launch();
 
-    // Lane roles.
-    const int qr = lane & 3;
-    int qi, stream;
-    if (MT == 1)
+    if constexpr (MT == 16)
     {
-        qi = (lane >> 2) & 1;
-        stream = warp * 4 + (lane >> 3);
+        // 32 queries (16 rows x 2 heads), key-stationary: warp w takes query
+        // half w & 1 (16 queries) and position group w >> 1 (positions
+        // 8 pg .. 8 pg + 7 of every 32-position stage); lane = (query, dim
+        // half): query 16 * (w & 1) + lane / 2 and dims 8 i + 4 h (i < 16,
+        // h = lane & 1), so a K/V read is two 16-byte broadcasts in
+        // different banks and a score needs one shuffle. Positions go in
+        // blocks of 8: one rescale of the running state per block.
+        const int h = lane & 1;
+        const int qi = (warp & 1) * 16 + (lane >> 1);
+        const int stream = warp >> 1;
+        const int qm = qi % MT;
+        float4 qv[16], ov[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+        {
+            qv[i] = *reinterpret_cast<const float4*>(qs + qi * kHeadDim + 8 * i + 4 * h);
+            ov[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        float mx = -INFINITY, l = 0.f;
+        // Up to 8 positions: rows krow0 + j*kHeadDim for j < nv; position j is
+        // visible to this lane's query iff vis(j).
+        auto block8 = [&](const auto* kb, const auto* vb, int nv, auto vis) {
+            float sc[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+            {
+                float a0 = 0.f, a1 = 0.f;
+                if (j < nv)
+                {
+#pragma unroll
+                    for (int i = 0; i < 16; i += 2)
+                    {
+                        a0 += dot4(qv[i], load4(kb + j * kHeadDim + 8 * i + 4 * h));
+                        a1 += dot4(qv[i + 1], load4(kb + j * kHeadDim + 8 * (i + 1) + 4 * h));
+                    }
+                }
+                sc[j] = a0 + a1;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) sc[j] += __shfl_xor_sync(0xffffffffu, sc[j], 1);
+            float mb = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (j < nv && vis(j)) mb = fmaxf(mb, sc[j]);
+            if (mb == -INFINITY) return;   // nothing visible to this query in the block
+            const float mn = fmaxf(mx, mb);
+            const float corr = (mx == -INFINITY) ? 0.f : exp2f(mx - mn);
+            l *= corr;
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+            {
+                ov[i].x *= corr; ov[i].y *= corr; ov[i].z *= corr; ov[i].w *= corr;
+            }
+            mx = mn;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+            {
+                if (j < nv && vis(j))
+                {
+                    const float pe = exp2f(sc[j] - mn);
+                    l += pe;
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                    {
+                        const float4 vv = load4(vb + j * kHeadDim + 8 * i + 4 * h);
+                        ov[i].x += pe * vv.x; ov[i].y += pe * vv.y; ov[i].z += pe * vv.z; ov[i].w += pe * vv.w;
+                    }
+                }
+            }
+        };
+        for (int i = 0; i < nstage; ++i)
+        {
+            const int slot = i % kAttnStages;
+            const bool ok = mbar_wait(&full[slot], (i / kAttnStages) & 1, a.err, kErrTimeoutFull);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            const KT* kst = reinterpret_cast<const KT*>(ring + slot * STAGE);
+            const KT* vst = reinterpret_cast<const KT*>(ring + slot * STAGE + kAttnPos * ROWB);
+            const int n = min(kAttnPos, npos - i * kAttnPos);
+            const int j0 = 8 * stream;
+            if (j0 < n)
+                block8(kst + j0 * kHeadDim, vst + j0 * kHeadDim, min(8, n - j0), [](int) { return true; });
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        // New rows (causal inside the block: row m sees new row j iff j <= m);
+        // position group pg takes new rows 4 pg .. 4 pg + 3.
+        if (new_split)
+        {
+            const int j0 = 4 * stream;
+            if (j0 < rows)
+                block8(knew + j0 * kHeadDim, vnew + j0 * kHeadDim, min(4, rows - j0),
+                       [&](int j) { return j0 + j <= qm; });
+        }
+        // Per-stream states to shared memory (aliasing the drained ring).
+        attn_consumers_sync();
+        if (h == 0)
+        {
+            scr_ml[(stream * NQ + qi) * 2 + 0] = mx;
+            scr_ml[(stream * NQ + qi) * 2 + 1] = l;
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+            *reinterpret_cast<float4*>(scr_acc + (stream * NQ + qi) * kHeadDim + 8 * i + 4 * h) = ov[i];
+        attn_consumers_sync();
     }
     else
     {
-        qi = (warp & 3) * 8 + (lane >> 2);
-        stream = warp >> 2;
-    }
-    const int qm = qi % MT;   // query row of this lane's query
-    float4 q4[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) q4[j] = *reinterpret_cast<const float4*>(qs + qi * kHeadDim + 4 * (qr + 4 * j));
-    float mx = -INFINITY, l = 0.f;
-    float4 acc[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        // Lane roles.
+        const int qr = lane & 3;
+        int qi, stream;
+        if (MT == 1)
+        {
+            qi = (lane >> 2) & 1;
+            stream = warp * 4 + (lane >> 3);
+        }
+        else
+        {
+            qi = (warp & 3) * 8 + (lane >> 2);
+            stream = warp >> 2;
+        }
+        const int qm = qi % MT;   // query row of this lane's query
+        float4 q4[8];
+    #pragma unroll
+        for (int j = 0; j < 8; ++j) q4[j] = *reinterpret_cast<const float4*>(qs + qi * kHeadDim + 4 * (qr + 4 * j));
+        float mx = -INFINITY, l = 0.f;
+        float4 acc[8];
+    #pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
 
-    // One key position for this lane's query; every lane of the warp calls it
-    // the same number of times (the shuffles use the full mask).
-    auto visit = [&](const auto* krow, const auto* vrow, bool visible) {
-        float sc = 0.f;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) sc += dot4(q4[j], load4(krow + 4 * (qr + 4 * j)));
-        sc += __shfl_xor_sync(0xffffffffu, sc, 1);
-        sc += __shfl_xor_sync(0xffffffffu, sc, 2);
-        if (!visible) return;
-        const float mn = fmaxf(mx, sc);
-        const float corr = exp2f(mx - mn);
-        const float pe = exp2f(sc - mn);
-        l = l * corr + pe;
-#pragma unroll
+        // One key position for this lane's query; every lane of the warp calls it
+        // the same number of times (the shuffles use the full mask).
+        auto visit = [&](const auto* krow, const auto* vrow, bool visible) {
+            float sc = 0.f;
+    #pragma unroll
+            for (int j = 0; j < 8; ++j) sc += dot4(q4[j], load4(krow + 4 * (qr + 4 * j)));
+            sc += __shfl_xor_sync(0xffffffffu, sc, 1);
+            sc += __shfl_xor_sync(0xffffffffu, sc, 2);
+            if (!visible) return;
+            const float mn = fmaxf(mx, sc);
+            const float corr = exp2f(mx - mn);
+            const float pe = exp2f(sc - mn);
+            l = l * corr + pe;
+    #pragma unroll
+            for (int j = 0; j < 8; ++j)
+            {
+                const float4 vv = load4(vrow + 4 * (qr + 4 * j));
+                acc[j].x = acc[j].x * corr + pe * vv.x;
+                acc[j].y = acc[j].y * corr + pe * vv.y;
+                acc[j].z = acc[j].z * corr + pe * vv.z;
+                acc[j].w = acc[j].w * corr + pe * vv.w;
+            }
+            mx = mn;
+        };
+
+        // Past rows from the ring.
+        for (int i = 0; i < nstage; ++i)
+        {
+            const int slot = i % kAttnStages;
+            const bool ok = mbar_wait(&full[slot], (i / kAttnStages) & 1, a.err, kErrTimeoutFull);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            const KT* kst = reinterpret_cast<const KT*>(ring + slot * STAGE);
+            const KT* vst = reinterpret_cast<const KT*>(ring + slot * STAGE + kAttnPos * ROWB);
+            const int n = min(kAttnPos, npos - i * kAttnPos);
+            for (int jb = 0; jb < n; jb += NSTREAM)
+            {
+                const int j = jb + stream;
+                const int jj = (j < n) ? j : 0;
+                visit(kst + jj * kHeadDim, vst + jj * kHeadDim, j < n);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        // New rows (causal inside the block: row m sees new row j iff j <= m).
+        if (new_split)
+        {
+            for (int jb = 0; jb < rows; jb += NSTREAM)
+            {
+                const int j = jb + stream;
+                const int jj = (j < rows) ? j : 0;
+                visit(knew + jj * kHeadDim, vnew + jj * kHeadDim, j < rows && j <= qm);
+            }
+        }
+
+        // Per-stream states to shared memory (aliasing the drained ring).
+        attn_consumers_sync();
+        if (qr == 0)
+        {
+            scr_ml[(stream * NQ + qi) * 2 + 0] = mx;
+            scr_ml[(stream * NQ + qi) * 2 + 1] = l;
+        }
+    #pragma unroll
         for (int j = 0; j < 8; ++j)
-        {
-            const float4 vv = load4(vrow + 4 * (qr + 4 * j));
-            acc[j].x = acc[j].x * corr + pe * vv.x;
-            acc[j].y = acc[j].y * corr + pe * vv.y;
-            acc[j].z = acc[j].z * corr + pe * vv.z;
-            acc[j].w = acc[j].w * corr + pe * vv.w;
-        }
-        mx = mn;
-    };
-
-    // Past rows from the ring.
-    for (int i = 0; i < nstage; ++i)
-    {
-        const int slot = i % kAttnStages;
-        const bool ok = mbar_wait(&full[slot], (i / kAttnStages) & 1, a.err, kErrTimeoutFull);
-        if (!__all_sync(0xffffffffu, ok)) break;
-        const KT* kst = reinterpret_cast<const KT*>(ring + slot * STAGE);
-        const KT* vst = reinterpret_cast<const KT*>(ring + slot * STAGE + kAttnPos * ROWB);
-        const int n = min(kAttnPos, npos - i * kAttnPos);
-        for (int jb = 0; jb < n; jb += NSTREAM)
-        {
-            const int j = jb + stream;
-            const int jj = (j < n) ? j : 0;
-            visit(kst + jj * kHeadDim, vst + jj * kHeadDim, j < n);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
+            *reinterpret_cast<float4*>(scr_acc + (stream * NQ + qi) * kHeadDim + 4 * (qr + 4 * j)) = acc[j];
+        attn_consumers_sync();
     }
-    // New rows (causal inside the block: row m sees new row j iff j <= m).
-    if (new_split)
-    {
-        for (int jb = 0; jb < rows; jb += NSTREAM)
-        {
-            const int j = jb + stream;
-            const int jj = (j < rows) ? j : 0;
-            visit(knew + jj * kHeadDim, vnew + jj * kHeadDim, j < rows && j <= qm);
-        }
-    }
-
-    // Per-stream states to shared memory (aliasing the drained ring).
-    attn_consumers_sync();
-    if (qr == 0)
-    {
-        scr_ml[(stream * NQ + qi) * 2 + 0] = mx;
-        scr_ml[(stream * NQ + qi) * 2 + 1] = l;
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-        *reinterpret_cast<float4*>(scr_acc + (stream * NQ + qi) * kHeadDim + 4 * (qr + 4 * j)) = acc[j];
-    attn_consumers_sync();
 
     // CTA partial per query.
     float* part = a.part + (static_cast<size_t>(g) * nsplit + split) * NQ * kPartStride;
@@ -353,26 +504,56 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_kernel(const AttnArgs a)
     if (!s_last) return;
     __threadfence();
 
-    // Last CTA of this head: merge the S partials.
+    // Last CTA of this head: merge the S partials. First the (max, sum) of
+    // every split and query, the merged max / sum and each split's weight (in
+    // the drained ring), then the accumulators, every split's float4 of an
+    // output in flight at once.
     const float* hp = a.part + static_cast<size_t>(g) * nsplit * NQ * kPartStride;
-    for (int e = tid; e < NQ * kHeadDim; e += 256)
+    float* mw = reinterpret_cast<float*>(ring);   // [nsplit][NQ] split max -> weight
+    float* ls = mw + nsplit * NQ;                 // [nsplit][NQ] split sum
+    float* inv_l = ls + nsplit * NQ;              // [NQ] 1 / merged sum
+    for (int e = tid; e < nsplit * NQ; e += 256)
     {
-        const int q = e / kHeadDim, d = e % kHeadDim;
+        mw[e] = __ldcg(hp + e * kPartStride);
+        ls[e] = __ldcg(hp + e * kPartStride + 1);
+    }
+    attn_consumers_sync();
+    for (int q = tid; q < NQ; q += 256)
+    {
+        float M = -INFINITY;
+        for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, mw[sp * NQ + q]);
+        float L = 0.f;
+        for (int sp = 0; sp < nsplit; ++sp)
+        {
+            const float ms = mw[sp * NQ + q];
+            const float f = (ms == -INFINITY) ? 0.f : exp2f(ms - M);
+            mw[sp * NQ + q] = f;
+            L += f * ls[sp * NQ + q];
+        }
+        inv_l[q] = 1.0f / L;
+    }
+    attn_consumers_sync();
+    constexpr int kMaxS = 20;
+    for (int e = tid; e < NQ * (kHeadDim / 4); e += 256)
+    {
+        const int q = e / (kHeadDim / 4), d4 = e % (kHeadDim / 4);
         const int m = q % MT, head = q / MT;
         if (m >= rows) continue;
-        float M = -INFINITY;
-        for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(hp + (s * NQ + q) * kPartStride));
-        float L = 0.f, A = 0.f;
-        for (int s = 0; s < nsplit; ++s)
+        float4 v[kMaxS];
+#pragma unroll
+        for (int sp = 0; sp < kMaxS; ++sp)
+            if (sp < nsplit) v[sp] = __ldcg(reinterpret_cast<const float4*>(hp + (sp * NQ + q) * kPartStride + 4) + d4);
+        float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int sp = 0; sp < kMaxS; ++sp)
         {
-            const float* ps = hp + (s * NQ + q) * kPartStride;
-            const float ms = __ldcg(ps);
-            if (ms == -INFINITY) continue;
-            const float f = exp2f(ms - M);
-            L += f * __ldcg(ps + 1);
-            A += f * __ldcg(ps + 4 + d);
+            if (sp >= nsplit) break;
+            const float f = mw[sp * NQ + q];
+            A.x += f * v[sp].x; A.y += f * v[sp].y; A.z += f * v[sp].z; A.w += f * v[sp].w;
         }
-        a.out[static_cast<size_t>(m) * kQWidth + (2 * g + head) * kHeadDim + d] = A / L;
+        const float il = inv_l[q];
+        A.x *= il; A.y *= il; A.z *= il; A.w *= il;
+        *reinterpret_cast<float4*>(a.out + static_cast<size_t>(m) * kQWidth + (2 * g + head) * kHeadDim + 4 * d4) = A;
     }
     if (tid == 0) a.counter[g] = 0;
 }

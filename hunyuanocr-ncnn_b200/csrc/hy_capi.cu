@@ -43,7 +43,7 @@ int fail(int code, const std::string& msg)
 
 constexpr int kFfn = 3584;                // kernels are specialised for the model's FFN width
 constexpr int kAttnSplitsAR = 19;         // 18 past splits + the new-row split (152 CTAs)
-constexpr int kAttnSplitsVerify = 10;
+constexpr int kAttnSplitsVerify = 18;         // 17 past splits + the new-row split (144 CTAs, one per SM)
 constexpr int kMaxSplits = 20;
 constexpr int kArStepsPerGraph = 4;
 constexpr int kMegaChunk = 64;            // tokens per persistent-kernel launch
@@ -84,6 +84,7 @@ struct hy_ctx {
     float* attn = nullptr;      // [16 x 2048]
     float* gu = nullptr;        // [16 x 2 ffn]
     float* tmp = nullptr;       // [16 x 1024]
+    float* act = nullptr;       // [16 x ffn] silu(gate) * up of 16-row steps
     float* hidden = nullptr;    // [16 x 1024]
     float* aux = nullptr;       // [4 x 16 x 1024]
     float* attn_part = nullptr;
@@ -325,9 +326,19 @@ cudaError_t enqueue_step_t(hy_ctx* c, const StepPlan& p)
         gu.x = c->x;
         gu.ldx = kHidden;
         gu.norm_w = c->post_norm(l);
-        gu.out = c->gu;
-        gu.ldo = 2 * ffn;
-        if ((e = run_gemv<WT, kHidden, MT, PRO_NORM, EPI_STORE>(c, gu)) != cudaSuccess) return e;
+        if constexpr (MT == 1)
+        {
+            gu.out = c->gu;
+            gu.ldo = 2 * ffn;
+            if ((e = run_gemv<WT, kHidden, MT, PRO_NORM, EPI_STORE>(c, gu)) != cudaSuccess) return e;
+        }
+        else
+        {
+            // 16 rows: the epilogue applies SwiGLU (act = silu(gate) * up).
+            gu.out = c->act;
+            gu.ldo = ffn;
+            if ((e = run_gemv<WT, kHidden, MT, PRO_NORM, EPI_ACT>(c, gu)) != cudaSuccess) return e;
+        }
 
         float* aux = nullptr;
         if (p.aux)
@@ -351,12 +362,15 @@ cudaError_t enqueue_step_t(hy_ctx* c, const StepPlan& p)
         }
         else
         {
-            // K split in two halves so the 16 activation rows fit in shared memory.
+            // K split in two halves so the 16 activation rows fit in shared memory;
+            // the inputs are the act rows of the gate/up step.
+            d.x = c->act;
+            d.ldx = ffn;
             GemvArgs d1 = d;
             d1.k_off = 0;
             d1.out = c->tmp;
             d1.ldo = kHidden;
-            if ((e = run_gemv<WT, kFfn / 2, MT, PRO_SWIGLU, EPI_STORE>(c, d1)) != cudaSuccess) return e;
+            if ((e = run_gemv<WT, kFfn / 2, MT, PRO_PLAIN, EPI_STORE>(c, d1)) != cudaSuccess) return e;
             GemvArgs d2 = d;
             d2.k_off = kFfn / 2;
             d2.out = c->x;
@@ -364,7 +378,7 @@ cudaError_t enqueue_step_t(hy_ctx* c, const StepPlan& p)
             d2.extra = c->tmp;
             d2.aux = aux;
             d2.ld_aux = kHidden;
-            if ((e = run_gemv<WT, kFfn / 2, MT, PRO_SWIGLU, EPI_RESID>(c, d2)) != cudaSuccess) return e;
+            if ((e = run_gemv<WT, kFfn / 2, MT, PRO_PLAIN, EPI_RESID>(c, d2)) != cudaSuccess) return e;
         }
     }
     if (p.lm_mode >= 0)
@@ -749,6 +763,7 @@ int alloc_ctx(hy_ctx* c)
     if ((rc = dalloc(c, &c->attn, kMaxStepRows * kQWidth))) return rc;
     if ((rc = dalloc(c, &c->gu, static_cast<size_t>(kMaxStepRows) * 2 * ffn))) return rc;
     if ((rc = dalloc(c, &c->tmp, kMaxStepRows * kHidden))) return rc;
+    if ((rc = dalloc(c, &c->act, static_cast<size_t>(kMaxStepRows) * cfg.ffn_dim))) return rc;
     if ((rc = dalloc(c, &c->hidden, kMaxStepRows * kHidden))) return rc;
     if ((rc = dalloc(c, &c->aux, static_cast<size_t>(kAuxLayers) * kMaxStepRows * kHidden))) return rc;
     if ((rc = dalloc(c, &c->attn_part, static_cast<size_t>(kNumKVHeads) * kMaxSplits * 2 * kMaxStepRows * kPartStride)))

@@ -145,6 +145,15 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
+// Bulk global->shared copy with the default L2 policy (for data other CTAs read too).
+__device__ __forceinline__ void bulk_g2s_plain(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
 // Bulk prefetch of global memory into L2 (no destination, no completion).
 // src and bytes must be 16-byte aligned.
 __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes)

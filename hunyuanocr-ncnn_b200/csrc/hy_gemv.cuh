@@ -27,7 +27,7 @@
 namespace hy {
 
 enum { PRO_PLAIN = 0, PRO_NORM = 1, PRO_SWIGLU = 2 };
-enum { EPI_STORE = 0, EPI_RESID = 1, EPI_ARGMAX = 2 };
+enum { EPI_STORE = 0, EPI_RESID = 1, EPI_ARGMAX = 2, EPI_ACT = 3 };   // EPI_ACT: M = 16 only
 enum { SRC_X = 0, SRC_GATHER_STATE = 1, SRC_GATHER_IDS = 2, SRC_GATHER_DRAFT = 3 };
 enum { LM_NONE = 0, LM_AR = 1, LM_VERIFY = 2 };
 
@@ -93,6 +93,36 @@ struct GemvShape {
     static constexpr int SMEM = RED_OFF + RED_BYTES;
 };
 
+// M = 16 (DFlash verify blocks, prefill chunks): a stage holds RPL whole
+// weight rows (<= 16 KB, one contiguous copy when the rows are contiguous) and
+// belongs to one consumer warp (stage i -> warp i % 8). In it, lane (r, s) =
+// (lane % RPL, lane / RPL) owns row r and columns 4 (SUBS j + s) .. + 3 and
+// multiplies each weight float4 by the 16 activation rows. One instruction
+// reads RPL rows x SUBS consecutive float4s: one 128-byte line per row, which
+// is the minimum number of shared-memory wavefronts, and each activation read
+// is one broadcast line. The SUBS partial sums of a row are added with
+// shuffles at the end of the stage.
+template <typename WT, int KP>
+struct GemvShape<WT, KP, 16> {
+    static constexpr int SEG = KP * static_cast<int>(sizeof(WT));
+    static constexpr int RPL = (SEG <= 4096) ? 4 : 2;   // rows per stage (and per warp step)
+    static constexpr int SUBS = 32 / RPL;
+    static constexpr int SPS = RPL;
+    static constexpr int STAGE = RPL * SEG;
+    static constexpr int RPW = RPL, GPS = 1;
+    static constexpr int XS_BYTES = 16 * KP * 4;
+    static constexpr int WSCR_BYTES = kGemvWarps * 16 * 16 * 4;  // per-warp [row][m]
+    static constexpr int RED_BYTES = (kGemvWarps * 16 + 16) * 16 + 16;
+    static constexpr int NST_FIT = (kSmemBudget - XS_BYTES - WSCR_BYTES - RED_BYTES - 512) / STAGE;
+    static constexpr int NST = NST_FIT < 8 ? NST_FIT : 8;
+    static constexpr int WSCR_OFF = XS_BYTES + NST * STAGE;
+    static constexpr int BAR_OFF = WSCR_OFF + WSCR_BYTES;
+    static constexpr int RED_OFF = BAR_OFF + 2 * NST * 8;
+    static constexpr int SMEM = RED_OFF + RED_BYTES;
+    static_assert(STAGE <= 16384, "a stage is at most 16 KB");
+    static_assert(KP % (4 * SUBS) == 0, "K slice must be a multiple of a warp step");
+};
+
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 struct ArgBest {
@@ -145,11 +175,14 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, b = blockIdx.x;
-    const int r0 = static_cast<int>(static_cast<long long>(a.N) * b / G);
-    const int r1 = static_cast<int>(static_cast<long long>(a.N) * (b + 1) / G);
+    // EPI_ACT pairs rows (2j = gate_j, 2j+1 = up_j): split the rows by pairs.
+    const int unit = (EPI == EPI_ACT) ? 2 : 1;
+    const int r0 = unit * static_cast<int>(static_cast<long long>(a.N / unit) * b / G);
+    const int r1 = unit * static_cast<int>(static_cast<long long>(a.N / unit) * (b + 1) / G);
     const int R = r1 - r0;
     const int nstage = (R + SPS - 1) / SPS;
 
+    __shared__ uint64_t s_xbar;   // M = 16: bulk copy of the activation rows
     if (tid == 0)
     {
         for (int s = 0; s < NST; ++s)
@@ -157,6 +190,7 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kGemvWarps);
         }
+        mbar_init(&s_xbar, 1);
         fence_mbar_init();
     }
     __syncthreads();
@@ -173,10 +207,10 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
             {
                 const int slot = i % NST;
                 if (i >= NST && !mbar_wait(&empty[slot], ((i / NST) - 1) & 1, a.err, kErrTimeoutEmpty)) break;
+                unsigned char* dst = ring + slot * STAGE;
                 const int sr0 = r0 + i * SPS;
                 const int nseg = min(SPS, r1 - sr0);
                 mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(nseg * SEG));
-                unsigned char* dst = ring + slot * STAGE;
                 if (a.ldw == KP)
                 {
                     bulk_g2s(dst, W + static_cast<size_t>(sr0) * KP, static_cast<uint32_t>(nseg * SEG), &full[slot], pol);
@@ -228,6 +262,70 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
     consumers_sync();
 
     // Stage the activation rows (fp32) in shared memory.
+    if constexpr (MT == 16)
+    {
+        // Batches of rows with every load of a batch in flight before its
+        // stores (one L2 round trip per batch instead of per row).
+        constexpr int KI = (KP + 1023) / 1024;            // float4 columns per thread and row
+        constexpr int B = 8;                              // rows per batch
+        const bool bulk = (a.src == SRC_X && PRO != PRO_SWIGLU);
+        if (bulk)
+        {
+            // Plain / normed rows: one bulk copy per row, the padding rows zeroed.
+            if (tid == 0)
+            {
+                mbar_arrive_expect_tx(&s_xbar, static_cast<uint32_t>(rows * KP * 4));
+                for (int m = 0; m < rows; ++m)
+                    bulk_g2s_plain(xs + m * KP, a.x + static_cast<size_t>(m) * a.ldx + a.k_off, KP * 4, &s_xbar);
+            }
+            for (int i = tid; i < (MT - rows) * (KP / 4); i += 256)
+                reinterpret_cast<float4*>(xs + rows * KP)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            mbar_wait(&s_xbar, 0, a.err, kErrTimeoutFull);
+        }
+        for (int m0 = 0; m0 < MT && !bulk; m0 += B)
+        {
+            float4 p0[B][KI], p1[B][KI];
+#pragma unroll
+            for (int mm = 0; mm < B; ++mm)
+#pragma unroll
+                for (int i = 0; i < KI; ++i)
+                {
+                    const int m = m0 + mm, k = tid * 4 + 1024 * i;
+                    p0[mm][i] = p1[mm][i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (m >= rows || k >= KP) continue;
+                    if (a.src != SRC_X)
+                        p0[mm][i] = load4(static_cast<const WT*>(a.table) + static_cast<size_t>(s_ids[m]) * kHidden + k);
+                    else if (PRO == PRO_SWIGLU)
+                    {
+                        const float* gu = a.x + static_cast<size_t>(m) * a.ldx + 2 * a.k_off;
+                        p0[mm][i] = *reinterpret_cast<const float4*>(gu + 2 * k);
+                        p1[mm][i] = *reinterpret_cast<const float4*>(gu + 2 * k + 4);
+                    }
+                    else
+                        p0[mm][i] = *reinterpret_cast<const float4*>(a.x + static_cast<size_t>(m) * a.ldx + a.k_off + k);
+                }
+#pragma unroll
+            for (int mm = 0; mm < B; ++mm)
+#pragma unroll
+                for (int i = 0; i < KI; ++i)
+                {
+                    const int m = m0 + mm, k = tid * 4 + 1024 * i;
+                    if (k >= KP) continue;
+                    float4 r = p0[mm][i];
+                    if (a.src == SRC_X && PRO == PRO_SWIGLU && m < rows)
+                    {
+                        // act_k = silu(gate_k) * up_k; the gate/up projection rows are interleaved.
+                        const float4 q0 = p0[mm][i], q1 = p1[mm][i];
+                        r.x = (q0.x / (1.0f + expf(-q0.x))) * q0.y;
+                        r.y = (q0.z / (1.0f + expf(-q0.z))) * q0.w;
+                        r.z = (q1.x / (1.0f + expf(-q1.x))) * q1.y;
+                        r.w = (q1.z / (1.0f + expf(-q1.z))) * q1.w;
+                    }
+                    *reinterpret_cast<float4*>(xs + m * KP + k) = r;
+                }
+        }
+    }
+    else
     for (int m = 0; m < MT; ++m)
     {
         float* xr = xs + m * KP;
@@ -279,7 +377,36 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
         for (int i = beg + tid; i < end; i += 256) a.x_store[i] = xs[(i / kHidden) * KP + (i % kHidden)];
     }
 
-    if (PRO == PRO_NORM)
+    if (PRO == PRO_NORM && MT == 16)
+    {
+        // Per-row 1/sqrt(mean(x^2) + eps) (warp w: rows w and w + 8), then xs = w * (x * rinv).
+        for (int m = warp; m < MT; m += kGemvWarps)
+        {
+            float ss = 0.f;
+            for (int k = lane * 4; k < KP; k += 128)
+            {
+                const float4 v = *reinterpret_cast<const float4*>(xs + m * KP + k);
+                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+            }
+            ss = warp_sum(ss);
+            if (lane == 0) s_rinv[m] = 1.0f / sqrtf(ss / static_cast<float>(KP) + a.eps);
+        }
+        consumers_sync();
+        for (int i = tid; i < rows * (KP / 4); i += 256)
+        {
+            const int m = i / (KP / 4), k = 4 * (i % (KP / 4));
+            const float ri = s_rinv[m];
+            float4 v = *reinterpret_cast<float4*>(xs + m * KP + k);
+            const float4 w = *reinterpret_cast<const float4*>(a.norm_w + a.k_off + k);
+            v.x = w.x * (v.x * ri);
+            v.y = w.y * (v.y * ri);
+            v.z = w.z * (v.z * ri);
+            v.w = w.w * (v.w * ri);
+            *reinterpret_cast<float4*>(xs + m * KP + k) = v;
+        }
+        consumers_sync();
+    }
+    else if (PRO == PRO_NORM)
     {
         // Per-row 1/sqrt(mean(x^2) + eps), then xs = w * (x * rinv).
         float* wsum = reinterpret_cast<float*>(red4);   // [8 warps][MT]
@@ -330,92 +457,191 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
     // computes it before arriving. (An mbarrier parity wait is only meaningful
     // one phase ahead, so no warp may skip past a stage that has not landed, nor
     // let a slot be reused before it has seen it.)
-    const int ngroups = (R + RPW - 1) / RPW;
-    int gi = warp;   // next group this warp owns
-    for (int stage = 0; stage < nstage; ++stage)
+    if constexpr (MT == 16)
     {
-        const int slot = stage % NST;
-        const bool ok = mbar_wait(&full[slot], (stage / NST) & 1, a.err, kErrTimeoutFull);
-        if (!__all_sync(0xffffffffu, ok)) break;
-        const int seg0 = gi * RPW;
-        const bool mine = gi < ngroups && seg0 < (stage + 1) * SPS;   // at most one group per warp per stage
-        const int nr = mine ? min(RPW, R - seg0) : 0;
-        float acc[RPW][MT];
-#pragma unroll
-        for (int r = 0; r < RPW; ++r)
-#pragma unroll
-            for (int m = 0; m < MT; ++m) acc[r][m] = 0.f;
-        if (mine)
-        {
-            const WT* wrow = reinterpret_cast<const WT*>(ring + slot * STAGE + (seg0 % SPS) * SEG);
-#pragma unroll 4
-            for (int c = lane; c < KP / 4; c += 32)
+        constexpr int RPL = S::RPL, SUBS = S::SUBS;
+        float* wscr = reinterpret_cast<float*>(smem + S::WSCR_OFF) + warp * 256;   // [row][m]
+        const int rr = lane % RPL, sub = lane / RPL;
+        // Store / residual / argmax epilogue of one output (row n of activation row m).
+        auto emit = [&](int m, int n, float v) {
+            if (EPI == EPI_STORE || EPI == EPI_RESID)
             {
-                float4 w[RPW];
-#pragma unroll
-                for (int r = 0; r < RPW; ++r)
-                    w[r] = (r < nr) ? load4(wrow + r * KP + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                for (int m = 0; m < MT; ++m)
+                const size_t o = static_cast<size_t>(m) * a.ldo + n;
+                if (EPI == EPI_RESID)
                 {
-                    const float4 xv = *reinterpret_cast<const float4*>(xs + m * KP + 4 * c);
+                    if (a.extra) v = a.extra[o] + v;
+                    v = a.out[o] + v;
+                    if (a.aux) a.aux[static_cast<size_t>(m) * a.ld_aux + n] = v;
+                }
+                a.out[o] = v;
+            }
+            else
+            {
+                if (a.logits) a.logits[static_cast<size_t>(m) * a.ldl + n] = v;
+                bool hit = (a.hist[n >> 5] >> (n & 31)) & 1u;
+                for (int j = 0; j <= m; ++j) hit |= (s_prefix[j] == n);
+                const float ps = hit ? (v < 0.0f ? v * pen : v / pen) : v;
+                if (best.ri < 0 || v > best.rv) { best.rv = v; best.ri = n; }
+                if (best.pi < 0 || ps > best.pv) { best.pv = ps; best.pi = n; }
+            }
+        };
+        // Every consumer warp observes every stage in order and arrives once on it.
+        for (int stage = 0; stage < nstage; ++stage)
+        {
+            const int slot = stage % NST;
+            const bool ok = mbar_wait(&full[slot], (stage / NST) & 1, a.err, kErrTimeoutFull);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            const bool mine = (stage % kGemvWarps) == warp;
+            float acc[16];
+            if (mine)
+            {
 #pragma unroll
-                    for (int r = 0; r < RPW; ++r) acc[r][m] += dot4(w[r], xv);
+                for (int m = 0; m < 16; ++m) acc[m] = 0.f;
+                const WT* wrow = reinterpret_cast<const WT*>(ring + slot * STAGE + rr * SEG);
+                const float* xb = xs + 4 * sub;
+#pragma unroll 2
+                for (int j = 0; j < KP / (4 * SUBS); ++j)
+                {
+                    const float4 w = load4(wrow + 4 * (SUBS * j + sub));
+#pragma unroll
+                    for (int m = 0; m < 16; ++m)
+                        acc[m] += dot4(w, *reinterpret_cast<const float4*>(xb + m * KP + 4 * SUBS * j));
                 }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (!mine) continue;
+            // Add the SUBS partial sums of each row: lanes 0 .. RPL-1 hold the totals.
 #pragma unroll
-            for (int r = 0; r < RPW; ++r)
+            for (int o = RPL; o < 32; o <<= 1)
 #pragma unroll
-                for (int m = 0; m < MT; ++m) acc[r][m] = warp_sum(acc[r][m]);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
-        if (!mine) continue;
-        gi += kGemvWarps;
-
-        const int n0 = r0 + seg0;
-        if (EPI == EPI_STORE || EPI == EPI_RESID)
-        {
+                for (int m = 0; m < 16; ++m) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+            const int n0 = r0 + stage * RPL;
+            const int nr = min(RPL, R - stage * RPL);
+            if (lane < RPL)
+            {
 #pragma unroll
-            for (int r = 0; r < RPW; ++r)
-#pragma unroll
-                for (int m = 0; m < MT; ++m)
+                for (int m = 0; m < 16; ++m) wscr[lane * 16 + m] = acc[m];
+            }
+            __syncwarp();
+            if (EPI == EPI_ARGMAX)
+            {
+                if (lane < rows)
+                    for (int row = 0; row < nr; ++row) emit(lane, n0 + row, wscr[row * 16 + lane]);
+            }
+            else if (EPI == EPI_ACT)
+            {
+                // act[m][j] = silu(gate_j) * up_j for the row pairs of the stage (n0 is even).
+                for (int p = lane; p < 16 * (RPL / 2); p += 32)
                 {
-                    if (lane == ((r * MT + m) & 31) && r < nr && m < rows)
+                    const int m = p / (RPL / 2), pr = p % (RPL / 2);
+                    if (2 * pr + 1 < nr && m < rows)
                     {
-                        const size_t o = static_cast<size_t>(m) * a.ldo + (n0 + r);
-                        float v = acc[r][m];
-                        if (EPI == EPI_RESID)
-                        {
-                            if (a.extra) v = a.extra[o] + v;
-                            v = a.out[o] + v;
-                            if (a.aux) a.aux[static_cast<size_t>(m) * a.ld_aux + (n0 + r)] = v;
-                        }
-                        a.out[o] = v;
+                        const float gt = wscr[(2 * pr) * 16 + m], up = wscr[(2 * pr + 1) * 16 + m];
+                        a.out[static_cast<size_t>(m) * a.ldo + ((n0 >> 1) + pr)] = (gt / (1.0f + expf(-gt))) * up;
                     }
                 }
-        }
-        else
-        {
-            // Penalised argmax: lane m tracks activation row m.
-#pragma unroll
-            for (int r = 0; r < RPW; ++r)
+            }
+            else
             {
-                if (r >= nr) break;
-                const int v = n0 + r;
-                const bool in_hist = (a.hist[v >> 5] >> (v & 31)) & 1u;
-#pragma unroll
-                for (int m = 0; m < MT; ++m)
+                for (int p = lane; p < 16 * RPL; p += 32)
                 {
-                    if (lane == m && m < rows)
+                    const int m = p / RPL, row = p % RPL;
+                    if (row < nr && m < rows) emit(m, n0 + row, wscr[row * 16 + m]);
+                }
+            }
+            __syncwarp();
+        }
+    }
+    else
+    {
+        const int ngroups = (R + RPW - 1) / RPW;
+        int gi = warp;   // next group this warp owns
+        for (int stage = 0; stage < nstage; ++stage)
+        {
+            const int slot = stage % NST;
+            const bool ok = mbar_wait(&full[slot], (stage / NST) & 1, a.err, kErrTimeoutFull);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            const int seg0 = gi * RPW;
+            const bool mine = gi < ngroups && seg0 < (stage + 1) * SPS;   // at most one group per warp per stage
+            const int nr = mine ? min(RPW, R - seg0) : 0;
+            float acc[RPW][MT];
+    #pragma unroll
+            for (int r = 0; r < RPW; ++r)
+    #pragma unroll
+                for (int m = 0; m < MT; ++m) acc[r][m] = 0.f;
+            if (mine)
+            {
+                const WT* wrow = reinterpret_cast<const WT*>(ring + slot * STAGE + (seg0 % SPS) * SEG);
+    #pragma unroll 4
+                for (int c = lane; c < KP / 4; c += 32)
+                {
+                    float4 w[RPW];
+    #pragma unroll
+                    for (int r = 0; r < RPW; ++r)
+                        w[r] = (r < nr) ? load4(wrow + r * KP + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    #pragma unroll
+                    for (int m = 0; m < MT; ++m)
                     {
-                        const float s = acc[r][m];
-                        if (a.logits) a.logits[static_cast<size_t>(m) * a.ldl + v] = s;
-                        bool hit = in_hist;
-                        for (int j = 0; j <= m; ++j) hit |= (s_prefix[j] == v);
-                        const float ps = hit ? (s < 0.0f ? s * pen : s / pen) : s;
-                        if (best.ri < 0 || s > best.rv) { best.rv = s; best.ri = v; }
-                        if (best.pi < 0 || ps > best.pv) { best.pv = ps; best.pi = v; }
+                        const float4 xv = *reinterpret_cast<const float4*>(xs + m * KP + 4 * c);
+    #pragma unroll
+                        for (int r = 0; r < RPW; ++r) acc[r][m] += dot4(w[r], xv);
+                    }
+                }
+    #pragma unroll
+                for (int r = 0; r < RPW; ++r)
+    #pragma unroll
+                    for (int m = 0; m < MT; ++m) acc[r][m] = warp_sum(acc[r][m]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (!mine) continue;
+            gi += kGemvWarps;
+
+            const int n0 = r0 + seg0;
+            if (EPI == EPI_STORE || EPI == EPI_RESID)
+            {
+    #pragma unroll
+                for (int r = 0; r < RPW; ++r)
+    #pragma unroll
+                    for (int m = 0; m < MT; ++m)
+                    {
+                        if (lane == ((r * MT + m) & 31) && r < nr && m < rows)
+                        {
+                            const size_t o = static_cast<size_t>(m) * a.ldo + (n0 + r);
+                            float v = acc[r][m];
+                            if (EPI == EPI_RESID)
+                            {
+                                if (a.extra) v = a.extra[o] + v;
+                                v = a.out[o] + v;
+                                if (a.aux) a.aux[static_cast<size_t>(m) * a.ld_aux + (n0 + r)] = v;
+                            }
+                            a.out[o] = v;
+                        }
+                    }
+            }
+            else
+            {
+                // Penalised argmax: lane m tracks activation row m.
+    #pragma unroll
+                for (int r = 0; r < RPW; ++r)
+                {
+                    if (r >= nr) break;
+                    const int v = n0 + r;
+                    const bool in_hist = (a.hist[v >> 5] >> (v & 31)) & 1u;
+    #pragma unroll
+                    for (int m = 0; m < MT; ++m)
+                    {
+                        if (lane == m && m < rows)
+                        {
+                            const float s = acc[r][m];
+                            if (a.logits) a.logits[static_cast<size_t>(m) * a.ldl + v] = s;
+                            bool hit = in_hist;
+                            for (int j = 0; j <= m; ++j) hit |= (s_prefix[j] == v);
+                            const float ps = hit ? (s < 0.0f ? s * pen : s / pen) : s;
+                            if (best.ri < 0 || s > best.rv) { best.rv = s; best.ri = v; }
+                            if (best.pi < 0 || ps > best.pv) { best.pv = ps; best.pi = v; }
+                        }
                     }
                 }
             }
