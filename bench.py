@@ -316,6 +316,91 @@ def run_b200(args, world, rank, local):
     }
 
 
+def load_batch_module():
+    import importlib.util
+    if "hy_b200_batch" in sys.modules:
+        return sys.modules["hy_b200_batch"]
+    spec = importlib.util.spec_from_file_location("hy_b200_batch", os.path.join(REPO, "hunyuanocr-ncnn_b200", "batch.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["hy_b200_batch"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def run_requests(args, world, rank, local):
+    """Config 4: `--requests` independent requests (prompt of request i seeded by i: 768
+    image rows + 256 text ids), `--req-tokens` generated tokens each, partitioned
+    round-robin across the ranks (one GPU each, full weight copy, no collective on the
+    data path). AR mode: the reference-facing call per request. DFlash mode: prefill
+    through the same call, then the on-device DFlash loop with synthetic drafts equal to
+    the request's greedy tokens with probability 0.7 (the greedy tokens come from an
+    untimed AR pass)."""
+    sys.path.insert(0, REPO)
+    import __graft_entry__ as ge
+    import torch
+    pkg = ge.load_package()
+    pkg.load_library()
+    batch = load_batch_module()
+    n_tok = args.req_tokens
+    seq = PROMPT_GRID[0] * PROMPT_GRID[1] + PROMPT_TEXT
+    rt = pkg.TextRuntime.synthetic(seed=0, device=local, max_prefill=seq, max_tokens=n_tok + 64,
+                                   max_context=seq + n_tok + 64)
+    prompts = {i: prompt_arrays(seed=i) for i in batch.partition(args.requests, world, rank)}
+    greedy = {}
+    if args.mode == "dflash":
+        for i, (ids, pos, feats, img) in prompts.items():
+            greedy[i] = rt.run_vlm_decode_with_prompt(ids, pos, img, feats, max_tokens=n_tok + 16).generated_tokens
+
+    def infer(i):
+        ids, pos, feats, img = prompts[i]
+        if args.mode == "ar":
+            return rt.run_vlm_decode_with_prompt(ids, pos, img, feats, max_tokens=n_tok).generated_tokens
+        first = rt.run_vlm_decode_with_prompt(ids, pos, img, feats, max_tokens=1).generated_tokens[0]
+        r = rt.dflash_generate_synthetic(first, n_tok, PENALTY, greedy[i], 0.7, seed=i)
+        if r.generated_tokens != greedy[i][:len(r.generated_tokens)]:
+            raise RuntimeError(f"request {i}: DFlash tokens differ from the AR tokens")
+        return r.generated_tokens
+
+    records = list(range(args.requests))
+    if prompts:
+        infer(next(iter(prompts)))   # warm-up (graphs, first-touch)
+    ext = torch.cuda.ExternalStream(rt.stream, device=local)
+    dist_barrier(world)
+    torch.cuda.synchronize(local)
+    with ClockSampler(local) as clocks:
+        t0 = time.perf_counter()
+        local_out, summary = batch.run_partition(records, infer, world=world, rank=rank)
+        torch.cuda.synchronize(local)
+        dt = time.perf_counter() - t0
+        dist_barrier(world)
+    dt_max = dist_max(dt, world)
+    merged, total = batch.gather_in_order(local_out, world, rank)
+    rt.close()
+    if rank != 0:
+        return None
+    tokens = sum(len(r.tokens) for r in merged)
+    return {
+        "metric": f"request throughput (config 4, {args.mode.upper()}, bs=1 per GPU)",
+        "value": round(tokens / dt_max, 2),
+        "unit": "tokens/s",
+        "requests_per_s": round(total.succeeded / dt_max, 3),
+        "n_gpus": world,
+        "steps": 1,
+        "warmup": 1,
+        "ms_per_step": round(dt_max * 1e3, 1),
+        "higher_is_better": True,
+        "scaling": "weak" if args.requests % world == 0 else "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded random-init weights; request i prompt seeded by i)",
+        "config": {"workload": f"config4: {args.requests} requests x ({seq} prompt + {n_tok} tokens), "
+                               f"round-robin over {world} GPU(s), {args.mode}",
+                   "parallelism": f"replicas x{world} (request-parallel, no collective)"},
+        "summary": {"total": total.total, "succeeded": total.succeeded, "failed": total.failed},
+        "clocks": clocks.summary(),
+    }
+
+
 def cpu_decode_sample(steps: int, threads: int | None = None):
     """Time the oracle's AR decode step at full size on a KV cache of 1024 rows."""
     import importlib.util
@@ -386,13 +471,18 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=16)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-dflash", action="store_true")
+    ap.add_argument("--workload", choices=["decode", "requests"], default="decode",
+                    help="decode: config 0 step (default); requests: config 4 request throughput")
+    ap.add_argument("--requests", type=int, default=64)
+    ap.add_argument("--req-tokens", type=int, default=512)
+    ap.add_argument("--mode", choices=["ar", "dflash"], default="ar")
     args = ap.parse_args()
     if args.impl == "reference":
         world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
         out = run_reference(args, world, rank)
     else:
         world, rank, local = dist_setup(args.gpus)
-        out = run_b200(args, world, rank, local)
+        out = run_requests(args, world, rank, local) if args.workload == "requests" else run_b200(args, world, rank, local)
         if world > 1:
             import torch.distributed as dist
             dist.destroy_process_group()

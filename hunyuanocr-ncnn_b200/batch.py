@@ -1,0 +1,95 @@
+"""Request-parallel batch decoding across GPUs (independent replicas).
+
+The reference's JSONL batch driver (src/batch_jsonl.cpp `run_jsonl_batch`,
+384-480; src/batch_jsonl.h:25-45) runs records sequentially through one
+`HunyuanOCR`, calls a `BatchInfer` callback per record, writes one output
+record per input record in input order (failures are records with
+`ok: false`, stage and message) and returns a `BatchSummary` (total,
+succeeded, failed).
+
+Here the same contract is kept per process, and the records are partitioned
+across GPUs: one process per GPU, each holding its own full copy of the
+weights, takes the records with index i % world == rank. There is no
+collective on the data path; the host gathers the per-rank results once at
+the end (`gather_in_order`) and merges them in input order, which gives the
+same output file as the sequential driver.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Callable, Iterable, List, Optional, Sequence
+
+
+@dataclass
+class BatchSummary:
+    """src/batch_jsonl.h:27-31."""
+    total: int = 0
+    succeeded: int = 0
+    failed: int = 0
+
+
+@dataclass
+class BatchRecord:
+    """One output record: `ok` with the generated tokens, or the failing stage and message."""
+    index: int
+    id: str
+    ok: bool
+    tokens: List[int] = field(default_factory=list)
+    stage: str = ""
+    error: str = ""
+
+
+def partition(n_records: int, world: int, rank: int) -> List[int]:
+    """Record indices of one rank: round-robin by index (i mod world)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"invalid rank {rank} of world {world}")
+    return list(range(rank, n_records, world))
+
+
+def run_partition(records: Sequence, infer: Callable, world: int = 1, rank: int = 0,
+                  record_id: Optional[Callable] = None) -> tuple[List[BatchRecord], BatchSummary]:
+    """Run this rank's records through `infer(record) -> tokens` (which raises on failure,
+    like a BatchInfer returning false with a RuntimeError). Returns this rank's output
+    records in input order and its summary."""
+    out: List[BatchRecord] = []
+    summary = BatchSummary()
+    for i in partition(len(records), world, rank):
+        rid = record_id(records[i]) if record_id else str(i)
+        summary.total += 1
+        try:
+            tokens = infer(records[i])
+        except Exception as exc:  # noqa: BLE001 - every failure becomes an ok:false record
+            summary.failed += 1
+            stage = getattr(exc, "stage", "inference")
+            out.append(BatchRecord(i, rid, False, stage=stage, error=str(exc) or "inference failed"))
+            continue
+        summary.succeeded += 1
+        out.append(BatchRecord(i, rid, True, tokens=list(tokens)))
+    return out, summary
+
+
+def merge_in_order(parts: Iterable[Sequence[BatchRecord]]) -> tuple[List[BatchRecord], BatchSummary]:
+    """Merge per-rank outputs into input order and add up the summaries."""
+    merged = sorted((r for p in parts for r in p), key=lambda r: r.index)
+    for a, b in zip(merged, merged[1:]):
+        if a.index == b.index:
+            raise ValueError(f"record {a.index} was produced by two ranks")
+    s = BatchSummary(total=len(merged), succeeded=sum(r.ok for r in merged),
+                     failed=sum(not r.ok for r in merged))
+    return merged, s
+
+
+def gather_in_order(local: Sequence[BatchRecord], world: int, rank: int):
+    """Gather every rank's records on rank 0 (torch.distributed object gather, once,
+    after the work) and merge them in input order. Returns (records, summary) on
+    rank 0 and (None, None) elsewhere."""
+    if world == 1:
+        return merge_in_order([local])
+    import torch.distributed as dist
+
+    parts = [None] * world if rank == 0 else None
+    dist.gather_object(list(local), parts, dst=0)
+    if rank != 0:
+        return None, None
+    return merge_in_order(parts)

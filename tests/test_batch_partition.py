@@ -1,0 +1,116 @@
+"""Request partitioning across GPUs (CPU): round-robin assignment, per-record
+failures, and the in-order merge on rank 0, with two gloo ranks as processes.
+
+Mirrors the reference's batch contract (src/batch_jsonl.cpp:384-480: one output
+record per input record, in input order; failed records are `ok: false`;
+BatchSummary counts) and tests/batch_jsonl_test.cpp's use of an injected
+inference callback.
+"""
+import importlib.util
+import os
+import socket
+import sys
+
+import pytest
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _batch():
+    if "hy_batch" in sys.modules:
+        return sys.modules["hy_batch"]
+    spec = importlib.util.spec_from_file_location("hy_batch", os.path.join(REPO, "hunyuanocr-ncnn_b200", "batch.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["hy_batch"] = mod   # dataclasses look their module up by name
+    spec.loader.exec_module(mod)
+    return mod
+
+
+class _Fail(RuntimeError):
+    stage = "decode"
+
+
+def _infer(rec):
+    # Injected callback: record 5 fails, the rest "decode" to a token list derived from the record.
+    if rec == 5:
+        raise _Fail("synthetic failure on record 5")
+    return [rec, rec * 2 + 1]
+
+
+def test_partition_round_robin_covers_every_record_once():
+    b = _batch()
+    for n in (0, 1, 7, 64):
+        for world in (1, 2, 3, 8):
+            parts = [b.partition(n, world, r) for r in range(world)]
+            flat = sorted(i for p in parts for i in p)
+            assert flat == list(range(n))
+            for r, p in enumerate(parts):
+                assert all(i % world == r for i in p)
+    with pytest.raises(ValueError):
+        b.partition(4, 2, 2)
+
+
+def test_single_process_matches_sequential_contract():
+    b = _batch()
+    records = list(range(9))
+    out, s = b.run_partition(records, _infer)
+    merged, ms = b.merge_in_order([out])
+    assert [r.index for r in merged] == records
+    assert (ms.total, ms.succeeded, ms.failed) == (9, 8, 1)
+    assert (s.total, s.succeeded, s.failed) == (9, 8, 1)
+    bad = merged[5]
+    assert not bad.ok and bad.stage == "decode" and "record 5" in bad.error
+    assert merged[3].tokens == [3, 7]
+
+
+def test_merge_rejects_duplicates():
+    b = _batch()
+    r = b.BatchRecord(1, "1", True, [1])
+    with pytest.raises(ValueError):
+        b.merge_in_order([[r], [r]])
+
+
+def _worker(rank, world, port, n, q):
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        b = _batch()
+        records = list(range(n))
+        local, s = b.run_partition(records, _infer, world=world, rank=rank)
+        merged, ms = b.gather_in_order(local, world, rank)
+        if rank == 0:
+            q.put(([(r.index, r.ok, r.tokens) for r in merged], (ms.total, ms.succeeded, ms.failed)))
+        q.put(("rank", rank, [r.index for r in local], (s.total, s.succeeded, s.failed)))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_two_gloo_ranks_merge_in_input_order():
+    import multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    n, world, port = 11, 2, _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, n, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    msgs = [q.get(timeout=60) for _ in range(world + 1)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    ranks = {m[1]: m for m in msgs if m[0] == "rank"}
+    assert ranks[0][2] == list(range(0, n, 2)) and ranks[1][2] == list(range(1, n, 2))
+    merged, summary = next(m for m in msgs if m[0] != "rank")
+    assert [i for i, _, _ in merged] == list(range(n))
+    assert summary == (n, n - 1, 1)
+    assert all(ok == (i != 5) for i, ok, _ in merged)
+    assert merged[4][2] == [4, 9]
