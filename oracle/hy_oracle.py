@@ -149,6 +149,7 @@ class ModelConfig:
     ffn: int = FFN
     rms_eps: float = RMS_EPS
     attn_scale: float = NCNN_SDPA_SCALE
+    kv_bf16: bool = False   # bf16 variant: cached K/V rows rounded to bf16 (RNE)
 
 
 @dataclass
@@ -173,13 +174,23 @@ class Weights:
     layers: list = field(default_factory=list)
 
 
+def round_bf16(a: np.ndarray) -> np.ndarray:
+    """fp32 -> nearest bf16 (ties to even), returned as fp32 (finite inputs)."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32).reshape(np.shape(a))
+
+
 def make_weights(cfg: ModelConfig, seed: int, std: float = 0.02, norm_std: float = 0.0,
-                 fast: bool = True) -> Weights:
-    """Seeded N(0, std)-like linears/embedding, norms = 1 + N(0, norm_std)."""
+                 fast: bool = True, bf16: bool = False) -> Weights:
+    """Seeded N(0, std)-like linears/embedding, norms = 1 + N(0, norm_std).
+    bf16: the linears and the embedding rounded to bf16 (the library's bf16-weight
+    variant rounds the same fp32 values); norms stay fp32."""
     gen = synth_tensor_fast if fast else synth_tensor
 
     def lin(tid, rows, cols):
-        return gen(seed, tid, rows * cols, std).reshape(rows, cols)
+        t = gen(seed, tid, rows * cols, std).reshape(rows, cols)
+        return round_bf16(t) if bf16 else t
 
     def norm(tid, n):
         return gen(seed, tid, n, norm_std, 1.0)
@@ -368,6 +379,8 @@ def layer_forward(lw: LayerWeights, x: np.ndarray, mask: np.ndarray, cos: np.nda
     k = apply_rope(k, cos, sin)
     q = rms_norm(q, lw.q_norm, cfg.rms_eps)
     k = rms_norm(k, lw.k_norm, cfg.rms_eps)
+    if cfg.kv_bf16:
+        k, v = round_bf16(k), round_bf16(v)
     cache_k[:, past:past + m_rows] = k
     cache_v[:, past:past + m_rows] = v
     L = past + m_rows
