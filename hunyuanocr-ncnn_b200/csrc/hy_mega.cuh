@@ -48,7 +48,7 @@ constexpr int kMegaConsumers = kMegaWarps * 32;
 constexpr int kMegaThreads = kMegaConsumers + 32;      // + the producer warp
 constexpr int kMegaStage = 16384;        // bytes per slot
 constexpr int kMegaSlots = 2;            // slots per warp
-constexpr int kMegaSplits = 9;           // per KV head: 8 splits of the past rows + the new-row split
+constexpr int kMegaSplits = 18;          // per KV head: 17 splits of the past rows + the new-row split (144 CTAs)
 constexpr int kMegaMaxK = 3584;
 constexpr int kMegaHistWords = 64;       // LM rows per CTA <= 32 * 62
 constexpr int kMegaResRows = 32;         // o/down rows per CTA (1024 / gridDim.x)
