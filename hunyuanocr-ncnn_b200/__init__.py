@@ -417,8 +417,11 @@ class TextRuntime:
         return ms.value
 
     def trace_persistent(self, tokens: int, trace_token: int) -> np.ndarray:
-        """Phase timestamps (ns) [4 CTAs, phases, 8]: start, after grid wait, after prologue, arrive,
-        producer first issue, producer last issue, consumer (thread 0) passing the first and last stage wait."""
+        """Per-phase trace of one token of the persistent kernel, [4 CTAs, phases, 12] uint64:
+        0 phase start, 1 inputs ready, 2 prologue done, 3 phase end (%globaltimer ns);
+        4 / 5 / 6: warp 0's SM cycles waiting on its slots / working, and its stages;
+        7 / 8 / 9 / 10 (attention): slot-wait cycles, work cycles, stages of the warp owning
+        the split's first stage, and the time its stage loop ended (ns)."""
         phases = 5 * self.cfg.num_layers + 1
         out = np.zeros((4, phases, 12), np.uint64)
         _check(_LIB.hy_trace_persistent(self._ctx, tokens, trace_token, _ptr(out)))
