@@ -28,6 +28,9 @@ def main(argv=None):
     ap.add_argument("--calls", type=int, default=3)
     ap.add_argument("--path", choices=["persistent", "graph"], default="persistent")
     ap.add_argument("--dtype", choices=["f32", "bf16"], default="f32", help="weight and KV dtype")
+    ap.add_argument("--kernel", choices=["decode", "lm", "gate_up", "attention", "verify"], default="decode",
+                    help="decode: AR launches; lm / gate_up / attention: the M=1 kernels alone "
+                         "(hy_bench_kernel); verify: DFlash verify blocks (16-row kernels)")
     args = ap.parse_args(argv)
 
     import __graft_entry__ as ge
@@ -35,9 +38,28 @@ def main(argv=None):
     pkg = ge.load_package()
     dt = pkg.DTYPE_F32 if args.dtype == "f32" else pkg.DTYPE_BF16
     rt = pkg.TextRuntime.synthetic(seed=0, num_layers=args.layers, vocab_size=args.vocab, max_prefill=64,
-                                   max_tokens=args.tokens + 8, max_context=args.past + args.tokens + 8,
+                                   max_tokens=args.tokens + 40, max_context=args.past + args.tokens + 40,
                                    weight_dtype=dt, kv_dtype=dt)
     rt.ar_path = pkg.AR_PATH_PERSISTENT if args.path == "persistent" else pkg.AR_PATH_GRAPH
+    if args.kernel in ("lm", "gate_up", "attention"):
+        rt.set_length(args.past)
+        which = {"lm": 0, "gate_up": 1, "attention": 2}[args.kernel]
+        ms = rt.bench_kernel(which, args.calls)
+        print(f"{args.kernel} {args.dtype} layers={args.layers} vocab={args.vocab} past={args.past}: "
+              f"{ms * 1e3:.2f} us per launch")
+        rt.close()
+        return
+    if args.kernel == "verify":
+        rt.set_length(args.past)
+        rt.set_history([1, 2, 3])
+        greedy = [5] * (args.tokens + 32)
+        for _ in range(args.calls):
+            rt.set_length(args.past)
+            r = rt.dflash_generate_synthetic(7, args.tokens, 1.08, greedy, 0.0, seed=3)
+        print(f"verify {args.dtype} layers={args.layers} vocab={args.vocab} past={args.past}: "
+              f"{r.block_count} blocks per call")
+        rt.close()
+        return
     ms = 0.0
     for _ in range(args.calls):
         rt.set_length(args.past)
