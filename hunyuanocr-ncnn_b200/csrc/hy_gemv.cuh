@@ -91,37 +91,99 @@ struct GemvShape {
     static constexpr int BAR_OFF = XS_BYTES + NST * STAGE;
     static constexpr int RED_OFF = BAR_OFF + 2 * NST * 8;
     static constexpr int SMEM = RED_OFF + RED_BYTES;
+    static constexpr int XP = KP;   // activation row pitch (floats)
+    static constexpr int KC16 = KP;  // (M = 16 only)
 };
 
-// M = 16 (DFlash verify blocks, prefill chunks): a stage holds RPL whole
-// weight rows (<= 16 KB, one contiguous copy when the rows are contiguous) and
-// belongs to one consumer warp (stage i -> warp i % 8). In it, lane (r, s) =
-// (lane % RPL, lane / RPL) owns row r and columns 4 (SUBS j + s) .. + 3 and
-// multiplies each weight float4 by the 16 activation rows. One instruction
-// reads RPL rows x SUBS consecutive float4s: one 128-byte line per row, which
-// is the minimum number of shared-memory wavefronts, and each activation read
-// is one broadcast line. The SUBS partial sums of a row are added with
-// shuffles at the end of the stage.
+// M = 16 (DFlash verify blocks, prefill chunks) on the tensor cores (mma.sync
+// m16n8k8, tf32 with a three-term split, see tf32_mma3): the CTA's weight rows
+// are cut into units of 8 rows x KC columns; a unit is one stage, its rows at a
+// padded pitch (row chunk + 16 bytes) and the 16 activation rows likewise
+// (pitch KP + 4 floats), so the fragment loads of a warp fall in 32 different
+// banks. The unit is the B operand (n = weight row), the activation rows the A
+// operand (m = activation row), one 16 x 8 tile per unit.
+//   K mode (few row groups: q/k/v, o, down): stage u = unit u = (group u / NKC,
+//     chunk u % NKC), owned by warp u % 8; the units' tiles go to shared memory
+//     and are added in chunk order at the end.
+//   G mode (many row groups: gate/up, the LM head): warp w owns groups w, w + 8,
+//     ... and takes all NKC chunks of a group in order, accumulating in its
+//     fragments; the stages of a round of 8 groups are interleaved chunk-major.
 template <typename WT, int KP>
 struct GemvShape<WT, KP, 16> {
-    static constexpr int SEG = KP * static_cast<int>(sizeof(WT));
-    static constexpr int RPL = (SEG <= 4096) ? 4 : 2;   // rows per stage (and per warp step)
-    static constexpr int SUBS = 32 / RPL;
-    static constexpr int SPS = RPL;
-    static constexpr int STAGE = RPL * SEG;
-    static constexpr int RPW = RPL, GPS = 1;
-    static constexpr int XS_BYTES = 16 * KP * 4;
-    static constexpr int WSCR_BYTES = kGemvWarps * 16 * 16 * 4;  // per-warp [row][m]
+    static constexpr int KC = (KP == 1024) ? 256 : KP / 8;   // columns per unit
+    static constexpr int NKC = KP / KC;
+    static constexpr int ROWB = KC * static_cast<int>(sizeof(WT));
+    static constexpr int PITCH = ROWB + 16;
+    static constexpr int STAGE = 8 * PITCH;
+    static constexpr int XP = KP + 4;
+    static constexpr int XS_BYTES = 16 * XP * 4;
+    static constexpr int PART_UNITS = 16;                        // K-mode tile slots
+    static constexpr int PART_BYTES = PART_UNITS * 16 * 8 * 4;   // [unit][m][n]
+    static constexpr int WSCR_BYTES = kGemvWarps * 16 * 8 * 4;   // G-mode per-warp [m][n]
     static constexpr int RED_BYTES = (kGemvWarps * 16 + 16) * 16 + 16;
-    static constexpr int NST_FIT = (kSmemBudget - XS_BYTES - WSCR_BYTES - RED_BYTES - 512) / STAGE;
-    static constexpr int NST = NST_FIT < 8 ? NST_FIT : 8;
-    static constexpr int WSCR_OFF = XS_BYTES + NST * STAGE;
+    static constexpr int NST_FIT = (kSmemBudget - XS_BYTES - PART_BYTES - WSCR_BYTES - RED_BYTES - 512) / STAGE;
+    static constexpr int NST = NST_FIT >= 16 ? 16 : 8;   // slots: 2 or 1 per consumer warp
+    static_assert(NST_FIT >= 8, "one slot per consumer warp must fit");
+    static constexpr int PART_OFF = XS_BYTES + NST * STAGE;
+    static constexpr int WSCR_OFF = PART_OFF + PART_BYTES;
     static constexpr int BAR_OFF = WSCR_OFF + WSCR_BYTES;
     static constexpr int RED_OFF = BAR_OFF + 2 * NST * 8;
     static constexpr int SMEM = RED_OFF + RED_BYTES;
-    static_assert(STAGE <= 16384, "a stage is at most 16 KB");
-    static_assert(KP % (4 * SUBS) == 0, "K slice must be a multiple of a warp step");
+    // Names the generic code refers to.
+    static constexpr int RPW = 8, SEG = ROWB, SPS = 8, GPS = 1, KC16 = KC;
+    static_assert(KP % KC == 0 && KC % 8 == 0 && ROWB % 16 == 0, "unit geometry");
 };
+
+struct Unit16 {
+    int g, c, w, j;   // row group, column chunk, owner warp, index among the owner's units
+};
+
+__device__ __forceinline__ Unit16 unit16_of(int s, int ngroups, int nkc, bool kmode)
+{
+    if (kmode) return Unit16{s / nkc, s % nkc, s % kGemvWarps, s / kGemvWarps};
+    const int per_round = nkc * kGemvWarps;
+    const int r = s / per_round;   // every round before the last is full
+    const int aw = min(kGemvWarps, ngroups - kGemvWarps * r);
+    const int i = s - r * per_round;
+    const int w = i % aw;
+    return Unit16{kGemvWarps * r + w, i / aw, w, r * nkc + i / aw};
+}
+
+// d += A(x) * B(w) for one m16n8k8 tf32 tile with fp32-level accuracy: the
+// operands are split into a tf32 head (mantissa truncated to 10 bits) and the
+// fp32 remainder, and the three products head*head + lo*head + head*lo are
+// accumulated (lo*lo, ~2^-22 relative, is dropped). With bf16 weights the
+// weight head is exact and its remainder is zero (two products).
+__device__ __forceinline__ unsigned tf32_head(float v) { return __float_as_uint(v) & 0xFFFFE000u; }
+
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const unsigned (&a)[4], unsigned b0, unsigned b1)
+{
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <bool W_EXACT>
+__device__ __forceinline__ void tf32_mma3(float (&d)[4], const float (&x)[4], float w0, float w1)
+{
+    unsigned ah[4], al[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+    {
+        ah[i] = tf32_head(x[i]);
+        al[i] = __float_as_uint(x[i] - __uint_as_float(ah[i]));
+    }
+    const unsigned bh0 = tf32_head(w0), bh1 = tf32_head(w1);
+    mma_tf32(d, al, bh0, bh1);
+    if constexpr (!W_EXACT)
+    {
+        const unsigned bl0 = __float_as_uint(w0 - __uint_as_float(bh0));
+        const unsigned bl1 = __float_as_uint(w1 - __uint_as_float(bh1));
+        mma_tf32(d, ah, bl0, bl1);
+    }
+    mma_tf32(d, ah, bh0, bh1);
+}
 
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
@@ -160,6 +222,7 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
 {
     using S = GemvShape<WT, KP, MT>;
     constexpr int RPW = S::RPW, SEG = S::SEG, SPS = S::SPS, STAGE = S::STAGE, NST = S::NST;
+    constexpr int XP = S::XP;   // activation row pitch in shared memory
     static_assert(NST >= 2, "ring too small");
     static_assert(S::GPS <= kGemvWarps, "a warp may own at most one row group per stage");
     static_assert(SEG % 16 == 0, "segments must be 16-byte multiples");
@@ -180,7 +243,10 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
     const int r0 = unit * static_cast<int>(static_cast<long long>(a.N / unit) * b / G);
     const int r1 = unit * static_cast<int>(static_cast<long long>(a.N / unit) * (b + 1) / G);
     const int R = r1 - r0;
-    const int nstage = (R + SPS - 1) / SPS;
+    // M = 16: row groups of 8, K mode when all units fit the tile slots.
+    const int ngroups16 = (R + 7) / 8;
+    const bool kmode16 = (MT == 16) && ngroups16 * (KP / S::KC16) <= 16;
+    const int nstage = (MT == 16) ? ngroups16 * (KP / S::KC16) : (R + SPS - 1) / SPS;
 
     __shared__ uint64_t s_xbar;   // M = 16: bulk copy of the activation rows
     if (tid == 0)
@@ -188,7 +254,7 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
         for (int s = 0; s < NST; ++s)
         {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kGemvWarps);
+            mbar_init(&empty[s], (MT == 16) ? 1 : kGemvWarps);
         }
         mbar_init(&s_xbar, 1);
         fence_mbar_init();
@@ -203,11 +269,32 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
             const uint64_t pol = l2_evict_first_policy();
             const WT* W = static_cast<const WT*>(a.W);
             int issued = 0;
+            int fills[(MT == 16) ? NST : 1] = {};   // M = 16: copies issued into each slot
             for (int i = 0; i < nstage; ++i)
             {
                 const int slot = i % NST;
-                if (i >= NST && !mbar_wait(&empty[slot], ((i / NST) - 1) & 1, a.err, kErrTimeoutEmpty)) break;
+                if (MT != 16 && i >= NST && !mbar_wait(&empty[slot], ((i / NST) - 1) & 1, a.err, kErrTimeoutEmpty)) break;
                 unsigned char* dst = ring + slot * STAGE;
+                if constexpr (MT == 16)
+                {
+                    // Unit (g, c): up to 8 row chunks of S::ROWB bytes at the padded pitch,
+                    // into the next of its owner warp's slots.
+                    const Unit16 u = unit16_of(i, ngroups16, S::NKC, kmode16);
+                    constexpr int SPW = NST / kGemvWarps;
+                    const int ws = u.w * SPW + u.j % SPW;
+                    if (u.j >= SPW && !mbar_wait(&empty[ws], ((u.j / SPW) - 1) & 1, a.err, kErrTimeoutEmpty)) break;
+                    fills[ws] += 1;
+                    dst = ring + ws * STAGE;
+                    const int slot = ws;
+                    const int gr0 = r0 + 8 * u.g;
+                    const int nr = min(8, r1 - gr0);
+                    mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(nr * S::ROWB));
+                    for (int j = 0; j < nr; ++j)
+                        bulk_g2s(dst + j * S::PITCH, W + static_cast<size_t>(gr0 + j) * a.ldw + a.k_off + u.c * S::KC,
+                                 S::ROWB, &full[slot], pol);
+                    issued = i + 1;
+                    continue;
+                }
                 const int sr0 = r0 + i * SPS;
                 const int nseg = min(SPS, r1 - sr0);
                 mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(nseg * SEG));
@@ -223,8 +310,16 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
                 issued = i + 1;
             }
             // Drain: never leave the CTA with copies in flight.
-            for (int i = (issued > NST ? issued - NST : 0); i < issued; ++i)
-                mbar_wait(&full[i % NST], (i / NST) & 1, a.err, kErrTimeoutFull);
+            if constexpr (MT == 16)
+            {
+                for (int ws = 0; ws < NST; ++ws)
+                    if (fills[ws] > 0) mbar_wait(&full[ws], (fills[ws] - 1) & 1, a.err, kErrTimeoutFull);
+            }
+            else
+            {
+                for (int i = (issued > NST ? issued - NST : 0); i < issued; ++i)
+                    mbar_wait(&full[i % NST], (i / NST) & 1, a.err, kErrTimeoutFull);
+            }
         }
         return;
     }
@@ -259,6 +354,11 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
         }
     }
     if (EPI == EPI_ARGMAX && tid < MT) s_prefix[tid] = (a.prefix && tid < rows) ? a.prefix[tid] : -1;
+    // M = 16 argmax: the penalty-history words of this CTA's rows, read once.
+    constexpr int kHistWords16 = 64;
+    __shared__ unsigned s_hist[(MT == 16 && EPI == EPI_ARGMAX) ? kHistWords16 : 1];
+    const bool hist_s_ok = (MT == 16 && EPI == EPI_ARGMAX) && R > 0 && ((r1 - 1) >> 5) - (r0 >> 5) < kHistWords16;
+    if (hist_s_ok && tid <= ((r1 - 1) >> 5) - (r0 >> 5)) s_hist[tid] = a.hist[(r0 >> 5) + tid];
     consumers_sync();
 
     // Stage the activation rows (fp32) in shared memory.
@@ -276,10 +376,10 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
             {
                 mbar_arrive_expect_tx(&s_xbar, static_cast<uint32_t>(rows * KP * 4));
                 for (int m = 0; m < rows; ++m)
-                    bulk_g2s_plain(xs + m * KP, a.x + static_cast<size_t>(m) * a.ldx + a.k_off, KP * 4, &s_xbar);
+                    bulk_g2s_plain(xs + m * XP, a.x + static_cast<size_t>(m) * a.ldx + a.k_off, KP * 4, &s_xbar);
             }
-            for (int i = tid; i < (MT - rows) * (KP / 4); i += 256)
-                reinterpret_cast<float4*>(xs + rows * KP)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int i = tid; i < (MT - rows) * (XP / 4); i += 256)
+                reinterpret_cast<float4*>(xs + rows * XP)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
             mbar_wait(&s_xbar, 0, a.err, kErrTimeoutFull);
         }
         for (int m0 = 0; m0 < MT && !bulk; m0 += B)
@@ -321,7 +421,7 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
                         r.z = (q1.x / (1.0f + expf(-q1.x))) * q1.y;
                         r.w = (q1.z / (1.0f + expf(-q1.z))) * q1.w;
                     }
-                    *reinterpret_cast<float4*>(xs + m * KP + k) = r;
+                    *reinterpret_cast<float4*>(xs + m * XP + k) = r;
                 }
         }
     }
@@ -374,7 +474,7 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
         const int total = rows * kHidden;
         const int per = (total + G - 1) / G;
         const int beg = b * per, end = min(total, beg + per);
-        for (int i = beg + tid; i < end; i += 256) a.x_store[i] = xs[(i / kHidden) * KP + (i % kHidden)];
+        for (int i = beg + tid; i < end; i += 256) a.x_store[i] = xs[(i / kHidden) * XP + (i % kHidden)];
     }
 
     if (PRO == PRO_NORM && MT == 16)
@@ -385,7 +485,7 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
             float ss = 0.f;
             for (int k = lane * 4; k < KP; k += 128)
             {
-                const float4 v = *reinterpret_cast<const float4*>(xs + m * KP + k);
+                const float4 v = *reinterpret_cast<const float4*>(xs + m * XP + k);
                 ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
             }
             ss = warp_sum(ss);
@@ -396,13 +496,13 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
         {
             const int m = i / (KP / 4), k = 4 * (i % (KP / 4));
             const float ri = s_rinv[m];
-            float4 v = *reinterpret_cast<float4*>(xs + m * KP + k);
+            float4 v = *reinterpret_cast<float4*>(xs + m * XP + k);
             const float4 w = *reinterpret_cast<const float4*>(a.norm_w + a.k_off + k);
             v.x = w.x * (v.x * ri);
             v.y = w.y * (v.y * ri);
             v.z = w.z * (v.z * ri);
             v.w = w.w * (v.w * ri);
-            *reinterpret_cast<float4*>(xs + m * KP + k) = v;
+            *reinterpret_cast<float4*>(xs + m * XP + k) = v;
         }
         consumers_sync();
     }
@@ -452,16 +552,33 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
     const float pen = (EPI == EPI_ARGMAX) ? ((a.lm_mode == LM_NONE) ? a.penalty : a.st->penalty) : 1.0f;
     ArgBest best;
     best.rv = 0.f; best.ri = -1; best.pv = 0.f; best.pi = -1;
-    // Every consumer warp observes every stage in order and arrives once on it;
-    // the warp owning a row group of the stage (group gi -> warp gi % 8)
+    // M = 1: every consumer warp observes every stage in order and arrives once
+    // on it; the warp owning a row group of the stage (group gi -> warp gi % 8)
     // computes it before arriving. (An mbarrier parity wait is only meaningful
     // one phase ahead, so no warp may skip past a stage that has not landed, nor
-    // let a slot be reused before it has seen it.)
+    // let a slot be reused before it has seen it.) M = 16: each warp has slots
+    // of its own and waits only on those.
     if constexpr (MT == 16)
     {
-        constexpr int RPL = S::RPL, SUBS = S::SUBS;
-        float* wscr = reinterpret_cast<float*>(smem + S::WSCR_OFF) + warp * 256;   // [row][m]
-        const int rr = lane % RPL, sub = lane / RPL;
+        constexpr int NKC = S::NKC, KC = S::KC, PITCH = S::PITCH;
+        constexpr bool W_EXACT = sizeof(WT) == 2;   // bf16 weights are exact tf32 heads
+        float* part = reinterpret_cast<float*>(smem + S::PART_OFF);                 // [unit][m][n]
+        float* wscr = reinterpret_cast<float*>(smem + S::WSCR_OFF) + warp * 128;   // [m][n]
+        const int g8 = lane >> 2, t4 = lane & 3;
+        float d[4];
+        // Tile of the unit in `slot` (chunk c): d += x[0:16, chunk] * W[8 rows, chunk]^T.
+        auto unit_mma = [&](int slot, int c) {
+            const WT* wr = reinterpret_cast<const WT*>(ring + slot * STAGE + g8 * PITCH);
+            const float* x0 = xs + g8 * XP + c * KC + t4;
+            const float* x1 = x0 + 8 * XP;
+#pragma unroll 4
+            for (int k8 = 0; k8 < KC / 8; ++k8)
+            {
+                const float xa[4] = {x0[8 * k8], x1[8 * k8], x0[8 * k8 + 4], x1[8 * k8 + 4]};
+                const float w0 = to_f32<WT>(wr[8 * k8 + t4]), w1 = to_f32<WT>(wr[8 * k8 + t4 + 4]);
+                tf32_mma3<W_EXACT>(d, xa, w0, w1);
+            }
+        };
         // Store / residual / argmax epilogue of one output (row n of activation row m).
         auto emit = [&](int m, int n, float v) {
             if (EPI == EPI_STORE || EPI == EPI_RESID)
@@ -478,79 +595,91 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
             else
             {
                 if (a.logits) a.logits[static_cast<size_t>(m) * a.ldl + n] = v;
-                bool hit = (a.hist[n >> 5] >> (n & 31)) & 1u;
+                const unsigned hw = hist_s_ok ? s_hist[(n >> 5) - (r0 >> 5)] : a.hist[n >> 5];
+                bool hit = (hw >> (n & 31)) & 1u;
                 for (int j = 0; j <= m; ++j) hit |= (s_prefix[j] == n);
                 const float ps = hit ? (v < 0.0f ? v * pen : v / pen) : v;
                 if (best.ri < 0 || v > best.rv) { best.rv = v; best.ri = n; }
                 if (best.pi < 0 || ps > best.pv) { best.pv = ps; best.pi = n; }
             }
         };
-        // Every consumer warp observes every stage in order and arrives once on it.
-        for (int stage = 0; stage < nstage; ++stage)
-        {
-            const int slot = stage % NST;
-            const bool ok = mbar_wait(&full[slot], (stage / NST) & 1, a.err, kErrTimeoutFull);
-            if (!__all_sync(0xffffffffu, ok)) break;
-            const bool mine = (stage % kGemvWarps) == warp;
-            float acc[16];
-            if (mine)
-            {
-#pragma unroll
-                for (int m = 0; m < 16; ++m) acc[m] = 0.f;
-                const WT* wrow = reinterpret_cast<const WT*>(ring + slot * STAGE + rr * SEG);
-                const float* xb = xs + 4 * sub;
-#pragma unroll 2
-                for (int j = 0; j < KP / (4 * SUBS); ++j)
-                {
-                    const float4 w = load4(wrow + 4 * (SUBS * j + sub));
-#pragma unroll
-                    for (int m = 0; m < 16; ++m)
-                        acc[m] += dot4(w, *reinterpret_cast<const float4*>(xb + m * KP + 4 * SUBS * j));
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
-            if (!mine) continue;
-            // Add the SUBS partial sums of each row: lanes 0 .. RPL-1 hold the totals.
-#pragma unroll
-            for (int o = RPL; o < 32; o <<= 1)
-#pragma unroll
-                for (int m = 0; m < 16; ++m) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
-            const int n0 = r0 + stage * RPL;
-            const int nr = min(RPL, R - stage * RPL);
-            if (lane < RPL)
-            {
-#pragma unroll
-                for (int m = 0; m < 16; ++m) wscr[lane * 16 + m] = acc[m];
-            }
-            __syncwarp();
+        // Epilogue of a finished 8-row group from its [m][n] tile.
+        auto group_epilogue = [&](const float* tile, int g) {
+            const int n0 = r0 + 8 * g;
+            const int nr = min(8, R - 8 * g);
             if (EPI == EPI_ARGMAX)
             {
                 if (lane < rows)
-                    for (int row = 0; row < nr; ++row) emit(lane, n0 + row, wscr[row * 16 + lane]);
+                    for (int row = 0; row < nr; ++row) emit(lane, n0 + row, tile[lane * 8 + row]);
             }
             else if (EPI == EPI_ACT)
             {
-                // act[m][j] = silu(gate_j) * up_j for the row pairs of the stage (n0 is even).
-                for (int p = lane; p < 16 * (RPL / 2); p += 32)
+                // act[m][j] = silu(gate_j) * up_j for the row pairs (n0 is even).
+                for (int p = lane; p < 16 * 4; p += 32)
                 {
-                    const int m = p / (RPL / 2), pr = p % (RPL / 2);
+                    const int m = p >> 2, pr = p & 3;
                     if (2 * pr + 1 < nr && m < rows)
                     {
-                        const float gt = wscr[(2 * pr) * 16 + m], up = wscr[(2 * pr + 1) * 16 + m];
+                        const float gt = tile[m * 8 + 2 * pr], up = tile[m * 8 + 2 * pr + 1];
                         a.out[static_cast<size_t>(m) * a.ldo + ((n0 >> 1) + pr)] = (gt / (1.0f + expf(-gt))) * up;
                     }
                 }
             }
             else
             {
-                for (int p = lane; p < 16 * RPL; p += 32)
+                for (int p = lane; p < 16 * 8; p += 32)
                 {
-                    const int m = p / RPL, row = p % RPL;
-                    if (row < nr && m < rows) emit(m, n0 + row, wscr[row * 16 + m]);
+                    const int m = p >> 3, row = p & 7;
+                    if (row < nr && m < rows) emit(m, n0 + row, tile[m * 8 + row]);
                 }
             }
+        };
+        // This warp's own units, in order, from its own slots (each refilled by the
+        // producer once this warp released it, so every wait is one phase ahead).
+        constexpr int SPW = NST / kGemvWarps;
+        int jown = 0;
+        for (int stage = 0; stage < nstage; ++stage)
+        {
+            const Unit16 u = unit16_of(stage, ngroups16, NKC, kmode16);
+            if (u.w != warp) continue;
+            const int slot = warp * SPW + jown % SPW;
+            const bool ok = mbar_wait(&full[slot], (jown / SPW) & 1, a.err, kErrTimeoutFull);
+            ++jown;
+            if (!__all_sync(0xffffffffu, ok)) break;
+            if (kmode16 || u.c == 0) d[0] = d[1] = d[2] = d[3] = 0.f;
+            unit_mma(slot, u.c);
             __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            // Tile element (m, n): d0 (g8, 2 t4), d1 (g8, 2 t4 + 1), d2 (g8 + 8, 2 t4), d3 (g8 + 8, 2 t4 + 1).
+            float* tile = kmode16 ? part + stage * 128 : wscr;
+            if (kmode16 || u.c == NKC - 1)
+            {
+                tile[g8 * 8 + 2 * t4] = d[0];
+                tile[g8 * 8 + 2 * t4 + 1] = d[1];
+                tile[(g8 + 8) * 8 + 2 * t4] = d[2];
+                tile[(g8 + 8) * 8 + 2 * t4 + 1] = d[3];
+            }
+            if (!kmode16 && u.c == NKC - 1)
+            {
+                __syncwarp();
+                group_epilogue(wscr, u.g);
+                __syncwarp();
+            }
+        }
+        if (kmode16)
+        {
+            // Add the units' tiles in chunk order and run the epilogue.
+            consumers_sync();
+            float* sum = reinterpret_cast<float*>(smem + S::PART_OFF);   // group g's sum overwrites unit g*NKC
+            for (int e = tid; e < ngroups16 * 128; e += 256)
+            {
+                const int g = e >> 7, i = e & 127;
+                float v = 0.f;
+                for (int c = 0; c < NKC; ++c) v += part[(g * NKC + c) * 128 + i];
+                sum[(g * NKC) * 128 + i] = v;
+            }
+            consumers_sync();
+            for (int g = warp; g < ngroups16; g += kGemvWarps) group_epilogue(sum + (g * NKC) * 128, g);
         }
     }
     else
