@@ -6,6 +6,7 @@
 #include "hy_device.cuh"
 #include "hy_gemv.cuh"
 #include "hy_mega.cuh"
+#include "hy_prefill.cuh"
 #include "hy_util.cuh"
 
 #include "hy_decode.h"
@@ -47,6 +48,7 @@ constexpr int kAttnSplitsVerify = 18;         // 17 past splits + the new-row sp
 constexpr int kMaxSplits = 20;
 constexpr int kArStepsPerGraph = 4;
 constexpr int kMegaChunk = 64;            // tokens per persistent-kernel launch
+constexpr int kPrefillChunk = 1024;       // prompt rows per prefill pass (all layers)
 constexpr unsigned long long kTidEmbed = 1, kTidFinalNorm = 2, kLayerTidBase = 100, kLayerTidStride = 16;
 constexpr unsigned long long kTidDrafts = 9003;
 enum { J_INPUT_NORM, J_Q, J_K, J_V, J_Q_NORM, J_K_NORM, J_O, J_POST_NORM, J_GATE, J_UP, J_DOWN };
@@ -106,6 +108,12 @@ struct hy_ctx {
     int* feat_idx = nullptr;    // [max_prefill]
     float* feats = nullptr;     // vision features [max_prefill x 1024]
     float* logits = nullptr;    // [16 x V] (lazily)
+    // Prompt prefill in chunks of up to pf_rows rows (the residual stream is ctx->prompt).
+    int pf_rows = 0;
+    float* pf_xn = nullptr;     // [pf_rows x 1024] normed rows
+    float* pf_qkv = nullptr;    // [pf_rows x 4096]
+    float* pf_attn = nullptr;   // [pf_rows x 2048]
+    float* pf_act = nullptr;    // [pf_rows x ffn]
     int* err = nullptr;
     DecodeState* h_st = nullptr;  // pinned mirror
     int kv_len = 0;               // host mirror of the sequence length
@@ -758,6 +766,11 @@ int alloc_ctx(hy_ctx* c)
     if ((rc = dalloc(c, &c->feats, pre_rows * kHidden))) return rc;
     if ((rc = dalloc(c, &c->ids_buf, pre_rows))) return rc;
     if ((rc = dalloc(c, &c->feat_idx, pre_rows))) return rc;
+    c->pf_rows = std::min(cfg.max_prefill, kPrefillChunk);
+    if ((rc = dalloc(c, &c->pf_xn, static_cast<size_t>(c->pf_rows) * kHidden))) return rc;
+    if ((rc = dalloc(c, &c->pf_qkv, static_cast<size_t>(c->pf_rows) * kQKVRows))) return rc;
+    if ((rc = dalloc(c, &c->pf_attn, static_cast<size_t>(c->pf_rows) * kQWidth))) return rc;
+    if ((rc = dalloc(c, &c->pf_act, static_cast<size_t>(c->pf_rows) * ffn))) return rc;
     if ((rc = dalloc(c, &c->x, kMaxStepRows * kHidden))) return rc;
     if ((rc = dalloc(c, &c->qkv, kMaxStepRows * kQKVRows))) return rc;
     if ((rc = dalloc(c, &c->attn, kMaxStepRows * kQWidth))) return rc;
@@ -1009,6 +1022,112 @@ int run_direct_step(hy_ctx* c, int rows, int past, const float* cos, const float
     t_next_plain = true;   // the rows were just copied into ctx->x
     cudaError_t e = enqueue_step(c, p);
     if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("decoder step launch: ") + cudaGetErrorString(e));
+    return HY_OK;
+}
+
+template <typename WT, int EPI>
+cudaError_t run_prefill_gemm(hy_ctx* c, const float* A, int lda, const void* W, int ldw, int M, int N, int K, float* C,
+                             int ldc)
+{
+    using S = PgShape<WT>;
+    auto k = prefill_gemm_kernel<WT, EPI>;
+    static unsigned long long configured = 0;
+    const unsigned long long bit = 1ull << (c->cfg.device & 63);
+    if (!(configured & bit))
+    {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
+        if (e != cudaSuccess) return e;
+        configured |= bit;
+    }
+    if (N % kPgBN != 0 || K % kPgBK != 0 || M <= 0) return cudaErrorInvalidValue;
+    PrefillGemmArgs a{A, lda, W, ldw, M, N, K, C, ldc};
+    k<<<dim3(N / kPgBN, (M + kPgBM - 1) / kPgBM), kPgThreads, S::SMEM, c->stream>>>(a);
+    return cudaGetLastError();
+}
+
+// Prompt prefill: the decoder over rows [0, seq) of ctx->prompt (the residual
+// stream, updated in place), in passes of up to pf_rows rows through all
+// layers; rope rows come from pre_cos / pre_sin. The projections of a pass run
+// as many-row tensor-core GEMMs; attention runs per 16-row slice in order (each
+// slice appends its K/V rows and attends to every earlier row). Leaves the
+// final-normed last row in ctx->hidden.
+template <typename WT, typename KT>
+cudaError_t enqueue_prefill_t(hy_ctx* c, int seq)
+{
+    const hy_config& cfg = c->cfg;
+    const int ffn = cfg.ffn_dim;
+    cudaError_t e = cudaSuccess;
+    for (int p0 = 0; p0 < seq; p0 += c->pf_rows)
+    {
+        const int rows = std::min(c->pf_rows, seq - p0);
+        float* xr = c->prompt + static_cast<size_t>(p0) * kHidden;
+        for (int l = 0; l < cfg.num_layers; ++l)
+        {
+            rmsnorm_rows_kernel<<<rows, 256, 0, c->stream>>>(xr, c->in_norm(l), cfg.rms_norm_eps, c->pf_xn, kHidden);
+            if ((e = cudaGetLastError()) != cudaSuccess) return e;
+            if ((e = run_prefill_gemm<WT, PG_STORE>(c, c->pf_xn, kHidden, c->wqkv[l], kHidden, rows, kQKVRows, kHidden,
+                                                    c->pf_qkv, kQKVRows)) != cudaSuccess)
+                return e;
+            for (int r0 = 0; r0 < rows; r0 += kMaxStepRows)
+            {
+                AttnArgs at;
+                std::memset(&at, 0, sizeof(at));
+                at.qkv = c->pf_qkv + static_cast<size_t>(r0) * kQKVRows;
+                at.ldq = kQKVRows;
+                at.qn_w = c->qn(l);
+                at.kn_w = c->kn(l);
+                at.cos = c->pre_cos + static_cast<size_t>(p0 + r0) * kHeadDim;
+                at.sin = c->pre_sin + static_cast<size_t>(p0 + r0) * kHeadDim;
+                at.rope_state = 0;
+                at.kc = c->kc_layer(l);
+                at.vc = c->vc_layer(l);
+                at.cap = cfg.max_context;
+                at.st = nullptr;
+                at.past_fixed = p0 + r0;
+                at.rows = std::min(kMaxStepRows, rows - r0);
+                at.scale_log2 = cfg.attn_scale * 1.4426950408889634f;
+                at.eps = cfg.rms_norm_eps;
+                at.part = c->attn_part;
+                at.counter = c->attn_cnt + l * kNumKVHeads;
+                at.out = c->pf_attn + static_cast<size_t>(r0) * kQWidth;
+                at.err = c->err;
+                // Plain launch: the slice reads the K/V rows the previous slice appended
+                // before its griddepcontrol.wait.
+                t_next_plain = true;
+                if ((e = run_attn<16, KT>(c, at, kAttnSplitsVerify)) != cudaSuccess) return e;
+            }
+            if ((e = run_prefill_gemm<WT, PG_RESID>(c, c->pf_attn, kQWidth, c->wo[l], kQWidth, rows, kHidden, kQWidth, xr,
+                                                    kHidden)) != cudaSuccess)
+                return e;
+            rmsnorm_rows_kernel<<<rows, 256, 0, c->stream>>>(xr, c->post_norm(l), cfg.rms_norm_eps, c->pf_xn, kHidden);
+            if ((e = cudaGetLastError()) != cudaSuccess) return e;
+            if ((e = run_prefill_gemm<WT, PG_SWIGLU>(c, c->pf_xn, kHidden, c->wgu[l], kHidden, rows, 2 * ffn, kHidden,
+                                                     c->pf_act, ffn)) != cudaSuccess)
+                return e;
+            if ((e = run_prefill_gemm<WT, PG_RESID>(c, c->pf_act, ffn, c->wd[l], ffn, rows, kHidden, ffn, xr, kHidden)) !=
+                cudaSuccess)
+                return e;
+        }
+        if (p0 + rows == seq)
+        {
+            rmsnorm_rows_kernel<<<1, 256, 0, c->stream>>>(xr + static_cast<size_t>(rows - 1) * kHidden, c->final_norm(),
+                                                         cfg.rms_norm_eps, c->hidden, kHidden);
+            if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        }
+    }
+    t_next_plain = true;
+    return cudaSuccess;
+}
+
+int run_prefill(hy_ctx* c, int seq)
+{
+    const bool wb = c->cfg.weight_dtype == HY_DTYPE_BF16, kb = c->cfg.kv_dtype == HY_DTYPE_BF16;
+    cudaError_t e;
+    if (!wb && !kb) e = enqueue_prefill_t<float, float>(c, seq);
+    else if (!wb && kb) e = enqueue_prefill_t<float, __nv_bfloat16>(c, seq);
+    else if (wb && !kb) e = enqueue_prefill_t<__nv_bfloat16, float>(c, seq);
+    else e = enqueue_prefill_t<__nv_bfloat16, __nv_bfloat16>(c, seq);
+    if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("prefill launch: ") + cudaGetErrorString(e));
     return HY_OK;
 }
 
@@ -1304,22 +1423,9 @@ int hy_prefill(hy_ctx* c, const float* embeds, const float* cos, const float* si
     HY_CUDA(cudaMemcpyAsync(c->prompt, embeds, sizeof(float) * seq * kHidden, cudaMemcpyHostToDevice, c->stream));
     HY_CUDA(cudaMemcpyAsync(c->pre_cos, cos, sizeof(float) * seq * kHeadDim, cudaMemcpyHostToDevice, c->stream));
     HY_CUDA(cudaMemcpyAsync(c->pre_sin, sin, sizeof(float) * seq * kHeadDim, cudaMemcpyHostToDevice, c->stream));
-    for (int p0 = 0; p0 < seq; p0 += kMaxStepRows)
-    {
-        const int rows = std::min(kMaxStepRows, seq - p0);
-        HY_CUDA(cudaMemcpyAsync(c->x, c->prompt + static_cast<size_t>(p0) * kHidden, sizeof(float) * rows * kHidden,
-                                cudaMemcpyDeviceToDevice, c->stream));
-        if ((rc = run_direct_step(c, rows, p0, c->pre_cos + static_cast<size_t>(p0) * kHeadDim,
-                                  c->pre_sin + static_cast<size_t>(p0) * kHeadDim, nullptr)))
-            return rc;
-        if (p0 + rows == seq && last_hidden)
-        {
-            rmsnorm_rows_kernel<<<1, 256, 0, c->stream>>>(c->x + static_cast<size_t>(rows - 1) * kHidden, c->final_norm(),
-                                                         c->cfg.rms_norm_eps, c->hidden, kHidden);
-            HY_CUDA(cudaGetLastError());
-            HY_CUDA(cudaMemcpyAsync(last_hidden, c->hidden, sizeof(float) * kHidden, cudaMemcpyDeviceToHost, c->stream));
-        }
-    }
+    if ((rc = run_prefill(c, seq))) return rc;
+    if (last_hidden)
+        HY_CUDA(cudaMemcpyAsync(last_hidden, c->hidden, sizeof(float) * kHidden, cudaMemcpyDeviceToHost, c->stream));
     if ((rc = check_device_error(c))) return rc;
     return set_length(c, seq);
 }
@@ -1587,21 +1693,7 @@ int hy_run_vlm_decode_with_prompt(hy_ctx* c, const int* input_ids, const int* po
     HY_CUDA(cudaMemsetAsync(c->hist, 0, sizeof(unsigned) * ((c->cfg.vocab_size + 31) / 32), c->stream));
     hist_add_kernel<<<(seq_len + 255) / 256, 256, 0, c->stream>>>(c->hist, c->ids_buf, seq_len, c->cfg.vocab_size);
     HY_CUDA(cudaGetLastError());
-    for (int p0 = 0; p0 < seq_len; p0 += kMaxStepRows)
-    {
-        const int rows = std::min(kMaxStepRows, seq_len - p0);
-        HY_CUDA(cudaMemcpyAsync(c->x, c->prompt + static_cast<size_t>(p0) * kHidden, sizeof(float) * rows * kHidden,
-                                cudaMemcpyDeviceToDevice, c->stream));
-        if ((rc = run_direct_step(c, rows, p0, c->pre_cos + static_cast<size_t>(p0) * kHeadDim,
-                                  c->pre_sin + static_cast<size_t>(p0) * kHeadDim, nullptr)))
-            return rc;
-        if (p0 + rows == seq_len)
-        {
-            rmsnorm_rows_kernel<<<1, 256, 0, c->stream>>>(c->x + static_cast<size_t>(rows - 1) * kHidden, c->final_norm(),
-                                                         c->cfg.rms_norm_eps, c->hidden, kHidden);
-            HY_CUDA(cudaGetLastError());
-        }
-    }
+    if ((rc = run_prefill(c, seq_len))) return rc;
     cudaError_t e = enqueue_lm_select(c, 1, c->hidden, repetition_penalty, false, nullptr);
     if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("LM head launch: ") + cudaGetErrorString(e));
     int first = 0, first_raw = 0;
