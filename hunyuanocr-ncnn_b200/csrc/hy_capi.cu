@@ -1045,12 +1045,31 @@ cudaError_t run_prefill_gemm(hy_ctx* c, const float* A, int lda, const void* W, 
     return cudaGetLastError();
 }
 
+template <typename KT>
+cudaError_t run_prefill_attn(hy_ctx* c, const float* q, int ldq, int layer, int past, int rows, float* out)
+{
+    using S = PaShape<KT>;
+    auto k = prefill_attn_kernel<KT>;
+    static unsigned long long configured = 0;
+    const unsigned long long bit = 1ull << (c->cfg.device & 63);
+    if (!(configured & bit))
+    {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
+        if (e != cudaSuccess) return e;
+        configured |= bit;
+    }
+    PrefillAttnArgs a{q, ldq, c->kc_layer(layer), c->vc_layer(layer), c->cfg.max_context, past, rows, out};
+    k<<<dim3((rows + kPaRows - 1) / kPaRows, kNumKVHeads), kPaThreads, S::SMEM, c->stream>>>(a);
+    return cudaGetLastError();
+}
+
 // Prompt prefill: the decoder over rows [0, seq) of ctx->prompt (the residual
 // stream, updated in place), in passes of up to pf_rows rows through all
-// layers; rope rows come from pre_cos / pre_sin. The projections of a pass run
-// as many-row tensor-core GEMMs; attention runs per 16-row slice in order (each
-// slice appends its K/V rows and attends to every earlier row). Leaves the
-// final-normed last row in ctx->hidden.
+// layers; rope rows come from pre_cos / pre_sin. Per layer: RMSNorm, the q/k/v
+// GEMM, RoPE + QK norm + KV append of every row, causal attention of the pass's
+// rows over the cache, then o_proj, RMSNorm, gate/up with SwiGLU and down_proj
+// (GEMMs with residual-add / SwiGLU epilogues). Leaves the final-normed last
+// row in ctx->hidden.
 template <typename WT, typename KT>
 cudaError_t enqueue_prefill_t(hy_ctx* c, int seq)
 {
@@ -1068,33 +1087,15 @@ cudaError_t enqueue_prefill_t(hy_ctx* c, int seq)
             if ((e = run_prefill_gemm<WT, PG_STORE>(c, c->pf_xn, kHidden, c->wqkv[l], kHidden, rows, kQKVRows, kHidden,
                                                     c->pf_qkv, kQKVRows)) != cudaSuccess)
                 return e;
-            for (int r0 = 0; r0 < rows; r0 += kMaxStepRows)
             {
-                AttnArgs at;
-                std::memset(&at, 0, sizeof(at));
-                at.qkv = c->pf_qkv + static_cast<size_t>(r0) * kQKVRows;
-                at.ldq = kQKVRows;
-                at.qn_w = c->qn(l);
-                at.kn_w = c->kn(l);
-                at.cos = c->pre_cos + static_cast<size_t>(p0 + r0) * kHeadDim;
-                at.sin = c->pre_sin + static_cast<size_t>(p0 + r0) * kHeadDim;
-                at.rope_state = 0;
-                at.kc = c->kc_layer(l);
-                at.vc = c->vc_layer(l);
-                at.cap = cfg.max_context;
-                at.st = nullptr;
-                at.past_fixed = p0 + r0;
-                at.rows = std::min(kMaxStepRows, rows - r0);
-                at.scale_log2 = cfg.attn_scale * 1.4426950408889634f;
-                at.eps = cfg.rms_norm_eps;
-                at.part = c->attn_part;
-                at.counter = c->attn_cnt + l * kNumKVHeads;
-                at.out = c->pf_attn + static_cast<size_t>(r0) * kQWidth;
-                at.err = c->err;
-                // Plain launch: the slice reads the K/V rows the previous slice appended
-                // before its griddepcontrol.wait.
-                t_next_plain = true;
-                if ((e = run_attn<16, KT>(c, at, kAttnSplitsVerify)) != cudaSuccess) return e;
+                PrefillRopeArgs ra{c->pf_qkv, kQKVRows,
+                                   c->pre_cos + static_cast<size_t>(p0) * kHeadDim,
+                                   c->pre_sin + static_cast<size_t>(p0) * kHeadDim,
+                                   c->qn(l), c->kn(l), c->kc_layer(l), c->vc_layer(l), cfg.max_context, p0,
+                                   cfg.rms_norm_eps, cfg.attn_scale * 1.4426950408889634f};
+                prefill_rope_kernel<KT><<<rows, 256, 0, c->stream>>>(ra);
+                if ((e = cudaGetLastError()) != cudaSuccess) return e;
+                if ((e = run_prefill_attn<KT>(c, c->pf_qkv, kQKVRows, l, p0, rows, c->pf_attn)) != cudaSuccess) return e;
             }
             if ((e = run_prefill_gemm<WT, PG_RESID>(c, c->pf_attn, kQWidth, c->wo[l], kQWidth, rows, kHidden, kQWidth, xr,
                                                     kHidden)) != cudaSuccess)

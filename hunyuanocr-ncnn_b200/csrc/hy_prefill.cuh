@@ -5,7 +5,7 @@
 //
 // Replaces, for a prompt of M rows, the decoder's Gemm layers
 // (export/text_decoder_kv.py:64-69, 93-95) that the reference runs once per
-// prefill over the whole prompt (src/text_runtime.cpp:1387-1420). The 16-row
+// prefill over the whole prompt (run_decoder_prefill, src/text_runtime.cpp:648-674). The 16-row
 // step kernels stream every weight once per 16 prompt rows; here a weight tile
 // is read once per 128 rows and the work is compute-bound.
 //
@@ -21,6 +21,7 @@
 // loads fall in 32 distinct banks. Two CTAs per SM.
 #pragma once
 
+#include "hy_attn.cuh"
 #include "hy_device.cuh"
 #include "hy_gemv.cuh"
 
@@ -199,6 +200,288 @@ __global__ void __launch_bounds__(kPgThreads, 2) prefill_gemm_kernel(const Prefi
                 }
             }
         }
+}
+
+
+// ---------------------------------------------------------------------------
+// Prefill attention.
+//
+// RoPE + QK RMSNorm + KV append for every row of a prefill pass (the same
+// per-head arithmetic as the decode/verify attention prologue): q heads are
+// rewritten in place (times scale * log2 e), k heads and v heads go to the
+// cache rows past .. past + rows - 1. One CTA per row, a warp per 4 heads.
+// ---------------------------------------------------------------------------
+struct PrefillRopeArgs {
+    float* qkv;   // [rows x ldq]: q [0, 2048) rewritten, k [2048, 3072), v [3072, 4096)
+    int ldq;
+    const float* cos;   // [rows x 128]
+    const float* sin;
+    const float* qn_w;
+    const float* kn_w;
+    void* kc;     // this layer's cache [8][cap][128] of KT
+    void* vc;
+    int cap, past;
+    float eps, scale_log2;
+};
+
+template <typename KT>
+__global__ void __launch_bounds__(256) prefill_rope_kernel(const PrefillRopeArgs a)
+{
+    const int m = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float* row = a.qkv + static_cast<size_t>(m) * a.ldq;
+    const float* c = a.cos + static_cast<size_t>(m) * kHeadDim;
+    const float* s = a.sin + static_cast<size_t>(m) * kHeadDim;
+    for (int j = warp; j < kNumQHeads + 2 * kNumKVHeads; j += 8)
+    {
+        if (j < kNumQHeads)
+        {
+            float* x = row + j * kHeadDim;
+            float o[4];
+            rope_norm_vec(x, c, s, a.qn_w, a.eps, lane, o);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) x[lane + 32 * i] = o[i] * a.scale_log2;
+        }
+        else if (j < kNumQHeads + kNumKVHeads)
+        {
+            const int h = j - kNumQHeads;
+            float o[4];
+            rope_norm_vec(row + kQWidth + h * kHeadDim, c, s, a.kn_w, a.eps, lane, o);
+            KT* dst = static_cast<KT*>(a.kc) + (static_cast<size_t>(h) * a.cap + a.past + m) * kHeadDim;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = from_f32<KT>(o[i]);
+        }
+        else
+        {
+            const int h = j - kNumQHeads - kNumKVHeads;
+            const float* x = row + kQWidth + kKVWidth + h * kHeadDim;
+            KT* dst = static_cast<KT*>(a.vc) + (static_cast<size_t>(h) * a.cap + a.past + m) * kHeadDim;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = from_f32<KT>(x[lane + 32 * i]);
+        }
+    }
+}
+
+// Causal attention of the rows of a prefill pass over the cache rows
+// [0, past + row] (PreciseSDPA::forward, src/precise_sdpa.cpp:281-329, with the
+// prefill mask of src/text_runtime.cpp:207-219), flash-attention style on the
+// tensor cores: S = Q K^T and O += P V as mma.sync m16n8k8 tf32 with the
+// three-term split, an online base-2 softmax in fp32 between them.
+//
+// CTA = 32 query rows x the 2 q heads of one KV head (64 query vectors, one
+// m16 tile per warp), so each K/V tile in shared memory serves both heads.
+// K/V stream in 32-key tiles through a 2-stage cp.async ring; the heaviest
+// (last) row blocks are scheduled first.
+// Within a 8-key step of P V the k order is permuted (logical k = t <-> key
+// 2t, k = t + 4 <-> key 2t + 1), so the S accumulator fragments are the P
+// operand fragments as they lie, with no shuffles.
+// ---------------------------------------------------------------------------
+constexpr int kPaRows = 32, kPaKeys = 32, kPaThreads = 128;
+
+template <typename KT>
+struct PaShape {
+    static constexpr int KP = (sizeof(KT) == 4) ? kHeadDim + 4 : kHeadDim + 8;   // K/V tile pitch (elements)
+    static constexpr int QP = kHeadDim + 4;                                      // Q tile pitch (floats)
+    static constexpr int Q_BYTES = 2 * kPaRows * QP * 4;
+    static constexpr int T_BYTES = kPaKeys * KP * static_cast<int>(sizeof(KT));
+    static constexpr int STAGE = 2 * T_BYTES;
+    static constexpr int SMEM = Q_BYTES + 2 * STAGE;
+    static_assert(Q_BYTES % 16 == 0 && T_BYTES % 16 == 0, "16-byte tile layout");
+};
+
+struct PrefillAttnArgs {
+    const float* q;   // [rows x ldq]: roped, normed q heads times scale * log2 e
+    int ldq;
+    const void* kc;   // this layer's cache [8][cap][128] of KT, rows [0, past + rows) written
+    const void* vc;
+    int cap, past, rows;
+    float* out;       // [rows x 2048]
+};
+
+template <typename KT>
+__global__ void __launch_bounds__(kPaThreads, 2) prefill_attn_kernel(const PrefillAttnArgs a)
+{
+    using S = PaShape<KT>;
+    constexpr int KP = S::KP, QP = S::QP;
+    constexpr bool KV_EXACT = sizeof(KT) == 2;
+    constexpr int EPC = 16 / static_cast<int>(sizeof(KT));
+    constexpr int CPR = kHeadDim / EPC;
+    extern __shared__ __align__(128) unsigned char smem[];
+    float* Qs = reinterpret_cast<float*>(smem);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int nqb = (a.rows + kPaRows - 1) / kPaRows;
+    const int qb = nqb - 1 - static_cast<int>(blockIdx.x);
+    const int kvh = blockIdx.y;
+    const int m0 = qb * kPaRows;
+    const int nkeys = min(a.past + m0 + kPaRows, a.past + a.rows);
+    const int nkb = (nkeys + kPaKeys - 1) / kPaKeys;
+    const KT* kbase = static_cast<const KT*>(a.kc) + static_cast<size_t>(kvh) * a.cap * kHeadDim;
+    const KT* vbase = static_cast<const KT*>(a.vc) + static_cast<size_t>(kvh) * a.cap * kHeadDim;
+
+    auto load_kv = [&](int slot, int kb) {
+        KT* Ks = reinterpret_cast<KT*>(smem + S::Q_BYTES + slot * S::STAGE);
+        KT* Vs = Ks + kPaKeys * KP;
+        for (int i = tid; i < kPaKeys * CPR; i += kPaThreads)
+        {
+            const int r = i / CPR, ch = i % CPR;
+            const int key = kb * kPaKeys + r;
+            const bool ok = key < nkeys;   // keys past the block's last row are zero-filled (and masked)
+            const size_t off = static_cast<size_t>(ok ? key : 0) * kHeadDim + ch * EPC;
+            cp_async16(Ks + r * KP + ch * EPC, kbase + off, ok);
+            cp_async16(Vs + r * KP + ch * EPC, vbase + off, ok);
+        }
+    };
+
+    // Query vector j = hl * 32 + r: row m0 + r, q head 2 kvh + hl.
+    for (int i = tid; i < 2 * kPaRows * (kHeadDim / 4); i += kPaThreads)
+    {
+        const int j = i / (kHeadDim / 4), ch = i % (kHeadDim / 4);
+        const int hl = j / kPaRows, r = j % kPaRows;
+        const bool ok = m0 + r < a.rows;
+        const float* src = a.q + static_cast<size_t>(ok ? m0 + r : 0) * a.ldq + (2 * kvh + hl) * kHeadDim + ch * 4;
+        cp_async16(Qs + j * QP + ch * 4, src, ok);
+    }
+    load_kv(0, 0);
+    cp_async_commit();
+
+    const int hl = warp >> 1, r0 = (warp & 1) * 16;
+    const float* Qw = Qs + (hl * kPaRows + r0) * QP;
+    const int pq0 = a.past + m0 + r0 + g, pq1 = pq0 + 8;   // positions of rows g and g + 8
+    float o[16][4];
+#pragma unroll
+    for (int dt = 0; dt < 16; ++dt) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.f;
+    float mrow0 = -INFINITY, mrow1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+
+    for (int kb = 0; kb < nkb; ++kb)
+    {
+        if (kb + 1 < nkb) load_kv((kb + 1) & 1, kb + 1);
+        cp_async_commit();
+        cp_async_wait<1>();
+        __syncthreads();
+        const KT* Ks = reinterpret_cast<const KT*>(smem + S::Q_BYTES + (kb & 1) * S::STAGE);
+        const KT* Vs = Ks + kPaKeys * KP;
+
+        // S = Q K^T for 16 rows x 32 keys.
+        float s[4][4];
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+#pragma unroll 4
+        for (int ks = 0; ks < kHeadDim / 8; ++ks)
+        {
+            const float* qa = Qw + g * QP + 8 * ks + t;
+            const float x[4] = {qa[0], qa[8 * QP], qa[4], qa[8 * QP + 4]};
+            unsigned ah[4], al[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+            {
+                ah[e] = tf32_head(x[e]);
+                al[e] = __float_as_uint(x[e] - __uint_as_float(ah[e]));
+            }
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt)
+            {
+                const KT* kr = Ks + (8 * nt + g) * KP + 8 * ks + t;
+                const float k0 = to_f32<KT>(kr[0]), k1 = to_f32<KT>(kr[4]);
+                const unsigned bh0 = tf32_head(k0), bh1 = tf32_head(k1);
+                mma_tf32(s[nt], al, bh0, bh1);
+                if constexpr (!KV_EXACT)
+                    mma_tf32(s[nt], ah, __float_as_uint(k0 - __uint_as_float(bh0)),
+                             __float_as_uint(k1 - __uint_as_float(bh1)));
+                mma_tf32(s[nt], ah, bh0, bh1);
+            }
+        }
+
+        // Causal mask, online softmax (scores are already in log2 units).
+        float mx0 = mrow0, mx1 = mrow1;
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e)
+            {
+                const int key = kb * kPaKeys + 8 * nt + 2 * t + e;
+                if (key > pq0) s[nt][e] = -INFINITY;
+                if (key > pq1) s[nt][2 + e] = -INFINITY;
+                mx0 = fmaxf(mx0, s[nt][e]);
+                mx1 = fmaxf(mx1, s[nt][2 + e]);
+            }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        // Key 0 is visible to every row, so mx0 / mx1 are finite from the first tile on.
+        const float c0 = exp2f(mrow0 - mx0), c1 = exp2f(mrow1 - mx1);
+        mrow0 = mx0;
+        mrow1 = mx1;
+        float ls0 = 0.f, ls1 = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e)
+            {
+                s[nt][e] = exp2f(s[nt][e] - mx0);
+                s[nt][2 + e] = exp2f(s[nt][2 + e] - mx1);
+                ls0 += s[nt][e];
+                ls1 += s[nt][2 + e];
+            }
+        l0 = l0 * c0 + ls0;   // per-lane partial sums; the quad adds them at the end
+        l1 = l1 * c1 + ls1;
+#pragma unroll
+        for (int dt = 0; dt < 16; ++dt)
+        {
+            o[dt][0] *= c0;
+            o[dt][1] *= c0;
+            o[dt][2] *= c1;
+            o[dt][3] *= c1;
+        }
+
+        // O += P V: 4 steps of 8 keys x 16 tiles of 8 dims.
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+        {
+            const float p[4] = {s[j][0], s[j][2], s[j][1], s[j][3]};
+            unsigned ph[4], pl[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+            {
+                ph[e] = tf32_head(p[e]);
+                pl[e] = __float_as_uint(p[e] - __uint_as_float(ph[e]));
+            }
+            const KT* vr = Vs + (8 * j + 2 * t) * KP + g;
+#pragma unroll
+            for (int dt = 0; dt < 16; ++dt)
+            {
+                const float v0 = to_f32<KT>(vr[8 * dt]), v1 = to_f32<KT>(vr[KP + 8 * dt]);
+                const unsigned bh0 = tf32_head(v0), bh1 = tf32_head(v1);
+                mma_tf32(o[dt], pl, bh0, bh1);
+                if constexpr (!KV_EXACT)
+                    mma_tf32(o[dt], ph, __float_as_uint(v0 - __uint_as_float(bh0)),
+                             __float_as_uint(v1 - __uint_as_float(bh1)));
+                mma_tf32(o[dt], ph, bh0, bh1);
+            }
+        }
+        __syncthreads();   // every warp is done with this slot before it is refilled
+    }
+    cp_async_wait<0>();
+
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
+    const int h = 2 * kvh + hl;
+    const int ma = m0 + r0 + g, mb = ma + 8;
+#pragma unroll
+    for (int dt = 0; dt < 16; ++dt)
+    {
+        const int d = h * kHeadDim + 8 * dt + 2 * t;
+        if (ma < a.rows)
+            *reinterpret_cast<float2*>(a.out + static_cast<size_t>(ma) * kQWidth + d) =
+                make_float2(o[dt][0] * inv0, o[dt][1] * inv0);
+        if (mb < a.rows)
+            *reinterpret_cast<float2*>(a.out + static_cast<size_t>(mb) * kQWidth + d) =
+                make_float2(o[dt][2] * inv1, o[dt][3] * inv1);
+    }
 }
 
 }  // namespace hy
