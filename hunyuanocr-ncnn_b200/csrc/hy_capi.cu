@@ -7,6 +7,7 @@
 #include "hy_gemv.cuh"
 #include "hy_mega.cuh"
 #include "hy_prefill.cuh"
+#include "hy_umma.cuh"
 #include "hy_util.cuh"
 
 #include "hy_decode.h"
@@ -108,12 +109,16 @@ struct hy_ctx {
     int* feat_idx = nullptr;    // [max_prefill]
     float* feats = nullptr;     // vision features [max_prefill x 1024]
     float* logits = nullptr;    // [16 x V] (lazily)
-    // Prompt prefill in chunks of up to pf_rows rows (the residual stream is ctx->prompt).
-    int pf_rows = 0;
-    float* pf_xn = nullptr;     // [pf_rows x 1024] normed rows
-    float* pf_qkv = nullptr;    // [pf_rows x 4096]
-    float* pf_attn = nullptr;   // [pf_rows x 2048]
-    float* pf_act = nullptr;    // [pf_rows x ffn]
+    // Prompt prefill in passes of up to pf_rows rows (the residual stream is ctx->prompt).
+    // GEMM operands are split (hi / lo) and tiled for the tensor core (hy_umma.cuh);
+    // activation buffers hold pf_pad = pf_rows rounded up to 128 rows.
+    int pf_rows = 0, pf_pad = 0;
+    float* pf_qkv = nullptr;                         // [pf_rows x 4096] row-major
+    float* pf_a_hi = nullptr, *pf_a_lo = nullptr;    // normed rows, tiled [pf_pad x 1024]
+    float* pf_at_hi = nullptr, *pf_at_lo = nullptr;  // attention output, tiled [pf_pad x 2048]
+    float* pf_ac_hi = nullptr, *pf_ac_lo = nullptr;  // SwiGLU output, tiled [pf_pad x ffn]
+    // Per layer: q/k/v, o, gate/up, down weights, tiled hi (and lo for fp32 weights).
+    std::vector<float*> tq_hi, tq_lo, to_hi, to_lo, tg_hi, tg_lo, td_hi, td_lo;
     int* err = nullptr;
     DecodeState* h_st = nullptr;  // pinned mirror
     int kv_len = 0;               // host mirror of the sequence length
@@ -767,10 +772,42 @@ int alloc_ctx(hy_ctx* c)
     if ((rc = dalloc(c, &c->ids_buf, pre_rows))) return rc;
     if ((rc = dalloc(c, &c->feat_idx, pre_rows))) return rc;
     c->pf_rows = std::min(cfg.max_prefill, kPrefillChunk);
-    if ((rc = dalloc(c, &c->pf_xn, static_cast<size_t>(c->pf_rows) * kHidden))) return rc;
-    if ((rc = dalloc(c, &c->pf_qkv, static_cast<size_t>(c->pf_rows) * kQKVRows))) return rc;
-    if ((rc = dalloc(c, &c->pf_attn, static_cast<size_t>(c->pf_rows) * kQWidth))) return rc;
-    if ((rc = dalloc(c, &c->pf_act, static_cast<size_t>(c->pf_rows) * ffn))) return rc;
+    c->pf_pad = (c->pf_rows + kUmBM - 1) / kUmBM * kUmBM;
+    {
+        const size_t pad = static_cast<size_t>(c->pf_pad);
+        if ((rc = dalloc(c, &c->pf_qkv, static_cast<size_t>(c->pf_rows) * kQKVRows))) return rc;
+        float** bufs[6] = {&c->pf_a_hi, &c->pf_a_lo, &c->pf_at_hi, &c->pf_at_lo, &c->pf_ac_hi, &c->pf_ac_lo};
+        const size_t cols[6] = {kHidden, kHidden, kQWidth, kQWidth, static_cast<size_t>(ffn), static_cast<size_t>(ffn)};
+        for (int i = 0; i < 6; ++i)
+            if ((rc = dalloc(c, bufs[i], pad * cols[i]))) return rc;
+    }
+    {
+        // Tiled prefill weights: hi for every weight, lo for fp32 weights.
+        const size_t per_layer = static_cast<size_t>(kQKVRows) * kHidden + static_cast<size_t>(kHidden) * kQWidth +
+                                 static_cast<size_t>(2 * ffn) * kHidden + static_cast<size_t>(kHidden) * ffn;
+        const int planes = (cfg.weight_dtype == HY_DTYPE_BF16) ? 1 : 2;
+        float* tw = nullptr;
+        if ((rc = dalloc(c, &tw, per_layer * L * planes))) return rc;
+        for (int pl = 0; pl < planes; ++pl)
+            for (int l = 0; l < L; ++l)
+            {
+                float* p = tw + (static_cast<size_t>(pl) * L + l) * per_layer;
+                (pl ? c->tq_lo : c->tq_hi).push_back(p);
+                p += static_cast<size_t>(kQKVRows) * kHidden;
+                (pl ? c->to_lo : c->to_hi).push_back(p);
+                p += static_cast<size_t>(kHidden) * kQWidth;
+                (pl ? c->tg_lo : c->tg_hi).push_back(p);
+                p += static_cast<size_t>(2 * ffn) * kHidden;
+                (pl ? c->td_lo : c->td_hi).push_back(p);
+            }
+        if (planes == 1)
+        {
+            c->tq_lo.assign(L, nullptr);
+            c->to_lo.assign(L, nullptr);
+            c->tg_lo.assign(L, nullptr);
+            c->td_lo.assign(L, nullptr);
+        }
+    }
     if ((rc = dalloc(c, &c->x, kMaxStepRows * kHidden))) return rc;
     if ((rc = dalloc(c, &c->qkv, kMaxStepRows * kQKVRows))) return rc;
     if ((rc = dalloc(c, &c->attn, kMaxStepRows * kQWidth))) return rc;
@@ -987,9 +1024,39 @@ void free_ctx(hy_ctx* c)
     delete c;
 }
 
+// Splits and tiles every decoder weight for the prefill GEMMs (after the
+// weights are loaded or synthesised).
+template <typename WT>
+int tile_weights_t(hy_ctx* c)
+{
+    const int L = c->cfg.num_layers, ffn = c->cfg.ffn_dim;
+    for (int l = 0; l < L; ++l)
+    {
+        const void* src[4] = {c->wqkv[l], c->wo[l], c->wgu[l], c->wd[l]};
+        float* hi[4] = {c->tq_hi[l], c->to_hi[l], c->tg_hi[l], c->td_hi[l]};
+        float* lo[4] = {c->tq_lo[l], c->to_lo[l], c->tg_lo[l], c->td_lo[l]};
+        const int R[4] = {kQKVRows, kHidden, 2 * ffn, kHidden}, K[4] = {kHidden, kQWidth, kHidden, ffn};
+        for (int i = 0; i < 4; ++i)
+        {
+            const size_t n = static_cast<size_t>(R[i]) * (K[i] / 4);
+            tile_weight_kernel<WT><<<static_cast<unsigned>((n + 255) / 256), 256, 0, c->stream>>>(
+                static_cast<const WT*>(src[i]), R[i], K[i], hi[i], lo[i]);
+            HY_CUDA(cudaGetLastError());
+        }
+    }
+    HY_CUDA(cudaStreamSynchronize(c->stream));
+    return HY_OK;
+}
+
 int finish_create(hy_ctx* c, hy_ctx** out)
 {
-    int rc = ensure_graphs(c);
+    int rc = (c->cfg.weight_dtype == HY_DTYPE_BF16) ? tile_weights_t<__nv_bfloat16>(c) : tile_weights_t<float>(c);
+    if (rc)
+    {
+        free_ctx(c);
+        return rc;
+    }
+    rc = ensure_graphs(c);
     if (rc)
     {
         free_ctx(c);
@@ -1025,12 +1092,11 @@ int run_direct_step(hy_ctx* c, int rows, int past, const float* cos, const float
     return HY_OK;
 }
 
-template <typename WT, int EPI>
-cudaError_t run_prefill_gemm(hy_ctx* c, const float* A, int lda, const void* W, int ldw, int M, int N, int K, float* C,
-                             int ldc)
+template <int EPI, int BN, bool B_SPLIT>
+cudaError_t run_umma_gemm_bn(hy_ctx* c, const UmmaGemmArgs& a)
 {
-    using S = PgShape<WT>;
-    auto k = prefill_gemm_kernel<WT, EPI>;
+    using S = UmShape<BN, B_SPLIT>;
+    auto k = umma_gemm_kernel<EPI, BN, B_SPLIT>;
     static unsigned long long configured = 0;
     const unsigned long long bit = 1ull << (c->cfg.device & 63);
     if (!(configured & bit))
@@ -1039,14 +1105,42 @@ cudaError_t run_prefill_gemm(hy_ctx* c, const float* A, int lda, const void* W, 
         if (e != cudaSuccess) return e;
         configured |= bit;
     }
-    if (N % kPgBN != 0 || K % kPgBK != 0 || M <= 0) return cudaErrorInvalidValue;
-    PrefillGemmArgs a{A, lda, W, ldw, M, N, K, C, ldc};
-    k<<<dim3(N / kPgBN, (M + kPgBM - 1) / kPgBM), kPgThreads, S::SMEM, c->stream>>>(a);
+    k<<<dim3(a.N / BN, (a.M + kUmBM - 1) / kUmBM), kUmThreads, S::SMEM, c->stream>>>(a);
     return cudaGetLastError();
 }
 
+// C = A . W^T on the tcgen05 tensor cores from split, tiled operands; 128 x 128
+// output tiles, or 128 x 64 when N is small (1024 rows: 2x the CTAs).
+template <int EPI>
+cudaError_t run_prefill_gemm(hy_ctx* c, UmmaGemmArgs a)
+{
+    if (a.M <= 0 || a.N % 64 != 0 || a.K % kUmBK != 0 || a.a_rows % kUmBM != 0 || a.a_rows < a.M)
+        return cudaErrorInvalidValue;
+    a.err = c->err;
+    const bool split = a.w_lo != nullptr;
+    if (a.N % 128 == 0 && a.N > 2048)
+        return split ? run_umma_gemm_bn<EPI, 128, true>(c, a) : run_umma_gemm_bn<EPI, 128, false>(c, a);
+    return split ? run_umma_gemm_bn<EPI, 64, true>(c, a) : run_umma_gemm_bn<EPI, 64, false>(c, a);
+}
+
+UmmaGemmArgs gemm_args(const float* a_hi, const float* a_lo, int a_rows, const float* w_hi, const float* w_lo, int M,
+                       int N, int K)
+{
+    UmmaGemmArgs g;
+    std::memset(&g, 0, sizeof(g));
+    g.a_hi = a_hi;
+    g.a_lo = a_lo;
+    g.a_rows = a_rows;
+    g.w_hi = w_hi;
+    g.w_lo = w_lo;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    return g;
+}
+
 template <typename KT>
-cudaError_t run_prefill_attn(hy_ctx* c, const float* q, int ldq, int layer, int past, int rows, float* out)
+cudaError_t run_prefill_attn(hy_ctx* c, const float* q, int ldq, int layer, int past, int rows, int rows_pad)
 {
     using S = PaShape<KT>;
     auto k = prefill_attn_kernel<KT>;
@@ -1058,19 +1152,20 @@ cudaError_t run_prefill_attn(hy_ctx* c, const float* q, int ldq, int layer, int 
         if (e != cudaSuccess) return e;
         configured |= bit;
     }
-    PrefillAttnArgs a{q, ldq, c->kc_layer(layer), c->vc_layer(layer), c->cfg.max_context, past, rows, out};
+    PrefillAttnArgs a{q, ldq, c->kc_layer(layer), c->vc_layer(layer), c->cfg.max_context, past, rows,
+                      c->pf_at_hi, c->pf_at_lo, rows_pad};
     k<<<dim3((rows + kPaRows - 1) / kPaRows, kNumKVHeads), kPaThreads, S::SMEM, c->stream>>>(a);
     return cudaGetLastError();
 }
 
 // Prompt prefill: the decoder over rows [0, seq) of ctx->prompt (the residual
 // stream, updated in place), in passes of up to pf_rows rows through all
-// layers; rope rows come from pre_cos / pre_sin. Per layer: RMSNorm, the q/k/v
-// GEMM, RoPE + QK norm + KV append of every row, causal attention of the pass's
-// rows over the cache, then o_proj, RMSNorm, gate/up with SwiGLU and down_proj
-// (GEMMs with residual-add / SwiGLU epilogues). Leaves the final-normed last
-// row in ctx->hidden.
-template <typename WT, typename KT>
+// layers; rope rows come from pre_cos / pre_sin. Per layer: RMSNorm (written
+// split and tiled), the q/k/v GEMM, RoPE + QK norm + KV append of every row,
+// causal attention of the pass's rows over the cache, then o_proj (residual
+// add), RMSNorm, gate/up with SwiGLU (written split and tiled) and down_proj
+// (residual add). Leaves the final-normed last row in ctx->hidden.
+template <typename KT>
 cudaError_t enqueue_prefill_t(hy_ctx* c, int seq)
 {
     const hy_config& cfg = c->cfg;
@@ -1079,35 +1174,40 @@ cudaError_t enqueue_prefill_t(hy_ctx* c, int seq)
     for (int p0 = 0; p0 < seq; p0 += c->pf_rows)
     {
         const int rows = std::min(c->pf_rows, seq - p0);
+        const int pad = (rows + kUmBM - 1) / kUmBM * kUmBM;
         float* xr = c->prompt + static_cast<size_t>(p0) * kHidden;
         for (int l = 0; l < cfg.num_layers; ++l)
         {
-            rmsnorm_rows_kernel<<<rows, 256, 0, c->stream>>>(xr, c->in_norm(l), cfg.rms_norm_eps, c->pf_xn, kHidden);
+            rmsnorm_tiled_kernel<<<rows, 256, 0, c->stream>>>(xr, c->in_norm(l), cfg.rms_norm_eps, pad, c->pf_a_hi,
+                                                               c->pf_a_lo);
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
-            if ((e = run_prefill_gemm<WT, PG_STORE>(c, c->pf_xn, kHidden, c->wqkv[l], kHidden, rows, kQKVRows, kHidden,
-                                                    c->pf_qkv, kQKVRows)) != cudaSuccess)
-                return e;
-            {
-                PrefillRopeArgs ra{c->pf_qkv, kQKVRows,
-                                   c->pre_cos + static_cast<size_t>(p0) * kHeadDim,
-                                   c->pre_sin + static_cast<size_t>(p0) * kHeadDim,
-                                   c->qn(l), c->kn(l), c->kc_layer(l), c->vc_layer(l), cfg.max_context, p0,
-                                   cfg.rms_norm_eps, cfg.attn_scale * 1.4426950408889634f};
-                prefill_rope_kernel<KT><<<rows, 256, 0, c->stream>>>(ra);
-                if ((e = cudaGetLastError()) != cudaSuccess) return e;
-                if ((e = run_prefill_attn<KT>(c, c->pf_qkv, kQKVRows, l, p0, rows, c->pf_attn)) != cudaSuccess) return e;
-            }
-            if ((e = run_prefill_gemm<WT, PG_RESID>(c, c->pf_attn, kQWidth, c->wo[l], kQWidth, rows, kHidden, kQWidth, xr,
-                                                    kHidden)) != cudaSuccess)
-                return e;
-            rmsnorm_rows_kernel<<<rows, 256, 0, c->stream>>>(xr, c->post_norm(l), cfg.rms_norm_eps, c->pf_xn, kHidden);
+            UmmaGemmArgs q = gemm_args(c->pf_a_hi, c->pf_a_lo, pad, c->tq_hi[l], c->tq_lo[l], rows, kQKVRows, kHidden);
+            q.C = c->pf_qkv;
+            q.ldc = kQKVRows;
+            if ((e = run_prefill_gemm<UG_STORE>(c, q)) != cudaSuccess) return e;
+            PrefillRopeArgs ra{c->pf_qkv, kQKVRows,
+                               c->pre_cos + static_cast<size_t>(p0) * kHeadDim,
+                               c->pre_sin + static_cast<size_t>(p0) * kHeadDim,
+                               c->qn(l), c->kn(l), c->kc_layer(l), c->vc_layer(l), cfg.max_context, p0,
+                               cfg.rms_norm_eps, cfg.attn_scale * 1.4426950408889634f};
+            prefill_rope_kernel<KT><<<rows, 256, 0, c->stream>>>(ra);
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
-            if ((e = run_prefill_gemm<WT, PG_SWIGLU>(c, c->pf_xn, kHidden, c->wgu[l], kHidden, rows, 2 * ffn, kHidden,
-                                                     c->pf_act, ffn)) != cudaSuccess)
-                return e;
-            if ((e = run_prefill_gemm<WT, PG_RESID>(c, c->pf_act, ffn, c->wd[l], ffn, rows, kHidden, ffn, xr, kHidden)) !=
-                cudaSuccess)
-                return e;
+            if ((e = run_prefill_attn<KT>(c, c->pf_qkv, kQKVRows, l, p0, rows, pad)) != cudaSuccess) return e;
+            UmmaGemmArgs o = gemm_args(c->pf_at_hi, c->pf_at_lo, pad, c->to_hi[l], c->to_lo[l], rows, kHidden, kQWidth);
+            o.C = xr;
+            o.ldc = kHidden;
+            if ((e = run_prefill_gemm<UG_RESID>(c, o)) != cudaSuccess) return e;
+            rmsnorm_tiled_kernel<<<rows, 256, 0, c->stream>>>(xr, c->post_norm(l), cfg.rms_norm_eps, pad, c->pf_a_hi,
+                                                               c->pf_a_lo);
+            if ((e = cudaGetLastError()) != cudaSuccess) return e;
+            UmmaGemmArgs gu = gemm_args(c->pf_a_hi, c->pf_a_lo, pad, c->tg_hi[l], c->tg_lo[l], rows, 2 * ffn, kHidden);
+            gu.act_hi = c->pf_ac_hi;
+            gu.act_lo = c->pf_ac_lo;
+            if ((e = run_prefill_gemm<UG_SWIGLU_TILED>(c, gu)) != cudaSuccess) return e;
+            UmmaGemmArgs d = gemm_args(c->pf_ac_hi, c->pf_ac_lo, pad, c->td_hi[l], c->td_lo[l], rows, kHidden, ffn);
+            d.C = xr;
+            d.ldc = kHidden;
+            if ((e = run_prefill_gemm<UG_RESID>(c, d)) != cudaSuccess) return e;
         }
         if (p0 + rows == seq)
         {
@@ -1122,12 +1222,8 @@ cudaError_t enqueue_prefill_t(hy_ctx* c, int seq)
 
 int run_prefill(hy_ctx* c, int seq)
 {
-    const bool wb = c->cfg.weight_dtype == HY_DTYPE_BF16, kb = c->cfg.kv_dtype == HY_DTYPE_BF16;
-    cudaError_t e;
-    if (!wb && !kb) e = enqueue_prefill_t<float, float>(c, seq);
-    else if (!wb && kb) e = enqueue_prefill_t<float, __nv_bfloat16>(c, seq);
-    else if (wb && !kb) e = enqueue_prefill_t<__nv_bfloat16, float>(c, seq);
-    else e = enqueue_prefill_t<__nv_bfloat16, __nv_bfloat16>(c, seq);
+    const cudaError_t e = (c->cfg.kv_dtype == HY_DTYPE_BF16) ? enqueue_prefill_t<__nv_bfloat16>(c, seq)
+                                                             : enqueue_prefill_t<float>(c, seq);
     if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("prefill launch: ") + cudaGetErrorString(e));
     return HY_OK;
 }
