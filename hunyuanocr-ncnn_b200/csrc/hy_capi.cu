@@ -117,6 +117,12 @@ struct hy_ctx {
     float* pf_a_hi = nullptr, *pf_a_lo = nullptr;    // normed rows, tiled [pf_pad x 1024]
     float* pf_at_hi = nullptr, *pf_at_lo = nullptr;  // attention output, tiled [pf_pad x 2048]
     float* pf_ac_hi = nullptr, *pf_ac_lo = nullptr;  // SwiGLU output, tiled [pf_pad x ffn]
+    // Prefill attention work items (row block, key tiles, partial slot), merge items and partials.
+    int4* pf_work = nullptr;
+    int4* pf_merge = nullptr;
+    float* pf_part = nullptr;
+    int pf_nwork = 0, pf_nmerge = 0;
+    std::vector<int4> h_work, h_merge;
     // Per layer: q/k/v, o, gate/up, down weights, tiled hi (and lo for fp32 weights).
     std::vector<float*> tq_hi, tq_lo, to_hi, to_lo, tg_hi, tg_lo, td_hi, td_lo;
     int* err = nullptr;
@@ -780,6 +786,10 @@ int alloc_ctx(hy_ctx* c)
         const size_t cols[6] = {kHidden, kHidden, kQWidth, kQWidth, static_cast<size_t>(ffn), static_cast<size_t>(ffn)};
         for (int i = 0; i < 6; ++i)
             if ((rc = dalloc(c, bufs[i], pad * cols[i]))) return rc;
+        const size_t nqb = pad / kPaRows;
+        if ((rc = dalloc(c, &c->pf_work, nqb * kPaMaxChunks))) return rc;
+        if ((rc = dalloc(c, &c->pf_merge, nqb))) return rc;
+        if ((rc = dalloc(c, &c->pf_part, nqb * kPaMaxChunks * kNumKVHeads * 64 * kPaPartStride))) return rc;
     }
     {
         // Tiled prefill weights: hi for every weight, lo for fp32 weights.
@@ -1153,9 +1163,47 @@ cudaError_t run_prefill_attn(hy_ctx* c, const float* q, int ldq, int layer, int 
         configured |= bit;
     }
     PrefillAttnArgs a{q, ldq, c->kc_layer(layer), c->vc_layer(layer), c->cfg.max_context, past, rows,
-                      c->pf_at_hi, c->pf_at_lo, rows_pad};
-    k<<<dim3((rows + kPaRows - 1) / kPaRows, kNumKVHeads), kPaThreads, S::SMEM, c->stream>>>(a);
+                      c->pf_at_hi, c->pf_at_lo, rows_pad, c->pf_work, c->pf_part};
+    k<<<dim3(c->pf_nwork, kNumKVHeads), kPaThreads, S::SMEM, c->stream>>>(a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || c->pf_nmerge == 0) return e;
+    prefill_attn_merge_kernel<<<dim3(c->pf_nmerge, kNumKVHeads), 256, 0, c->stream>>>(c->pf_part, c->pf_merge, rows,
+                                                                                     rows_pad, c->pf_at_hi, c->pf_at_lo);
     return cudaGetLastError();
+}
+
+// Work items of the prefill attention for one pass (rows at positions past ..):
+// each 32-row block's keys [0, past + block end) in chunks of at least 8 tiles
+// of 32 keys and at most kPaMaxChunks chunks per block, longest blocks first.
+cudaError_t plan_prefill_attn(hy_ctx* c, int past, int rows)
+{
+    const int nqb = (rows + kPaRows - 1) / kPaRows;
+    const int max_nkb = (past + rows + kPaKeys - 1) / kPaKeys;
+    const int ckb = std::max(kPaMinChunkTiles, (max_nkb + kPaMaxChunks - 1) / kPaMaxChunks);
+    c->h_work.clear();
+    c->h_merge.clear();
+    int slot = 0;
+    for (int qb = nqb - 1; qb >= 0; --qb)
+    {
+        const int nkeys = std::min(past + qb * kPaRows + kPaRows, past + rows);
+        const int nkb = (nkeys + kPaKeys - 1) / kPaKeys;
+        const int nch = (nkb + ckb - 1) / ckb;
+        if (nch == 1)
+        {
+            c->h_work.push_back(make_int4(qb, 0, nkb, -1));
+            continue;
+        }
+        c->h_merge.push_back(make_int4(qb, slot, nch, 0));
+        for (int ch = 0; ch < nch; ++ch)
+            c->h_work.push_back(make_int4(qb, ch * ckb, std::min(nkb, (ch + 1) * ckb), slot++));
+    }
+    c->pf_nwork = static_cast<int>(c->h_work.size());
+    c->pf_nmerge = static_cast<int>(c->h_merge.size());
+    cudaError_t e = cudaMemcpyAsync(c->pf_work, c->h_work.data(), sizeof(int4) * c->h_work.size(),
+                                    cudaMemcpyHostToDevice, c->stream);
+    if (e != cudaSuccess || c->h_merge.empty()) return e;
+    return cudaMemcpyAsync(c->pf_merge, c->h_merge.data(), sizeof(int4) * c->h_merge.size(), cudaMemcpyHostToDevice,
+                           c->stream);
 }
 
 // Prompt prefill: the decoder over rows [0, seq) of ctx->prompt (the residual
@@ -1176,6 +1224,7 @@ cudaError_t enqueue_prefill_t(hy_ctx* c, int seq)
         const int rows = std::min(c->pf_rows, seq - p0);
         const int pad = (rows + kUmBM - 1) / kUmBM * kUmBM;
         float* xr = c->prompt + static_cast<size_t>(p0) * kHidden;
+        if ((e = plan_prefill_attn(c, p0, rows)) != cudaSuccess) return e;
         for (int l = 0; l < cfg.num_layers; ++l)
         {
             rmsnorm_tiled_kernel<<<rows, 256, 0, c->stream>>>(xr, c->in_norm(l), cfg.rms_norm_eps, pad, c->pf_a_hi,

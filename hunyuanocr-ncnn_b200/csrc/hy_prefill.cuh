@@ -87,14 +87,22 @@ __global__ void __launch_bounds__(256) prefill_rope_kernel(const PrefillRopeArgs
 // three-term split, an online base-2 softmax in fp32 between them.
 //
 // CTA = 32 query rows x the 2 q heads of one KV head (64 query vectors, one
-// m16 tile per warp), so each K/V tile in shared memory serves both heads.
-// K/V stream in 32-key tiles through a 2-stage cp.async ring; the heaviest
-// (last) row blocks are scheduled first.
+// m16 tile per warp), so each K/V tile in shared memory serves both heads,
+// over one chunk of that row block's keys (a work item): K/V stream in 32-key
+// tiles through a 2-stage cp.async ring. A row block whose keys span several
+// chunks (the causal mask makes later blocks longer) leaves per-chunk partials
+// (running max, sum, unnormalised output) that prefill_attn_merge_kernel
+// combines; a single-chunk block writes its output directly. Outputs are
+// written split and tiled for the o_proj GEMM.
 // Within a 8-key step of P V the k order is permuted (logical k = t <-> key
 // 2t, k = t + 4 <-> key 2t + 1), so the S accumulator fragments are the P
 // operand fragments as they lie, with no shuffles.
 // ---------------------------------------------------------------------------
 constexpr int kPaRows = 32, kPaKeys = 32, kPaThreads = 128;
+constexpr int kPaMaxChunks = 4;            // chunks per row block at most
+constexpr int kPaMinChunkTiles = 8;        // 32-key tiles per chunk at least
+constexpr int kPaPartStride = 132;         // (max, sum, -, -) + out[128]
+constexpr float kPaMasked = -1.0e30f;      // masked score (finite: a fully masked chunk merges with weight 0)
 
 template <typename KT>
 struct PaShape {
@@ -116,6 +124,8 @@ struct PrefillAttnArgs {
     float* out_hi;    // output [rows x 2048], split and tiled (rows_pad rows) for the o_proj GEMM
     float* out_lo;
     int rows_pad;
+    const int4* work; // per CTA (blockIdx.x): row block, first and end 32-key tile, partial slot (-1: direct)
+    float* part;      // [slot][8 KV heads][64 query vectors][kPaPartStride]
 };
 
 template <typename KT>
@@ -131,12 +141,11 @@ __global__ void __launch_bounds__(kPaThreads, 2) prefill_attn_kernel(const Prefi
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
-    const int nqb = (a.rows + kPaRows - 1) / kPaRows;
-    const int qb = nqb - 1 - static_cast<int>(blockIdx.x);
+    const int4 wk = a.work[blockIdx.x];
+    const int qb = wk.x, kb0 = wk.y, kb1 = wk.z, slot = wk.w;
     const int kvh = blockIdx.y;
     const int m0 = qb * kPaRows;
     const int nkeys = min(a.past + m0 + kPaRows, a.past + a.rows);
-    const int nkb = (nkeys + kPaKeys - 1) / kPaKeys;
     const KT* kbase = static_cast<const KT*>(a.kc) + static_cast<size_t>(kvh) * a.cap * kHeadDim;
     const KT* vbase = static_cast<const KT*>(a.vc) + static_cast<size_t>(kvh) * a.cap * kHeadDim;
 
@@ -163,7 +172,7 @@ __global__ void __launch_bounds__(kPaThreads, 2) prefill_attn_kernel(const Prefi
         const float* src = a.q + static_cast<size_t>(ok ? m0 + r : 0) * a.ldq + (2 * kvh + hl) * kHeadDim + ch * 4;
         cp_async16(Qs + j * QP + ch * 4, src, ok);
     }
-    load_kv(0, 0);
+    load_kv(0, kb0);
     cp_async_commit();
 
     const int hl = warp >> 1, r0 = (warp & 1) * 16;
@@ -172,15 +181,16 @@ __global__ void __launch_bounds__(kPaThreads, 2) prefill_attn_kernel(const Prefi
     float o[16][4];
 #pragma unroll
     for (int dt = 0; dt < 16; ++dt) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.f;
-    float mrow0 = -INFINITY, mrow1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float mrow0 = kPaMasked, mrow1 = kPaMasked, l0 = 0.f, l1 = 0.f;
 
-    for (int kb = 0; kb < nkb; ++kb)
+    for (int kb = kb0; kb < kb1; ++kb)
     {
-        if (kb + 1 < nkb) load_kv((kb + 1) & 1, kb + 1);
+        const int it = kb - kb0;
+        if (kb + 1 < kb1) load_kv((it + 1) & 1, kb + 1);
         cp_async_commit();
         cp_async_wait<1>();
         __syncthreads();
-        const KT* Ks = reinterpret_cast<const KT*>(smem + S::Q_BYTES + (kb & 1) * S::STAGE);
+        const KT* Ks = reinterpret_cast<const KT*>(smem + S::Q_BYTES + (it & 1) * S::STAGE);
         const KT* Vs = Ks + kPaKeys * KP;
 
         // S = Q K^T for 16 rows x 32 keys.
@@ -221,8 +231,8 @@ __global__ void __launch_bounds__(kPaThreads, 2) prefill_attn_kernel(const Prefi
             for (int e = 0; e < 2; ++e)
             {
                 const int key = kb * kPaKeys + 8 * nt + 2 * t + e;
-                if (key > pq0) s[nt][e] = -INFINITY;
-                if (key > pq1) s[nt][2 + e] = -INFINITY;
+                if (key > pq0) s[nt][e] = kPaMasked;
+                if (key > pq1) s[nt][2 + e] = kPaMasked;
                 mx0 = fmaxf(mx0, s[nt][e]);
                 mx1 = fmaxf(mx1, s[nt][2 + e]);
             }
@@ -230,7 +240,9 @@ __global__ void __launch_bounds__(kPaThreads, 2) prefill_attn_kernel(const Prefi
         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-        // Key 0 is visible to every row, so mx0 / mx1 are finite from the first tile on.
+        // Keys come in increasing order: a row's first tile with a visible key makes its
+        // max a real score, after which masked scores weigh exp2(-1e30 - max) = 0. A row
+        // with no visible key in this chunk keeps max = -1e30 and merges with weight 0.
         const float c0 = exp2f(mrow0 - mx0), c1 = exp2f(mrow1 - mx1);
         mrow0 = mx0;
         mrow1 = mx1;
@@ -289,31 +301,97 @@ __global__ void __launch_bounds__(kPaThreads, 2) prefill_attn_kernel(const Prefi
     l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-    const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
     const int h = 2 * kvh + hl;
     const int ma = m0 + r0 + g, mb = ma + 8;
+    if (slot >= 0)
+    {
+        // Partial of this chunk: (max, sum) per query vector, unnormalised output.
+        float* pa = a.part + ((static_cast<size_t>(slot) * kNumKVHeads + kvh) * 64 + hl * kPaRows + r0 + g) * kPaPartStride;
+        float* pb = pa + 8 * kPaPartStride;
+        if (t == 0)
+        {
+            pa[0] = mrow0;
+            pa[1] = l0;
+            pb[0] = mrow1;
+            pb[1] = l1;
+        }
+#pragma unroll
+        for (int dt = 0; dt < 16; ++dt)
+        {
+            *reinterpret_cast<float2*>(pa + 4 + 8 * dt + 2 * t) = make_float2(o[dt][0], o[dt][1]);
+            *reinterpret_cast<float2*>(pb + 4 + 8 * dt + 2 * t) = make_float2(o[dt][2], o[dt][3]);
+        }
+        return;
+    }
+    const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
 #pragma unroll
     for (int dt = 0; dt < 16; ++dt)
     {
         const int d = h * kHeadDim + 8 * dt + 2 * t;
-        float h0, l0, h1, l1;
+        float xh, xl, yh, yl;
         if (ma < a.rows)
         {
-            split_hi_lo(o[dt][0] * inv0, h0, l0);
-            split_hi_lo(o[dt][1] * inv0, h1, l1);
+            split_hi_lo(o[dt][0] * inv0, xh, xl);
+            split_hi_lo(o[dt][1] * inv0, yh, yl);
             const size_t i = tiled_index(ma, d, a.rows_pad);
-            *reinterpret_cast<float2*>(a.out_hi + i) = make_float2(h0, h1);
-            *reinterpret_cast<float2*>(a.out_lo + i) = make_float2(l0, l1);
+            *reinterpret_cast<float2*>(a.out_hi + i) = make_float2(xh, yh);
+            *reinterpret_cast<float2*>(a.out_lo + i) = make_float2(xl, yl);
         }
         if (mb < a.rows)
         {
-            split_hi_lo(o[dt][2] * inv1, h0, l0);
-            split_hi_lo(o[dt][3] * inv1, h1, l1);
+            split_hi_lo(o[dt][2] * inv1, xh, xl);
+            split_hi_lo(o[dt][3] * inv1, yh, yl);
             const size_t i = tiled_index(mb, d, a.rows_pad);
-            *reinterpret_cast<float2*>(a.out_hi + i) = make_float2(h0, h1);
-            *reinterpret_cast<float2*>(a.out_lo + i) = make_float2(l0, l1);
+            *reinterpret_cast<float2*>(a.out_hi + i) = make_float2(xh, yh);
+            *reinterpret_cast<float2*>(a.out_lo + i) = make_float2(xl, yl);
         }
     }
+}
+
+// Combines the chunk partials of a row block (merge item: row block, first
+// slot, chunk count): out = sum_c 2^(m_c - M) acc_c / sum_c 2^(m_c - M) l_c,
+// M = max_c m_c, written split and tiled. CTA = one item x one KV head; thread
+// = (query vector tid / 4, 32 dims).
+__global__ void __launch_bounds__(256) prefill_attn_merge_kernel(const float* __restrict__ part, const int4* __restrict__ items,
+                                                                 int rows, int rows_pad, float* out_hi, float* out_lo)
+{
+    const int4 it = items[blockIdx.x];
+    const int qb = it.x, slot0 = it.y, nch = it.z;
+    const int kvh = blockIdx.y, tid = threadIdx.x;
+    const int qv = tid >> 2, d0 = (tid & 3) * 32;
+    const int r = qv % kPaRows, hl = qv / kPaRows;
+    const int m = qb * kPaRows + r;
+    if (m >= rows) return;
+    auto base = [&](int c) {
+        return part + ((static_cast<size_t>(slot0 + c) * kNumKVHeads + kvh) * 64 + qv) * kPaPartStride;
+    };
+    float M = kPaMasked;
+    for (int c = 0; c < nch; ++c) M = fmaxf(M, base(c)[0]);
+    float L = 0.f;
+    float acc[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+    for (int c = 0; c < nch; ++c)
+    {
+        const float* p = base(c);
+        const float w = exp2f(p[0] - M);
+        L += w * p[1];
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+        {
+            const float4 v = *reinterpret_cast<const float4*>(p + 4 + d0 + i);
+            acc[i] += w * v.x;
+            acc[i + 1] += w * v.y;
+            acc[i + 2] += w * v.z;
+            acc[i + 3] += w * v.w;
+        }
+    }
+    const float inv = 1.0f / L;
+    const int col = (2 * kvh + hl) * kHeadDim + d0;
+#pragma unroll
+    for (int i = 0; i < 32; i += 4)
+        store_tiled4(out_hi, out_lo, rows_pad, m, col + i,
+                     make_float4(acc[i] * inv, acc[i + 1] * inv, acc[i + 2] * inv, acc[i + 3] * inv));
 }
 
 }  // namespace hy
