@@ -469,7 +469,7 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--cpu-steps", type=int, default=16)
+    ap.add_argument("--cpu-steps", type=int, default=144)   # ~10 s of oracle decode on the host
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-dflash", action="store_true")
     ap.add_argument("--workload", choices=["decode", "requests"], default="decode",

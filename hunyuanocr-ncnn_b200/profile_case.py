@@ -28,15 +28,38 @@ def main(argv=None):
     ap.add_argument("--calls", type=int, default=3)
     ap.add_argument("--path", choices=["persistent", "graph"], default="persistent")
     ap.add_argument("--dtype", choices=["f32", "bf16"], default="f32", help="weight and KV dtype")
-    ap.add_argument("--kernel", choices=["decode", "lm", "gate_up", "attention", "verify"], default="decode",
+    ap.add_argument("--kernel", choices=["decode", "lm", "gate_up", "attention", "verify", "prefill"],
+                    default="decode",
                     help="decode: AR launches; lm / gate_up / attention: the M=1 kernels alone "
-                         "(hy_bench_kernel); verify: DFlash verify blocks (16-row kernels)")
+                         "(hy_bench_kernel); verify: DFlash verify blocks (16-row kernels); "
+                         "prefill: prompt prefill of --past rows (tcgen05 GEMMs, prefill attention)")
     args = ap.parse_args(argv)
 
     import __graft_entry__ as ge
 
     pkg = ge.load_package()
     dt = pkg.DTYPE_F32 if args.dtype == "f32" else pkg.DTYPE_BF16
+    if args.kernel == "prefill":
+        import time
+
+        import numpy as np
+
+        rows = args.past
+        rt = pkg.TextRuntime.synthetic(seed=0, num_layers=args.layers, vocab_size=args.vocab, max_prefill=rows,
+                                       max_tokens=16, max_context=rows + 16, weight_dtype=dt, kv_dtype=dt)
+        rng = np.random.default_rng(0)
+        emb = rng.standard_normal((rows, 1024)).astype(np.float32)
+        ang = np.arange(rows)[:, None] * 1e-3 * np.arange(128)[None, :]
+        cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+        dt_ms = 0.0
+        for _ in range(args.calls):
+            rt.reset()
+            t0 = time.perf_counter()
+            rt.prefill(emb, cos, sin)
+            dt_ms = (time.perf_counter() - t0) * 1e3
+        print(f"prefill {args.dtype} layers={args.layers} vocab={args.vocab} rows={rows}: {dt_ms:.2f} ms per call (wall)")
+        rt.close()
+        return
     rt = pkg.TextRuntime.synthetic(seed=0, num_layers=args.layers, vocab_size=args.vocab, max_prefill=64,
                                    max_tokens=args.tokens + 40, max_context=args.past + args.tokens + 40,
                                    weight_dtype=dt, kv_dtype=dt)
