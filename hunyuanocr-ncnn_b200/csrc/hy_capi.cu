@@ -45,7 +45,7 @@ int fail(int code, const std::string& msg)
 
 constexpr int kFfn = 3584;                // kernels are specialised for the model's FFN width
 constexpr int kAttnSplitsAR = 19;         // 18 past splits + the new-row split (152 CTAs)
-constexpr int kAttnSplitsVerify = 18;         // 17 past splits + the new-row split (144 CTAs, one per SM)
+constexpr int kVerifyChunks = 36;         // key chunks per KV head of a <= 16-row step (288 CTAs, 2 per SM)
 constexpr int kMaxSplits = 20;
 constexpr int kArStepsPerGraph = 4;
 constexpr int kMegaChunk = 64;            // tokens per persistent-kernel launch
@@ -121,6 +121,7 @@ struct hy_ctx {
     int4* pf_work = nullptr;
     int4* pf_merge = nullptr;
     float* pf_part = nullptr;
+    float* va_part = nullptr;   // chunk partials of <= 16-row attention [kVerifyChunks][8][32][kPaPartStride]
     int pf_nwork = 0, pf_nmerge = 0;
     std::vector<int4> h_work, h_merge;
     // Per layer: q/k/v, o, gate/up, down weights, tiled hi (and lo for fp32 weights).
@@ -242,6 +243,44 @@ cudaError_t run_attn(hy_ctx* c, const AttnArgs& a, int splits)
     return launch_pdl(k, dim3(splits, kNumKVHeads), dim3(kAttnThreads), S::SMEM, c->stream, a);
 }
 
+// Attention of a step of 2..16 rows (DFlash verify, decoder steps): RoPE + QK
+// norm + KV append of the rows, then the tensor-core attention over the keys
+// [0, past + rows) in kVerifyChunks chunks per KV head, then the chunk merge.
+template <typename KT>
+cudaError_t run_attn16(hy_ctx* c, const AttnArgs& at)
+{
+    PrefillRopeArgs ra{const_cast<float*>(at.qkv), at.ldq, at.cos, at.sin, at.qn_w, at.kn_w, at.kc, at.vc, at.cap,
+                       at.past_fixed, at.eps, at.scale_log2, at.st, at.rope_state, c->err};
+    cudaError_t e = launch_pdl(prefill_rope_kernel<KT>, dim3(at.rows, 4), dim3(256), 0, c->stream, ra);
+    if (e != cudaSuccess) return e;
+    static_assert(kVerifyChunks <= kMaxVerifyChunks, "chunk merge capacity");
+    using S = PaShape<KT, 16>;
+    auto k = prefill_attn_kernel<KT, 16>;
+    static unsigned long long configured = 0;
+    const unsigned long long bit = 1ull << (c->cfg.device & 63);
+    if (!(configured & bit))
+    {
+        if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM)) != cudaSuccess) return e;
+        configured |= bit;
+    }
+    PrefillAttnArgs pa;
+    std::memset(&pa, 0, sizeof(pa));
+    pa.q = at.qkv;
+    pa.ldq = at.ldq;
+    pa.kc = at.kc;
+    pa.vc = at.vc;
+    pa.cap = at.cap;
+    pa.past = at.past_fixed;
+    pa.rows = at.rows;
+    pa.part = c->va_part;
+    pa.st = at.st;
+    pa.err = c->err;
+    if ((e = launch_pdl(k, dim3(kVerifyChunks, kNumKVHeads), dim3(S::THREADS), S::SMEM, c->stream, pa)) != cudaSuccess)
+        return e;
+    const ChunkMergeArgs ma{c->va_part, kVerifyChunks, at.rows, at.out};
+    return launch_pdl(attn_chunk_merge_kernel, dim3(32, kNumKVHeads), dim3(kHeadDim), 0, c->stream, ma);
+}
+
 // How the first layer's input rows are produced.
 struct StepSource {
     int src;          // SRC_X (ctx->x already holds the rows) or a gather mode
@@ -322,7 +361,14 @@ cudaError_t enqueue_step_t(hy_ctx* c, const StepPlan& p)
         at.counter = c->attn_cnt + l * kNumKVHeads;
         at.out = c->attn;
         at.err = c->err;
-        if ((e = run_attn<MT, KT>(c, at, MT == 1 ? kAttnSplitsAR : kAttnSplitsVerify)) != cudaSuccess) return e;
+        if constexpr (MT == 1)
+        {
+            if ((e = run_attn<1, KT>(c, at, kAttnSplitsAR)) != cudaSuccess) return e;
+        }
+        else
+        {
+            if ((e = run_attn16<KT>(c, at)) != cudaSuccess) return e;
+        }
 
         GemvArgs o = base_args(c);
         o.W = c->wo[l];
@@ -790,6 +836,8 @@ int alloc_ctx(hy_ctx* c)
         if ((rc = dalloc(c, &c->pf_work, nqb * kPaMaxChunks))) return rc;
         if ((rc = dalloc(c, &c->pf_merge, nqb))) return rc;
         if ((rc = dalloc(c, &c->pf_part, nqb * kPaMaxChunks * kNumKVHeads * 64 * kPaPartStride))) return rc;
+        if ((rc = dalloc(c, &c->va_part, static_cast<size_t>(kVerifyChunks) * kNumKVHeads * 32 * kPaPartStride)))
+            return rc;
     }
     {
         // Tiled prefill weights: hi for every weight, lo for fp32 weights.
@@ -1152,8 +1200,8 @@ UmmaGemmArgs gemm_args(const float* a_hi, const float* a_lo, int a_rows, const f
 template <typename KT>
 cudaError_t run_prefill_attn(hy_ctx* c, const float* q, int ldq, int layer, int past, int rows, int rows_pad)
 {
-    using S = PaShape<KT>;
-    auto k = prefill_attn_kernel<KT>;
+    using S = PaShape<KT, kPaRows>;
+    auto k = prefill_attn_kernel<KT, kPaRows>;
     static unsigned long long configured = 0;
     const unsigned long long bit = 1ull << (c->cfg.device & 63);
     if (!(configured & bit))
@@ -1163,8 +1211,8 @@ cudaError_t run_prefill_attn(hy_ctx* c, const float* q, int ldq, int layer, int 
         configured |= bit;
     }
     PrefillAttnArgs a{q, ldq, c->kc_layer(layer), c->vc_layer(layer), c->cfg.max_context, past, rows,
-                      c->pf_at_hi, c->pf_at_lo, rows_pad, c->pf_work, c->pf_part};
-    k<<<dim3(c->pf_nwork, kNumKVHeads), kPaThreads, S::SMEM, c->stream>>>(a);
+                      c->pf_at_hi, c->pf_at_lo, rows_pad, c->pf_work, c->pf_part, nullptr, c->err};
+    k<<<dim3(c->pf_nwork, kNumKVHeads), S::THREADS, S::SMEM, c->stream>>>(a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess || c->pf_nmerge == 0) return e;
     prefill_attn_merge_kernel<<<dim3(c->pf_nmerge, kNumKVHeads), 256, 0, c->stream>>>(c->pf_part, c->pf_merge, rows,
@@ -1238,8 +1286,8 @@ cudaError_t enqueue_prefill_t(hy_ctx* c, int seq)
                                c->pre_cos + static_cast<size_t>(p0) * kHeadDim,
                                c->pre_sin + static_cast<size_t>(p0) * kHeadDim,
                                c->qn(l), c->kn(l), c->kc_layer(l), c->vc_layer(l), cfg.max_context, p0,
-                               cfg.rms_norm_eps, cfg.attn_scale * 1.4426950408889634f};
-            prefill_rope_kernel<KT><<<rows, 256, 0, c->stream>>>(ra);
+                               cfg.rms_norm_eps, cfg.attn_scale * 1.4426950408889634f, nullptr, 0, c->err};
+            prefill_rope_kernel<KT><<<dim3(rows, 4), 256, 0, c->stream>>>(ra);
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
             if ((e = run_prefill_attn<KT>(c, c->pf_qkv, kQKVRows, l, p0, rows, pad)) != cudaSuccess) return e;
             UmmaGemmArgs o = gemm_args(c->pf_at_hi, c->pf_at_lo, pad, c->to_hi[l], c->to_lo[l], rows, kHidden, kQWidth);
@@ -1886,7 +1934,7 @@ int hy_attention(hy_ctx* c, int layer, const float* qkv, int rows, const float* 
     if (rows == 1)
         e = kb ? run_attn<1, __nv_bfloat16>(c, at, kAttnSplitsAR) : run_attn<1, float>(c, at, kAttnSplitsAR);
     else
-        e = kb ? run_attn<16, __nv_bfloat16>(c, at, kAttnSplitsVerify) : run_attn<16, float>(c, at, kAttnSplitsVerify);
+        e = kb ? run_attn16<__nv_bfloat16>(c, at) : run_attn16<float>(c, at);
     if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("attention launch: ") + cudaGetErrorString(e));
     HY_CUDA(cudaMemcpyAsync(out, c->attn, sizeof(float) * rows * kQWidth, cudaMemcpyDeviceToHost, c->stream));
     if ((rc = check_device_error(c))) return rc;

@@ -28,7 +28,7 @@ __device__ __forceinline__ void cp_async_wait()
 // RoPE + QK RMSNorm + KV append for every row of a prefill pass (the same
 // per-head arithmetic as the decode/verify attention prologue): q heads are
 // rewritten in place (times scale * log2 e), k heads and v heads go to the
-// cache rows past .. past + rows - 1. One CTA per row, a warp per 4 heads.
+// cache rows past .. past + rows - 1. Grid (rows, 4): one warp per (row, head).
 // ---------------------------------------------------------------------------
 struct PrefillRopeArgs {
     float* qkv;   // [rows x ldq]: q [0, 2048) rewritten, k [2048, 3072), v [3072, 4096)
@@ -41,17 +41,28 @@ struct PrefillRopeArgs {
     void* vc;
     int cap, past;
     float eps, scale_log2;
+    const DecodeState* st;   // when set, past = st->kv_len (rows appended at the current length)
+    int rope_state;          // rope row of row m: (rope_state ? past : 0) + m
+    int* err;                // kErrBounds when a row would land past the capacity
 };
 
 template <typename KT>
 __global__ void __launch_bounds__(256) prefill_rope_kernel(const PrefillRopeArgs a)
 {
+    pdl_wait();
     const int m = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float* row = a.qkv + static_cast<size_t>(m) * a.ldq;
-    const float* c = a.cos + static_cast<size_t>(m) * kHeadDim;
-    const float* s = a.sin + static_cast<size_t>(m) * kHeadDim;
-    for (int j = warp; j < kNumQHeads + 2 * kNumKVHeads; j += 8)
+    const int past = a.st ? a.st->kv_len : a.past;
+    if (past + m >= a.cap)
     {
+        if (threadIdx.x == 0 && a.err) atomicOr(a.err, kErrBounds);
+        return;
+    }
+    const int rr = (a.rope_state ? past : 0) + m;
+    float* row = a.qkv + static_cast<size_t>(m) * a.ldq;
+    const float* c = a.cos + static_cast<size_t>(rr) * kHeadDim;
+    const float* s = a.sin + static_cast<size_t>(rr) * kHeadDim;
+    {
+        const int j = blockIdx.y * 8 + warp;   // 0..15 q heads, 16..23 k heads, 24..31 v heads
         if (j < kNumQHeads)
         {
             float* x = row + j * kHeadDim;
@@ -65,7 +76,7 @@ __global__ void __launch_bounds__(256) prefill_rope_kernel(const PrefillRopeArgs
             const int h = j - kNumQHeads;
             float o[4];
             rope_norm_vec(row + kQWidth + h * kHeadDim, c, s, a.kn_w, a.eps, lane, o);
-            KT* dst = static_cast<KT*>(a.kc) + (static_cast<size_t>(h) * a.cap + a.past + m) * kHeadDim;
+            KT* dst = static_cast<KT*>(a.kc) + (static_cast<size_t>(h) * a.cap + past + m) * kHeadDim;
 #pragma unroll
             for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = from_f32<KT>(o[i]);
         }
@@ -73,7 +84,7 @@ __global__ void __launch_bounds__(256) prefill_rope_kernel(const PrefillRopeArgs
         {
             const int h = j - kNumQHeads - kNumKVHeads;
             const float* x = row + kQWidth + kKVWidth + h * kHeadDim;
-            KT* dst = static_cast<KT*>(a.vc) + (static_cast<size_t>(h) * a.cap + a.past + m) * kHeadDim;
+            KT* dst = static_cast<KT*>(a.vc) + (static_cast<size_t>(h) * a.cap + past + m) * kHeadDim;
 #pragma unroll
             for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = from_f32<KT>(x[lane + 32 * i]);
         }
@@ -86,29 +97,35 @@ __global__ void __launch_bounds__(256) prefill_rope_kernel(const PrefillRopeArgs
 // tensor cores: S = Q K^T and O += P V as mma.sync m16n8k8 tf32 with the
 // three-term split, an online base-2 softmax in fp32 between them.
 //
-// CTA = 32 query rows x the 2 q heads of one KV head (64 query vectors, one
+// CTA = QR query rows x the 2 q heads of one KV head (2 QR query vectors, one
 // m16 tile per warp), so each K/V tile in shared memory serves both heads,
-// over one chunk of that row block's keys (a work item): K/V stream in 32-key
-// tiles through a 2-stage cp.async ring. A row block whose keys span several
-// chunks (the causal mask makes later blocks longer) leaves per-chunk partials
-// (running max, sum, unnormalised output) that prefill_attn_merge_kernel
-// combines; a single-chunk block writes its output directly. Outputs are
-// written split and tiled for the o_proj GEMM.
+// over one chunk of the rows' keys: K/V stream in 32-key tiles through a
+// 2-stage cp.async ring.
+//   Prefill (QR = 32, host work list): a row block whose keys span several
+//   chunks (the causal mask makes later blocks longer) leaves per-chunk
+//   partials (running max, sum, unnormalised output) that
+//   prefill_attn_merge_kernel combines; a single-chunk block writes its output
+//   directly, split and tiled for the o_proj GEMM.
+//   Verify / decoder steps of <= 16 rows (QR = 16, no work list): the keys
+//   [0, kv_len + rows) are cut into gridDim.x equal chunks on the device (the
+//   length is read from the decode state), every CTA leaves a partial and
+//   attn_chunk_merge_kernel merges them into the row-major output.
 // Within a 8-key step of P V the k order is permuted (logical k = t <-> key
 // 2t, k = t + 4 <-> key 2t + 1), so the S accumulator fragments are the P
 // operand fragments as they lie, with no shuffles.
 // ---------------------------------------------------------------------------
-constexpr int kPaRows = 32, kPaKeys = 32, kPaThreads = 128;
+constexpr int kPaRows = 32, kPaKeys = 32, kPaThreads = 128;   // prefill: QR = 32 rows, 4 warps
 constexpr int kPaMaxChunks = 4;            // chunks per row block at most
 constexpr int kPaMinChunkTiles = 8;        // 32-key tiles per chunk at least
 constexpr int kPaPartStride = 132;         // (max, sum, -, -) + out[128]
 constexpr float kPaMasked = -1.0e30f;      // masked score (finite: a fully masked chunk merges with weight 0)
 
-template <typename KT>
+template <typename KT, int QR>
 struct PaShape {
+    static constexpr int THREADS = 4 * QR;                                       // 2 heads x QR / 16 warps
     static constexpr int KP = (sizeof(KT) == 4) ? kHeadDim + 4 : kHeadDim + 8;   // K/V tile pitch (elements)
     static constexpr int QP = kHeadDim + 4;                                      // Q tile pitch (floats)
-    static constexpr int Q_BYTES = 2 * kPaRows * QP * 4;
+    static constexpr int Q_BYTES = 2 * QR * QP * 4;
     static constexpr int T_BYTES = kPaKeys * KP * static_cast<int>(sizeof(KT));
     static constexpr int STAGE = 2 * T_BYTES;
     static constexpr int SMEM = Q_BYTES + 2 * STAGE;
@@ -124,15 +141,19 @@ struct PrefillAttnArgs {
     float* out_hi;    // output [rows x 2048], split and tiled (rows_pad rows) for the o_proj GEMM
     float* out_lo;
     int rows_pad;
-    const int4* work; // per CTA (blockIdx.x): row block, first and end 32-key tile, partial slot (-1: direct)
-    float* part;      // [slot][8 KV heads][64 query vectors][kPaPartStride]
+    const int4* work; // per CTA (blockIdx.x): row block, first and end 32-key tile, partial slot (-1: direct);
+                      // nullptr: device-side chunks (QR = 16)
+    float* part;      // [slot][8 KV heads][2 QR query vectors][kPaPartStride]
+    const DecodeState* st;   // device-side chunks: past = st->kv_len when set
+    int* err;         // kErrBounds when past + rows exceeds the capacity (nothing is read then)
 };
 
-template <typename KT>
-__global__ void __launch_bounds__(kPaThreads, 2) prefill_attn_kernel(const PrefillAttnArgs a)
+template <typename KT, int QR>
+__global__ void __launch_bounds__(4 * QR, 2) prefill_attn_kernel(const PrefillAttnArgs a)
 {
-    using S = PaShape<KT>;
-    constexpr int KP = S::KP, QP = S::QP;
+    using S = PaShape<KT, QR>;
+    constexpr int KP = S::KP, QP = S::QP, NT = S::THREADS;
+    constexpr int NQV = 2 * QR;   // query vectors per CTA
     constexpr bool KV_EXACT = sizeof(KT) == 2;
     constexpr int EPC = 16 / static_cast<int>(sizeof(KT));
     constexpr int CPR = kHeadDim / EPC;
@@ -141,18 +162,40 @@ __global__ void __launch_bounds__(kPaThreads, 2) prefill_attn_kernel(const Prefi
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
-    const int4 wk = a.work[blockIdx.x];
-    const int qb = wk.x, kb0 = wk.y, kb1 = wk.z, slot = wk.w;
     const int kvh = blockIdx.y;
-    const int m0 = qb * kPaRows;
-    const int nkeys = min(a.past + m0 + kPaRows, a.past + a.rows);
+    pdl_wait();
+    const bool dev = (a.work == nullptr);
+    const int past = (dev && a.st) ? a.st->kv_len : a.past;
+    int qb = 0, kb0, kb1, slot;
+    if (!dev)
+    {
+        const int4 wk = a.work[blockIdx.x];
+        qb = wk.x;
+        kb0 = wk.y;
+        kb1 = wk.z;
+        slot = wk.w;
+    }
+    else
+    {
+        const int nkb = (past + a.rows + kPaKeys - 1) / kPaKeys;
+        kb0 = static_cast<int>(blockIdx.x) * nkb / static_cast<int>(gridDim.x);
+        kb1 = (static_cast<int>(blockIdx.x) + 1) * nkb / static_cast<int>(gridDim.x);
+        slot = blockIdx.x;
+    }
+    if (past + a.rows > a.cap)
+    {
+        if (tid == 0 && a.err) atomicOr(a.err, kErrBounds);
+        return;
+    }
+    const int m0 = qb * QR;
+    const int nkeys = min(past + m0 + QR, past + a.rows);
     const KT* kbase = static_cast<const KT*>(a.kc) + static_cast<size_t>(kvh) * a.cap * kHeadDim;
     const KT* vbase = static_cast<const KT*>(a.vc) + static_cast<size_t>(kvh) * a.cap * kHeadDim;
 
     auto load_kv = [&](int slot, int kb) {
         KT* Ks = reinterpret_cast<KT*>(smem + S::Q_BYTES + slot * S::STAGE);
         KT* Vs = Ks + kPaKeys * KP;
-        for (int i = tid; i < kPaKeys * CPR; i += kPaThreads)
+        for (int i = tid; i < kPaKeys * CPR; i += NT)
         {
             const int r = i / CPR, ch = i % CPR;
             const int key = kb * kPaKeys + r;
@@ -163,11 +206,11 @@ __global__ void __launch_bounds__(kPaThreads, 2) prefill_attn_kernel(const Prefi
         }
     };
 
-    // Query vector j = hl * 32 + r: row m0 + r, q head 2 kvh + hl.
-    for (int i = tid; i < 2 * kPaRows * (kHeadDim / 4); i += kPaThreads)
+    // Query vector j = hl * QR + r: row m0 + r, q head 2 kvh + hl.
+    for (int i = tid; i < NQV * (kHeadDim / 4); i += NT)
     {
         const int j = i / (kHeadDim / 4), ch = i % (kHeadDim / 4);
-        const int hl = j / kPaRows, r = j % kPaRows;
+        const int hl = j / QR, r = j % QR;
         const bool ok = m0 + r < a.rows;
         const float* src = a.q + static_cast<size_t>(ok ? m0 + r : 0) * a.ldq + (2 * kvh + hl) * kHeadDim + ch * 4;
         cp_async16(Qs + j * QP + ch * 4, src, ok);
@@ -175,9 +218,9 @@ __global__ void __launch_bounds__(kPaThreads, 2) prefill_attn_kernel(const Prefi
     load_kv(0, kb0);
     cp_async_commit();
 
-    const int hl = warp >> 1, r0 = (warp & 1) * 16;
-    const float* Qw = Qs + (hl * kPaRows + r0) * QP;
-    const int pq0 = a.past + m0 + r0 + g, pq1 = pq0 + 8;   // positions of rows g and g + 8
+    const int hl = warp / (QR / 16), r0 = (warp % (QR / 16)) * 16;
+    const float* Qw = Qs + (hl * QR + r0) * QP;
+    const int pq0 = past + m0 + r0 + g, pq1 = pq0 + 8;   // positions of rows g and g + 8
     float o[16][4];
 #pragma unroll
     for (int dt = 0; dt < 16; ++dt) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.f;
@@ -306,7 +349,7 @@ __global__ void __launch_bounds__(kPaThreads, 2) prefill_attn_kernel(const Prefi
     if (slot >= 0)
     {
         // Partial of this chunk: (max, sum) per query vector, unnormalised output.
-        float* pa = a.part + ((static_cast<size_t>(slot) * kNumKVHeads + kvh) * 64 + hl * kPaRows + r0 + g) * kPaPartStride;
+        float* pa = a.part + ((static_cast<size_t>(slot) * kNumKVHeads + kvh) * NQV + hl * QR + r0 + g) * kPaPartStride;
         float* pb = pa + 8 * kPaPartStride;
         if (t == 0)
         {
@@ -392,6 +435,53 @@ __global__ void __launch_bounds__(256) prefill_attn_merge_kernel(const float* __
     for (int i = 0; i < 32; i += 4)
         store_tiled4(out_hi, out_lo, rows_pad, m, col + i,
                      make_float4(acc[i] * inv, acc[i + 1] * inv, acc[i + 2] * inv, acc[i + 3] * inv));
+}
+
+// Merge of the device-side chunks of a <= 16-row step: CTA = (query vector, KV
+// head), thread = output dimension; every chunk's (max, sum, value) is loaded at
+// once. out[row][head * 128 + d] = sum_c 2^(m_c - M) acc_c[d] / sum_c 2^(m_c - M) l_c.
+constexpr int kMaxVerifyChunks = 40;
+struct ChunkMergeArgs {
+    const float* part;   // [chunk][8 KV heads][32 query vectors][kPaPartStride]
+    int nch, rows;
+    float* out;          // [rows x 2048]
+};
+
+__global__ void __launch_bounds__(kHeadDim) attn_chunk_merge_kernel(const ChunkMergeArgs a)
+{
+    pdl_wait();
+    const int qv = blockIdx.x, kvh = blockIdx.y, d = threadIdx.x;   // qv = hl * 16 + row
+    const int row = qv % 16, hl = qv / 16;
+    if (row >= a.rows) return;
+    const size_t cstride = static_cast<size_t>(kNumKVHeads) * 32 * kPaPartStride;
+    const float* p0 = a.part + (static_cast<size_t>(kvh) * 32 + qv) * kPaPartStride;
+    float m[kMaxVerifyChunks], l[kMaxVerifyChunks], v[kMaxVerifyChunks];
+#pragma unroll
+    for (int c = 0; c < kMaxVerifyChunks; ++c)
+    {
+        m[c] = kPaMasked;
+        l[c] = 0.f;
+        v[c] = 0.f;
+        if (c < a.nch)
+        {
+            const float* p = p0 + c * cstride;
+            m[c] = __ldcg(p);
+            l[c] = __ldcg(p + 1);
+            v[c] = __ldcg(p + 4 + d);
+        }
+    }
+    float M = kPaMasked;
+#pragma unroll
+    for (int c = 0; c < kMaxVerifyChunks; ++c) M = fmaxf(M, m[c]);
+    float L = 0.f, acc = 0.f;
+#pragma unroll
+    for (int c = 0; c < kMaxVerifyChunks; ++c)
+    {
+        const float w = exp2f(m[c] - M);
+        L += w * l[c];
+        acc += w * v[c];
+    }
+    a.out[static_cast<size_t>(row) * kQWidth + (2 * kvh + hl) * kHeadDim + d] = acc / L;
 }
 
 }  // namespace hy
