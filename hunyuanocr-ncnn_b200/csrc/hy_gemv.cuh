@@ -36,6 +36,7 @@ constexpr int kGemvThreads = (kGemvWarps + 1) * 32;
 constexpr int kStageBytes = 16384;
 constexpr int kRingBytes = 96 * 1024;
 constexpr int kSmemBudget = 225 * 1024;   // dynamic shared memory per CTA we allow ourselves
+constexpr int kPartUnits16 = 32;          // M = 16 K-mode tile slots (units of one launch at most)
 
 struct GemvArgs {
     const void* W;   // [N x ldw] of WT; this launch reads columns [k_off, k_off + KP)
@@ -102,10 +103,10 @@ struct GemvShape {
 // (pitch KP + 4 floats), so the fragment loads of a warp fall in 32 different
 // banks. The unit is the B operand (n = weight row), the activation rows the A
 // operand (m = activation row), one 16 x 8 tile per unit.
-//   K mode (few row groups: q/k/v, o, down): stage u = unit u = (group u / NKC,
-//     chunk u % NKC), owned by warp u % 8; the units' tiles go to shared memory
-//     and are added in chunk order at the end.
-//   G mode (many row groups: gate/up, the LM head): warp w owns groups w, w + 8,
+//   K mode (at most 32 units: q/k/v, o, gate/up, down): stage u = unit u =
+//     (group u / NKC, chunk u % NKC), owned by warp u % 8; the units' tiles go to
+//     shared memory and are added in chunk order at the end.
+//   G mode (many row groups: the LM head): warp w owns groups w, w + 8,
 //     ... and takes all NKC chunks of a group in order, accumulating in its
 //     fragments; the stages of a round of 8 groups are interleaved chunk-major.
 template <typename WT, int KP>
@@ -117,7 +118,7 @@ struct GemvShape<WT, KP, 16> {
     static constexpr int STAGE = 8 * PITCH;
     static constexpr int XP = KP + 4;
     static constexpr int XS_BYTES = 16 * XP * 4;
-    static constexpr int PART_UNITS = 16;                        // K-mode tile slots
+    static constexpr int PART_UNITS = kPartUnits16;              // K-mode tile slots
     static constexpr int PART_BYTES = PART_UNITS * 16 * 8 * 4;   // [unit][m][n]
     static constexpr int WSCR_BYTES = kGemvWarps * 16 * 8 * 4;   // G-mode per-warp [m][n]
     static constexpr int RED_BYTES = (kGemvWarps * 16 + 16) * 16 + 16;
@@ -245,7 +246,7 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
     const int R = r1 - r0;
     // M = 16: row groups of 8, K mode when all units fit the tile slots.
     const int ngroups16 = (R + 7) / 8;
-    const bool kmode16 = (MT == 16) && ngroups16 * (KP / S::KC16) <= 16;
+    const bool kmode16 = (MT == 16) && ngroups16 * (KP / S::KC16) <= kPartUnits16;
     const int nstage = (MT == 16) ? ngroups16 * (KP / S::KC16) : (R + SPS - 1) / SPS;
 
     __shared__ uint64_t s_xbar;   // M = 16: bulk copy of the activation rows
