@@ -147,6 +147,9 @@ struct hy_ctx {
     int ar_path = HY_AR_PATH_PERSISTENT;
     bool mega_ok = false;
 
+    // Tensor map of the tied table for the 16-row LM head (64-row x 128-byte boxes, 128-byte swizzle).
+    CUtensorMap lm_tmap;
+
     cudaGraphExec_t g_ar = nullptr;
     cudaGraphExec_t g_verify_draft = nullptr;
     cudaGraphExec_t g_verify_ids = nullptr;
@@ -215,16 +218,17 @@ template <typename WT, int KP, int MT, int PRO, int EPI>
 cudaError_t run_gemv(hy_ctx* c, const GemvArgs& a)
 {
     using S = GemvShape<WT, KP, MT>;
+    constexpr int smem = (MT == 16 && EPI == EPI_ARGMAX) ? S::SMEM_TL : S::SMEM;
     auto k = gemv_kernel<WT, KP, MT, PRO, EPI>;
     static unsigned long long configured = 0;  // per instantiation, one bit per device
     const unsigned long long bit = 1ull << (c->cfg.device & 63);
     if (!(configured & bit))
     {
-        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         configured |= bit;
     }
-    return launch_pdl(k, dim3(c->num_sms), dim3(kGemvThreads), S::SMEM, c->stream, a);
+    return launch_pdl(k, dim3(c->num_sms), dim3(kGemvThreads), smem, c->stream, a);
 }
 
 template <int MT, typename KT>
@@ -311,6 +315,7 @@ GemvArgs base_args(hy_ctx* c)
     a.hist = c->hist;
     a.part = c->lm_part;
     a.counter = c->lm_cnt;
+    a.tmap = c->lm_tmap;
     return a;
 }
 
@@ -1106,9 +1111,37 @@ int tile_weights_t(hy_ctx* c)
     return HY_OK;
 }
 
+// Tensor map of the tied table [vocab x 1024] for the 16-row LM head: boxes of
+// 128 bytes of a row x 64 rows, 128-byte swizzle (conflict-free fragment reads
+// without padding), rows past the table zero-filled. cuTensorMapEncodeTiled is
+// taken from the driver through the runtime's entry-point query.
+int encode_lm_tmap(hy_ctx* c)
+{
+    using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    HY_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+    if (!fn || q != cudaDriverEntryPointSuccess) return fail(HY_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+    const bool bf = c->cfg.weight_dtype == HY_DTYPE_BF16;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kHidden), static_cast<cuuint64_t>(c->cfg.vocab_size)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kHidden) * c->w_elem()};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / c->w_elem()), 64};
+    const cuuint32_t estr[2] = {1, 1};
+    std::memset(&c->lm_tmap, 0, sizeof(c->lm_tmap));
+    const CUresult r = reinterpret_cast<EncodeFn>(fn)(
+        &c->lm_tmap, bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, c->embed, dims,
+        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(HY_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string(static_cast<int>(r)));
+    return HY_OK;
+}
+
 int finish_create(hy_ctx* c, hy_ctx** out)
 {
     int rc = (c->cfg.weight_dtype == HY_DTYPE_BF16) ? tile_weights_t<__nv_bfloat16>(c) : tile_weights_t<float>(c);
+    if (!rc) rc = encode_lm_tmap(c);
     if (rc)
     {
         free_ctx(c);

@@ -156,6 +156,17 @@ __device__ __forceinline__ void bulk_g2s_plain(void* dst, const void* src, uint3
 
 // Bulk prefetch of global memory into L2 (no destination, no completion).
 // src and bytes must be 16-byte aligned.
+// 2-D tiled TMA load (no multicast) of the box at element coordinates (x, y)
+// of the tensor map `tmap` (kernel-parameter space), completing on `bar`.
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, int y, uint64_t* bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes)
 {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");

@@ -24,6 +24,8 @@
 
 #include "hy_device.cuh"
 
+#include <cuda.h>   // CUtensorMap (the map is encoded on the host through the driver entry point)
+
 namespace hy {
 
 enum { PRO_PLAIN = 0, PRO_NORM = 1, PRO_SWIGLU = 2 };
@@ -74,6 +76,8 @@ struct GemvArgs {
     int* posterior_out;   // LM_VERIFY [16]
     float penalty;        // LM_NONE penalty (AR / verify read st->penalty)
     int* err;
+    // M = 16 LM head: tensor map of the tied table (64-row x 128-byte boxes, 128-byte swizzle).
+    CUtensorMap tmap;
 };
 
 template <typename WT, int KP, int MT>
@@ -94,6 +98,7 @@ struct GemvShape {
     static constexpr int SMEM = RED_OFF + RED_BYTES;
     static constexpr int XP = KP;   // activation row pitch (floats)
     static constexpr int KC16 = KP;  // (M = 16 only)
+    static constexpr int TL_NST = 2, TL_TILE = 0, TL_KC = 8, TL_BAR_OFF = 0, TL_RED_OFF = 0, SMEM_TL = 0;   // (M = 16 only)
 };
 
 // M = 16 (DFlash verify blocks, prefill chunks) on the tensor cores (mma.sync
@@ -130,6 +135,17 @@ struct GemvShape<WT, KP, 16> {
     static constexpr int BAR_OFF = WSCR_OFF + WSCR_BYTES;
     static constexpr int RED_OFF = BAR_OFF + 2 * NST * 8;
     static constexpr int SMEM = RED_OFF + RED_BYTES;
+    // LM head (argmax epilogue): tiles of 64 rows x 128 bytes fetched by one TMA
+    // copy each (tensor map with 128-byte swizzle), ring aligned to 1 KB at run time.
+    static constexpr int TL_ROWS = 64;
+    static constexpr int TL_KC = 128 / static_cast<int>(sizeof(WT));   // columns per tile
+    static constexpr int TL_TILE = TL_ROWS * 128;
+    static constexpr int TL_NST = 16;
+    static constexpr int TL_WSCR_OFF = XS_BYTES + 1024 + TL_NST * TL_TILE;
+    static constexpr int TL_BAR_OFF = TL_WSCR_OFF + WSCR_BYTES;
+    static constexpr int TL_RED_OFF = TL_BAR_OFF + 2 * TL_NST * 8;
+    static constexpr int SMEM_TL = TL_RED_OFF + RED_BYTES;
+    static_assert(KP != 1024 || SMEM_TL <= 227 * 1024, "LM head tile ring (the LM head has K = 1024)");
     // Names the generic code refers to.
     static constexpr int RPW = 8, SEG = ROWB, SPS = 8, GPS = 1, KC16 = KC;
     static_assert(KP % KC == 0 && KC % 8 == 0 && ROWB % 16 == 0, "unit geometry");
@@ -219,7 +235,7 @@ __device__ __forceinline__ int draft_id(const DecodeState* st, const int* greedy
 }
 
 template <typename WT, int KP, int MT, int PRO, int EPI>
-__global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(const GemvArgs a)
+__global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(const __grid_constant__ GemvArgs a)
 {
     using S = GemvShape<WT, KP, MT>;
     constexpr int RPW = S::RPW, SEG = S::SEG, SPS = S::SPS, STAGE = S::STAGE, NST = S::NST;
@@ -229,12 +245,16 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
     static_assert(SEG % 16 == 0, "segments must be 16-byte multiples");
     static_assert(KP % 128 == 0, "K slice must be a multiple of 128");
 
+    // M = 16 LM head: 64-row tiles by TMA (see GemvShape<WT, KP, 16>).
+    constexpr bool TL = (MT == 16 && EPI == EPI_ARGMAX);
+    constexpr int NS = TL ? S::TL_NST : NST;
     extern __shared__ __align__(128) unsigned char smem[];
     float* xs = reinterpret_cast<float*>(smem);
     unsigned char* ring = smem + S::XS_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
-    uint64_t* empty = full + NST;
-    float4* red4 = reinterpret_cast<float4*>(smem + S::RED_OFF);   // [8 warps][MT] trackers, [MT] merged
+    if constexpr (TL) ring += (1024u - (smem_u32(ring) & 1023u)) & 1023u;   // 128-byte swizzle wants 1 KB alignment
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + (TL ? S::TL_BAR_OFF : S::BAR_OFF));
+    uint64_t* empty = full + NS;
+    float4* red4 = reinterpret_cast<float4*>(smem + (TL ? S::TL_RED_OFF : S::RED_OFF));   // [8 warps][MT] trackers, [MT] merged
     int* redi = reinterpret_cast<int*>(red4 + kGemvWarps * MT + MT);  // last-CTA flag
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -247,15 +267,16 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
     // M = 16: row groups of 8, K mode when all units fit the tile slots.
     const int ngroups16 = (R + 7) / 8;
     const bool kmode16 = (MT == 16) && ngroups16 * (KP / S::KC16) <= kPartUnits16;
-    const int nstage = (MT == 16) ? ngroups16 * (KP / S::KC16) : (R + SPS - 1) / SPS;
+    const int nk_tl = KP / S::TL_KC;                    // TL: tiles per 64-row block
+    const int nstage = TL ? ((R + 63) / 64) * nk_tl : (MT == 16) ? ngroups16 * (KP / S::KC16) : (R + SPS - 1) / SPS;
 
     __shared__ uint64_t s_xbar;   // M = 16: bulk copy of the activation rows
     if (tid == 0)
     {
-        for (int s = 0; s < NST; ++s)
+        for (int s = 0; s < NS; ++s)
         {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], (MT == 16) ? 1 : kGemvWarps);
+            mbar_init(&empty[s], (MT == 16 && !TL) ? 1 : kGemvWarps);
         }
         mbar_init(&s_xbar, 1);
         fence_mbar_init();
@@ -270,6 +291,23 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
             const uint64_t pol = l2_evict_first_policy();
             const WT* W = static_cast<const WT*>(a.W);
             int issued = 0;
+            if constexpr (TL)
+            {
+                // One TMA copy per tile: rows r0 + 64 rb .., columns k_off + TL_KC kc ..
+                // (rows past the table are zero-filled by the copy).
+                for (int i = 0; i < nstage; ++i)
+                {
+                    const int slot = i % NS;
+                    if (i >= NS && !mbar_wait(&empty[slot], ((i / NS) - 1) & 1, a.err, kErrTimeoutEmpty)) break;
+                    const int rb = i / nk_tl, kc = i % nk_tl;
+                    mbar_arrive_expect_tx(&full[slot], S::TL_TILE);
+                    tma_load_2d(ring + slot * S::TL_TILE, &a.tmap, a.k_off + kc * S::TL_KC, r0 + 64 * rb, &full[slot]);
+                    issued = i + 1;
+                }
+                for (int i = (issued > NS ? issued - NS : 0); i < issued; ++i)
+                    mbar_wait(&full[i % NS], (i / NS) & 1, a.err, kErrTimeoutFull);
+                return;
+            }
             int fills[(MT == 16) ? NST : 1] = {};   // M = 16: copies issued into each slot
             for (int i = 0; i < nstage; ++i)
             {
@@ -564,7 +602,7 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
         constexpr int NKC = S::NKC, KC = S::KC, PITCH = S::PITCH;
         constexpr bool W_EXACT = sizeof(WT) == 2;   // bf16 weights are exact tf32 heads
         float* part = reinterpret_cast<float*>(smem + S::PART_OFF);                 // [unit][m][n]
-        float* wscr = reinterpret_cast<float*>(smem + S::WSCR_OFF) + warp * 128;   // [m][n]
+        float* wscr = reinterpret_cast<float*>(smem + (TL ? S::TL_WSCR_OFF : S::WSCR_OFF)) + warp * 128;   // [m][n]
         const int g8 = lane >> 2, t4 = lane & 3;
         float d[4];
         // Tile of the unit in `slot` (chunk c): d += x[0:16, chunk] * W[8 rows, chunk]^T.
@@ -635,6 +673,71 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
                 }
             }
         };
+        if constexpr (TL)
+        {
+            // Every warp reads every tile (rows 8 w .. 8 w + 7 of its 64) and arrives on it;
+            // a row block's tiles come in column order, so the accumulator runs across them.
+            // Element k of tile row r sits in 16-byte chunk (k * size / 16) ^ (r & 7).
+            // Three accumulators (lo.hi, hi.lo, hi.hi products): three independent MMA
+            // chains per warp, added when the row block's tile is read out.
+            const int r = 8 * warp + g8;
+            float acc3[3][4];
+            for (int stage = 0; stage < nstage; ++stage)
+            {
+                const int slot = stage % NS;
+                const bool ok = mbar_wait(&full[slot], (stage / NS) & 1, a.err, kErrTimeoutFull);
+                if (!__all_sync(0xffffffffu, ok)) break;
+                const int rb = stage / nk_tl, kc = stage % nk_tl;
+                if (kc == 0)
+                {
+#pragma unroll
+                    for (int i = 0; i < 3; ++i) acc3[i][0] = acc3[i][1] = acc3[i][2] = acc3[i][3] = 0.f;
+                }
+                const unsigned char* trow = ring + slot * S::TL_TILE + r * 128;
+                const float* x0 = xs + g8 * XP + kc * S::TL_KC + t4;
+                const float* x1 = x0 + 8 * XP;
+#pragma unroll
+                for (int kk = 0; kk < S::TL_KC / 8; ++kk)
+                {
+                    const int k = 8 * kk + t4;
+                    constexpr int ES = static_cast<int>(sizeof(WT));
+                    const int b0 = k * ES, b1 = (k + 4) * ES;
+                    const WT* p0 = reinterpret_cast<const WT*>(trow + ((((b0 >> 4) ^ (r & 7)) << 4) | (b0 & 15)));
+                    const WT* p1 = reinterpret_cast<const WT*>(trow + ((((b1 >> 4) ^ (r & 7)) << 4) | (b1 & 15)));
+                    const float xa[4] = {x0[8 * kk], x1[8 * kk], x0[8 * kk + 4], x1[8 * kk + 4]};
+                    const float w0 = to_f32<WT>(*p0), w1 = to_f32<WT>(*p1);
+                    unsigned ah[4], al[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                    {
+                        ah[i] = tf32_head(xa[i]);
+                        al[i] = __float_as_uint(xa[i] - __uint_as_float(ah[i]));
+                    }
+                    const unsigned bh0 = tf32_head(w0), bh1 = tf32_head(w1);
+                    mma_tf32(acc3[0], al, bh0, bh1);
+                    if constexpr (!W_EXACT)
+                        mma_tf32(acc3[1], ah, __float_as_uint(w0 - __uint_as_float(bh0)),
+                                 __float_as_uint(w1 - __uint_as_float(bh1)));
+                    mma_tf32(acc3[2], ah, bh0, bh1);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[slot]);
+                if (kc == nk_tl - 1)
+                {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) d[e] = acc3[2][e] + (acc3[0][e] + acc3[1][e]);
+                    wscr[g8 * 8 + 2 * t4] = d[0];
+                    wscr[g8 * 8 + 2 * t4 + 1] = d[1];
+                    wscr[(g8 + 8) * 8 + 2 * t4] = d[2];
+                    wscr[(g8 + 8) * 8 + 2 * t4 + 1] = d[3];
+                    __syncwarp();
+                    group_epilogue(wscr, rb * 8 + warp);
+                    __syncwarp();
+                }
+            }
+        }
+        else
+        {
         // This warp's own units, in order, from its own slots (each refilled by the
         // producer once this warp released it, so every wait is one phase ahead).
         constexpr int SPW = NST / kGemvWarps;
@@ -681,6 +784,7 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
             }
             consumers_sync();
             for (int g = warp; g < ngroups16; g += kGemvWarps) group_epilogue(sum + (g * NKC) * 128, g);
+        }
         }
     }
     else
