@@ -147,7 +147,7 @@ struct hy_ctx {
     int ar_path = HY_AR_PATH_PERSISTENT;
     bool mega_ok = false;
 
-    // Tensor map of the tied table for the 16-row LM head (64-row x 128-byte boxes, 128-byte swizzle).
+    // Tensor map of the tied table for the 16-row LM head (128-row x 128-byte boxes, 128-byte swizzle).
     CUtensorMap lm_tmap;
 
     cudaGraphExec_t g_ar = nullptr;
@@ -1112,7 +1112,7 @@ int tile_weights_t(hy_ctx* c)
 }
 
 // Tensor map of the tied table [vocab x 1024] for the 16-row LM head: boxes of
-// 128 bytes of a row x 64 rows, 128-byte swizzle (conflict-free fragment reads
+// 128 bytes of a row x 128 rows, 128-byte swizzle (conflict-free fragment reads
 // without padding), rows past the table zero-filled. cuTensorMapEncodeTiled is
 // taken from the driver through the runtime's entry-point query.
 int encode_lm_tmap(hy_ctx* c)
@@ -1127,7 +1127,7 @@ int encode_lm_tmap(hy_ctx* c)
     const bool bf = c->cfg.weight_dtype == HY_DTYPE_BF16;
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kHidden), static_cast<cuuint64_t>(c->cfg.vocab_size)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kHidden) * c->w_elem()};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / c->w_elem()), 64};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / c->w_elem()), 128};
     const cuuint32_t estr[2] = {1, 1};
     std::memset(&c->lm_tmap, 0, sizeof(c->lm_tmap));
     const CUresult r = reinterpret_cast<EncodeFn>(fn)(

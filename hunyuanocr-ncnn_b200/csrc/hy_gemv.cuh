@@ -76,7 +76,7 @@ struct GemvArgs {
     int* posterior_out;   // LM_VERIFY [16]
     float penalty;        // LM_NONE penalty (AR / verify read st->penalty)
     int* err;
-    // M = 16 LM head: tensor map of the tied table (64-row x 128-byte boxes, 128-byte swizzle).
+    // M = 16 LM head: tensor map of the tied table (128-row x 128-byte boxes, 128-byte swizzle).
     CUtensorMap tmap;
 };
 
@@ -135,12 +135,12 @@ struct GemvShape<WT, KP, 16> {
     static constexpr int BAR_OFF = WSCR_OFF + WSCR_BYTES;
     static constexpr int RED_OFF = BAR_OFF + 2 * NST * 8;
     static constexpr int SMEM = RED_OFF + RED_BYTES;
-    // LM head (argmax epilogue): tiles of 64 rows x 128 bytes fetched by one TMA
+    // LM head (argmax epilogue): tiles of 128 rows x 128 bytes fetched by one TMA
     // copy each (tensor map with 128-byte swizzle), ring aligned to 1 KB at run time.
-    static constexpr int TL_ROWS = 64;
+    static constexpr int TL_ROWS = 128;
     static constexpr int TL_KC = 128 / static_cast<int>(sizeof(WT));   // columns per tile
     static constexpr int TL_TILE = TL_ROWS * 128;
-    static constexpr int TL_NST = 16;
+    static constexpr int TL_NST = 8;
     static constexpr int TL_WSCR_OFF = XS_BYTES + 1024 + TL_NST * TL_TILE;
     static constexpr int TL_BAR_OFF = TL_WSCR_OFF + WSCR_BYTES;
     static constexpr int TL_RED_OFF = TL_BAR_OFF + 2 * TL_NST * 8;
@@ -268,7 +268,7 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
     const int ngroups16 = (R + 7) / 8;
     const bool kmode16 = (MT == 16) && ngroups16 * (KP / S::KC16) <= kPartUnits16;
     const int nk_tl = KP / S::TL_KC;                    // TL: tiles per 64-row block
-    const int nstage = TL ? ((R + 63) / 64) * nk_tl : (MT == 16) ? ngroups16 * (KP / S::KC16) : (R + SPS - 1) / SPS;
+    const int nstage = TL ? ((R + 127) / 128) * nk_tl : (MT == 16) ? ngroups16 * (KP / S::KC16) : (R + SPS - 1) / SPS;
 
     __shared__ uint64_t s_xbar;   // M = 16: bulk copy of the activation rows
     if (tid == 0)
@@ -293,7 +293,7 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
             int issued = 0;
             if constexpr (TL)
             {
-                // One TMA copy per tile: rows r0 + 64 rb .., columns k_off + TL_KC kc ..
+                // One TMA copy per tile: rows r0 + 128 rb .., columns k_off + TL_KC kc ..
                 // (rows past the table are zero-filled by the copy).
                 for (int i = 0; i < nstage; ++i)
                 {
@@ -301,7 +301,7 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
                     if (i >= NS && !mbar_wait(&empty[slot], ((i / NS) - 1) & 1, a.err, kErrTimeoutEmpty)) break;
                     const int rb = i / nk_tl, kc = i % nk_tl;
                     mbar_arrive_expect_tx(&full[slot], S::TL_TILE);
-                    tma_load_2d(ring + slot * S::TL_TILE, &a.tmap, a.k_off + kc * S::TL_KC, r0 + 64 * rb, &full[slot]);
+                    tma_load_2d(ring + slot * S::TL_TILE, &a.tmap, a.k_off + kc * S::TL_KC, r0 + 128 * rb, &full[slot]);
                     issued = i + 1;
                 }
                 for (int i = (issued > NS ? issued - NS : 0); i < issued; ++i)
@@ -675,13 +675,12 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
         };
         if constexpr (TL)
         {
-            // Every warp reads every tile (rows 8 w .. 8 w + 7 of its 64) and arrives on it;
-            // a row block's tiles come in column order, so the accumulator runs across them.
+            // Every warp reads every tile (rows 16 w .. 16 w + 15 of its 128: two 8-row MMA
+            // tiles sharing each activation fragment) and arrives on it; a row block's tiles
+            // come in column order, so the accumulators run across them.
             // Element k of tile row r sits in 16-byte chunk (k * size / 16) ^ (r & 7).
-            // Three accumulators (lo.hi, hi.lo, hi.hi products): three independent MMA
-            // chains per warp, added when the row block's tile is read out.
-            const int r = 8 * warp + g8;
-            float acc3[3][4];
+            // Three accumulators per 8-row tile (lo.hi, hi.lo, hi.hi products), added at readout.
+            float acc3[2][3][4];
             for (int stage = 0; stage < nstage; ++stage)
             {
                 const int slot = stage % NS;
@@ -691,21 +690,16 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
                 if (kc == 0)
                 {
 #pragma unroll
-                    for (int i = 0; i < 3; ++i) acc3[i][0] = acc3[i][1] = acc3[i][2] = acc3[i][3] = 0.f;
+                    for (int h = 0; h < 2; ++h)
+#pragma unroll
+                        for (int i = 0; i < 3; ++i) acc3[h][i][0] = acc3[h][i][1] = acc3[h][i][2] = acc3[h][i][3] = 0.f;
                 }
-                const unsigned char* trow = ring + slot * S::TL_TILE + r * 128;
                 const float* x0 = xs + g8 * XP + kc * S::TL_KC + t4;
                 const float* x1 = x0 + 8 * XP;
 #pragma unroll
                 for (int kk = 0; kk < S::TL_KC / 8; ++kk)
                 {
-                    const int k = 8 * kk + t4;
-                    constexpr int ES = static_cast<int>(sizeof(WT));
-                    const int b0 = k * ES, b1 = (k + 4) * ES;
-                    const WT* p0 = reinterpret_cast<const WT*>(trow + ((((b0 >> 4) ^ (r & 7)) << 4) | (b0 & 15)));
-                    const WT* p1 = reinterpret_cast<const WT*>(trow + ((((b1 >> 4) ^ (r & 7)) << 4) | (b1 & 15)));
                     const float xa[4] = {x0[8 * kk], x1[8 * kk], x0[8 * kk + 4], x1[8 * kk + 4]};
-                    const float w0 = to_f32<WT>(*p0), w1 = to_f32<WT>(*p1);
                     unsigned ah[4], al[4];
 #pragma unroll
                     for (int i = 0; i < 4; ++i)
@@ -713,26 +707,41 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
                         ah[i] = tf32_head(xa[i]);
                         al[i] = __float_as_uint(xa[i] - __uint_as_float(ah[i]));
                     }
-                    const unsigned bh0 = tf32_head(w0), bh1 = tf32_head(w1);
-                    mma_tf32(acc3[0], al, bh0, bh1);
-                    if constexpr (!W_EXACT)
-                        mma_tf32(acc3[1], ah, __float_as_uint(w0 - __uint_as_float(bh0)),
-                                 __float_as_uint(w1 - __uint_as_float(bh1)));
-                    mma_tf32(acc3[2], ah, bh0, bh1);
+                    const int k = 8 * kk + t4;
+                    constexpr int ES = static_cast<int>(sizeof(WT));
+                    const int b0 = k * ES, b1 = (k + 4) * ES;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+                    {
+                        const int r = 16 * warp + 8 * h + g8;   // tile row; r & 7 == g8
+                        const unsigned char* trow = ring + slot * S::TL_TILE + r * 128;
+                        const float w0 = to_f32<WT>(*reinterpret_cast<const WT*>(trow + ((((b0 >> 4) ^ g8) << 4) | (b0 & 15))));
+                        const float w1 = to_f32<WT>(*reinterpret_cast<const WT*>(trow + ((((b1 >> 4) ^ g8) << 4) | (b1 & 15))));
+                        const unsigned bh0 = tf32_head(w0), bh1 = tf32_head(w1);
+                        mma_tf32(acc3[h][0], al, bh0, bh1);
+                        if constexpr (!W_EXACT)
+                            mma_tf32(acc3[h][1], ah, __float_as_uint(w0 - __uint_as_float(bh0)),
+                                     __float_as_uint(w1 - __uint_as_float(bh1)));
+                        mma_tf32(acc3[h][2], ah, bh0, bh1);
+                    }
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[slot]);
                 if (kc == nk_tl - 1)
                 {
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) d[e] = acc3[2][e] + (acc3[0][e] + acc3[1][e]);
-                    wscr[g8 * 8 + 2 * t4] = d[0];
-                    wscr[g8 * 8 + 2 * t4 + 1] = d[1];
-                    wscr[(g8 + 8) * 8 + 2 * t4] = d[2];
-                    wscr[(g8 + 8) * 8 + 2 * t4 + 1] = d[3];
-                    __syncwarp();
-                    group_epilogue(wscr, rb * 8 + warp);
-                    __syncwarp();
+                    for (int h = 0; h < 2; ++h)
+                    {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) d[e] = acc3[h][2][e] + (acc3[h][0][e] + acc3[h][1][e]);
+                        wscr[g8 * 8 + 2 * t4] = d[0];
+                        wscr[g8 * 8 + 2 * t4 + 1] = d[1];
+                        wscr[(g8 + 8) * 8 + 2 * t4] = d[2];
+                        wscr[(g8 + 8) * 8 + 2 * t4 + 1] = d[3];
+                        __syncwarp();
+                        group_epilogue(wscr, rb * 16 + 2 * warp + h);
+                        __syncwarp();
+                    }
                 }
             }
         }
