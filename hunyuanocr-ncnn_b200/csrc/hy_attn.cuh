@@ -1,8 +1,9 @@
-// GQA decode/verify attention over the KV cache, split over the key axis
+// GQA decode attention (one row) over the KV cache, split over the key axis
 // (flash-decode), with the per-head RoPE, QK RMSNorm and KV append fused into
-// the prologue.
+// the prologue; used by the per-phase AR path and the standalone attention
+// entry point (steps of 2..16 rows: hy_prefill.cuh).
 //
-// Replaces, for the decode and DFlash-verify steps:
+// Replaces, for the decode step:
 //   - MultimodalRotaryEmbed (src/multimodal_rope.cpp:176-187): full-width
 //     cos/sin, out[d] = x[d]c[d] - x[d+64]s[d], out[d+64] = x[d+64]c[d+64] + x[d]s[d+64];
 //   - query_layernorm / key_layernorm applied after RoPE (export/text_decoder_kv.py:70-73);
@@ -102,6 +103,9 @@ __device__ __forceinline__ void rope_norm_vec(const float* x, const float* c, co
 template <int MT, typename KT>
 __global__ void __launch_bounds__(kAttnThreads, (MT == 1) ? 2 : 1) attn_kernel(const AttnArgs a)
 {
+    // Steps of 2..16 rows use the tensor-core kernels of hy_prefill.cuh (RoPE /
+    // append kernel, key chunks, chunk merge).
+    static_assert(MT == 1, "one-row decode attention");
     using S = AttnShape<MT, KT>;
     constexpr int NQ = S::NQ, NSTREAM = S::NSTREAM, ROWB = S::ROWB, STAGE = S::STAGE;
     extern __shared__ __align__(128) unsigned char smem[];
@@ -273,114 +277,6 @@ __global__ void __launch_bounds__(kAttnThreads, (MT == 1) ? 2 : 1) attn_kernel(c
     attn_consumers_sync();
     pdl_launch();
 
-    if constexpr (MT == 16)
-    {
-        // 32 queries (16 rows x 2 heads), key-stationary: warp w takes query
-        // half w & 1 (16 queries) and position group w >> 1 (positions
-        // 8 pg .. 8 pg + 7 of every 32-position stage); lane = (query, dim
-        // half): query 16 * (w & 1) + lane / 2 and dims 8 i + 4 h (i < 16,
-        // h = lane & 1), so a K/V read is two 16-byte broadcasts in
-        // different banks and a score needs one shuffle. Positions go in
-        // blocks of 8: one rescale of the running state per block.
-        const int h = lane & 1;
-        const int qi = (warp & 1) * 16 + (lane >> 1);
-        const int stream = warp >> 1;
-        const int qm = qi % MT;
-        float4 qv[16], ov[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-        {
-            qv[i] = *reinterpret_cast<const float4*>(qs + qi * kHeadDim + 8 * i + 4 * h);
-            ov[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        float mx = -INFINITY, l = 0.f;
-        // Up to 8 positions: rows krow0 + j*kHeadDim for j < nv; position j is
-        // visible to this lane's query iff vis(j).
-        auto block8 = [&](const auto* kb, const auto* vb, int nv, auto vis) {
-            float sc[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-            {
-                float a0 = 0.f, a1 = 0.f;
-                if (j < nv)
-                {
-#pragma unroll
-                    for (int i = 0; i < 16; i += 2)
-                    {
-                        a0 += dot4(qv[i], load4(kb + j * kHeadDim + 8 * i + 4 * h));
-                        a1 += dot4(qv[i + 1], load4(kb + j * kHeadDim + 8 * (i + 1) + 4 * h));
-                    }
-                }
-                sc[j] = a0 + a1;
-            }
-#pragma unroll
-            for (int j = 0; j < 8; ++j) sc[j] += __shfl_xor_sync(0xffffffffu, sc[j], 1);
-            float mb = -INFINITY;
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                if (j < nv && vis(j)) mb = fmaxf(mb, sc[j]);
-            if (mb == -INFINITY) return;   // nothing visible to this query in the block
-            const float mn = fmaxf(mx, mb);
-            const float corr = (mx == -INFINITY) ? 0.f : exp2f(mx - mn);
-            l *= corr;
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-            {
-                ov[i].x *= corr; ov[i].y *= corr; ov[i].z *= corr; ov[i].w *= corr;
-            }
-            mx = mn;
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-            {
-                if (j < nv && vis(j))
-                {
-                    const float pe = exp2f(sc[j] - mn);
-                    l += pe;
-#pragma unroll
-                    for (int i = 0; i < 16; ++i)
-                    {
-                        const float4 vv = load4(vb + j * kHeadDim + 8 * i + 4 * h);
-                        ov[i].x += pe * vv.x; ov[i].y += pe * vv.y; ov[i].z += pe * vv.z; ov[i].w += pe * vv.w;
-                    }
-                }
-            }
-        };
-        for (int i = 0; i < nstage; ++i)
-        {
-            const int slot = i % kAttnStages;
-            const bool ok = mbar_wait(&full[slot], (i / kAttnStages) & 1, a.err, kErrTimeoutFull);
-            if (!__all_sync(0xffffffffu, ok)) break;
-            const KT* kst = reinterpret_cast<const KT*>(ring + slot * STAGE);
-            const KT* vst = reinterpret_cast<const KT*>(ring + slot * STAGE + kAttnPos * ROWB);
-            const int n = min(kAttnPos, npos - i * kAttnPos);
-            const int j0 = 8 * stream;
-            if (j0 < n)
-                block8(kst + j0 * kHeadDim, vst + j0 * kHeadDim, min(8, n - j0), [](int) { return true; });
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
-        }
-        // New rows (causal inside the block: row m sees new row j iff j <= m);
-        // position group pg takes new rows 4 pg .. 4 pg + 3.
-        if (new_split)
-        {
-            const int j0 = 4 * stream;
-            if (j0 < rows)
-                block8(knew + j0 * kHeadDim, vnew + j0 * kHeadDim, min(4, rows - j0),
-                       [&](int j) { return j0 + j <= qm; });
-        }
-        // Per-stream states to shared memory (aliasing the drained ring).
-        attn_consumers_sync();
-        if (h == 0)
-        {
-            scr_ml[(stream * NQ + qi) * 2 + 0] = mx;
-            scr_ml[(stream * NQ + qi) * 2 + 1] = l;
-        }
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-            *reinterpret_cast<float4*>(scr_acc + (stream * NQ + qi) * kHeadDim + 8 * i + 4 * h) = ov[i];
-        attn_consumers_sync();
-    }
-    else
     {
         // Lane roles.
         const int qr = lane & 3;

@@ -1,6 +1,8 @@
-// Prompt prefill, per layer, besides the projections (hy_umma.cuh): RoPE +
-// QK RMSNorm + KV append for every row of a prefill pass, and the causal
-// attention of those rows over the KV cache on the tensor cores.
+// Attention of many-row steps on the tensor cores: RoPE + QK RMSNorm + KV
+// append for every row of a step, and the causal attention of those rows over
+// the KV cache - for prompt prefill passes (up to 1024 rows; the projections
+// are in hy_umma.cuh) and for the steps of 2..16 rows (DFlash verify blocks,
+// decoder steps).
 #pragma once
 
 #include "hy_attn.cuh"
