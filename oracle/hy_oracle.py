@@ -567,23 +567,24 @@ def decode_ar(w: Weights, cfg: ModelConfig, prompt: Prompt, max_tokens: int, pen
 
 
 def verify_block(w: Weights, cfg: ModelConfig, cache: KVCache, proposed, history_before_block,
-                 penalty: float):
+                 penalty: float, aux: bool = False):
     """The verify half of run_dflash_block (src/text_runtime.cpp:959-1070).
 
     Runs the M=16 verify forward at positions context_len..context_len+15 with
     the causal-in-block mask, then select_logit_rows with the growing history.
-    Returns (posterior, acceptance_length, logits, hidden); the cache keeps
-    context_len + 16 rows (the caller rolls back).
+    Returns (posterior, acceptance_length, logits, hidden), or with aux the
+    block's aux hidden states (layers 1, 8, 15, 22) in place of hidden; the
+    cache keeps context_len + 16 rows (the caller rolls back).
     """
     ctx = cache.length
     emb = w.embed[np.asarray(proposed, dtype=np.int64)]
     mask = build_dflash_verify_mask(ctx)
     cos = rope_rows(ctx, DFLASH_BLOCK, True)
     sin = rope_rows(ctx, DFLASH_BLOCK, False)
-    hidden, _ = decoder_forward(w, cfg, emb, mask, cos, sin, cache)
+    hidden, aux_h = decoder_forward(w, cfg, emb, mask, cos, sin, cache, aux)
     logits = lm_head(w, hidden)
     posterior = select_logit_rows(logits, history_before_block, proposed, penalty)
-    return posterior, dflash_acceptance_length(proposed, posterior), logits, hidden
+    return posterior, dflash_acceptance_length(proposed, posterior), logits, (aux_h if aux else hidden)
 
 
 @dataclass
@@ -673,3 +674,180 @@ def synthetic_drafter(greedy: list, p: float, vocab: int, seed: int):
                 out.append(int((h & 0xFFFFFFFF) % vocab))
         return out
     return fn
+
+
+# ---------------------------------------------------------------------------
+# DFlash draft network (export/dflash_export.py:88-177, the graph that
+# DFlashDraftRuntime::run executes, src/dflash_runtime.cpp:213-290; called by
+# run_dflash_block, src/text_runtime.cpp:880-950).
+#
+# target_hidden = hidden_norm(fc(concat(aux_0..3))) over the context rows; per
+# draft layer: q from the 16 noise rows, k/v from the context rows followed by
+# the noise rows; q_norm / k_norm BEFORE RoPE (theta 10000, positions 0..ctx+15,
+# src/dflash_runtime.cpp:27-48); SDPA with the all-zero mask
+# (src/dflash_runtime.cpp:50-58) and scale 1/sqrt(128); o_proj + residual;
+# SwiGLU MLP + residual; final RMSNorm. The block's drafts are the argmax of the
+# tied LM head on rows 1..15 (penalty 1, no history).
+# The draft's layers here have the decoder's geometry (16 q heads, 8 KV heads,
+# head_dim 128, the FFN width of the config); the number of layers is a parameter.
+# ---------------------------------------------------------------------------
+DRAFT_ROPE_THETA = 10000.0
+DRAFT_SCALE = 1.0 / math.sqrt(HEAD_DIM)
+TID_DRAFT_FC = 19990
+TID_DRAFT_HIDDEN_NORM = 19991
+TID_DRAFT_NORM = 19992
+DRAFT_TID_BASE = 20000
+DRAFT_TID_STRIDE = 16
+
+
+@dataclass
+class DraftWeights:
+    fc: np.ndarray            # [1024 x 4096] (aux layers 1, 8, 15, 22 concatenated)
+    hidden_norm: np.ndarray   # [1024]
+    norm: np.ndarray          # [1024]
+    layers: list = field(default_factory=list)   # LayerWeights
+
+
+def make_draft_weights(num_layers: int, seed: int, std: float = 0.02, norm_std: float = 0.0,
+                       ffn: int = FFN, bf16: bool = False) -> DraftWeights:
+    """Seeded draft weights on the same counter generator (tensor ids from DRAFT_TID_BASE)."""
+    def lin(tid, rows, cols):
+        t = synth_tensor_fast(seed, tid, rows * cols, std).reshape(rows, cols)
+        return round_bf16(t) if bf16 else t
+
+    def norm(tid, n):
+        return synth_tensor_fast(seed, tid, n, norm_std, 1.0)
+
+    layers = []
+    for li in range(num_layers):
+        b = DRAFT_TID_BASE + DRAFT_TID_STRIDE * li
+        layers.append(LayerWeights(
+            input_norm=norm(b + J_INPUT_NORM, HIDDEN), q=lin(b + J_Q, Q_WIDTH, HIDDEN),
+            k=lin(b + J_K, KV_WIDTH, HIDDEN), v=lin(b + J_V, KV_WIDTH, HIDDEN),
+            q_norm=norm(b + J_Q_NORM, HEAD_DIM), k_norm=norm(b + J_K_NORM, HEAD_DIM),
+            o=lin(b + J_O, HIDDEN, Q_WIDTH), post_norm=norm(b + J_POST_NORM, HIDDEN),
+            gate=lin(b + J_GATE, ffn, HIDDEN), up=lin(b + J_UP, ffn, HIDDEN), down=lin(b + J_DOWN, HIDDEN, ffn)))
+    return DraftWeights(fc=lin(TID_DRAFT_FC, HIDDEN, 4 * HIDDEN), hidden_norm=norm(TID_DRAFT_HIDDEN_NORM, HIDDEN),
+                        norm=norm(TID_DRAFT_NORM, HIDDEN), layers=layers)
+
+
+def build_dflash_rope(start: int, rows: int, use_cos: bool) -> np.ndarray:
+    """build_dflash_rope (src/dflash_runtime.cpp:27-48) rows start..start+rows-1:
+    angle = float(position) / powf(10000, float(2 * (d % 64)) / 128), then cosf / sinf."""
+    out = np.empty((rows, HEAD_DIM), dtype=np.float32)
+    den = np.empty(HEAD_DIM, dtype=np.float32)
+    for d in range(HEAD_DIM):
+        expo = _f32(_f32(2 * (d % (HEAD_DIM // 2))) / _f32(HEAD_DIM))
+        den[d] = _f32(math.pow(DRAFT_ROPE_THETA, float(expo)))
+    pos = np.arange(start, start + rows, dtype=np.int64).astype(np.float32)
+    angle = (pos[:, None] / den[None, :]).astype(np.float32)
+    return _cos32(angle) if use_cos else _sin32(angle)
+
+
+@dataclass
+class DraftCache:
+    """Per draft layer K (normed, roped) / V [8, capacity, 128] of the context rows."""
+    k: list
+    v: list
+    length: int = 0
+
+    @staticmethod
+    def empty(num_layers: int, capacity: int) -> "DraftCache":
+        return DraftCache([np.zeros((NUM_KV_HEADS, capacity, HEAD_DIM), np.float32) for _ in range(num_layers)],
+                          [np.zeros((NUM_KV_HEADS, capacity, HEAD_DIM), np.float32) for _ in range(num_layers)], 0)
+
+
+def draft_context_rows(dw: DraftWeights, aux: list, eps: float = RMS_EPS) -> np.ndarray:
+    """target_hidden = hidden_norm(fc(concat(aux_0..3))) for rows [n, 1024] each."""
+    cat = np.concatenate([np.asarray(a, np.float32) for a in aux], axis=-1)
+    return rms_norm(cat @ dw.fc.T, dw.hidden_norm, eps)
+
+
+def draft_append_context(dw: DraftWeights, cache: DraftCache, aux: list, eps: float = RMS_EPS) -> None:
+    """Append context rows: each layer's k = rope(k_norm(k_proj(th))), v = v_proj(th) at their positions."""
+    th = draft_context_rows(dw, aux, eps)
+    n = th.shape[0]
+    start = cache.length
+    cos, sin = build_dflash_rope(start, n, True), build_dflash_rope(start, n, False)
+    for li, lw in enumerate(dw.layers):
+        k = (th @ lw.k.T).reshape(n, NUM_KV_HEADS, HEAD_DIM).transpose(1, 0, 2)
+        v = (th @ lw.v.T).reshape(n, NUM_KV_HEADS, HEAD_DIM).transpose(1, 0, 2)
+        k = apply_rope(rms_norm(k, lw.k_norm, eps), cos, sin)
+        cache.k[li][:, start:start + n] = k
+        cache.v[li][:, start:start + n] = v
+    cache.length = start + n
+
+
+def draft_forward(dw: DraftWeights, noise: np.ndarray, cache: DraftCache, eps: float = RMS_EPS) -> np.ndarray:
+    """The draft graph for the 16 noise rows over the cached context; returns the
+    final-normed hidden rows [16, 1024]."""
+    m = noise.shape[0]
+    ctx = cache.length
+    cos, sin = build_dflash_rope(ctx, m, True), build_dflash_rope(ctx, m, False)
+    h = np.asarray(noise, np.float32)
+    mask = np.zeros((m, ctx + m), np.float32)
+    for li, lw in enumerate(dw.layers):
+        a = rms_norm(h, lw.input_norm, eps)
+        q = (a @ lw.q.T).reshape(m, NUM_Q_HEADS, HEAD_DIM).transpose(1, 0, 2)
+        k = (a @ lw.k.T).reshape(m, NUM_KV_HEADS, HEAD_DIM).transpose(1, 0, 2)
+        v = (a @ lw.v.T).reshape(m, NUM_KV_HEADS, HEAD_DIM).transpose(1, 0, 2)
+        q = apply_rope(rms_norm(q, lw.q_norm, eps), cos, sin)
+        k = apply_rope(rms_norm(k, lw.k_norm, eps), cos, sin)
+        K = np.concatenate([cache.k[li][:, :ctx], k], axis=1)
+        V = np.concatenate([cache.v[li][:, :ctx], v], axis=1)
+        att = precise_sdpa(q, K, V, mask, DRAFT_SCALE).transpose(1, 0, 2).reshape(m, Q_WIDTH)
+        h = (h + att @ lw.o.T).astype(np.float32)
+        p = rms_norm(h, lw.post_norm, eps)
+        g = p @ lw.gate.T
+        u = p @ lw.up.T
+        h = (h + ((g / (np.float32(1.0) + np.exp(-g))) * u).astype(np.float32) @ lw.down.T).astype(np.float32)
+    return rms_norm(h, dw.norm, eps)
+
+
+def draft_propose(w: Weights, dw: DraftWeights, cache: DraftCache, current: int, eps: float = RMS_EPS):
+    """run_dflash_block's draft half (src/text_runtime.cpp:913-978): noise = embed([current, MASK x 15]),
+    drafts = argmax of the LM head on draft rows 1..15 (penalty 1, no history).
+    Returns (proposed block [16], draft hidden [16, 1024])."""
+    block = build_dflash_block(current)
+    hidden = draft_forward(dw, w.embed[np.asarray(block)], cache, eps)
+    logits = lm_head(w, hidden[1:])
+    block[1:] = select_logit_rows(logits, [], None, 1.0)
+    return block, hidden
+
+
+def decode_dflash_draft(w: Weights, cfg: ModelConfig, dw: DraftWeights, prompt: Prompt, max_tokens: int,
+                        penalty: float = DEFAULT_PENALTY, eos_ids=()) -> DFlashTrace:
+    """decode_dflash_from_embeddings with the draft network: the draft context starts
+    as the prompt's aux hidden states (run_dflash_prefill) and grows by the aux
+    rows of every block's committed tokens (append_dflash_rows)."""
+    seq = prompt.input_ids.shape[0]
+    capacity = seq + max_tokens + 2 * DFLASH_BLOCK
+    hidden, cache, aux = prefill(w, cfg, prompt, capacity, aux=True)
+    dcache = DraftCache.empty(len(dw.layers), capacity)
+    draft_append_context(dw, dcache, aux, cfg.rms_eps)
+    logits = lm_head(w, hidden[seq - 1:seq])[0]
+    history = [int(t) for t in prompt.input_ids]
+    current, _ = select_next_token(logits, history, penalty)
+    tr = DFlashTrace([], [])
+    while len(tr.tokens) < max_tokens:
+        ctx = cache.length
+        proposed, _ = draft_propose(w, dw, dcache, current, cfg.rms_eps)
+        posterior, accept, _, vaux = verify_block(w, cfg, cache, proposed, history, penalty, aux=True)
+        available = accept + 1
+        committed = min(available, max_tokens - len(tr.tokens))
+        stop = False
+        for i in range(committed):
+            tr.tokens.append(proposed[i])
+            if proposed[i] in eos_ids:
+                committed = i + 1
+                stop = True
+                break
+        tr.block_count += 1
+        tr.acceptance_lengths.append(max(0, committed - 1))
+        if committed < available or stop or len(tr.tokens) >= max_tokens:
+            break
+        cache.length = ctx + committed
+        draft_append_context(dw, dcache, [a[:committed] for a in vaux], cfg.rms_eps)
+        history.extend(proposed[:committed])
+        current = posterior[accept]
+    return tr

@@ -146,3 +146,32 @@ def test_oracle_matches_reference_wrapper(oracle, case):
     assert accept == int(g["verify_accept"])
     np.testing.assert_allclose(np.take_along_axis(vlogits, g["verify_top8_idx"], 1), g["verify_top8_val"],
                                rtol=0, atol=2e-4)
+
+
+def test_draft_network_matches_reference_wrapper(oracle):
+    """The oracle's DFlash draft forward (context append + 2 draft layers) against the
+    reference's own draft graph (export/dflash_export.py DFlashExportWrapper), run by
+    tests/golden/make_dflash_draft_golden.py on the same synthetic draft weights."""
+    g = load_golden("dflash_draft_2l")
+    layers, ctx = int(g["layers"]), int(g["ctx"])
+    dw = oracle.make_draft_weights(layers, int(g["seed"]), 0.02, float(g["norm_std"]))
+    rng = np.random.default_rng(int(g["input_seed"]))
+    noise = rng.standard_normal((oracle.DFLASH_BLOCK, oracle.HIDDEN)).astype(np.float32)
+    aux = [rng.standard_normal((ctx, oracle.HIDDEN)).astype(np.float32) for _ in range(4)]
+    assert math.isclose(noise.astype(np.float64).sum(), float(g["noise_sum"]), rel_tol=0, abs_tol=1e-9)
+    assert math.isclose(sum(a.astype(np.float64).sum() for a in aux), float(g["aux_sum"]), rel_tol=0, abs_tol=1e-9)
+    cache = oracle.DraftCache.empty(layers, ctx + oracle.DFLASH_BLOCK)
+    oracle.draft_append_context(dw, cache, aux)
+    out = oracle.draft_forward(dw, noise, cache)
+    np.testing.assert_allclose(out, g["out"], rtol=1e-4, atol=2e-5)
+
+
+def test_draft_rope_formula(oracle):
+    """build_dflash_rope (src/dflash_runtime.cpp:27-48): position p, dim d uses
+    p / 10000^(2 (d % 64) / 128); position 0 is cos 1, sin 0; dims d and d + 64 match."""
+    c = oracle.build_dflash_rope(0, 5, True)
+    s = oracle.build_dflash_rope(0, 5, False)
+    assert np.all(c[0] == 1.0) and np.all(s[0] == 0.0)
+    np.testing.assert_array_equal(c[:, :64], c[:, 64:])
+    np.testing.assert_allclose(c[3, 1], math.cos(3.0 / 10000.0 ** (2.0 / 128.0)), rtol=1e-6)
+    np.testing.assert_allclose(s[4, 0], math.sin(4.0), rtol=1e-6)
