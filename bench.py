@@ -13,7 +13,8 @@ decoder steps run by the persistent decode kernel, 64 tokens per launch: embed
 device). `value` = decode tokens/s with the prompt state resident in HBM;
 `e2e` = tokens/s of the reference-facing call (hy_run_vlm_decode_with_prompt:
 host prompt -> prefill -> 256 tokens -> host). `dflash` = config 3 (KV 2048,
-block 16, synthetic drafts at p = 0.3 / 0.7 / 0.9), device-timed.
+block 16, synthetic drafts at p = 0.3 / 0.7 / 0.9), device-timed, plus the cost of
+a block with the draft network (`draft_net`, random-init draft weights).
 
 Multi-GPU (torchrun, one process per GPU): replicas only - each rank decodes its
 own request; value = tokens of all ranks / max rank time ("scaling": "weak").
@@ -52,6 +53,9 @@ MEGA_CHUNK = 64                      # tokens per persistent-kernel launch (hy_c
 # DRAM bytes (read + write) of one full 64-token launch (tokens 129-192), from the 1-pass ncu
 # capture summarised in profiles/mega_decode_kernel_config0.md.
 MEGA_TRAFFIC_PER_LAUNCH = 152.88e9
+# Draft depth of the DFlash draft network leg. The reference loads the draft from its
+# DFlash package (export/dflash_export.py takes any depth); 5 layers is an assumption.
+DRAFT_LAYERS = 5
 
 
 def measured_peaks():
@@ -203,6 +207,30 @@ def dflash_leg(pkg, local):
     rt.set_history(hist)
     ms, _ = device_ms(rt, lambda: rt.bench_ar_steps(n_tok - 1))
     out["ar_tokens_per_s_kv2048"] = round((n_tok - 1) / (ms / 1e3), 1)
+
+    # The draft network (hy_dflash_generate): a random-init draft of DRAFT_LAYERS layers over a
+    # 2048-row draft context. Its drafts are essentially never accepted, so this measures the
+    # cost of a block with the draft (draft + verify + context rows + commit), not an acceptance law.
+    rt.reset()
+    rt.load_draft_synthetic(DRAFT_LAYERS, seed=3, std=0.02)
+    aux = np.random.default_rng(0).standard_normal((4, seq, HIDDEN), dtype=np.float32)
+    rt.draft_context_append(aux)
+    n_draft = 64
+    rt.set_length(seq)
+    rt.set_history(hist)
+    rt.draft_propose(1234)
+    d_ms, _ = device_ms(rt, lambda: [rt.draft_propose(1234) for _ in range(10)])
+    best = None
+    for _ in range(2):
+        rt.set_length(seq)
+        rt.set_history(hist)
+        ms, r = device_ms(rt, lambda: rt.dflash_generate(1234, n_draft, PENALTY))
+        assert r.generated_tokens == greedy[:len(r.generated_tokens)], "DFlash with the draft is not lossless"
+        best = ms if best is None else min(best, ms)
+    out["draft_net"] = {"layers": DRAFT_LAYERS, "draft_ms": round(d_ms / 10, 3),
+                        "ms_per_block": round(best / max(1, r.block_count), 3),
+                        "tokens_per_s": round(len(r.generated_tokens) / (best / 1e3), 1),
+                        "blocks": r.block_count, "mean_accept": round(float(np.mean(r.acceptance_lengths)), 3)}
     rt.close()
     return out
 

@@ -46,8 +46,11 @@ EXPORTED_SYMBOLS = (
     "hy_dflash_generate_synthetic", "hy_run_vlm_decode_with_prompt", "hy_attention", "hy_kv_write",
     "hy_kv_read", "hy_seq_set_length", "hy_bench_ar_steps", "hy_bench_kernel", "hy_ctx_stream",
     "hy_ctx_set_ar_path", "hy_ctx_ar_path", "hy_trace_persistent", "hy_debug_progress",
-    "hy_lm_head_select_noalloc",
+    "hy_lm_head_select_noalloc", "hy_draft_load", "hy_draft_load_synthetic", "hy_draft_context_length",
+    "hy_draft_context_append", "hy_draft_run", "hy_draft_propose", "hy_dflash_generate",
+    "hy_run_vlm_dflash_with_prompt",
 )
+DFLASH_MASK_TOKEN = 120817
 AR_PATH_PERSISTENT = 0
 AR_PATH_GRAPH = 1
 
@@ -72,6 +75,12 @@ class _LayerWeights(ctypes.Structure):
     _fields_ = [(n, ctypes.c_void_p) for n in (
         "input_norm", "q_proj", "k_proj", "v_proj", "query_norm", "key_norm", "o_proj", "post_norm",
         "gate_proj", "up_proj", "down_proj")]
+
+
+class _DraftWeights(ctypes.Structure):
+    _fields_ = [("num_layers", ctypes.c_int), ("mask_token", ctypes.c_int), ("fc", ctypes.c_void_p),
+                ("hidden_norm", ctypes.c_void_p), ("norm", ctypes.c_void_p),
+                ("layers", ctypes.POINTER(_LayerWeights))]
 
 
 class _Weights(ctypes.Structure):
@@ -131,6 +140,15 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "hy_ctx_set_ar_path": ([_P, _I], _I),
         "hy_ctx_ar_path": ([_P], _I),
         "hy_trace_persistent": ([_P, _I, _I, _P], _I),
+        "hy_draft_load": ([_P, ctypes.POINTER(_DraftWeights)], _I),
+        "hy_draft_load_synthetic": ([_P, _I, _I, ctypes.c_uint64, _F, _F], _I),
+        "hy_draft_context_length": ([_P, ctypes.POINTER(_I)], _I),
+        "hy_draft_context_append": ([_P, _P, _I], _I),
+        "hy_draft_run": ([_P, _P, _P], _I),
+        "hy_draft_propose": ([_P, _I, _P], _I),
+        "hy_dflash_generate": ([_P, _I, _I, _F, _P, _I, _P, ctypes.POINTER(_I), _P, ctypes.POINTER(_I)], _I),
+        "hy_run_vlm_dflash_with_prompt": ([_P, _P, _P, _I, _I, _P, _I, _I, _F, _P, _I, _P, ctypes.POINTER(_I), _P,
+                                           ctypes.POINTER(_I)], _I),
         "hy_debug_progress": ([_P, _P, _I], _I),
     }
     for name, (argtypes, restype) in sig.items():
@@ -409,6 +427,85 @@ class TextRuntime:
                                                   _ptr(eos), 0 if eos is None else eos.size, _ptr(tokens),
                                                   _ptr(raw), ctypes.byref(n)))
         return TextDecodeResult(ids.size, repetition_penalty, tokens[:n.value].tolist(), raw[:n.value].tolist())
+
+    # -- DFlash draft network -------------------------------------------------
+    def load_draft(self, draft_weights, mask_token: int = DFLASH_MASK_TOKEN) -> None:
+        """DFlashDraftRuntime::load (src/dflash_runtime.cpp:175-201). draft_weights: an object with
+        .fc, .hidden_norm, .norm and .layers[i] as in from_weights (numpy fp32, nn.Linear layout)."""
+        keep = []
+
+        def p(a):
+            a = _f32(a)
+            keep.append(a)
+            return a.ctypes.data
+
+        n = len(draft_weights.layers)
+        layers = (_LayerWeights * n)()
+        for i, lw in enumerate(draft_weights.layers):
+            layers[i] = _LayerWeights(p(lw.input_norm), p(lw.q), p(lw.k), p(lw.v), p(lw.q_norm), p(lw.k_norm),
+                                      p(lw.o), p(lw.post_norm), p(lw.gate), p(lw.up), p(lw.down))
+        w = _DraftWeights(n, mask_token, p(draft_weights.fc), p(draft_weights.hidden_norm), p(draft_weights.norm),
+                          layers)
+        _check(_LIB.hy_draft_load(self._ctx, ctypes.byref(w)))
+
+    def load_draft_synthetic(self, num_layers: int, seed: int, std: float = 0.02, norm_std: float = 0.0,
+                             mask_token: int = DFLASH_MASK_TOKEN) -> None:
+        _check(_LIB.hy_draft_load_synthetic(self._ctx, num_layers, mask_token, seed, std, norm_std))
+
+    @property
+    def draft_context_length(self) -> int:
+        n = ctypes.c_int()
+        _check(_LIB.hy_draft_context_length(self._ctx, ctypes.byref(n)))
+        return n.value
+
+    def draft_context_append(self, aux_hidden) -> None:
+        """append_dflash_rows (src/dflash_runtime.cpp:121-166): aux_hidden [4, rows, 1024]."""
+        a = _f32(aux_hidden)
+        _check(_LIB.hy_draft_context_append(self._ctx, _ptr(a), a.shape[1]))
+
+    def draft_run(self, noise) -> np.ndarray:
+        """DFlashDraftRuntime::run (src/dflash_runtime.cpp:213-290): final-normed draft rows [16, 1024]."""
+        x = _f32(noise)
+        out = np.empty((DFLASH_BLOCK, HIDDEN), np.float32)
+        _check(_LIB.hy_draft_run(self._ctx, _ptr(x), _ptr(out)))
+        return out
+
+    def draft_propose(self, current_token: int) -> list:
+        out = np.empty(DFLASH_BLOCK, np.int32)
+        _check(_LIB.hy_draft_propose(self._ctx, current_token, _ptr(out)))
+        return out.tolist()
+
+    def dflash_generate(self, first_token: int, max_tokens: int, penalty: float, eos_ids=()) -> DFlashDecodeResult:
+        eos = _i32(list(eos_ids)) if len(eos_ids) else None
+        tokens = np.empty(max_tokens, np.int32)
+        acc = np.empty(max_tokens + DFLASH_BLOCK, np.int32)
+        n, nb = ctypes.c_int(), ctypes.c_int()
+        _check(_LIB.hy_dflash_generate(self._ctx, first_token, max_tokens, penalty, _ptr(eos),
+                                       0 if eos is None else eos.size, _ptr(tokens), ctypes.byref(n), _ptr(acc),
+                                       ctypes.byref(nb)))
+        accl = acc[:nb.value].tolist()
+        return DFlashDecodeResult(tokens[:n.value].tolist(), nb.value, nb.value * (DFLASH_BLOCK - 1),
+                                  int(sum(accl)), accl)
+
+    def run_vlm_dflash_with_prompt(self, input_ids, position_ids, image_token_id: int, vision_features,
+                                   max_tokens: int, repetition_penalty: float = 1.08,
+                                   eos_ids=()) -> DFlashDecodeResult:
+        """run_vlm_decode_with_prompt with --dflash (src/text_runtime.cpp:1142-1305)."""
+        ids = _i32(input_ids)
+        pos = _i32(position_ids).reshape(-1)
+        feats = _f32(vision_features).reshape(-1, HIDDEN)
+        eos = _i32(list(eos_ids)) if len(eos_ids) else None
+        mt = max_tokens if max_tokens > 0 else 1024
+        tokens = np.empty(mt, np.int32)
+        acc = np.empty(mt + DFLASH_BLOCK, np.int32)
+        n, nb = ctypes.c_int(), ctypes.c_int()
+        _check(_LIB.hy_run_vlm_dflash_with_prompt(self._ctx, _ptr(ids), _ptr(pos), ids.size, image_token_id,
+                                                  _ptr(feats), feats.shape[0], max_tokens, repetition_penalty,
+                                                  _ptr(eos), 0 if eos is None else eos.size, _ptr(tokens),
+                                                  ctypes.byref(n), _ptr(acc), ctypes.byref(nb)))
+        accl = acc[:nb.value].tolist()
+        return DFlashDecodeResult(tokens[:n.value].tolist(), nb.value, nb.value * (DFLASH_BLOCK - 1),
+                                  int(sum(accl)), accl)
 
     # -- timing hooks --------------------------------------------------------
     def bench_ar_steps(self, count: int) -> float:

@@ -100,6 +100,22 @@ __device__ __forceinline__ void rope_norm_vec(const float* x, const float* c, co
     out[3] = w[lane + 96] * (y3 * ri);
 }
 
+// RMSNorm, then RoPE, of one 128-vector by one warp: the DFlash draft's order
+// (q_norm / k_norm before apply_external_rope, export/dflash_export.py:104-128).
+__device__ __forceinline__ void norm_rope_vec(const float* x, const float* c, const float* s, const float* w, float eps,
+                                              int lane, float out[4])
+{
+    const float x0 = x[lane], x1 = x[lane + 32], x2 = x[lane + 64], x3 = x[lane + 96];
+    const float ss = warp_sum(x0 * x0 + x1 * x1 + x2 * x2 + x3 * x3);
+    const float ri = 1.0f / sqrtf(ss / static_cast<float>(kHeadDim) + eps);
+    const float n0 = w[lane] * (x0 * ri), n1 = w[lane + 32] * (x1 * ri);
+    const float n2 = w[lane + 64] * (x2 * ri), n3 = w[lane + 96] * (x3 * ri);
+    out[0] = n0 * c[lane] - n2 * s[lane];
+    out[1] = n1 * c[lane + 32] - n3 * s[lane + 32];
+    out[2] = n2 * c[lane + 64] + n0 * s[lane + 64];
+    out[3] = n3 * c[lane + 96] + n1 * s[lane + 96];
+}
+
 template <int MT, typename KT>
 __global__ void __launch_bounds__(kAttnThreads, (MT == 1) ? 2 : 1) attn_kernel(const AttnArgs a)
 {

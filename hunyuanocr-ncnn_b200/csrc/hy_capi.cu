@@ -154,6 +154,34 @@ struct hy_ctx {
     cudaGraphExec_t g_verify_draft = nullptr;
     cudaGraphExec_t g_verify_ids = nullptr;
 
+    // DFlash draft network (hy_draft_load*): its weights (decoder-layer geometry),
+    // its K/V cache of the context rows, its RoPE table (theta 10000) and buffers.
+    // The draft context covers KV rows [0, d_len); every path that appends KV
+    // rows while a draft is loaded appends their context rows too.
+    int d_layers = 0;
+    int d_mask = 0;                          // mask token of the noise block
+    int d_len = 0;                           // host mirror: rows with draft context
+    void* d_fc = nullptr;                    // [1024 x 4096] WT
+    std::vector<void*> d_wqkv, d_wo, d_wgu, d_wd;
+    float* d_norms = nullptr;                // per layer input, post, qn, kn (2304); then hidden_norm, norm
+    void* d_kc = nullptr;                    // [d_layers][8][cap][128] KT
+    void* d_vc = nullptr;
+    float* d_cos = nullptr;                  // [max_context x 128], theta 10000
+    float* d_sin = nullptr;
+    float* d_x = nullptr;                    // [16 x 1024] draft residual stream
+    float* d_aux = nullptr;                  // [16 x 4096] aux rows of a step (layers 1, 8, 15, 22 side by side)
+    float* d_pf_aux = nullptr;               // [pf_rows x 4096] aux rows of a prefill pass
+    float* d_pf_a_hi = nullptr;              // the same, split and tiled [pf_pad x 4096]
+    float* d_pf_a_lo = nullptr;
+    float* d_pf_fc = nullptr;                // [pf_rows x 1024] fc output
+    float* d_tfc_hi = nullptr;               // fc tiled [1024 x 4096]
+    float* d_tfc_lo = nullptr;
+    std::vector<float*> d_tkv_hi, d_tkv_lo;  // k | v rows tiled [2048 x 1024] per draft layer
+    std::vector<void*> d_allocs;
+    size_t d_bytes = 0;
+    cudaGraphExec_t g_dflash = nullptr;           // draft + verify + context append + commit
+    cudaGraphExec_t g_verify_ids_ctx = nullptr;   // verify of given ids + context append + commit
+
     size_t kv_elem() const { return cfg.kv_dtype == HY_DTYPE_BF16 ? 2 : 4; }
     size_t w_elem() const { return cfg.weight_dtype == HY_DTYPE_BF16 ? 2 : 4; }
     float* in_norm(int l) const { return norms + static_cast<size_t>(l) * 2304; }
@@ -168,6 +196,20 @@ struct hy_ctx {
     void* vc_layer(int l) const
     {
         return static_cast<char*>(vc) + static_cast<size_t>(l) * kNumKVHeads * cfg.max_context * kHeadDim * kv_elem();
+    }
+    float* d_in_norm(int l) const { return d_norms + static_cast<size_t>(l) * 2304; }
+    float* d_post_norm(int l) const { return d_norms + static_cast<size_t>(l) * 2304 + 1024; }
+    float* d_qn(int l) const { return d_norms + static_cast<size_t>(l) * 2304 + 2048; }
+    float* d_kn(int l) const { return d_norms + static_cast<size_t>(l) * 2304 + 2176; }
+    float* d_hidden_norm() const { return d_norms + static_cast<size_t>(d_layers) * 2304; }
+    float* d_final_norm() const { return d_norms + static_cast<size_t>(d_layers) * 2304 + 1024; }
+    void* d_kc_layer(int l) const
+    {
+        return static_cast<char*>(d_kc) + static_cast<size_t>(l) * kNumKVHeads * cfg.max_context * kHeadDim * kv_elem();
+    }
+    void* d_vc_layer(int l) const
+    {
+        return static_cast<char*>(d_vc) + static_cast<size_t>(l) * kNumKVHeads * cfg.max_context * kHeadDim * kv_elem();
     }
 };
 
@@ -250,11 +292,13 @@ cudaError_t run_attn(hy_ctx* c, const AttnArgs& a, int splits)
 // Attention of a step of 2..16 rows (DFlash verify, decoder steps): RoPE + QK
 // norm + KV append of the rows, then the tensor-core attention over the keys
 // [0, past + rows) in kVerifyChunks chunks per KV head, then the chunk merge.
+// The DFlash draft (draft = true) normalises q / k before RoPE and attends
+// without a mask.
 template <typename KT>
-cudaError_t run_attn16(hy_ctx* c, const AttnArgs& at)
+cudaError_t run_attn16(hy_ctx* c, const AttnArgs& at, bool draft = false)
 {
     PrefillRopeArgs ra{const_cast<float*>(at.qkv), at.ldq, at.cos, at.sin, at.qn_w, at.kn_w, at.kc, at.vc, at.cap,
-                       at.past_fixed, at.eps, at.scale_log2, at.st, at.rope_state, c->err};
+                       at.past_fixed, at.eps, at.scale_log2, at.st, at.rope_state, c->err, draft ? 1 : 0, 0};
     cudaError_t e = launch_pdl(prefill_rope_kernel<KT>, dim3(at.rows, 4), dim3(256), 0, c->stream, ra);
     if (e != cudaSuccess) return e;
     static_assert(kVerifyChunks <= kMaxVerifyChunks, "chunk merge capacity");
@@ -279,6 +323,7 @@ cudaError_t run_attn16(hy_ctx* c, const AttnArgs& at)
     pa.part = c->va_part;
     pa.st = at.st;
     pa.err = c->err;
+    pa.noncausal = draft ? 1 : 0;
     if ((e = launch_pdl(k, dim3(kVerifyChunks, kNumKVHeads), dim3(S::THREADS), S::SMEM, c->stream, pa)) != cudaSuccess)
         return e;
     const ChunkMergeArgs ma{c->va_part, kVerifyChunks, at.rows, at.out};
@@ -300,7 +345,8 @@ struct StepPlan {
     bool past_from_state;
     int past_fixed;
     int lm_mode;       // -1: no LM head; else LM_* with PRO_NORM on x
-    float** aux;       // optional [4] aux outputs (row stride 1024), nullable
+    float** aux;       // optional [4] aux outputs, nullable
+    int ld_aux;        // their row stride (0: 1024)
 };
 
 GemvArgs base_args(hy_ctx* c)
@@ -318,6 +364,9 @@ GemvArgs base_args(hy_ctx* c)
     a.tmap = c->lm_tmap;
     return a;
 }
+
+template <typename WT, int MT>
+cudaError_t enqueue_step_lm_t(hy_ctx* c, const StepPlan& p);
 
 template <typename WT, typename KT, int MT>
 cudaError_t enqueue_step_t(hy_ctx* c, const StepPlan& p)
@@ -427,7 +476,7 @@ cudaError_t enqueue_step_t(hy_ctx* c, const StepPlan& p)
             d.out = c->x;
             d.ldo = kHidden;
             d.aux = aux;
-            d.ld_aux = kHidden;
+            d.ld_aux = p.ld_aux ? p.ld_aux : kHidden;
             if ((e = run_gemv<WT, kFfn, MT, PRO_SWIGLU, EPI_RESID>(c, d)) != cudaSuccess) return e;
         }
         else
@@ -447,11 +496,20 @@ cudaError_t enqueue_step_t(hy_ctx* c, const StepPlan& p)
             d2.ldo = kHidden;
             d2.extra = c->tmp;
             d2.aux = aux;
-            d2.ld_aux = kHidden;
+            d2.ld_aux = p.ld_aux ? p.ld_aux : kHidden;
             if ((e = run_gemv<WT, kFfn / 2, MT, PRO_PLAIN, EPI_RESID>(c, d2)) != cudaSuccess) return e;
         }
     }
-    if (p.lm_mode >= 0)
+    if (p.lm_mode >= 0) return enqueue_step_lm_t<WT, MT>(c, p);
+    return cudaSuccess;
+}
+
+// Final norm + LM head + selection (and the AR / verify commit) of a step's rows in ctx->x.
+template <typename WT, int MT>
+cudaError_t enqueue_step_lm_t(hy_ctx* c, const StepPlan& p)
+{
+    const hy_config& cfg = c->cfg;
+    cudaError_t e = cudaSuccess;
     {
         GemvArgs lm = base_args(c);
         lm.W = c->embed;
@@ -1079,6 +1137,9 @@ void free_ctx(hy_ctx* c)
     if (c->g_ar) cudaGraphExecDestroy(c->g_ar);
     if (c->g_verify_draft) cudaGraphExecDestroy(c->g_verify_draft);
     if (c->g_verify_ids) cudaGraphExecDestroy(c->g_verify_ids);
+    if (c->g_dflash) cudaGraphExecDestroy(c->g_dflash);
+    if (c->g_verify_ids_ctx) cudaGraphExecDestroy(c->g_verify_ids_ctx);
+    for (void* p : c->d_allocs) cudaFree(p);
     for (void* p : c->allocs) cudaFree(p);
     if (c->logits) cudaFree(c->logits);
     if (c->h_st) cudaFreeHost(c->h_st);
@@ -1165,7 +1226,7 @@ int set_device(hy_ctx* c)
 
 // One step outside a graph (prefill chunks, hy_decoder_step): rows of ctx->x at
 // explicit positions past..past+rows-1 with explicit rope rows.
-int run_direct_step(hy_ctx* c, int rows, int past, const float* cos, const float* sin, float** aux)
+int run_direct_step(hy_ctx* c, int rows, int past, const float* cos, const float* sin, float** aux, int ld_aux = 0)
 {
     StepPlan p{};
     p.rows = rows;
@@ -1177,6 +1238,7 @@ int run_direct_step(hy_ctx* c, int rows, int past, const float* cos, const float
     p.past_fixed = past;
     p.lm_mode = -1;
     p.aux = aux;
+    p.ld_aux = ld_aux;
     t_next_plain = true;   // the rows were just copied into ctx->x
     cudaError_t e = enqueue_step(c, p);
     if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("decoder step launch: ") + cudaGetErrorString(e));
@@ -1294,6 +1356,8 @@ cudaError_t plan_prefill_attn(hy_ctx* c, int past, int rows)
 // causal attention of the pass's rows over the cache, then o_proj (residual
 // add), RMSNorm, gate/up with SwiGLU (written split and tiled) and down_proj
 // (residual add). Leaves the final-normed last row in ctx->hidden.
+cudaError_t enqueue_draft_context_rows(hy_ctx* c, int rows, int past);
+
 template <typename KT>
 cudaError_t enqueue_prefill_t(hy_ctx* c, int seq)
 {
@@ -1338,7 +1402,15 @@ cudaError_t enqueue_prefill_t(hy_ctx* c, int seq)
             d.C = xr;
             d.ldc = kHidden;
             if ((e = run_prefill_gemm<UG_RESID>(c, d)) != cudaSuccess) return e;
+            // With a DFlash draft: this layer's output rows as draft context input.
+            for (int i = 0; i < kAuxLayers && c->d_layers > 0; ++i)
+                if (kAuxLayerIds[i] == l &&
+                    (e = cudaMemcpy2DAsync(c->d_pf_aux + i * kHidden, sizeof(float) * kAuxLayers * kHidden, xr,
+                                           sizeof(float) * kHidden, sizeof(float) * kHidden, rows,
+                                           cudaMemcpyDeviceToDevice, c->stream)) != cudaSuccess)
+                    return e;
         }
+        if (c->d_layers > 0 && (e = enqueue_draft_context_rows(c, rows, p0)) != cudaSuccess) return e;
         if (p0 + rows == seq)
         {
             rmsnorm_rows_kernel<<<1, 256, 0, c->stream>>>(xr + static_cast<size_t>(rows - 1) * kHidden, c->final_norm(),
@@ -1364,6 +1436,551 @@ int set_length(hy_ctx* c, int rows)
     c->kv_len = rows;
     HY_CUDA(cudaMemcpyAsync(&c->st->kv_len, &c->h_st->kv_len, sizeof(int), cudaMemcpyHostToDevice, c->stream));
     HY_CUDA(cudaStreamSynchronize(c->stream));
+    return HY_OK;
+}
+
+// ---------------------------------------------------------------------------
+// DFlash draft network: the graph of export/dflash_export.py:88-177, run by
+// DFlashDraftRuntime::run (src/dflash_runtime.cpp:213-290) from
+// run_dflash_block (src/text_runtime.cpp:880-950).
+//
+// The reference hands the draft graph the aux hidden states of every context
+// row on every block, and the graph recomputes fc / hidden_norm / k_proj /
+// v_proj over all of them. A context row's draft keys and values depend only
+// on that row and its position, so here they are computed once, when the row
+// joins the sequence, and kept in a draft K/V cache beside the decoder's:
+//   context rows: th = hidden_norm(fc(aux_1 | aux_8 | aux_15 | aux_22)); per
+//     draft layer k = rope(k_norm(k_proj(th))), v = v_proj(th) at the row's
+//     position (RoPE theta 10000, build_dflash_rope, src/dflash_runtime.cpp:27-48);
+//   noise block (16 rows at positions len .. len + 15): per draft layer q / k /
+//     v of RMSNorm(h), q_norm / k_norm then RoPE, the rows' k / v written after
+//     the context, attention over keys [0, len + 16) with no mask and scale
+//     1/sqrt(128), o_proj + residual, SwiGLU MLP + residual; final norm;
+//   drafts: argmax of the tied LM head over rows 1 .. 15 (penalty 1, no history).
+// A prompt's context rows go through the tcgen05 GEMMs (split, tiled operands);
+// a step's (<= 16 rows, e.g. a verify block) through the 16-row projections.
+// ---------------------------------------------------------------------------
+constexpr unsigned long long kTidDraftFc = 19990, kTidDraftHiddenNorm = 19991, kTidDraftNorm = 19992;
+constexpr unsigned long long kDraftTidBase = 20000, kDraftTidStride = 16;
+constexpr int kMaxDraftLayers = 8;
+constexpr int kAuxWidth = kAuxLayers * kHidden;   // 4096: the fc input row
+const float kDraftScaleLog2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(kHeadDim)));
+
+bool draft_ready(const hy_ctx* c) { return c->d_layers > 0; }
+
+// Context rows of a step: aux rows [rows x 4096] at `aux` (rows <= 16), KV
+// positions past .. past + rows - 1 (past = st->kv_len when from_state).
+template <typename WT, typename KT>
+cudaError_t enqueue_draft_context16_t(hy_ctx* c, const float* aux, int rows, bool from_state, int past)
+{
+    cudaError_t e = cudaSuccess;
+    // fc over the two column halves (the 16 activation rows of 2048 columns fit in
+    // shared memory): tmp = aux[:, :2048] fc[:, :2048]^T, then tmp += aux[:, 2048:] fc[:, 2048:]^T.
+    GemvArgs f = base_args(c);
+    f.W = c->d_fc;
+    f.N = kHidden;
+    f.ldw = kAuxWidth;
+    f.rows = rows;
+    f.src = SRC_X;
+    f.x = aux;
+    f.ldx = kAuxWidth;
+    f.out = c->tmp;
+    f.ldo = kHidden;
+    f.k_off = 0;
+    if ((e = run_gemv<WT, kAuxWidth / 2, 16, PRO_PLAIN, EPI_STORE>(c, f)) != cudaSuccess) return e;
+    f.k_off = kAuxWidth / 2;
+    if ((e = run_gemv<WT, kAuxWidth / 2, 16, PRO_PLAIN, EPI_RESID>(c, f)) != cudaSuccess) return e;
+    for (int l = 0; l < c->d_layers; ++l)
+    {
+        // k | v = hidden_norm(tmp) [k_proj; v_proj]^T into columns 2048.. of the qkv rows.
+        GemvArgs kv = base_args(c);
+        kv.W = static_cast<const WT*>(c->d_wqkv[l]) + static_cast<size_t>(kQWidth) * kHidden;
+        kv.N = 2 * kKVWidth;
+        kv.ldw = kHidden;
+        kv.rows = rows;
+        kv.src = SRC_X;
+        kv.x = c->tmp;
+        kv.ldx = kHidden;
+        kv.norm_w = c->d_hidden_norm();
+        kv.out = c->qkv + kQWidth;
+        kv.ldo = kQKVRows;
+        if ((e = run_gemv<WT, kHidden, 16, PRO_NORM, EPI_STORE>(c, kv)) != cudaSuccess) return e;
+        PrefillRopeArgs ra{c->qkv, kQKVRows, c->d_cos, c->d_sin, c->d_qn(l), c->d_kn(l), c->d_kc_layer(l),
+                           c->d_vc_layer(l), c->cfg.max_context, past, c->cfg.rms_norm_eps, kDraftScaleLog2,
+                           from_state ? c->st : nullptr, 1, c->err, 1, 1};
+        if ((e = launch_pdl(prefill_rope_kernel<KT>, dim3(rows, 2), dim3(256), 0, c->stream, ra)) != cudaSuccess)
+            return e;
+    }
+    return cudaSuccess;
+}
+
+// The 16 noise rows through the draft layers. src: SRC_GATHER_BLOCK (embed
+// [st->cur_token, mask x 15], ids written to ctx->proposed) or SRC_X (rows
+// already in d_x). select: drafts into ctx->proposed[1..15]; else the
+// final-normed rows into ctx->hidden.
+template <typename WT, typename KT>
+cudaError_t enqueue_draft_forward_t(hy_ctx* c, int src, bool from_state, int past, bool select)
+{
+    const hy_config& cfg = c->cfg;
+    const int ffn = cfg.ffn_dim;
+    cudaError_t e = cudaSuccess;
+    for (int l = 0; l < c->d_layers; ++l)
+    {
+        GemvArgs q = base_args(c);
+        q.W = c->d_wqkv[l];
+        q.N = kQKVRows;
+        q.ldw = kHidden;
+        q.rows = kBlock;
+        q.src = (l == 0) ? src : SRC_X;
+        q.mask_token = c->d_mask;
+        q.ids_out = (l == 0 && src == SRC_GATHER_BLOCK) ? c->proposed : nullptr;
+        q.x_store = c->d_x;
+        q.x = c->d_x;
+        q.ldx = kHidden;
+        q.norm_w = c->d_in_norm(l);
+        q.out = c->qkv;
+        q.ldo = kQKVRows;
+        if ((e = run_gemv<WT, kHidden, 16, PRO_NORM, EPI_STORE>(c, q)) != cudaSuccess) return e;
+
+        AttnArgs at;
+        std::memset(&at, 0, sizeof(at));
+        at.qkv = c->qkv;
+        at.ldq = kQKVRows;
+        at.qn_w = c->d_qn(l);
+        at.kn_w = c->d_kn(l);
+        at.cos = c->d_cos;
+        at.sin = c->d_sin;
+        at.rope_state = 1;
+        at.kc = c->d_kc_layer(l);
+        at.vc = c->d_vc_layer(l);
+        at.cap = cfg.max_context;
+        at.st = from_state ? c->st : nullptr;
+        at.past_fixed = past;
+        at.rows = kBlock;
+        at.scale_log2 = kDraftScaleLog2;
+        at.eps = cfg.rms_norm_eps;
+        at.out = c->attn;
+        at.err = c->err;
+        if ((e = run_attn16<KT>(c, at, true)) != cudaSuccess) return e;
+
+        GemvArgs o = base_args(c);
+        o.W = c->d_wo[l];
+        o.N = kHidden;
+        o.ldw = kQWidth;
+        o.rows = kBlock;
+        o.src = SRC_X;
+        o.x = c->attn;
+        o.ldx = kQWidth;
+        o.out = c->d_x;
+        o.ldo = kHidden;
+        if ((e = run_gemv<WT, kQWidth, 16, PRO_PLAIN, EPI_RESID>(c, o)) != cudaSuccess) return e;
+
+        GemvArgs gu = base_args(c);
+        gu.W = c->d_wgu[l];
+        gu.N = 2 * ffn;
+        gu.ldw = kHidden;
+        gu.rows = kBlock;
+        gu.src = SRC_X;
+        gu.x = c->d_x;
+        gu.ldx = kHidden;
+        gu.norm_w = c->d_post_norm(l);
+        gu.out = c->act;
+        gu.ldo = ffn;
+        if ((e = run_gemv<WT, kHidden, 16, PRO_NORM, EPI_ACT>(c, gu)) != cudaSuccess) return e;
+
+        GemvArgs d = base_args(c);
+        d.W = c->d_wd[l];
+        d.N = kHidden;
+        d.ldw = ffn;
+        d.rows = kBlock;
+        d.src = SRC_X;
+        d.x = c->act;
+        d.ldx = ffn;
+        GemvArgs d1 = d;
+        d1.k_off = 0;
+        d1.out = c->tmp;
+        d1.ldo = kHidden;
+        if ((e = run_gemv<WT, kFfn / 2, 16, PRO_PLAIN, EPI_STORE>(c, d1)) != cudaSuccess) return e;
+        GemvArgs d2 = d;
+        d2.k_off = kFfn / 2;
+        d2.out = c->d_x;
+        d2.ldo = kHidden;
+        d2.extra = c->tmp;
+        if ((e = run_gemv<WT, kFfn / 2, 16, PRO_PLAIN, EPI_RESID>(c, d2)) != cudaSuccess) return e;
+    }
+    if (!select)
+    {
+        rmsnorm_rows_kernel<<<kBlock, 256, 0, c->stream>>>(c->d_x, c->d_final_norm(), cfg.rms_norm_eps, c->hidden,
+                                                          kHidden);
+        t_next_plain = true;
+        return cudaGetLastError();
+    }
+    // Drafts: final norm + tied LM head + argmax of rows 1..15 (run_dflash_block,
+    // src/text_runtime.cpp:951-978: penalty 1, so the history bits change nothing).
+    GemvArgs lm = base_args(c);
+    lm.W = c->embed;
+    lm.N = cfg.vocab_size;
+    lm.ldw = kHidden;
+    lm.rows = kBlock - 1;
+    lm.src = SRC_X;
+    lm.x = c->d_x + kHidden;
+    lm.ldx = kHidden;
+    lm.norm_w = c->d_final_norm();
+    lm.lm_mode = LM_NONE;
+    lm.penalty = 1.0f;
+    lm.tok_out = c->proposed + 1;
+    lm.raw_out = c->raw_out;
+    return run_gemv<WT, kHidden, 16, PRO_NORM, EPI_ARGMAX>(c, lm);
+}
+
+// Context rows of a prefill pass: aux rows [rows x 4096] in d_pf_aux (rows <=
+// pf_rows) at KV positions past .., through the tcgen05 GEMMs.
+template <typename KT>
+cudaError_t enqueue_draft_context_rows_t(hy_ctx* c, int rows, int past)
+{
+    const hy_config& cfg = c->cfg;
+    const int pad = (rows + kUmBM - 1) / kUmBM * kUmBM;
+    cudaError_t e = cudaSuccess;
+    split_tiled_kernel<<<rows, 256, 0, c->stream>>>(c->d_pf_aux, kAuxWidth, pad, c->d_pf_a_hi, c->d_pf_a_lo);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    UmmaGemmArgs f = gemm_args(c->d_pf_a_hi, c->d_pf_a_lo, pad, c->d_tfc_hi, c->d_tfc_lo, rows, kHidden, kAuxWidth);
+    f.C = c->d_pf_fc;
+    f.ldc = kHidden;
+    if ((e = run_prefill_gemm<UG_STORE>(c, f)) != cudaSuccess) return e;
+    rmsnorm_tiled_kernel<<<rows, 256, 0, c->stream>>>(c->d_pf_fc, c->d_hidden_norm(), cfg.rms_norm_eps, pad, c->pf_a_hi,
+                                                       c->pf_a_lo);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    for (int l = 0; l < c->d_layers; ++l)
+    {
+        UmmaGemmArgs kv = gemm_args(c->pf_a_hi, c->pf_a_lo, pad, c->d_tkv_hi[l], c->d_tkv_lo[l], rows, 2 * kKVWidth,
+                                    kHidden);
+        kv.C = c->pf_qkv + kQWidth;
+        kv.ldc = kQKVRows;
+        if ((e = run_prefill_gemm<UG_STORE>(c, kv)) != cudaSuccess) return e;
+        PrefillRopeArgs ra{c->pf_qkv, kQKVRows, c->d_cos, c->d_sin, c->d_qn(l), c->d_kn(l), c->d_kc_layer(l),
+                           c->d_vc_layer(l), cfg.max_context, past, cfg.rms_norm_eps, kDraftScaleLog2, nullptr, 1,
+                           c->err, 1, 1};
+        prefill_rope_kernel<KT><<<dim3(rows, 2), 256, 0, c->stream>>>(ra);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    t_next_plain = true;
+    return cudaSuccess;
+}
+
+cudaError_t enqueue_draft_context_rows(hy_ctx* c, int rows, int past)
+{
+    return (c->cfg.kv_dtype == HY_DTYPE_BF16) ? enqueue_draft_context_rows_t<__nv_bfloat16>(c, rows, past)
+                                              : enqueue_draft_context_rows_t<float>(c, rows, past);
+}
+
+cudaError_t enqueue_draft_context16(hy_ctx* c, const float* aux, int rows, bool from_state, int past)
+{
+    const bool wb = c->cfg.weight_dtype == HY_DTYPE_BF16, kb = c->cfg.kv_dtype == HY_DTYPE_BF16;
+    if (!wb && !kb) return enqueue_draft_context16_t<float, float>(c, aux, rows, from_state, past);
+    if (!wb && kb) return enqueue_draft_context16_t<float, __nv_bfloat16>(c, aux, rows, from_state, past);
+    if (wb && !kb) return enqueue_draft_context16_t<__nv_bfloat16, float>(c, aux, rows, from_state, past);
+    return enqueue_draft_context16_t<__nv_bfloat16, __nv_bfloat16>(c, aux, rows, from_state, past);
+}
+
+cudaError_t enqueue_draft_forward(hy_ctx* c, int src, bool from_state, int past, bool select)
+{
+    const bool wb = c->cfg.weight_dtype == HY_DTYPE_BF16, kb = c->cfg.kv_dtype == HY_DTYPE_BF16;
+    if (!wb && !kb) return enqueue_draft_forward_t<float, float>(c, src, from_state, past, select);
+    if (!wb && kb) return enqueue_draft_forward_t<float, __nv_bfloat16>(c, src, from_state, past, select);
+    if (wb && !kb) return enqueue_draft_forward_t<__nv_bfloat16, float>(c, src, from_state, past, select);
+    return enqueue_draft_forward_t<__nv_bfloat16, __nv_bfloat16>(c, src, from_state, past, select);
+}
+
+// One verify block at the state's length whose draft context rows are
+// appended before the commit (the commit moves the length; the block's rows
+// past the committed ones are rewritten by the next block before any read).
+// With `draft`, the block's ids come from the draft network first.
+cudaError_t enqueue_verify_with_context(hy_ctx* c, bool draft)
+{
+    cudaError_t e = cudaSuccess;
+    if (draft && (e = enqueue_draft_forward(c, SRC_GATHER_BLOCK, true, 0, true)) != cudaSuccess) return e;
+    float* aux[kAuxLayers];
+    for (int i = 0; i < kAuxLayers; ++i) aux[i] = c->d_aux + i * kHidden;
+    StepPlan p{};
+    p.rows = kBlock;
+    p.source.src = SRC_GATHER_IDS;
+    p.source.ids = c->proposed;
+    p.cos = c->rope_cos;
+    p.sin = c->rope_sin;
+    p.rope_state = 1;
+    p.past_from_state = true;
+    p.lm_mode = -1;
+    p.aux = aux;
+    p.ld_aux = kAuxWidth;
+    if ((e = enqueue_step(c, p)) != cudaSuccess) return e;
+    if ((e = enqueue_draft_context16(c, c->d_aux, kBlock, true, 0)) != cudaSuccess) return e;
+    p.lm_mode = LM_VERIFY;
+    return (c->cfg.weight_dtype == HY_DTYPE_BF16) ? enqueue_step_lm_t<__nv_bfloat16, 16>(c, p)
+                                                  : enqueue_step_lm_t<float, 16>(c, p);
+}
+
+int capture_fn(hy_ctx* c, cudaGraphExec_t* out, bool draft)
+{
+    cudaGraph_t graph = nullptr;
+    HY_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    const cudaError_t e = enqueue_verify_with_context(c, draft);
+    const cudaError_t e2 = cudaStreamEndCapture(c->stream, &graph);
+    if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+    if (e2 != cudaSuccess) return fail(HY_ERR_CUDA, std::string("graph capture end: ") + cudaGetErrorString(e2));
+    const cudaError_t e3 = cudaGraphInstantiate(out, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e3 != cudaSuccess) return fail(HY_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e3));
+    return HY_OK;
+}
+
+void draft_free(hy_ctx* c)
+{
+    if (c->g_dflash) cudaGraphExecDestroy(c->g_dflash);
+    if (c->g_verify_ids_ctx) cudaGraphExecDestroy(c->g_verify_ids_ctx);
+    c->g_dflash = c->g_verify_ids_ctx = nullptr;
+    for (void* p : c->d_allocs) cudaFree(p);
+    c->d_allocs.clear();
+    c->d_wqkv.clear();
+    c->d_wo.clear();
+    c->d_wgu.clear();
+    c->d_wd.clear();
+    c->d_tkv_hi.clear();
+    c->d_tkv_lo.clear();
+    c->d_layers = 0;
+    c->d_len = 0;
+    c->device_bytes -= c->d_bytes;
+    c->d_bytes = 0;
+}
+
+template <typename T>
+int draft_dalloc(hy_ctx* c, T** p, size_t count)
+{
+    void* v = nullptr;
+    const size_t bytes = align_up(std::max<size_t>(count * sizeof(T), 16), 256);
+    cudaError_t e = cudaMalloc(&v, bytes);
+    if (e != cudaSuccess)
+        return fail(HY_ERR_OUT_OF_MEMORY, "cudaMalloc(" + std::to_string(bytes) + " bytes) failed: " + cudaGetErrorString(e));
+    c->d_allocs.push_back(v);
+    c->d_bytes += bytes;
+    c->device_bytes += bytes;
+    *p = static_cast<T*>(v);
+    return HY_OK;
+}
+
+// Device memory of a draft of `layers` layers: weights (the context's weight
+// dtype), norms, the tiled fc / k|v operands, the draft K/V cache, the RoPE
+// table (filled here) and the step and prefill-pass buffers.
+int draft_alloc(hy_ctx* c, int layers, int mask_token)
+{
+    const hy_config& cfg = c->cfg;
+    if (layers < 1 || layers > kMaxDraftLayers)
+        return fail(HY_ERR_INVALID_ARGUMENT, "draft num_layers must be in 1.." + std::to_string(kMaxDraftLayers));
+    if (mask_token < 0 || mask_token >= cfg.vocab_size) return fail(HY_ERR_INVALID_ARGUMENT, "draft mask_token out of range");
+    draft_free(c);
+    const size_t we = c->w_elem();
+    const int ffn = cfg.ffn_dim;
+    int rc;
+    unsigned char* w = nullptr;
+    const size_t sz[4] = {align_up(static_cast<size_t>(kQKVRows) * kHidden * we, 256),
+                          align_up(static_cast<size_t>(kHidden) * kQWidth * we, 256),
+                          align_up(static_cast<size_t>(2 * ffn) * kHidden * we, 256),
+                          align_up(static_cast<size_t>(kHidden) * ffn * we, 256)};
+    const size_t fc_bytes = align_up(static_cast<size_t>(kHidden) * kAuxWidth * we, 256);
+    if ((rc = draft_dalloc(c, &w, fc_bytes + (sz[0] + sz[1] + sz[2] + sz[3]) * layers))) return rc;
+    c->d_fc = w;
+    w += fc_bytes;
+    for (int l = 0; l < layers; ++l)
+    {
+        c->d_wqkv.push_back(w);
+        c->d_wo.push_back(w += sz[0]);
+        c->d_wgu.push_back(w += sz[1]);
+        c->d_wd.push_back(w += sz[2]);
+        w += sz[3];
+    }
+    c->d_layers = layers;
+    c->d_mask = mask_token;
+    if ((rc = draft_dalloc(c, &c->d_norms, static_cast<size_t>(layers) * 2304 + 2 * kHidden))) return rc;
+    const int planes = (cfg.weight_dtype == HY_DTYPE_BF16) ? 1 : 2;
+    float* tw = nullptr;
+    const size_t tfc = static_cast<size_t>(kHidden) * kAuxWidth, tkv = static_cast<size_t>(2 * kKVWidth) * kHidden;
+    if ((rc = draft_dalloc(c, &tw, (tfc + tkv * layers) * planes))) return rc;
+    c->d_tfc_hi = tw;
+    c->d_tfc_lo = (planes == 2) ? tw + tfc : nullptr;
+    for (int l = 0; l < layers; ++l)
+    {
+        float* p = tw + tfc * planes + tkv * planes * l;
+        c->d_tkv_hi.push_back(p);
+        c->d_tkv_lo.push_back(planes == 2 ? p + tkv : nullptr);
+    }
+    const size_t kv_count = static_cast<size_t>(layers) * kNumKVHeads * cfg.max_context * kHeadDim;
+    unsigned char* kvb = nullptr;
+    if ((rc = draft_dalloc(c, &kvb, kv_count * c->kv_elem()))) return rc;
+    c->d_kc = kvb;
+    if ((rc = draft_dalloc(c, &kvb, kv_count * c->kv_elem()))) return rc;
+    c->d_vc = kvb;
+    HY_CUDA(cudaMemsetAsync(c->d_kc, 0, kv_count * c->kv_elem(), c->stream));
+    HY_CUDA(cudaMemsetAsync(c->d_vc, 0, kv_count * c->kv_elem(), c->stream));
+    const size_t rows = static_cast<size_t>(cfg.max_context);
+    if ((rc = draft_dalloc(c, &c->d_cos, rows * kHeadDim))) return rc;
+    if ((rc = draft_dalloc(c, &c->d_sin, rows * kHeadDim))) return rc;
+    if ((rc = draft_dalloc(c, &c->d_x, static_cast<size_t>(kBlock) * kHidden))) return rc;
+    if ((rc = draft_dalloc(c, &c->d_aux, static_cast<size_t>(kBlock) * kAuxWidth))) return rc;
+    if ((rc = draft_dalloc(c, &c->d_pf_aux, static_cast<size_t>(c->pf_rows) * kAuxWidth))) return rc;
+    if ((rc = draft_dalloc(c, &c->d_pf_a_hi, static_cast<size_t>(c->pf_pad) * kAuxWidth))) return rc;
+    if ((rc = draft_dalloc(c, &c->d_pf_a_lo, static_cast<size_t>(c->pf_pad) * kAuxWidth))) return rc;
+    if ((rc = draft_dalloc(c, &c->d_pf_fc, static_cast<size_t>(c->pf_rows) * kHidden))) return rc;
+    // build_dflash_rope (src/dflash_runtime.cpp:27-48) in the reference's float arithmetic.
+    std::vector<float> cs(rows * kHeadDim), sn(rows * kHeadDim);
+    for (size_t pos = 0; pos < rows; ++pos)
+        for (int d = 0; d < kHeadDim; ++d)
+        {
+            const float exponent = static_cast<float>(2 * (d % (kHeadDim / 2))) / kHeadDim;
+            const float angle = static_cast<float>(static_cast<int>(pos)) / std::pow(10000.0f, exponent);
+            cs[pos * kHeadDim + d] = std::cos(angle);
+            sn[pos * kHeadDim + d] = std::sin(angle);
+        }
+    HY_CUDA(cudaMemcpy(c->d_cos, cs.data(), cs.size() * sizeof(float), cudaMemcpyHostToDevice));
+    HY_CUDA(cudaMemcpy(c->d_sin, sn.data(), sn.size() * sizeof(float), cudaMemcpyHostToDevice));
+    return HY_OK;
+}
+
+// After the draft weights are in place: tiled operands and the two graphs.
+template <typename WT>
+int draft_finish_t(hy_ctx* c)
+{
+    {
+        const size_t n = static_cast<size_t>(kHidden) * (kAuxWidth / 4);
+        tile_weight_kernel<WT><<<static_cast<unsigned>((n + 255) / 256), 256, 0, c->stream>>>(
+            static_cast<const WT*>(c->d_fc), kHidden, kAuxWidth, c->d_tfc_hi, c->d_tfc_lo);
+        HY_CUDA(cudaGetLastError());
+    }
+    for (int l = 0; l < c->d_layers; ++l)
+    {
+        const size_t n = static_cast<size_t>(2 * kKVWidth) * (kHidden / 4);
+        tile_weight_kernel<WT><<<static_cast<unsigned>((n + 255) / 256), 256, 0, c->stream>>>(
+            static_cast<const WT*>(c->d_wqkv[l]) + static_cast<size_t>(kQWidth) * kHidden, 2 * kKVWidth, kHidden,
+            c->d_tkv_hi[l], c->d_tkv_lo[l]);
+        HY_CUDA(cudaGetLastError());
+    }
+    HY_CUDA(cudaStreamSynchronize(c->stream));
+    int rc = capture_fn(c, &c->g_dflash, true);
+    if (!rc) rc = capture_fn(c, &c->g_verify_ids_ctx, false);
+    if (!rc) c->d_len = 0;
+    return rc;
+}
+
+int draft_finish(hy_ctx* c)
+{
+    const int rc = (c->cfg.weight_dtype == HY_DTYPE_BF16) ? draft_finish_t<__nv_bfloat16>(c) : draft_finish_t<float>(c);
+    if (rc) draft_free(c);
+    return rc;
+}
+
+// Seeded synthetic draft weights on the library's counter generator (tensor
+// ids from kDraftTidBase; linears ~N(0, std), norms 1 + ~N(0, norm_std)).
+int draft_fill_synthetic(hy_ctx* c, unsigned long long seed, float std_dev, float norm_std)
+{
+    const hy_config& cfg = c->cfg;
+    const int ffn = cfg.ffn_dim;
+    const bool bf = cfg.weight_dtype == HY_DTYPE_BF16;
+    auto lin = [&](void* dst, size_t off_elems, unsigned long long tid, size_t count) {
+        if (bf)
+            launch_synth(static_cast<__nv_bfloat16*>(dst) + off_elems, count, seed, tid, std_dev, 0.f, c->stream);
+        else
+            launch_synth(static_cast<float*>(dst) + off_elems, count, seed, tid, std_dev, 0.f, c->stream);
+    };
+    auto lin_rows = [&](void* dst, unsigned long long tid, int rows, int cols, int row_mult, int row_off) {
+        const unsigned long long base = synth_base(seed, tid);
+        const float mult = host_synth_mult(std_dev);
+        if (bf)
+            synth_fill_rows_kernel<__nv_bfloat16><<<1184, 256, 0, c->stream>>>(static_cast<__nv_bfloat16*>(dst), rows,
+                                                                               cols, row_mult, row_off, base, mult);
+        else
+            synth_fill_rows_kernel<float><<<1184, 256, 0, c->stream>>>(static_cast<float*>(dst), rows, cols, row_mult,
+                                                                       row_off, base, mult);
+    };
+    lin(c->d_fc, 0, kTidDraftFc, static_cast<size_t>(kHidden) * kAuxWidth);
+    launch_synth(c->d_hidden_norm(), kHidden, seed, kTidDraftHiddenNorm, norm_std, 1.0f, c->stream);
+    launch_synth(c->d_final_norm(), kHidden, seed, kTidDraftNorm, norm_std, 1.0f, c->stream);
+    for (int l = 0; l < c->d_layers; ++l)
+    {
+        const unsigned long long b = kDraftTidBase + kDraftTidStride * l;
+        launch_synth(c->d_in_norm(l), kHidden, seed, b + J_INPUT_NORM, norm_std, 1.0f, c->stream);
+        launch_synth(c->d_post_norm(l), kHidden, seed, b + J_POST_NORM, norm_std, 1.0f, c->stream);
+        launch_synth(c->d_qn(l), kHeadDim, seed, b + J_Q_NORM, norm_std, 1.0f, c->stream);
+        launch_synth(c->d_kn(l), kHeadDim, seed, b + J_K_NORM, norm_std, 1.0f, c->stream);
+        lin(c->d_wqkv[l], 0, b + J_Q, static_cast<size_t>(kQWidth) * kHidden);
+        lin(c->d_wqkv[l], static_cast<size_t>(kQWidth) * kHidden, b + J_K, static_cast<size_t>(kKVWidth) * kHidden);
+        lin(c->d_wqkv[l], static_cast<size_t>(kQWidth + kKVWidth) * kHidden, b + J_V,
+            static_cast<size_t>(kKVWidth) * kHidden);
+        lin(c->d_wo[l], 0, b + J_O, static_cast<size_t>(kHidden) * kQWidth);
+        lin_rows(c->d_wgu[l], b + J_GATE, ffn, kHidden, 2, 0);
+        lin_rows(c->d_wgu[l], b + J_UP, ffn, kHidden, 2, 1);
+        lin(c->d_wd[l], 0, b + J_DOWN, static_cast<size_t>(kHidden) * ffn);
+    }
+    HY_CUDA(cudaGetLastError());
+    HY_CUDA(cudaStreamSynchronize(c->stream));
+    return HY_OK;
+}
+
+// Host fp32 draft weights -> device (bf16 contexts convert on the device).
+int draft_upload(hy_ctx* c, const hy_draft_weights* w)
+{
+    const hy_config& cfg = c->cfg;
+    const int ffn = cfg.ffn_dim;
+    const bool bf = cfg.weight_dtype == HY_DTYPE_BF16;
+    float* staging = nullptr;
+    if (bf)
+    {
+        void* s = nullptr;
+        HY_CUDA(cudaMalloc(&s, static_cast<size_t>(std::max(kAuxWidth, 2 * ffn)) * kHidden * sizeof(float)));
+        staging = static_cast<float*>(s);
+    }
+    auto put = [&](void* dst, size_t off_elems, const float* src, size_t count) -> cudaError_t {
+        if (!bf)
+            return cudaMemcpy(static_cast<float*>(dst) + off_elems, src, count * sizeof(float), cudaMemcpyHostToDevice);
+        cudaError_t e = cudaMemcpy(staging, src, count * sizeof(float), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return e;
+        f32_to_bf16_kernel<<<1184, 256, 0, c->stream>>>(staging, static_cast<__nv_bfloat16*>(dst) + off_elems, count);
+        e = cudaGetLastError();
+        return e != cudaSuccess ? e : cudaStreamSynchronize(c->stream);
+    };
+    auto put_rows = [&](void* dst, const float* src, int rows, int off) -> cudaError_t {
+        if (!bf)
+            return cudaMemcpy2D(static_cast<float*>(dst) + static_cast<size_t>(off) * kHidden, 2 * kHidden * sizeof(float),
+                                src, kHidden * sizeof(float), kHidden * sizeof(float), rows, cudaMemcpyHostToDevice);
+        cudaError_t e = cudaMemcpy(staging, src, static_cast<size_t>(rows) * kHidden * sizeof(float), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return e;
+        f32_to_bf16_rows_kernel<<<1184, 256, 0, c->stream>>>(staging, static_cast<__nv_bfloat16*>(dst), rows, kHidden, 2, off);
+        e = cudaGetLastError();
+        return e != cudaSuccess ? e : cudaStreamSynchronize(c->stream);
+    };
+    auto vec = [&](float* dst, const float* src, size_t n) {
+        return cudaMemcpy(dst, src, n * sizeof(float), cudaMemcpyHostToDevice);
+    };
+    cudaError_t e = put(c->d_fc, 0, w->fc, static_cast<size_t>(kHidden) * kAuxWidth);
+    if (e == cudaSuccess) e = vec(c->d_hidden_norm(), w->hidden_norm, kHidden);
+    if (e == cudaSuccess) e = vec(c->d_final_norm(), w->norm, kHidden);
+    for (int l = 0; l < c->d_layers && e == cudaSuccess; ++l)
+    {
+        const hy_layer_weights& lw = w->layers[l];
+        e = put(c->d_wqkv[l], 0, lw.q_proj, static_cast<size_t>(kQWidth) * kHidden);
+        if (e == cudaSuccess)
+            e = put(c->d_wqkv[l], static_cast<size_t>(kQWidth) * kHidden, lw.k_proj, static_cast<size_t>(kKVWidth) * kHidden);
+        if (e == cudaSuccess)
+            e = put(c->d_wqkv[l], static_cast<size_t>(kQWidth + kKVWidth) * kHidden, lw.v_proj,
+                    static_cast<size_t>(kKVWidth) * kHidden);
+        if (e == cudaSuccess) e = put(c->d_wo[l], 0, lw.o_proj, static_cast<size_t>(kHidden) * kQWidth);
+        if (e == cudaSuccess) e = put_rows(c->d_wgu[l], lw.gate_proj, ffn, 0);
+        if (e == cudaSuccess) e = put_rows(c->d_wgu[l], lw.up_proj, ffn, 1);
+        if (e == cudaSuccess) e = put(c->d_wd[l], 0, lw.down_proj, static_cast<size_t>(kHidden) * ffn);
+        if (e == cudaSuccess) e = vec(c->d_in_norm(l), lw.input_norm, kHidden);
+        if (e == cudaSuccess) e = vec(c->d_post_norm(l), lw.post_norm, kHidden);
+        if (e == cudaSuccess) e = vec(c->d_qn(l), lw.query_norm, kHeadDim);
+        if (e == cudaSuccess) e = vec(c->d_kn(l), lw.key_norm, kHeadDim);
+    }
+    if (staging) cudaFree(staging);
+    if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("draft weight upload: ") + cudaGetErrorString(e));
     return HY_OK;
 }
 
@@ -1586,6 +2203,7 @@ int hy_seq_reset(hy_ctx* c)
     int rc = set_device(c);
     if (rc) return rc;
     HY_CUDA(cudaMemsetAsync(c->hist, 0, sizeof(unsigned) * ((c->cfg.vocab_size + 31) / 32), c->stream));
+    c->d_len = 0;
     return set_length(c, 0);
 }
 
@@ -1603,6 +2221,7 @@ int hy_seq_truncate(hy_ctx* c, int rows)
     if (rows <= 0 || rows > c->kv_len) return fail(HY_ERR_INVALID_ARGUMENT, "invalid DFlash row view");
     int rc = set_device(c);
     if (rc) return rc;
+    c->d_len = std::min(c->d_len, rows);
     return set_length(c, rows);
 }
 
@@ -1612,6 +2231,7 @@ int hy_seq_set_length(hy_ctx* c, int rows)
     if (rows < 0 || rows > c->cfg.max_context) return fail(HY_ERR_CAPACITY, "length exceeds the KV capacity");
     int rc = set_device(c);
     if (rc) return rc;
+    c->d_len = std::min(c->d_len, rows);
     return set_length(c, rows);
 }
 
@@ -1654,6 +2274,7 @@ int hy_prefill(hy_ctx* c, const float* embeds, const float* cos, const float* si
     if (last_hidden)
         HY_CUDA(cudaMemcpyAsync(last_hidden, c->hidden, sizeof(float) * kHidden, cudaMemcpyDeviceToHost, c->stream));
     if ((rc = check_device_error(c))) return rc;
+    if (draft_ready(c)) c->d_len = seq;
     return set_length(c, seq);
 }
 
@@ -1668,9 +2289,20 @@ int hy_decoder_step(hy_ctx* c, const float* embeds, int rows, const float* cos, 
     HY_CUDA(cudaMemcpyAsync(c->x, embeds, sizeof(float) * rows * kHidden, cudaMemcpyHostToDevice, c->stream));
     HY_CUDA(cudaMemcpyAsync(c->pre_cos, cos, sizeof(float) * rows * kHeadDim, cudaMemcpyHostToDevice, c->stream));
     HY_CUDA(cudaMemcpyAsync(c->pre_sin, sin, sizeof(float) * rows * kHeadDim, cudaMemcpyHostToDevice, c->stream));
+    // With a DFlash draft whose context covers the sequence, the rows' aux states
+    // also become draft context rows.
+    const bool ctx_rows = draft_ready(c) && c->d_len == c->kv_len;
     float* aux[kAuxLayers];
-    for (int i = 0; i < kAuxLayers; ++i) aux[i] = c->aux + static_cast<size_t>(i) * kMaxStepRows * kHidden;
-    if ((rc = run_direct_step(c, rows, c->kv_len, c->pre_cos, c->pre_sin, aux_hidden ? aux : nullptr))) return rc;
+    for (int i = 0; i < kAuxLayers; ++i)
+        aux[i] = ctx_rows ? c->d_aux + i * kHidden : c->aux + static_cast<size_t>(i) * kMaxStepRows * kHidden;
+    if ((rc = run_direct_step(c, rows, c->kv_len, c->pre_cos, c->pre_sin, (aux_hidden || ctx_rows) ? aux : nullptr,
+                              ctx_rows ? kAuxWidth : kHidden)))
+        return rc;
+    if (ctx_rows)
+    {
+        const cudaError_t e = enqueue_draft_context16(c, c->d_aux, rows, false, c->kv_len);
+        if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("draft context launch: ") + cudaGetErrorString(e));
+    }
     if (hidden)
     {
         rmsnorm_rows_kernel<<<rows, 256, 0, c->stream>>>(c->x, c->final_norm(), c->cfg.rms_norm_eps, c->hidden, kHidden);
@@ -1679,9 +2311,11 @@ int hy_decoder_step(hy_ctx* c, const float* embeds, int rows, const float* cos, 
     }
     if (aux_hidden)
         for (int i = 0; i < kAuxLayers; ++i)
-            HY_CUDA(cudaMemcpyAsync(aux_hidden + static_cast<size_t>(i) * rows * kHidden, aux[i],
-                                    sizeof(float) * rows * kHidden, cudaMemcpyDeviceToHost, c->stream));
+            HY_CUDA(cudaMemcpy2DAsync(aux_hidden + static_cast<size_t>(i) * rows * kHidden, sizeof(float) * kHidden, aux[i],
+                                      sizeof(float) * (ctx_rows ? kAuxWidth : kHidden), sizeof(float) * kHidden, rows,
+                                      cudaMemcpyDeviceToHost, c->stream));
     if ((rc = check_device_error(c))) return rc;
+    if (ctx_rows) c->d_len = c->kv_len + rows;
     return set_length(c, c->kv_len + rows);
 }
 
@@ -1817,9 +2451,13 @@ int hy_verify_block(hy_ctx* c, const int* proposed, int max_commit, float penalt
     h.block_count = 0;
     if ((rc = push_state(c))) return rc;
     HY_CUDA(cudaMemcpyAsync(c->proposed, proposed, sizeof(int) * kBlock, cudaMemcpyHostToDevice, c->stream));
-    HY_CUDA(cudaGraphLaunch(c->g_verify_ids, c->stream));
+    // With a DFlash draft whose context covers the sequence, the committed rows
+    // also become draft context rows (append_dflash_rows, src/dflash_runtime.cpp:121-166).
+    const bool ctx_rows = draft_ready(c) && c->d_len == c->kv_len;
+    HY_CUDA(cudaGraphLaunch(ctx_rows ? c->g_verify_ids_ctx : c->g_verify_ids, c->stream));
     if ((rc = check_device_error(c))) return rc;
     if ((rc = sync_state_to_host(c))) return rc;
+    if (ctx_rows) c->d_len = c->kv_len;
     if (posterior) HY_CUDA(cudaMemcpy(posterior, c->posterior, sizeof(int) * kBlock, cudaMemcpyDeviceToHost));
     if (acceptance_length) *acceptance_length = h.accept;
     if (committed) *committed = h.committed;
@@ -1872,20 +2510,21 @@ int hy_dflash_generate_synthetic(hy_ctx* c, int first_token, int max_tokens, flo
     return HY_OK;
 }
 
-int hy_run_vlm_decode_with_prompt(hy_ctx* c, const int* input_ids, const int* position_ids, int seq_len,
-                                  int image_token_id, const float* vision_features, int vision_token_count,
-                                  int max_tokens, float repetition_penalty, const int* eos_ids, int n_eos, int* tokens,
-                                  int* raw_top1, int* n_tokens)
+// The prompt half of run_vlm_decode_with_prompt (src/text_runtime.cpp:2053-2094,
+// 1307-1416): prompt embedding with vision-feature injection, mRoPE tables,
+// prefill (and the draft context when a draft is loaded), history = prompt ids,
+// and the first token from the last row's logits.
+static int prompt_prefill_first(hy_ctx* c, const int* input_ids, const int* position_ids, int seq_len,
+                                int image_token_id, const float* vision_features, int vision_token_count,
+                                float repetition_penalty, int* first, int* first_raw)
 {
     // prepare_prompt_embeddings checks (src/text_runtime.cpp:506-568).
-    if (!c || !input_ids || !position_ids || !n_tokens) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    if (!c || !input_ids || !position_ids) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
     if (seq_len <= 0) return fail(HY_ERR_INVALID_ARGUMENT, "prompt input_ids must not be empty");
     if (vision_token_count <= 0 || !vision_features) return fail(HY_ERR_INVALID_ARGUMENT, "vision feature size mismatch");
     if (!std::isfinite(repetition_penalty) || repetition_penalty <= 0.f)
         return fail(HY_ERR_INVALID_ARGUMENT, "repetition_penalty must be positive");
     if (seq_len > c->cfg.max_prefill) return fail(HY_ERR_CAPACITY, "prompt exceeds max_prefill");
-    if (max_tokens <= 0) max_tokens = 1024;   // src/text_runtime.cpp:1336-1341
-    if (max_tokens > c->cfg.max_tokens) return fail(HY_ERR_CAPACITY, "max_tokens exceeds config max_tokens");
     std::vector<int> feat_idx(seq_len, -1);
     int injected = 0;
     for (int t = 0; t < seq_len; ++t)
@@ -1923,12 +2562,194 @@ int hy_run_vlm_decode_with_prompt(hy_ctx* c, const int* input_ids, const int* po
     if ((rc = run_prefill(c, seq_len))) return rc;
     cudaError_t e = enqueue_lm_select(c, 1, c->hidden, repetition_penalty, false, nullptr);
     if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("LM head launch: ") + cudaGetErrorString(e));
-    int first = 0, first_raw = 0;
-    HY_CUDA(cudaMemcpyAsync(&first, c->tok_out, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
-    HY_CUDA(cudaMemcpyAsync(&first_raw, c->raw_out, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    HY_CUDA(cudaMemcpyAsync(first, c->tok_out, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    HY_CUDA(cudaMemcpyAsync(first_raw, c->raw_out, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
     if ((rc = check_device_error(c))) return rc;
     if ((rc = set_length(c, seq_len))) return rc;
+    if (c->d_layers > 0) c->d_len = seq_len;
+    return HY_OK;
+}
+
+int hy_run_vlm_decode_with_prompt(hy_ctx* c, const int* input_ids, const int* position_ids, int seq_len,
+                                  int image_token_id, const float* vision_features, int vision_token_count,
+                                  int max_tokens, float repetition_penalty, const int* eos_ids, int n_eos, int* tokens,
+                                  int* raw_top1, int* n_tokens)
+{
+    if (!c || !n_tokens) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    if (max_tokens <= 0) max_tokens = 1024;   // src/text_runtime.cpp:1336-1341
+    if (max_tokens > c->cfg.max_tokens) return fail(HY_ERR_CAPACITY, "max_tokens exceeds config max_tokens");
+    int first = 0, first_raw = 0;
+    int rc = prompt_prefill_first(c, input_ids, position_ids, seq_len, image_token_id, vision_features,
+                                  vision_token_count, repetition_penalty, &first, &first_raw);
+    if (rc) return rc;
     return hy_generate(c, first, first_raw, max_tokens, repetition_penalty, eos_ids, n_eos, tokens, raw_top1, n_tokens);
+}
+
+// ---- DFlash draft network --------------------------------------------------
+
+static int draft_loaded_finish(hy_ctx* c, int rc)
+{
+    if (rc)
+    {
+        draft_free(c);
+        return rc;
+    }
+    return draft_finish(c);
+}
+
+int hy_draft_load(hy_ctx* c, const hy_draft_weights* w)
+{
+    if (!c || !w || !w->fc || !w->hidden_norm || !w->norm || !w->layers)
+        return fail(HY_ERR_INVALID_ARGUMENT, "DFlash draft weights are incomplete");
+    for (int l = 0; l < w->num_layers; ++l)
+    {
+        const hy_layer_weights& lw = w->layers[l];
+        if (!lw.input_norm || !lw.q_proj || !lw.k_proj || !lw.v_proj || !lw.query_norm || !lw.key_norm || !lw.o_proj ||
+            !lw.post_norm || !lw.gate_proj || !lw.up_proj || !lw.down_proj)
+            return fail(HY_ERR_INVALID_ARGUMENT, "DFlash draft layer " + std::to_string(l) + " weights are incomplete");
+    }
+    int rc = set_device(c);
+    if (rc) return rc;
+    if ((rc = draft_alloc(c, w->num_layers, w->mask_token))) return draft_loaded_finish(c, rc);
+    return draft_loaded_finish(c, draft_upload(c, w));
+}
+
+int hy_draft_load_synthetic(hy_ctx* c, int num_layers, int mask_token, uint64_t seed, float std_dev, float norm_std)
+{
+    if (!c) return fail(HY_ERR_INVALID_ARGUMENT, "ctx is null");
+    int rc = set_device(c);
+    if (rc) return rc;
+    if ((rc = draft_alloc(c, num_layers, mask_token))) return draft_loaded_finish(c, rc);
+    return draft_loaded_finish(c, draft_fill_synthetic(c, seed, std_dev, norm_std));
+}
+
+int hy_draft_context_length(const hy_ctx* c, int* rows)
+{
+    if (!c || !rows) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    *rows = c->d_len;
+    return HY_OK;
+}
+
+int hy_draft_context_append(hy_ctx* c, const float* aux_hidden, int rows)
+{
+    if (!c || !aux_hidden) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    if (!draft_ready(c)) return fail(HY_ERR_NOT_READY, "DFlash draft runtime is not loaded");
+    if (rows <= 0) return fail(HY_ERR_INVALID_ARGUMENT, "DFlash target hidden shapes do not match");
+    if (c->d_len + rows + kBlock > c->cfg.max_context) return fail(HY_ERR_CAPACITY, "draft context exceeds the KV capacity");
+    int rc = set_device(c);
+    if (rc) return rc;
+    for (int p0 = 0; p0 < rows; p0 += c->pf_rows)
+    {
+        const int n = std::min(c->pf_rows, rows - p0);
+        for (int i = 0; i < kAuxLayers; ++i)
+            HY_CUDA(cudaMemcpy2DAsync(c->d_pf_aux + i * kHidden, sizeof(float) * kAuxWidth,
+                                      aux_hidden + (static_cast<size_t>(i) * rows + p0) * kHidden, sizeof(float) * kHidden,
+                                      sizeof(float) * kHidden, n, cudaMemcpyHostToDevice, c->stream));
+        const cudaError_t e = enqueue_draft_context_rows(c, n, c->d_len + p0);
+        if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("draft context launch: ") + cudaGetErrorString(e));
+    }
+    if ((rc = check_device_error(c))) return rc;
+    c->d_len += rows;
+    return HY_OK;
+}
+
+int hy_draft_run(hy_ctx* c, const float* noise, float* hidden)
+{
+    if (!c || !noise || !hidden) return fail(HY_ERR_INVALID_ARGUMENT, "DFlash output pointer is null");
+    if (!draft_ready(c)) return fail(HY_ERR_NOT_READY, "DFlash draft runtime is not loaded");
+    if (c->d_len <= 0) return fail(HY_ERR_INVALID_ARGUMENT, "invalid DFlash noise/context shape");
+    if (c->d_len + kBlock > c->cfg.max_context) return fail(HY_ERR_CAPACITY, "draft block exceeds the KV capacity");
+    int rc = set_device(c);
+    if (rc) return rc;
+    HY_CUDA(cudaMemcpyAsync(c->d_x, noise, sizeof(float) * kBlock * kHidden, cudaMemcpyHostToDevice, c->stream));
+    t_next_plain = true;
+    const cudaError_t e = enqueue_draft_forward(c, SRC_X, false, c->d_len, false);
+    if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("draft launch: ") + cudaGetErrorString(e));
+    HY_CUDA(cudaMemcpyAsync(hidden, c->hidden, sizeof(float) * kBlock * kHidden, cudaMemcpyDeviceToHost, c->stream));
+    return check_device_error(c);
+}
+
+static int draft_in_sync(hy_ctx* c)
+{
+    if (!draft_ready(c)) return fail(HY_ERR_NOT_READY, "DFlash draft runtime is not loaded");
+    if (c->kv_len <= 0 || c->d_len != c->kv_len)
+        return fail(HY_ERR_INVALID_ARGUMENT, "invalid DFlash block context: the draft context covers " +
+                                                 std::to_string(c->d_len) + " of " + std::to_string(c->kv_len) + " rows");
+    return HY_OK;
+}
+
+int hy_draft_propose(hy_ctx* c, int current_token, int* proposed)
+{
+    if (!c || !proposed) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    int rc = draft_in_sync(c);
+    if (rc) return rc;
+    if (current_token < 0 || current_token >= c->cfg.vocab_size) return fail(HY_ERR_INVALID_ARGUMENT, "invalid DFlash block context");
+    if (c->kv_len + kBlock > c->cfg.max_context) return fail(HY_ERR_CAPACITY, "KV capacity exceeded");
+    if ((rc = set_device(c))) return rc;
+    c->h_st->kv_len = c->kv_len;
+    c->h_st->cur_token = current_token;
+    if ((rc = push_state(c))) return rc;
+    t_next_plain = true;
+    const cudaError_t e = enqueue_draft_forward(c, SRC_GATHER_BLOCK, true, 0, true);
+    if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("draft launch: ") + cudaGetErrorString(e));
+    HY_CUDA(cudaMemcpyAsync(proposed, c->proposed, sizeof(int) * kBlock, cudaMemcpyDeviceToHost, c->stream));
+    return check_device_error(c);
+}
+
+int hy_dflash_generate(hy_ctx* c, int first_token, int max_tokens, float penalty, const int* eos_ids, int n_eos,
+                       int* tokens, int* n_tokens, int* acceptance_lengths, int* n_blocks)
+{
+    if (!c || !n_tokens) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    int rc = draft_in_sync(c);
+    if (rc) return rc;
+    if (max_tokens < 1 || max_tokens > c->cfg.max_tokens)
+        return fail(HY_ERR_CAPACITY, "max_tokens must be in 1..config max_tokens");
+    if (first_token < 0 || first_token >= c->cfg.vocab_size) return fail(HY_ERR_INVALID_ARGUMENT, "first_token out of range");
+    if (!std::isfinite(penalty) || penalty <= 0.f) return fail(HY_ERR_INVALID_ARGUMENT, "repetition_penalty must be positive");
+    if (c->kv_len + max_tokens + kBlock > c->cfg.max_context) return fail(HY_ERR_CAPACITY, "KV capacity exceeded");
+    if ((rc = set_device(c))) return rc;
+    if ((rc = set_eos(c, eos_ids, n_eos))) return rc;
+    DecodeState& h = *c->h_st;
+    h.kv_len = c->kv_len;
+    h.cur_token = first_token;
+    h.n_gen = 0;
+    h.max_tokens = max_tokens;
+    h.done = 0;
+    h.penalty = penalty;
+    h.block_count = 0;
+    if ((rc = push_state(c))) return rc;
+    int launched = 0;
+    while (!h.done && launched < max_tokens)
+    {
+        for (int i = 0; i < 4 && launched < max_tokens; ++i, ++launched) HY_CUDA(cudaGraphLaunch(c->g_dflash, c->stream));
+        if ((rc = sync_state_to_host(c))) return rc;
+    }
+    if ((rc = check_device_error(c))) return rc;
+    if ((rc = sync_state_to_host(c))) return rc;
+    c->d_len = c->kv_len;
+    *n_tokens = h.n_gen;
+    if (n_blocks) *n_blocks = h.block_count;
+    if (tokens) HY_CUDA(cudaMemcpy(tokens, c->log_tokens, sizeof(int) * h.n_gen, cudaMemcpyDeviceToHost));
+    if (acceptance_lengths)
+        HY_CUDA(cudaMemcpy(acceptance_lengths, c->accept_log, sizeof(int) * h.block_count, cudaMemcpyDeviceToHost));
+    return HY_OK;
+}
+
+int hy_run_vlm_dflash_with_prompt(hy_ctx* c, const int* input_ids, const int* position_ids, int seq_len,
+                                  int image_token_id, const float* vision_features, int vision_token_count,
+                                  int max_tokens, float repetition_penalty, const int* eos_ids, int n_eos, int* tokens,
+                                  int* n_tokens, int* acceptance_lengths, int* n_blocks)
+{
+    if (!c || !n_tokens) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    if (!draft_ready(c)) return fail(HY_ERR_NOT_READY, "DFlash draft runtime is not loaded");
+    if (max_tokens <= 0) max_tokens = 1024;   // src/text_runtime.cpp:1168-1171
+    if (max_tokens > c->cfg.max_tokens) return fail(HY_ERR_CAPACITY, "max_tokens exceeds config max_tokens");
+    int first = 0, first_raw = 0;
+    int rc = prompt_prefill_first(c, input_ids, position_ids, seq_len, image_token_id, vision_features,
+                                  vision_token_count, repetition_penalty, &first, &first_raw);
+    if (rc) return rc;
+    return hy_dflash_generate(c, first, max_tokens, repetition_penalty, eos_ids, n_eos, tokens, n_tokens,
+                              acceptance_lengths, n_blocks);
 }
 
 int hy_attention(hy_ctx* c, int layer, const float* qkv, int rows, const float* cos, const float* sin, float* out)

@@ -30,7 +30,9 @@ namespace hy {
 
 enum { PRO_PLAIN = 0, PRO_NORM = 1, PRO_SWIGLU = 2 };
 enum { EPI_STORE = 0, EPI_RESID = 1, EPI_ARGMAX = 2, EPI_ACT = 3 };   // EPI_ACT: M = 16 only
-enum { SRC_X = 0, SRC_GATHER_STATE = 1, SRC_GATHER_IDS = 2, SRC_GATHER_DRAFT = 3 };
+// SRC_GATHER_BLOCK: the DFlash draft's noise block [st->cur_token, mask_token x 15]
+// (build_dflash_block, src/dflash_runtime.cpp:20-25).
+enum { SRC_X = 0, SRC_GATHER_STATE = 1, SRC_GATHER_IDS = 2, SRC_GATHER_DRAFT = 3, SRC_GATHER_BLOCK = 4 };
 enum { LM_NONE = 0, LM_AR = 1, LM_VERIFY = 2 };
 
 constexpr int kGemvWarps = 8;
@@ -54,6 +56,7 @@ struct GemvArgs {
     DecodeState* st;
     const int* greedy;    // SRC_GATHER_DRAFT
     int vocab;
+    int mask_token;       // SRC_GATHER_BLOCK
     int* ids_out;         // gather: CTA 0 writes the gathered ids
     float* x_store;       // gather: fp32 rows written to the residual stream [rows x 1024]
     float* out;           // STORE / RESID target, out[m * ldo + n]
@@ -381,6 +384,7 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
             {
                 if (a.src == SRC_GATHER_STATE) id = a.st->cur_token;
                 else if (a.src == SRC_GATHER_IDS) id = a.ids[tid];
+                else if (a.src == SRC_GATHER_BLOCK) id = (tid == 0) ? a.st->cur_token : a.mask_token;
                 else id = draft_id(a.st, a.greedy, a.vocab, tid);
                 if (id < 0 || id >= a.vocab)
                 {

@@ -46,6 +46,8 @@ struct PrefillRopeArgs {
     const DecodeState* st;   // when set, past = st->kv_len (rows appended at the current length)
     int rope_state;          // rope row of row m: (rope_state ? past : 0) + m
     int* err;                // kErrBounds when a row would land past the capacity
+    int norm_first;          // DFlash draft: RMSNorm before RoPE (the decoder ropes first)
+    int kv_only;             // only k / v heads (grid y = 2): context rows of the draft cache
 };
 
 template <typename KT>
@@ -64,12 +66,14 @@ __global__ void __launch_bounds__(256) prefill_rope_kernel(const PrefillRopeArgs
     const float* c = a.cos + static_cast<size_t>(rr) * kHeadDim;
     const float* s = a.sin + static_cast<size_t>(rr) * kHeadDim;
     {
-        const int j = blockIdx.y * 8 + warp;   // 0..15 q heads, 16..23 k heads, 24..31 v heads
+        // 0..15 q heads, 16..23 k heads, 24..31 v heads
+        const int j = (a.kv_only ? kNumQHeads : 0) + blockIdx.y * 8 + warp;
         if (j < kNumQHeads)
         {
             float* x = row + j * kHeadDim;
             float o[4];
-            rope_norm_vec(x, c, s, a.qn_w, a.eps, lane, o);
+            if (a.norm_first) norm_rope_vec(x, c, s, a.qn_w, a.eps, lane, o);
+            else rope_norm_vec(x, c, s, a.qn_w, a.eps, lane, o);
 #pragma unroll
             for (int i = 0; i < 4; ++i) x[lane + 32 * i] = o[i] * a.scale_log2;
         }
@@ -77,7 +81,8 @@ __global__ void __launch_bounds__(256) prefill_rope_kernel(const PrefillRopeArgs
         {
             const int h = j - kNumQHeads;
             float o[4];
-            rope_norm_vec(row + kQWidth + h * kHeadDim, c, s, a.kn_w, a.eps, lane, o);
+            if (a.norm_first) norm_rope_vec(row + kQWidth + h * kHeadDim, c, s, a.kn_w, a.eps, lane, o);
+            else rope_norm_vec(row + kQWidth + h * kHeadDim, c, s, a.kn_w, a.eps, lane, o);
             KT* dst = static_cast<KT*>(a.kc) + (static_cast<size_t>(h) * a.cap + past + m) * kHeadDim;
 #pragma unroll
             for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = from_f32<KT>(o[i]);
@@ -148,6 +153,8 @@ struct PrefillAttnArgs {
     float* part;      // [slot][8 KV heads][2 QR query vectors][kPaPartStride]
     const DecodeState* st;   // device-side chunks: past = st->kv_len when set
     int* err;         // kErrBounds when past + rows exceeds the capacity (nothing is read then)
+    int noncausal;    // every row sees all keys [0, past + rows) (the DFlash draft's all-zero
+                      // mask, src/dflash_runtime.cpp:50-58); device-side chunks only
 };
 
 template <typename KT, int QR>
@@ -190,7 +197,7 @@ __global__ void __launch_bounds__(4 * QR, 2) prefill_attn_kernel(const PrefillAt
         return;
     }
     const int m0 = qb * QR;
-    const int nkeys = min(past + m0 + QR, past + a.rows);
+    const int nkeys = a.noncausal ? past + a.rows : min(past + m0 + QR, past + a.rows);
     const KT* kbase = static_cast<const KT*>(a.kc) + static_cast<size_t>(kvh) * a.cap * kHeadDim;
     const KT* vbase = static_cast<const KT*>(a.vc) + static_cast<size_t>(kvh) * a.cap * kHeadDim;
 
@@ -222,7 +229,9 @@ __global__ void __launch_bounds__(4 * QR, 2) prefill_attn_kernel(const PrefillAt
 
     const int hl = warp / (QR / 16), r0 = (warp % (QR / 16)) * 16;
     const float* Qw = Qs + (hl * QR + r0) * QP;
-    const int pq0 = past + m0 + r0 + g, pq1 = pq0 + 8;   // positions of rows g and g + 8
+    // Last visible key of rows g and g + 8: their own positions (causal), or the last key.
+    const int pq0 = a.noncausal ? nkeys - 1 : past + m0 + r0 + g;
+    const int pq1 = a.noncausal ? nkeys - 1 : pq0 + 8;
     float o[16][4];
 #pragma unroll
     for (int dt = 0; dt < 16; ++dt) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.f;

@@ -211,6 +211,16 @@ __global__ void rmsnorm_tiled_kernel(const float* __restrict__ x, const float* _
                  make_float4(wv.x * (v.x * ri), wv.y * (v.y * ri), wv.z * (v.z * ri), wv.w * (v.w * ri)));
 }
 
+// Row m of x [rows x K] (K a multiple of 1024), split, into tiled hi / lo of
+// `rows_pad` rows. One CTA (256 threads) per row.
+__global__ void split_tiled_kernel(const float* __restrict__ x, int K, int rows_pad, float* __restrict__ hi,
+                                   float* __restrict__ lo)
+{
+    const int m = blockIdx.x;
+    for (int k = threadIdx.x * 4; k < K; k += 256 * 4)
+        store_tiled4(hi, lo, rows_pad, m, k, *reinterpret_cast<const float4*>(x + static_cast<size_t>(m) * K + k));
+}
+
 // ---------------------------------------------------------------------------
 // The prefill GEMM.
 // ---------------------------------------------------------------------------

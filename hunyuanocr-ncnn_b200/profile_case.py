@@ -28,11 +28,13 @@ def main(argv=None):
     ap.add_argument("--calls", type=int, default=3)
     ap.add_argument("--path", choices=["persistent", "graph"], default="persistent")
     ap.add_argument("--dtype", choices=["f32", "bf16"], default="f32", help="weight and KV dtype")
-    ap.add_argument("--kernel", choices=["decode", "lm", "gate_up", "attention", "verify", "prefill"],
+    ap.add_argument("--draft-layers", type=int, default=5, help="draft mode: DFlash draft depth")
+    ap.add_argument("--kernel", choices=["decode", "lm", "gate_up", "attention", "verify", "prefill", "draft"],
                     default="decode",
                     help="decode: AR launches; lm / gate_up / attention: the M=1 kernels alone "
                          "(hy_bench_kernel); verify: DFlash verify blocks (16-row kernels); "
-                         "prefill: prompt prefill of --past rows (tcgen05 GEMMs, prefill attention)")
+                         "prefill: prompt prefill of --past rows (tcgen05 GEMMs, prefill attention); "
+                         "draft: DFlash blocks with a synthetic draft network over a --past-row context")
     args = ap.parse_args(argv)
 
     import __graft_entry__ as ge
@@ -70,6 +72,19 @@ def main(argv=None):
         ms = rt.bench_kernel(which, args.calls)
         print(f"{args.kernel} {args.dtype} layers={args.layers} vocab={args.vocab} past={args.past}: "
               f"{ms * 1e3:.2f} us per launch")
+        rt.close()
+        return
+    if args.kernel == "draft":
+        import numpy as np
+
+        rt.load_draft_synthetic(args.draft_layers, seed=3, std=0.02)
+        rt.draft_context_append(np.random.default_rng(0).standard_normal((4, args.past, 1024), dtype=np.float32))
+        for _ in range(args.calls):
+            rt.set_length(args.past)
+            rt.set_history([1, 2, 3])
+            r = rt.dflash_generate(7, args.tokens, 1.08)
+        print(f"draft {args.dtype} layers={args.layers} draft_layers={args.draft_layers} vocab={args.vocab} "
+              f"past={args.past}: {r.block_count} blocks per call")
         rt.close()
         return
     if args.kernel == "verify":

@@ -222,6 +222,65 @@ int hy_dflash_generate_synthetic(hy_ctx* ctx, int first_token, int max_tokens, f
                                  uint64_t seed, int* tokens, int* n_tokens, int* acceptance_lengths,
                                  int* n_blocks);
 
+/* ---- DFlash draft network -------------------------------------------- */
+/* Draft weights: the graph of export/dflash_export.py:40-177 (fc over the four
+ * aux hidden states side by side, hidden_norm, draft layers, norm). Each draft
+ * layer has the decoder layer's geometry and nn.Linear layout (q_norm /
+ * k_norm in query_norm / key_norm; ffn = the context's ffn_dim). */
+typedef struct hy_draft_weights {
+    int num_layers;                 /* 1..8 */
+    int mask_token;                 /* noise-block filler id: 120817
+                                       (include/hunyuan_ocr/dflash_runtime.h:17-18) */
+    const float* fc;                /* [1024 x 4096] */
+    const float* hidden_norm;       /* [1024] */
+    const float* norm;              /* [1024] */
+    const hy_layer_weights* layers; /* [num_layers] */
+} hy_draft_weights;
+
+/* DFlashDraftRuntime::load (src/dflash_runtime.cpp:175-201): uploads the draft
+ * (in the context's weight dtype) beside the decoder and reserves its K/V cache
+ * of context rows. Replaces a draft loaded before. From then on every call that
+ * appends KV rows (hy_prefill, hy_decoder_step, hy_verify_block,
+ * hy_run_vlm_*_with_prompt) also appends the rows' draft context (k / v of
+ * hidden_norm(fc(aux_1 | aux_8 | aux_15 | aux_22)) per draft layer) while the
+ * draft context covers the sequence; hy_generate (AR) does not. */
+int hy_draft_load(hy_ctx* ctx, const hy_draft_weights* weights);
+/* Same with seeded synthetic draft weights (linears ~N(0, std), norms
+ * 1 + ~N(0, norm_std)) from the library's counter generator. */
+int hy_draft_load_synthetic(hy_ctx* ctx, int num_layers, int mask_token, uint64_t seed, float std, float norm_std);
+/* Rows [0, rows) of the sequence that have draft context. */
+int hy_draft_context_length(const hy_ctx* ctx, int* rows);
+/* The target_hidden input of DFlashDraftRuntime::run for `rows` more context
+ * rows (append_dflash_rows, src/dflash_runtime.cpp:121-166): aux_hidden
+ * [4 x rows x 1024] (hy_decoder_step's layout), appended at positions
+ * context_length .. context_length + rows - 1. */
+int hy_draft_context_append(hy_ctx* ctx, const float* aux_hidden, int rows);
+/* DFlashDraftRuntime::run (src/dflash_runtime.cpp:213-290): the draft graph for
+ * noise [16 x 1024] at positions context_length .. + 15 over the draft context
+ * (RoPE theta 10000, no mask); hidden [16 x 1024] = the final-normed rows. */
+int hy_draft_run(hy_ctx* ctx, const float* noise, float* hidden);
+/* The draft half of run_dflash_block (src/text_runtime.cpp:913-978) at the
+ * sequence length: noise = embed([current_token, mask x 15]), draft, then
+ * proposed[0] = current_token and proposed[1..15] = argmax of the tied LM head
+ * over draft rows 1..15. Needs the draft context to cover the sequence. */
+int hy_draft_propose(hy_ctx* ctx, int current_token, int* proposed);
+/* decode_dflash_from_embeddings' block loop (src/text_runtime.cpp:1206-1296)
+ * with the draft network, on the device: per block one CUDA-graph launch of
+ * draft -> verify forward (M = 16) -> draft context of the block's rows ->
+ * posterior, dflash_acceptance_length, commit of min(accept + 1, remaining)
+ * tokens (cut at EOS) and rollback. first_token is not yet in the history.
+ * tokens [n_tokens], acceptance_lengths [n_blocks] (nullable). */
+int hy_dflash_generate(hy_ctx* ctx, int first_token, int max_tokens, float penalty, const int* eos_ids, int n_eos,
+                       int* tokens, int* n_tokens, int* acceptance_lengths, int* n_blocks);
+/* run_vlm_decode_with_prompt with the --dflash switch (src/hunyuan_ocr.cpp:166,
+ * 357 -> decode_dflash_from_embeddings, src/text_runtime.cpp:1142-1305):
+ * prompt embedding, prefill with the prompt's draft context, first token, then
+ * hy_dflash_generate. */
+int hy_run_vlm_dflash_with_prompt(hy_ctx* ctx, const int* input_ids, const int* position_ids, int seq_len,
+                                  int image_token_id, const float* vision_features, int vision_token_count,
+                                  int max_tokens, float repetition_penalty, const int* eos_ids, int n_eos, int* tokens,
+                                  int* n_tokens, int* acceptance_lengths, int* n_blocks);
+
 /* TextRuntime::run_vlm_decode_with_prompt (src/text_runtime.cpp:2053-2094):
  * prompt embedding with vision-feature injection (prepare_prompt_embeddings,
  * 506-568), mRoPE tables, prefill, first-token selection and the AR loop.

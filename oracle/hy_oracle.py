@@ -287,9 +287,10 @@ def build_dflash_verify_mask(past_len: int) -> np.ndarray:
     return np.where(col > past_len + row, MASK_NEG_INF, np.float32(0.0)).astype(np.float32)
 
 
-def build_dflash_block(first_token: int) -> list:
-    """src/dflash_runtime.cpp:20-25."""
-    return [int(first_token)] + [DFLASH_MASK_TOKEN] * (DFLASH_BLOCK - 1)
+def build_dflash_block(first_token: int, mask_token: int = DFLASH_MASK_TOKEN) -> list:
+    """src/dflash_runtime.cpp:20-25 (mask_token: kDFlashMaskTokenId = 120817; a
+    smaller test vocabulary passes its own filler id)."""
+    return [int(first_token)] + [int(mask_token)] * (DFLASH_BLOCK - 1)
 
 
 def dflash_acceptance_length(proposed, posterior) -> int:
@@ -804,11 +805,12 @@ def draft_forward(dw: DraftWeights, noise: np.ndarray, cache: DraftCache, eps: f
     return rms_norm(h, dw.norm, eps)
 
 
-def draft_propose(w: Weights, dw: DraftWeights, cache: DraftCache, current: int, eps: float = RMS_EPS):
+def draft_propose(w: Weights, dw: DraftWeights, cache: DraftCache, current: int, eps: float = RMS_EPS,
+                  mask_token: int = DFLASH_MASK_TOKEN):
     """run_dflash_block's draft half (src/text_runtime.cpp:913-978): noise = embed([current, MASK x 15]),
     drafts = argmax of the LM head on draft rows 1..15 (penalty 1, no history).
     Returns (proposed block [16], draft hidden [16, 1024])."""
-    block = build_dflash_block(current)
+    block = build_dflash_block(current, mask_token)
     hidden = draft_forward(dw, w.embed[np.asarray(block)], cache, eps)
     logits = lm_head(w, hidden[1:])
     block[1:] = select_logit_rows(logits, [], None, 1.0)
@@ -816,7 +818,8 @@ def draft_propose(w: Weights, dw: DraftWeights, cache: DraftCache, current: int,
 
 
 def decode_dflash_draft(w: Weights, cfg: ModelConfig, dw: DraftWeights, prompt: Prompt, max_tokens: int,
-                        penalty: float = DEFAULT_PENALTY, eos_ids=()) -> DFlashTrace:
+                        penalty: float = DEFAULT_PENALTY, eos_ids=(), mask_token: int = DFLASH_MASK_TOKEN,
+                        proposals: list | None = None) -> DFlashTrace:
     """decode_dflash_from_embeddings with the draft network: the draft context starts
     as the prompt's aux hidden states (run_dflash_prefill) and grows by the aux
     rows of every block's committed tokens (append_dflash_rows)."""
@@ -831,7 +834,9 @@ def decode_dflash_draft(w: Weights, cfg: ModelConfig, dw: DraftWeights, prompt: 
     tr = DFlashTrace([], [])
     while len(tr.tokens) < max_tokens:
         ctx = cache.length
-        proposed, _ = draft_propose(w, dw, dcache, current, cfg.rms_eps)
+        proposed, _ = draft_propose(w, dw, dcache, current, cfg.rms_eps, mask_token)
+        if proposals is not None:
+            proposals.append(list(proposed))
         posterior, accept, _, vaux = verify_block(w, cfg, cache, proposed, history, penalty, aux=True)
         available = accept + 1
         committed = min(available, max_tokens - len(tr.tokens))
