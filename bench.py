@@ -290,11 +290,13 @@ def run_b200(args, world, rank, local):
 
     # e2e: reference-facing call with host buffers (prompt upload, prefill, 256 tokens, tokens back).
     e2e_times = []
-    for _ in range(max(1, args.steps)):
-        t0 = time.perf_counter()
-        r2 = rt.run_vlm_decode_with_prompt(ids, pos, image_token, feats, max_tokens=GEN_TOKENS)
-        e2e_times.append(time.perf_counter() - t0)
-        assert r2.generated_tokens == res.generated_tokens
+    rt.run_vlm_decode_with_prompt(ids, pos, image_token, feats, max_tokens=GEN_TOKENS)   # untimed warm-up
+    with ClockSampler(local) as e2e_clocks:
+        for _ in range(max(1, args.steps)):
+            t0 = time.perf_counter()
+            r2 = rt.run_vlm_decode_with_prompt(ids, pos, image_token, feats, max_tokens=GEN_TOKENS)
+            e2e_times.append(time.perf_counter() - t0)
+            assert r2.generated_tokens == res.generated_tokens
     # Whole-job throughput over the timed calls (tokens of all calls / their total time), max over ranks.
     e2e_t = dist_max(sum(e2e_times), world)
     e2e_value = len(r2.generated_tokens) * len(e2e_times) * world / e2e_t
@@ -337,6 +339,7 @@ def run_b200(args, world, rank, local):
                       "lm_head_m1_gbs": round(LM_HEAD_BYTES / (lm_ms / 1e3) / 1e9, 1)},
         "dflash": dflash,
         "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "scope": "prefill + 256 tokens per call",
+                "ms_per_call": [round(t * 1e3, 1) for t in e2e_times], "clocks": e2e_clocks.summary(),
                 "h2d_bytes_per_step": int(ids.nbytes + pos.nbytes + feats.nbytes),
                 "d2h_bytes_per_step": int(2 * 4 * len(r2.generated_tokens))},
         "gpu_launches": int(launches * args.steps),
