@@ -48,7 +48,7 @@ EXPORTED_SYMBOLS = (
     "hy_ctx_set_ar_path", "hy_ctx_ar_path", "hy_trace_persistent", "hy_debug_progress",
     "hy_lm_head_select_noalloc", "hy_draft_load", "hy_draft_load_synthetic", "hy_draft_context_length",
     "hy_draft_context_append", "hy_draft_run", "hy_draft_propose", "hy_dflash_generate",
-    "hy_run_vlm_dflash_with_prompt",
+    "hy_run_vlm_dflash_with_prompt", "hy_batch_decode",
 )
 DFLASH_MASK_TOKEN = 120817
 AR_PATH_PERSISTENT = 0
@@ -81,6 +81,12 @@ class _DraftWeights(ctypes.Structure):
     _fields_ = [("num_layers", ctypes.c_int), ("mask_token", ctypes.c_int), ("fc", ctypes.c_void_p),
                 ("hidden_norm", ctypes.c_void_p), ("norm", ctypes.c_void_p),
                 ("layers", ctypes.POINTER(_LayerWeights))]
+
+
+class _Request(ctypes.Structure):
+    _fields_ = [("input_ids", ctypes.c_void_p), ("position_ids", ctypes.c_void_p), ("seq_len", ctypes.c_int),
+                ("image_token_id", ctypes.c_int), ("vision_features", ctypes.c_void_p),
+                ("vision_token_count", ctypes.c_int)]
 
 
 class _Weights(ctypes.Structure):
@@ -141,6 +147,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "hy_ctx_ar_path": ([_P], _I),
         "hy_trace_persistent": ([_P, _I, _I, _P], _I),
         "hy_draft_load": ([_P, ctypes.POINTER(_DraftWeights)], _I),
+        "hy_batch_decode": ([_P, ctypes.POINTER(_Request), _I, _I, _I, _F, _P, _I, _P, _P, _P], _I),
         "hy_draft_load_synthetic": ([_P, _I, _I, ctypes.c_uint64, _F, _F], _I),
         "hy_draft_context_length": ([_P, ctypes.POINTER(_I)], _I),
         "hy_draft_context_append": ([_P, _P, _I], _I),
@@ -427,6 +434,26 @@ class TextRuntime:
                                                   _ptr(eos), 0 if eos is None else eos.size, _ptr(tokens),
                                                   _ptr(raw), ctypes.byref(n)))
         return TextDecodeResult(ids.size, repetition_penalty, tokens[:n.value].tolist(), raw[:n.value].tolist())
+
+    def batch_decode(self, requests, max_tokens: int, slots: int = 16, repetition_penalty: float = 1.08,
+                     eos_ids=()):
+        """Records decoded together, up to `slots` at a time (hy_batch_decode).
+        requests: (input_ids, position_ids, image_token_id, vision_features) tuples.
+        Returns (tokens per record, status per record)."""
+        keep = []
+        reqs = (_Request * max(1, len(requests)))()
+        for i, (ids, pos, img, feats) in enumerate(requests):
+            ids, pos, feats = _i32(ids), _i32(pos).reshape(-1), _f32(feats).reshape(-1, HIDDEN)
+            keep += [ids, pos, feats]
+            reqs[i] = _Request(ids.ctypes.data, pos.ctypes.data, ids.size, img, feats.ctypes.data, feats.shape[0])
+        n = len(requests)
+        eos = _i32(list(eos_ids)) if len(eos_ids) else None
+        tokens = np.zeros((max(1, n), max_tokens), np.int32)
+        counts = np.zeros(max(1, n), np.int32)
+        status = np.zeros(max(1, n), np.int32)
+        _check(_LIB.hy_batch_decode(self._ctx, reqs, n, slots, max_tokens, repetition_penalty, _ptr(eos),
+                                    0 if eos is None else eos.size, _ptr(tokens), _ptr(counts), _ptr(status)))
+        return [tokens[i, :counts[i]].tolist() for i in range(n)], status[:n].tolist()
 
     # -- DFlash draft network -------------------------------------------------
     def load_draft(self, draft_weights, mask_token: int = DFLASH_MASK_TOKEN) -> None:

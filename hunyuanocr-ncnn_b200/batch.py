@@ -69,6 +69,28 @@ def run_partition(records: Sequence, infer: Callable, world: int = 1, rank: int 
     return out, summary
 
 
+def run_partition_batched(records: Sequence, infer_many: Callable, world: int = 1, rank: int = 0,
+                          record_id: Optional[Callable] = None) -> tuple[List[BatchRecord], BatchSummary]:
+    """run_partition for a rank that decodes its records together (several sequences
+    per GPU step): `infer_many(records) -> [(ok, tokens or error message)]`, one entry
+    per record in order. Same output records and summary as run_partition."""
+    idx = partition(len(records), world, rank)
+    results = infer_many([records[i] for i in idx]) if idx else []
+    if len(results) != len(idx):
+        raise ValueError(f"infer_many returned {len(results)} results for {len(idx)} records")
+    out: List[BatchRecord] = []
+    summary = BatchSummary(total=len(idx))
+    for i, (ok, value) in zip(idx, results):
+        rid = record_id(records[i]) if record_id else str(i)
+        if ok:
+            summary.succeeded += 1
+            out.append(BatchRecord(i, rid, True, tokens=list(value)))
+        else:
+            summary.failed += 1
+            out.append(BatchRecord(i, rid, False, stage="inference", error=str(value) or "inference failed"))
+    return out, summary
+
+
 def merge_in_order(parts: Iterable[Sequence[BatchRecord]]) -> tuple[List[BatchRecord], BatchSummary]:
     """Merge per-rank outputs into input order and add up the summaries."""
     merged = sorted((r for p in parts for r in p), key=lambda r: r.index)

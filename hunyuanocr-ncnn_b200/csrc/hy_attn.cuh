@@ -61,6 +61,11 @@ struct AttnArgs {
     int* counter;       // [8]
     float* out;         // [rows x 2048]
     int* err;
+    // Batched decode (one row per sequence, grid z = row): row z attends to its own
+    // slot's cache (kc / vc + z * slot_stride elements) at its own length; rows of
+    // inactive slots do nothing. part / counter / out / qkv are offset by row.
+    const SlotState* slots;
+    size_t slot_stride;
 };
 
 template <int MT, typename KT>
@@ -136,12 +141,18 @@ __global__ void __launch_bounds__(kAttnThreads, (MT == 1) ? 2 : 1) attn_kernel(c
     __shared__ int s_last;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int nsplit = gridDim.x, split = blockIdx.x, g = blockIdx.y;
+    const int nsplit = gridDim.x, split = blockIdx.x, g = blockIdx.y, bz = blockIdx.z;
     const bool new_split = (split == nsplit - 1);
     // Rows [0, past) were written by earlier steps, so they (and past itself)
-    // may be read before griddepcontrol.wait.
-    const int past = a.st ? a.st->kv_len : a.past_fixed;
+    // may be read before griddepcontrol.wait (the slot states too: the commit
+    // that wrote them ran at least two kernels earlier).
+    if (a.slots && !a.slots[bz].active) return;
+    const int past = a.slots ? a.slots[bz].kv_len : a.st ? a.st->kv_len : a.past_fixed;
     const int rows = a.rows;
+    const size_t slot_off = a.slots ? static_cast<size_t>(bz) * a.slot_stride : 0;
+    const float* qkv_base = a.qkv + static_cast<size_t>(bz) * a.ldq;
+    float* out_base = a.out + static_cast<size_t>(bz) * kQWidth;
+    int* counter = a.counter + bz * kNumKVHeads;
     int p0 = 0, p1 = 0;
     if (!new_split)
     {
@@ -163,8 +174,8 @@ __global__ void __launch_bounds__(kAttnThreads, (MT == 1) ? 2 : 1) attn_kernel(c
     }
     __syncthreads();
 
-    const KT* kbase = static_cast<const KT*>(a.kc) + static_cast<size_t>(g) * a.cap * kHeadDim;
-    const KT* vbase = static_cast<const KT*>(a.vc) + static_cast<size_t>(g) * a.cap * kHeadDim;
+    const KT* kbase = static_cast<const KT*>(a.kc) + slot_off + static_cast<size_t>(g) * a.cap * kHeadDim;
+    const KT* vbase = static_cast<const KT*>(a.vc) + slot_off + static_cast<size_t>(g) * a.cap * kHeadDim;
 
     if (warp == kAttnWarps)
     {
@@ -215,7 +226,7 @@ __global__ void __launch_bounds__(kAttnThreads, (MT == 1) ? 2 : 1) attn_kernel(c
 #pragma unroll
         for (int i = 0; i < 4; ++i) xv[jv][i] = cv[jv][i] = sv[jv][i] = 0.f;
         if (v >= nvec || m >= rows) continue;
-        const float* src = a.qkv + static_cast<size_t>(m) * a.ldq +
+        const float* src = qkv_base + static_cast<size_t>(m) * a.ldq +
                            ((kind == 0) ? (2 * g + head) * kHeadDim : (kind == 1) ? kQWidth + g * kHeadDim
                                                                                   : kQWidth + kKVWidth + g * kHeadDim);
         const int prow = (a.rope_state ? past : 0) + m;
@@ -384,7 +395,8 @@ __global__ void __launch_bounds__(kAttnThreads, (MT == 1) ? 2 : 1) attn_kernel(c
     }
 
     // CTA partial per query.
-    float* part = a.part + (static_cast<size_t>(g) * nsplit + split) * NQ * kPartStride;
+    float* const part_base = a.part + static_cast<size_t>(bz) * kNumKVHeads * nsplit * NQ * kPartStride;
+    float* part = part_base + (static_cast<size_t>(g) * nsplit + split) * NQ * kPartStride;
     for (int e = tid; e < NQ * kHeadDim; e += 256)
     {
         const int q = e / kHeadDim, d = e % kHeadDim;
@@ -411,7 +423,7 @@ __global__ void __launch_bounds__(kAttnThreads, (MT == 1) ? 2 : 1) attn_kernel(c
     }
     __threadfence();
     attn_consumers_sync();
-    if (tid == 0) s_last = (atomicAdd(&a.counter[g], 1) == nsplit - 1) ? 1 : 0;
+    if (tid == 0) s_last = (atomicAdd(&counter[g], 1) == nsplit - 1) ? 1 : 0;
     attn_consumers_sync();
     if (!s_last) return;
     __threadfence();
@@ -420,7 +432,7 @@ __global__ void __launch_bounds__(kAttnThreads, (MT == 1) ? 2 : 1) attn_kernel(c
     // every split and query, the merged max / sum and each split's weight (in
     // the drained ring), then the accumulators, every split's float4 of an
     // output in flight at once.
-    const float* hp = a.part + static_cast<size_t>(g) * nsplit * NQ * kPartStride;
+    const float* hp = part_base + static_cast<size_t>(g) * nsplit * NQ * kPartStride;
     float* mw = reinterpret_cast<float*>(ring);   // [nsplit][NQ] split max -> weight
     float* ls = mw + nsplit * NQ;                 // [nsplit][NQ] split sum
     float* inv_l = ls + nsplit * NQ;              // [NQ] 1 / merged sum
@@ -465,9 +477,9 @@ __global__ void __launch_bounds__(kAttnThreads, (MT == 1) ? 2 : 1) attn_kernel(c
         }
         const float il = inv_l[q];
         A.x *= il; A.y *= il; A.z *= il; A.w *= il;
-        *reinterpret_cast<float4*>(a.out + static_cast<size_t>(m) * kQWidth + (2 * g + head) * kHeadDim + 4 * d4) = A;
+        *reinterpret_cast<float4*>(out_base + static_cast<size_t>(m) * kQWidth + (2 * g + head) * kHeadDim + 4 * d4) = A;
     }
-    if (tid == 0) a.counter[g] = 0;
+    if (tid == 0) counter[g] = 0;
 }
 
 }  // namespace hy

@@ -182,6 +182,25 @@ struct hy_ctx {
     cudaGraphExec_t g_dflash = nullptr;           // draft + verify + context append + commit
     cudaGraphExec_t g_verify_ids_ctx = nullptr;   // verify of given ids + context append + commit
 
+    // Batched decode (hy_batch_decode): up to 16 sequences, sequence s in step row s,
+    // each with its own KV cache [layer][8][cap][128] (slot-major), history bitmap
+    // and token log; one CUDA graph = one decode step of every slot.
+    int b_rows = 0;                          // rows (slots) of the captured step graph
+    void* b_kc = nullptr;                    // [16][layers][8][cap][128] KT
+    void* b_vc = nullptr;
+    SlotState* b_state = nullptr;            // [16]
+    SlotState* h_bstate = nullptr;           // pinned mirror
+    int* b_cur = nullptr;                    // [16] next token per slot
+    unsigned* b_hist = nullptr;              // [16][hist words]
+    int* b_log = nullptr;                    // [16][max_tokens + 32]
+    int* b_lograw = nullptr;
+    int* b_cnt = nullptr;                    // [layers][16][8] attention tickets
+    std::vector<void*> b_allocs;
+    cudaGraphExec_t g_batch = nullptr;
+    int hist_words() const { return (cfg.vocab_size + 31) / 32; }
+    int log_stride() const { return cfg.max_tokens + 2 * kBlock; }
+    size_t slot_elems() const { return static_cast<size_t>(cfg.num_layers) * kNumKVHeads * cfg.max_context * kHeadDim; }
+
     size_t kv_elem() const { return cfg.kv_dtype == HY_DTYPE_BF16 ? 2 : 4; }
     size_t w_elem() const { return cfg.weight_dtype == HY_DTYPE_BF16 ? 2 : 4; }
     float* in_norm(int l) const { return norms + static_cast<size_t>(l) * 2304; }
@@ -1139,7 +1158,10 @@ void free_ctx(hy_ctx* c)
     if (c->g_verify_ids) cudaGraphExecDestroy(c->g_verify_ids);
     if (c->g_dflash) cudaGraphExecDestroy(c->g_dflash);
     if (c->g_verify_ids_ctx) cudaGraphExecDestroy(c->g_verify_ids_ctx);
+    if (c->g_batch) cudaGraphExecDestroy(c->g_batch);
     for (void* p : c->d_allocs) cudaFree(p);
+    for (void* p : c->b_allocs) cudaFree(p);
+    if (c->h_bstate) cudaFreeHost(c->h_bstate);
     for (void* p : c->allocs) cudaFree(p);
     if (c->logits) cudaFree(c->logits);
     if (c->h_st) cudaFreeHost(c->h_st);
@@ -1985,6 +2007,212 @@ int draft_upload(hy_ctx* c, const hy_draft_weights* w)
 }
 
 // ---------------------------------------------------------------------------
+// Batched decode: the reference's JSONL batch runs its records one after the
+// other through one runtime (run_jsonl_batch, src/batch_jsonl.cpp:384-480;
+// decode_from_embeddings per record). Here up to 16 records decode together:
+// step row m carries the next token of the sequence in slot m, so one pass of
+// the 16-row projections (weights streamed once) advances every sequence by a
+// token. Per layer: q/k/v (16 rows, input RMSNorm), the one-row attention
+// kernel with grid z = row (RoPE / QK norm / append and split-K attention over
+// the row's own cache at its own length), o_proj, gate/up + SwiGLU, down_proj;
+// then the LM head with per-row history bitmaps and a per-slot commit (token
+// log, history, KV length, EOS / max_tokens). Prompts are prefilled into their
+// slot's cache by the ordinary prefill when a slot frees up.
+// ---------------------------------------------------------------------------
+constexpr int kBatchSplits = 4;   // 3 past-key splits + the new-row split per (row, KV head)
+
+template <typename T>
+int batch_dalloc(hy_ctx* c, T** p, size_t count)
+{
+    void* v = nullptr;
+    const size_t bytes = align_up(std::max<size_t>(count * sizeof(T), 16), 256);
+    cudaError_t e = cudaMalloc(&v, bytes);
+    if (e != cudaSuccess)
+        return fail(HY_ERR_OUT_OF_MEMORY, "cudaMalloc(" + std::to_string(bytes) + " bytes) failed: " + cudaGetErrorString(e));
+    c->b_allocs.push_back(v);
+    c->device_bytes += bytes;
+    *p = static_cast<T*>(v);
+    return HY_OK;
+}
+
+template <typename WT, typename KT>
+cudaError_t enqueue_batch_step_t(hy_ctx* c, int rows)
+{
+    const hy_config& cfg = c->cfg;
+    const int ffn = cfg.ffn_dim;
+    cudaError_t e = cudaSuccess;
+    for (int l = 0; l < cfg.num_layers; ++l)
+    {
+        GemvArgs q = base_args(c);
+        q.W = c->wqkv[l];
+        q.N = kQKVRows;
+        q.ldw = kHidden;
+        q.rows = rows;
+        q.src = (l == 0) ? SRC_GATHER_IDS : SRC_X;
+        q.ids = c->b_cur;
+        q.x_store = c->x;
+        q.x = c->x;
+        q.ldx = kHidden;
+        q.norm_w = c->in_norm(l);
+        q.out = c->qkv;
+        q.ldo = kQKVRows;
+        if ((e = run_gemv<WT, kHidden, 16, PRO_NORM, EPI_STORE>(c, q)) != cudaSuccess) return e;
+
+        AttnArgs at;
+        std::memset(&at, 0, sizeof(at));
+        at.qkv = c->qkv;
+        at.ldq = kQKVRows;
+        at.qn_w = c->qn(l);
+        at.kn_w = c->kn(l);
+        at.cos = c->rope_cos;
+        at.sin = c->rope_sin;
+        at.rope_state = 1;
+        const size_t layer_off = static_cast<size_t>(l) * kNumKVHeads * cfg.max_context * kHeadDim * c->kv_elem();
+        at.kc = static_cast<char*>(c->b_kc) + layer_off;
+        at.vc = static_cast<char*>(c->b_vc) + layer_off;
+        at.cap = cfg.max_context;
+        at.rows = 1;
+        at.scale_log2 = cfg.attn_scale * 1.4426950408889634f;
+        at.eps = cfg.rms_norm_eps;
+        at.part = c->attn_part;
+        at.counter = c->b_cnt + static_cast<size_t>(l) * kMaxStepRows * kNumKVHeads;
+        at.out = c->attn;
+        at.err = c->err;
+        at.slots = c->b_state;
+        at.slot_stride = c->slot_elems();
+        {
+            using S = AttnShape<1, KT>;
+            auto k = attn_kernel<1, KT>;
+            static unsigned long long configured = 0;
+            const unsigned long long bit = 1ull << (c->cfg.device & 63);
+            if (!(configured & bit))
+            {
+                if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM)) != cudaSuccess)
+                    return e;
+                configured |= bit;
+            }
+            if ((e = launch_pdl(k, dim3(kBatchSplits, kNumKVHeads, rows), dim3(kAttnThreads), S::SMEM, c->stream, at)) !=
+                cudaSuccess)
+                return e;
+        }
+
+        GemvArgs o = base_args(c);
+        o.W = c->wo[l];
+        o.N = kHidden;
+        o.ldw = kQWidth;
+        o.rows = rows;
+        o.src = SRC_X;
+        o.x = c->attn;
+        o.ldx = kQWidth;
+        o.out = c->x;
+        o.ldo = kHidden;
+        if ((e = run_gemv<WT, kQWidth, 16, PRO_PLAIN, EPI_RESID>(c, o)) != cudaSuccess) return e;
+
+        GemvArgs gu = base_args(c);
+        gu.W = c->wgu[l];
+        gu.N = 2 * ffn;
+        gu.ldw = kHidden;
+        gu.rows = rows;
+        gu.src = SRC_X;
+        gu.x = c->x;
+        gu.ldx = kHidden;
+        gu.norm_w = c->post_norm(l);
+        gu.out = c->act;
+        gu.ldo = ffn;
+        if ((e = run_gemv<WT, kHidden, 16, PRO_NORM, EPI_ACT>(c, gu)) != cudaSuccess) return e;
+
+        GemvArgs d = base_args(c);
+        d.W = c->wd[l];
+        d.N = kHidden;
+        d.ldw = ffn;
+        d.rows = rows;
+        d.src = SRC_X;
+        d.x = c->act;
+        d.ldx = ffn;
+        GemvArgs d1 = d;
+        d1.k_off = 0;
+        d1.out = c->tmp;
+        d1.ldo = kHidden;
+        if ((e = run_gemv<WT, kFfn / 2, 16, PRO_PLAIN, EPI_STORE>(c, d1)) != cudaSuccess) return e;
+        GemvArgs d2 = d;
+        d2.k_off = kFfn / 2;
+        d2.out = c->x;
+        d2.ldo = kHidden;
+        d2.extra = c->tmp;
+        if ((e = run_gemv<WT, kFfn / 2, 16, PRO_PLAIN, EPI_RESID>(c, d2)) != cudaSuccess) return e;
+    }
+    GemvArgs lm = base_args(c);
+    lm.W = c->embed;
+    lm.N = cfg.vocab_size;
+    lm.ldw = kHidden;
+    lm.rows = rows;
+    lm.src = SRC_X;
+    lm.x = c->x;
+    lm.ldx = kHidden;
+    lm.norm_w = c->final_norm();
+    lm.lm_mode = LM_BATCH;
+    lm.hist = c->b_hist;
+    lm.hist_stride = c->hist_words();
+    lm.slots = c->b_state;
+    lm.slot_cur = c->b_cur;
+    lm.log_tokens = c->b_log;
+    lm.log_raw = c->b_lograw;
+    lm.log_stride = c->log_stride();
+    return run_gemv<WT, kHidden, 16, PRO_NORM, EPI_ARGMAX>(c, lm);
+}
+
+cudaError_t enqueue_batch_step(hy_ctx* c, int rows)
+{
+    const bool wb = c->cfg.weight_dtype == HY_DTYPE_BF16, kb = c->cfg.kv_dtype == HY_DTYPE_BF16;
+    if (!wb && !kb) return enqueue_batch_step_t<float, float>(c, rows);
+    if (!wb && kb) return enqueue_batch_step_t<float, __nv_bfloat16>(c, rows);
+    if (wb && !kb) return enqueue_batch_step_t<__nv_bfloat16, float>(c, rows);
+    return enqueue_batch_step_t<__nv_bfloat16, __nv_bfloat16>(c, rows);
+}
+
+// Slot buffers (first use) and the step graph for `rows` slots.
+int batch_prepare(hy_ctx* c, int rows)
+{
+    int rc;
+    if (!c->b_kc)
+    {
+        const size_t kv = static_cast<size_t>(kMaxStepRows) * c->slot_elems() * c->kv_elem();
+        unsigned char* p = nullptr;
+        if ((rc = batch_dalloc(c, &p, kv))) return rc;
+        c->b_kc = p;
+        if ((rc = batch_dalloc(c, &p, kv))) return rc;
+        c->b_vc = p;
+        if ((rc = batch_dalloc(c, &c->b_state, kMaxStepRows))) return rc;
+        if ((rc = batch_dalloc(c, &c->b_cur, kMaxStepRows))) return rc;
+        if ((rc = batch_dalloc(c, &c->b_hist, static_cast<size_t>(kMaxStepRows) * c->hist_words()))) return rc;
+        if ((rc = batch_dalloc(c, &c->b_log, static_cast<size_t>(kMaxStepRows) * c->log_stride()))) return rc;
+        if ((rc = batch_dalloc(c, &c->b_lograw, static_cast<size_t>(kMaxStepRows) * c->log_stride()))) return rc;
+        if ((rc = batch_dalloc(c, &c->b_cnt, static_cast<size_t>(c->cfg.num_layers) * kMaxStepRows * kNumKVHeads)))
+            return rc;
+        HY_CUDA(cudaMemsetAsync(c->b_cnt, 0, sizeof(int) * c->cfg.num_layers * kMaxStepRows * kNumKVHeads, c->stream));
+        HY_CUDA(cudaMallocHost(reinterpret_cast<void**>(&c->h_bstate), sizeof(SlotState) * kMaxStepRows));
+    }
+    std::memset(c->h_bstate, 0, sizeof(SlotState) * kMaxStepRows);
+    HY_CUDA(cudaMemcpyAsync(c->b_state, c->h_bstate, sizeof(SlotState) * kMaxStepRows, cudaMemcpyHostToDevice, c->stream));
+    HY_CUDA(cudaMemsetAsync(c->b_cur, 0, sizeof(int) * kMaxStepRows, c->stream));
+    if (c->g_batch && c->b_rows == rows) return HY_OK;
+    if (c->g_batch) cudaGraphExecDestroy(c->g_batch);
+    c->g_batch = nullptr;
+    cudaGraph_t graph = nullptr;
+    HY_CUDA(cudaStreamSynchronize(c->stream));
+    HY_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    const cudaError_t e = enqueue_batch_step(c, rows);
+    const cudaError_t e2 = cudaStreamEndCapture(c->stream, &graph);
+    if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("batch graph capture: ") + cudaGetErrorString(e));
+    if (e2 != cudaSuccess) return fail(HY_ERR_CUDA, std::string("batch graph capture end: ") + cudaGetErrorString(e2));
+    const cudaError_t e3 = cudaGraphInstantiate(&c->g_batch, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e3 != cudaSuccess) return fail(HY_ERR_CUDA, std::string("batch graph instantiate: ") + cudaGetErrorString(e3));
+    c->b_rows = rows;
+    return HY_OK;
+}
+
+// ---------------------------------------------------------------------------
 // LM-head select with device-global scratch, allocating nothing.
 //
 // For callers that cannot allocate device memory while they decode: a host
@@ -2750,6 +2978,115 @@ int hy_run_vlm_dflash_with_prompt(hy_ctx* c, const int* input_ids, const int* po
     if (rc) return rc;
     return hy_dflash_generate(c, first, max_tokens, repetition_penalty, eos_ids, n_eos, tokens, n_tokens,
                               acceptance_lengths, n_blocks);
+}
+
+// ---- batched decode -----------------------------------------------------
+
+// Prefill request r into slot `slot`'s cache and make the slot decode it: the
+// context's own KV pointers are aimed at the slot for the prefill.
+static int batch_admit(hy_ctx* c, int slot, const hy_request& r, int max_tokens, float penalty, const int* eos_ids,
+                       int n_eos, bool* finished)
+{
+    if (r.seq_len <= 0 || r.seq_len > c->cfg.max_prefill || r.seq_len + max_tokens > c->cfg.max_context)
+        return fail(HY_ERR_CAPACITY, "request of " + std::to_string(r.seq_len) + " prompt rows + " +
+                                         std::to_string(max_tokens) + " tokens exceeds the context's capacity");
+    void* const kc0 = c->kc;
+    void* const vc0 = c->vc;
+    const int d_layers = c->d_layers;
+    const size_t off = static_cast<size_t>(slot) * c->slot_elems() * c->kv_elem();
+    c->kc = static_cast<char*>(c->b_kc) + off;
+    c->vc = static_cast<char*>(c->b_vc) + off;
+    c->d_layers = 0;   // slots keep no draft context
+    int first = 0, first_raw = 0;
+    int rc = prompt_prefill_first(c, r.input_ids, r.position_ids, r.seq_len, r.image_token_id, r.vision_features,
+                                  r.vision_token_count, penalty, &first, &first_raw);
+    c->kc = kc0;
+    c->vc = vc0;
+    c->d_layers = d_layers;
+    if (rc) return rc;
+    const int hw = c->hist_words();
+    unsigned* hist = c->b_hist + static_cast<size_t>(slot) * hw;
+    HY_CUDA(cudaMemcpyAsync(hist, c->hist, sizeof(unsigned) * hw, cudaMemcpyDeviceToDevice, c->stream));
+    HY_CUDA(cudaMemcpyAsync(c->b_cur + slot, &first, sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    hist_add_kernel<<<1, 256, 0, c->stream>>>(hist, c->b_cur + slot, 1, c->cfg.vocab_size);
+    HY_CUDA(cudaGetLastError());
+    const size_t lo = static_cast<size_t>(slot) * c->log_stride();
+    HY_CUDA(cudaMemcpyAsync(c->b_log + lo, &first, sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    HY_CUDA(cudaMemcpyAsync(c->b_lograw + lo, &first_raw, sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    bool first_eos = false;
+    for (int i = 0; i < n_eos; ++i) first_eos |= (eos_ids[i] == first);
+    SlotState& st = c->h_bstate[slot];
+    st.kv_len = r.seq_len;
+    st.n_gen = 1;
+    st.max_tokens = max_tokens;
+    st.active = (first_eos || max_tokens <= 1) ? 0 : 1;
+    HY_CUDA(cudaMemcpyAsync(c->b_state + slot, &st, sizeof(SlotState), cudaMemcpyHostToDevice, c->stream));
+    HY_CUDA(cudaStreamSynchronize(c->stream));
+    *finished = !st.active;
+    return HY_OK;
+}
+
+int hy_batch_decode(hy_ctx* c, const hy_request* requests, int n_requests, int slots, int max_tokens,
+                    float repetition_penalty, const int* eos_ids, int n_eos, int* tokens, int* n_tokens, int* status)
+{
+    if (!c || (n_requests > 0 && (!requests || !tokens || !n_tokens))) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    if (n_requests < 0) return fail(HY_ERR_INVALID_ARGUMENT, "n_requests must not be negative");
+    if (slots < 1 || slots > kMaxStepRows) return fail(HY_ERR_INVALID_ARGUMENT, "slots must be in 1..16");
+    if (max_tokens < 1 || max_tokens > c->cfg.max_tokens)
+        return fail(HY_ERR_CAPACITY, "max_tokens must be in 1..config max_tokens");
+    if (!std::isfinite(repetition_penalty) || repetition_penalty <= 0.f)
+        return fail(HY_ERR_INVALID_ARGUMENT, "repetition_penalty must be positive");
+    int rc = set_device(c);
+    if (rc) return rc;
+    if ((rc = set_eos(c, eos_ids, n_eos))) return rc;
+    c->h_st->penalty = repetition_penalty;
+    if ((rc = push_state(c))) return rc;
+    if ((rc = batch_prepare(c, slots))) return rc;
+    std::vector<int> owner(slots, -1);
+    auto finish = [&](int s) -> int {
+        const int r = owner[s];
+        const int n = c->h_bstate[s].n_gen;
+        HY_CUDA(cudaMemcpy(tokens + static_cast<size_t>(r) * max_tokens, c->b_log + static_cast<size_t>(s) * c->log_stride(),
+                           sizeof(int) * n, cudaMemcpyDeviceToHost));
+        n_tokens[r] = n;
+        if (status) status[r] = HY_OK;
+        owner[s] = -1;
+        return HY_OK;
+    };
+    int next = 0;
+    for (;;)
+    {
+        for (int s = 0; s < slots; ++s)
+            while (owner[s] < 0 && next < n_requests)
+            {
+                const int r = next++;
+                bool fin = false;
+                n_tokens[r] = 0;
+                rc = batch_admit(c, s, requests[r], max_tokens, repetition_penalty, eos_ids, n_eos, &fin);
+                if (rc == HY_ERR_INVALID_ARGUMENT || rc == HY_ERR_CAPACITY)
+                {
+                    // A malformed record fails alone (run_jsonl_batch writes an error record and goes on).
+                    if (status) status[r] = rc;
+                    continue;
+                }
+                if (rc) return rc;
+                owner[s] = r;
+                if (fin && (rc = finish(s))) return rc;
+            }
+        bool any = false;
+        for (int s = 0; s < slots; ++s) any |= owner[s] >= 0;
+        if (!any) break;
+        for (int i = 0; i < 4; ++i) HY_CUDA(cudaGraphLaunch(c->g_batch, c->stream));
+        HY_CUDA(cudaMemcpyAsync(c->h_bstate, c->b_state, sizeof(SlotState) * kMaxStepRows, cudaMemcpyDeviceToHost,
+                                c->stream));
+        if ((rc = check_device_error(c))) return rc;
+        for (int s = 0; s < slots; ++s)
+            if (owner[s] >= 0 && !c->h_bstate[s].active && (rc = finish(s))) return rc;
+    }
+    // The context's own sequence was used for the prompts' first tokens: leave it empty.
+    c->d_len = 0;
+    HY_CUDA(cudaMemsetAsync(c->hist, 0, sizeof(unsigned) * c->hist_words(), c->stream));
+    return set_length(c, 0);
 }
 
 int hy_attention(hy_ctx* c, int layer, const float* qkv, int rows, const float* cos, const float* sin, float* out)

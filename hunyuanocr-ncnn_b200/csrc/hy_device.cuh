@@ -59,6 +59,15 @@ struct DecodeState {
     int pad1;
 };
 
+// One sequence of a batched decode (hy_batch_decode): step row m decodes the
+// sequence in slot m, with its own KV cache, history bitmap and token log.
+struct SlotState {
+    int kv_len;       // rows in this slot's KV cache
+    int active;       // 1 while the slot decodes; 0: empty or finished
+    int n_gen;        // tokens in this slot's log
+    int max_tokens;
+};
+
 // ---------------------------------------------------------------------------
 // PTX wrappers.
 // ---------------------------------------------------------------------------

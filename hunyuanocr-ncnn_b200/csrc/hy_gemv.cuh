@@ -33,7 +33,9 @@ enum { EPI_STORE = 0, EPI_RESID = 1, EPI_ARGMAX = 2, EPI_ACT = 3 };   // EPI_ACT
 // SRC_GATHER_BLOCK: the DFlash draft's noise block [st->cur_token, mask_token x 15]
 // (build_dflash_block, src/dflash_runtime.cpp:20-25).
 enum { SRC_X = 0, SRC_GATHER_STATE = 1, SRC_GATHER_IDS = 2, SRC_GATHER_DRAFT = 3, SRC_GATHER_BLOCK = 4 };
-enum { LM_NONE = 0, LM_AR = 1, LM_VERIFY = 2 };
+// LM_BATCH: row m is the next token of the sequence in slot m (batched decode):
+// per-row history bitmaps, per-slot commit.
+enum { LM_NONE = 0, LM_AR = 1, LM_VERIFY = 2, LM_BATCH = 3 };
 
 constexpr int kGemvWarps = 8;
 constexpr int kGemvThreads = (kGemvWarps + 1) * 32;
@@ -79,6 +81,10 @@ struct GemvArgs {
     int* posterior_out;   // LM_VERIFY [16]
     float penalty;        // LM_NONE penalty (AR / verify read st->penalty)
     int* err;
+    SlotState* slots;     // LM_BATCH: per-row sequence state
+    int* slot_cur;        // LM_BATCH: each row's next token (the next step's gather ids)
+    int hist_stride;      // LM_BATCH: words between the rows' history bitmaps
+    int log_stride;       // LM_BATCH: token-log entries per row
     // M = 16 LM head: tensor map of the tied table (128-row x 128-byte boxes, 128-byte swizzle).
     CUtensorMap tmap;
 };
@@ -400,7 +406,8 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
     // M = 16 argmax: the penalty-history words of this CTA's rows, read once.
     constexpr int kHistWords16 = 64;
     __shared__ unsigned s_hist[(MT == 16 && EPI == EPI_ARGMAX) ? kHistWords16 : 1];
-    const bool hist_s_ok = (MT == 16 && EPI == EPI_ARGMAX) && R > 0 && ((r1 - 1) >> 5) - (r0 >> 5) < kHistWords16;
+    const bool hist_s_ok = (MT == 16 && EPI == EPI_ARGMAX) && a.hist_stride == 0 && R > 0 &&
+                           ((r1 - 1) >> 5) - (r0 >> 5) < kHistWords16;
     if (hist_s_ok && tid <= ((r1 - 1) >> 5) - (r0 >> 5)) s_hist[tid] = a.hist[(r0 >> 5) + tid];
     consumers_sync();
 
@@ -638,7 +645,9 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
             else
             {
                 if (a.logits) a.logits[static_cast<size_t>(m) * a.ldl + n] = v;
-                const unsigned hw = hist_s_ok ? s_hist[(n >> 5) - (r0 >> 5)] : a.hist[n >> 5];
+                const unsigned hw = a.hist_stride ? a.hist[static_cast<size_t>(m) * a.hist_stride + (n >> 5)]
+                                    : hist_s_ok     ? s_hist[(n >> 5) - (r0 >> 5)]
+                                                    : a.hist[n >> 5];
                 bool hit = (hw >> (n & 31)) & 1u;
                 for (int j = 0; j <= m; ++j) hit |= (s_prefix[j] == n);
                 const float ps = hit ? (v < 0.0f ? v * pen : v / pen) : v;
@@ -949,6 +958,26 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
         return;
     }
     DecodeState* st = a.st;
+    if (a.lm_mode == LM_BATCH)
+    {
+        // Per slot: log the token, extend the history and the KV length (this step
+        // appended the row), stop at EOS or the slot's max_tokens.
+        for (int m = 0; m < rows; ++m)
+        {
+            SlotState& ss = a.slots[m];
+            if (!ss.active) continue;
+            const int tok = __float_as_int(merged[m].w);
+            const int n = ss.n_gen;
+            a.log_tokens[static_cast<size_t>(m) * a.log_stride + n] = tok;
+            a.log_raw[static_cast<size_t>(m) * a.log_stride + n] = __float_as_int(merged[m].y);
+            ss.n_gen = n + 1;
+            ss.kv_len += 1;
+            a.slot_cur[m] = tok;
+            a.hist[static_cast<size_t>(m) * a.hist_stride + (tok >> 5)] |= 1u << (tok & 31);
+            if (is_eos(st, tok) || n + 1 >= ss.max_tokens) ss.active = 0;
+        }
+        return;
+    }
     if (st->done) return;
     if (a.lm_mode == LM_AR)
     {

@@ -290,6 +290,31 @@ int hy_run_vlm_decode_with_prompt(hy_ctx* ctx, const int* input_ids, const int* 
                                   int max_tokens, float repetition_penalty, const int* eos_ids, int n_eos,
                                   int* tokens, int* raw_top1, int* n_tokens);
 
+/* ---- batched decode (several requests on one GPU) --------------------- */
+/* One prompt of a JSONL batch record (the arguments of run_vlm_decode_with_prompt). */
+typedef struct hy_request {
+    const int* input_ids;          /* [seq_len] */
+    const int* position_ids;       /* [4 x seq_len], axis-major */
+    int seq_len;
+    int image_token_id;
+    const float* vision_features;  /* [vision_token_count x 1024] */
+    int vision_token_count;
+} hy_request;
+
+/* run_jsonl_batch's per-record decode (src/batch_jsonl.cpp:384-480: each record
+ * through run_vlm_decode_with_prompt, one after the other) with up to `slots`
+ * (1..16) records decoding together: each decode step advances every active
+ * record by one AR greedy token (16-row projections stream the weights once for
+ * all of them; attention, history, EOS and max_tokens are per record). A record
+ * enters a slot when one frees up (its prompt is prefilled into the slot's own
+ * KV cache). Each record's tokens equal hy_run_vlm_decode_with_prompt's for it.
+ * tokens [n_requests x max_tokens] (record r's at r * max_tokens), n_tokens
+ * [n_requests], status [n_requests] (nullable): a record whose prompt is
+ * malformed or too long gets its error status and no tokens, the others go on
+ * (run_jsonl_batch's error records). The context's own sequence is left empty. */
+int hy_batch_decode(hy_ctx* ctx, const hy_request* requests, int n_requests, int slots, int max_tokens,
+                    float repetition_penalty, const int* eos_ids, int n_eos, int* tokens, int* n_tokens, int* status);
+
 /* ---- standalone kernels (benchmarks and parity tests) ----------------- */
 /* Attention alone (PreciseSDPA decode/verify, src/precise_sdpa.cpp:281-329,
  * with the RoPE/QK-norm/append of export/text_decoder_kv.py:66-79): on layer

@@ -63,6 +63,37 @@ def test_single_process_matches_sequential_contract():
     assert merged[3].tokens == [3, 7]
 
 
+def test_batched_partition_matches_per_record_contract():
+    """Records decoded together (one infer_many call per rank) give the same output
+    records and summaries as one record at a time."""
+    b = _batch()
+    records = list(range(11))
+
+    def infer_many(recs):
+        out = []
+        for r in recs:
+            try:
+                out.append((True, _infer(r)))
+            except _Fail as exc:
+                out.append((False, str(exc)))
+        return out
+
+    for world in (1, 3):
+        parts, seq_parts = [], []
+        for rank in range(world):
+            o1, s1 = b.run_partition_batched(records, infer_many, world=world, rank=rank)
+            o2, s2 = b.run_partition(records, _infer, world=world, rank=rank)
+            assert (s1.total, s1.succeeded, s1.failed) == (s2.total, s2.succeeded, s2.failed)
+            parts.append(o1)
+            seq_parts.append(o2)
+        m1, t1 = b.merge_in_order(parts)
+        m2, t2 = b.merge_in_order(seq_parts)
+        assert [(r.index, r.ok, r.tokens) for r in m1] == [(r.index, r.ok, r.tokens) for r in m2]
+        assert (t1.total, t1.succeeded, t1.failed) == (11, 10, 1)
+    with pytest.raises(ValueError):
+        b.run_partition_batched(records, lambda recs: [], world=1, rank=0)
+
+
 def test_merge_rejects_duplicates():
     b = _batch()
     r = b.BatchRecord(1, "1", True, [1])
