@@ -235,6 +235,35 @@ def dflash_leg(pkg, local):
     return out
 
 
+def requests_leg(pkg, local, n_req: int = 16, n_tok: int = 512):
+    """Config 4 shape on this GPU: n_req records (prompt 1024 = 768 image rows + 256 text ids,
+    seeded by record index) x n_tok tokens, decoded together by hy_batch_decode (16 slots),
+    against the same records one at a time (hy_run_vlm_decode_with_prompt), wall-clocked."""
+    import torch
+    seq = PROMPT_GRID[0] * PROMPT_GRID[1] + PROMPT_TEXT
+    rt = pkg.TextRuntime.synthetic(seed=0, device=local, max_prefill=seq, max_tokens=n_tok + 64,
+                                   max_context=seq + n_tok + 64)
+    prompts = [prompt_arrays(seed=i) for i in range(n_req)]
+    reqs = [(ids, pos, img, feats) for ids, pos, feats, img in prompts]
+    rt.batch_decode(reqs[:2], 8)   # warm-up: slot buffers, step graph
+    torch.cuda.synchronize(local)
+    t0 = time.perf_counter()
+    toks, status = rt.batch_decode(reqs, n_tok)
+    dt_batch = time.perf_counter() - t0
+    assert all(s == 0 for s in status)
+    t0 = time.perf_counter()
+    single = [rt.run_vlm_decode_with_prompt(ids, pos, img, feats, max_tokens=n_tok).generated_tokens
+              for ids, pos, img, feats in reqs[:4]]
+    dt_single = (time.perf_counter() - t0) * n_req / 4
+    assert single == toks[:4], "batched tokens differ from the one-record tokens"
+    rt.close()
+    n_all = sum(len(t) for t in toks)
+    return {"records": n_req, "tokens_per_record": n_tok, "batched_tokens_per_s": round(n_all / dt_batch, 1),
+            "batched_requests_per_s": round(n_req / dt_batch, 3),
+            "one_at_a_time_tokens_per_s": round(n_all / dt_single, 1),
+            "note": "wall clock incl. prefills; one-at-a-time timed on 4 records"}
+
+
 def run_b200(args, world, rank, local):
     sys.path.insert(0, REPO)
     import __graft_entry__ as ge
@@ -307,6 +336,7 @@ def run_b200(args, world, rank, local):
     attn_ms = rt.bench_kernel(2, 50)
     rt.close()
     dflash = dflash_leg(pkg, local) if (world == 1 and not args.no_dflash) else None
+    requests = requests_leg(pkg, local) if (world == 1 and not args.no_requests) else None
     if rank != 0:
         return None
     cs = clocks.summary()
@@ -338,6 +368,7 @@ def run_b200(args, world, rank, local):
                       "attention_kv1024_q1": round(attn_ms * 1e3, 2),
                       "lm_head_m1_gbs": round(LM_HEAD_BYTES / (lm_ms / 1e3) / 1e9, 1)},
         "dflash": dflash,
+        "requests_config4_per_gpu": requests,
         "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "scope": "prefill + 256 tokens per call",
                 "ms_per_call": [round(t * 1e3, 1) for t in e2e_times], "clocks": e2e_clocks.summary(),
                 "h2d_bytes_per_step": int(ids.nbytes + pos.nbytes + feats.nbytes),
@@ -515,6 +546,7 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=144)   # ~10 s of oracle decode on the host
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-dflash", action="store_true")
+    ap.add_argument("--no-requests", action="store_true")
     ap.add_argument("--workload", choices=["decode", "requests"], default="decode",
                     help="decode: config 0 step (default); requests: config 4 request throughput")
     ap.add_argument("--requests", type=int, default=64)
