@@ -43,6 +43,11 @@
 
 namespace hy {
 
+// Back-off (ns) between polling rounds of the epoch words.
+#ifndef HY_POLL_NS
+#define HY_POLL_NS 32
+#endif
+
 constexpr int kMegaWarps = 6;                          // consumer warps
 constexpr int kMegaConsumers = kMegaWarps * 32;
 constexpr int kMegaThreads = kMegaConsumers + 32;      // + the producer warp
@@ -349,7 +354,7 @@ __device__ __forceinline__ bool poll_words(const unsigned long long* src, int n,
             ok = false;
             break;
         }
-        __nanosleep(32);
+        __nanosleep(HY_POLL_NS);
 #pragma unroll
         for (int u = 0; u < PER; ++u)
             if (static_cast<unsigned>(w[u] >> 32) != e) w[u] = ld_relaxed_u64(src + first + stride * u);
@@ -779,7 +784,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                                 redi[0] = 1;
                                 break;
                             }
-                            __nanosleep(32);
+                            __nanosleep(HY_POLL_NS);
                             w = ld_acquire_u64(a.tok_ep);
                         }
                         id = static_cast<int>(static_cast<unsigned>(w));
