@@ -43,9 +43,11 @@
 
 namespace hy {
 
-// Back-off (ns) between polling rounds of the epoch words.
+// Back-off (ns) between polling rounds of the epoch words. The exchanges are
+// latency-bound, not contended: at config 0 a 1 ns back-off gave 1638 tokens/s,
+// 32 ns 1610, 100 ns 1599, 250 ns 1579, 600 ns 1466 (device loop, KV 1024-1279).
 #ifndef HY_POLL_NS
-#define HY_POLL_NS 32
+#define HY_POLL_NS 1
 #endif
 
 constexpr int kMegaWarps = 6;                          // consumer warps

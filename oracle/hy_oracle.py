@@ -779,9 +779,11 @@ def draft_append_context(dw: DraftWeights, cache: DraftCache, aux: list, eps: fl
     cache.length = start + n
 
 
-def draft_forward(dw: DraftWeights, noise: np.ndarray, cache: DraftCache, eps: float = RMS_EPS) -> np.ndarray:
+def draft_forward(dw: DraftWeights, noise: np.ndarray, cache: DraftCache, eps: float = RMS_EPS,
+                  kv_round: bool = False) -> np.ndarray:
     """The draft graph for the 16 noise rows over the cached context; returns the
-    final-normed hidden rows [16, 1024]."""
+    final-normed hidden rows [16, 1024]. kv_round: the noise rows' keys and values
+    are rounded to bf16 as a bf16 draft cache stores them."""
     m = noise.shape[0]
     ctx = cache.length
     cos, sin = build_dflash_rope(ctx, m, True), build_dflash_rope(ctx, m, False)
@@ -794,6 +796,8 @@ def draft_forward(dw: DraftWeights, noise: np.ndarray, cache: DraftCache, eps: f
         v = (a @ lw.v.T).reshape(m, NUM_KV_HEADS, HEAD_DIM).transpose(1, 0, 2)
         q = apply_rope(rms_norm(q, lw.q_norm, eps), cos, sin)
         k = apply_rope(rms_norm(k, lw.k_norm, eps), cos, sin)
+        if kv_round:
+            k, v = round_bf16(k), round_bf16(v)
         K = np.concatenate([cache.k[li][:, :ctx], k], axis=1)
         V = np.concatenate([cache.v[li][:, :ctx], v], axis=1)
         att = precise_sdpa(q, K, V, mask, DRAFT_SCALE).transpose(1, 0, 2).reshape(m, Q_WIDTH)

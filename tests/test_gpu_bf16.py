@@ -71,3 +71,36 @@ def test_bf16_dflash_is_lossless(bf16, oracle):
     out = rt.dflash_generate_synthetic(first, 64, 1.08, ar.generated_tokens, 0.7, seed=5)
     assert out.generated_tokens == ar.generated_tokens[:len(out.generated_tokens)]
     assert len(out.generated_tokens) == 64
+
+
+def test_bf16_batched_decode_matches_rounded_oracle(bf16, oracle):
+    """hy_batch_decode on the bf16 variant: every record's tokens equal the rounded
+    oracle's AR decode of that record alone."""
+    cfg, w, rt = bf16
+    prompts = [oracle.synthetic_prompt(300 + i, 2 + i % 3, 4, 10 + 7 * i, cfg.vocab, cfg.vocab - 3) for i in range(5)]
+    toks, status = rt.batch_decode([(p.input_ids, p.position_ids, p.image_token_id, p.vision_features)
+                                    for p in prompts], 24, slots=4)
+    assert status == [0] * len(prompts)
+    for p, got in zip(prompts, toks):
+        assert got == oracle.decode_ar(w, cfg, p, 24).tokens
+
+
+def test_bf16_draft_run_matches_rounded_oracle(pkg, oracle):
+    """The DFlash draft network with bf16 draft weights and bf16 draft K/V against the
+    oracle with the same roundings (weights rounded at load; the oracle's draft cache
+    rounds its K/V rows to bf16 as the device cache stores them)."""
+    dw = oracle.make_draft_weights(2, 19, 0.02, NORM_STD, bf16=True)
+    rng = np.random.default_rng(9)
+    aux = rng.standard_normal((4, 40, 1024)).astype(np.float32)
+    noise = rng.standard_normal((16, 1024)).astype(np.float32)
+    with pkg.TextRuntime.synthetic(seed=1, device=0, **dict(SMALL, max_context=256)) as rt:
+        rt.load_draft_synthetic(2, 19, 0.02, NORM_STD, 4095)
+        rt.draft_context_append(aux)
+        got = rt.draft_run(noise)
+    cache = oracle.DraftCache.empty(2, 56)
+    oracle.draft_append_context(dw, cache, list(aux))
+    for li in range(2):
+        cache.k[li] = oracle.round_bf16(cache.k[li])
+        cache.v[li] = oracle.round_bf16(cache.v[li])
+    want = oracle.draft_forward(dw, noise, cache, kv_round=True)
+    np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
