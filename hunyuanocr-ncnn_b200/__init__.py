@@ -16,7 +16,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 
 import numpy as np
 
@@ -48,7 +48,7 @@ EXPORTED_SYMBOLS = (
     "hy_ctx_set_ar_path", "hy_ctx_ar_path", "hy_trace_persistent", "hy_debug_progress",
     "hy_lm_head_select_noalloc", "hy_draft_load", "hy_draft_load_synthetic", "hy_draft_context_length",
     "hy_draft_context_append", "hy_draft_run", "hy_draft_propose", "hy_dflash_generate",
-    "hy_run_vlm_dflash_with_prompt", "hy_batch_decode",
+    "hy_run_vlm_dflash_with_prompt", "hy_batch_decode", "hy_fixture_meta", "hy_fixture_load",
 )
 DFLASH_MASK_TOKEN = 120817
 AR_PATH_PERSISTENT = 0
@@ -148,6 +148,9 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "hy_trace_persistent": ([_P, _I, _I, _P], _I),
         "hy_draft_load": ([_P, ctypes.POINTER(_DraftWeights)], _I),
         "hy_batch_decode": ([_P, ctypes.POINTER(_Request), _I, _I, _I, _F, _P, _I, _P, _P, _P], _I),
+        "hy_fixture_meta": ([ctypes.c_char_p, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I),
+                             ctypes.POINTER(_I)], _I),
+        "hy_fixture_load": ([ctypes.c_char_p, _P, _P, _P, _P], _I),
         "hy_draft_load_synthetic": ([_P, _I, _I, ctypes.c_uint64, _F, _F], _I),
         "hy_draft_context_length": ([_P, ctypes.POINTER(_I)], _I),
         "hy_draft_context_append": ([_P, _P, _I], _I),
@@ -218,6 +221,12 @@ class TextDecodeResult:
     repetition_penalty: float
     generated_tokens: list
     raw_top1_tokens: list
+    checked_tokens: int = 0
+    expected_tokens: list = field(default_factory=list)
+
+    def matches_expected(self) -> bool:
+        """TextDecodeResult::matches_expected (src/text_runtime.cpp:1788-1791)."""
+        return self.generated_tokens == self.expected_tokens
 
 
 @dataclass
@@ -228,6 +237,56 @@ class DFlashDecodeResult:
     drafted_token_count: int
     accepted_draft_token_count: int
     acceptance_lengths: list
+    expected_tokens: list = field(default_factory=list)
+
+    def matches_expected(self) -> bool:
+        return self.generated_tokens == self.expected_tokens
+
+
+@dataclass
+class VlmFixture:
+    """VlmFixtureInputs + vision features (src/text_runtime.cpp:278-381): one regression
+    fixture directory (meta.txt, input_ids.i32, position_ids.i32, expected_tokens.i32,
+    vision_features.f32)."""
+    seq_len: int
+    image_token_id: int
+    vision_token_count: int
+    input_ids: np.ndarray
+    position_ids: np.ndarray
+    expected_tokens: np.ndarray
+    vision_features: np.ndarray | None
+
+
+def read_vlm_fixture(fixture_dir: str, with_features: bool = True) -> VlmFixture:
+    """load_vlm_fixture_with_features through the library's host reader (the reference's
+    sizes, checks and messages: "failed to open", "short read", "unexpected extra bytes")."""
+    lib = load_library()
+    d = os.fsencode(fixture_dir)
+    seq, exp, img, vis = ctypes.c_int(), ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    _check(lib.hy_fixture_meta(d, ctypes.byref(seq), ctypes.byref(exp), ctypes.byref(img), ctypes.byref(vis)))
+    ids = np.empty(seq.value, np.int32)
+    pos = np.empty((4, seq.value), np.int32)
+    expected = np.empty(exp.value, np.int32)
+    feats = np.empty((vis.value, HIDDEN), np.float32) if with_features else None
+    _check(lib.hy_fixture_load(d, _ptr(ids), _ptr(pos), _ptr(expected), _ptr(feats)))
+    return VlmFixture(seq.value, img.value, vis.value, ids, pos, expected, feats)
+
+
+def write_vlm_fixture(fixture_dir: str, input_ids, position_ids, image_token_id: int, vision_features,
+                      expected_tokens) -> None:
+    """Writes a fixture directory in the reference's format (tools/prepare_regression_fixtures.py:
+    little-endian int32 / float32 arrays and meta.txt with the four sizes)."""
+    os.makedirs(fixture_dir, exist_ok=True)
+    ids = _i32(input_ids).reshape(-1)
+    feats = _f32(vision_features).reshape(-1, HIDDEN)
+    exp = _i32(expected_tokens).reshape(-1)
+    ids.astype("<i4").tofile(os.path.join(fixture_dir, "input_ids.i32"))
+    _i32(position_ids).reshape(4, ids.size).astype("<i4").tofile(os.path.join(fixture_dir, "position_ids.i32"))
+    exp.astype("<i4").tofile(os.path.join(fixture_dir, "expected_tokens.i32"))
+    feats.astype("<f4").tofile(os.path.join(fixture_dir, "vision_features.f32"))
+    with open(os.path.join(fixture_dir, "meta.txt"), "w") as f:
+        f.write(f"seq_len={ids.size}\nexpected_token_count={exp.size}\nimage_token_id={int(image_token_id)}\n"
+                f"vision_token_count={feats.shape[0]}\n")
 
 
 class TextRuntime:
@@ -533,6 +592,33 @@ class TextRuntime:
         accl = acc[:nb.value].tolist()
         return DFlashDecodeResult(tokens[:n.value].tolist(), nb.value, nb.value * (DFLASH_BLOCK - 1),
                                   int(sum(accl)), accl)
+
+    # -- regression fixtures ---------------------------------------------------
+    @staticmethod
+    def _checked(max_tokens: int, expected) -> int:
+        # decode_from_embeddings (src/text_runtime.cpp:1341-1350): with expected tokens,
+        # max_tokens <= 0 or past their count means all of them.
+        n = len(expected)
+        return n if (max_tokens <= 0 or max_tokens > n) else max_tokens
+
+    def run_vlm_fixture_decode(self, fixture_dir: str, max_tokens: int = 0, eos_ids=()) -> TextDecodeResult:
+        """TextRuntime::run_vlm_fixture_decode (src/text_runtime.cpp:1793-1837), penalty 1.08."""
+        fx = read_vlm_fixture(fixture_dir)
+        n = self._checked(max_tokens, fx.expected_tokens)
+        res = self.run_vlm_decode_with_prompt(fx.input_ids, fx.position_ids, fx.image_token_id, fx.vision_features,
+                                              max_tokens=n, eos_ids=eos_ids)
+        res.checked_tokens = n
+        res.expected_tokens = fx.expected_tokens[:n].tolist()
+        return res
+
+    def run_vlm_fixture_dflash_decode(self, fixture_dir: str, max_tokens: int = 0, eos_ids=()) -> DFlashDecodeResult:
+        """TextRuntime::run_vlm_fixture_dflash_decode (src/text_runtime.cpp:1886-1920), penalty 1.08."""
+        fx = read_vlm_fixture(fixture_dir)
+        n = self._checked(max_tokens, fx.expected_tokens)
+        res = self.run_vlm_dflash_with_prompt(fx.input_ids, fx.position_ids, fx.image_token_id, fx.vision_features,
+                                              max_tokens=n, eos_ids=eos_ids)
+        res.expected_tokens = fx.expected_tokens[:n].tolist()
+        return res
 
     # -- timing hooks --------------------------------------------------------
     def bench_ar_steps(self, count: int) -> float:

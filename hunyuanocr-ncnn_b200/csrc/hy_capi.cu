@@ -15,10 +15,12 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cerrno>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <fstream>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -1851,6 +1853,9 @@ int draft_alloc(hy_ctx* c, int layers, int mask_token)
     if ((rc = draft_dalloc(c, &c->d_pf_a_hi, static_cast<size_t>(c->pf_pad) * kAuxWidth))) return rc;
     if ((rc = draft_dalloc(c, &c->d_pf_a_lo, static_cast<size_t>(c->pf_pad) * kAuxWidth))) return rc;
     if ((rc = draft_dalloc(c, &c->d_pf_fc, static_cast<size_t>(c->pf_rows) * kHidden))) return rc;
+    // Aux columns of layers a shallow decoder does not have stay zero (finite drafts).
+    HY_CUDA(cudaMemsetAsync(c->d_aux, 0, sizeof(float) * kBlock * kAuxWidth, c->stream));
+    HY_CUDA(cudaMemsetAsync(c->d_pf_aux, 0, sizeof(float) * c->pf_rows * kAuxWidth, c->stream));
     // build_dflash_rope (src/dflash_runtime.cpp:27-48) in the reference's float arithmetic.
     std::vector<float> cs(rows * kHeadDim), sn(rows * kHeadDim);
     for (size_t pos = 0; pos < rows; ++pos)
@@ -3087,6 +3092,84 @@ int hy_batch_decode(hy_ctx* c, const hy_request* requests, int n_requests, int s
     c->d_len = 0;
     HY_CUDA(cudaMemsetAsync(c->hist, 0, sizeof(unsigned) * c->hist_words(), c->stream));
     return set_length(c, 0);
+}
+
+// ---- regression fixtures (host only) -------------------------------------
+
+// parse_vlm_fixture_meta (src/text_runtime.cpp:285-321): key=value lines.
+static int fixture_meta(const std::string& dir, int* seq_len, int* expected, int* image_token, int* vision)
+{
+    const std::string path = dir + "/meta.txt";
+    std::ifstream f(path);
+    if (!f.is_open()) return fail(HY_ERR_INVALID_ARGUMENT, "failed to open fixture meta: " + path);
+    int m[4] = {0, 0, -1, 0};
+    const char* keys[4] = {"seq_len", "expected_token_count", "image_token_id", "vision_token_count"};
+    std::string line;
+    while (std::getline(f, line))
+    {
+        if (line.empty()) continue;
+        const size_t eq = line.find('=');
+        if (eq == std::string::npos) continue;
+        const std::string key = line.substr(0, eq), value = line.substr(eq + 1);
+        for (int i = 0; i < 4; ++i)
+        {
+            if (key != keys[i]) continue;
+            char* end = nullptr;
+            errno = 0;
+            const long v = std::strtol(value.c_str(), &end, 10);
+            if (end == value.c_str() || errno != 0 || v < -2147483647L || v > 2147483647L)
+                return fail(HY_ERR_INVALID_ARGUMENT, "invalid fixture meta value: " + line);
+            m[i] = static_cast<int>(v);
+        }
+    }
+    if (m[0] <= 0 || m[1] <= 0 || m[2] < 0 || m[3] <= 0)
+        return fail(HY_ERR_INVALID_ARGUMENT,
+                    "vlm fixture meta must define positive seq_len, expected_token_count, image_token_id, and "
+                    "vision_token_count");
+    *seq_len = m[0];
+    *expected = m[1];
+    *image_token = m[2];
+    *vision = m[3];
+    return HY_OK;
+}
+
+// read_binary_vector (src/text_runtime.cpp:253-276): exactly `count` elements, no extra bytes.
+static int fixture_vector(const std::string& path, size_t count, size_t elem, void* out)
+{
+    std::ifstream f(path, std::ios::binary);
+    if (!f.is_open()) return fail(HY_ERR_INVALID_ARGUMENT, "failed to open: " + path);
+    f.read(static_cast<char*>(out), static_cast<std::streamsize>(count * elem));
+    if (f.gcount() != static_cast<std::streamsize>(count * elem)) return fail(HY_ERR_INVALID_ARGUMENT, "short read: " + path);
+    char extra = 0;
+    if (f.read(&extra, 1)) return fail(HY_ERR_INVALID_ARGUMENT, "unexpected extra bytes: " + path);
+    return HY_OK;
+}
+
+int hy_fixture_meta(const char* fixture_dir, int* seq_len, int* expected_token_count, int* image_token_id,
+                    int* vision_token_count)
+{
+    if (!fixture_dir || !seq_len || !expected_token_count || !image_token_id || !vision_token_count)
+        return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    return fixture_meta(fixture_dir, seq_len, expected_token_count, image_token_id, vision_token_count);
+}
+
+int hy_fixture_load(const char* fixture_dir, int* input_ids, int* position_ids, int* expected_tokens,
+                    float* vision_features)
+{
+    if (!fixture_dir || !input_ids || !position_ids || !expected_tokens) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    int seq = 0, expected = 0, image = 0, vision = 0;
+    int rc = fixture_meta(fixture_dir, &seq, &expected, &image, &vision);
+    if (rc) return rc;
+    const std::string root(fixture_dir);
+    if ((rc = fixture_vector(root + "/input_ids.i32", seq, sizeof(int), input_ids))) return rc;
+    if ((rc = fixture_vector(root + "/position_ids.i32", static_cast<size_t>(seq) * 4, sizeof(int), position_ids)))
+        return rc;
+    if ((rc = fixture_vector(root + "/expected_tokens.i32", expected, sizeof(int), expected_tokens))) return rc;
+    if (vision_features &&
+        (rc = fixture_vector(root + "/vision_features.f32", static_cast<size_t>(vision) * kHidden, sizeof(float),
+                             vision_features)))
+        return rc;
+    return HY_OK;
 }
 
 int hy_attention(hy_ctx* c, int layer, const float* qkv, int rows, const float* cos, const float* sin, float* out)

@@ -315,6 +315,22 @@ typedef struct hy_request {
 int hy_batch_decode(hy_ctx* ctx, const hy_request* requests, int n_requests, int slots, int max_tokens,
                     float repetition_penalty, const int* eos_ids, int n_eos, int* tokens, int* n_tokens, int* status);
 
+/* ---- regression fixtures (host code, no device work) ------------------ */
+/* parse_vlm_fixture_meta (src/text_runtime.cpp:285-321): `fixture_dir`/meta.txt
+ * (key=value lines: seq_len, expected_token_count, image_token_id,
+ * vision_token_count; all must be present and positive, image_token_id >= 0). */
+int hy_fixture_meta(const char* fixture_dir, int* seq_len, int* expected_token_count, int* image_token_id,
+                    int* vision_token_count);
+/* load_vlm_fixture_with_features (src/text_runtime.cpp:334-381): input_ids.i32
+ * [seq_len], position_ids.i32 [4 x seq_len], expected_tokens.i32
+ * [expected_token_count] and vision_features.f32 [vision_token_count x 1024]
+ * (skipped when vision_features is NULL), each exactly that size ("short read",
+ * "unexpected extra bytes" otherwise). Sizes come from meta.txt. The fixture
+ * runs through hy_run_vlm_decode_with_prompt / hy_run_vlm_dflash_with_prompt
+ * (TextRuntime::run_vlm_fixture_decode / run_vlm_fixture_dflash_decode). */
+int hy_fixture_load(const char* fixture_dir, int* input_ids, int* position_ids, int* expected_tokens,
+                    float* vision_features);
+
 /* ---- standalone kernels (benchmarks and parity tests) ----------------- */
 /* Attention alone (PreciseSDPA decode/verify, src/precise_sdpa.cpp:281-329,
  * with the RoPE/QK-norm/append of export/text_decoder_kv.py:66-79): on layer
