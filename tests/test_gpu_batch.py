@@ -72,3 +72,24 @@ def test_malformed_record_fails_alone(pkg, model, oracle):
     assert status[0] == status[2] == 0
     assert toks[0] == oracle.decode_ar(w, cfg, prompts[0], 12).tokens
     assert toks[2] == oracle.decode_ar(w, cfg, prompts[2], 12).tokens
+
+
+def test_batch_edge_cases(pkg, model, oracle):
+    """No records; more slots than records; a record whose first token is EOS or whose
+    max_tokens is 1 finishes at admission; bad arguments are rejected."""
+    cfg, w, rt = model
+    assert rt.batch_decode([], 8) == ([], [])
+    prompts = _prompts(oracle, 2)
+    want = [oracle.decode_ar(w, cfg, p, 6).tokens for p in prompts]
+    toks, status = rt.batch_decode([_req(p) for p in prompts], 6, slots=16)
+    assert status == [0, 0] and toks == want
+    toks, _ = rt.batch_decode([_req(p) for p in prompts], 1, slots=2)
+    assert toks == [t[:1] for t in want]
+    toks, _ = rt.batch_decode([_req(p) for p in prompts], 6, slots=2, eos_ids=[want[0][0]])
+    assert toks[0] == want[0][:1]
+    with pytest.raises(pkg.HyError) as e:
+        rt.batch_decode([_req(prompts[0])], 6, slots=17)
+    assert e.value.status == pkg.HY_ERR_INVALID_ARGUMENT
+    with pytest.raises(pkg.HyError) as e:
+        rt.batch_decode([_req(prompts[0])], CFG["max_tokens"] + 1)
+    assert e.value.status == pkg.HY_ERR_CAPACITY
