@@ -2024,7 +2024,10 @@ int draft_upload(hy_ctx* c, const hy_draft_weights* w)
 // log, history, KV length, EOS / max_tokens). Prompts are prefilled into their
 // slot's cache by the ordinary prefill when a slot frees up.
 // ---------------------------------------------------------------------------
-constexpr int kBatchSplits = 4;   // 3 past-key splits + the new-row split per (row, KV head)
+#ifndef HY_BATCH_SPLITS
+#define HY_BATCH_SPLITS 4
+#endif
+constexpr int kBatchSplits = HY_BATCH_SPLITS;   // past-key splits + the new-row split per (row, KV head)
 
 template <typename T>
 int batch_dalloc(hy_ctx* c, T** p, size_t count)
