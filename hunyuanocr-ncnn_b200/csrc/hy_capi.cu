@@ -2024,10 +2024,12 @@ int draft_upload(hy_ctx* c, const hy_draft_weights* w)
 // log, history, KV length, EOS / max_tokens). Prompts are prefilled into their
 // slot's cache by the ordinary prefill when a slot frees up.
 // ---------------------------------------------------------------------------
+// Past-key splits + the new-row split per (record, KV head) of the batched attention.
+// 16 records x 256 tokens at KV 1024..1280: 3 -> 2.19 ms per step, 4 -> 2.24, 6 -> 2.31, 9 -> 2.41.
 #ifndef HY_BATCH_SPLITS
-#define HY_BATCH_SPLITS 4
+#define HY_BATCH_SPLITS 3
 #endif
-constexpr int kBatchSplits = HY_BATCH_SPLITS;   // past-key splits + the new-row split per (row, KV head)
+constexpr int kBatchSplits = HY_BATCH_SPLITS;
 
 template <typename T>
 int batch_dalloc(hy_ctx* c, T** p, size_t count)
