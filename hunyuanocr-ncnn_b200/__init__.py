@@ -49,7 +49,9 @@ EXPORTED_SYMBOLS = (
     "hy_lm_head_select_noalloc", "hy_draft_load", "hy_draft_load_synthetic", "hy_draft_context_length",
     "hy_draft_context_append", "hy_draft_run", "hy_draft_propose", "hy_dflash_generate",
     "hy_run_vlm_dflash_with_prompt", "hy_batch_decode", "hy_fixture_meta", "hy_fixture_load",
+    "hy_ctx_set_token_callback",
 )
+TOKEN_CALLBACK = ctypes.CFUNCTYPE(None, ctypes.c_int, ctypes.c_void_p)
 DFLASH_MASK_TOKEN = 120817
 AR_PATH_PERSISTENT = 0
 AR_PATH_GRAPH = 1
@@ -151,6 +153,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "hy_fixture_meta": ([ctypes.c_char_p, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I),
                              ctypes.POINTER(_I)], _I),
         "hy_fixture_load": ([ctypes.c_char_p, _P, _P, _P, _P], _I),
+        "hy_ctx_set_token_callback": ([_P, TOKEN_CALLBACK, _P, _I], _I),
         "hy_draft_load_synthetic": ([_P, _I, _I, ctypes.c_uint64, _F, _F], _I),
         "hy_draft_context_length": ([_P, ctypes.POINTER(_I)], _I),
         "hy_draft_context_append": ([_P, _P, _I], _I),
@@ -347,6 +350,11 @@ class TextRuntime:
 
     def __exit__(self, *exc):
         self.close()
+
+    def set_token_callback(self, fn, tokens_per_sync: int = 0) -> None:
+        """stream_callback: fn(token) for every committed token, in order (None removes it)."""
+        self._cb = TOKEN_CALLBACK(lambda tok, _user: fn(int(tok))) if fn is not None else TOKEN_CALLBACK()
+        _check(_LIB.hy_ctx_set_token_callback(self._ctx, self._cb, None, tokens_per_sync))
 
     @property
     def ar_path(self) -> int:

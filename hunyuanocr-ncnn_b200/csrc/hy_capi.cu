@@ -199,6 +199,12 @@ struct hy_ctx {
     int* b_cnt = nullptr;                    // [layers][16][8] attention tickets
     std::vector<void*> b_allocs;
     cudaGraphExec_t g_batch = nullptr;
+    // Streaming: called with each committed token, in order, when the host reads
+    // the decode state (every `cb_sync` AR tokens, every 4 DFlash blocks).
+    hy_token_callback cb = nullptr;
+    void* cb_user = nullptr;
+    int cb_sync = 0;
+    int cb_emitted = 0;     // tokens of the current generation already passed to cb
     int hist_words() const { return (cfg.vocab_size + 31) / 32; }
     int log_stride() const { return cfg.max_tokens + 2 * kBlock; }
     size_t slot_elems() const { return static_cast<size_t>(cfg.num_layers) * kNumKVHeads * cfg.max_context * kHeadDim; }
@@ -2283,6 +2289,17 @@ cudaError_t enqueue_lm_select_scratch_t(hy_ctx* c, int rows, const float* x, flo
     return run_gemv<WT, kHidden, MT, PRO_PLAIN, EPI_ARGMAX>(c, lm);
 }
 
+// Pass the tokens committed since the last call, log entries [cb_emitted, n), to the callback.
+int emit_tokens(hy_ctx* c, int n)
+{
+    if (!c->cb || n <= c->cb_emitted) return HY_OK;
+    std::vector<int> t(static_cast<size_t>(n - c->cb_emitted));
+    HY_CUDA(cudaMemcpy(t.data(), c->log_tokens + c->cb_emitted, sizeof(int) * t.size(), cudaMemcpyDeviceToHost));
+    c->cb_emitted = n;
+    for (int tok : t) c->cb(tok, c->cb_user);
+    return HY_OK;
+}
+
 }  // namespace
 
 // ===========================================================================
@@ -2378,6 +2395,17 @@ int hy_build_mrope(const int* position_ids, int seq_len, int use_cos, float* out
 }
 
 float hy_rope_value(int position, int dim, int use_cos) { return rope_value_host(position, dim, use_cos != 0); }
+
+int hy_ctx_set_token_callback(hy_ctx* c, hy_token_callback cb, void* user, int tokens_per_sync)
+{
+    if (!c) return fail(HY_ERR_INVALID_ARGUMENT, "ctx is null");
+    if (tokens_per_sync < 0 || tokens_per_sync > kMegaChunk)
+        return fail(HY_ERR_INVALID_ARGUMENT, "tokens_per_sync must be in 0.." + std::to_string(kMegaChunk));
+    c->cb = cb;
+    c->cb_user = user;
+    c->cb_sync = tokens_per_sync ? tokens_per_sync : kMegaChunk;
+    return HY_OK;
+}
 
 int hy_ctx_set_ar_path(hy_ctx* c, int path)
 {
@@ -2638,12 +2666,15 @@ int hy_generate(hy_ctx* c, int first_token, int first_raw_top1, int max_tokens, 
     HY_CUDA(cudaMemcpyAsync(c->log_tokens, &first_token, sizeof(int), cudaMemcpyHostToDevice, c->stream));
     HY_CUDA(cudaMemcpyAsync(c->log_raw, &first_raw_top1, sizeof(int), cudaMemcpyHostToDevice, c->stream));
     if ((rc = history_upload(c, &first_token, 1, false))) return rc;
+    c->cb_emitted = 0;
+    if ((rc = emit_tokens(c, 1))) return rc;
+    const int chunk = c->cb ? c->cb_sync : kMegaChunk;
     int launched_steps = 0;
     while (!h.done && launched_steps < max_tokens - 1)
     {
         if (c->ar_path == HY_AR_PATH_PERSISTENT)
         {
-            const int n = std::min(kMegaChunk, max_tokens - 1 - launched_steps);
+            const int n = std::min(chunk, max_tokens - 1 - launched_steps);
             cudaError_t e = launch_mega(c, n);
             if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("persistent decode launch: ") + cudaGetErrorString(e));
             launched_steps += n;
@@ -2658,9 +2689,12 @@ int hy_generate(hy_ctx* c, int first_token, int first_raw_top1, int max_tokens, 
         }
         if ((rc = sync_state_to_host(c))) return rc;
         if (h.kv_len + 0 > c->cfg.max_context) return fail(HY_ERR_CAPACITY, "KV capacity exceeded");
+        if (c->cb && (rc = check_device_error(c)) == HY_OK) rc = emit_tokens(c, h.n_gen);
+        if (rc) return rc;
     }
     if ((rc = check_device_error(c))) return rc;
     if ((rc = sync_state_to_host(c))) return rc;
+    if ((rc = emit_tokens(c, h.n_gen))) return rc;
     *n_tokens = h.n_gen;
     if (tokens) HY_CUDA(cudaMemcpy(tokens, c->log_tokens, sizeof(int) * h.n_gen, cudaMemcpyDeviceToHost));
     if (raw_top1) HY_CUDA(cudaMemcpy(raw_top1, c->log_raw, sizeof(int) * h.n_gen, cudaMemcpyDeviceToHost));
@@ -2732,14 +2766,18 @@ int hy_dflash_generate_synthetic(hy_ctx* c, int first_token, int max_tokens, flo
     h.draft_base = synth_base(seed, kTidDrafts);
     if ((rc = push_state(c))) return rc;
     int launched = 0;
+    c->cb_emitted = 0;
     while (!h.done && launched < max_tokens)
     {
         for (int i = 0; i < 4 && launched < max_tokens; ++i, ++launched)
             HY_CUDA(cudaGraphLaunch(c->g_verify_draft, c->stream));
         if ((rc = sync_state_to_host(c))) return rc;
+        if (c->cb && (rc = check_device_error(c)) == HY_OK) rc = emit_tokens(c, h.n_gen);
+        if (rc) return rc;
     }
     if ((rc = check_device_error(c))) return rc;
     if ((rc = sync_state_to_host(c))) return rc;
+    if ((rc = emit_tokens(c, h.n_gen))) return rc;
     *n_tokens = h.n_gen;
     if (n_blocks) *n_blocks = h.block_count;
     if (tokens) HY_CUDA(cudaMemcpy(tokens, c->log_tokens, sizeof(int) * h.n_gen, cudaMemcpyDeviceToHost));
@@ -2957,13 +2995,17 @@ int hy_dflash_generate(hy_ctx* c, int first_token, int max_tokens, float penalty
     h.block_count = 0;
     if ((rc = push_state(c))) return rc;
     int launched = 0;
+    c->cb_emitted = 0;
     while (!h.done && launched < max_tokens)
     {
         for (int i = 0; i < 4 && launched < max_tokens; ++i, ++launched) HY_CUDA(cudaGraphLaunch(c->g_dflash, c->stream));
         if ((rc = sync_state_to_host(c))) return rc;
+        if (c->cb && (rc = check_device_error(c)) == HY_OK) rc = emit_tokens(c, h.n_gen);
+        if (rc) return rc;
     }
     if ((rc = check_device_error(c))) return rc;
     if ((rc = sync_state_to_host(c))) return rc;
+    if ((rc = emit_tokens(c, h.n_gen))) return rc;
     c->d_len = c->kv_len;
     *n_tokens = h.n_gen;
     if (n_blocks) *n_blocks = h.block_count;

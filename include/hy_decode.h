@@ -119,6 +119,17 @@ void hy_ctx_destroy(hy_ctx* ctx);
 enum hy_ar_path { HY_AR_PATH_PERSISTENT = 0, HY_AR_PATH_GRAPH = 1 };
 int hy_ctx_set_ar_path(hy_ctx* ctx, int path);
 int hy_ctx_ar_path(const hy_ctx* ctx);
+/* Streaming (InferenceRequest::stream_callback, include/hunyuan_ocr/hunyuan_ocr.h:43-45,
+ * and the TextTokenCallback of run_vlm_decode_with_prompt, text_runtime.h:21, 126-143):
+ * callback(token, user) is called on the calling thread, in order, once for every
+ * committed token of hy_generate, hy_dflash_generate(_synthetic) and the
+ * hy_run_vlm_*_with_prompt calls (the first token included). The library calls it
+ * when it reads the decode state: after every `tokens_per_sync` AR tokens (1..64,
+ * 0 = 64; smaller values mean more launches of the persistent kernel) and after
+ * every 4 DFlash blocks, so tokens arrive in small groups rather than one by one.
+ * NULL removes the callback. */
+typedef void (*hy_token_callback)(int token, void* user);
+int hy_ctx_set_token_callback(hy_ctx* ctx, hy_token_callback callback, void* user, int tokens_per_sync);
 /* Per-phase trace of the persistent kernel (the counterpart of the reference's
  * stage timers, include/hunyuan_ocr/text_runtime.h:32-39): runs `tokens` AR
  * steps from the current state and, for CTAs 0..3 during token `trace_token`,
