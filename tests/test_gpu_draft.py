@@ -109,6 +109,38 @@ def test_draft_propose_matches_oracle(deep, oracle):
         assert sure.sum() >= 12
 
 
+def test_decoder_steps_extend_the_draft_context(deep, oracle):
+    """Explicit decoder steps (1 row, then 5 rows) on a prefilled sequence also append
+    their rows' draft context; the drafts then match the oracle's over the same context."""
+    cfg, w, dw, rt, prompt = deep
+    seq = prompt.input_ids.shape[0]
+    emb = oracle.prepare_prompt_embeddings(w, prompt)
+    rt.reset()
+    rt.prefill(emb, oracle.build_mrope(prompt.position_ids, seq, True),
+               oracle.build_mrope(prompt.position_ids, seq, False))
+    _, cache, aux = oracle.prefill(w, cfg, prompt, seq + 64, aux=True)
+    dcache = oracle.DraftCache.empty(DRAFT_LAYERS, seq + 64)
+    oracle.draft_append_context(dw, dcache, aux, cfg.rms_eps)
+    past = seq
+    for ids in ([7], [8, 9, 10, 11, 12]):
+        n = len(ids)
+        x = w.embed[np.asarray(ids)]
+        cos, sin = oracle.rope_rows(past, n, True), oracle.rope_rows(past, n, False)
+        rt.run_decoder_step(x, cos, sin)
+        col = np.arange(past + n)[None, :]
+        mask = np.where(col > past + np.arange(n)[:, None], np.float32(-1e38), np.float32(0)).astype(np.float32)
+        _, step_aux = oracle.decoder_forward(w, cfg, x, mask, cos, sin, cache, aux=True)
+        oracle.draft_append_context(dw, dcache, step_aux, cfg.rms_eps)
+        past += n
+    assert rt.draft_context_length == rt.kv_length == past
+    got = rt.draft_propose(33)
+    want, hidden = oracle.draft_propose(w, dw, dcache, 33, cfg.rms_eps, MASK)
+    top2 = np.sort(oracle.lm_head(w, hidden[1:]), axis=1)[:, -2:]
+    sure = (top2[:, 1] - top2[:, 0]) > 1e-3
+    assert [a for a, s_ in zip(got[1:], sure) if s_] == [b for b, s_ in zip(want[1:], sure) if s_]
+    assert sure.sum() >= 12
+
+
 def test_dflash_with_draft_is_lossless_and_matches_oracle(deep, oracle):
     """--dflash end to end on the device: tokens equal the AR greedy tokens (the
     lossless invariant, tests/hunyuan_ocr_runtime_integration_test.cpp:138-139),
