@@ -180,6 +180,28 @@ def device_ms(rt, fn):
     return e0.elapsed_time(e1), out
 
 
+def bf16_leg(pkg, local, seq: int, n_tok: int = GEN_TOKENS):
+    """The bf16 variant at config 0 (bf16 weights and KV cache, fp32 activations and
+    accumulation): device-timed AR decode of n_tok - 1 tokens from KV length seq, and its
+    roofline (bf16 weights + bf16 KV rows per token)."""
+    rt = pkg.TextRuntime.synthetic(seed=0, device=local, max_prefill=64, max_tokens=n_tok + 64,
+                                   max_context=seq + n_tok + 64, weight_dtype=pkg.DTYPE_BF16,
+                                   kv_dtype=pkg.DTYPE_BF16)
+    best = None
+    for _ in range(3):
+        rt.set_length(seq)
+        rt.set_history(list(range(1, 257)))
+        ms, _ = device_ms(rt, lambda: rt.bench_ar_steps(n_tok - 1))
+        best = ms if best is None else min(best, ms)
+    rt.close()
+    mean_past = seq + (n_tok - 2) / 2.0
+    bpt = (DECODER_WEIGHT_BYTES + LM_HEAD_BYTES) / 2 + (mean_past + 1) * KV_ROW_BYTES / 2 + HIDDEN * 4
+    peak, _ = measured_peaks()
+    tps = (n_tok - 1) / (best / 1e3)
+    return {"tokens_per_s": round(tps, 1), "bytes_per_token": round(bpt),
+            "roofline_frac": round(tps * bpt / 1e9 / peak, 4), "roofline_tokens_per_s": round(peak * 1e9 / bpt, 1)}
+
+
 def dflash_leg(pkg, local):
     """DFlash (config 3): KV length 2048, block 16, synthetic drafts equal to the greedy token
     with probability p, repeated for 256 committed tokens; tokens/s per p, device-timed."""
@@ -336,6 +358,7 @@ def run_b200(args, world, rank, local):
     attn_ms = rt.bench_kernel(2, 50)
     rt.close()
     dflash = dflash_leg(pkg, local) if (world == 1 and not args.no_dflash) else None
+    bf16 = bf16_leg(pkg, local, seq) if world == 1 else None
     requests = requests_leg(pkg, local) if (world == 1 and not args.no_requests) else None
     if rank != 0:
         return None
@@ -367,6 +390,7 @@ def run_b200(args, world, rank, local):
         "kernel_us": {"lm_head_m1": round(lm_ms * 1e3, 2), "gate_up_gemv_m1": round(gu_ms * 1e3, 2),
                       "attention_kv1024_q1": round(attn_ms * 1e3, 2),
                       "lm_head_m1_gbs": round(LM_HEAD_BYTES / (lm_ms / 1e3) / 1e9, 1)},
+        "ar_bf16": bf16,
         "dflash": dflash,
         "requests_config4_per_gpu": requests,
         "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "scope": "prefill + 256 tokens per call",
