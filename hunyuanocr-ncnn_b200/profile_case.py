@@ -29,12 +29,15 @@ def main(argv=None):
     ap.add_argument("--path", choices=["persistent", "graph"], default="persistent")
     ap.add_argument("--dtype", choices=["f32", "bf16"], default="f32", help="weight and KV dtype")
     ap.add_argument("--draft-layers", type=int, default=5, help="draft mode: DFlash draft depth")
-    ap.add_argument("--kernel", choices=["decode", "lm", "gate_up", "attention", "verify", "prefill", "draft"],
+    ap.add_argument("--records", type=int, default=16, help="batch mode: records decoding together")
+    ap.add_argument("--kernel", choices=["decode", "lm", "gate_up", "attention", "verify", "prefill", "draft",
+                                         "batch"],
                     default="decode",
                     help="decode: AR launches; lm / gate_up / attention: the M=1 kernels alone "
                          "(hy_bench_kernel); verify: DFlash verify blocks (16-row kernels); "
                          "prefill: prompt prefill of --past rows (tcgen05 GEMMs, prefill attention); "
-                         "draft: DFlash blocks with a synthetic draft network over a --past-row context")
+                         "draft: DFlash blocks with a synthetic draft network over a --past-row context; "
+                         "batch: --records prompts of --past rows decoded together (hy_batch_decode)")
     args = ap.parse_args(argv)
 
     import __graft_entry__ as ge
@@ -60,6 +63,26 @@ def main(argv=None):
             rt.prefill(emb, cos, sin)
             dt_ms = (time.perf_counter() - t0) * 1e3
         print(f"prefill {args.dtype} layers={args.layers} vocab={args.vocab} rows={rows}: {dt_ms:.2f} ms per call (wall)")
+        rt.close()
+        return
+    if args.kernel == "batch":
+        import numpy as np
+
+        rt = pkg.TextRuntime.synthetic(seed=0, num_layers=args.layers, vocab_size=args.vocab, max_prefill=args.past,
+                                       max_tokens=args.tokens + 8, max_context=args.past + args.tokens + 8,
+                                       weight_dtype=dt, kv_dtype=dt)
+        rng = np.random.default_rng(0)
+        img = args.vocab - 3
+        reqs = []
+        for _ in range(args.records):
+            ids = rng.integers(0, args.vocab - 3, args.past).astype(np.int32)
+            ids[:16] = img
+            pos = np.tile(np.arange(args.past, dtype=np.int32), (4, 1))
+            reqs.append((ids, pos, img, rng.standard_normal((16, 1024)).astype(np.float32)))
+        for _ in range(args.calls):
+            toks, _ = rt.batch_decode(reqs, args.tokens)
+        print(f"batch {args.dtype} layers={args.layers} vocab={args.vocab} prompt={args.past} "
+              f"records={args.records}: {len(toks[0])} tokens per record")
         rt.close()
         return
     rt = pkg.TextRuntime.synthetic(seed=0, num_layers=args.layers, vocab_size=args.vocab, max_prefill=64,
