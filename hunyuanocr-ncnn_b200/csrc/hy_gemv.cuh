@@ -243,6 +243,27 @@ __device__ __forceinline__ int draft_id(const DecodeState* st, const int* greedy
     return static_cast<int>((h & 0xFFFFFFFFull) % static_cast<unsigned long long>(vocab));
 }
 
+// The elements of a 16-byte chunk as floats (4 fp32 or 8 bf16, little-endian lanes).
+template <typename WT>
+__device__ __forceinline__ void unpack_chunk(const uint4& c, float* out)
+{
+    const unsigned w[4] = {c.x, c.y, c.z, c.w};
+    if constexpr (sizeof(WT) == 4)
+    {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) out[i] = __uint_as_float(w[i]);
+    }
+    else
+    {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+        {
+            out[2 * i] = __uint_as_float(w[i] << 16);
+            out[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+        }
+    }
+}
+
 template <typename WT, int KP, int MT, int PRO, int EPI>
 __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(const __grid_constant__ GemvArgs a)
 {
@@ -707,12 +728,40 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
 #pragma unroll
                         for (int i = 0; i < 3; ++i) acc3[h][i][0] = acc3[h][i][1] = acc3[h][i][2] = acc3[h][i][3] = 0.f;
                 }
-                const float* x0 = xs + g8 * XP + kc * S::TL_KC + t4;
+                // The tile's k order is permuted so that each thread's operands are
+                // contiguous: in k-step kk, logical k = t4 is column t4 * SPAN + 2 kk and
+                // logical k = t4 + 4 is the column after it (A and B alike, so the sum
+                // over k is unchanged). A thread then reads its SPAN activation columns of
+                // rows g8 and g8 + 8 and its SPAN weights of each tile row with 16-byte loads
+                // (the weights are two swizzled 16-byte chunks, 2 t4 and 2 t4 + 1).
+                constexpr int NKK = S::TL_KC / 8;   // k-steps per tile
+                constexpr int SPAN = 2 * NKK;       // columns per thread
+                const float* x0 = xs + g8 * XP + kc * S::TL_KC + t4 * SPAN;
                 const float* x1 = x0 + 8 * XP;
+                float xv0[SPAN], xv1[SPAN];
 #pragma unroll
-                for (int kk = 0; kk < S::TL_KC / 8; ++kk)
+                for (int i = 0; i < SPAN; i += 4)
                 {
-                    const float xa[4] = {x0[8 * kk], x1[8 * kk], x0[8 * kk + 4], x1[8 * kk + 4]};
+                    const float4 u0 = *reinterpret_cast<const float4*>(x0 + i);
+                    const float4 u1 = *reinterpret_cast<const float4*>(x1 + i);
+                    xv0[i] = u0.x; xv0[i + 1] = u0.y; xv0[i + 2] = u0.z; xv0[i + 3] = u0.w;
+                    xv1[i] = u1.x; xv1[i + 1] = u1.y; xv1[i + 2] = u1.z; xv1[i + 3] = u1.w;
+                }
+                float wv[2][SPAN];
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+                {
+                    const int r = 16 * warp + 8 * h + g8;   // tile row; r & 7 == g8
+                    const unsigned char* trow = ring + slot * S::TL_TILE + r * 128;
+                    const uint4 c0 = *reinterpret_cast<const uint4*>(trow + (((2 * t4) ^ g8) << 4));
+                    const uint4 c1 = *reinterpret_cast<const uint4*>(trow + (((2 * t4 + 1) ^ g8) << 4));
+                    unpack_chunk<WT>(c0, wv[h]);
+                    unpack_chunk<WT>(c1, wv[h] + SPAN / 2);
+                }
+#pragma unroll
+                for (int kk = 0; kk < NKK; ++kk)
+                {
+                    const float xa[4] = {xv0[2 * kk], xv1[2 * kk], xv0[2 * kk + 1], xv1[2 * kk + 1]};
                     unsigned ah[4], al[4];
 #pragma unroll
                     for (int i = 0; i < 4; ++i)
@@ -720,16 +769,10 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
                         ah[i] = tf32_head(xa[i]);
                         al[i] = __float_as_uint(xa[i] - __uint_as_float(ah[i]));
                     }
-                    const int k = 8 * kk + t4;
-                    constexpr int ES = static_cast<int>(sizeof(WT));
-                    const int b0 = k * ES, b1 = (k + 4) * ES;
 #pragma unroll
                     for (int h = 0; h < 2; ++h)
                     {
-                        const int r = 16 * warp + 8 * h + g8;   // tile row; r & 7 == g8
-                        const unsigned char* trow = ring + slot * S::TL_TILE + r * 128;
-                        const float w0 = to_f32<WT>(*reinterpret_cast<const WT*>(trow + ((((b0 >> 4) ^ g8) << 4) | (b0 & 15))));
-                        const float w1 = to_f32<WT>(*reinterpret_cast<const WT*>(trow + ((((b1 >> 4) ^ g8) << 4) | (b1 & 15))));
+                        const float w0 = wv[h][2 * kk], w1 = wv[h][2 * kk + 1];
                         const unsigned bh0 = tf32_head(w0), bh1 = tf32_head(w1);
                         mma_tf32(acc3[h][0], al, bh0, bh1);
                         if constexpr (!W_EXACT)
