@@ -23,7 +23,6 @@
 #pragma once
 
 #include "hy_device.cuh"
-#include "hy_umma.cuh"
 
 #include <cuda.h>   // CUtensorMap (the map is encoded on the host through the driver entry point)
 
@@ -150,22 +149,11 @@ struct GemvShape<WT, KP, 16> {
     static constexpr int TL_ROWS = 128;
     static constexpr int TL_KC = 128 / static_cast<int>(sizeof(WT));   // columns per tile
     static constexpr int TL_TILE = TL_ROWS * 128;
-    static constexpr int TL_NST = 3;
-    // tcgen05 operands of one tile, in the UMMA K-major no-swizzle layout (blocks of
-    // 8 rows x 16 columns, 512 bytes; hy_umma.cuh): the weight tile's hi (and, for fp32
-    // weights, lo) planes [128 rows x TL_KC], the activations' hi / lo [16 x TL_KC].
-    // Two such buffers: the split of tile i + 1 overlaps the MMAs of tile i.
-    static constexpr int TL_WPL = (sizeof(WT) == 4) ? 2 : 1;
-    static constexpr int TL_WPLANE = TL_ROWS * TL_KC * 4;
-    static constexpr int TL_XPLANE = 16 * TL_KC * 4;
-    static constexpr int TL_SPLIT = TL_WPL * TL_WPLANE + 2 * TL_XPLANE;
-    static constexpr int TL_SPLIT_OFF = XS_BYTES + 1024 + TL_NST * TL_TILE;
-    static constexpr int TL_WSCR_OFF = TL_SPLIT_OFF + 2 * TL_SPLIT;
+    static constexpr int TL_NST = 8;
+    static constexpr int TL_WSCR_OFF = XS_BYTES + 1024 + TL_NST * TL_TILE;
     static constexpr int TL_BAR_OFF = TL_WSCR_OFF + WSCR_BYTES;
-    static constexpr int TL_NBAR = 2 * TL_NST + 8;   // full, empty; split full / empty; accumulator full / empty
-    static constexpr int TL_RED_OFF = TL_BAR_OFF + TL_NBAR * 8;
+    static constexpr int TL_RED_OFF = TL_BAR_OFF + 2 * TL_NST * 8;
     static constexpr int SMEM_TL = TL_RED_OFF + RED_BYTES;
-    static_assert(TL_SPLIT_OFF % 16 == 0 && TL_SPLIT % 16 == 0, "UMMA operands are 16-byte aligned");
     static_assert(KP != 1024 || SMEM_TL <= 227 * 1024, "LM head tile ring (the LM head has K = 1024)");
     // Names the generic code refers to.
     static constexpr int RPW = 8, SEG = ROWB, SPS = 8, GPS = 1, KC16 = KC;
