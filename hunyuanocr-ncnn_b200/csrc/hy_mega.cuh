@@ -50,11 +50,19 @@ namespace hy {
 #define HY_POLL_NS 1
 #endif
 
-constexpr int kMegaWarps = 6;                          // consumer warps
+// Consumer warps. A CTA's share of the q/k/v, o and down phases is 4-7 stages
+// (28 rows of 4 KB at 4 rows per stage; 7 rows of 8 KB at 2; 7 rows of 14 KB at
+// 1): 7 warps take each of them in one round, 6 needed two.
+#ifndef HY_MEGA_WARPS
+#define HY_MEGA_WARPS 7
+#endif
+constexpr int kMegaWarps = HY_MEGA_WARPS;
 constexpr int kMegaConsumers = kMegaWarps * 32;
 constexpr int kMegaThreads = kMegaConsumers + 32;      // + the producer warp
 constexpr int kMegaStage = 16384;        // bytes per slot
-constexpr int kMegaSlots = 2;            // slots per warp
+// Ring slots, shared by the consumer warps: global stage g lands in slot
+// g % kMegaSlots (its use g / kMegaSlots) and is consumed by warp g % kMegaWarps.
+constexpr int kMegaSlots = 12;
 constexpr int kMegaSplits = 18;          // per KV head: 17 splits of the past rows + the new-row split (144 CTAs)
 constexpr int kMegaMaxK = 3584;
 constexpr int kMegaHistWords = 64;       // LM rows per CTA <= 32 * 62
@@ -119,8 +127,8 @@ constexpr int kTraceCtas = 4;
 constexpr int kTraceSlots = 12;
 
 struct MegaSmem {
-    static constexpr int RING = 0;                                          // [warp][slot] x 16 KB
-    static constexpr int XS = RING + kMegaWarps * kMegaSlots * kMegaStage;  // [3584] f32 activation vector
+    static constexpr int RING = 0;                                          // [slot] x 16 KB
+    static constexpr int XS = RING + kMegaSlots * kMegaStage;               // [3584] f32 activation vector
     // Attention phases do not use the activation vector; their buffers alias it.
     static constexpr int QS = XS;                                           // [2][128]
     static constexpr int NEWKV = QS + 2 * kHeadDim * 4;                     // k[128], v[128]
@@ -130,10 +138,14 @@ struct MegaSmem {
     static constexpr int PARTS = MINE + 2 * kPartStride * 4;                // [8 splits][2][130] polled partials
     static constexpr int XS_END = PARTS + (kMegaSplits - 1) * 2 * kAttnWords * 4;
     static constexpr int RED = (XS_END > XS + kMegaMaxK * 4 ? XS_END : XS + kMegaMaxK * 4);   // 64 float4 + 64 ints
-    static constexpr int BARS = RED + 64 * 16 + 64 * 4;                     // full[warp][slot], empty[warp][slot]
-    static constexpr int TOKBAR = BARS + 2 * kMegaWarps * kMegaSlots * 8;  // token-start mbarrier
+    static constexpr int BARS = RED + 64 * 16 + 64 * 4;                     // full[slot], empty[slot]
+    static constexpr int TOKBAR = BARS + 2 * kMegaSlots * 8;                // token-start mbarrier
     static constexpr int SIZE = TOKBAR + 8;
 };
+// Dynamic shared memory plus the kernel's static arrays (plan tables, history
+// words, residual rows) must fit one SM's 227 KB, or the occupancy check
+// turns the persistent path off.
+static_assert(MegaSmem::SIZE + 4096 <= 227 * 1024, "persistent decode shared memory exceeds 227 KB");
 
 enum { PH_QKV = 0, PH_ATTN = 1, PH_O = 2, PH_GU = 3, PH_DOWN = 4, PH_LM = 5 };
 
@@ -475,7 +487,7 @@ __device__ __forceinline__ void rope_norm_vec_cg(const float* x, const float* c,
 // Named barrier of the consumer warps (the producer warp never joins it).
 __device__ __forceinline__ void mega_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kMegaConsumers) : "memory"); }
 
-// xs = w * x for a 1024-vector x given as float4 i = tid + 192 u in v[u];
+// xs = w * x for a 1024-vector x given as float4 i = tid + kMegaConsumers u in v[u];
 // returns 1/sqrt(mean(x^2)+eps) after one CTA barrier. The GEMV multiplies its
 // dot products by it, i.e. the RMSNorm's per-row scale is applied after the projection.
 __device__ __forceinline__ float mega_load_normed(float* xs, const float4 v[2], const float* w, float eps,
@@ -507,10 +519,10 @@ __device__ __forceinline__ float mega_load_normed(float* xs, const float4 v[2], 
     return 1.0f / sqrtf(t / static_cast<float>(kHidden) + eps);
 }
 
-// xs = w * x for a 1024-vector x given as x[tid + 192 u] in v[u] (u < 6);
+// xs = w * x for a 1024-vector x given as x[tid + kMegaConsumers u] in v[u] (u < kXPer);
 // returns 1/sqrt(mean(x^2)+eps) after one consumer barrier (the GEMV applies
 // the RMSNorm's per-row scale to its dot products).
-constexpr int kXPer = (kHidden + kMegaConsumers - 1) / kMegaConsumers;   // 6
+constexpr int kXPer = (kHidden + kMegaConsumers - 1) / kMegaConsumers;
 
 __device__ __forceinline__ float mega_load_normed_s(float* xs, const float (&v)[kXPer], const float* w, float eps,
                                                     float* s_norm, int tid)
@@ -625,8 +637,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
     float* pbuf_all = reinterpret_cast<float*>(smem + MegaSmem::PBUF);
     float4* red4 = reinterpret_cast<float4*>(smem + MegaSmem::RED);
     int* redi = reinterpret_cast<int*>(red4 + 64);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + MegaSmem::BARS);   // [warp][slot]
-    uint64_t* empty = full + kMegaWarps * kMegaSlots;                      // [warp][slot]
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + MegaSmem::BARS);   // [slot]
+    uint64_t* empty = full + kMegaSlots;                                   // [slot]
     // Completes once per token t >= 1 when the consumers have acquired the
     // previous token's commit; the producer waits on it before streaming the
     // token's K/V rows, whose newest row the previous token wrote.
@@ -644,7 +656,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
 
     if (tid == 0)
     {
-        for (int s = 0; s < kMegaWarps * kMegaSlots; ++s)
+        for (int s = 0; s < kMegaSlots; ++s)
         {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
@@ -661,7 +673,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
         // ======================= producer =======================
         if (lane != 0) return;
         const uint64_t pol = l2_evict_first_policy();
-        unsigned g = 0;   // global stage index: owner warp g % 6, its stage number g / 6
+        unsigned g = 0;   // global stage index: slot g % kMegaSlots, owner warp g % kMegaWarps
         bool ok = true;
         for (int t = 0; t < a.steps && ok; ++t)
         {
@@ -678,11 +690,10 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                 }
                 for (int i = 0; i < p.nstage; ++i, ++g)
                 {
-                    const int w = g % kMegaWarps;
-                    const unsigned j = g / kMegaWarps;
-                    const int s = w * kMegaSlots + static_cast<int>(j % kMegaSlots);
-                    // The owner released this slot's previous stage (j - kMegaSlots).
-                    if (j >= kMegaSlots && !mbar_wait(&empty[s], ((j / kMegaSlots) - 1) & 1, a.err, kErrTimeoutEmpty))
+                    const int s = static_cast<int>(g % kMegaSlots);
+                    const unsigned j = g / kMegaSlots;   // use of the slot
+                    // The slot's previous stage (g - kMegaSlots) was released by its warp.
+                    if (j >= 1 && !mbar_wait(&empty[s], (j - 1) & 1, a.err, kErrTimeoutEmpty))
                     {
                         ok = false;
                         break;
@@ -706,30 +717,30 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                 }
             }
         }
-        // Drain: the last kMegaSlots stages of every warp (earlier ones landed
-        // before their slot was released).
-        const unsigned tail = kMegaWarps * kMegaSlots;
-        for (unsigned gg = (g > tail ? g - tail : 0); gg < g; ++gg)
-        {
-            const unsigned j = gg / kMegaWarps;
-            mbar_wait(&full[(gg % kMegaWarps) * kMegaSlots + j % kMegaSlots], (j / kMegaSlots) & 1, a.err,
-                      kErrTimeoutFull);
-        }
+        // Drain: the last kMegaSlots stages (earlier ones landed before their
+        // slot was released).
+        for (unsigned gg = (g > kMegaSlots ? g - kMegaSlots : 0); gg < g; ++gg)
+            mbar_wait(&full[gg % kMegaSlots], (gg / kMegaSlots) & 1, a.err, kErrTimeoutFull);
         return;
     }
 
     // ======================= consumers =======================
-    uint64_t* myfull = full + warp * kMegaSlots;
-    uint64_t* myempty = empty + warp * kMegaSlots;
-    const unsigned char* myring = ring + static_cast<size_t>(warp) * kMegaSlots * kMegaStage;
-    unsigned consumed = 0;   // this warp's stages consumed so far
-    // Wait for the next own stage; its slot, or -1 on timeout. Each wait is on
-    // the barrier's next phase: the producer refills a slot only after the
-    // warp released it (parity waits are exact one phase ahead).
-    auto wait_own = [&]() -> int {
-        const int slot = consumed % kMegaSlots;
-        const bool okw = mbar_wait(&myfull[slot], (consumed / kMegaSlots) & 1, a.err, kErrTimeoutFull);
-        ++consumed;
+    // Wait for global stage g (one of this warp's); its slot, or -1 on timeout.
+    // A parity wait is exact only on the barrier's current phase or the one
+    // just completed, and the slot's previous stage g - kMegaSlots belongs to
+    // another warp, which may not have received (or released) it yet - copies
+    // issued earlier can land later. So the warp first waits until that stage
+    // was released (empty phase j - 1), then for stage g itself (full phase j).
+    // Both waits start at most one phase early: if g - kMegaSlots is in this
+    // phase, so is this warp's previous stage g - kMegaWarps, whose issue needed
+    // g - kMegaSlots issued and so g - 2 kMegaSlots released; if it is in an
+    // earlier phase, the phase-end barrier saw it released. A released stage
+    // has landed, and no use after j can start before this warp releases g.
+    auto wait_stage = [&](unsigned g) -> int {
+        const int slot = static_cast<int>(g % kMegaSlots);
+        const unsigned j = g / kMegaSlots;
+        bool okw = (j == 0) || mbar_wait(&empty[slot], (j - 1) & 1, a.err, kErrTimeoutEmpty);
+        okw = okw && mbar_wait(&full[slot], j & 1, a.err, kErrTimeoutFull);
         return __all_sync(0xffffffffu, okw) ? slot : -1;
     };
 
@@ -756,7 +767,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
             long long wwait = 0, wwork = 0, wn = 0;
             const MegaPlan p = mega_plan<KT>(a, tb, layer, kind, past, b);
             const float* lnorm = a.norms + static_cast<size_t>(layer) * 2304;
-            // This warp's stages of the phase: first, first + 6, ...
+            // This warp's stages of the phase: first, first + kMegaWarps, ...
             const int first = static_cast<int>((warp - static_cast<int>(gs % kMegaWarps) + kMegaWarps) % kMegaWarps);
 
             // ---------------- prologue: wait for and stage the activation vector ----------------
@@ -875,7 +886,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                 for (int i = first; i < p.nstage && !bad; i += kMegaWarps)
                 {
                     const long long c0 = wtr ? clock64() : 0;
-                    const int slot = wait_own();
+                    const int slot = wait_stage(gs + static_cast<unsigned>(i));
                     const long long c1 = wtr ? clock64() : 0;
                     if (slot < 0)
                     {
@@ -883,17 +894,17 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                         bad = true;
                         break;
                     }
-                    const WT* rows = reinterpret_cast<const WT*>(myring + slot * kMegaStage);
+                    const WT* rows = reinterpret_cast<const WT*>(ring + slot * kMegaStage);
                     const int q0 = i * p.per_stage;
                     if (p.K == kHidden)
                         gemv_stage<WT, kHidden, true>(a, p, kind, rows, xr, xs, q0, rinv, eo, xres_s, hist_s, pen, best,
-                                                      &myempty[slot], lane, b, ph);
+                                                      &empty[slot], lane, b, ph);
                     else if (p.K == kQWidth)
                         gemv_stage<WT, kQWidth, false>(a, p, kind, rows, xr, xs, q0, rinv, eo, xres_s, hist_s, pen, best,
-                                                       &myempty[slot], lane, b, ph);
+                                                       &empty[slot], lane, b, ph);
                     else
                         gemv_stage<WT, kMegaMaxK, false>(a, p, kind, rows, xr, xs, q0, rinv, eo, xres_s, hist_s, pen,
-                                                         best, &myempty[slot], lane, b, ph);
+                                                         best, &empty[slot], lane, b, ph);
                     if (wtr)
                     {
                         wwait += c1 - c0;
@@ -1135,7 +1146,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                 for (int i = first; i < p.nstage && !bad; i += kMegaWarps)
                 {
                     const long long c0 = atr ? clock64() : 0;
-                    const int slot = wait_own();
+                    const int slot = wait_stage(gs + static_cast<unsigned>(i));
                     const long long c1 = atr ? clock64() : 0;
                     if (slot < 0)
                     {
@@ -1143,14 +1154,14 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                         bad = true;
                         break;
                     }
-                    const KT* kst = reinterpret_cast<const KT*>(myring + slot * kMegaStage);
+                    const KT* kst = reinterpret_cast<const KT*>(ring + slot * kMegaStage);
                     const KT* vst = kst + static_cast<size_t>(p.per_stage) * kHeadDim;
                     const int n = min(p.per_stage, p.count - i * p.per_stage);
                     for (int h = 0; h < n; h += 16)
                         block16(kst + static_cast<size_t>(h) * kHeadDim, vst + static_cast<size_t>(h) * kHeadDim,
                                 min(16, n - h));
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&myempty[slot]);
+                    if (lane == 0) mbar_arrive(&empty[slot]);
                     if (atr)
                     {
                         await_ += c1 - c0;

@@ -31,13 +31,15 @@ def main(argv=None):
     ap.add_argument("--draft-layers", type=int, default=5, help="draft mode: DFlash draft depth")
     ap.add_argument("--records", type=int, default=16, help="batch mode: records decoding together")
     ap.add_argument("--kernel", choices=["decode", "lm", "gate_up", "attention", "verify", "prefill", "draft",
-                                         "batch"],
+                                         "batch", "trace"],
                     default="decode",
                     help="decode: AR launches; lm / gate_up / attention: the M=1 kernels alone "
                          "(hy_bench_kernel); verify: DFlash verify blocks (16-row kernels); "
                          "prefill: prompt prefill of --past rows (tcgen05 GEMMs, prefill attention); "
                          "draft: DFlash blocks with a synthetic draft network over a --past-row context; "
-                         "batch: --records prompts of --past rows decoded together (hy_batch_decode)")
+                         "batch: --records prompts of --past rows decoded together (hy_batch_decode); "
+                         "trace: per-phase timeline of the middle token of a --tokens launch of the "
+                         "persistent kernel (hy_trace_persistent), averaged over the layers for CTA 0")
     args = ap.parse_args(argv)
 
     import __graft_entry__ as ge
@@ -89,6 +91,29 @@ def main(argv=None):
                                    max_tokens=args.tokens + 40, max_context=args.past + args.tokens + 40,
                                    weight_dtype=dt, kv_dtype=dt)
     rt.ar_path = pkg.AR_PATH_PERSISTENT if args.path == "persistent" else pkg.AR_PATH_GRAPH
+    if args.kernel == "trace":
+        import numpy as np
+
+        rt.set_length(args.past)
+        rt.set_history([1, 2, 3])
+        tr = rt.trace_persistent(args.tokens, args.tokens // 2).astype(np.int64)
+        c0 = tr[0]
+        names = ["q/k/v", "attention", "o_proj", "gate/up", "down_proj"]
+        L = args.layers
+        print(f"trace layers={L} vocab={args.vocab} past={args.past} tokens={args.tokens} token={args.tokens // 2}: "
+              f"token time {(c0[-1, 3] - c0[0, 0]) / 1e3:.1f} us (CTA 0)")
+        print("phase        duration_us  inputs_ready_after_us  work_after_us")
+        for k, name in enumerate(names):
+            rows = c0[k:5 * L:5]
+            dur, ready = (rows[:, 3] - rows[:, 0]) / 1e3, (rows[:, 1] - rows[:, 0]) / 1e3
+            print(f"{name:<12} {dur.mean():11.2f} {ready.mean():22.2f} {(dur - ready).mean():14.2f}")
+        lm = c0[5 * L]
+        print(f"{'LM head':<12} {(lm[3] - lm[0]) / 1e3:11.2f} {(lm[1] - lm[0]) / 1e3:22.2f} "
+              f"{(lm[3] - lm[1]) / 1e3:14.2f}")
+        spread = (tr[:, :5 * L, 1].max(axis=0) - tr[:, :5 * L, 1].min(axis=0)) / 1e3
+        print(f"inputs-ready spread over CTAs 0-3: mean {spread.mean():.2f} us, max {spread.max():.2f} us")
+        rt.close()
+        return
     if args.kernel in ("lm", "gate_up", "attention"):
         rt.set_length(args.past)
         which = {"lm": 0, "gate_up": 1, "attention": 2}[args.kernel]
