@@ -123,7 +123,10 @@ struct MegaArgs {
     unsigned epoch_base;
 };
 
-constexpr int kTraceCtas = 4;
+#ifndef HY_TRACE_CTAS
+#define HY_TRACE_CTAS 4
+#endif
+constexpr int kTraceCtas = HY_TRACE_CTAS;   // CTAs 0 .. kTraceCtas - 1 are traced
 constexpr int kTraceSlots = 12;
 
 struct MegaSmem {
