@@ -63,7 +63,10 @@ constexpr int kMegaStage = 16384;        // bytes per slot
 // Ring slots, shared by the consumer warps: global stage g lands in slot
 // g % kMegaSlots (its use g / kMegaSlots) and is consumed by warp g % kMegaWarps.
 constexpr int kMegaSlots = 12;
-constexpr int kMegaSplits = 18;          // per KV head: 17 splits of the past rows + the new-row split (144 CTAs)
+#ifndef HY_MEGA_SPLITS
+#define HY_MEGA_SPLITS 18
+#endif
+constexpr int kMegaSplits = HY_MEGA_SPLITS;   // per KV head: the past rows' splits + the new-row split (8 x 18 = 144 CTAs)
 constexpr int kMegaMaxK = 3584;
 constexpr int kMegaHistWords = 64;       // LM rows per CTA <= 32 * 62
 constexpr int kMegaResRows = 32;         // o/down rows per CTA (1024 / gridDim.x)
