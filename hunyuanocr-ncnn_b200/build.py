@@ -30,16 +30,26 @@ def up_to_date() -> bool:
     return all(os.path.getmtime(d) <= t for d in DEPS + [__file__])
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and up_to_date():
+def build(force: bool = False, verbose: bool = False, defines=(), out: str = LIB) -> str:
+    """Build the library (into `out`; `defines` such as "HY_TRACE_CTAS=148" become -D flags,
+    for instrumented builds kept beside the in-tree one)."""
+    if out == LIB and not defines and not force and up_to_date():
         return LIB
-    cmd = [NVCC, *FLAGS, "-o", LIB, *SOURCES]
+    cmd = [NVCC, *FLAGS, *[f"-D{d}" for d in defines], "-o", out, *SOURCES]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd))
     subprocess.run(cmd, check=True)
-    return LIB
+    return out
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    import argparse
+
+    ap = argparse.ArgumentParser(description="build libhy_decode.so for sm_100a")
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("-v", action="store_true", help="print the command and ptxas resource usage")
+    ap.add_argument("--define", action="append", default=[], help="NAME=VALUE, passed as -D (repeatable)")
+    ap.add_argument("--out", default=LIB, help="output path (default: the in-tree library)")
+    a = ap.parse_args()
+    print(build(force=a.force, verbose=a.v, defines=a.define, out=a.out))

@@ -30,6 +30,9 @@ def main(argv=None):
     ap.add_argument("--dtype", choices=["f32", "bf16"], default="f32", help="weight and KV dtype")
     ap.add_argument("--draft-layers", type=int, default=5, help="draft mode: DFlash draft depth")
     ap.add_argument("--records", type=int, default=16, help="batch mode: records decoding together")
+    ap.add_argument("--lib", default=None, help="library to load (default: the in-tree build)")
+    ap.add_argument("--trace-ctas", type=int, default=4,
+                    help="trace mode: CTAs the library traces (its HY_TRACE_CTAS; 4 in the default build)")
     ap.add_argument("--kernel", choices=["decode", "lm", "gate_up", "attention", "verify", "prefill", "draft",
                                          "batch", "trace"],
                     default="decode",
@@ -45,6 +48,8 @@ def main(argv=None):
     import __graft_entry__ as ge
 
     pkg = ge.load_package()
+    if args.lib:
+        pkg.load_library(os.path.abspath(args.lib))
     dt = pkg.DTYPE_F32 if args.dtype == "f32" else pkg.DTYPE_BF16
     if args.kernel == "prefill":
         import time
@@ -96,7 +101,15 @@ def main(argv=None):
 
         rt.set_length(args.past)
         rt.set_history([1, 2, 3])
-        tr = rt.trace_persistent(args.tokens, args.tokens // 2).astype(np.int64)
+        import ctypes
+
+        phases = 5 * args.layers + 1
+        raw = np.zeros((args.trace_ctas, phases, 12), np.uint64)
+        lib = pkg.load_library()
+        rc = lib.hy_trace_persistent(rt._ctx, args.tokens, args.tokens // 2, raw.ctypes.data_as(ctypes.c_void_p))
+        if rc != 0:
+            raise RuntimeError(f"hy_trace_persistent: status {rc}")
+        tr = raw.astype(np.int64)
         c0 = tr[0]
         names = ["q/k/v", "attention", "o_proj", "gate/up", "down_proj"]
         L = args.layers
@@ -111,7 +124,17 @@ def main(argv=None):
         print(f"{'LM head':<12} {(lm[3] - lm[0]) / 1e3:11.2f} {(lm[1] - lm[0]) / 1e3:22.2f} "
               f"{(lm[3] - lm[1]) / 1e3:14.2f}")
         spread = (tr[:, :5 * L, 1].max(axis=0) - tr[:, :5 * L, 1].min(axis=0)) / 1e3
-        print(f"inputs-ready spread over CTAs 0-3: mean {spread.mean():.2f} us, max {spread.max():.2f} us")
+        print(f"inputs-ready spread over CTAs 0-{args.trace_ctas - 1}: mean {spread.mean():.2f} us, "
+              f"max {spread.max():.2f} us")
+        ready = (c0[:5 * L, 1] - c0[:5 * L, 0]) / 1e3
+        print(f"token boundary: layer 0 q/k/v inputs ready after {ready[0]:.2f} us, layers 1-{L - 1}: "
+              f"{ready[5::5].mean():.2f} us (CTA 0)")
+        for k, name in enumerate(names):
+            ends = tr[:, k:5 * L:5, 3]
+            late = ((ends - ends.min(axis=0, keepdims=True)) / 1e3).mean(axis=1)
+            order = np.argsort(-late)[:4]
+            print(f"{name:<12} phase end after the earliest CTA's: mean {late.mean():.2f} us, max {late.max():.2f} us "
+                  f"(latest CTAs {[int(i) for i in order]})")
         rt.close()
         return
     if args.kernel in ("lm", "gate_up", "attention"):
