@@ -49,7 +49,8 @@ EXPORTED_SYMBOLS = (
     "hy_lm_head_select_noalloc", "hy_draft_load", "hy_draft_load_synthetic", "hy_draft_context_length",
     "hy_draft_context_append", "hy_draft_run", "hy_draft_propose", "hy_dflash_generate",
     "hy_run_vlm_dflash_with_prompt", "hy_batch_decode", "hy_fixture_meta", "hy_fixture_load",
-    "hy_ctx_set_token_callback",
+    "hy_ctx_set_token_callback", "hy_debug_wait_stats", "hy_ctx_last_timing", "hy_ctx_last_dflash_timing",
+    "hy_ctx_set_wait_limit", "hy_debug_wait_probe",
 )
 TOKEN_CALLBACK = ctypes.CFUNCTYPE(None, ctypes.c_int, ctypes.c_void_p)
 DFLASH_MASK_TOKEN = 120817
@@ -89,6 +90,17 @@ class _Request(ctypes.Structure):
     _fields_ = [("input_ids", ctypes.c_void_p), ("position_ids", ctypes.c_void_p), ("seq_len", ctypes.c_int),
                 ("image_token_id", ctypes.c_int), ("vision_features", ctypes.c_void_p),
                 ("vision_token_count", ctypes.c_int)]
+
+
+class _DecodeTiming(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_double) for n in ("text_embed_ms", "prefill_ms", "decode_ms", "lm_head_ms",
+                                                "token_select_ms", "total_ms", "host_overhead_ms")]
+
+
+class _DFlashTiming(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_double) for n in ("prefill_ms", "draft_ms", "verify_ms", "commit_ms", "blocks_ms",
+                                                "total_ms", "host_overhead_ms")] + [
+        (n, ctypes.c_int) for n in ("block_count", "drafted_token_count", "accepted_draft_token_count")]
 
 
 class _Weights(ctypes.Structure):
@@ -152,7 +164,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "hy_batch_decode": ([_P, ctypes.POINTER(_Request), _I, _I, _I, _F, _P, _I, _P, _P, _P], _I),
         "hy_fixture_meta": ([ctypes.c_char_p, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I),
                              ctypes.POINTER(_I)], _I),
-        "hy_fixture_load": ([ctypes.c_char_p, _P, _P, _P, _P], _I),
+        "hy_fixture_load": ([ctypes.c_char_p, _I, _I, _I, _P, _P, _P, _P], _I),
         "hy_ctx_set_token_callback": ([_P, TOKEN_CALLBACK, _P, _I], _I),
         "hy_draft_load_synthetic": ([_P, _I, _I, ctypes.c_uint64, _F, _F], _I),
         "hy_draft_context_length": ([_P, ctypes.POINTER(_I)], _I),
@@ -163,6 +175,11 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "hy_run_vlm_dflash_with_prompt": ([_P, _P, _P, _I, _I, _P, _I, _I, _F, _P, _I, _P, ctypes.POINTER(_I), _P,
                                            ctypes.POINTER(_I)], _I),
         "hy_debug_progress": ([_P, _P, _I], _I),
+        "hy_debug_wait_stats": ([_P, _P, _I, _I], _I),
+        "hy_ctx_set_wait_limit": ([_P, ctypes.c_uint64], _I),
+        "hy_debug_wait_probe": ([_P, _I, ctypes.c_uint64], _I),
+        "hy_ctx_last_timing": ([_P, ctypes.POINTER(_DecodeTiming)], _I),
+        "hy_ctx_last_dflash_timing": ([_P, ctypes.POINTER(_DFlashTiming)], _I),
     }
     for name, (argtypes, restype) in sig.items():
         fn = getattr(lib, name)
@@ -218,6 +235,34 @@ def rope_rows(start: int, rows: int, use_cos: bool) -> np.ndarray:
 
 
 @dataclass
+class TextDecodeTiming:
+    """include/hunyuan_ocr/text_runtime.h:32-39 (device stages from CUDA events; the LM head of
+    every token after the first and all token selection are fused into decode_ms), plus
+    host_overhead_ms = total_ms minus the device stages."""
+    text_embed_ms: float = 0.0
+    prefill_ms: float = 0.0
+    decode_ms: float = 0.0
+    lm_head_ms: float = 0.0
+    token_select_ms: float = 0.0
+    total_ms: float = 0.0
+    host_overhead_ms: float = 0.0
+
+
+@dataclass
+class DFlashDecodeTiming:
+    """include/hunyuan_ocr/text_runtime.h:64-74 in three device stages per block (draft =
+    draft_prepare + draft_infer + draft_postprocess; verify = verify_prepare + verify_infer;
+    commit = verify_postprocess + commit), plus blocks_ms and host_overhead_ms."""
+    prefill_ms: float = 0.0
+    draft_ms: float = 0.0
+    verify_ms: float = 0.0
+    commit_ms: float = 0.0
+    blocks_ms: float = 0.0
+    total_ms: float = 0.0
+    host_overhead_ms: float = 0.0
+
+
+@dataclass
 class TextDecodeResult:
     """include/hunyuan_ocr/text_runtime.h:41-51 (the fields this path fills)."""
     seq_len: int
@@ -226,6 +271,7 @@ class TextDecodeResult:
     raw_top1_tokens: list
     checked_tokens: int = 0
     expected_tokens: list = field(default_factory=list)
+    timing: TextDecodeTiming = field(default_factory=TextDecodeTiming)
 
     def matches_expected(self) -> bool:
         """TextDecodeResult::matches_expected (src/text_runtime.cpp:1788-1791)."""
@@ -234,13 +280,14 @@ class TextDecodeResult:
 
 @dataclass
 class DFlashDecodeResult:
-    """include/hunyuan_ocr/text_runtime.h:76-83."""
+    """include/hunyuan_ocr/text_runtime.h:76-83 (counts as the library reports them)."""
     generated_tokens: list
     block_count: int
     drafted_token_count: int
     accepted_draft_token_count: int
     acceptance_lengths: list
     expected_tokens: list = field(default_factory=list)
+    timing: DFlashDecodeTiming = field(default_factory=DFlashDecodeTiming)
 
     def matches_expected(self) -> bool:
         return self.generated_tokens == self.expected_tokens
@@ -271,7 +318,8 @@ def read_vlm_fixture(fixture_dir: str, with_features: bool = True) -> VlmFixture
     pos = np.empty((4, seq.value), np.int32)
     expected = np.empty(exp.value, np.int32)
     feats = np.empty((vis.value, HIDDEN), np.float32) if with_features else None
-    _check(lib.hy_fixture_load(d, _ptr(ids), _ptr(pos), _ptr(expected), _ptr(feats)))
+    _check(lib.hy_fixture_load(d, ids.size, expected.size, 0 if feats is None else feats.shape[0], _ptr(ids),
+                               _ptr(pos), _ptr(expected), _ptr(feats)))
     return VlmFixture(seq.value, img.value, vis.value, ids, pos, expected, feats)
 
 
@@ -450,6 +498,20 @@ class TextRuntime:
         _check(_LIB.hy_kv_read(self._ctx, layer, start, rows, _ptr(k), _ptr(v)))
         return k, v
 
+    # -- timing -------------------------------------------------------------
+    def last_timing(self) -> TextDecodeTiming:
+        """TextDecodeTiming of the last AR call (hy_ctx_last_timing)."""
+        t = _DecodeTiming()
+        _check(_LIB.hy_ctx_last_timing(self._ctx, ctypes.byref(t)))
+        return TextDecodeTiming(*[getattr(t, n) for n, _ in _DecodeTiming._fields_])
+
+    def _dflash_result(self, tokens, n, acc, nb) -> DFlashDecodeResult:
+        t = _DFlashTiming()
+        _check(_LIB.hy_ctx_last_dflash_timing(self._ctx, ctypes.byref(t)))
+        timing = DFlashDecodeTiming(*[getattr(t, n) for n, _ in _DFlashTiming._fields_[:7]])
+        return DFlashDecodeResult(tokens[:n.value].tolist(), t.block_count, t.drafted_token_count,
+                                  t.accepted_draft_token_count, acc[:nb.value].tolist(), timing=timing)
+
     # -- loops -------------------------------------------------------------
     def generate(self, first_token: int, first_raw: int, max_tokens: int, penalty: float, eos_ids=()):
         eos = _i32(list(eos_ids)) if len(eos_ids) else None
@@ -480,9 +542,7 @@ class TextRuntime:
         _check(_LIB.hy_dflash_generate_synthetic(self._ctx, first_token, max_tokens, penalty, _ptr(eos),
                                                  0 if eos is None else eos.size, _ptr(g), g.size, p, seed,
                                                  _ptr(tokens), ctypes.byref(n), _ptr(acc), ctypes.byref(nb)))
-        accl = acc[:nb.value].tolist()
-        return DFlashDecodeResult(tokens[:n.value].tolist(), nb.value, nb.value * (DFLASH_BLOCK - 1),
-                                  int(sum(accl)), accl)
+        return self._dflash_result(tokens, n, acc, nb)
 
     def run_vlm_decode_with_prompt(self, input_ids, position_ids, image_token_id: int, vision_features,
                                    max_tokens: int, repetition_penalty: float = 1.08,
@@ -500,7 +560,8 @@ class TextRuntime:
                                                   _ptr(feats), feats.shape[0], max_tokens, repetition_penalty,
                                                   _ptr(eos), 0 if eos is None else eos.size, _ptr(tokens),
                                                   _ptr(raw), ctypes.byref(n)))
-        return TextDecodeResult(ids.size, repetition_penalty, tokens[:n.value].tolist(), raw[:n.value].tolist())
+        return TextDecodeResult(ids.size, repetition_penalty, tokens[:n.value].tolist(), raw[:n.value].tolist(),
+                                timing=self.last_timing())
 
     def batch_decode(self, requests, max_tokens: int, slots: int = 16, repetition_penalty: float = 1.08,
                      eos_ids=()):
@@ -577,9 +638,7 @@ class TextRuntime:
         _check(_LIB.hy_dflash_generate(self._ctx, first_token, max_tokens, penalty, _ptr(eos),
                                        0 if eos is None else eos.size, _ptr(tokens), ctypes.byref(n), _ptr(acc),
                                        ctypes.byref(nb)))
-        accl = acc[:nb.value].tolist()
-        return DFlashDecodeResult(tokens[:n.value].tolist(), nb.value, nb.value * (DFLASH_BLOCK - 1),
-                                  int(sum(accl)), accl)
+        return self._dflash_result(tokens, n, acc, nb)
 
     def run_vlm_dflash_with_prompt(self, input_ids, position_ids, image_token_id: int, vision_features,
                                    max_tokens: int, repetition_penalty: float = 1.08,
@@ -597,9 +656,7 @@ class TextRuntime:
                                                   _ptr(feats), feats.shape[0], max_tokens, repetition_penalty,
                                                   _ptr(eos), 0 if eos is None else eos.size, _ptr(tokens),
                                                   ctypes.byref(n), _ptr(acc), ctypes.byref(nb)))
-        accl = acc[:nb.value].tolist()
-        return DFlashDecodeResult(tokens[:n.value].tolist(), nb.value, nb.value * (DFLASH_BLOCK - 1),
-                                  int(sum(accl)), accl)
+        return self._dflash_result(tokens, n, acc, nb)
 
     # -- regression fixtures ---------------------------------------------------
     @staticmethod
@@ -644,6 +701,32 @@ class TextRuntime:
         out = np.zeros((4, phases, 12), np.uint64)
         _check(_LIB.hy_trace_persistent(self._ctx, tokens, trace_token, _ptr(out)))
         return out
+
+    WAIT_KINDS = ("slot_free", "slot_full", "prod_slot", "prod_token", "poll_x", "poll_act", "poll_attn_out",
+                  "poll_qkv", "poll_parts", "poll_token")
+
+    def wait_stats(self, reset: bool = True):
+        """Wait statistics of the persistent kernel (library built with HY_WAIT_STATS):
+        (per-CTA [160, kinds, 3] = waits over 20 us, their ns, longest ns;
+        per-launch [64, 2] = first CTA start, last CTA exit in %globaltimer ns, 0 if unused)."""
+        n = 160 * len(self.WAIT_KINDS) * 3 + 64 * 2
+        out = np.zeros(n, np.uint64)
+        _check(_LIB.hy_debug_wait_stats(self._ctx, _ptr(out), n, int(reset)))
+        per = out[:160 * len(self.WAIT_KINDS) * 3].reshape(160, len(self.WAIT_KINDS), 3)
+        lw = out[160 * len(self.WAIT_KINDS) * 3:].reshape(64, 2).copy()
+        used = lw[:, 1] != 0
+        lw[used, 0] = ~lw[used, 0]
+        lw[~used] = 0
+        return per, lw
+
+    def set_wait_limit(self, limit_ns: int) -> None:
+        """Bound of the persistent kernel's waits (hy_ctx_set_wait_limit)."""
+        _check(_LIB.hy_ctx_set_wait_limit(self._ctx, limit_ns))
+
+    def wait_probe(self, kind: int, limit_ns: int) -> None:
+        """Run the bounded-wait self-test (hy_debug_wait_probe); raises HyError
+        (HY_ERR_DEVICE_TIMEOUT) when the wait ran out, as it should."""
+        _check(_LIB.hy_debug_wait_probe(self._ctx, kind, limit_ns))
 
     def debug_progress(self, n: int = 148) -> np.ndarray:
         out = np.zeros(n, np.uint32)

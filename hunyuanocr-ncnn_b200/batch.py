@@ -48,12 +48,17 @@ def partition(n_records: int, world: int, rank: int) -> List[int]:
 
 
 def run_partition(records: Sequence, infer: Callable, world: int = 1, rank: int = 0,
-                  record_id: Optional[Callable] = None) -> tuple[List[BatchRecord], BatchSummary]:
+                  record_id: Optional[Callable] = None,
+                  channel: Optional["StoreChannel"] = None) -> tuple[List[BatchRecord], BatchSummary]:
     """Run this rank's records through `infer(record) -> tokens` (which raises on failure,
     like a BatchInfer returning false with a RuntimeError). Returns this rank's output
-    records in input order and its summary."""
+    records in input order and its summary. With a `channel`, every record is published
+    as soon as it is done (and counts as this rank's heartbeat), and the rank reports
+    that it finished after its last record."""
     out: List[BatchRecord] = []
     summary = BatchSummary()
+    if channel is not None:
+        channel.beat()
     for i in partition(len(records), world, rank):
         rid = record_id(records[i]) if record_id else str(i)
         summary.total += 1
@@ -63,9 +68,13 @@ def run_partition(records: Sequence, infer: Callable, world: int = 1, rank: int 
             summary.failed += 1
             stage = getattr(exc, "stage", "inference")
             out.append(BatchRecord(i, rid, False, stage=stage, error=str(exc) or "inference failed"))
-            continue
-        summary.succeeded += 1
-        out.append(BatchRecord(i, rid, True, tokens=list(tokens)))
+        else:
+            summary.succeeded += 1
+            out.append(BatchRecord(i, rid, True, tokens=list(tokens)))
+        if channel is not None:
+            channel.publish(out[-1])
+    if channel is not None:
+        channel.finish()
     return out, summary
 
 
@@ -115,3 +124,79 @@ def gather_in_order(local: Sequence[BatchRecord], world: int, rank: int):
     if rank != 0:
         return None, None
     return merge_in_order(parts)
+
+
+class StoreChannel:
+    """Per-record results and liveness of the ranks through the process group's
+    key-value store, so that rank 0 can assemble the output without a collective
+    that would wait forever for a rank that left.
+
+    Every rank publishes each finished record (which also bumps its heartbeat
+    counter) and a `done` flag after its last one. Rank 0 (`collect`) polls the
+    store: a record appears when its rank published it; a rank whose heartbeat
+    has not moved for `rank_timeout_s` seconds and that never reported `done`
+    is taken to have left, and each of its unpublished records becomes an
+    ok:false record (stage "rank") - the reference's per-record failure path,
+    src/batch_jsonl.cpp:274-296, extended to a rank that is gone. The timeout
+    must exceed the longest single infer call."""
+
+    def __init__(self, store, world: int, rank: int, prefix: str = "hy_batch"):
+        self.store, self.world, self.rank, self.prefix = store, world, rank, prefix
+
+    @classmethod
+    def from_default_group(cls, prefix: str = "hy_batch") -> "StoreChannel":
+        import torch.distributed as dist
+        return cls(dist.distributed_c10d._get_default_store(), dist.get_world_size(), dist.get_rank(), prefix)
+
+    def _key(self, *parts) -> str:
+        return "/".join((self.prefix,) + tuple(str(p) for p in parts))
+
+    def beat(self) -> None:
+        self.store.add(self._key("beat", self.rank), 1)
+
+    def publish(self, rec: BatchRecord) -> None:
+        import pickle
+        self.store.set(self._key("rec", rec.index), pickle.dumps(rec))
+        self.beat()
+
+    def finish(self) -> None:
+        self.store.set(self._key("done", self.rank), b"1")
+
+    def collect(self, n_records: int, rank_timeout_s: float = 120.0, poll_s: float = 0.02,
+                clock: Callable = None) -> tuple[List[BatchRecord], BatchSummary]:
+        """On rank 0, after its own records: every record in input order and the summary.
+        Returns once each record was published or its rank was found gone."""
+        import pickle
+        import time
+        clock = clock or time.monotonic
+        got = {}
+        pending = set(range(n_records))
+        last_beat = {r: None for r in range(self.world)}
+        last_move = {r: clock() for r in range(self.world)}
+        while pending:
+            now = clock()
+            for i in sorted(pending):
+                k = self._key("rec", i)
+                if self.store.check([k]):
+                    got[i] = pickle.loads(self.store.get(k))
+                    pending.discard(i)
+            if not pending:
+                break
+            owners = {i % self.world for i in pending}
+            for r in owners:
+                beat = self.store.add(self._key("beat", r), 0)
+                if beat != last_beat[r]:
+                    last_beat[r], last_move[r] = beat, now
+                done = self.store.check([self._key("done", r)])
+                if done or now - last_move[r] > rank_timeout_s:
+                    why = ("finished without publishing it" if done else
+                           f"stopped responding (no progress for {rank_timeout_s:g} s)")
+                    for i in [i for i in pending if i % self.world == r]:
+                        k = self._key("rec", i)
+                        if self.store.check([k]):   # published since the scan above
+                            got[i] = pickle.loads(self.store.get(k))
+                        else:
+                            got[i] = BatchRecord(i, str(i), False, stage="rank", error=f"rank {r} {why}")
+                        pending.discard(i)
+            time.sleep(poll_s)
+        return merge_in_order([[got[i] for i in range(n_records)]])

@@ -11,6 +11,7 @@
 #include "hy_util.cuh"
 
 #include "hy_decode.h"
+#include "hy_debug.h"
 
 #include <cuda_runtime.h>
 
@@ -21,6 +22,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <fstream>
+#include <chrono>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -61,6 +63,12 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 float host_synth_mult(float std_dev) { return static_cast<float>(static_cast<double>(std_dev) * std::sqrt(3.0) / 65536.0); }
 
+}  // namespace
+
+namespace {
+constexpr int kHistChunk = 4096;     // history ids per upload round
+constexpr int kTimingEvents = 6;     // start, embedded, prefilled, first token, decode start, decode end
+constexpr int kDflashGraphs = 4;     // DFlash blocks launched between host reads of the decode state
 }  // namespace
 
 struct hy_ctx {
@@ -131,6 +139,22 @@ struct hy_ctx {
     int* err = nullptr;
     DecodeState* h_st = nullptr;  // pinned mirror
     int kv_len = 0;               // host mirror of the sequence length
+    // Staging that keeps allocation and pageable copies off the call paths:
+    // pinned host areas for the prompt uploads (ids, feature index, features,
+    // cos, sin), history ids and small device reads; device buffers for history
+    // ids and KV-row conversions. Every call that uses them has finished with
+    // them (its stream synchronised) before it returns.
+    unsigned char* h_stage = nullptr;
+    size_t h_stage_bytes = 0;
+    int* h_hist = nullptr;        // pinned [kHistChunk]
+    int* h_small = nullptr;       // pinned [16]: first token, raw top-1, error words
+    int* h_log = nullptr;         // pinned [2 x (max_tokens + 2 x 16)]: token logs read back at the end of a loop
+    int* hist_ids = nullptr;      // device [kHistChunk]
+    float* kv_stage = nullptr;    // device [max_context x 128]
+    // Per-stage timing of the last AR / DFlash decode call (CUDA events on the stream).
+    cudaEvent_t tev[kTimingEvents] = {};
+    hy_decode_timing timing{};
+    hy_dflash_timing dtiming{};
 
     // Persistent AR decode kernel (cooperative, one CTA per SM).
     const void** wptrs = nullptr;  // device arrays: wqkv[L], wo[L], wgu[L], wd[L]
@@ -146,6 +170,10 @@ struct hy_ctx {
     unsigned mega_seq = 0;
     int* dbg = nullptr;            // persistent-kernel self-check record [4]
     unsigned* progress = nullptr;  // host-mapped per-CTA phase progress (HY_DEBUG_PROGRESS=1)
+    unsigned long long* wstat = nullptr;  // wait statistics (builds with HY_WAIT_STATS only)
+    unsigned long long wait_limit_ns = kWaitLimitNs;   // bound of the persistent kernel's waits
+    unsigned long long* probe_word = nullptr;          // an epoch word nothing publishes (wait probe)
+    int mega_launches = 0;                // persistent launches since the statistics were reset
     int ar_path = HY_AR_PATH_PERSISTENT;
     bool mega_ok = false;
 
@@ -181,7 +209,11 @@ struct hy_ctx {
     std::vector<float*> d_tkv_hi, d_tkv_lo;  // k | v rows tiled [2048 x 1024] per draft layer
     std::vector<void*> d_allocs;
     size_t d_bytes = 0;
-    cudaGraphExec_t g_dflash = nullptr;           // draft + verify + context append + commit
+    // draft + verify + context append + commit: one graph per block of a group of
+    // kDflashGraphs blocks between host reads, each recording its stage events
+    // (block start, draft done, verify and context rows done).
+    cudaGraphExec_t g_dflash[kDflashGraphs] = {};
+    cudaEvent_t dflash_ev[kDflashGraphs][3] = {};
     cudaGraphExec_t g_verify_ids_ctx = nullptr;   // verify of given ids + context append + commit
 
     // Batched decode (hy_batch_decode): up to 16 sequences, sequence s in step row s,
@@ -606,22 +638,20 @@ cudaError_t enqueue_lm_select(hy_ctx* c, int rows, const float* x, float penalty
 
 int check_device_error(hy_ctx* c)
 {
-    if (c->dbg)
-    {
-        int d[4] = {0, 0, 0, 0};
-        HY_CUDA(cudaMemcpyAsync(d, c->dbg, sizeof(d), cudaMemcpyDeviceToHost, c->stream));
-        HY_CUDA(cudaStreamSynchronize(c->stream));
-        if (d[0] != 0)
-        {
-            HY_CUDA(cudaMemsetAsync(c->dbg, 0, sizeof(d), c->stream));
-            return fail(HY_ERR_INVALID_ARGUMENT, "persistent kernel self-check " + std::to_string(d[0]) + " failed (cta " +
-                                                     std::to_string(d[1]) + ", phase " + std::to_string(d[2]) + ", index " +
-                                                     std::to_string(d[3]) + ")");
-        }
-    }
-    int h = 0;
-    HY_CUDA(cudaMemcpyAsync(&h, c->err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    // Both words in one synchronisation, into pinned memory (h_small[8..12]).
+    int* d = c->h_small + 8;
+    if (c->dbg) HY_CUDA(cudaMemcpyAsync(d, c->dbg, 4 * sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    HY_CUDA(cudaMemcpyAsync(d + 4, c->err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
     HY_CUDA(cudaStreamSynchronize(c->stream));
+    if (c->dbg && d[0] != 0)
+    {
+        const std::string msg = "persistent kernel self-check " + std::to_string(d[0]) + " failed (cta " +
+                                std::to_string(d[1]) + ", phase " + std::to_string(d[2]) + ", index " +
+                                std::to_string(d[3]) + ")";
+        HY_CUDA(cudaMemsetAsync(c->dbg, 0, 4 * sizeof(int), c->stream));
+        return fail(HY_ERR_INVALID_ARGUMENT, msg);
+    }
+    const int h = d[4];
     if (h != 0)
     {
         HY_CUDA(cudaMemsetAsync(c->err, 0, sizeof(int), c->stream));
@@ -716,6 +746,9 @@ cudaError_t launch_mega_t(hy_ctx* c, int steps)
     a.trace = t_trace;
     a.trace_token = t_trace_token;
     a.dbg = c->dbg;
+    a.wstat = c->wstat;
+    a.launch_slot = c->mega_launches++;
+    a.wait_limit_ns = c->wait_limit_ns;
     if (c->progress)
     {
         unsigned* dp = nullptr;
@@ -865,6 +898,38 @@ int validate_config(const hy_config* cfg)
     return HY_OK;
 }
 
+// Pinned staging of one prompt upload: ids, feature index [rows] int, features
+// [rows x 1024], cos, sin [rows x 128] float, each 256-byte aligned.
+struct PromptStage {
+    int* ids;
+    int* feat_idx;
+    float* feats;
+    float* cos;
+    float* sin;
+};
+size_t prompt_stage_bytes(int rows)
+{
+    const size_t r = static_cast<size_t>(std::max(rows, kMaxStepRows));
+    return 2 * align_up(r * sizeof(int), 256) + align_up(r * kHidden * sizeof(float), 256) +
+           2 * align_up(r * kHeadDim * sizeof(float), 256);
+}
+PromptStage prompt_stage(hy_ctx* c)
+{
+    const size_t r = static_cast<size_t>(std::max(c->cfg.max_prefill, kMaxStepRows));
+    unsigned char* p = c->h_stage;
+    PromptStage s;
+    s.ids = reinterpret_cast<int*>(p);
+    p += align_up(r * sizeof(int), 256);
+    s.feat_idx = reinterpret_cast<int*>(p);
+    p += align_up(r * sizeof(int), 256);
+    s.feats = reinterpret_cast<float*>(p);
+    p += align_up(r * kHidden * sizeof(float), 256);
+    s.cos = reinterpret_cast<float*>(p);
+    p += align_up(r * kHeadDim * sizeof(float), 256);
+    s.sin = reinterpret_cast<float*>(p);
+    return s;
+}
+
 int alloc_ctx(hy_ctx* c)
 {
     const hy_config& cfg = c->cfg;
@@ -991,6 +1056,10 @@ int alloc_ctx(hy_ctx* c)
     if ((rc = dalloc(c, &c->attn_ep, static_cast<size_t>(kNumKVHeads) * (kMegaSplits - 1) * 2 * kAttnWords))) return rc;
     if ((rc = dalloc(c, &c->attn_out_ep, kQWidth))) return rc;
     HY_CUDA(cudaMemsetAsync(c->dbg, 0, 4 * sizeof(int), c->stream));
+#ifdef HY_WAIT_STATS
+    if ((rc = dalloc(c, &c->wstat, kWsWords))) return rc;
+    HY_CUDA(cudaMemsetAsync(c->wstat, 0, kWsWords * sizeof(unsigned long long), c->stream));
+#endif
     if (const char* e = std::getenv("HY_DEBUG_PROGRESS"); e && e[0] == '1')
     {
         HY_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&c->progress), 1024 * sizeof(unsigned), cudaHostAllocMapped));
@@ -1018,6 +1087,18 @@ int alloc_ctx(hy_ctx* c)
     std::memset(c->h_st, 0, sizeof(DecodeState));
     c->h_st->penalty = 1.08f;
     if ((rc = push_state(c))) return rc;
+    // Staging (see hy_ctx): prompt uploads in one pinned area, history ids, small reads.
+    c->h_stage_bytes = prompt_stage_bytes(cfg.max_prefill);
+    HY_CUDA(cudaMallocHost(reinterpret_cast<void**>(&c->h_stage), c->h_stage_bytes));
+    HY_CUDA(cudaMallocHost(reinterpret_cast<void**>(&c->h_hist), sizeof(int) * kHistChunk));
+    HY_CUDA(cudaMallocHost(reinterpret_cast<void**>(&c->h_small), sizeof(int) * 16));
+    HY_CUDA(cudaMallocHost(reinterpret_cast<void**>(&c->h_log), sizeof(int) * 2 * (cfg.max_tokens + 2 * kBlock)));
+    std::memset(c->h_small, 0, sizeof(int) * 16);
+    if ((rc = dalloc(c, &c->hist_ids, kHistChunk))) return rc;
+    if ((rc = dalloc(c, &c->kv_stage, static_cast<size_t>(cfg.max_context) * kHeadDim))) return rc;
+    if ((rc = dalloc(c, &c->probe_word, 2))) return rc;
+    HY_CUDA(cudaMemsetAsync(c->probe_word, 0, 2 * sizeof(unsigned long long), c->stream));
+    for (int i = 0; i < kTimingEvents; ++i) HY_CUDA(cudaEventCreate(&c->tev[i]));
 
     // 1-D RoPE table for decode / verify positions.
     std::vector<float> cs(rope_rows * kHeadDim), sn(rope_rows * kHeadDim);
@@ -1164,7 +1245,12 @@ void free_ctx(hy_ctx* c)
     if (c->g_ar) cudaGraphExecDestroy(c->g_ar);
     if (c->g_verify_draft) cudaGraphExecDestroy(c->g_verify_draft);
     if (c->g_verify_ids) cudaGraphExecDestroy(c->g_verify_ids);
-    if (c->g_dflash) cudaGraphExecDestroy(c->g_dflash);
+    for (int b = 0; b < kDflashGraphs; ++b)
+    {
+        if (c->g_dflash[b]) cudaGraphExecDestroy(c->g_dflash[b]);
+        for (cudaEvent_t e : c->dflash_ev[b])
+            if (e) cudaEventDestroy(e);
+    }
     if (c->g_verify_ids_ctx) cudaGraphExecDestroy(c->g_verify_ids_ctx);
     if (c->g_batch) cudaGraphExecDestroy(c->g_batch);
     for (void* p : c->d_allocs) cudaFree(p);
@@ -1173,6 +1259,12 @@ void free_ctx(hy_ctx* c)
     for (void* p : c->allocs) cudaFree(p);
     if (c->logits) cudaFree(c->logits);
     if (c->h_st) cudaFreeHost(c->h_st);
+    if (c->h_stage) cudaFreeHost(c->h_stage);
+    if (c->h_hist) cudaFreeHost(c->h_hist);
+    if (c->h_small) cudaFreeHost(c->h_small);
+    if (c->h_log) cudaFreeHost(c->h_log);
+    for (cudaEvent_t e : c->tev)
+        if (e) cudaEventDestroy(e);
     if (c->progress) cudaFreeHost(c->progress);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
@@ -1725,10 +1817,14 @@ cudaError_t enqueue_draft_forward(hy_ctx* c, int src, bool from_state, int past,
 // appended before the commit (the commit moves the length; the block's rows
 // past the committed ones are rewritten by the next block before any read).
 // With `draft`, the block's ids come from the draft network first.
-cudaError_t enqueue_verify_with_context(hy_ctx* c, bool draft)
+// ev (nullable): stage events recorded inside the captured graph (block start,
+// draft done, verify and context rows done).
+cudaError_t enqueue_verify_with_context(hy_ctx* c, bool draft, cudaEvent_t* ev = nullptr)
 {
     cudaError_t e = cudaSuccess;
+    if (ev && (e = cudaEventRecordWithFlags(ev[0], c->stream, cudaEventRecordExternal)) != cudaSuccess) return e;
     if (draft && (e = enqueue_draft_forward(c, SRC_GATHER_BLOCK, true, 0, true)) != cudaSuccess) return e;
+    if (ev && (e = cudaEventRecordWithFlags(ev[1], c->stream, cudaEventRecordExternal)) != cudaSuccess) return e;
     float* aux[kAuxLayers];
     for (int i = 0; i < kAuxLayers; ++i) aux[i] = c->d_aux + i * kHidden;
     StepPlan p{};
@@ -1744,16 +1840,17 @@ cudaError_t enqueue_verify_with_context(hy_ctx* c, bool draft)
     p.ld_aux = kAuxWidth;
     if ((e = enqueue_step(c, p)) != cudaSuccess) return e;
     if ((e = enqueue_draft_context16(c, c->d_aux, kBlock, true, 0)) != cudaSuccess) return e;
+    if (ev && (e = cudaEventRecordWithFlags(ev[2], c->stream, cudaEventRecordExternal)) != cudaSuccess) return e;
     p.lm_mode = LM_VERIFY;
     return (c->cfg.weight_dtype == HY_DTYPE_BF16) ? enqueue_step_lm_t<__nv_bfloat16, 16>(c, p)
                                                   : enqueue_step_lm_t<float, 16>(c, p);
 }
 
-int capture_fn(hy_ctx* c, cudaGraphExec_t* out, bool draft)
+int capture_fn(hy_ctx* c, cudaGraphExec_t* out, bool draft, cudaEvent_t* ev = nullptr)
 {
     cudaGraph_t graph = nullptr;
     HY_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
-    const cudaError_t e = enqueue_verify_with_context(c, draft);
+    const cudaError_t e = enqueue_verify_with_context(c, draft, ev);
     const cudaError_t e2 = cudaStreamEndCapture(c->stream, &graph);
     if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
     if (e2 != cudaSuccess) return fail(HY_ERR_CUDA, std::string("graph capture end: ") + cudaGetErrorString(e2));
@@ -1765,9 +1862,13 @@ int capture_fn(hy_ctx* c, cudaGraphExec_t* out, bool draft)
 
 void draft_free(hy_ctx* c)
 {
-    if (c->g_dflash) cudaGraphExecDestroy(c->g_dflash);
+    for (cudaGraphExec_t& g : c->g_dflash)
+    {
+        if (g) cudaGraphExecDestroy(g);
+        g = nullptr;
+    }
     if (c->g_verify_ids_ctx) cudaGraphExecDestroy(c->g_verify_ids_ctx);
-    c->g_dflash = c->g_verify_ids_ctx = nullptr;
+    c->g_verify_ids_ctx = nullptr;
     for (void* p : c->d_allocs) cudaFree(p);
     c->d_allocs.clear();
     c->d_wqkv.clear();
@@ -1896,7 +1997,13 @@ int draft_finish_t(hy_ctx* c)
         HY_CUDA(cudaGetLastError());
     }
     HY_CUDA(cudaStreamSynchronize(c->stream));
-    int rc = capture_fn(c, &c->g_dflash, true);
+    int rc = HY_OK;
+    for (int b = 0; b < kDflashGraphs && !rc; ++b)
+    {
+        for (cudaEvent_t& ev : c->dflash_ev[b])
+            if (!ev) HY_CUDA(cudaEventCreate(&ev));
+        rc = capture_fn(c, &c->g_dflash[b], true, c->dflash_ev[b]);
+    }
     if (!rc) rc = capture_fn(c, &c->g_verify_ids_ctx, false);
     if (!rc) c->d_len = 0;
     return rc;
@@ -2427,6 +2534,47 @@ int hy_debug_progress(const hy_ctx* c, unsigned* out, int n)
     return HY_OK;
 }
 
+int hy_ctx_set_wait_limit(hy_ctx* c, unsigned long long limit_ns)
+{
+    if (!c) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    if (limit_ns < 1000000ull || limit_ns > 60000000000ull)
+        return fail(HY_ERR_INVALID_ARGUMENT, "wait limit must be in 1 ms .. 60 s");
+    c->wait_limit_ns = limit_ns;
+    return HY_OK;
+}
+
+int hy_debug_wait_probe(hy_ctx* c, int kind, unsigned long long limit_ns)
+{
+    if (!c || (kind != 0 && kind != 1)) return fail(HY_ERR_INVALID_ARGUMENT, "kind must be 0 (epoch word) or 1 (mbarrier)");
+    if (limit_ns < 1000ull || limit_ns > 10000000000ull)
+        return fail(HY_ERR_INVALID_ARGUMENT, "probe limit must be in 1 us .. 10 s");
+    int rc = set_device(c);
+    if (rc) return rc;
+    wait_probe_kernel<<<1, 32, 0, c->stream>>>(c->probe_word, kind, limit_ns, c->err);
+    HY_CUDA(cudaGetLastError());
+    return check_device_error(c);
+}
+
+int hy_debug_wait_stats(hy_ctx* c, unsigned long long* out, int n_words, int reset)
+{
+    if (!c || n_words < 0 || (n_words > 0 && !out)) return fail(HY_ERR_INVALID_ARGUMENT, "invalid arguments");
+    if (!c->wstat) return fail(HY_ERR_UNSUPPORTED, "wait statistics need a library built with HY_WAIT_STATS");
+    int rc = set_device(c);
+    if (rc) return rc;
+    if (n_words > 0)
+    {
+        HY_CUDA(cudaMemcpyAsync(out, c->wstat, sizeof(unsigned long long) * std::min(n_words, kWsWords),
+                                cudaMemcpyDeviceToHost, c->stream));
+    }
+    if (reset)
+    {
+        HY_CUDA(cudaMemsetAsync(c->wstat, 0, kWsWords * sizeof(unsigned long long), c->stream));
+        c->mega_launches = 0;
+    }
+    HY_CUDA(cudaStreamSynchronize(c->stream));
+    return HY_OK;
+}
+
 int hy_trace_persistent(hy_ctx* c, int tokens, int trace_token, unsigned long long* out)
 {
     if (!c || !out || tokens < 1 || trace_token < 0 || trace_token >= tokens || tokens > kMegaChunk)
@@ -2507,14 +2655,16 @@ static int history_upload(hy_ctx* c, const int* ids, int n, bool clear)
     int rc = set_device(c);
     if (rc) return rc;
     if (clear) HY_CUDA(cudaMemsetAsync(c->hist, 0, sizeof(unsigned) * ((c->cfg.vocab_size + 31) / 32), c->stream));
-    if (n > 0)
+    // Through the context's pinned and device id buffers, kHistChunk ids per round
+    // (no allocation; each round's copy has finished before the next refills them).
+    for (int done = 0; done < n; done += kHistChunk)
     {
-        int* d = nullptr;
-        HY_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&d), sizeof(int) * n, c->stream));
-        HY_CUDA(cudaMemcpyAsync(d, ids, sizeof(int) * n, cudaMemcpyHostToDevice, c->stream));
-        hist_add_kernel<<<(n + 255) / 256, 256, 0, c->stream>>>(c->hist, d, n, c->cfg.vocab_size);
+        const int m = std::min(kHistChunk, n - done);
+        if (done > 0) HY_CUDA(cudaStreamSynchronize(c->stream));
+        std::memcpy(c->h_hist, ids + done, sizeof(int) * m);
+        HY_CUDA(cudaMemcpyAsync(c->hist_ids, c->h_hist, sizeof(int) * m, cudaMemcpyHostToDevice, c->stream));
+        hist_add_kernel<<<(m + 255) / 256, 256, 0, c->stream>>>(c->hist, c->hist_ids, m, c->cfg.vocab_size);
         HY_CUDA(cudaGetLastError());
-        HY_CUDA(cudaFreeAsync(d, c->stream));
     }
     HY_CUDA(cudaStreamSynchronize(c->stream));
     return HY_OK;
@@ -2641,10 +2791,27 @@ int hy_lm_head_select_noalloc(hy_ctx* c, const float* hidden_dev, int rows, floa
     return check_device_error(c);
 }
 
-int hy_generate(hy_ctx* c, int first_token, int first_raw_top1, int max_tokens, float penalty, const int* eos_ids,
-                int n_eos, int* tokens, int* raw_top1, int* n_tokens)
+// Copy n ints of two device logs to the caller's (nullable) buffers through the
+// pinned h_log area (one synchronisation).
+static int read_logs(hy_ctx* c, const int* dev_a, int* out_a, const int* dev_b, int* out_b, int n_a, int n_b)
 {
-    if (!c || !n_tokens) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    const int cap = c->cfg.max_tokens + 2 * kBlock;
+    if (n_a > cap || n_b > cap) return fail(HY_ERR_CAPACITY, "log longer than the context's token capacity");
+    if (out_a && n_a > 0) HY_CUDA(cudaMemcpyAsync(c->h_log, dev_a, sizeof(int) * n_a, cudaMemcpyDeviceToHost, c->stream));
+    if (out_b && n_b > 0)
+        HY_CUDA(cudaMemcpyAsync(c->h_log + cap, dev_b, sizeof(int) * n_b, cudaMemcpyDeviceToHost, c->stream));
+    HY_CUDA(cudaStreamSynchronize(c->stream));
+    if (out_a && n_a > 0) std::memcpy(out_a, c->h_log, sizeof(int) * n_a);
+    if (out_b && n_b > 0) std::memcpy(out_b, c->h_log + cap, sizeof(int) * n_b);
+    return HY_OK;
+}
+
+// The AR loop behind hy_generate and hy_run_vlm_decode_with_prompt; fills the
+// decode stage of the context's timing (events around the launches).
+static int generate_impl(hy_ctx* c, int first_token, int first_raw_top1, int max_tokens, float penalty,
+                         const int* eos_ids, int n_eos, int* tokens, int* raw_top1, int* n_tokens)
+{
+    if (!n_tokens) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
     if (max_tokens < 1 || max_tokens > c->cfg.max_tokens)
         return fail(HY_ERR_CAPACITY, "max_tokens must be in 1..config max_tokens");
     if (first_token < 0 || first_token >= c->cfg.vocab_size) return fail(HY_ERR_INVALID_ARGUMENT, "first_token out of range");
@@ -2663,13 +2830,16 @@ int hy_generate(hy_ctx* c, int first_token, int first_raw_top1, int max_tokens, 
     for (int i = 0; i < n_eos; ++i) first_eos |= (eos_ids[i] == first_token);
     h.done = (first_eos || max_tokens <= 1) ? 1 : 0;
     if ((rc = push_state(c))) return rc;
-    HY_CUDA(cudaMemcpyAsync(c->log_tokens, &first_token, sizeof(int), cudaMemcpyHostToDevice, c->stream));
-    HY_CUDA(cudaMemcpyAsync(c->log_raw, &first_raw_top1, sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    c->h_small[2] = first_token;
+    c->h_small[3] = first_raw_top1;
+    HY_CUDA(cudaMemcpyAsync(c->log_tokens, c->h_small + 2, sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    HY_CUDA(cudaMemcpyAsync(c->log_raw, c->h_small + 3, sizeof(int), cudaMemcpyHostToDevice, c->stream));
     if ((rc = history_upload(c, &first_token, 1, false))) return rc;
     c->cb_emitted = 0;
     if ((rc = emit_tokens(c, 1))) return rc;
     const int chunk = c->cb ? c->cb_sync : kMegaChunk;
     int launched_steps = 0;
+    HY_CUDA(cudaEventRecord(c->tev[4], c->stream));
     while (!h.done && launched_steps < max_tokens - 1)
     {
         if (c->ar_path == HY_AR_PATH_PERSISTENT)
@@ -2687,17 +2857,87 @@ int hy_generate(hy_ctx* c, int first_token, int first_raw_top1, int max_tokens, 
                 launched_steps += kArStepsPerGraph;
             }
         }
+        HY_CUDA(cudaEventRecord(c->tev[5], c->stream));
         if ((rc = sync_state_to_host(c))) return rc;
         if (h.kv_len + 0 > c->cfg.max_context) return fail(HY_ERR_CAPACITY, "KV capacity exceeded");
         if (c->cb && (rc = check_device_error(c)) == HY_OK) rc = emit_tokens(c, h.n_gen);
         if (rc) return rc;
     }
+    if (launched_steps == 0) HY_CUDA(cudaEventRecord(c->tev[5], c->stream));
     if ((rc = check_device_error(c))) return rc;
     if ((rc = sync_state_to_host(c))) return rc;
     if ((rc = emit_tokens(c, h.n_gen))) return rc;
+    float td = 0.f;
+    HY_CUDA(cudaEventElapsedTime(&td, c->tev[4], c->tev[5]));
+    c->timing.decode_ms = td;
     *n_tokens = h.n_gen;
-    if (tokens) HY_CUDA(cudaMemcpy(tokens, c->log_tokens, sizeof(int) * h.n_gen, cudaMemcpyDeviceToHost));
-    if (raw_top1) HY_CUDA(cudaMemcpy(raw_top1, c->log_raw, sizeof(int) * h.n_gen, cudaMemcpyDeviceToHost));
+    return read_logs(c, c->log_tokens, tokens, c->log_raw, raw_top1, h.n_gen, h.n_gen);
+}
+
+using TimingClock = std::chrono::steady_clock;
+
+// Close the timing of an AR call: wall clock and the part not covered by device stages.
+static int finish_timing(hy_ctx* c, TimingClock::time_point t0, int rc)
+{
+    hy_decode_timing& t = c->timing;
+    t.total_ms = std::chrono::duration<double, std::milli>(TimingClock::now() - t0).count();
+    t.host_overhead_ms = t.total_ms - (t.text_embed_ms + t.prefill_ms + t.lm_head_ms + t.decode_ms);
+    return rc;
+}
+
+// Token and acceptance logs of a DFlash loop to the caller, and the counts of
+// DFlashDecodeResult / DecoderStatistics into the context's DFlash timing.
+static int dflash_results(hy_ctx* c, int* tokens, int* acceptance_lengths)
+{
+    const DecodeState& h = *c->h_st;
+    const int cap = c->cfg.max_tokens + 2 * kBlock;
+    if (h.n_gen > cap || h.block_count > cap) return fail(HY_ERR_CAPACITY, "log longer than the context's token capacity");
+    int* acc = c->h_log + cap;
+    if (tokens && h.n_gen > 0)
+        HY_CUDA(cudaMemcpyAsync(c->h_log, c->log_tokens, sizeof(int) * h.n_gen, cudaMemcpyDeviceToHost, c->stream));
+    if (h.block_count > 0)
+        HY_CUDA(cudaMemcpyAsync(acc, c->accept_log, sizeof(int) * h.block_count, cudaMemcpyDeviceToHost, c->stream));
+    HY_CUDA(cudaStreamSynchronize(c->stream));
+    if (tokens && h.n_gen > 0) std::memcpy(tokens, c->h_log, sizeof(int) * h.n_gen);
+    long long accepted = 0;
+    for (int b = 0; b < h.block_count; ++b) accepted += acc[b];
+    if (acceptance_lengths) std::memcpy(acceptance_lengths, acc, sizeof(int) * h.block_count);
+    c->dtiming.block_count = h.block_count;
+    c->dtiming.drafted_token_count = h.block_count * (kBlock - 1);
+    c->dtiming.accepted_draft_token_count = static_cast<int>(accepted);
+    return HY_OK;
+}
+
+static int finish_dflash_timing(hy_ctx* c, TimingClock::time_point t0, int rc)
+{
+    hy_dflash_timing& t = c->dtiming;
+    t.total_ms = std::chrono::duration<double, std::milli>(TimingClock::now() - t0).count();
+    t.host_overhead_ms = t.total_ms - (t.prefill_ms + t.blocks_ms);
+    return rc;
+}
+
+int hy_generate(hy_ctx* c, int first_token, int first_raw_top1, int max_tokens, float penalty, const int* eos_ids,
+                int n_eos, int* tokens, int* raw_top1, int* n_tokens)
+{
+    if (!c) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    const auto t0 = TimingClock::now();
+    c->timing = hy_decode_timing{};
+    return finish_timing(c, t0,
+                         generate_impl(c, first_token, first_raw_top1, max_tokens, penalty, eos_ids, n_eos, tokens,
+                                       raw_top1, n_tokens));
+}
+
+int hy_ctx_last_timing(const hy_ctx* c, hy_decode_timing* out)
+{
+    if (!c || !out) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    *out = c->timing;
+    return HY_OK;
+}
+
+int hy_ctx_last_dflash_timing(const hy_ctx* c, hy_dflash_timing* out)
+{
+    if (!c || !out) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    *out = c->dtiming;
     return HY_OK;
 }
 
@@ -2767,11 +3007,18 @@ int hy_dflash_generate_synthetic(hy_ctx* c, int first_token, int max_tokens, flo
     if ((rc = push_state(c))) return rc;
     int launched = 0;
     c->cb_emitted = 0;
+    const auto t0 = TimingClock::now();
+    c->dtiming = hy_dflash_timing{};
     while (!h.done && launched < max_tokens)
     {
-        for (int i = 0; i < 4 && launched < max_tokens; ++i, ++launched)
+        HY_CUDA(cudaEventRecord(c->tev[4], c->stream));
+        for (int i = 0; i < kDflashGraphs && launched < max_tokens; ++i, ++launched)
             HY_CUDA(cudaGraphLaunch(c->g_verify_draft, c->stream));
+        HY_CUDA(cudaEventRecord(c->tev[5], c->stream));
         if ((rc = sync_state_to_host(c))) return rc;
+        float ms = 0.f;
+        HY_CUDA(cudaEventElapsedTime(&ms, c->tev[4], c->tev[5]));
+        c->dtiming.blocks_ms += ms;
         if (c->cb && (rc = check_device_error(c)) == HY_OK) rc = emit_tokens(c, h.n_gen);
         if (rc) return rc;
     }
@@ -2780,10 +3027,8 @@ int hy_dflash_generate_synthetic(hy_ctx* c, int first_token, int max_tokens, flo
     if ((rc = emit_tokens(c, h.n_gen))) return rc;
     *n_tokens = h.n_gen;
     if (n_blocks) *n_blocks = h.block_count;
-    if (tokens) HY_CUDA(cudaMemcpy(tokens, c->log_tokens, sizeof(int) * h.n_gen, cudaMemcpyDeviceToHost));
-    if (acceptance_lengths)
-        HY_CUDA(cudaMemcpy(acceptance_lengths, c->accept_log, sizeof(int) * h.block_count, cudaMemcpyDeviceToHost));
-    return HY_OK;
+    rc = dflash_results(c, tokens, acceptance_lengths);
+    return finish_dflash_timing(c, t0, rc);
 }
 
 // The prompt half of run_vlm_decode_with_prompt (src/text_runtime.cpp:2053-2094,
@@ -2814,15 +3059,22 @@ static int prompt_prefill_first(hy_ctx* c, const int* input_ids, const int* posi
                                                  ", expected " + std::to_string(vision_token_count));
     int rc = set_device(c);
     if (rc) return rc;
-    std::vector<float> cos(static_cast<size_t>(seq_len) * kHeadDim), sin(static_cast<size_t>(seq_len) * kHeadDim);
-    if ((rc = hy_build_mrope(position_ids, seq_len, 1, cos.data())) || (rc = hy_build_mrope(position_ids, seq_len, 0, sin.data())))
+    // The prompt's host inputs and tables go through the context's pinned staging
+    // area (filled on the host, then copied without a staging pass in the driver);
+    // the previous call finished with it before returning.
+    const PromptStage ps = prompt_stage(c);
+    std::memcpy(ps.ids, input_ids, sizeof(int) * seq_len);
+    std::memcpy(ps.feat_idx, feat_idx.data(), sizeof(int) * seq_len);
+    std::memcpy(ps.feats, vision_features, sizeof(float) * vision_token_count * kHidden);
+    if ((rc = hy_build_mrope(position_ids, seq_len, 1, ps.cos)) || (rc = hy_build_mrope(position_ids, seq_len, 0, ps.sin)))
         return rc;
-    HY_CUDA(cudaMemcpyAsync(c->ids_buf, input_ids, sizeof(int) * seq_len, cudaMemcpyHostToDevice, c->stream));
-    HY_CUDA(cudaMemcpyAsync(c->feat_idx, feat_idx.data(), sizeof(int) * seq_len, cudaMemcpyHostToDevice, c->stream));
-    HY_CUDA(cudaMemcpyAsync(c->feats, vision_features, sizeof(float) * vision_token_count * kHidden,
-                            cudaMemcpyHostToDevice, c->stream));
-    HY_CUDA(cudaMemcpyAsync(c->pre_cos, cos.data(), sizeof(float) * seq_len * kHeadDim, cudaMemcpyHostToDevice, c->stream));
-    HY_CUDA(cudaMemcpyAsync(c->pre_sin, sin.data(), sizeof(float) * seq_len * kHeadDim, cudaMemcpyHostToDevice, c->stream));
+    HY_CUDA(cudaEventRecord(c->tev[0], c->stream));
+    HY_CUDA(cudaMemcpyAsync(c->ids_buf, ps.ids, sizeof(int) * seq_len, cudaMemcpyHostToDevice, c->stream));
+    HY_CUDA(cudaMemcpyAsync(c->feat_idx, ps.feat_idx, sizeof(int) * seq_len, cudaMemcpyHostToDevice, c->stream));
+    HY_CUDA(cudaMemcpyAsync(c->feats, ps.feats, sizeof(float) * vision_token_count * kHidden, cudaMemcpyHostToDevice,
+                            c->stream));
+    HY_CUDA(cudaMemcpyAsync(c->pre_cos, ps.cos, sizeof(float) * seq_len * kHeadDim, cudaMemcpyHostToDevice, c->stream));
+    HY_CUDA(cudaMemcpyAsync(c->pre_sin, ps.sin, sizeof(float) * seq_len * kHeadDim, cudaMemcpyHostToDevice, c->stream));
     if (c->cfg.weight_dtype == HY_DTYPE_BF16)
         embed_prompt_kernel<__nv_bfloat16><<<seq_len, 256, 0, c->stream>>>(
             c->ids_buf, c->feat_idx, c->feats, static_cast<const __nv_bfloat16*>(c->embed), c->cfg.vocab_size, c->prompt, c->err);
@@ -2835,14 +3087,28 @@ static int prompt_prefill_first(hy_ctx* c, const int* input_ids, const int* posi
     HY_CUDA(cudaMemsetAsync(c->hist, 0, sizeof(unsigned) * ((c->cfg.vocab_size + 31) / 32), c->stream));
     hist_add_kernel<<<(seq_len + 255) / 256, 256, 0, c->stream>>>(c->hist, c->ids_buf, seq_len, c->cfg.vocab_size);
     HY_CUDA(cudaGetLastError());
+    HY_CUDA(cudaEventRecord(c->tev[1], c->stream));
     if ((rc = run_prefill(c, seq_len))) return rc;
+    HY_CUDA(cudaEventRecord(c->tev[2], c->stream));
     cudaError_t e = enqueue_lm_select(c, 1, c->hidden, repetition_penalty, false, nullptr);
     if (e != cudaSuccess) return fail(HY_ERR_CUDA, std::string("LM head launch: ") + cudaGetErrorString(e));
-    HY_CUDA(cudaMemcpyAsync(first, c->tok_out, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
-    HY_CUDA(cudaMemcpyAsync(first_raw, c->raw_out, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    HY_CUDA(cudaEventRecord(c->tev[3], c->stream));
+    HY_CUDA(cudaMemcpyAsync(c->h_small, c->tok_out, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    HY_CUDA(cudaMemcpyAsync(c->h_small + 1, c->raw_out, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
     if ((rc = check_device_error(c))) return rc;
+    *first = c->h_small[0];
+    *first_raw = c->h_small[1];
     if ((rc = set_length(c, seq_len))) return rc;
     if (c->d_layers > 0) c->d_len = seq_len;
+    // Device time of the prompt stages (the events have completed).
+    float te = 0.f, tp = 0.f, tl = 0.f;
+    HY_CUDA(cudaEventElapsedTime(&te, c->tev[0], c->tev[1]));
+    HY_CUDA(cudaEventElapsedTime(&tp, c->tev[1], c->tev[2]));
+    HY_CUDA(cudaEventElapsedTime(&tl, c->tev[2], c->tev[3]));
+    c->timing.text_embed_ms = te;
+    c->timing.prefill_ms = tp;
+    c->timing.lm_head_ms = tl;
+    c->timing.token_select_ms = 0.0;
     return HY_OK;
 }
 
@@ -2854,11 +3120,14 @@ int hy_run_vlm_decode_with_prompt(hy_ctx* c, const int* input_ids, const int* po
     if (!c || !n_tokens) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
     if (max_tokens <= 0) max_tokens = 1024;   // src/text_runtime.cpp:1336-1341
     if (max_tokens > c->cfg.max_tokens) return fail(HY_ERR_CAPACITY, "max_tokens exceeds config max_tokens");
+    const auto t0 = TimingClock::now();
+    c->timing = hy_decode_timing{};
     int first = 0, first_raw = 0;
     int rc = prompt_prefill_first(c, input_ids, position_ids, seq_len, image_token_id, vision_features,
                                   vision_token_count, repetition_penalty, &first, &first_raw);
-    if (rc) return rc;
-    return hy_generate(c, first, first_raw, max_tokens, repetition_penalty, eos_ids, n_eos, tokens, raw_top1, n_tokens);
+    if (rc) return finish_timing(c, t0, rc);
+    return finish_timing(c, t0, generate_impl(c, first, first_raw, max_tokens, repetition_penalty, eos_ids, n_eos,
+                                              tokens, raw_top1, n_tokens));
 }
 
 // ---- DFlash draft network --------------------------------------------------
@@ -2972,10 +3241,10 @@ int hy_draft_propose(hy_ctx* c, int current_token, int* proposed)
     return check_device_error(c);
 }
 
-int hy_dflash_generate(hy_ctx* c, int first_token, int max_tokens, float penalty, const int* eos_ids, int n_eos,
-                       int* tokens, int* n_tokens, int* acceptance_lengths, int* n_blocks)
+static int dflash_generate_impl(hy_ctx* c, int first_token, int max_tokens, float penalty, const int* eos_ids,
+                                int n_eos, int* tokens, int* n_tokens, int* acceptance_lengths, int* n_blocks)
 {
-    if (!c || !n_tokens) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    if (!n_tokens) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
     int rc = draft_in_sync(c);
     if (rc) return rc;
     if (max_tokens < 1 || max_tokens > c->cfg.max_tokens)
@@ -2996,23 +3265,46 @@ int hy_dflash_generate(hy_ctx* c, int first_token, int max_tokens, float penalty
     if ((rc = push_state(c))) return rc;
     int launched = 0;
     c->cb_emitted = 0;
+    hy_dflash_timing& t = c->dtiming;
     while (!h.done && launched < max_tokens)
     {
-        for (int i = 0; i < 4 && launched < max_tokens; ++i, ++launched) HY_CUDA(cudaGraphLaunch(c->g_dflash, c->stream));
+        int n = 0;
+        for (; n < kDflashGraphs && launched < max_tokens; ++n, ++launched)
+            HY_CUDA(cudaGraphLaunch(c->g_dflash[n], c->stream));
+        HY_CUDA(cudaEventRecord(c->tev[5], c->stream));
         if ((rc = sync_state_to_host(c))) return rc;
+        // Stage times of this group's blocks (each block ends where the next starts).
+        for (int b = 0; b < n; ++b)
+        {
+            float a = 0.f, v = 0.f, m = 0.f;
+            HY_CUDA(cudaEventElapsedTime(&a, c->dflash_ev[b][0], c->dflash_ev[b][1]));
+            HY_CUDA(cudaEventElapsedTime(&v, c->dflash_ev[b][1], c->dflash_ev[b][2]));
+            HY_CUDA(cudaEventElapsedTime(&m, c->dflash_ev[b][2], b + 1 < n ? c->dflash_ev[b + 1][0] : c->tev[5]));
+            t.draft_ms += a;
+            t.verify_ms += v;
+            t.commit_ms += m;
+        }
         if (c->cb && (rc = check_device_error(c)) == HY_OK) rc = emit_tokens(c, h.n_gen);
         if (rc) return rc;
     }
+    t.blocks_ms = t.draft_ms + t.verify_ms + t.commit_ms;
     if ((rc = check_device_error(c))) return rc;
     if ((rc = sync_state_to_host(c))) return rc;
     if ((rc = emit_tokens(c, h.n_gen))) return rc;
     c->d_len = c->kv_len;
     *n_tokens = h.n_gen;
     if (n_blocks) *n_blocks = h.block_count;
-    if (tokens) HY_CUDA(cudaMemcpy(tokens, c->log_tokens, sizeof(int) * h.n_gen, cudaMemcpyDeviceToHost));
-    if (acceptance_lengths)
-        HY_CUDA(cudaMemcpy(acceptance_lengths, c->accept_log, sizeof(int) * h.block_count, cudaMemcpyDeviceToHost));
-    return HY_OK;
+    return dflash_results(c, tokens, acceptance_lengths);
+}
+
+int hy_dflash_generate(hy_ctx* c, int first_token, int max_tokens, float penalty, const int* eos_ids, int n_eos,
+                       int* tokens, int* n_tokens, int* acceptance_lengths, int* n_blocks)
+{
+    if (!c) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
+    const auto t0 = TimingClock::now();
+    c->dtiming = hy_dflash_timing{};
+    return finish_dflash_timing(c, t0, dflash_generate_impl(c, first_token, max_tokens, penalty, eos_ids, n_eos, tokens,
+                                                            n_tokens, acceptance_lengths, n_blocks));
 }
 
 int hy_run_vlm_dflash_with_prompt(hy_ctx* c, const int* input_ids, const int* position_ids, int seq_len,
@@ -3024,12 +3316,15 @@ int hy_run_vlm_dflash_with_prompt(hy_ctx* c, const int* input_ids, const int* po
     if (!draft_ready(c)) return fail(HY_ERR_NOT_READY, "DFlash draft runtime is not loaded");
     if (max_tokens <= 0) max_tokens = 1024;   // src/text_runtime.cpp:1168-1171
     if (max_tokens > c->cfg.max_tokens) return fail(HY_ERR_CAPACITY, "max_tokens exceeds config max_tokens");
+    const auto t0 = TimingClock::now();
+    c->dtiming = hy_dflash_timing{};
     int first = 0, first_raw = 0;
     int rc = prompt_prefill_first(c, input_ids, position_ids, seq_len, image_token_id, vision_features,
                                   vision_token_count, repetition_penalty, &first, &first_raw);
-    if (rc) return rc;
-    return hy_dflash_generate(c, first, max_tokens, repetition_penalty, eos_ids, n_eos, tokens, n_tokens,
-                              acceptance_lengths, n_blocks);
+    c->dtiming.prefill_ms = c->timing.text_embed_ms + c->timing.prefill_ms + c->timing.lm_head_ms;
+    if (rc) return finish_dflash_timing(c, t0, rc);
+    return finish_dflash_timing(c, t0, dflash_generate_impl(c, first, max_tokens, repetition_penalty, eos_ids, n_eos,
+                                                            tokens, n_tokens, acceptance_lengths, n_blocks));
 }
 
 // ---- batched decode -----------------------------------------------------
@@ -3200,13 +3495,21 @@ int hy_fixture_meta(const char* fixture_dir, int* seq_len, int* expected_token_c
     return fixture_meta(fixture_dir, seq_len, expected_token_count, image_token_id, vision_token_count);
 }
 
-int hy_fixture_load(const char* fixture_dir, int* input_ids, int* position_ids, int* expected_tokens,
-                    float* vision_features)
+int hy_fixture_load(const char* fixture_dir, int seq_capacity, int expected_capacity, int vision_capacity,
+                    int* input_ids, int* position_ids, int* expected_tokens, float* vision_features)
 {
     if (!fixture_dir || !input_ids || !position_ids || !expected_tokens) return fail(HY_ERR_INVALID_ARGUMENT, "null argument");
     int seq = 0, expected = 0, image = 0, vision = 0;
     int rc = fixture_meta(fixture_dir, &seq, &expected, &image, &vision);
     if (rc) return rc;
+    // meta.txt is read again here: the buffers were sized from an earlier read,
+    // which the file may no longer match.
+    if (seq > seq_capacity || expected > expected_capacity || (vision_features && vision > vision_capacity))
+        return fail(HY_ERR_CAPACITY, "fixture meta asks for seq_len=" + std::to_string(seq) +
+                                         ", expected_token_count=" + std::to_string(expected) +
+                                         ", vision_token_count=" + std::to_string(vision) +
+                                         " but the buffers hold " + std::to_string(seq_capacity) + ", " +
+                                         std::to_string(expected_capacity) + ", " + std::to_string(vision_capacity));
     const std::string root(fixture_dir);
     if ((rc = fixture_vector(root + "/input_ids.i32", seq, sizeof(int), input_ids))) return rc;
     if ((rc = fixture_vector(root + "/position_ids.i32", static_cast<size_t>(seq) * 4, sizeof(int), position_ids)))
@@ -3271,8 +3574,7 @@ static int kv_copy(hy_ctx* c, int layer, int start, int rows, const float* k, co
     if (rc) return rc;
     const size_t es = c->kv_elem();
     const size_t n = static_cast<size_t>(rows) * kHeadDim;
-    float* stage = nullptr;
-    HY_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&stage), n * sizeof(float), c->stream));
+    float* stage = c->kv_stage;   // [max_context x 128]: one head's rows at a time (reuse ordered by the stream)
     for (int which = 0; which < 2; ++which)
     {
         char* base = static_cast<char*>(which == 0 ? c->kc_layer(layer) : c->vc_layer(layer));
@@ -3304,7 +3606,6 @@ static int kv_copy(hy_ctx* c, int layer, int start, int rows, const float* k, co
             }
         }
     }
-    HY_CUDA(cudaFreeAsync(stage, c->stream));
     HY_CUDA(cudaStreamSynchronize(c->stream));
     return HY_OK;
 }

@@ -121,15 +121,16 @@ __device__ __forceinline__ unsigned long long global_ns()
 }
 
 // Bounded wait for phase `parity` of `bar`. Returns false (and sets `err_bit`
-// in *err) when the wall-clock limit passes first.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int err_bit)
+// in *err) when the wall-clock limit (limit_ns) passes first.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int err_bit,
+                                          unsigned long long limit_ns = kWaitLimitNs)
 {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = global_ns();
     while (true)
     {
         if (mbar_try_wait(bar, parity)) return true;
-        if (global_ns() - t0 > kWaitLimitNs)
+        if (global_ns() - t0 > limit_ns)
         {
             if (err) atomicOr(err, err_bit);
             return false;

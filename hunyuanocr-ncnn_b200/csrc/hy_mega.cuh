@@ -124,7 +124,47 @@ struct MegaArgs {
     unsigned long long* attn_ep;      // split partials [8 heads][8 past splits][2][kAttnWords]
     unsigned long long* attn_out_ep;  // merged attention output [2048]
     unsigned epoch_base;
+    // Wait statistics (only in builds with HY_WAIT_STATS defined; nullptr otherwise):
+    // per CTA and wait kind the waits longer than kWsLongNs (count, total ns, longest),
+    // and per launch slot the first CTA start and last CTA exit (%globaltimer).
+    unsigned long long* wstat;
+    int launch_slot;
+    unsigned long long wait_limit_ns;   // bound of every wait in the kernel (default 2 s)
 };
+
+// Kinds of wait counted by the HY_WAIT_STATS build.
+enum {
+    WS_SLOT_FREE = 0,   // consumer: the slot's previous stage released
+    WS_SLOT_FULL,       // consumer: the stage's bytes landed
+    WS_PROD_EMPTY,      // producer: the slot released for refill
+    WS_PROD_TOKEN,      // producer: the consumers acquired the previous token
+    WS_POLL_X,          // residual stream (q/k/v, gate/up and LM prologues)
+    WS_POLL_ACT,        // SwiGLU outputs (down_proj prologue)
+    WS_POLL_ATTN_OUT,   // merged attention outputs (o_proj prologue)
+    WS_POLL_QKV,        // q/k/v rows (attention prologue)
+    WS_POLL_PARTS,      // split partials (attention merge)
+    WS_POLL_TOKEN,      // the previous token's commit
+    WS_KINDS
+};
+constexpr int kWsCtas = 160;
+constexpr int kWsLaunches = 64;
+constexpr unsigned long long kWsLongNs = 20000;
+// Layout of the statistics buffer (unsigned long long words).
+constexpr int kWsLaunchBase = kWsCtas * WS_KINDS * 3;            // [kWsLaunches][2]: ~first start, last end
+constexpr int kWsWords = kWsLaunchBase + kWsLaunches * 2;
+
+__device__ __forceinline__ void ws_record(unsigned long long* ws, int b, int kind, unsigned long long ns)
+{
+#ifdef HY_WAIT_STATS
+    if (ws && b < kWsCtas && ns > kWsLongNs)
+    {
+        unsigned long long* r = ws + (static_cast<size_t>(b) * WS_KINDS + kind) * 3;
+        atomicAdd(r, 1ull);
+        atomicAdd(r + 1, ns);
+        atomicMax(r + 2, ns);
+    }
+#endif
+}
 
 #ifndef HY_TRACE_CTAS
 #define HY_TRACE_CTAS 4
@@ -348,7 +388,8 @@ __device__ __forceinline__ void st_release_u64(unsigned long long* p, unsigned l
 // (and sets the timeout bit) when the wall-clock limit passes first.
 template <int PER>
 __device__ __forceinline__ bool poll_words(const unsigned long long* src, int n, int first, int stride, unsigned e,
-                                           float (&out)[PER], int* err)
+                                           float (&out)[PER], int* err, unsigned long long limit_ns,
+                                           unsigned long long* ws = nullptr, int b = 0, int kind = 0)
 {
     const unsigned long long done = static_cast<unsigned long long>(e) << 32;   // value 0, epoch e
     unsigned long long w[PER];
@@ -368,7 +409,7 @@ __device__ __forceinline__ bool poll_words(const unsigned long long* src, int n,
         if (all) break;
         const unsigned long long now = global_ns();
         if (t0 == 0) t0 = now;
-        else if (now - t0 > kWaitLimitNs)
+        else if (now - t0 > limit_ns)
         {
             atomicOr(err, kErrTimeoutFull);
             ok = false;
@@ -379,9 +420,52 @@ __device__ __forceinline__ bool poll_words(const unsigned long long* src, int n,
         for (int u = 0; u < PER; ++u)
             if (static_cast<unsigned>(w[u] >> 32) != e) w[u] = ld_relaxed_u64(src + first + stride * u);
     }
+#ifdef HY_WAIT_STATS
+    if (t0) ws_record(ws, b, kind, global_ns() - t0);
+#endif
 #pragma unroll
     for (int u = 0; u < PER; ++u) out[u] = __uint_as_float(static_cast<unsigned>(w[u]));
     return ok;
+}
+
+// mbar_wait that also counts long waits in the HY_WAIT_STATS build.
+__device__ __forceinline__ bool mega_mbar_wait(uint64_t* bar, uint32_t parity, int* err, int err_bit,
+                                               unsigned long long limit_ns, unsigned long long* ws, int b, int kind)
+{
+#ifdef HY_WAIT_STATS
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    const bool ok = mbar_wait(bar, parity, err, err_bit, limit_ns);
+    ws_record(ws, b, kind, global_ns() - t0);
+    return ok;
+#else
+    return mbar_wait(bar, parity, err, err_bit, limit_ns);
+#endif
+}
+
+// Bounded-wait self-test: waits, with the library's own primitives, for
+// something that nothing provides. kind 0: poll_words on an epoch word that
+// never carries the awaited epoch; kind 1: mbar_wait on a shared-memory
+// mbarrier phase that never completes. Each gives up after limit_ns and sets
+// the timeout bit in *err; no copy is in flight, so the early return is clean.
+__global__ void wait_probe_kernel(const unsigned long long* word, int kind, unsigned long long limit_ns, int* err)
+{
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0)
+    {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (kind == 0)
+    {
+        float v[1];
+        poll_words<1>(word, 1, 0, 1, 0xFFFFFFFFu, v, err, limit_ns);
+    }
+    else
+    {
+        mbar_wait(&bar, 0, err, kErrTimeoutFull, limit_ns);
+    }
 }
 
 // Where a GEMV phase's epilogue publishes its outputs, and with which epoch.
@@ -672,6 +756,10 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
         redi[0] = 0;  // abort flag
     }
     mega_init_tables<WT>(a, tb, b, G, tid);
+#ifdef HY_WAIT_STATS
+    if (tid == 0 && a.wstat)
+        atomicMax(a.wstat + kWsLaunchBase + 2 * (a.launch_slot % kWsLaunches), ~global_ns());
+#endif
     __syncthreads();
 
     if (warp == kMegaWarps)
@@ -689,7 +777,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                 mega_phase_of(ph, L, layer, kind);
                 const MegaPlan p = mega_plan<KT>(a, tb, layer, kind, kv0 + t, b);
                 if (kind == PH_ATTN && layer == 0 && t > 0 && p.nstage > 0 &&
-                    !mbar_wait(tokbar, (t - 1) & 1, a.err, kErrTimeoutEmpty))
+                    !mega_mbar_wait(tokbar, (t - 1) & 1, a.err, kErrTimeoutEmpty, a.wait_limit_ns, a.wstat, b, WS_PROD_TOKEN))
                 {
                     ok = false;
                     break;
@@ -699,7 +787,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                     const int s = static_cast<int>(g % kMegaSlots);
                     const unsigned j = g / kMegaSlots;   // use of the slot
                     // The slot's previous stage (g - kMegaSlots) was released by its warp.
-                    if (j >= 1 && !mbar_wait(&empty[s], (j - 1) & 1, a.err, kErrTimeoutEmpty))
+                    if (j >= 1 && !mega_mbar_wait(&empty[s], (j - 1) & 1, a.err, kErrTimeoutEmpty, a.wait_limit_ns, a.wstat, b, WS_PROD_EMPTY))
                     {
                         ok = false;
                         break;
@@ -745,8 +833,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
     auto wait_stage = [&](unsigned g) -> int {
         const int slot = static_cast<int>(g % kMegaSlots);
         const unsigned j = g / kMegaSlots;
-        bool okw = (j == 0) || mbar_wait(&empty[slot], (j - 1) & 1, a.err, kErrTimeoutEmpty);
-        okw = okw && mbar_wait(&full[slot], j & 1, a.err, kErrTimeoutFull);
+        bool okw = (j == 0) || mega_mbar_wait(&empty[slot], (j - 1) & 1, a.err, kErrTimeoutEmpty, a.wait_limit_ns, a.wstat, b, WS_SLOT_FREE);
+        okw = okw && mega_mbar_wait(&full[slot], j & 1, a.err, kErrTimeoutFull, a.wait_limit_ns, a.wstat, b, WS_SLOT_FULL);
         return __all_sync(0xffffffffu, okw) ? slot : -1;
     };
 
@@ -797,7 +885,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                         const unsigned long long t0 = global_ns();
                         while (static_cast<unsigned>(w >> 32) != e_in)
                         {
-                            if (global_ns() - t0 > kWaitLimitNs)
+                            if (global_ns() - t0 > a.wait_limit_ns)
                             {
                                 atomicOr(a.err, kErrTimeoutFull);
                                 redi[0] = 1;
@@ -806,6 +894,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                             __nanosleep(HY_POLL_NS);
                             w = ld_acquire_u64(a.tok_ep);
                         }
+#ifdef HY_WAIT_STATS
+                        ws_record(a.wstat, b, WS_POLL_TOKEN, global_ns() - t0);
+#endif
                         id = static_cast<int>(static_cast<unsigned>(w));
                         if (tid == 0) mbar_arrive(tokbar);   // after this thread's acquire
                     }
@@ -824,7 +915,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                     // The residual rows this CTA owns start as the embedding.
                     if (tid < po.count && tid < kMegaResRows) xres_s[tid] = to_f32<WT>(erow[po.r0 + tid]);
                 }
-                else if (!poll_words<kXPer>(a.x_ep, kHidden, tid, kMegaConsumers, e_in, v, a.err))
+                else if (!poll_words<kXPer>(a.x_ep, kHidden, tid, kMegaConsumers, e_in, v, a.err, a.wait_limit_ns, a.wstat, b, WS_POLL_X))
                 {
                     redi[0] = 1;
                 }
@@ -844,7 +935,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                 // act = silu(gate) * up from the gate/up phase.
                 constexpr int kPer = (kMegaMaxK + kMegaConsumers - 1) / kMegaConsumers;
                 float v[kPer];
-                if (!poll_words<kPer>(a.act_ep, a.ffn, tid, kMegaConsumers, e_in, v, a.err)) redi[0] = 1;
+                if (!poll_words<kPer>(a.act_ep, a.ffn, tid, kMegaConsumers, e_in, v, a.err, a.wait_limit_ns, a.wstat, b, WS_POLL_ACT))
+                    redi[0] = 1;
 #pragma unroll
                 for (int u = 0; u < kPer; ++u)
                 {
@@ -858,7 +950,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                 // The attention output of all 16 heads (merged by each head pair's new-row split).
                 constexpr int kPer = (kQWidth + kMegaConsumers - 1) / kMegaConsumers;
                 float v[kPer];
-                if (!poll_words<kPer>(a.attn_out_ep, kQWidth, tid, kMegaConsumers, e_in, v, a.err)) redi[0] = 1;
+                if (!poll_words<kPer>(a.attn_out_ep, kQWidth, tid, kMegaConsumers, e_in, v, a.err, a.wait_limit_ns, a.wstat, b,
+                                      WS_POLL_ATTN_OUT))
+                    redi[0] = 1;
 #pragma unroll
                 for (int u = 0; u < kPer; ++u)
                 {
@@ -1029,7 +1123,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                 if (warp < 2)
                 {
                     float x[4], o[4];
-                    if (!poll_words<4>(a.qkv_ep + (2 * g + warp) * kHeadDim, kHeadDim, lane, 32, e_in, x, a.err))
+                    if (!poll_words<4>(a.qkv_ep + (2 * g + warp) * kHeadDim, kHeadDim, lane, 32, e_in, x, a.err,
+                                       a.wait_limit_ns, a.wstat, b, WS_POLL_QKV))
                         redi[0] = 1;
                     rope_norm_vals(x, c, s, qn_w, a.eps, lane, o);
 #pragma unroll
@@ -1038,7 +1133,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                 else if (new_split && warp == 2)
                 {
                     float x[4], o[4];
-                    if (!poll_words<4>(a.qkv_ep + kQWidth + g * kHeadDim, kHeadDim, lane, 32, e_in, x, a.err))
+                    if (!poll_words<4>(a.qkv_ep + kQWidth + g * kHeadDim, kHeadDim, lane, 32, e_in, x, a.err, a.wait_limit_ns, a.wstat, b,
+                                       WS_POLL_QKV))
                         redi[0] = 1;
                     rope_norm_vals(x, c, s, kn_w, a.eps, lane, o);
                     mega_check(past >= 0 && past < a.cap, a.dbg, 5, b, ph, past);
@@ -1057,7 +1153,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                 else if (new_split && warp == 3)
                 {
                     float x[4];
-                    if (!poll_words<4>(a.qkv_ep + kQWidth + kKVWidth + g * kHeadDim, kHeadDim, lane, 32, e_in, x, a.err))
+                    if (!poll_words<4>(a.qkv_ep + kQWidth + kKVWidth + g * kHeadDim, kHeadDim, lane, 32, e_in, x, a.err,
+                                       a.wait_limit_ns, a.wstat, b, WS_POLL_QKV))
                         redi[0] = 1;
                     KT* vrow = static_cast<KT*>(a.vc) +
                                ((static_cast<size_t>(layer) * kNumKVHeads + g) * a.cap + min(past, a.cap - 1)) * kHeadDim;
@@ -1269,7 +1366,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                     float* parts = reinterpret_cast<float*>(smem + MegaSmem::PARTS);
                     float v[kPer];
                     if (!poll_words<kPer>(a.attn_ep + static_cast<size_t>(g) * kWords, kWords, tid, kMegaConsumers, eo.e,
-                                          v, a.err))
+                                          v, a.err, a.wait_limit_ns, a.wstat, b, WS_POLL_PARTS))
                         redi[0] = 1;
 #pragma unroll
                     for (int u = 0; u < kPer; ++u)
@@ -1322,6 +1419,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
             if (tid == 0 && a.progress) a.progress[b] = static_cast<unsigned>(t * phases + ph + 1);
         }
     }
+#ifdef HY_WAIT_STATS
+    if (tid == 0 && a.wstat) atomicMax(a.wstat + kWsLaunchBase + 2 * (a.launch_slot % kWsLaunches) + 1, global_ns());
+#endif
 }
 
 }  // namespace hy

@@ -113,7 +113,8 @@ void hy_ctx_destroy(hy_ctx* ctx);
 
 /* How hy_generate runs the AR loop. HY_AR_PATH_PERSISTENT (default): one
  * cooperative kernel per up to 64 tokens, one CTA per SM, all 24 layers and the
- * LM head of each token inside it with grid barriers between phases.
+ * LM head of each token inside it; the CTAs exchange each phase's outputs as
+ * epoch-tagged words that the next phase polls (no grid barrier).
  * HY_AR_PATH_GRAPH: one CUDA-graph replay of 121 kernels per token. Both compute
  * the same step (the reference's decode loop, src/text_runtime.cpp:1417-1508). */
 enum hy_ar_path { HY_AR_PATH_PERSISTENT = 0, HY_AR_PATH_GRAPH = 1 };
@@ -130,22 +131,48 @@ int hy_ctx_ar_path(const hy_ctx* ctx);
  * NULL removes the callback. */
 typedef void (*hy_token_callback)(int token, void* user);
 int hy_ctx_set_token_callback(hy_ctx* ctx, hy_token_callback callback, void* user, int tokens_per_sync);
-/* Per-phase trace of the persistent kernel (the counterpart of the reference's
- * stage timers, include/hunyuan_ocr/text_runtime.h:32-39): runs `tokens` AR
- * steps from the current state and, for CTAs 0..3 during token `trace_token`,
- * stores %globaltimer (ns) at phase start, after the grid wait, after the
- * prologue, at the barrier arrive, and the producer's first and last stage
- * issue, the first and last stage observed, and for warp 0 of a GEMV phase the
- * ns spent waiting for stages, the ns spent in its dot products and its unit
- * count: out[(cta * (5 * num_layers + 1) + phase) * 12 + i] (slot 11 unused).
- * The sequence length is restored afterwards. */
-int hy_trace_persistent(hy_ctx* ctx, int tokens, int trace_token, unsigned long long* out);
-/* Failure diagnosis for the persistent kernel: with HY_DEBUG_PROGRESS=1 in the
- * environment at context creation, each CTA records in host-mapped memory how
- * many phases it completed; readable even after a device fault. */
-int hy_debug_progress(const hy_ctx* ctx, unsigned* out, int n);
 int hy_ctx_config(const hy_ctx* ctx, hy_config* cfg);
 size_t hy_ctx_device_bytes(const hy_ctx* ctx);   /* replaces mapped_weight_bytes() */
+
+/* TextDecodeTiming (include/hunyuan_ocr/text_runtime.h:32-39, filled by host
+ * clocks at src/text_runtime.cpp:1389-1511) of the last hy_generate /
+ * hy_run_vlm_decode_with_prompt call on the context. Device stages are CUDA
+ * events on the context's stream; total_ms is the host clock of the call. */
+typedef struct hy_decode_timing {
+    double text_embed_ms;     /* prompt upload, embedding with vision-feature injection, history */
+    double prefill_ms;        /* prefill of all prompt rows */
+    double decode_ms;         /* the decode loop: per token embed, all layers, LM head and selection
+                                 (one fused kernel), launch gaps included */
+    double lm_head_ms;        /* the first token's LM head and selection (later tokens': decode_ms) */
+    double token_select_ms;   /* 0: selection is fused into the LM-head kernels */
+    double total_ms;          /* host clock of the call */
+    double host_overhead_ms;  /* total_ms minus the device stages: host work, copies, waits */
+} hy_decode_timing;
+int hy_ctx_last_timing(const hy_ctx* ctx, hy_decode_timing* out);
+
+/* DFlashDecodeTiming (text_runtime.h:64-74, filled at src/text_runtime.cpp:
+ * 913-1069, 1240-1302) with the counts of DFlashDecodeResult (76-83) and
+ * DecoderStatistics (include/hunyuan_ocr/hunyuan_ocr.h:55-65) of the last
+ * hy_dflash_generate / hy_run_vlm_dflash_with_prompt /
+ * hy_dflash_generate_synthetic call. A block is one graph on the device; with
+ * the draft network its stages are split by events inside every block's graph:
+ * draft (draft_prepare + draft_infer + draft_postprocess of the reference),
+ * verify (verify_prepare + verify_infer, with the block's draft context rows)
+ * and commit (verify_postprocess + commit: LM head, posterior, acceptance,
+ * commit and rollback). With the synthetic drafter only blocks_ms is split off. */
+typedef struct hy_dflash_timing {
+    double prefill_ms;        /* prompt upload, embedding, prefill and first token (device) */
+    double draft_ms;
+    double verify_ms;
+    double commit_ms;
+    double blocks_ms;         /* all blocks on the device */
+    double total_ms;          /* host clock of the call */
+    double host_overhead_ms;  /* total_ms minus prefill_ms and blocks_ms */
+    int block_count;
+    int drafted_token_count;          /* 15 per block */
+    int accepted_draft_token_count;   /* sum of the acceptance lengths */
+} hy_dflash_timing;
+int hy_ctx_last_dflash_timing(const hy_ctx* ctx, hy_dflash_timing* out);
 
 /* ---- host table builders (host code, no device work) ---------------- */
 /* detail::build_mrope (src/text_runtime.cpp:42-63): position_ids [4 x seq]
@@ -199,8 +226,15 @@ int hy_lm_head_select(hy_ctx* ctx, const float* hidden, int rows, const int* row
  * array of 65,792 bytes (partials for at most 16 rows x 256 CTAs), one per
  * device and process: rows > 16 or a device launching more than 256 CTAs is
  * rejected with HY_ERR_CAPACITY, and calls that overlap in time on one device
- * race on the scratch. The first call on each device resolves the array's
- * address (cudaGetSymbolAddress), so make one call before any stream capture. */
+ * race on the scratch. The first call on each device does a one-time set-up
+ * (it resolves the array's device address with cudaGetSymbolAddress); make
+ * that first call before any stream capture starts. Ordering: the call runs on
+ * the context's stream (hy_ctx_stream), so hidden_dev must be complete before
+ * it is made - synchronise the stream that wrote it, or record an event there
+ * and make the context's stream wait on it. Every call blocks the calling
+ * thread until the select has finished (it synchronises the context's stream
+ * to read the device error word); tokens_dev / raw_top1_dev hold the result
+ * on return. */
 int hy_lm_head_select_noalloc(hy_ctx* ctx, const float* hidden_dev, int rows, float penalty, int* tokens_dev,
                               int* raw_top1_dev);
 
@@ -336,11 +370,15 @@ int hy_fixture_meta(const char* fixture_dir, int* seq_len, int* expected_token_c
  * [seq_len], position_ids.i32 [4 x seq_len], expected_tokens.i32
  * [expected_token_count] and vision_features.f32 [vision_token_count x 1024]
  * (skipped when vision_features is NULL), each exactly that size ("short read",
- * "unexpected extra bytes" otherwise). Sizes come from meta.txt. The fixture
- * runs through hy_run_vlm_decode_with_prompt / hy_run_vlm_dflash_with_prompt
+ * "unexpected extra bytes" otherwise). Sizes come from meta.txt, read again by
+ * this call; the buffers hold seq_capacity ids (4 x seq_capacity position ids),
+ * expected_capacity tokens and vision_capacity feature rows, and a meta.txt
+ * asking for more fails with HY_ERR_CAPACITY before anything is written (the
+ * reference reads into vectors it sizes itself). The fixture runs through
+ * hy_run_vlm_decode_with_prompt / hy_run_vlm_dflash_with_prompt
  * (TextRuntime::run_vlm_fixture_decode / run_vlm_fixture_dflash_decode). */
-int hy_fixture_load(const char* fixture_dir, int* input_ids, int* position_ids, int* expected_tokens,
-                    float* vision_features);
+int hy_fixture_load(const char* fixture_dir, int seq_capacity, int expected_capacity, int vision_capacity,
+                    int* input_ids, int* position_ids, int* expected_tokens, float* vision_features);
 
 /* ---- standalone kernels (benchmarks and parity tests) ----------------- */
 /* Attention alone (PreciseSDPA decode/verify, src/precise_sdpa.cpp:281-329,
@@ -355,15 +393,8 @@ int hy_kv_write(hy_ctx* ctx, int layer, int start, int rows, const float* k, con
 int hy_kv_read(hy_ctx* ctx, int layer, int start, int rows, float* k, float* v);
 int hy_seq_set_length(hy_ctx* ctx, int rows);
 
-/* ---- device-resident timing hooks (benchmarks) ------------------------ */
-/* Replays `count` AR step graphs back to back on the context's stream
- * without host copies and returns the device time in ms (CUDA events). */
-int hy_bench_ar_steps(hy_ctx* ctx, int count, float* ms);
-/* Times `count` launches of one kernel family on the context's stream:
- * which = 0: LM head GEMV + argmax (M=1); 1: gate/up GEMV of layer 0;
- * 2: attention of layer 0 at the current length (M=1). ms = mean per launch. */
-int hy_bench_kernel(hy_ctx* ctx, int which, int count, float* ms);
-/* Raw stream handle (cudaStream_t) for external event timing. */
+/* Raw stream handle (cudaStream_t): the context's calls run on it; a caller
+ * orders its own work before or after them with events on this stream. */
 void* hy_ctx_stream(hy_ctx* ctx);
 
 #ifdef __cplusplus

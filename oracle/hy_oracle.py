@@ -412,6 +412,55 @@ def decoder_forward(w: Weights, cfg: ModelConfig, x: np.ndarray, mask: np.ndarra
     return rms_norm(x, w.final_norm, cfg.rms_eps), aux_out
 
 
+def attention_rows(lw: LayerWeights, qkv: np.ndarray, cos: np.ndarray, sin: np.ndarray, k_past: np.ndarray,
+                   v_past: np.ndarray, scale: float, eps: float):
+    """The attention block of one decoder layer for `rows` new rows over a cache
+    (export/text_decoder_kv.py:66-79 RoPE, query/key layernorm, append; PreciseSDPA
+    with the decode / verify mask, src/precise_sdpa.cpp:281-329 and
+    src/text_runtime.cpp:221-226 / src/dflash_runtime.cpp:60-76: row r sees keys
+    <= past + r).
+
+    qkv [rows, 4096] raw projections (q 2048 | k 1024 | v 1024); k_past, v_past
+    [8, past, 128]. Returns (attention output [rows, 2048], new k rows [8, rows, 128],
+    new v rows [8, rows, 128]).
+    """
+    rows = qkv.shape[0]
+    q = qkv[:, :Q_WIDTH].reshape(rows, NUM_Q_HEADS, HEAD_DIM).transpose(1, 0, 2)
+    k = qkv[:, Q_WIDTH:Q_WIDTH + KV_WIDTH].reshape(rows, NUM_KV_HEADS, HEAD_DIM).transpose(1, 0, 2)
+    v = qkv[:, Q_WIDTH + KV_WIDTH:].reshape(rows, NUM_KV_HEADS, HEAD_DIM).transpose(1, 0, 2)
+    q = rms_norm(apply_rope(q, cos, sin), lw.q_norm, eps)
+    k = rms_norm(apply_rope(k, cos, sin), lw.k_norm, eps)
+    keys = np.concatenate([k_past, k], axis=1)
+    vals = np.concatenate([v_past, v], axis=1)
+    past = k_past.shape[1]
+    col = np.arange(past + rows)[None, :]
+    mask = np.where(col > past + np.arange(rows)[:, None], MASK_NEG_INF, np.float32(0)).astype(np.float32)
+    out = precise_sdpa(q, keys, vals, mask, scale)
+    return out.transpose(1, 0, 2).reshape(rows, Q_WIDTH), k, np.ascontiguousarray(v)
+
+
+def decode_from_cache(w: Weights, cfg: ModelConfig, cache: KVCache, first_token: int, max_tokens: int,
+                      history, penalty: float = DEFAULT_PENALTY) -> DecodeTrace:
+    """The AR loop of decode_from_embeddings (src/text_runtime.cpp:1417-1508) from a
+    cache that already holds cache.length rows: first_token is the first output
+    (not yet in `history`), each step embeds the last token at position
+    cache.length with the 1-D RoPE, runs the decoder and selects the next token."""
+    hist = list(history) + [int(first_token)]
+    tr = DecodeTrace([int(first_token)], [int(first_token)], [], [], [])
+    tok = int(first_token)
+    for _ in range(max_tokens - 1):
+        pos = cache.length
+        h, _ = decoder_forward(w, cfg, w.embed[tok:tok + 1], make_decode_mask(pos), rope_rows(pos, 1, True),
+                               rope_rows(pos, 1, False), cache)
+        logits = lm_head(w, h)[0]
+        tok, raw = select_next_token(logits, hist, penalty)
+        hist.append(tok)
+        tr.tokens.append(tok)
+        tr.raw_top1.append(raw)
+        tr.margins.append(top2_margin(logits))
+    return tr
+
+
 def lm_head(w: Weights, hidden: np.ndarray) -> np.ndarray:
     """Tied LM head (export/export_lm_head.py:16-24): logits = h E^T."""
     return (hidden.astype(np.float32) @ w.embed.T).astype(np.float32)

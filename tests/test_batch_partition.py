@@ -145,3 +145,71 @@ def test_two_gloo_ranks_merge_in_input_order():
     assert summary == (n, n - 1, 1)
     assert all(ok == (i != 5) for i, ok, _ in merged)
     assert merged[4][2] == [4, 9]
+
+
+def _leaving_worker(rank, world, port, n, q):
+    """Rank 1 finishes one record, then leaves without a word (between records);
+    rank 0 must still return every record: rank 1's first as published, the rest
+    as ok:false rank failures, within the rank timeout."""
+    import datetime
+    import time
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    b = _batch()
+    ch = b.StoreChannel.from_default_group(prefix="leave")
+    records = list(range(n))
+    if rank == 1:
+        calls = []
+
+        def infer(i):
+            if calls:
+                q.put(("left", rank))
+                q.close()
+                q.join_thread()   # the message is out before the process ends
+                os._exit(0)    # the rank is gone: no more records, no done flag, no goodbye
+            calls.append(i)
+            return _infer(i)
+
+        b.run_partition(records, infer, world=world, rank=rank, channel=ch)
+        return
+    t0 = time.monotonic()
+    local, _ = b.run_partition(records, _infer, world=world, rank=rank, channel=ch)
+    merged, summary = ch.collect(n, rank_timeout_s=3.0)
+    q.put(("merged", [(r.index, r.ok, r.stage, r.tokens) for r in merged],
+           (summary.total, summary.succeeded, summary.failed), time.monotonic() - t0))
+    q.close()
+    q.join_thread()
+    os._exit(0)   # the peer is gone: skip the process-group teardown
+
+
+def test_rank_leaving_between_records_gives_failure_records():
+    import multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    n, world, port = 9, 2, _free_port()
+    procs = [ctx.Process(target=_leaving_worker, args=(r, world, port, n, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    msgs = [q.get(timeout=90) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert ("left", 1) in msgs
+    _, merged, summary, seconds = next(m for m in msgs if m[0] == "merged")
+    assert [i for i, *_ in merged] == list(range(n))
+    # Rank 0 (even records): its own results. Rank 1 (odd records): record 1
+    # published before it left; 3, 5, 7 rank failures.
+    for i, ok, stage, toks in merged:
+        if i % 2 == 0:
+            assert ok and toks == _infer(i)
+        elif i == 1:
+            assert ok and toks == _infer(1)
+        else:
+            assert not ok and stage == "rank", (i, ok, stage)
+    assert summary == (n, 5 + 1, 3)
+    assert seconds < 30

@@ -3,6 +3,7 @@ its host-side table builders match the reference's known answers. No device
 work runs here."""
 
 import ctypes
+import glob
 import os
 import re
 
@@ -12,9 +13,12 @@ from conftest import REPO
 
 
 def _declared_symbols():
-    text = open(os.path.join(REPO, "include", "hy_decode.h")).read()
-    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(hy_[a-z0-9_]+)\s*\(", text)))
+    """Every function declared in include/*.h (the reference-facing hy_decode.h and hy_debug.h)."""
+    names = set()
+    for path in glob.glob(os.path.join(REPO, "include", "*.h")):
+        text = re.sub(r"/\*.*?\*/", "", open(path).read(), flags=re.S)
+        names.update(re.findall(r"\b(hy_[a-z0-9_]+)\s*\(", text))
+    return sorted(names)
 
 
 def test_library_exports_every_declared_symbol(pkg):

@@ -55,3 +55,24 @@ def test_fixture_errors(pkg, tmp_path, case):
     with pytest.raises(pkg.HyError) as e:
         pkg.read_vlm_fixture(d)
     assert e.value.status == pkg.HY_ERR_INVALID_ARGUMENT and want in e.value.message
+
+
+def test_fixture_load_checks_buffer_capacity(pkg, tmp_path):
+    """A meta.txt that asks for more than the caller's buffers hold fails before any write."""
+    import ctypes
+    d, ids, pos, feats, exp = _fixture(pkg, tmp_path)
+    lib = pkg.load_library()
+    seq = ids.size - 1                      # buffers sized one row short of meta.txt's seq_len
+    b_ids = np.full(seq, -7, np.int32)
+    b_pos = np.full((4, seq), -7, np.int32)
+    b_exp = np.full(exp.size, -7, np.int32)
+    b_feat = np.zeros((feats.shape[0], 1024), np.float32)
+    rc = lib.hy_fixture_load(os.fsencode(d), seq, exp.size, feats.shape[0], b_ids.ctypes.data, b_pos.ctypes.data,
+                             b_exp.ctypes.data, b_feat.ctypes.data)
+    assert rc == pkg.HY_ERR_CAPACITY
+    assert b"seq_len=7" in lib.hy_last_error()
+    assert (b_ids == -7).all() and (b_pos == -7).all() and (b_exp == -7).all()
+    rc = lib.hy_fixture_load(os.fsencode(d), ids.size, exp.size, feats.shape[0] - 1, b_ids.ctypes.data,
+                             b_pos.ctypes.data, b_exp.ctypes.data, b_feat.ctypes.data)
+    assert rc == pkg.HY_ERR_CAPACITY
+    del ctypes

@@ -62,22 +62,6 @@ def test_lm_head_select_matches_oracle(small, oracle, rows):
     assert raw.tolist() == [int(np.argmax(logits_ref[r])) for r in range(rows)]
 
 
-def _attention_reference(oracle, lw, qkv, cos, sin, kpast, vpast, scale, eps):
-    rows = qkv.shape[0]
-    q = qkv[:, :2048].reshape(rows, 16, 128).transpose(1, 0, 2)
-    k = qkv[:, 2048:3072].reshape(rows, 8, 128).transpose(1, 0, 2)
-    v = qkv[:, 3072:].reshape(rows, 8, 128).transpose(1, 0, 2)
-    q = oracle.rms_norm(oracle.apply_rope(q, cos, sin), lw.q_norm, eps)
-    k = oracle.rms_norm(oracle.apply_rope(k, cos, sin), lw.k_norm, eps)
-    K = np.concatenate([kpast, k], axis=1)
-    V = np.concatenate([vpast, v], axis=1)
-    past = kpast.shape[1]
-    col = np.arange(past + rows)[None, :]
-    mask = np.where(col > past + np.arange(rows)[:, None], np.float32(-1e38), np.float32(0)).astype(np.float32)
-    out = oracle.precise_sdpa(q, K, V, mask, scale)
-    return out.transpose(1, 0, 2).reshape(rows, 2048), k, v
-
-
 @pytest.mark.parametrize("rows", [1, 16])
 @pytest.mark.parametrize("past", [0, 3, 100, 700, 2048])
 def test_attention_matches_precise_sdpa(small, oracle, rows, past):
@@ -93,8 +77,7 @@ def test_attention_matches_precise_sdpa(small, oracle, rows, past):
     cos = oracle.rope_rows(past, rows, True)
     sin = oracle.rope_rows(past, rows, False)
     out = rt.attention(0, qkv, cos, sin)
-    ref, knew, vnew = _attention_reference(oracle, w.layers[0], qkv, cos, sin, kpast, vpast, cfg.attn_scale,
-                                           cfg.rms_eps)
+    ref, knew, vnew = oracle.attention_rows(w.layers[0], qkv, cos, sin, kpast, vpast, cfg.attn_scale, cfg.rms_eps)
     np.testing.assert_allclose(out, ref, rtol=RTOL, atol=ATOL)
     k, v = rt.kv_read(0, past, rows)
     np.testing.assert_allclose(k, knew, rtol=1e-5, atol=1e-5)
@@ -240,15 +223,62 @@ def test_capacity_and_argument_errors(pkg, small):
 
 
 def test_full_config_ar_tokens_match_oracle(pkg, oracle):
-    """Config 0 geometry (24 layers, vocab 120818, 768 image rows on 24x32 + 256 text ids), fp32,
-    ncnn SDPA scale; 64 greedy tokens with penalty 1.08 identical to the oracle."""
+    """The AR decode workload in full (24 layers, vocab 120818, 768 image rows on 24x32 + 256 text
+    ids, fp32, ncnn SDPA scale): all 256 greedy tokens with penalty 1.08 identical to the oracle."""
     cfg = oracle.ModelConfig()
     w = oracle.make_weights(cfg, 0)
     prompt = oracle.synthetic_prompt(0, 24, 32, 256, cfg.vocab)
-    n = 64
+    n = 256
     want = oracle.decode_ar(w, cfg, prompt, n)
     with pkg.TextRuntime.synthetic(seed=0, max_prefill=1024, max_tokens=256, max_context=2048, device=0) as rt:
         res = rt.run_vlm_decode_with_prompt(prompt.input_ids, prompt.position_ids, prompt.image_token_id,
                                             prompt.vision_features, max_tokens=n)
     mism = [i for i, (a, b) in enumerate(zip(res.generated_tokens, want.tokens)) if a != b]
     assert not mism, f"first mismatch at {mism[0]}, oracle top-2 margin {want.margins[mism[0]]:.3g}"
+
+
+def test_lm_head_m1_full_vocab_logits(pkg, oracle):
+    """The LM-head workload at M = 1: hidden N(0,1) against the full 120818 x 1024 tied table;
+    logits within the fp32 tolerance, raw and penalised argmax bit-exact."""
+    vocab = 120818
+    w = oracle.make_weights(oracle.ModelConfig(num_layers=0, vocab=vocab), 3)
+    rng = np.random.default_rng(120818)
+    with pkg.TextRuntime.synthetic(seed=3, num_layers=2, vocab_size=vocab, max_prefill=64, max_tokens=32,
+                                   max_context=256, device=0) as rt:
+        for trial in range(3):
+            h = rng.standard_normal((1, 1024)).astype(np.float32)
+            ref = oracle.lm_head(w, h)
+            hist = rng.integers(0, vocab, 500).tolist() + [int(np.argmax(ref[0]))]
+            rt.set_history(hist)
+            tok, raw, logits = rt.select_logit_rows(h, 1.08, want_logits=True)
+            np.testing.assert_allclose(logits, ref, rtol=RTOL, atol=ATOL)
+            assert raw.tolist() == [int(np.argmax(ref[0]))]
+            assert tok.tolist() == oracle.select_logit_rows(ref, hist, None, 1.08)
+
+
+def test_full_24l_golden_logits_within_tolerance(pkg, oracle):
+    """The 24-layer golden of the reference's own decoder wrapper, step by step through the
+    step interface (prefill, then run_decoder_step + LM head per token): every step's top-16
+    logits within 1e-3 relative of the golden, tokens and raw top-1 exact."""
+    g = load_golden("full_24l")
+    prompt = _golden_prompt(oracle, g)
+    seq = prompt.input_ids.shape[0]
+    emb_w = oracle.make_weights(oracle.ModelConfig(num_layers=0, vocab=int(g["vocab"])), int(g["seed"]))
+    emb = oracle.prepare_prompt_embeddings(emb_w, prompt)
+    penalty = float(g["penalty"])
+    with _golden_runtime(pkg, g, max_context=2048, max_prefill=1024, max_tokens=64) as rt:
+        rt.reset()
+        last = rt.prefill(emb, oracle.build_mrope(prompt.position_ids, seq, True),
+                          oracle.build_mrope(prompt.position_ids, seq, False))
+        # fp32 hidden state after 24 layers: 2e-4 absolute, the tolerance the oracle itself meets here.
+        np.testing.assert_allclose(last, g["prefill_last_hidden"], rtol=1e-3, atol=2e-4)
+        rt.set_history(prompt.input_ids)
+        hidden = last[None, :]
+        for i in range(len(g["tokens"])):
+            tok, raw, logits = rt.select_logit_rows(hidden, penalty, want_logits=True)
+            np.testing.assert_allclose(logits[0, g["top16_idx"][i]], g["top16_val"][i], rtol=1e-3, atol=1e-4)
+            assert int(tok[0]) == int(g["tokens"][i]) and int(raw[0]) == int(g["raw_top1"][i])
+            rt.add_history([int(tok[0])])
+            pos = seq + i
+            hidden, _ = rt.run_decoder_step(emb_w.embed[int(tok[0]):int(tok[0]) + 1], oracle.rope_rows(pos, 1, True),
+                                            oracle.rope_rows(pos, 1, False))
