@@ -50,7 +50,8 @@ EXPORTED_SYMBOLS = (
     "hy_draft_context_append", "hy_draft_run", "hy_draft_propose", "hy_dflash_generate",
     "hy_run_vlm_dflash_with_prompt", "hy_batch_decode", "hy_fixture_meta", "hy_fixture_load",
     "hy_ctx_set_token_callback", "hy_debug_wait_stats", "hy_ctx_last_timing", "hy_ctx_last_dflash_timing",
-    "hy_ctx_set_wait_limit", "hy_debug_wait_probe",
+    "hy_ctx_set_wait_limit", "hy_debug_wait_probe", "hy_ctx_create_from_package", "hy_draft_load_package",
+    "hy_package_inspect", "hy_package_read_tensor",
 )
 TOKEN_CALLBACK = ctypes.CFUNCTYPE(None, ctypes.c_int, ctypes.c_void_p)
 DFLASH_MASK_TOKEN = 120817
@@ -176,6 +177,12 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
                                            ctypes.POINTER(_I)], _I),
         "hy_debug_progress": ([_P, _P, _I], _I),
         "hy_debug_wait_stats": ([_P, _P, _I, _I], _I),
+        "hy_ctx_create_from_package": ([ctypes.POINTER(Config), ctypes.c_char_p, ctypes.POINTER(_P)], _I),
+        "hy_draft_load_package": ([_P, ctypes.c_char_p, _I], _I),
+        "hy_package_inspect": ([ctypes.c_char_p, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I),
+                                ctypes.POINTER(_I)], _I),
+        "hy_package_read_tensor": ([ctypes.c_char_p, _I, _I, ctypes.c_char_p, _P, ctypes.c_size_t,
+                                    ctypes.POINTER(ctypes.c_size_t)], _I),
         "hy_ctx_set_wait_limit": ([_P, ctypes.c_uint64], _I),
         "hy_debug_wait_probe": ([_P, _I, ctypes.c_uint64], _I),
         "hy_ctx_last_timing": ([_P, ctypes.POINTER(_DecodeTiming)], _I),
@@ -213,6 +220,26 @@ def default_config(**overrides) -> Config:
     for k, v in overrides.items():
         setattr(cfg, k, v)
     return cfg
+
+
+def package_inspect(model_root: str) -> dict:
+    """Geometry of a model package (the reference's exported ncnn files), read on the host."""
+    lib = load_library()
+    n, v, f, d = ctypes.c_int(), ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    _check(lib.hy_package_inspect(os.fsencode(model_root), ctypes.byref(n), ctypes.byref(v), ctypes.byref(f),
+                                  ctypes.byref(d)))
+    return {"num_layers": n.value, "vocab_size": v.value, "ffn_dim": f.value, "draft_layers": d.value}
+
+
+def package_tensor(model_root: str, field: str, layer: int = -1, draft: bool = False) -> np.ndarray:
+    """One weight of a package as the library's reader sees it (fp16 storage converted)."""
+    lib = load_library()
+    n = ctypes.c_size_t()
+    root, f = os.fsencode(model_root), field.encode()
+    _check(lib.hy_package_read_tensor(root, int(draft), layer, f, None, 0, ctypes.byref(n)))
+    out = np.empty(n.value, np.float32)
+    _check(lib.hy_package_read_tensor(root, int(draft), layer, f, _ptr(out), out.size, ctypes.byref(n)))
+    return out
 
 
 def build_mrope(position_ids: np.ndarray, seq_len: int, use_cos: bool) -> np.ndarray:
@@ -381,6 +408,18 @@ class TextRuntime:
         ctx = ctypes.c_void_p()
         _check(lib.hy_ctx_create(ctypes.byref(cfg), ctypes.byref(w), ctypes.byref(ctx)))
         return cls(ctx, cfg)
+
+    @classmethod
+    def from_package(cls, model_root: str, **cfg_overrides) -> "TextRuntime":
+        """TextRuntime::load from a model package directory (hy_ctx_create_from_package):
+        num_layers, vocab_size and ffn_dim come from the package."""
+        lib = load_library()
+        cfg = default_config(**cfg_overrides)
+        ctx = ctypes.c_void_p()
+        _check(lib.hy_ctx_create_from_package(ctypes.byref(cfg), os.fsencode(model_root), ctypes.byref(ctx)))
+        out = Config()
+        _check(lib.hy_ctx_config(ctx, ctypes.byref(out)))
+        return cls(ctx, out)
 
     def close(self) -> None:
         if self._ctx:
@@ -602,6 +641,10 @@ class TextRuntime:
         w = _DraftWeights(n, mask_token, p(draft_weights.fc), p(draft_weights.hidden_norm), p(draft_weights.norm),
                           layers)
         _check(_LIB.hy_draft_load(self._ctx, ctypes.byref(w)))
+
+    def load_draft_package(self, model_root: str, mask_token: int = DFLASH_MASK_TOKEN) -> None:
+        """DFlashDraftRuntime::load from <model_root>/dflash (hy_draft_load_package)."""
+        _check(_LIB.hy_draft_load_package(self._ctx, os.fsencode(model_root), mask_token))
 
     def load_draft_synthetic(self, num_layers: int, seed: int, std: float = 0.02, norm_std: float = 0.0,
                              mask_token: int = DFLASH_MASK_TOKEN) -> None:

@@ -15,7 +15,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libhy_decode.so")
-SOURCES = [os.path.join(HERE, "csrc", "hy_capi.cu")]
+SOURCES = [os.path.join(HERE, "csrc", "hy_capi.cu"), os.path.join(HERE, "csrc", "hy_package.cpp")]
 DEPS = [os.path.join(HERE, "csrc", f) for f in os.listdir(os.path.join(HERE, "csrc"))] + [
     os.path.join(REPO, "include", "hy_decode.h")]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")

@@ -2418,6 +2418,16 @@ const char* hy_version(void) { return "hy_decode 0.1 (sm_100a)"; }
 
 const char* hy_last_error(void) { return g_error.c_str(); }
 
+}  // extern "C"
+
+// The message of a failure in the library's host code outside this file (the
+// model-package reader), for hy_last_error.
+namespace hy_internal {
+void set_last_error(const std::string& msg) { g_error = msg; }
+}  // namespace hy_internal
+
+extern "C" {
+
 int hy_config_init(hy_config* cfg)
 {
     if (!cfg) return fail(HY_ERR_INVALID_ARGUMENT, "config is null");

@@ -111,6 +111,30 @@ int hy_ctx_create_synthetic(const hy_config* cfg, uint64_t seed, float std, floa
 
 void hy_ctx_destroy(hy_ctx* ctx);
 
+/* ---- model package (the reference's exported ncnn files) -------------- */
+/* TextRuntime::load (src/text_runtime.cpp:1685-1749) from a model package
+ * root (models/README.md): text_embed/text_embed.ncnn.{param,bin} - the tied
+ * table, which the LM head's param also points at (1705-1745) - and
+ * text_decoder/text_decoder_kv.ncnn.{param,bin}. The .bin files are
+ * memory-mapped (src/mapped_model_file.cpp:156) and read in .param order by
+ * ncnn's model-bin layout (fp32 or fp16 arrays); weights are found by the pnnx
+ * layer names of the exported modules (layers.<i>.self_attn.q_proj, ...,
+ * layers.<i>.mlp.down_proj, norm). num_layers, vocab_size and ffn_dim come
+ * from the package; the other fields from cfg. One device copy of the weights,
+ * the tied table shared by embedding and LM head. */
+int hy_ctx_create_from_package(const hy_config* cfg, const char* model_root, hy_ctx** out);
+/* DFlashDraftRuntime::load (src/dflash_runtime.cpp:175-201) from
+ * <model_root>/dflash/dflash.ncnn.{param,bin} (fc, hidden_norm, layers.<i>.*,
+ * norm), as hy_draft_load. */
+int hy_draft_load_package(hy_ctx* ctx, const char* model_root, int mask_token);
+/* Host-only checks of a package (no device work): its geometry, and one weight
+ * as the reader sees it (field: embed, final_norm, or a hy_layer_weights field
+ * name for `layer`; with draft != 0: fc, hidden_norm, norm or a draft layer's
+ * field). draft_layers (nullable) is 0 without a dflash directory. */
+int hy_package_inspect(const char* model_root, int* num_layers, int* vocab_size, int* ffn_dim, int* draft_layers);
+int hy_package_read_tensor(const char* model_root, int draft, int layer, const char* field, float* out,
+                           size_t capacity, size_t* count);
+
 /* How hy_generate runs the AR loop. HY_AR_PATH_PERSISTENT (default): one
  * cooperative kernel per up to 64 tokens, one CTA per SM, all 24 layers and the
  * LM head of each token inside it; the CTAs exchange each phase's outputs as
