@@ -50,8 +50,9 @@ DECODER_WEIGHT_BYTES = LAYERS * (4096 * 1024 + 1024 * 2048 + 2 * FFN * 1024 + 10
 LM_HEAD_BYTES = V * HIDDEN * 4
 KV_ROW_BYTES = LAYERS * 8 * 128 * 4 * 2
 MEGA_CHUNK = 64                      # tokens per persistent-kernel launch (hy_capi.cu kMegaChunk)
-# DRAM bytes (read + write) of one full 64-token launch (tokens 129-192), from the 1-pass ncu
-# capture summarised in profiles/mega_decode_kernel_config0.md.
+# DRAM bytes (read + write) of one 64-token launch at KV ~1184, from one ncu capture of
+# dram__bytes_read.sum + dram__bytes_write.sum (a profiler number: it cannot be taken
+# live inside the timed region).
 MEGA_TRAFFIC_PER_LAUNCH = 152.88e9
 # Draft depth of the DFlash draft network leg. The reference loads the draft from its
 # DFlash package (export/dflash_export.py takes any depth); 5 layers is an assumption.

@@ -43,6 +43,24 @@ def build(force: bool = False, verbose: bool = False, defines=(), out: str = LIB
     return out
 
 
+SHIM_TEST_SRC = os.path.join(REPO, "tests", "cpp", "test_shim.cpp")
+SHIM_TEST_BIN = os.path.join(REPO, "tests", "cpp", "test_shim")
+
+
+def build_shim_test(force: bool = False) -> str:
+    """Compile the C++17 layer's test program (tests/cpp/test_shim.cpp, over
+    include/hunyuan_ocr_cuda.h) against the in-tree library."""
+    deps = [SHIM_TEST_SRC, LIB, os.path.join(REPO, "include", "hunyuan_ocr_cuda.h"),
+            os.path.join(REPO, "include", "hy_decode.h")]
+    if not force and os.path.exists(SHIM_TEST_BIN) and all(
+            os.path.getmtime(d) <= os.path.getmtime(SHIM_TEST_BIN) for d in deps):
+        return SHIM_TEST_BIN
+    cxx = os.environ.get("CXX", "g++")
+    subprocess.run([cxx, "-std=c++17", "-O1", "-Wall", "-Wextra", "-I" + os.path.join(REPO, "include"), SHIM_TEST_SRC,
+                    "-L" + HERE, "-lhy_decode", "-Wl,-rpath," + HERE, "-o", SHIM_TEST_BIN], check=True)
+    return SHIM_TEST_BIN
+
+
 if __name__ == "__main__":
     import argparse
 

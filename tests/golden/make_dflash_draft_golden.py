@@ -95,7 +95,8 @@ def inputs(O):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="root of the HunyuanOCR-ncnn source tree (its export/ directory is imported)")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference) / "export"))
     from dflash_export import DFlashExportWrapper

@@ -198,7 +198,8 @@ def make_case(name: str, reference: Path, out_dir: Path) -> None:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    ap.add_argument("--reference", type=Path, required=True,
+                    help="root of the HunyuanOCR-ncnn source tree (its export/ directory is imported)")
     ap.add_argument("--cases", nargs="*", default=list(CASES))
     args = ap.parse_args()
     torch.set_num_threads(max(1, torch.get_num_threads()))
