@@ -63,6 +63,30 @@ constexpr int kMegaStage = 16384;        // bytes per slot
 // Ring slots, shared by the consumer warps: global stage g lands in slot
 // g % kMegaSlots (its use g / kMegaSlots) and is consumed by warp g % kMegaWarps.
 constexpr int kMegaSlots = 12;
+// Stages the producer keeps in flight (issued, not landed). More than the
+// bandwidth-delay product only queues in the memory fabric, where the epoch-word
+// polls of the exchanges wait behind it: with all 12 slots in flight a batch of
+// polls took 1-2.5 us although the words were already published. Measured at the
+// AR decode workload (tokens/s, device loop): 12 in flight 1674, 8 1694, 6 1712,
+// 4 1806, 3 1879, 2 1917, 1 1402; with 2 for the layers, the LM head at 4 / 6 / 8:
+// 1953 / 1955 / 1947.
+#ifndef HY_MEGA_INFLIGHT
+#define HY_MEGA_INFLIGHT 2
+#endif
+constexpr int kMegaInflight = HY_MEGA_INFLIGHT;
+// The LM head streams the tied table with no exchange to wait for: it keeps more in flight.
+#ifndef HY_MEGA_INFLIGHT_LM
+#define HY_MEGA_INFLIGHT_LM 6
+#endif
+constexpr int kMegaInflightLm = HY_MEGA_INFLIGHT_LM;
+// Attention streams cached K/V rows, which no exchange of the token waits for.
+#ifndef HY_MEGA_INFLIGHT_ATTN
+#define HY_MEGA_INFLIGHT_ATTN 2
+#endif
+constexpr int kMegaInflightAttn = HY_MEGA_INFLIGHT_ATTN;
+static_assert(kMegaInflightAttn >= 1 && kMegaInflightAttn <= kMegaSlots, "in-flight stages must fit the ring");
+static_assert(kMegaInflight >= 1 && kMegaInflight <= kMegaSlots, "in-flight stages must fit the ring");
+static_assert(kMegaInflightLm >= 1 && kMegaInflightLm <= kMegaSlots, "in-flight stages must fit the ring");
 #ifndef HY_MEGA_SPLITS
 #define HY_MEGA_SPLITS 18
 #endif
@@ -389,7 +413,8 @@ __device__ __forceinline__ void st_release_u64(unsigned long long* p, unsigned l
 template <int PER>
 __device__ __forceinline__ bool poll_words(const unsigned long long* src, int n, int first, int stride, unsigned e,
                                            float (&out)[PER], int* err, unsigned long long limit_ns,
-                                           unsigned long long* ws = nullptr, int b = 0, int kind = 0)
+                                           unsigned long long* ws = nullptr, int b = 0, int kind = 0,
+                                           int* rounds = nullptr)
 {
     const unsigned long long done = static_cast<unsigned long long>(e) << 32;   // value 0, epoch e
     unsigned long long w[PER];
@@ -416,6 +441,7 @@ __device__ __forceinline__ bool poll_words(const unsigned long long* src, int n,
             break;
         }
         __nanosleep(HY_POLL_NS);
+        if (rounds) ++*rounds;
 #pragma unroll
         for (int u = 0; u < PER; ++u)
             if (static_cast<unsigned>(w[u] >> 32) != e) w[u] = ld_relaxed_u64(src + first + stride * u);
@@ -792,6 +818,20 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                         ok = false;
                         break;
                     }
+                    // At most kMegaInflight stages in flight: stage g - kMegaInflight has
+                    // landed (its slot's full phase; that slot is re-armed only by a later
+                    // stage than g, so the parity wait is exact).
+                    const int cap = (kind == PH_LM) ? kMegaInflightLm : (kind == PH_ATTN) ? kMegaInflightAttn : kMegaInflight;
+                    if (cap < kMegaSlots && g >= static_cast<unsigned>(cap))
+                    {
+                        const unsigned gp = g - cap;
+                        if (!mega_mbar_wait(&full[gp % kMegaSlots], (gp / kMegaSlots) & 1, a.err, kErrTimeoutFull,
+                                            a.wait_limit_ns, a.wstat, b, WS_PROD_EMPTY))
+                        {
+                            ok = false;
+                            break;
+                        }
+                    }
                     const int n = min(p.per_stage, p.count - i * p.per_stage);
                     const uint32_t bytes = static_cast<uint32_t>(n * p.unit_bytes);
                     unsigned char* dst = ring + static_cast<size_t>(s) * kMegaStage;
@@ -915,9 +955,27 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                     // The residual rows this CTA owns start as the embedding.
                     if (tid < po.count && tid < kMegaResRows) xres_s[tid] = to_f32<WT>(erow[po.r0 + tid]);
                 }
-                else if (!poll_words<kXPer>(a.x_ep, kHidden, tid, kMegaConsumers, e_in, v, a.err, a.wait_limit_ns, a.wstat, b, WS_POLL_X))
+                else
                 {
-                    redi[0] = 1;
+                    int rounds = 0;
+                    const unsigned long long tp0 = tracing ? global_ns() : 0;
+                    if (!poll_words<kXPer>(a.x_ep, kHidden, tid, kMegaConsumers, e_in, v, a.err, a.wait_limit_ns,
+                                           a.wstat, b, WS_POLL_X, tracing ? &rounds : nullptr))
+                        redi[0] = 1;
+                    if (tracing)
+                    {
+                        // Poll rounds, ns polling, and one more load of a word already
+                        // published (its round trip in SM cycles).
+                        const unsigned long long tp1 = global_ns();
+                        const long long c0 = clock64();
+                        const unsigned long long probe = ld_relaxed_u64(a.x_ep + (kHidden - 1 - tid));
+                        asm volatile("" ::"l"(probe) : "memory");   // the load has returned
+                        const long long c1 = clock64();
+                        tr[7] = rounds;
+                        tr[8] = tp1 - tp0;
+                        tr[9] = static_cast<unsigned long long>(c1 - c0);
+                        tr[10] = tp0;
+                    }
                 }
                 if (kind == PH_LM && p.count > 0)
                 {
@@ -935,8 +993,17 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                 // act = silu(gate) * up from the gate/up phase.
                 constexpr int kPer = (kMegaMaxK + kMegaConsumers - 1) / kMegaConsumers;
                 float v[kPer];
-                if (!poll_words<kPer>(a.act_ep, a.ffn, tid, kMegaConsumers, e_in, v, a.err, a.wait_limit_ns, a.wstat, b, WS_POLL_ACT))
+                int rounds = 0;
+                const unsigned long long tp0 = tracing ? global_ns() : 0;
+                if (!poll_words<kPer>(a.act_ep, a.ffn, tid, kMegaConsumers, e_in, v, a.err, a.wait_limit_ns, a.wstat, b,
+                                      WS_POLL_ACT, tracing ? &rounds : nullptr))
                     redi[0] = 1;
+                if (tracing)
+                {
+                    tr[7] = rounds;
+                    tr[8] = global_ns() - tp0;
+                    tr[10] = tp0;
+                }
 #pragma unroll
                 for (int u = 0; u < kPer; ++u)
                 {
@@ -950,9 +1017,17 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                 // The attention output of all 16 heads (merged by each head pair's new-row split).
                 constexpr int kPer = (kQWidth + kMegaConsumers - 1) / kMegaConsumers;
                 float v[kPer];
+                int rounds = 0;
+                const unsigned long long tp0 = tracing ? global_ns() : 0;
                 if (!poll_words<kPer>(a.attn_out_ep, kQWidth, tid, kMegaConsumers, e_in, v, a.err, a.wait_limit_ns, a.wstat, b,
-                                      WS_POLL_ATTN_OUT))
+                                      WS_POLL_ATTN_OUT, tracing ? &rounds : nullptr))
                     redi[0] = 1;
+                if (tracing)
+                {
+                    tr[7] = rounds;
+                    tr[8] = global_ns() - tp0;
+                    tr[10] = tp0;
+                }
 #pragma unroll
                 for (int u = 0; u < kPer; ++u)
                 {
