@@ -640,8 +640,8 @@ __device__ __forceinline__ float mega_load_normed(float* xs, const float4 v[2], 
 // the RMSNorm's per-row scale to its dot products).
 constexpr int kXPer = (kHidden + kMegaConsumers - 1) / kMegaConsumers;
 
-__device__ __forceinline__ float mega_load_normed_s(float* xs, const float (&v)[kXPer], const float* w, float eps,
-                                                    float* s_norm, int tid)
+__device__ __forceinline__ float mega_load_normed_s(float* xs, const float (&v)[kXPer], const float (&w)[kXPer],
+                                                    float eps, float* s_norm, int tid)
 {
     float ss = 0.f;
 #pragma unroll
@@ -651,7 +651,7 @@ __device__ __forceinline__ float mega_load_normed_s(float* xs, const float (&v)[
         if (i < kHidden)
         {
             ss += v[u] * v[u];
-            xs[i] = w[i] * v[u];
+            xs[i] = w[u] * v[u];
         }
     }
     ss = warp_sum(ss);
@@ -663,20 +663,37 @@ __device__ __forceinline__ float mega_load_normed_s(float* xs, const float (&v)[
     return 1.0f / sqrtf(t / static_cast<float>(kHidden) + eps);
 }
 
-// RoPE + RMSNorm of one 128-vector given as x[lane + 32 j] in x[j] (as rope_norm_vec).
-__device__ __forceinline__ void rope_norm_vals(const float (&x)[4], const float* c, const float* s, const float* w,
-                                               float eps, int lane, float out[4])
+// The RoPE table entries and norm weights one lane needs for rope_norm_vals, loaded
+// before the lane waits for the vector itself (they are constants of the phase).
+struct RopeNormIn {
+    float c[4], s[4], w[4];
+};
+__device__ __forceinline__ RopeNormIn rope_norm_in(const float* c, const float* s, const float* w, int lane)
 {
-    float y0 = x[0] * c[lane] - x[2] * s[lane];
-    float y1 = x[1] * c[lane + 32] - x[3] * s[lane + 32];
-    float y2 = x[2] * c[lane + 64] + x[0] * s[lane + 64];
-    float y3 = x[3] * c[lane + 96] + x[1] * s[lane + 96];
+    RopeNormIn r;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+    {
+        r.c[j] = c[lane + 32 * j];
+        r.s[j] = s[lane + 32 * j];
+        r.w[j] = w[lane + 32 * j];
+    }
+    return r;
+}
+
+// RoPE + RMSNorm of one 128-vector given as x[lane + 32 j] in x[j] (as rope_norm_vec).
+__device__ __forceinline__ void rope_norm_vals(const float (&x)[4], const RopeNormIn& in, float eps, float out[4])
+{
+    float y0 = x[0] * in.c[0] - x[2] * in.s[0];
+    float y1 = x[1] * in.c[1] - x[3] * in.s[1];
+    float y2 = x[2] * in.c[2] + x[0] * in.s[2];
+    float y3 = x[3] * in.c[3] + x[1] * in.s[3];
     const float ss = warp_sum(y0 * y0 + y1 * y1 + y2 * y2 + y3 * y3);
     const float ri = 1.0f / sqrtf(ss / static_cast<float>(kHeadDim) + eps);
-    out[0] = w[lane] * (y0 * ri);
-    out[1] = w[lane + 32] * (y1 * ri);
-    out[2] = w[lane + 64] * (y2 * ri);
-    out[3] = w[lane + 96] * (y3 * ri);
+    out[0] = in.w[0] * (y0 * ri);
+    out[1] = in.w[1] * (y1 * ri);
+    out[2] = in.w[2] * (y2 * ri);
+    out[3] = in.w[3] * (y3 * ri);
 }
 
 // One GEMV stage of a consumer warp: dot products of the stage's rows, slot
@@ -908,6 +925,18 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
             float rinv = 1.0f;   // RMSNorm scale applied to the dot products
             if (kind == PH_QKV || kind == PH_GU || kind == PH_LM)
             {
+                // The RMSNorm weights are constants: their loads are in flight while the
+                // activation words are polled.
+                const float* nw = (kind == PH_QKV) ? lnorm
+                                  : (kind == PH_GU) ? lnorm + kHidden
+                                                    : a.norms + static_cast<size_t>(L) * 2304;
+                float nwv[kXPer];
+#pragma unroll
+                for (int u = 0; u < kXPer; ++u)
+                {
+                    const int i = tid + kMegaConsumers * u;
+                    nwv[u] = (i < kHidden) ? __ldg(nw + i) : 0.f;
+                }
                 float v[kXPer];
                 if (kind == PH_QKV && layer == 0)
                 {
@@ -983,10 +1012,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                     const int w0 = p.r0 >> 5, w1 = (p.r0 + p.count - 1) >> 5;
                     if (tid <= w1 - w0 && tid < kMegaHistWords) hist_s[tid] = __ldcg(a.hist + w0 + tid);
                 }
-                const float* nw = (kind == PH_QKV) ? lnorm
-                                  : (kind == PH_GU) ? lnorm + kHidden
-                                                    : a.norms + static_cast<size_t>(L) * 2304;
-                rinv = mega_load_normed_s(xs, v, nw, a.eps, s_norm, tid);   // (one consumer barrier)
+                rinv = mega_load_normed_s(xs, v, nwv, a.eps, s_norm, tid);   // (one consumer barrier)
             }
             else if (kind == PH_DOWN)
             {
@@ -1194,24 +1220,27 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                 const float* kn_w = lnorm + 2176;
                 const float* c = a.rope_cos + static_cast<size_t>(past) * kHeadDim;
                 const float* s = a.rope_sin + static_cast<size_t>(past) * kHeadDim;
-                // q/k/v of this KV head from the q/k/v phase (epoch words).
+                // q/k/v of this KV head from the q/k/v phase (epoch words); the RoPE
+                // entries and norm weights are loaded first, while the words are polled.
                 if (warp < 2)
                 {
+                    const RopeNormIn rin = rope_norm_in(c, s, qn_w, lane);
                     float x[4], o[4];
                     if (!poll_words<4>(a.qkv_ep + (2 * g + warp) * kHeadDim, kHeadDim, lane, 32, e_in, x, a.err,
                                        a.wait_limit_ns, a.wstat, b, WS_POLL_QKV))
                         redi[0] = 1;
-                    rope_norm_vals(x, c, s, qn_w, a.eps, lane, o);
+                    rope_norm_vals(x, rin, a.eps, o);
 #pragma unroll
                     for (int i = 0; i < 4; ++i) qs[warp * kHeadDim + lane + 32 * i] = o[i] * a.scale_log2;
                 }
                 else if (new_split && warp == 2)
                 {
+                    const RopeNormIn rin = rope_norm_in(c, s, kn_w, lane);
                     float x[4], o[4];
                     if (!poll_words<4>(a.qkv_ep + kQWidth + g * kHeadDim, kHeadDim, lane, 32, e_in, x, a.err, a.wait_limit_ns, a.wstat, b,
                                        WS_POLL_QKV))
                         redi[0] = 1;
-                    rope_norm_vals(x, c, s, kn_w, a.eps, lane, o);
+                    rope_norm_vals(x, rin, a.eps, o);
                     mega_check(past >= 0 && past < a.cap, a.dbg, 5, b, ph, past);
                     KT* krow = static_cast<KT*>(a.kc) +
                                ((static_cast<size_t>(layer) * kNumKVHeads + g) * a.cap + min(past, a.cap - 1)) * kHeadDim;
