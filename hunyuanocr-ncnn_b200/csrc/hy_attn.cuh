@@ -146,7 +146,11 @@ __global__ void __launch_bounds__(kAttnThreads, (MT == 1) ? 2 : 1) attn_kernel(c
     // Rows [0, past) were written by earlier steps, so they (and past itself)
     // may be read before griddepcontrol.wait (the slot states too: the commit
     // that wrote them ran at least two kernels earlier).
-    if (a.slots && !a.slots[bz].active) return;
+    if (a.slots && !a.slots[bz].active)
+    {
+        pdl_wait();   // (every CTA waits, so the grid never ends before its predecessor)
+        return;
+    }
     const int past = a.slots ? a.slots[bz].kv_len : a.st ? a.st->kv_len : a.past_fixed;
     const int rows = a.rows;
     const size_t slot_off = a.slots ? static_cast<size_t>(bz) * a.slot_stride : 0;

@@ -186,6 +186,13 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes
 // (a no-op when the launch carried no programmatic dependency) / let the next
 // grid start its prologue.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next kernel in the stream (launched with programmatic stream
+// serialization) start its CTAs once every CTA of this grid has called it or
+// exited; that kernel's producers then stream constant weights while this one
+// finishes, and its griddepcontrol.wait still waits for this grid's completion.
+// Every kernel calls it only after its own pdl_wait, so whatever the grid
+// before this one wrote is complete and visible when the next kernel starts:
+// code before that kernel's wait may read data written two kernels back.
 __device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------

@@ -54,6 +54,7 @@ template <typename KT>
 __global__ void __launch_bounds__(256) prefill_rope_kernel(const PrefillRopeArgs a)
 {
     pdl_wait();
+    pdl_launch();
     const int m = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int past = a.st ? a.st->kv_len : a.past;
     if (past + m >= a.cap)
@@ -173,6 +174,7 @@ __global__ void __launch_bounds__(4 * QR, 2) prefill_attn_kernel(const PrefillAt
     const int g = lane >> 2, t = lane & 3;
     const int kvh = blockIdx.y;
     pdl_wait();
+    pdl_launch();
     const bool dev = (a.work == nullptr);
     const int past = (dev && a.st) ? a.st->kv_len : a.past;
     int qb = 0, kb0, kb1, slot;
@@ -461,6 +463,7 @@ struct ChunkMergeArgs {
 __global__ void __launch_bounds__(kHeadDim) attn_chunk_merge_kernel(const ChunkMergeArgs a)
 {
     pdl_wait();
+    pdl_launch();
     const int qv = blockIdx.x, kvh = blockIdx.y, d = threadIdx.x;   // qv = hl * 16 + row
     const int row = qv % 16, hl = qv / 16;
     if (row >= a.rows) return;
