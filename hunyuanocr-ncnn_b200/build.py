@@ -8,13 +8,17 @@ produces hunyuanocr-ncnn_b200/libhy_decode.so from csrc/ with nvcc
 
 from __future__ import annotations
 
+import hashlib
+import json
 import os
 import subprocess
 import sys
+import time
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libhy_decode.so")
+RECORD = os.path.join(HERE, "libhy_decode.build.json")   # what the last in-tree build compiled, and how
 SOURCES = [os.path.join(HERE, "csrc", "hy_capi.cu"), os.path.join(HERE, "csrc", "hy_package.cpp")]
 DEPS = [os.path.join(HERE, "csrc", f) for f in os.listdir(os.path.join(HERE, "csrc"))] + [
     os.path.join(REPO, "include", "hy_decode.h")]
@@ -39,8 +43,27 @@ def build(force: bool = False, verbose: bool = False, defines=(), out: str = LIB
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd))
+    t0 = time.time()
     subprocess.run(cmd, check=True)
+    if out == LIB:
+        write_record(cmd, time.time() - t0)
     return out
+
+
+def write_record(cmd, seconds: float) -> None:
+    """Record of a fresh in-tree build: the nvcc command and version, the digest of
+    every source it read, and of the library it wrote."""
+    def digest(p):
+        with open(p, "rb") as f:
+            return hashlib.sha256(f.read()).hexdigest()
+
+    ver = subprocess.run([NVCC, "--version"], capture_output=True, text=True).stdout.strip().splitlines()
+    rec = {"built_at": time.strftime("%Y-%m-%dT%H:%M:%SZ", time.gmtime()), "seconds": round(seconds, 1),
+           "nvcc": ver[-1] if ver else "", "command": cmd,
+           "sources": {os.path.relpath(p, REPO): digest(p) for p in sorted(set(SOURCES + DEPS))},
+           "library": {"path": os.path.relpath(LIB, REPO), "sha256": digest(LIB), "bytes": os.path.getsize(LIB)}}
+    with open(RECORD, "w") as f:
+        json.dump(rec, f, indent=1)
 
 
 SHIM_TEST_SRC = os.path.join(REPO, "tests", "cpp", "test_shim.cpp")
