@@ -50,10 +50,13 @@ DECODER_WEIGHT_BYTES = LAYERS * (4096 * 1024 + 1024 * 2048 + 2 * FFN * 1024 + 10
 LM_HEAD_BYTES = V * HIDDEN * 4
 KV_ROW_BYTES = LAYERS * 8 * 128 * 4 * 2
 MEGA_CHUNK = 64                      # tokens per persistent-kernel launch (hy_capi.cu kMegaChunk)
-# DRAM bytes (read + write) of one 64-token launch at KV ~1184, from one ncu capture of
-# dram__bytes_read.sum + dram__bytes_write.sum (a profiler number: it cannot be taken
-# live inside the timed region).
-MEGA_TRAFFIC_PER_LAUNCH = 152.88e9
+# DRAM bytes (read + write) per algorithmic byte of the persistent kernel, from one ncu
+# capture of dram__bytes_read.sum + dram__bytes_write.sum on a small case of the same
+# kernel (4 layers, vocab 16384, 8 tokens at KV 1024: 3.0287 GB for 3.0211 GB algorithmic;
+# a profiler number, it cannot be taken live). The traffic of a full launch is this ratio
+# times its algorithmic bytes: every weight and KV byte is read once per token, so the
+# traffic grows with the tokens and layers a launch processes.
+MEGA_TRAFFIC_RATIO = 1.0025
 # Draft depth of the DFlash draft network leg. The reference loads the draft from its
 # DFlash package (export/dflash_export.py takes any depth); 5 layers is an assumption.
 DRAFT_LAYERS = 5
@@ -463,7 +466,7 @@ def run_b200(args, world, rank, local):
         "device_loop_tokens_per_s": round((GEN_TOKENS - 1) / (dev_ms / 1e3), 2),
         "roofline": {"bound": "hbm", "kernel": "mega_decode_kernel<f32,f32> (persistent: whole tokens per launch)",
                      "achieved": round(mega_gbs, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(mega_gbs / peak, 4), "traffic": MEGA_TRAFFIC_PER_LAUNCH,
+                     "frac": round(mega_gbs / peak, 4), "traffic": round(MEGA_TRAFFIC_RATIO * bpt * MEGA_CHUNK),
                      "peak_source": peak_kind, "bytes_per_token": round(bpt),
                      "tokens_per_launch": MEGA_CHUNK, "launch_us": round(dev_ms * 1e3 / launches, 1),
                      "roofline_tokens_per_s": round(peak * 1e9 / bpt, 1)},
