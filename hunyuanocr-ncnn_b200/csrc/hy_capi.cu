@@ -158,7 +158,6 @@ struct hy_ctx {
 
     // Persistent AR decode kernel (cooperative, one CTA per SM).
     const void** wptrs = nullptr;  // device arrays: wqkv[L], wo[L], wgu[L], wd[L]
-    unsigned* bar = nullptr;       // grid barrier counter
     // Persistent kernel: activations exchanged between CTAs as 64-bit words
     // (value | epoch << 32), and the launch counter that makes epochs unique.
     unsigned long long* x_ep = nullptr;    // [1024]
@@ -735,7 +734,6 @@ cudaError_t launch_mega_t(hy_ctx* c, int steps)
     a.st = c->st;
     a.log_tokens = c->log_tokens;
     a.log_raw = c->log_raw;
-    a.bar = c->bar;
     a.num_layers = L;
     a.vocab = c->cfg.vocab_size;
     a.ffn = c->cfg.ffn_dim;
@@ -779,8 +777,6 @@ cudaError_t launch_mega_t(hy_ctx* c, int steps)
     a.attn_ep = c->attn_ep;
     a.attn_out_ep = c->attn_out_ep;
     a.epoch_base = c->mega_seq * kMegaEpochSpan;
-    cudaError_t e = cudaMemsetAsync(c->bar, 0, sizeof(unsigned), c->stream);
-    if (e != cudaSuccess) return e;
     void* params[] = {&a};
     return cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(k), dim3(c->num_sms), dim3(kMegaThreads), params,
                                        MegaSmem::SIZE, c->stream);
@@ -1047,7 +1043,6 @@ int alloc_ctx(hy_ctx* c)
     if ((rc = dalloc(c, &c->raw_out, kBlock))) return rc;
     if ((rc = dalloc(c, &c->prefix, kBlock))) return rc;
     if ((rc = dalloc(c, &c->err, 1))) return rc;
-    if ((rc = dalloc(c, &c->bar, 1))) return rc;
     if ((rc = dalloc(c, &c->dbg, 4))) return rc;
     if ((rc = dalloc(c, &c->x_ep, kHidden))) return rc;
     if ((rc = dalloc(c, &c->qkv_ep, kQKVRows))) return rc;

@@ -122,14 +122,12 @@ struct MegaArgs {
     DecodeState* st;
     int* log_tokens;
     int* log_raw;
-    unsigned* bar;            // grid barrier counter, zero at launch
     int num_layers, vocab, ffn;
     float eps, scale_log2;
     int steps;                // tokens in this launch
     int* err;
     // Optional phase trace: for CTAs b < kTraceCtas and token trace_token,
-    // %globaltimer at phase start, after the grid wait, after the prologue and
-    // at the barrier arrive (thread 0): trace[(b * phases + ph) * kTraceSlots + i].
+    // trace[(b * phases + ph) * kTraceSlots + i] (thread 0; see hy_trace_persistent).
     unsigned long long* trace;
     int trace_token;
     // Self-checks: the first failed bounds check stores (code, cta, phase, index)
@@ -341,43 +339,6 @@ __device__ __forceinline__ void mega_phase_of(int ph, int num_layers, int& layer
         layer = num_layers;
         kind = PH_LM;
     }
-}
-
-__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p)
-{
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-// Thread 0 only: poll with acquire loads. Returns false on timeout.
-// (Measured on B200 under streaming load: __threadfence + red + acquire
-// polling costs ~2.0 us per grid barrier; red.release or a trailing
-// fence.acq_rel.gpu costs ~3.0 us.)
-__device__ __forceinline__ bool grid_wait(const unsigned* bar, unsigned target, int* err)
-{
-    if (ld_acquire_u32(bar) >= target) return true;
-    const unsigned long long t0 = global_ns();
-    while (true)
-    {
-        for (int i = 0; i < 16; ++i)
-        {
-            if (ld_acquire_u32(bar) >= target) return true;
-            __nanosleep(20);
-        }
-        if (global_ns() - t0 > kWaitLimitNs)
-        {
-            atomicOr(err, kErrTimeoutFull);
-            return false;
-        }
-    }
-}
-
-// Thread 0 after a CTA barrier: make the CTA's writes visible, then count in.
-__device__ __forceinline__ void grid_arrive(unsigned* bar)
-{
-    __threadfence();
-    asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
 }
 
 // ---- epoch words ----
@@ -993,16 +954,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_decode_kernel(const Mega
                         redi[0] = 1;
                     if (tracing)
                     {
-                        // Poll rounds, ns polling, and one more load of a word already
-                        // published (its round trip in SM cycles).
-                        const unsigned long long tp1 = global_ns();
-                        const long long c0 = clock64();
-                        const unsigned long long probe = ld_relaxed_u64(a.x_ep + (kHidden - 1 - tid));
-                        asm volatile("" ::"l"(probe) : "memory");   // the load has returned
-                        const long long c1 = clock64();
                         tr[7] = rounds;
-                        tr[8] = tp1 - tp0;
-                        tr[9] = static_cast<unsigned long long>(c1 - c0);
+                        tr[8] = global_ns() - tp0;
                         tr[10] = tp0;
                     }
                 }

@@ -41,14 +41,18 @@ int hy_debug_wait_probe(hy_ctx* ctx, int kind, unsigned long long limit_ns);
 
 /* ---- persistent-kernel diagnosis -------------------------------------- */
 /* Per-phase trace: runs `tokens` AR steps from the current state and, for the
- * traced CTAs during token `trace_token`, stores %globaltimer (ns) at phase
- * start, when the phase's inputs were ready, after the prologue and at phase
- * end; for warp 0 of a GEMV phase the SM cycles spent waiting for stages, the
- * cycles spent in its dot products and its stage count; for attention the
- * slot-wait / work cycles and stages of the warp owning the split's first
- * stage and the time its stage loop ended:
- * out[(cta * (5 * num_layers + 1) + phase) * 12 + i]. The sequence length is
- * restored afterwards. */
+ * traced CTAs during token `trace_token`, stores
+ * out[(cta * (5 * num_layers + 1) + phase) * 12 + i] (thread 0 of the CTA):
+ *   i = 0..3  %globaltimer (ns) at phase start, when the phase's inputs were
+ *             ready, after the prologue and at phase end;
+ *   i = 4..6  GEMV phases: warp 0's SM cycles waiting for its stages, cycles
+ *             in its dot products and epilogues, and its stage count;
+ *   i = 7, 8, 10  GEMV phases that poll (not layer 0's q/k/v): poll rounds,
+ *             ns from the first poll to the last word, and the first poll's
+ *             %globaltimer;
+ *   i = 7..10 attention: the slot-wait / work cycles and stages of the warp
+ *             owning the split's first stage, and the time its stage loop ended.
+ * The sequence length is restored afterwards. */
 int hy_trace_persistent(hy_ctx* ctx, int tokens, int trace_token, unsigned long long* out);
 /* With HY_DEBUG_PROGRESS=1 in the environment at context creation, each CTA
  * records in host-mapped memory how many phases it completed; readable even
