@@ -51,7 +51,7 @@ EXPORTED_SYMBOLS = (
     "hy_run_vlm_dflash_with_prompt", "hy_batch_decode", "hy_fixture_meta", "hy_fixture_load",
     "hy_ctx_set_token_callback", "hy_debug_wait_stats", "hy_ctx_last_timing", "hy_ctx_last_dflash_timing",
     "hy_ctx_set_wait_limit", "hy_debug_wait_probe", "hy_ctx_create_from_package", "hy_draft_load_package",
-    "hy_package_inspect", "hy_package_read_tensor",
+    "hy_package_inspect", "hy_package_read_tensor", "hy_debug_step_trace",
 )
 TOKEN_CALLBACK = ctypes.CFUNCTYPE(None, ctypes.c_int, ctypes.c_void_p)
 DFLASH_MASK_TOKEN = 120817
@@ -177,6 +177,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
                                            ctypes.POINTER(_I)], _I),
         "hy_debug_progress": ([_P, _P, _I], _I),
         "hy_debug_wait_stats": ([_P, _P, _I, _I], _I),
+        "hy_debug_step_trace": ([_P, _P, _I, _P, _I], _I),
         "hy_ctx_create_from_package": ([ctypes.POINTER(Config), ctypes.c_char_p, ctypes.POINTER(_P)], _I),
         "hy_draft_load_package": ([_P, ctypes.c_char_p, _I], _I),
         "hy_package_inspect": ([ctypes.c_char_p, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I),
@@ -744,6 +745,18 @@ class TextRuntime:
         out = np.zeros((4, phases, 12), np.uint64)
         _check(_LIB.hy_trace_persistent(self._ctx, tokens, trace_token, _ptr(out)))
         return out
+
+    def step_trace(self, reset: bool = True, max_records: int = 16384):
+        """Step trace of the per-phase kernels (library built with HY_STEP_TRACE): an
+        [n, 5] array of {kernel id, CTA 0's %globaltimer ns at entry, after its
+        griddepcontrol.wait, after its prologue, at its end; 16-row projections: ns its
+        thread 0 waited for its weight units, ns in their MMAs, %globaltimer after its
+        last unit; the latest exit of the CTAs of the kernels before it} per launch
+        ([n, 9]), in launch order."""
+        out = np.zeros(9 * max_records, np.uint64)
+        n = ctypes.c_int(0)
+        _check(_LIB.hy_debug_step_trace(self._ctx, _ptr(out), max_records, ctypes.byref(n), int(reset)))
+        return out.reshape(max_records, 9)[:min(n.value, max_records)].copy()
 
     WAIT_KINDS = ("slot_free", "slot_full", "prod_slot", "prod_token", "poll_x", "poll_act", "poll_attn_out",
                   "poll_qkv", "poll_parts", "poll_token")

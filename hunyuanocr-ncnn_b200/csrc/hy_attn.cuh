@@ -142,6 +142,7 @@ __global__ void __launch_bounds__(kAttnThreads, (MT == 1) ? 2 : 1) attn_kernel(c
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nsplit = gridDim.x, split = blockIdx.x, g = blockIdx.y, bz = blockIdx.z;
+    HY_STEP_TRACE_OPEN(0x500000000ull | MT);
     const bool new_split = (split == nsplit - 1);
     // Rows [0, past) were written by earlier steps, so they (and past itself)
     // may be read before griddepcontrol.wait (the slot states too: the commit
@@ -211,6 +212,7 @@ __global__ void __launch_bounds__(kAttnThreads, (MT == 1) ? 2 : 1) attn_kernel(c
 
     // ---------------- consumers ----------------
     pdl_wait();
+    HY_STEP_TRACE_MARK(2);
 
     // Prologue: rotate + normalise the 2*MT queries (and, in the new-row split,
     // the MT keys; values are copied), append the new rows to the cache.
@@ -484,6 +486,8 @@ __global__ void __launch_bounds__(kAttnThreads, (MT == 1) ? 2 : 1) attn_kernel(c
         *reinterpret_cast<float4*>(out_base + static_cast<size_t>(m) * kQWidth + (2 * g + head) * kHeadDim + 4 * d4) = A;
     }
     if (tid == 0) counter[g] = 0;
+    HY_STEP_TRACE_MARK(4);
+    HY_STEP_TRACE_EXIT();
 }
 
 }  // namespace hy

@@ -2580,6 +2580,34 @@ int hy_debug_wait_stats(hy_ctx* c, unsigned long long* out, int n_words, int res
     return HY_OK;
 }
 
+int hy_debug_step_trace(hy_ctx* c, unsigned long long* out, int max_records, int* n_records, int reset)
+{
+    if (!c || max_records < 0 || (max_records > 0 && !out) || !n_records)
+        return fail(HY_ERR_INVALID_ARGUMENT, "invalid arguments");
+#ifdef HY_STEP_TRACE
+    int rc = set_device(c);
+    if (rc) return rc;
+    HY_CUDA(cudaStreamSynchronize(c->stream));
+    unsigned n = 0;
+    HY_CUDA(cudaMemcpyFromSymbol(&n, g_step_trace_n, sizeof(n)));
+    n = std::min<unsigned>(n, static_cast<unsigned>(kStepTraceMax));
+    const int k = std::min<int>(static_cast<int>(n), max_records);
+    if (k > 0)
+        HY_CUDA(cudaMemcpyFromSymbol(out, g_step_trace, sizeof(unsigned long long) * kStepTraceWords * k));
+    *n_records = static_cast<int>(n);
+    if (reset)
+    {
+        const unsigned zero = 0;
+        HY_CUDA(cudaMemcpyToSymbol(g_step_trace_n, &zero, sizeof(zero)));
+    }
+    return HY_OK;
+#else
+    (void)reset;
+    *n_records = 0;
+    return fail(HY_ERR_UNSUPPORTED, "the step trace needs a library built with HY_STEP_TRACE");
+#endif
+}
+
 int hy_trace_persistent(hy_ctx* c, int tokens, int trace_token, unsigned long long* out)
 {
     if (!c || !out || tokens < 1 || trace_token < 0 || trace_token >= tokens || tokens > kMegaChunk)

@@ -195,6 +195,58 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 // code before that kernel's wait may read data written two kernels back.
 __device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Step trace (instrumented builds, -DHY_STEP_TRACE): CTA (0, 0, 0)'s thread 0 of
+// every kernel of the per-phase paths opens a record {kernel id, %globaltimer at
+// entry, after griddepcontrol.wait, after its prologue, at its end, three
+// kernel-specific words, the latest exit of any CTA of the kernels before it}
+// in g_step_trace, in launch order; hy_debug_step_trace reads them back. Every
+// CTA's thread 0 raises g_step_last_exit when it ends (HY_STEP_TRACE_EXIT);
+// read right after the wait, it is the previous grid's last exit. Off by
+// default: the macros expand to nothing.
+constexpr int kStepTraceMax = 16384;   // records
+constexpr int kStepTraceWords = 9;     // words per record
+#ifdef HY_STEP_TRACE
+__device__ unsigned long long g_step_trace[kStepTraceMax * kStepTraceWords];
+__device__ unsigned g_step_trace_n;
+__device__ unsigned long long g_step_last_exit;
+__device__ __forceinline__ unsigned long long step_trace_now()
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ unsigned long long* step_trace_open(unsigned long long id)
+{
+    const unsigned i = atomicAdd(&g_step_trace_n, 1u);
+    if (i >= static_cast<unsigned>(kStepTraceMax)) return nullptr;
+    unsigned long long* r = g_step_trace + static_cast<unsigned long long>(kStepTraceWords) * i;
+    r[0] = id;
+    r[1] = step_trace_now();
+    for (int j = 2; j < kStepTraceWords; ++j) r[j] = 0;
+    return r;
+}
+__device__ __forceinline__ void step_trace_mark(unsigned long long* r, int slot)
+{
+    if (!r) return;
+    r[slot] = step_trace_now();
+    if (slot == 2) r[8] = atomicAdd(&g_step_last_exit, 0ull);
+}
+#define HY_STEP_TRACE_OPEN(id)                                                                               \
+    unsigned long long* hy_str_ =                                                                            \
+        (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 0) ? step_trace_open(id) \
+                                                                                    : nullptr
+#define HY_STEP_TRACE_MARK(slot) step_trace_mark(hy_str_, (slot))
+#define HY_STEP_TRACE_EXIT()                                                       \
+    do                                                                             \
+    {                                                                              \
+        if (threadIdx.x == 0) atomicMax(&g_step_last_exit, step_trace_now());     \
+    } while (0)
+#else
+#define HY_STEP_TRACE_OPEN(id)
+#define HY_STEP_TRACE_MARK(slot)
+#define HY_STEP_TRACE_EXIT()
+#endif
+
 // ---------------------------------------------------------------------------
 // Numeric helpers.
 // ---------------------------------------------------------------------------

@@ -111,7 +111,7 @@ struct GemvShape {
 };
 
 // M = 16 (DFlash verify blocks, prefill chunks) on the tensor cores (mma.sync
-// m16n8k8, tf32 with a three-term split, see tf32_mma3): the CTA's weight rows
+// m16n8k8, tf32 with a three-term split, see tf32_mma3_split): the CTA's weight rows
 // are cut into units of 8 rows x KC columns; a unit is one stage, its rows at a
 // padded pitch (row chunk + 16 bytes) and the 16 activation rows likewise
 // (pitch KP + 4 floats), so the fragment loads of a warp fall in 32 different
@@ -190,8 +190,10 @@ __device__ __forceinline__ void mma_tf32(float (&d)[4], const unsigned (&a)[4], 
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// The three products go to three accumulators (lo.hi, hi.lo, hi.hi), so
+// consecutive MMAs do not wait on each other; the caller adds them.
 template <bool W_EXACT>
-__device__ __forceinline__ void tf32_mma3(float (&d)[4], const float (&x)[4], float w0, float w1)
+__device__ __forceinline__ void tf32_mma3_split(float (&d)[3][4], const float (&x)[4], float w0, float w1)
 {
     unsigned ah[4], al[4];
 #pragma unroll
@@ -201,14 +203,14 @@ __device__ __forceinline__ void tf32_mma3(float (&d)[4], const float (&x)[4], fl
         al[i] = __float_as_uint(x[i] - __uint_as_float(ah[i]));
     }
     const unsigned bh0 = tf32_head(w0), bh1 = tf32_head(w1);
-    mma_tf32(d, al, bh0, bh1);
+    mma_tf32(d[0], al, bh0, bh1);
     if constexpr (!W_EXACT)
     {
         const unsigned bl0 = __float_as_uint(w0 - __uint_as_float(bh0));
         const unsigned bl1 = __float_as_uint(w1 - __uint_as_float(bh1));
-        mma_tf32(d, ah, bl0, bl1);
+        mma_tf32(d[1], ah, bl0, bl1);
     }
-    mma_tf32(d, ah, bh0, bh1);
+    mma_tf32(d[2], ah, bh0, bh1);
 }
 
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
@@ -289,6 +291,7 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, b = blockIdx.x;
+    HY_STEP_TRACE_OPEN(0x100000000ull | (static_cast<unsigned long long>(MT) << 24) | ((KP / 128) << 8) | (PRO << 4) | EPI);
     // EPI_ACT pairs rows (2j = gate_j, 2j+1 = up_j): split the rows by pairs.
     const int unit = (EPI == EPI_ACT) ? 2 : 1;
     const int r0 = unit * static_cast<int>(static_cast<long long>(a.N / unit) * b / G);
@@ -394,7 +397,20 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
     }
 
     // ---------------- consumers (256 threads) ----------------
+    // M = 16 RMSNorm: this thread's norm weights (constants) are loaded before the wait.
+    constexpr int KI16 = (KP + 1023) / 1024;
+    float4 nwr[(MT == 16 && PRO == PRO_NORM) ? KI16 : 1];
+    if constexpr (MT == 16 && PRO == PRO_NORM)
+    {
+#pragma unroll
+        for (int j = 0; j < KI16; ++j)
+        {
+            const int k = 4 * tid + 1024 * j;
+            nwr[j] = (k < KP) ? __ldg(reinterpret_cast<const float4*>(a.norm_w + a.k_off + k)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
     pdl_wait();
+    HY_STEP_TRACE_MARK(2);
 
     __shared__ int s_ids[kMaxStepRows];
     __shared__ float s_rinv[kMaxStepRows];
@@ -563,17 +579,24 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
             if (lane == 0) s_rinv[m] = 1.0f / sqrtf(ss / static_cast<float>(KP) + a.eps);
         }
         consumers_sync();
-        for (int i = tid; i < rows * (KP / 4); i += 256)
+#pragma unroll
+        for (int m = 0; m < MT; ++m)
         {
-            const int m = i / (KP / 4), k = 4 * (i % (KP / 4));
+            if (m >= rows) break;
             const float ri = s_rinv[m];
-            float4 v = *reinterpret_cast<float4*>(xs + m * XP + k);
-            const float4 w = *reinterpret_cast<const float4*>(a.norm_w + a.k_off + k);
-            v.x = w.x * (v.x * ri);
-            v.y = w.y * (v.y * ri);
-            v.z = w.z * (v.z * ri);
-            v.w = w.w * (v.w * ri);
-            *reinterpret_cast<float4*>(xs + m * XP + k) = v;
+#pragma unroll
+            for (int j = 0; j < KI16; ++j)
+            {
+                const int k = 4 * tid + 1024 * j;
+                if (k >= KP) break;
+                const float4 w = nwr[j];
+                float4 v = *reinterpret_cast<float4*>(xs + m * XP + k);
+                v.x = w.x * (v.x * ri);
+                v.y = w.y * (v.y * ri);
+                v.z = w.z * (v.z * ri);
+                v.w = w.w * (v.w * ri);
+                *reinterpret_cast<float4*>(xs + m * XP + k) = v;
+            }
         }
         consumers_sync();
     }
@@ -617,6 +640,7 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
         consumers_sync();
     }
 
+    HY_STEP_TRACE_MARK(3);
     pdl_launch();
 
     // ---------------- main loop ----------------
@@ -638,17 +662,28 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
         const int g8 = lane >> 2, t4 = lane & 3;
         float d[4];
         // Tile of the unit in `slot` (chunk c): d += x[0:16, chunk] * W[8 rows, chunk]^T.
+        // Six accumulator chains (the three split products x even / odd k-steps),
+        // added at the end: one chain of dependent MMAs per unit left the tensor
+        // pipe idle for most of each MMA's latency.
         auto unit_mma = [&](int slot, int c) {
             const WT* wr = reinterpret_cast<const WT*>(ring + slot * STAGE + g8 * PITCH);
             const float* x0 = xs + g8 * XP + c * KC + t4;
             const float* x1 = x0 + 8 * XP;
+            float acc[2][3][4];
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int i = 0; i < 3; ++i) acc[h][i][0] = acc[h][i][1] = acc[h][i][2] = acc[h][i][3] = 0.f;
 #pragma unroll 4
             for (int k8 = 0; k8 < KC / 8; ++k8)
             {
                 const float xa[4] = {x0[8 * k8], x1[8 * k8], x0[8 * k8 + 4], x1[8 * k8 + 4]};
                 const float w0 = to_f32<WT>(wr[8 * k8 + t4]), w1 = to_f32<WT>(wr[8 * k8 + t4 + 4]);
-                tf32_mma3<W_EXACT>(d, xa, w0, w1);
+                tf32_mma3_split<W_EXACT>(acc[k8 & 1], xa, w0, w1);
             }
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                d[e] += (acc[0][2][e] + acc[1][2][e]) + ((acc[0][0][e] + acc[1][0][e]) + (acc[0][1][e] + acc[1][1][e]));
         };
         // Store / residual / argmax epilogue of one output (row n of activation row m).
         auto emit = [&](int m, int n, float v) {
@@ -807,16 +842,30 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
         // producer once this warp released it, so every wait is one phase ahead).
         constexpr int SPW = NST / kGemvWarps;
         int jown = 0;
+#ifdef HY_STEP_TRACE
+        unsigned long long st_wait = 0, st_mma = 0;   // thread 0: ns waiting for its units / in their MMAs
+#endif
         for (int stage = 0; stage < nstage; ++stage)
         {
             const Unit16 u = unit16_of(stage, ngroups16, NKC, kmode16);
             if (u.w != warp) continue;
             const int slot = warp * SPW + jown % SPW;
+#ifdef HY_STEP_TRACE
+            const unsigned long long sw0 = global_ns();
+#endif
             const bool ok = mbar_wait(&full[slot], (jown / SPW) & 1, a.err, kErrTimeoutFull);
             ++jown;
             if (!__all_sync(0xffffffffu, ok)) break;
             if (kmode16 || u.c == 0) d[0] = d[1] = d[2] = d[3] = 0.f;
+#ifdef HY_STEP_TRACE
+            const unsigned long long sw1 = global_ns();
+            st_wait += sw1 - sw0;
+#endif
             unit_mma(slot, u.c);
+#ifdef HY_STEP_TRACE
+            __syncwarp();
+            st_mma += global_ns() - sw1;
+#endif
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
             // Tile element (m, n): d0 (g8, 2 t4), d1 (g8, 2 t4 + 1), d2 (g8 + 8, 2 t4), d3 (g8 + 8, 2 t4 + 1).
@@ -835,6 +884,14 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
                 __syncwarp();
             }
         }
+#ifdef HY_STEP_TRACE
+        if (hy_str_)
+        {
+            hy_str_[5] = st_wait;
+            hy_str_[6] = st_mma;
+            hy_str_[7] = global_ns();
+        }
+#endif
         if (kmode16)
         {
             // Add the units' tiles in chunk order and run the epilogue.
@@ -947,7 +1004,12 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
         }
     }
 
-    if (EPI != EPI_ARGMAX) return;
+    if (EPI != EPI_ARGMAX)
+    {
+        HY_STEP_TRACE_MARK(4);
+        HY_STEP_TRACE_EXIT();
+        return;
+    }
 
     // ---------------- argmax reduction ----------------
     if (lane < MT)
@@ -970,6 +1032,8 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
     consumers_sync();
     if (tid == 0) redi[0] = (atomicAdd(a.counter, 1) == G - 1) ? 1 : 0;
     consumers_sync();
+    HY_STEP_TRACE_MARK(4);
+    HY_STEP_TRACE_EXIT();
     if (!redi[0]) return;
     __threadfence();
 

@@ -53,7 +53,9 @@ struct PrefillRopeArgs {
 template <typename KT>
 __global__ void __launch_bounds__(256) prefill_rope_kernel(const PrefillRopeArgs a)
 {
+    HY_STEP_TRACE_OPEN(0x200000000ull);
     pdl_wait();
+    HY_STEP_TRACE_MARK(2);
     pdl_launch();
     const int m = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int past = a.st ? a.st->kv_len : a.past;
@@ -97,6 +99,8 @@ __global__ void __launch_bounds__(256) prefill_rope_kernel(const PrefillRopeArgs
             for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = from_f32<KT>(x[lane + 32 * i]);
         }
     }
+    HY_STEP_TRACE_MARK(4);
+    HY_STEP_TRACE_EXIT();
 }
 
 // Causal attention of the rows of a prefill pass over the cache rows
@@ -173,7 +177,9 @@ __global__ void __launch_bounds__(4 * QR, 2) prefill_attn_kernel(const PrefillAt
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
     const int kvh = blockIdx.y;
+    HY_STEP_TRACE_OPEN(0x300000000ull | QR);
     pdl_wait();
+    HY_STEP_TRACE_MARK(2);
     pdl_launch();
     const bool dev = (a.work == nullptr);
     const int past = (dev && a.st) ? a.st->kv_len : a.past;
@@ -402,6 +408,8 @@ __global__ void __launch_bounds__(4 * QR, 2) prefill_attn_kernel(const PrefillAt
             *reinterpret_cast<float2*>(a.out_lo + i) = make_float2(xl, yl);
         }
     }
+    HY_STEP_TRACE_MARK(4);
+    HY_STEP_TRACE_EXIT();
 }
 
 // Combines the chunk partials of a row block (merge item: row block, first
@@ -462,7 +470,9 @@ struct ChunkMergeArgs {
 
 __global__ void __launch_bounds__(kHeadDim) attn_chunk_merge_kernel(const ChunkMergeArgs a)
 {
+    HY_STEP_TRACE_OPEN(0x400000000ull);
     pdl_wait();
+    HY_STEP_TRACE_MARK(2);
     pdl_launch();
     const int qv = blockIdx.x, kvh = blockIdx.y, d = threadIdx.x;   // qv = hl * 16 + row
     const int row = qv % 16, hl = qv / 16;
@@ -496,6 +506,8 @@ __global__ void __launch_bounds__(kHeadDim) attn_chunk_merge_kernel(const ChunkM
         acc += w * v[c];
     }
     a.out[static_cast<size_t>(row) * kQWidth + (2 * kvh + hl) * kHeadDim + d] = acc / L;
+    HY_STEP_TRACE_MARK(4);
+    HY_STEP_TRACE_EXIT();
 }
 
 }  // namespace hy

@@ -19,6 +19,62 @@ if _ROOT not in sys.path:
     sys.path.insert(0, _ROOT)
 
 
+KERNEL_NAMES = {0x2: "rope/append", 0x3: "step attention", 0x4: "chunk merge", 0x5: "decode attention"}
+LM16_ID = 0x100000000 | (16 << 24) | (8 << 8) | (1 << 4) | 2   # 16-row LM head (K 1024, norm, argmax)
+
+
+def kernel_name(kid: int) -> str:
+    kind = kid >> 32
+    if kind == 1:
+        mt, kp, pro, epi = (kid >> 24) & 0xFF, ((kid >> 8) & 0xFFFF) * 128, (kid >> 4) & 0xF, kid & 0xF
+        return (f"proj M{mt} K{kp} " + ["plain", "norm", "swiglu"][pro] + " -> " +
+                ["store", "resid", "argmax", "swiglu"][epi])
+    return KERNEL_NAMES.get(kind, hex(kid)) + (f" {kid & 0xFF}" if kind in (3, 5) else "")
+
+
+def print_step_trace(rec, label):
+    """Where a block's (or step's) time goes: the launches between the middle pair of
+    16-row LM-head launches, grouped by kernel. Per launch i: CTA 0's entry E, the return
+    of its griddepcontrol.wait W (= the previous grid complete), the end of its prologue
+    P and its end X; critical-path time W[i+1] - W[i]."""
+    import numpy as np
+
+    rec = rec.astype(np.int64)
+    lm = np.nonzero(rec[:, 0] == LM16_ID)[0]
+    if len(lm) < 3:
+        print(f"step trace: {len(rec)} records, fewer than 3 blocks")
+        return
+    a, b = lm[len(lm) // 2 - 1] + 1, lm[len(lm) // 2] + 1   # the block ending at LM-head launch lm[mid]
+    seg = rec[a:b + 1]
+    W = seg[:, 2]
+    total = (W[-1] - W[0]) / 1e3
+    print(f"step trace ({label}): {b - a} launches, {total:.1f} us from the first launch's wait to the next "
+          f"block's first wait")
+    print(f"{'kernel':<40} {'n':>4} {'crit_us':>8} {'entry_early':>11} {'prologue':>9} {'main':>7} {'tail':>7}"
+          f" {'spread':>7} {'handoff':>7} {'unit_wait':>9} {'unit_mma':>8} {'epilogue':>8}")
+    groups = {}
+    for i in range(len(seg) - 1):
+        kid = int(seg[i, 0])
+        g = groups.setdefault(kid, [])
+        e, w, p, x = seg[i, 1:5]
+        crit = (seg[i + 1, 2] - w) / 1e3
+        early = (w - seg[i + 1, 1]) / 1e3   # how long before this kernel's wait returned the next CTA 0 started
+        pro = (p - w) / 1e3 if p else 0.0
+        main = (x - (p if p else w)) / 1e3 if x else 0.0
+        tail = (seg[i + 1, 2] - x) / 1e3 if x else 0.0
+        uw, um = seg[i, 5] / 1e3, seg[i, 6] / 1e3
+        epi = (x - seg[i, 7]) / 1e3 if (x and seg[i, 7]) else 0.0
+        last = seg[i + 1, 8]   # this grid's last CTA exit, read by the next kernel after its wait
+        spread = (last - x) / 1e3 if (x and last) else 0.0
+        handoff = (seg[i + 1, 2] - last) / 1e3 if last else 0.0
+        g.append((crit, early, pro, main, tail, spread, handoff, uw, um, epi))
+    for kid, g in sorted(groups.items(), key=lambda kv: -sum(v[0] for v in kv[1])):
+        v = np.array(g)
+        m = v.mean(axis=0)
+        print(f"{kernel_name(kid):<40} {len(g):4d} {m[0]:8.2f} {m[1]:11.2f} {m[2]:9.2f} {m[3]:7.2f} {m[4]:7.2f}"
+              f" {m[5]:7.2f} {m[6]:7.2f} {m[7]:9.2f} {m[8]:8.2f} {m[9]:8.2f}   (sum {v[:, 0].sum():.1f} us)")
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--layers", type=int, default=4)
@@ -43,6 +99,9 @@ def main(argv=None):
                          "batch: --records prompts of --past rows decoded together (hy_batch_decode); "
                          "trace: per-phase timeline of the middle token of a --tokens launch of the "
                          "persistent kernel (hy_trace_persistent), averaged over the layers for CTA 0")
+    ap.add_argument("--step-trace", action="store_true",
+                    help="verify / batch / draft: read the step trace of the last call (a library built with "
+                         "HY_STEP_TRACE, given by --lib) and print where the middle block's or step's time goes")
     args = ap.parse_args(argv)
 
     import __graft_entry__ as ge
@@ -86,10 +145,14 @@ def main(argv=None):
             ids[:16] = img
             pos = np.tile(np.arange(args.past, dtype=np.int32), (4, 1))
             reqs.append((ids, pos, img, rng.standard_normal((16, 1024)).astype(np.float32)))
-        for _ in range(args.calls):
+        for c in range(args.calls):
+            if args.step_trace and c == args.calls - 1:
+                rt.step_trace(reset=True)
             toks, _ = rt.batch_decode(reqs, args.tokens)
         print(f"batch {args.dtype} layers={args.layers} vocab={args.vocab} prompt={args.past} "
               f"records={args.records}: {len(toks[0])} tokens per record")
+        if args.step_trace:
+            print_step_trace(rt.step_trace(reset=True), f"batched decode step, {args.records} records")
         rt.close()
         return
     rt = pkg.TextRuntime.synthetic(seed=0, num_layers=args.layers, vocab_size=args.vocab, max_prefill=64,
@@ -150,23 +213,31 @@ def main(argv=None):
 
         rt.load_draft_synthetic(args.draft_layers, seed=3, std=0.02)
         rt.draft_context_append(np.random.default_rng(0).standard_normal((4, args.past, 1024), dtype=np.float32))
-        for _ in range(args.calls):
+        for c in range(args.calls):
             rt.set_length(args.past)
             rt.set_history([1, 2, 3])
+            if args.step_trace and c == args.calls - 1:
+                rt.step_trace(reset=True)
             r = rt.dflash_generate(7, args.tokens, 1.08)
         print(f"draft {args.dtype} layers={args.layers} draft_layers={args.draft_layers} vocab={args.vocab} "
               f"past={args.past}: {r.block_count} blocks per call")
+        if args.step_trace:
+            print_step_trace(rt.step_trace(reset=True), "DFlash block with the draft network")
         rt.close()
         return
     if args.kernel == "verify":
         rt.set_length(args.past)
         rt.set_history([1, 2, 3])
         greedy = [5] * (args.tokens + 32)
-        for _ in range(args.calls):
+        for c in range(args.calls):
             rt.set_length(args.past)
+            if args.step_trace and c == args.calls - 1:
+                rt.step_trace(reset=True)
             r = rt.dflash_generate_synthetic(7, args.tokens, 1.08, greedy, 0.0, seed=3)
         print(f"verify {args.dtype} layers={args.layers} vocab={args.vocab} past={args.past}: "
               f"{r.block_count} blocks per call")
+        if args.step_trace:
+            print_step_trace(rt.step_trace(reset=True), "DFlash verify block")
         rt.close()
         return
     ms = 0.0
