@@ -211,16 +211,41 @@ __global__ void __launch_bounds__(kAttnThreads, (MT == 1) ? 2 : 1) attn_kernel(c
     }
 
     // ---------------- consumers ----------------
-    pdl_wait();
-    HY_STEP_TRACE_MARK(2);
-
     // Prologue: rotate + normalise the 2*MT queries (and, in the new-row split,
     // the MT keys; values are copied), append the new rows to the cache.
     const int nvec = new_split ? (NQ + 2 * MT) : NQ;
-    // A warp's vectors are v = warp + 8 jv; all their loads (the row, the RoPE
-    // cos / sin rows) are issued before any is used: one L2 round trip.
+    // A warp's vectors are v = warp + 8 jv. The constants (RoPE cos / sin rows of
+    // the rows' positions, known before the wait, and the QK-norm weights) are
+    // loaded before griddepcontrol.wait; the rows themselves, written by the
+    // previous kernel, after it, all in one L2 round trip.
     constexpr int kMaxVec = (4 * MT + kAttnWarps - 1) / kAttnWarps;
-    float xv[kMaxVec][4], cv[kMaxVec][4], sv[kMaxVec][4];
+    float xv[kMaxVec][4], cv[kMaxVec][4], sv[kMaxVec][4], nv[kMaxVec][4];
+#pragma unroll
+    for (int jv = 0; jv < kMaxVec; ++jv)
+    {
+        const int v = warp + kAttnWarps * jv;
+        int m, kind;
+        if (v < NQ) { kind = 0; m = v % MT; }
+        else if (v < NQ + MT) { kind = 1; m = v - NQ; }
+        else { kind = 2; m = v - NQ - MT; }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) xv[jv][i] = cv[jv][i] = sv[jv][i] = nv[jv][i] = 0.f;
+        if (v >= nvec || m >= rows || kind == 2) continue;
+        const int prow = (a.rope_state ? past : 0) + m;
+        const float* c = a.cos + static_cast<size_t>(prow) * kHeadDim;
+        const float* sn = a.sin + static_cast<size_t>(prow) * kHeadDim;
+        const float* nw = (kind == 0) ? a.qn_w : a.kn_w;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+        {
+            cv[jv][i] = __ldg(c + lane + 32 * i);
+            sv[jv][i] = __ldg(sn + lane + 32 * i);
+            nv[jv][i] = __ldg(nw + lane + 32 * i);
+        }
+    }
+    pdl_wait();
+    HY_STEP_TRACE_MARK(2);
+    pdl_launch();
 #pragma unroll
     for (int jv = 0; jv < kMaxVec; ++jv)
     {
@@ -229,25 +254,12 @@ __global__ void __launch_bounds__(kAttnThreads, (MT == 1) ? 2 : 1) attn_kernel(c
         if (v < NQ) { kind = 0; head = v / MT; m = v % MT; }
         else if (v < NQ + MT) { kind = 1; head = 0; m = v - NQ; }
         else { kind = 2; head = 0; m = v - NQ - MT; }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) xv[jv][i] = cv[jv][i] = sv[jv][i] = 0.f;
         if (v >= nvec || m >= rows) continue;
         const float* src = qkv_base + static_cast<size_t>(m) * a.ldq +
                            ((kind == 0) ? (2 * g + head) * kHeadDim : (kind == 1) ? kQWidth + g * kHeadDim
                                                                                   : kQWidth + kKVWidth + g * kHeadDim);
-        const int prow = (a.rope_state ? past : 0) + m;
-        const float* c = a.cos + static_cast<size_t>(prow) * kHeadDim;
-        const float* sn = a.sin + static_cast<size_t>(prow) * kHeadDim;
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-        {
-            xv[jv][i] = src[lane + 32 * i];
-            if (kind != 2)
-            {
-                cv[jv][i] = c[lane + 32 * i];
-                sv[jv][i] = sn[lane + 32 * i];
-            }
-        }
+        for (int i = 0; i < 4; ++i) xv[jv][i] = src[lane + 32 * i];
     }
 #pragma unroll
     for (int jv = 0; jv < kMaxVec; ++jv)
@@ -278,7 +290,6 @@ __global__ void __launch_bounds__(kAttnThreads, (MT == 1) ? 2 : 1) attn_kernel(c
             continue;
         }
         // RoPE (full-width, non-interleaved) + RMSNorm, lane l owning dims l + 32 i.
-        const float* nw = (kind == 0) ? a.qn_w : a.kn_w;
         const float y0 = xv[jv][0] * cv[jv][0] - xv[jv][2] * sv[jv][0];
         const float y1 = xv[jv][1] * cv[jv][1] - xv[jv][3] * sv[jv][1];
         const float y2 = xv[jv][2] * cv[jv][2] + xv[jv][0] * sv[jv][2];
@@ -286,10 +297,10 @@ __global__ void __launch_bounds__(kAttnThreads, (MT == 1) ? 2 : 1) attn_kernel(c
         const float ss = warp_sum(y0 * y0 + y1 * y1 + y2 * y2 + y3 * y3);
         const float ri = 1.0f / sqrtf(ss / static_cast<float>(kHeadDim) + a.eps);
         float o[4];
-        o[0] = nw[lane] * (y0 * ri);
-        o[1] = nw[lane + 32] * (y1 * ri);
-        o[2] = nw[lane + 64] * (y2 * ri);
-        o[3] = nw[lane + 96] * (y3 * ri);
+        o[0] = nv[jv][0] * (y0 * ri);
+        o[1] = nv[jv][1] * (y1 * ri);
+        o[2] = nv[jv][2] * (y2 * ri);
+        o[3] = nv[jv][3] * (y3 * ri);
         if (kind == 0)
         {
 #pragma unroll
@@ -308,7 +319,7 @@ __global__ void __launch_bounds__(kAttnThreads, (MT == 1) ? 2 : 1) attn_kernel(c
         }
     }
     attn_consumers_sync();
-    pdl_launch();
+    HY_STEP_TRACE_MARK(3);
 
     {
         // Lane roles.
@@ -431,7 +442,12 @@ __global__ void __launch_bounds__(kAttnThreads, (MT == 1) ? 2 : 1) attn_kernel(c
     attn_consumers_sync();
     if (tid == 0) s_last = (atomicAdd(&counter[g], 1) == nsplit - 1) ? 1 : 0;
     attn_consumers_sync();
-    if (!s_last) return;
+    HY_STEP_TRACE_MARK(4);
+    if (!s_last)
+    {
+        HY_STEP_TRACE_EXIT();
+        return;
+    }
     __threadfence();
 
     // Last CTA of this head: merge the S partials. First the (max, sum) of
@@ -486,7 +502,6 @@ __global__ void __launch_bounds__(kAttnThreads, (MT == 1) ? 2 : 1) attn_kernel(c
         *reinterpret_cast<float4*>(out_base + static_cast<size_t>(m) * kQWidth + (2 * g + head) * kHeadDim + 4 * d4) = A;
     }
     if (tid == 0) counter[g] = 0;
-    HY_STEP_TRACE_MARK(4);
     HY_STEP_TRACE_EXIT();
 }
 

@@ -48,9 +48,17 @@ int fail(int code, const std::string& msg)
     } while (0)
 
 constexpr int kFfn = 3584;                // kernels are specialised for the model's FFN width
-constexpr int kAttnSplitsAR = 19;         // 18 past splits + the new-row split (152 CTAs)
+// Splits per KV head of the M = 1 attention kernel: past splits + the new-row
+// split. Measured per launch (7 / 10 / 13 / 19 splits): KV 1024 10.2 / 9.3 /
+// 9.0 / 10.2 us, KV 8192 28.1 / 22.7 / 20.7 / 21.5 us - fewer splits shorten
+// the last-CTA merge, more shorten each CTA's stream.
+#ifndef HY_ATTN_SPLITS_AR
+#define HY_ATTN_SPLITS_AR 13
+#endif
+constexpr int kAttnSplitsAR = HY_ATTN_SPLITS_AR;
 constexpr int kVerifyChunks = 36;         // key chunks per KV head of a <= 16-row step (288 CTAs, 2 per SM)
 constexpr int kMaxSplits = 20;
+static_assert(kAttnSplitsAR >= 2 && kAttnSplitsAR <= kMaxSplits, "split count");
 constexpr int kArStepsPerGraph = 4;
 constexpr int kMegaChunk = 64;            // tokens per persistent-kernel launch
 constexpr int kPrefillChunk = 1024;       // prompt rows per prefill pass (all layers)

@@ -203,9 +203,21 @@ def main(argv=None):
     if args.kernel in ("lm", "gate_up", "attention"):
         rt.set_length(args.past)
         which = {"lm": 0, "gate_up": 1, "attention": 2}[args.kernel]
+        if args.step_trace:
+            rt.step_trace(reset=True)
         ms = rt.bench_kernel(which, args.calls)
         print(f"{args.kernel} {args.dtype} layers={args.layers} vocab={args.vocab} past={args.past}: "
               f"{ms * 1e3:.2f} us per launch")
+        if args.step_trace:
+            import numpy as np
+
+            rec = rt.step_trace(reset=True).astype(np.int64)[1:]   # the timed launches
+            e, w, x, last = rec[:, 1], rec[:, 2], rec[:, 4], rec[:, 8]
+            print(f"step trace ({len(rec)} launches of {kernel_name(int(rec[0, 0]))}, us): "
+                  f"critical path {np.mean(np.diff(w)) / 1e3:.2f}, CTA 0 entry before the previous wait "
+                  f"{np.mean(w[:-1] - e[1:]) / 1e3:.2f}, CTA 0 wait -> end {np.mean(x - w) / 1e3:.2f}, "
+                  f"CTA 0 end -> last CTA end {np.mean(last[1:] - x[:-1]) / 1e3:.2f}, "
+                  f"last CTA end -> next wait {np.mean(w[1:] - last[1:]) / 1e3:.2f}")
         rt.close()
         return
     if args.kernel == "draft":
