@@ -751,12 +751,13 @@ class TextRuntime:
         [n, 5] array of {kernel id, CTA 0's %globaltimer ns at entry, after its
         griddepcontrol.wait, after its prologue, at its end; 16-row projections: ns its
         thread 0 waited for its weight units, ns in their MMAs, %globaltimer after its
-        last unit; the latest exit of the CTAs of the kernels before it} per launch
-        ([n, 9]), in launch order."""
-        out = np.zeros(9 * max_records, np.uint64)
+        last unit; the latest exit of the CTAs of the kernels before it; 16-row
+        projections: each warp's last-unit time and its ns waiting for units} per launch
+        ([n, 25]), in launch order."""
+        out = np.zeros(25 * max_records, np.uint64)
         n = ctypes.c_int(0)
         _check(_LIB.hy_debug_step_trace(self._ctx, _ptr(out), max_records, ctypes.byref(n), int(reset)))
-        return out.reshape(max_records, 9)[:min(n.value, max_records)].copy()
+        return out.reshape(max_records, 25)[:min(n.value, max_records)].copy()
 
     WAIT_KINDS = ("slot_free", "slot_full", "prod_slot", "prod_token", "poll_x", "poll_act", "poll_attn_out",
                   "poll_qkv", "poll_parts", "poll_token")

@@ -198,13 +198,14 @@ __device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.laun
 // Step trace (instrumented builds, -DHY_STEP_TRACE): CTA (0, 0, 0)'s thread 0 of
 // every kernel of the per-phase paths opens a record {kernel id, %globaltimer at
 // entry, after griddepcontrol.wait, after its prologue, at its end, three
-// kernel-specific words, the latest exit of any CTA of the kernels before it}
+// kernel-specific words, the latest exit of any CTA of the kernels before it,
+// 16 more kernel-specific words}
 // in g_step_trace, in launch order; hy_debug_step_trace reads them back. Every
 // CTA's thread 0 raises g_step_last_exit when it ends (HY_STEP_TRACE_EXIT);
 // read right after the wait, it is the previous grid's last exit. Off by
 // default: the macros expand to nothing.
 constexpr int kStepTraceMax = 16384;   // records
-constexpr int kStepTraceWords = 9;     // words per record
+constexpr int kStepTraceWords = 25;    // words per record
 #ifdef HY_STEP_TRACE
 __device__ unsigned long long g_step_trace[kStepTraceMax * kStepTraceWords];
 __device__ unsigned g_step_trace_n;

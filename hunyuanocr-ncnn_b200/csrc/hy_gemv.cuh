@@ -304,6 +304,10 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
     const int nstage = TL ? ((R + 127) / 128) * nk_tl : (MT == 16) ? ngroups16 * (KP / S::KC16) : (R + SPS - 1) / SPS;
 
     __shared__ uint64_t s_xbar;   // M = 16: bulk copy of the activation rows
+#ifdef HY_STEP_TRACE
+    __shared__ unsigned long long* s_str;   // CTA 0's record, for every warp
+    if (tid == 0) s_str = hy_str_;
+#endif
     if (tid == 0)
     {
         for (int s = 0; s < NS; ++s)
@@ -397,17 +401,14 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
     }
 
     // ---------------- consumers (256 threads) ----------------
-    // M = 16 RMSNorm: this thread's norm weights (constants) are loaded before the wait.
-    constexpr int KI16 = (KP + 1023) / 1024;
-    float4 nwr[(MT == 16 && PRO == PRO_NORM) ? KI16 : 1];
+    // M = 16 RMSNorm: the norm weights of this lane's columns (k = 4 lane + 128 i;
+    // constants) are loaded before the wait.
+    float4 nwr[(MT == 16 && PRO == PRO_NORM) ? KP / 128 : 1];
     if constexpr (MT == 16 && PRO == PRO_NORM)
     {
 #pragma unroll
-        for (int j = 0; j < KI16; ++j)
-        {
-            const int k = 4 * tid + 1024 * j;
-            nwr[j] = (k < KP) ? __ldg(reinterpret_cast<const float4*>(a.norm_w + a.k_off + k)) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+        for (int i = 0; i < KP / 128; ++i)
+            nwr[i] = __ldg(reinterpret_cast<const float4*>(a.norm_w + a.k_off + 4 * lane + 128 * i));
     }
     pdl_wait();
     HY_STEP_TRACE_MARK(2);
@@ -566,37 +567,27 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
 
     if (PRO == PRO_NORM && MT == 16)
     {
-        // Per-row 1/sqrt(mean(x^2) + eps) (warp w: rows w and w + 8), then xs = w * (x * rinv).
+        // One pass (warp w: rows w and w + 8): xs = w * x and the row's
+        // 1/sqrt(mean(x^2) + eps), which the epilogue applies to the row's dot
+        // products (group_epilogue): the RMSNorm's per-row scale commutes with the
+        // projection, so the units need not wait for it.
         for (int m = warp; m < MT; m += kGemvWarps)
         {
             float ss = 0.f;
-            for (int k = lane * 4; k < KP; k += 128)
+#pragma unroll
+            for (int i = 0; i < KP / 128; ++i)
             {
-                const float4 v = *reinterpret_cast<const float4*>(xs + m * XP + k);
+                float4* p = reinterpret_cast<float4*>(xs + m * XP + 4 * lane + 128 * i);
+                float4 v = *p;
                 ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                v.x *= nwr[i].x;
+                v.y *= nwr[i].y;
+                v.z *= nwr[i].z;
+                v.w *= nwr[i].w;
+                *p = v;
             }
             ss = warp_sum(ss);
             if (lane == 0) s_rinv[m] = 1.0f / sqrtf(ss / static_cast<float>(KP) + a.eps);
-        }
-        consumers_sync();
-#pragma unroll
-        for (int m = 0; m < MT; ++m)
-        {
-            if (m >= rows) break;
-            const float ri = s_rinv[m];
-#pragma unroll
-            for (int j = 0; j < KI16; ++j)
-            {
-                const int k = 4 * tid + 1024 * j;
-                if (k >= KP) break;
-                const float4 w = nwr[j];
-                float4 v = *reinterpret_cast<float4*>(xs + m * XP + k);
-                v.x = w.x * (v.x * ri);
-                v.y = w.y * (v.y * ri);
-                v.z = w.z * (v.z * ri);
-                v.w = w.w * (v.w * ri);
-                *reinterpret_cast<float4*>(xs + m * XP + k) = v;
-            }
         }
         consumers_sync();
     }
@@ -711,14 +702,20 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
                 if (best.pi < 0 || ps > best.pv) { best.pv = ps; best.pi = n; }
             }
         };
-        // Epilogue of a finished 8-row group from its [m][n] tile.
+        // Epilogue of a finished 8-row group from its [m][n] tile (times the
+        // activation row's RMSNorm scale when the prologue normalised).
+        auto tval = [&](const float* tile, int m, int row) {
+            const float v = tile[m * 8 + row];
+            if constexpr (PRO == PRO_NORM) return v * s_rinv[m];
+            else return v;
+        };
         auto group_epilogue = [&](const float* tile, int g) {
             const int n0 = r0 + 8 * g;
             const int nr = min(8, R - 8 * g);
             if (EPI == EPI_ARGMAX)
             {
                 if (lane < rows)
-                    for (int row = 0; row < nr; ++row) emit(lane, n0 + row, tile[lane * 8 + row]);
+                    for (int row = 0; row < nr; ++row) emit(lane, n0 + row, tval(tile, lane, row));
             }
             else if (EPI == EPI_ACT)
             {
@@ -728,7 +725,7 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
                     const int m = p >> 2, pr = p & 3;
                     if (2 * pr + 1 < nr && m < rows)
                     {
-                        const float gt = tile[m * 8 + 2 * pr], up = tile[m * 8 + 2 * pr + 1];
+                        const float gt = tval(tile, m, 2 * pr), up = tval(tile, m, 2 * pr + 1);
                         a.out[static_cast<size_t>(m) * a.ldo + ((n0 >> 1) + pr)] = (gt / (1.0f + expf(-gt))) * up;
                     }
                 }
@@ -738,7 +735,7 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
                 for (int p = lane; p < 16 * 8; p += 32)
                 {
                     const int m = p >> 3, row = p & 7;
-                    if (row < nr && m < rows) emit(m, n0 + row, tile[m * 8 + row]);
+                    if (row < nr && m < rows) emit(m, n0 + row, tval(tile, m, row));
                 }
             }
         };
@@ -890,6 +887,11 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
             hy_str_[5] = st_wait;
             hy_str_[6] = st_mma;
             hy_str_[7] = global_ns();
+        }
+        if (s_str && lane == 0)
+        {
+            s_str[9 + warp] = global_ns();   // this warp's last unit done
+            s_str[17 + warp] = st_wait;      // and its waits for units
         }
 #endif
         if (kmode16)

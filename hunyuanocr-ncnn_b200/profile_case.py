@@ -68,6 +68,15 @@ def print_step_trace(rec, label):
         spread = (last - x) / 1e3 if (x and last) else 0.0
         handoff = (seg[i + 1, 2] - last) / 1e3 if last else 0.0
         g.append((crit, early, pro, main, tail, spread, handoff, uw, um, epi))
+    # Per-warp finish of the 16-row projections (CTA 0): last-unit time after the wait.
+    for kid in sorted(groups):
+        rows_k = [i for i in range(len(seg) - 1) if int(seg[i, 0]) == kid and seg[i, 9]]
+        if not rows_k:
+            continue
+        ends = np.array([(seg[i, 9:17] - seg[i, 2]) / 1e3 for i in rows_k]).mean(axis=0)
+        waits = np.array([seg[i, 17:25] / 1e3 for i in rows_k]).mean(axis=0)
+        print(f"  {kernel_name(kid):<38} warps' last unit after the wait: " + " ".join(f"{x:5.2f}" for x in ends) +
+              "  | waits: " + " ".join(f"{x:4.2f}" for x in waits))
     for kid, g in sorted(groups.items(), key=lambda kv: -sum(v[0] for v in kv[1])):
         v = np.array(g)
         m = v.mean(axis=0)

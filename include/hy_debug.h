@@ -71,15 +71,16 @@ int hy_debug_progress(const hy_ctx* ctx, unsigned* out, int n);
 int hy_debug_wait_stats(hy_ctx* ctx, unsigned long long* out, int n_words, int reset);
 /* Step trace of the per-phase kernels (projections, RoPE/append, attention,
  * merges), in a library built with HY_STEP_TRACE defined (HY_ERR_UNSUPPORTED
- * otherwise): after the context's stream is idle, out[9 * i ..] receives, for
+ * otherwise): after the context's stream is idle, out[25 * i ..] receives, for
  * the first max_records launches since the last reset in the order their
  * CTA 0 started, {kernel id, %globaltimer ns at CTA 0's entry, after its
  * griddepcontrol.wait, after its prologue (projections), at its end; for the
  * 16-row projections the ns thread 0 waited for its weight units, the ns in
  * their MMAs and the %globaltimer after its last unit; the latest exit of any
- * CTA of the kernels before it, read after its wait} (9 words per record), 0
- * where a point was not passed; *n_records = the launches recorded (at most
- * 16384).
+ * CTA of the kernels before it, read after its wait; for the 16-row
+ * projections each consumer warp's %globaltimer after its last unit (8 words)
+ * and its ns waiting for units (8 words)} (25 words per record), 0 where a
+ * point was not passed; *n_records = the launches recorded (at most 16384).
  * Kernel ids: 0x1_MM_KK_PE projections (MM rows, KK = K / 128, P prologue,
  * E epilogue), 0x2 RoPE/append, 0x3_QR step attention, 0x4 chunk merge,
  * 0x5_MT decode attention. reset != 0 restarts the record count. */
