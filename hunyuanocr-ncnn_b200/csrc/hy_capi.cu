@@ -56,7 +56,13 @@ constexpr int kFfn = 3584;                // kernels are specialised for the mod
 #define HY_ATTN_SPLITS_AR 13
 #endif
 constexpr int kAttnSplitsAR = HY_ATTN_SPLITS_AR;
-constexpr int kVerifyChunks = 36;         // key chunks per KV head of a <= 16-row step (288 CTAs, 2 per SM)
+// Key chunks per KV head of a <= 16-row step's attention (36: 288 CTAs, one wave at
+// 2 per SM). In the verify graph at KV 2048, 18 / 24 / 36 / 40 chunks: attention
+// 14.7 / 12.7 / 10.5 / 15.7 us + merge 2.8 / 3.1 / 3.8 / 4.1 us per layer.
+#ifndef HY_VERIFY_CHUNKS
+#define HY_VERIFY_CHUNKS 36
+#endif
+constexpr int kVerifyChunks = HY_VERIFY_CHUNKS;
 constexpr int kMaxSplits = 20;
 static_assert(kAttnSplitsAR >= 2 && kAttnSplitsAR <= kMaxSplits, "split count");
 constexpr int kArStepsPerGraph = 4;
