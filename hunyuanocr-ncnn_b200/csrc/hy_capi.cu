@@ -104,6 +104,7 @@ struct hy_ctx {
     float* rope_sin = nullptr;
     float* pre_cos = nullptr;   // prefill / explicit-row tables [max(max_prefill,16) x 128]
     float* pre_sin = nullptr;
+    int* pre_pos = nullptr;     // a prompt's position ids [4 x max(max_prefill,16)] (mRoPE gather)
     float* prompt = nullptr;    // [max_prefill x 1024]
     // step buffers
     float* x = nullptr;         // [16 x 1024] residual stream
@@ -983,6 +984,7 @@ int alloc_ctx(hy_ctx* c)
     if ((rc = dalloc(c, &c->rope_sin, rope_rows * kHeadDim))) return rc;
     const size_t pre_rows = static_cast<size_t>(std::max(cfg.max_prefill, kMaxStepRows));
     if ((rc = dalloc(c, &c->pre_cos, pre_rows * kHeadDim))) return rc;
+    if ((rc = dalloc(c, &c->pre_pos, 4 * pre_rows))) return rc;
     if ((rc = dalloc(c, &c->pre_sin, pre_rows * kHeadDim))) return rc;
     if ((rc = dalloc(c, &c->prompt, pre_rows * kHidden))) return rc;
     if ((rc = dalloc(c, &c->feats, pre_rows * kHidden))) return rc;
@@ -3113,15 +3115,32 @@ static int prompt_prefill_first(hy_ctx* c, const int* input_ids, const int* posi
     std::memcpy(ps.ids, input_ids, sizeof(int) * seq_len);
     std::memcpy(ps.feat_idx, feat_idx.data(), sizeof(int) * seq_len);
     std::memcpy(ps.feats, vision_features, sizeof(float) * vision_token_count * kHidden);
-    if ((rc = hy_build_mrope(position_ids, seq_len, 1, ps.cos)) || (rc = hy_build_mrope(position_ids, seq_len, 0, ps.sin)))
+    // mRoPE tables: gathered on the device from the 1-D table when every position
+    // lies inside it (mrope_gather_kernel), else built on the host.
+    bool gather = true;
+    for (int i = 0; i < 4 * seq_len && gather; ++i) gather = position_ids[i] >= 0 && position_ids[i] < c->cfg.max_context;
+    int* ps_pos = reinterpret_cast<int*>(ps.cos);   // (the table staging holds 4 x seq ints)
+    if (gather) std::memcpy(ps_pos, position_ids, sizeof(int) * 4 * seq_len);
+    else if ((rc = hy_build_mrope(position_ids, seq_len, 1, ps.cos)) ||
+             (rc = hy_build_mrope(position_ids, seq_len, 0, ps.sin)))
         return rc;
     HY_CUDA(cudaEventRecord(c->tev[0], c->stream));
     HY_CUDA(cudaMemcpyAsync(c->ids_buf, ps.ids, sizeof(int) * seq_len, cudaMemcpyHostToDevice, c->stream));
     HY_CUDA(cudaMemcpyAsync(c->feat_idx, ps.feat_idx, sizeof(int) * seq_len, cudaMemcpyHostToDevice, c->stream));
     HY_CUDA(cudaMemcpyAsync(c->feats, ps.feats, sizeof(float) * vision_token_count * kHidden, cudaMemcpyHostToDevice,
                             c->stream));
-    HY_CUDA(cudaMemcpyAsync(c->pre_cos, ps.cos, sizeof(float) * seq_len * kHeadDim, cudaMemcpyHostToDevice, c->stream));
-    HY_CUDA(cudaMemcpyAsync(c->pre_sin, ps.sin, sizeof(float) * seq_len * kHeadDim, cudaMemcpyHostToDevice, c->stream));
+    if (gather)
+    {
+        HY_CUDA(cudaMemcpyAsync(c->pre_pos, ps_pos, sizeof(int) * 4 * seq_len, cudaMemcpyHostToDevice, c->stream));
+        mrope_gather_kernel<<<seq_len, kHeadDim, 0, c->stream>>>(c->pre_pos, seq_len, c->rope_cos, c->rope_sin,
+                                                                 c->cfg.max_context, c->pre_cos, c->pre_sin, c->err);
+        HY_CUDA(cudaGetLastError());
+    }
+    else
+    {
+        HY_CUDA(cudaMemcpyAsync(c->pre_cos, ps.cos, sizeof(float) * seq_len * kHeadDim, cudaMemcpyHostToDevice, c->stream));
+        HY_CUDA(cudaMemcpyAsync(c->pre_sin, ps.sin, sizeof(float) * seq_len * kHeadDim, cudaMemcpyHostToDevice, c->stream));
+    }
     if (c->cfg.weight_dtype == HY_DTYPE_BF16)
         embed_prompt_kernel<__nv_bfloat16><<<seq_len, 256, 0, c->stream>>>(
             c->ids_buf, c->feat_idx, c->feats, static_cast<const __nv_bfloat16*>(c->embed), c->cfg.vocab_size, c->prompt, c->err);

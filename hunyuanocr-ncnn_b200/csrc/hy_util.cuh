@@ -102,6 +102,26 @@ __global__ void embed_prompt_kernel(const int* ids, const int* feat_idx, const f
     *dst = load4(table + static_cast<size_t>(id) * kHidden + tid * 4);
 }
 
+// build_mrope (src/text_runtime.cpp:42-63) for positions inside the context's
+// 1-D RoPE table: entry (t, d) of the 4-axis table is the 1-D table's entry at
+// position_ids[d / 32][t] (the same base, inverse frequency and float angle per
+// element), so the prompt's tables are gathered on the device rather than
+// evaluated on the host. Block t, thread d; positions outside the table were
+// rejected on the host (a bounds error here is a defect).
+__global__ void mrope_gather_kernel(const int* pos, int seq, const float* cos1, const float* sin1, int rows,
+                                    float* cos_out, float* sin_out, int* err)
+{
+    const int t = blockIdx.x, d = threadIdx.x;
+    int p = pos[(d / (kHeadDim / 4)) * seq + t];
+    if (p < 0 || p >= rows)
+    {
+        atomicOr(err, kErrBounds);
+        p = 0;
+    }
+    cos_out[static_cast<size_t>(t) * kHeadDim + d] = cos1[static_cast<size_t>(p) * kHeadDim + d];
+    sin_out[static_cast<size_t>(t) * kHeadDim + d] = sin1[static_cast<size_t>(p) * kHeadDim + d];
+}
+
 __global__ void hist_add_kernel(unsigned* bits, const int* ids, int n, int vocab)
 {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)

@@ -178,15 +178,17 @@ def test_dflash_is_lossless_and_matches_oracle(small, oracle):
         assert out.block_count == ref.block_count
 
 
+@pytest.mark.parametrize("penalty", [1.08, 1.0])
 @pytest.mark.parametrize("path", ["persistent", "graph"])
-def test_ar_paths_match_oracle(pkg, small, oracle, path):
+def test_ar_paths_match_oracle(pkg, small, oracle, path, penalty):
+    """Both AR paths, with the reference's default penalty and with none (config 0's two runs)."""
     cfg, w, rt = small
     prompt = oracle.synthetic_prompt(33, 4, 6, 16, cfg.vocab, cfg.vocab - 3)
-    want = oracle.decode_ar(w, cfg, prompt, 150)
+    want = oracle.decode_ar(w, cfg, prompt, 150, penalty=penalty)
     rt.ar_path = pkg.AR_PATH_PERSISTENT if path == "persistent" else pkg.AR_PATH_GRAPH
     try:
         res = rt.run_vlm_decode_with_prompt(prompt.input_ids, prompt.position_ids, prompt.image_token_id,
-                                            prompt.vision_features, max_tokens=150)
+                                            prompt.vision_features, max_tokens=150, repetition_penalty=penalty)
     finally:
         rt.ar_path = pkg.AR_PATH_PERSISTENT
     assert res.generated_tokens == want.tokens
