@@ -17,7 +17,7 @@ def pytest_configure(config):
 @pytest.fixture(scope="session")
 def pkg():
     import __graft_entry__ as ge
-    ge.build()
+    ge.build(force=False)   # compiles only what is older than its sources
     return ge.load_package()
 
 

@@ -178,6 +178,29 @@ def test_dflash_is_lossless_and_matches_oracle(small, oracle):
         assert out.block_count == ref.block_count
 
 
+def test_dflash_lossless_repeated(small, oracle):
+    """The verify path gives the same tokens on every run: 150 repetitions of the
+    lossless check at p = 0.9 (a race between the layer-0 residual publication and the
+    in-place RMSNorm once flipped one token in a few hundred runs)."""
+    cfg, w, rt = small
+    prompt = oracle.synthetic_prompt(21, 4, 6, 16, cfg.vocab, cfg.vocab - 3)
+    n = 48
+    greedy = oracle.decode_ar(w, cfg, prompt, n + 20).tokens
+    seq = prompt.input_ids.shape[0]
+    emb = oracle.prepare_prompt_embeddings(w, prompt)
+    cos = oracle.build_mrope(prompt.position_ids, seq, True)
+    sin = oracle.build_mrope(prompt.position_ids, seq, False)
+    bad = []
+    for rep in range(150):
+        rt.reset()
+        rt.prefill(emb, cos, sin)
+        rt.set_history(prompt.input_ids)
+        out = rt.dflash_generate_synthetic(greedy[0], n, 1.08, greedy, 0.9, seed=99)
+        if out.generated_tokens != greedy[:n]:
+            bad.append(rep)
+    assert not bad, f"runs with different tokens: {bad}"
+
+
 @pytest.mark.parametrize("penalty", [1.08, 1.0])
 @pytest.mark.parametrize("path", ["persistent", "graph"])
 def test_ar_paths_match_oracle(pkg, small, oracle, path, penalty):
