@@ -85,12 +85,6 @@ struct GemvArgs {
     int* slot_cur;        // LM_BATCH: each row's next token (the next step's gather ids)
     int hist_stride;      // LM_BATCH: words between the rows' history bitmaps
     int log_stride;       // LM_BATCH: token-log entries per row
-    // Optional L2 prefetch of the next projection's weights (16-row steps): the rows
-    // CTA b of that launch will read (same row split, pf_unit rows per unit), columns
-    // [pf_k_off, pf_k_off + pf_cols) of pf_ldw, issued once this launch's weights are
-    // requested, so the next launch's late CTAs find them in L2.
-    const void* pf_W;
-    int pf_N, pf_ldw, pf_k_off, pf_cols, pf_unit;
     // M = 16 LM head: tensor map of the tied table (128-row x 128-byte boxes, 128-byte swizzle).
     CUtensorMap tmap;
 };
@@ -390,27 +384,6 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
                         bulk_g2s(dst + j * SEG, W + static_cast<size_t>(sr0 + j) * a.ldw + a.k_off, SEG, &full[slot], pol);
                 }
                 issued = i + 1;
-            }
-            if (MT == 16 && a.pf_W)
-            {
-                const int u = a.pf_unit;
-                const int q0 = u * static_cast<int>(static_cast<long long>(a.pf_N / u) * b / G);
-                const int q1 = u * static_cast<int>(static_cast<long long>(a.pf_N / u) * (b + 1) / G);
-                const unsigned char* pw = static_cast<const unsigned char*>(a.pf_W);
-                const uint32_t rb = static_cast<uint32_t>(a.pf_cols) * sizeof(WT);
-                if (a.pf_cols == a.pf_ldw)
-                {
-                    // Whole rows: one contiguous range, in pieces of at most 32 KB.
-                    const size_t total = static_cast<size_t>(q1 - q0) * rb;
-                    const unsigned char* p0 = pw + static_cast<size_t>(q0) * rb;
-                    for (size_t o = 0; o < total; o += 32768)
-                        bulk_prefetch_l2(p0 + o, static_cast<uint32_t>(total - o < 32768 ? total - o : 32768));
-                }
-                else
-                {
-                    for (int r = q0; r < q1; ++r)
-                        bulk_prefetch_l2(pw + (static_cast<size_t>(r) * a.pf_ldw + a.pf_k_off) * sizeof(WT), rb);
-                }
             }
             // Drain: never leave the CTA with copies in flight.
             if constexpr (MT == 16)
