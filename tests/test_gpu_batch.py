@@ -49,6 +49,18 @@ def test_batch_tokens_match_oracle_per_record(model, oracle, slots):
     assert rt.kv_length == 0
 
 
+def test_batch_repeated(model, oracle):
+    """Ten batched runs of the same records give the same (oracle) tokens every time."""
+    cfg, w, rt = model
+    prompts = _prompts(oracle, 7)
+    n = 40
+    want = [oracle.decode_ar(w, cfg, p, n).tokens for p in prompts]
+    for rep in range(10):
+        toks, status = rt.batch_decode([_req(p) for p in prompts], n, slots=16)
+        assert status == [0] * len(prompts)
+        assert toks == want, rep
+
+
 def test_batch_equals_single_record_calls_with_eos(model, oracle):
     cfg, w, rt = model
     prompts = _prompts(oracle, 5)

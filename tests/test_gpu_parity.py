@@ -219,6 +219,27 @@ def test_ar_paths_match_oracle(pkg, small, oracle, path, penalty):
     assert rt.kv_length == prompt.input_ids.shape[0] + 149
 
 
+def test_ar_paths_repeated(pkg, small, oracle):
+    """Both AR paths give the oracle's tokens on every one of 40 runs each (the graph
+    path's kernels read constants and the decode state before waiting on the kernel
+    before them; a race there would show as a run that differs)."""
+    cfg, w, rt = small
+    prompt = oracle.synthetic_prompt(33, 4, 6, 16, cfg.vocab, cfg.vocab - 3)
+    want = oracle.decode_ar(w, cfg, prompt, 100).tokens
+    bad = []
+    try:
+        for path in (pkg.AR_PATH_GRAPH, pkg.AR_PATH_PERSISTENT):
+            rt.ar_path = path
+            for rep in range(40):
+                res = rt.run_vlm_decode_with_prompt(prompt.input_ids, prompt.position_ids, prompt.image_token_id,
+                                                    prompt.vision_features, max_tokens=100)
+                if res.generated_tokens != want:
+                    bad.append((path, rep))
+    finally:
+        rt.ar_path = pkg.AR_PATH_PERSISTENT
+    assert not bad, f"runs with different tokens: {bad}"
+
+
 def test_eos_stops_generation(small, oracle):
     cfg, w, rt = small
     prompt = oracle.synthetic_prompt(21, 4, 6, 16, cfg.vocab, cfg.vocab - 3)
