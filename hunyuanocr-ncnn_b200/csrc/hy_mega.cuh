@@ -10,31 +10,36 @@
 // range of cached positions for attention), and each CTA's share is cut into
 // stages of at most 16 KB.
 //
-// The CTA's stage sequence (over all phases and tokens of the launch) is dealt
-// round-robin to its 6 consumer warps: warp w owns the stages g with
-// g % 6 == w and has two 16 KB shared-memory slots of its own. A producer warp
-// walks the sequence and streams each stage into its owner's next slot with
-// cp.async.bulk (no multicast) as soon as the owner has released it, across
-// phase boundaries too - no weight byte depends on an activation, so the next
-// phase's weights are usually resident before its grid barrier opens. A
-// consumer warp waits only on its own slots, so the warps never wait on one
-// another inside a phase. A stage's rows are reduced in one pass: the warp
-// holds the activation vector in registers (K = 1024) and a transposing
-// butterfly leaves each row's sum in its own group of lanes, which then run the
-// epilogue in parallel.
+// Streaming: the CTA's stage sequence (over all phases and tokens of the
+// launch) is dealt round-robin to its 7 consumer warps (stage g to warp g % 7)
+// and into a ring of 12 shared-memory slots of 16 KB (stage g to slot g % 12).
+// A producer warp streams the stages with cp.async.bulk (no multicast) across
+// phase boundaries - no weight byte depends on an activation - keeping at most
+// 2 stages in flight (6 in the LM head): more copies in flight delay the
+// latency-critical exchange loads below. A consumer warp waits for its stage's
+// slot to have been released by the slot's previous stage, then for the stage
+// itself, so every mbarrier parity wait is at most one phase ahead. A stage's
+// rows are reduced in one pass: the activation vector sits in registers (K =
+// 1024) or shared memory, and a transposing butterfly leaves each row's sum in
+// its own group of lanes, which run the epilogue in parallel.
 //
-// Warps meet at phase boundaries, where a grid barrier makes the phase's input
-// activations visible and the CTA stages them in shared memory (fused RMSNorm,
-// SwiGLU, embedding gather, attention split-K merge). Attention splits each KV
-// head's cached positions over 8 CTAs plus one CTA for the new row (RoPE +
-// QK-norm + KV append); every CTA merges the split partials in the
-// o-projection prologue. The LM head's last CTA (atomic ticket) merges the
-// per-CTA argmax partials and commits the token.
+// Exchange between CTAs, with no grid barrier: every activation a phase
+// produces (q/k/v rows, the residual stream, SwiGLU outputs, attention split
+// partials and merged head outputs) is one 64-bit word, float bits | phase epoch
+// << 32, written with one relaxed store; the next phase polls the words it needs
+// until they carry its epoch, then stages them in shared memory (fused RMSNorm,
+// whose per-row scale is applied to the dot products; SwiGLU; embedding
+// gather). The residual rows a CTA owns stay in its shared memory. Attention
+// splits each KV head's cached positions over 17 CTAs plus one CTA for the new
+// row (RoPE + QK-norm + KV append); the new-row CTA of each head pair merges
+// the pair's split partials and publishes the merged head outputs for the o
+// projection. The LM head's last CTA (atomic ticket) merges the per-CTA argmax
+// partials, commits the token and publishes it with a release store; every CTA
+// acquires it, which also orders the previous token's KV rows and state.
 //
-// The grid barrier is a monotonic counter (zeroed before each launch): phase p
-// may start when it reaches p * gridDim.x. All waits are bounded by wall clock;
-// a wait that gives up sets the error word, the consumers leave together at the
-// end of the phase, and the producer drains its in-flight copies first.
+// All waits are bounded by wall clock (the launch's wait limit): a wait that
+// gives up sets the error word, the consumers leave together at the end of the
+// phase, and the producer drains its in-flight copies first.
 #pragma once
 
 #include "hy_attn.cuh"
