@@ -679,7 +679,8 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
                 d[e] += (acc[0][2][e] + acc[1][2][e]) + ((acc[0][0][e] + acc[1][0][e]) + (acc[0][1][e] + acc[1][1][e]));
         };
         // Store / residual / argmax epilogue of one output (row n of activation row m).
-        auto emit = [&](int m, int n, float v) {
+        // pm (argmax): bit j set when the block prefix's id j is n (see group_epilogue).
+        auto emit = [&](int m, int n, float v, unsigned pm = 0u) {
             if (EPI == EPI_STORE || EPI == EPI_RESID)
             {
                 const size_t o = static_cast<size_t>(m) * a.ldo + n;
@@ -697,8 +698,8 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
                 const unsigned hw = a.hist_stride ? a.hist[static_cast<size_t>(m) * a.hist_stride + (n >> 5)]
                                     : hist_s_ok     ? s_hist[(n >> 5) - (r0 >> 5)]
                                                     : a.hist[n >> 5];
-                bool hit = (hw >> (n & 31)) & 1u;
-                for (int j = 0; j <= m; ++j) hit |= (s_prefix[j] == n);
+                // History of row m: the block's earlier rows plus its prefix ids 0..m.
+                const bool hit = ((hw >> (n & 31)) & 1u) || (pm & ((2u << m) - 1u)) != 0u;
                 const float ps = hit ? (v < 0.0f ? v * pen : v / pen) : v;
                 if (best.ri < 0 || v > best.rv) { best.rv = v; best.ri = n; }
                 if (best.pi < 0 || ps > best.pv) { best.pv = ps; best.pi = n; }
@@ -716,8 +717,14 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
             const int nr = min(8, R - 8 * g);
             if (EPI == EPI_ARGMAX)
             {
-                if (lane < rows)
-                    for (int row = 0; row < nr; ++row) emit(lane, n0 + row, tval(tile, lane, row));
+                // Lane m takes activation row m; which prefix ids equal vocab row n is
+                // found once per n by a ballot over the (at most 16) prefix entries.
+                for (int row = 0; row < nr; ++row)
+                {
+                    const int n = n0 + row;
+                    const unsigned pm = __ballot_sync(0xffffffffu, lane < MT && s_prefix[lane < MT ? lane : 0] == n);
+                    if (lane < rows) emit(lane, n, tval(tile, lane, row), pm);
+                }
             }
             else if (EPI == EPI_ACT)
             {
