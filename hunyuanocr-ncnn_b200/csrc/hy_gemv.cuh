@@ -717,13 +717,19 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
             const int nr = min(8, R - 8 * g);
             if (EPI == EPI_ARGMAX)
             {
-                // Lane m takes activation row m; which prefix ids equal vocab row n is
-                // found once per n by a ballot over the (at most 16) prefix entries.
-                for (int row = 0; row < nr; ++row)
+                // Lanes m and m + 16 take activation row m, the first for the group's
+                // rows 0-3, the second for rows 4-7 (their trackers are merged before
+                // the reduction); which prefix ids equal vocab row n is found once per
+                // n by a ballot over the (at most 16) prefix entries.
+                const int m = lane & 15, half = lane >> 4;
+                const int pid = s_prefix[m];
+#pragma unroll
+                for (int r4 = 0; r4 < 4; ++r4)
                 {
-                    const int n = n0 + row;
-                    const unsigned pm = __ballot_sync(0xffffffffu, lane < MT && s_prefix[lane < MT ? lane : 0] == n);
-                    if (lane < rows) emit(lane, n, tval(tile, lane, row), pm);
+                    const unsigned pm0 = __ballot_sync(0xffffffffu, half == 0 && pid == n0 + r4);
+                    const unsigned pm1 = __ballot_sync(0xffffffffu, half == 0 && pid == n0 + 4 + r4);
+                    const int row = 4 * half + r4;
+                    if (row < nr && m < rows) emit(m, n0 + row, tval(tile, m, row), half ? pm1 : pm0);
                 }
             }
             else if (EPI == EPI_ACT)
@@ -1023,6 +1029,20 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
     }
 
     // ---------------- argmax reduction ----------------
+    if constexpr (MT == 16)
+    {
+        // Lane m + 16 tracked activation row m over the groups' rows 4-7: fold it into lane m
+        // (larger value, then lower index: the first index of the maximum).
+        const float orv = __shfl_down_sync(0xffffffffu, best.rv, 16);
+        const int ori = __shfl_down_sync(0xffffffffu, best.ri, 16);
+        const float opv = __shfl_down_sync(0xffffffffu, best.pv, 16);
+        const int opi = __shfl_down_sync(0xffffffffu, best.pi, 16);
+        if (lane < 16)
+        {
+            if (ori >= 0) best_update(best.rv, best.ri, orv, ori);
+            if (opi >= 0) best_update(best.pv, best.pi, opv, opi);
+        }
+    }
     if (lane < MT)
         red4[warp * MT + lane] = make_float4(best.rv, __int_as_float(best.ri), best.pv, __int_as_float(best.pi));
     consumers_sync();
