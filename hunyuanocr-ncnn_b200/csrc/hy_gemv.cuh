@@ -745,6 +745,38 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
                     }
                 }
             }
+            else if (EPI == EPI_RESID)
+            {
+                // The lane's 4 outputs: every residual (and first-half) load is issued
+                // before the first store, one L2 round trip instead of one per output.
+                float old[4], ext[4];
+#pragma unroll
+                for (int it = 0; it < 4; ++it)
+                {
+                    const int p = lane + 32 * it, m = p >> 3, row = p & 7;
+                    old[it] = ext[it] = 0.f;
+                    if (row < nr && m < rows)
+                    {
+                        const size_t o = static_cast<size_t>(m) * a.ldo + n0 + row;
+                        old[it] = a.out[o];
+                        if (a.extra) ext[it] = a.extra[o];
+                    }
+                }
+#pragma unroll
+                for (int it = 0; it < 4; ++it)
+                {
+                    const int p = lane + 32 * it, m = p >> 3, row = p & 7;
+                    if (row < nr && m < rows)
+                    {
+                        const size_t o = static_cast<size_t>(m) * a.ldo + n0 + row;
+                        float v = tval(tile, m, row);
+                        if (a.extra) v = ext[it] + v;
+                        v = old[it] + v;
+                        if (a.aux) a.aux[static_cast<size_t>(m) * a.ld_aux + n0 + row] = v;
+                        a.out[o] = v;
+                    }
+                }
+            }
             else
             {
                 for (int p = lane; p < 16 * 8; p += 32)
