@@ -656,8 +656,9 @@ __global__ void __launch_bounds__(kGemvThreads, (MT == 1) ? 2 : 1) gemv_kernel(c
         float d[4];
         // Tile of the unit in `slot` (chunk c): d += x[0:16, chunk] * W[8 rows, chunk]^T.
         // Six accumulator chains (the three split products x even / odd k-steps),
-        // added at the end: one chain of dependent MMAs per unit left the tensor
-        // pipe idle for most of each MMA's latency.
+        // added at the end, so consecutive MMAs of a unit do not wait on each other
+        // (a warp's MMA time per unit fell by a quarter; the launch's time is set by
+        // when its later weight units arrive).
         auto unit_mma = [&](int slot, int c) {
             const WT* wr = reinterpret_cast<const WT*>(ring + slot * STAGE + g8 * PITCH);
             const float* x0 = xs + g8 * XP + c * KC + t4;
